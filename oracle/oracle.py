@@ -1,0 +1,529 @@
+"""ctypes bindings for the two CPU checkers (TEST INFRASTRUCTURE ONLY).
+
+`Restatement` wraps libk3x_oracle.so (k3x_oracle.c, the C restatement of the
+reference algorithms). `Reference` wraps _ref/libk3x_ref.so (the reference's
+own CPU sources compiled by oracle/Makefile). Only tests/, __graft_entry__.smoke()
+and bench.py's CPU legs may import this module; the product never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+RESTATEMENT_SO = os.path.join(HERE, "libk3x_oracle.so")
+REFERENCE_SO = os.path.join(HERE, "_ref", "libk3x_ref.so")
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_sz = C.c_size_t
+_szp = C.POINTER(C.c_size_t)
+
+ACT_SWIGLU = 0
+ACT_SITU = 1
+
+
+class OracleError(RuntimeError):
+    def __init__(self, status: int, where: str):
+        super().__init__(f"{where} failed with status {status}")
+        self.status = status
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+class _MoeLayer(C.Structure):
+    _fields_ = [
+        ("hidden", _sz), ("inter", _sz), ("experts", _sz), ("top_k", _sz),
+        ("shared_inter", _sz),
+        ("router", C.c_void_p), ("correction", C.c_void_p),
+        ("gate_packed", C.c_void_p), ("gate_scales", C.c_void_p),
+        ("up_packed", C.c_void_p), ("up_scales", C.c_void_p),
+        ("down_packed", C.c_void_p), ("down_scales", C.c_void_p),
+        ("shared_gate", C.c_void_p), ("shared_up", C.c_void_p), ("shared_down", C.c_void_p),
+        ("activation", C.c_int), ("situ_beta", C.c_float), ("situ_linear_beta", C.c_float),
+    ]
+
+
+class _KdaWeights(C.Structure):
+    _fields_ = [
+        ("hidden", _sz), ("heads", _sz), ("head_dim", _sz), ("conv_width", _sz),
+        ("eps", C.c_float), ("gate_lower_bound", C.c_float),
+        ("q_proj", C.c_void_p), ("k_proj", C.c_void_p), ("v_proj", C.c_void_p),
+        ("q_conv", C.c_void_p), ("k_conv", C.c_void_p), ("v_conv", C.c_void_p),
+        ("f_a_proj", C.c_void_p), ("f_b_proj", C.c_void_p),
+        ("a_log", C.c_void_p), ("dt_bias", C.c_void_p),
+        ("b_proj", C.c_void_p), ("g_proj", C.c_void_p),
+        ("o_norm", C.c_void_p), ("o_proj", C.c_void_p),
+    ]
+
+
+def moe_struct(layer: dict):
+    """Builds the C layer descriptor from a dict of numpy arrays; returns
+    (struct, keepalive)."""
+    keep = {k: (_c(v, v.dtype) if isinstance(v, np.ndarray) else v) for k, v in layer.items()}
+    s = _MoeLayer()
+    s.hidden, s.inter = keep["hidden"], keep["inter"]
+    s.experts, s.top_k = keep["experts"], keep["top_k"]
+    s.shared_inter = keep.get("shared_inter", 0)
+    for name in ("router", "correction", "gate_packed", "gate_scales", "up_packed",
+                 "up_scales", "down_packed", "down_scales"):
+        setattr(s, name, _ptr(keep[name]))
+    for name in ("shared_gate", "shared_up", "shared_down"):
+        setattr(s, name, _ptr(keep.get(name)))
+    s.activation = keep.get("activation", ACT_SWIGLU)
+    s.situ_beta = keep.get("situ_beta", 4.0)
+    s.situ_linear_beta = keep.get("situ_linear_beta", 0.0)
+    return s, keep
+
+
+def kda_struct(w: dict):
+    keep = {k: (_c(v, v.dtype) if isinstance(v, np.ndarray) else v) for k, v in w.items()}
+    s = _KdaWeights()
+    for name in ("hidden", "heads", "head_dim", "conv_width", "eps", "gate_lower_bound"):
+        setattr(s, name, keep[name])
+    for name in ("q_proj", "k_proj", "v_proj", "q_conv", "k_conv", "v_conv", "f_a_proj",
+                 "f_b_proj", "a_log", "dt_bias", "b_proj", "g_proj", "o_norm", "o_proj"):
+        setattr(s, name, _ptr(keep[name]))
+    return s, keep
+
+
+class Restatement:
+    """The C restatement (k3x_oracle.c)."""
+
+    def __init__(self, path: str = RESTATEMENT_SO):
+        L = C.CDLL(path)
+        self.lib = L
+        L.k3xo_round_bf16.restype = C.c_float
+        L.k3xo_round_bf16.argtypes = [C.c_float]
+        L.k3xo_decode_mxfp4.argtypes = [_u8p, _u8p, _sz, _sz, _sz, _f32p]
+        L.k3xo_mxfp4_matmul.argtypes = [_f32p, _u8p, _u8p, _sz, _sz, _sz, _f32p]
+        L.k3xo_quantize_mxfp4.argtypes = [_f32p, _sz, _sz, _u8p, _u8p]
+        L.k3xo_quantize_mxfp4.restype = None
+        L.k3xo_e2m1_terms.argtypes = [_f32p, C.c_int, _u8p, _u8p]
+        L.k3xo_e2m1_terms.restype = C.c_float
+        L.k3xo_situ_glu.argtypes = [_f32p, _f32p, _f32p, _sz, C.c_float, C.c_float]
+        L.k3xo_situ_glu.restype = None
+        L.k3xo_swiglu.argtypes = [_f32p, _f32p, _f32p, _sz]
+        L.k3xo_swiglu.restype = None
+        L.k3xo_bf16_matvec.argtypes = [_f32p, _u16p, _sz, _sz, _f32p]
+        L.k3xo_router_logits.argtypes = [_f32p, _u16p, _sz, _sz, _f32p]
+        L.k3xo_route_logits.argtypes = [_f32p, _f32p, _sz, _sz, _u32p, _f32p, C.c_void_p]
+        L.k3xo_expert_major_plan.argtypes = [_u32p, _f32p, _sz, _sz, _u32p, _u32p, _u32p,
+                                             _u32p, _f32p, _szp]
+        L.k3xo_routed_combine.argtypes = [_f32p, _f32p, _sz, _sz, _f32p]
+        L.k3xo_routed_combine.restype = None
+        L.k3xo_moe_layer_forward.argtypes = [C.c_void_p, _f32p, _sz, _f32p, _u32p, _f32p]
+        L.k3xo_kda_step.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _sz, _sz, _f32p]
+        L.k3xo_kda_tree.argtypes = [_f32p, _i32p, _sz, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                    _sz, _sz, _f32p, C.c_void_p]
+        L.k3xo_kda_block.argtypes = [C.c_void_p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p, _f32p]
+        L.k3xo_argmax.restype = C.c_uint32
+        L.k3xo_argmax.argtypes = [_f32p, _sz]
+        L.k3xo_verify_greedy_block.argtypes = [C.c_uint32, _u32p, _sz, _sz, _sz, _u32p,
+                                               _szp, _u32p, _szp, C.POINTER(C.c_int)]
+        L.k3xo_uniform.restype = C.c_double
+        L.k3xo_uniform.argtypes = [C.c_uint64] * 4
+        L.k3xo_verify_rejection.argtypes = [_f32p, _f32p, _u32p, _sz, _sz, C.c_float,
+                                            C.c_uint64, C.c_uint64, _szp, _u32p, _szp]
+
+    # -- helpers ---------------------------------------------------------------
+    @staticmethod
+    def _check(st, where):
+        if st != 0:
+            raise OracleError(st, where)
+
+    def round_bf16(self, x):
+        x = _c(x, np.float32)
+        u = x.view(np.uint32).astype(np.uint64)
+        special = (u & 0x7F800000) == 0x7F800000
+        r = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+        s = np.where((u & 0x7FFFFF) != 0, (u | 0x400000) & 0xFFFF0000, u & 0xFFFF0000)
+        return np.where(special, s, r).astype(np.uint32).view(np.float32).reshape(x.shape)
+
+    def decode_mxfp4(self, packed, scales, rows, cols, group=32):
+        out = np.empty(rows * cols, np.float32)
+        self._check(self.lib.k3xo_decode_mxfp4(_c(packed, np.uint8), _c(scales, np.uint8),
+                                               rows, cols, group, out), "decode_mxfp4")
+        return out.reshape(rows, cols)
+
+    def mxfp4_matmul(self, x, packed, scales, rows, cols, group=32):
+        out = np.empty(rows, np.float32)
+        self._check(self.lib.k3xo_mxfp4_matmul(_c(x, np.float32), _c(packed, np.uint8),
+                                               _c(scales, np.uint8), rows, cols, group, out),
+                    "mxfp4_matmul")
+        return out
+
+    def quantize_mxfp4(self, x):
+        x = _c(x, np.float32)
+        rows, cols = x.shape
+        packed = np.empty((rows, cols // 2), np.uint8)
+        scales = np.empty((rows, cols // 32), np.uint8)
+        self.lib.k3xo_quantize_mxfp4(x, rows, cols, packed, scales)
+        return packed, scales
+
+    def e2m1_terms(self, x32, nterms):
+        packed = np.empty(nterms * 16, np.uint8)
+        scales = np.empty(nterms, np.uint8)
+        res = self.lib.k3xo_e2m1_terms(_c(x32, np.float32), nterms, packed, scales)
+        return packed.reshape(nterms, 16), scales, res
+
+    def situ_glu(self, gate, up, beta, linear_beta=0.0):
+        g, u = _c(gate, np.float32), _c(up, np.float32)
+        out = np.empty_like(g)
+        self.lib.k3xo_situ_glu(out, g, u, g.size, beta, linear_beta)
+        return out
+
+    def swiglu(self, gate, up):
+        g, u = _c(gate, np.float32), _c(up, np.float32)
+        out = np.empty_like(g)
+        self.lib.k3xo_swiglu(out, g, u, g.size)
+        return out
+
+    def bf16_matvec(self, x, w):
+        w = _c(w, np.uint16)
+        out = np.empty(w.shape[0], np.float32)
+        self._check(self.lib.k3xo_bf16_matvec(_c(x, np.float32), w, w.shape[0], w.shape[1], out),
+                    "bf16_matvec")
+        return out
+
+    def router_logits(self, hidden, router):
+        router = _c(router, np.uint16)
+        out = np.empty(router.shape[0], np.float32)
+        self._check(self.lib.k3xo_router_logits(_c(hidden, np.float32), router,
+                                                router.shape[0], router.shape[1], out),
+                    "router_logits")
+        return out
+
+    def route_logits(self, logits, correction, top_k, want_scores=False):
+        logits = _c(logits, np.float32)
+        E = logits.size
+        ids = np.empty(top_k, np.uint32)
+        contrib = np.empty(top_k, np.float32)
+        scores = np.empty(E, np.float32) if want_scores else None
+        self._check(self.lib.k3xo_route_logits(logits, _c(correction, np.float32), E, top_k, ids,
+                                               contrib, _ptr(scores)), "route_logits")
+        return (ids, contrib, scores) if want_scores else (ids, contrib)
+
+    def route(self, hidden, router, correction, top_k):
+        return self.route_logits(self.router_logits(hidden, router), correction, top_k)
+
+    def expert_major_plan(self, ids, contrib):
+        ids = _c(ids, np.uint32)
+        T, K = ids.shape
+        n = T * K
+        ge = np.zeros(n, np.uint32)
+        go = np.zeros(n + 1, np.uint32)
+        at = np.zeros(n, np.uint32)
+        asl = np.zeros(n, np.uint32)
+        ac = np.zeros(n, np.float32)
+        ng = C.c_size_t(0)
+        self._check(self.lib.k3xo_expert_major_plan(ids, _c(contrib, np.float32), T, K, ge, go, at,
+                                                    asl, ac, C.byref(ng)), "expert_major_plan")
+        g = ng.value
+        return dict(group_expert=ge[:g], group_offset=go[:g + 1], assign_token=at[:n],
+                    assign_slot=asl[:n], assign_contrib=ac[:n])
+
+    def routed_combine(self, y, contrib):
+        y = _c(y, np.float32)
+        K, H = y.shape
+        out = np.empty(H, np.float32)
+        self.lib.k3xo_routed_combine(y, _c(contrib, np.float32), K, H, out)
+        return out
+
+    def moe_layer(self, layer: dict, hidden):
+        hidden = _c(hidden, np.float32)
+        T = hidden.shape[0]
+        s, keep = moe_struct(layer)
+        out = np.empty((T, layer["hidden"]), np.float32)
+        ids = np.empty((T, layer["top_k"]), np.uint32)
+        contrib = np.empty((T, layer["top_k"]), np.float32)
+        self._check(self.lib.k3xo_moe_layer_forward(C.byref(s), hidden, T, out, ids, contrib),
+                    "moe_layer_forward")
+        del keep
+        return out, ids, contrib
+
+    def kda_step(self, state, q, k, v, log_decay, beta, heads, head_dim):
+        state = np.array(state, np.float32, copy=True, order="C")
+        out = np.empty(heads * head_dim, np.float32)
+        self._check(self.lib.k3xo_kda_step(state, _c(q, np.float32), _c(k, np.float32),
+                                           _c(v, np.float32), _c(log_decay, np.float32),
+                                           _c(beta, np.float32), heads, head_dim, out),
+                    "kda_step")
+        return state, out
+
+    def kda_tree(self, prefix_state, parent, q, k, v, log_decay, beta, heads, head_dim,
+                 want_states=False):
+        parent = _c(parent, np.int32)
+        n = parent.size
+        out = np.empty((n, heads * head_dim), np.float32)
+        states = np.empty((n, heads, head_dim, head_dim), np.float32) if want_states else None
+        self._check(self.lib.k3xo_kda_tree(_c(prefix_state, np.float32), parent, n,
+                                           _c(q, np.float32), _c(k, np.float32), _c(v, np.float32),
+                                           _c(log_decay, np.float32), _c(beta, np.float32),
+                                           heads, head_dim, out, _ptr(states)), "kda_tree")
+        return (out, states) if want_states else out
+
+    def kda_block(self, weights: dict, hidden, conv_q, conv_k, conv_v, recurrent):
+        s, keep = kda_struct(weights)
+        hidden = _c(hidden, np.float32)
+        T = hidden.size // weights["hidden"]
+        cq, ck, cv = (np.array(a, np.uint16, copy=True) for a in (conv_q, conv_k, conv_v))
+        rec = np.array(recurrent, np.float32, copy=True)
+        out = np.empty(T * weights["hidden"], np.float32)
+        self._check(self.lib.k3xo_kda_block(C.byref(s), hidden, T, cq, ck, cv, rec, out),
+                    "kda_block")
+        del keep
+        return out.reshape(T, weights["hidden"]), (cq, ck, cv, rec)
+
+    def argmax(self, logits):
+        logits = _c(logits, np.float32)
+        return int(self.lib.k3xo_argmax(logits, logits.size))
+
+    def verify_greedy_block(self, anchor, drafts, max_draft, vocab, targets):
+        drafts = _c(drafts, np.uint32)
+        acc, ncom, allacc = C.c_size_t(), C.c_size_t(), C.c_int()
+        com = np.zeros(drafts.size + 1, np.uint32)
+        self._check(self.lib.k3xo_verify_greedy_block(anchor, drafts, drafts.size, max_draft, vocab,
+                                                      _c(targets, np.uint32), C.byref(acc), com,
+                                                      C.byref(ncom), C.byref(allacc)),
+                    "verify_greedy_block")
+        return acc.value, com[:ncom.value].tolist(), bool(allacc.value)
+
+    def uniform(self, seed, seq, pos, purpose):
+        return self.lib.k3xo_uniform(seed, seq, pos, purpose)
+
+    def verify_rejection(self, target_logits, draft_logits, drafts, temperature, seed, sequence):
+        tl = _c(target_logits, np.float32)
+        dl = _c(draft_logits, np.float32)
+        drafts = _c(drafts, np.uint32)
+        p = drafts.size
+        V = tl.shape[-1]
+        acc, ncom = C.c_size_t(), C.c_size_t()
+        com = np.zeros(p + 1, np.uint32)
+        self._check(self.lib.k3xo_verify_rejection(tl, dl if p else np.zeros(1, np.float32),
+                                                   drafts if p else np.zeros(1, np.uint32), p, V,
+                                                   temperature, seed, sequence, C.byref(acc), com,
+                                                   C.byref(ncom)), "verify_rejection")
+        return acc.value, com[:ncom.value].tolist()
+
+
+_STEP_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_uint32, C.POINTER(C.c_uint32))
+
+
+class Reference:
+    """The reference's own CPU code (oracle/_ref/libk3x_ref.so)."""
+
+    def __init__(self, path: str = REFERENCE_SO):
+        L = C.CDLL(path)
+        self.lib = L
+        L.k3xr_decode_mxfp4.argtypes = [_u8p, _u8p, _sz, _sz, _sz, _f32p]
+        L.k3xr_mxfp4_matmul.argtypes = [_f32p, _u8p, _u8p, _sz, _sz, _sz, _f32p]
+        L.k3xr_situ_glu.argtypes = [_f32p, _f32p, _f32p, _sz, C.c_float, C.c_float]
+        L.k3xr_situ_glu.restype = None
+        L.k3xr_route_official_moe.argtypes = [_f32p, _u16p, _sz, _sz, _f32p, _sz, _u32p, _f32p,
+                                              C.c_void_p]
+        L.k3xr_route_official_moe_logits.argtypes = [_f32p, _f32p, _sz, _sz, _u32p, _f32p,
+                                                     C.c_void_p]
+        L.k3xr_expert_major_plan.argtypes = [_u32p, _f32p, _u32p, _sz, _u32p, _u32p, _u32p, _u32p,
+                                             _f32p, _szp]
+        L.k3xr_verify_greedy_target_block.argtypes = [C.c_uint32, _u32p, _sz, _sz, _sz, _u32p,
+                                                      _szp, _u32p, _szp, C.POINTER(C.c_int)]
+        L.k3xr_verify_greedy_draft.argtypes = [C.c_uint32, _u32p, _sz, _sz, _sz, _STEP_FN,
+                                               C.c_void_p, _szp, _u32p, _szp, C.POINTER(C.c_int)]
+        L.k3xr_moe_layer_forward.argtypes = [C.c_void_p, _f32p, _sz, _sz, _f32p, _u32p, _f32p,
+                                             C.c_int]
+        L.k3xr_official_kda_cpu.argtypes = [C.c_void_p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p,
+                                            _f32p]
+
+    def decode_mxfp4(self, packed, scales, rows, cols, group=32):
+        out = np.empty(rows * cols, np.float32)
+        st = self.lib.k3xr_decode_mxfp4(_c(packed, np.uint8), _c(scales, np.uint8), rows, cols,
+                                        group, out)
+        if st:
+            raise OracleError(st, "ref decode_mxfp4")
+        return out.reshape(rows, cols)
+
+    def mxfp4_matmul(self, x, packed, scales, rows, cols, group=32):
+        out = np.empty(rows, np.float32)
+        st = self.lib.k3xr_mxfp4_matmul(_c(x, np.float32), _c(packed, np.uint8),
+                                        _c(scales, np.uint8), rows, cols, group, out)
+        if st:
+            raise OracleError(st, "ref mxfp4_matmul")
+        return out
+
+    def situ_glu(self, gate, up, beta, linear_beta=0.0):
+        g, u = _c(gate, np.float32), _c(up, np.float32)
+        out = np.empty_like(g)
+        self.lib.k3xr_situ_glu(out, g, u, g.size, beta, linear_beta)
+        return out
+
+    def route(self, hidden, router, correction, top_k, want_scores=False):
+        router = _c(router, np.uint16)
+        E, H = router.shape
+        ids = np.empty(top_k, np.uint32)
+        contrib = np.empty(top_k, np.float32)
+        scores = np.empty(E, np.float32) if want_scores else None
+        st = self.lib.k3xr_route_official_moe(_c(hidden, np.float32), router, E, H,
+                                              _c(correction, np.float32), top_k, ids, contrib,
+                                              _ptr(scores))
+        if st:
+            raise OracleError(st, "ref route_official_moe")
+        return (ids, contrib, scores) if want_scores else (ids, contrib)
+
+    def route_logits(self, logits, correction, top_k):
+        logits = _c(logits, np.float32)
+        ids = np.empty(top_k, np.uint32)
+        contrib = np.empty(top_k, np.float32)
+        st = self.lib.k3xr_route_official_moe_logits(logits, _c(correction, np.float32),
+                                                     logits.size, top_k, ids, contrib, None)
+        if st:
+            raise OracleError(st, "ref route_official_moe_logits")
+        return ids, contrib
+
+    def expert_major_plan(self, ids_list, contrib_list):
+        counts = np.array([len(x) for x in ids_list], np.uint32)
+        ids = np.array([i for x in ids_list for i in x], np.uint32)
+        con = np.array([c for x in contrib_list for c in x], np.float32)
+        n = max(int(counts.sum()), 1)
+        ge = np.zeros(n, np.uint32)
+        go = np.zeros(n + 1, np.uint32)
+        at = np.zeros(n, np.uint32)
+        asl = np.zeros(n, np.uint32)
+        ac = np.zeros(n, np.float32)
+        ng = C.c_size_t(0)
+        st = self.lib.k3xr_expert_major_plan(ids if ids.size else np.zeros(1, np.uint32),
+                                             con if con.size else np.zeros(1, np.float32),
+                                             counts if counts.size else np.zeros(1, np.uint32),
+                                             len(ids_list), ge, go, at, asl, ac, C.byref(ng))
+        if st:
+            raise OracleError(st, "ref build_expert_major_plan")
+        g = ng.value
+        m = int(counts.sum())
+        return dict(group_expert=ge[:g], group_offset=go[:g + 1], assign_token=at[:m],
+                    assign_slot=asl[:m], assign_contrib=ac[:m])
+
+    def verify_greedy_block(self, anchor, drafts, max_draft, vocab, targets):
+        drafts = _c(drafts, np.uint32)
+        acc, ncom, allacc = C.c_size_t(), C.c_size_t(), C.c_int()
+        com = np.zeros(drafts.size + 1, np.uint32)
+        st = self.lib.k3xr_verify_greedy_target_block(anchor,
+                                                      drafts if drafts.size else np.zeros(1, np.uint32),
+                                                      drafts.size, max_draft, vocab,
+                                                      _c(targets, np.uint32), C.byref(acc), com,
+                                                      C.byref(ncom), C.byref(allacc))
+        if st:
+            raise OracleError(st, "ref verify_greedy_target_block")
+        return acc.value, com[:ncom.value].tolist(), bool(allacc.value)
+
+    def verify_greedy_draft(self, anchor, drafts, max_draft, vocab, step):
+        """step(input_token) -> (status, output_token)"""
+        drafts = _c(drafts, np.uint32)
+
+        def cb(_user, inp, outp):
+            st, tok = step(int(inp))
+            outp[0] = tok
+            return st
+
+        fn = _STEP_FN(cb)
+        acc, ncom, allacc = C.c_size_t(), C.c_size_t(), C.c_int()
+        com = np.zeros(drafts.size + 1, np.uint32)
+        st = self.lib.k3xr_verify_greedy_draft(anchor,
+                                               drafts if drafts.size else np.zeros(1, np.uint32),
+                                               drafts.size, max_draft, vocab, fn, None,
+                                               C.byref(acc), com, C.byref(ncom), C.byref(allacc))
+        if st:
+            raise OracleError(st, "ref verify_greedy_draft")
+        return acc.value, com[:ncom.value].tolist(), bool(allacc.value)
+
+    def moe_layer(self, layer: dict, hidden, token_begin=0, token_end=None, threads=1):
+        hidden = _c(hidden, np.float32)
+        T = hidden.shape[0]
+        token_end = T if token_end is None else token_end
+        s, keep = moe_struct(layer)
+        out = np.zeros((T, layer["hidden"]), np.float32)
+        ids = np.zeros((T, layer["top_k"]), np.uint32)
+        contrib = np.zeros((T, layer["top_k"]), np.float32)
+        st = self.lib.k3xr_moe_layer_forward(C.byref(s), hidden, token_begin, token_end, out, ids,
+                                             contrib, threads)
+        del keep
+        if st:
+            raise OracleError(st, "ref moe layer")
+        return out, ids, contrib
+
+    def kda_block(self, weights: dict, hidden, conv_q, conv_k, conv_v, recurrent):
+        s, keep = kda_struct(weights)
+        hidden = _c(hidden, np.float32)
+        T = hidden.size // weights["hidden"]
+        cq, ck, cv = (np.array(a, np.uint16, copy=True) for a in (conv_q, conv_k, conv_v))
+        rec = np.array(recurrent, np.float32, copy=True)
+        out = np.empty(T * weights["hidden"], np.float32)
+        st = self.lib.k3xr_official_kda_cpu(C.byref(s), hidden, T, cq, ck, cv, rec, out)
+        del keep
+        if st:
+            raise OracleError(st, "ref official_kda_cpu")
+        return out.reshape(T, weights["hidden"]), (cq, ck, cv, rec)
+
+
+def have_reference() -> bool:
+    return os.path.exists(REFERENCE_SO)
+
+
+# ---------------------------------------------------------------------------
+# seeded synthetic inputs shared by tests and bench (numpy; small sizes)
+# ---------------------------------------------------------------------------
+
+def bf16_words(x):
+    """float32 -> bf16 words with the reference's round-to-nearest-even."""
+    x = np.ascontiguousarray(x, np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    return (((u + 0x7FFF + ((u >> 16) & 1)) >> 16) & 0xFFFF).astype(np.uint16)
+
+
+def bf16_values(words):
+    return (np.asarray(words, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def make_moe_layer(rs: Restatement, seed, hidden, inter, experts, top_k, shared_inter=0,
+                   sigma=0.02, activation=ACT_SWIGLU):
+    """Synthetic plain MoE layer: N(0, sigma) weights, experts quantised to
+    MXFP4 with the restated quantiser, router/shared in bf16."""
+    g = np.random.default_rng(seed)
+
+    def mx(rows, cols):
+        w = g.normal(0.0, sigma, size=(rows, cols)).astype(np.float32)
+        return rs.quantize_mxfp4(w)
+
+    gp, gs, up_, us, dp, ds = [], [], [], [], [], []
+    for _ in range(experts):
+        a, b = mx(inter, hidden); gp.append(a); gs.append(b)
+        a, b = mx(inter, hidden); up_.append(a); us.append(b)
+        a, b = mx(hidden, inter); dp.append(a); ds.append(b)
+    layer = dict(
+        hidden=hidden, inter=inter, experts=experts, top_k=top_k, shared_inter=shared_inter,
+        router=bf16_words(g.normal(0.0, sigma, size=(experts, hidden))),
+        correction=g.normal(0.0, sigma, size=experts).astype(np.float32),
+        gate_packed=np.stack(gp), gate_scales=np.stack(gs),
+        up_packed=np.stack(up_), up_scales=np.stack(us),
+        down_packed=np.stack(dp), down_scales=np.stack(ds),
+        activation=activation, situ_beta=4.0, situ_linear_beta=25.0 if activation else 0.0,
+    )
+    if shared_inter:
+        layer["shared_gate"] = bf16_words(g.normal(0.0, sigma, size=(shared_inter, hidden)))
+        layer["shared_up"] = bf16_words(g.normal(0.0, sigma, size=(shared_inter, hidden)))
+        layer["shared_down"] = bf16_words(g.normal(0.0, sigma, size=(hidden, shared_inter)))
+    return layer
+
+
+def bf16_normal(g, shape, sigma=1.0):
+    return bf16_values(bf16_words(g.normal(0.0, sigma, size=shape).astype(np.float32)))

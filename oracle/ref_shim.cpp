@@ -1,0 +1,338 @@
+// ref_shim.cpp — extern "C" entry points over the reference's own CPU code.
+//
+// TEST INFRASTRUCTURE ONLY. oracle/Makefile compiles this file together with
+// the reference's unmodified sources (runtime/src/{ops,official_moe,
+// official_kda,official_layer,expert_major,speculative,routing_policy,
+// profile}.cpp, read in place from the reference checkout) into
+// oracle/_ref/libk3x_ref.so. Tests use it to pin the C restatement
+// (k3x_oracle.c); bench.py uses it as the timed CPU reference arm. Nothing
+// here is reference source: every function below only marshals plain C
+// arrays into the reference's C++ API and back.
+#include "k3x/expert_major.hpp"
+#include "k3x/official_kda.hpp"
+#include "k3x/official_moe.hpp"
+#include "k3x/ops.hpp"
+#include "k3x/speculative.hpp"
+
+#include <algorithm>
+#include <atomic>
+#include <bit>
+#include <cstdint>
+#include <cstring>
+#include <optional>
+#include <span>
+#include <thread>
+#include <vector>
+
+namespace {
+
+using k3x::ErrorCode;
+
+template <typename T>
+int code(const k3x::Result<T>& r) {
+    return r ? 0 : static_cast<int>(r.error());
+}
+
+std::span<const std::byte> bytes(const std::uint8_t* p, std::size_t n) {
+    return {reinterpret_cast<const std::byte*>(p), n};
+}
+
+// Rounding helper used where the reference's own (file-local) round_bf16
+// is applied by a composed step; same bit formula.
+float round_bf16(float value) {
+    auto bits = std::bit_cast<std::uint32_t>(value);
+    if ((bits & 0x7f800000U) == 0x7f800000U) {
+        if (bits & 0x007fffffU) bits |= 0x00400000U;
+        return std::bit_cast<float>(bits & 0xffff0000U);
+    }
+    bits += 0x7fffU + ((bits >> 16U) & 1U);
+    return std::bit_cast<float>(bits & 0xffff0000U);
+}
+
+std::optional<float> linear(float linear_beta) {
+    return linear_beta > 0.0F ? std::optional<float>(linear_beta) : std::nullopt;
+}
+
+}  // namespace
+
+extern "C" {
+
+struct k3xr_moe_layer {
+    std::size_t hidden, inter, experts, top_k, shared_inter;
+    const std::uint16_t* router;
+    const float* correction;
+    const std::uint8_t* gate_packed;
+    const std::uint8_t* gate_scales;
+    const std::uint8_t* up_packed;
+    const std::uint8_t* up_scales;
+    const std::uint8_t* down_packed;
+    const std::uint8_t* down_scales;
+    const std::uint16_t* shared_gate;
+    const std::uint16_t* shared_up;
+    const std::uint16_t* shared_down;
+    int activation;  // 0 = SwiGLU (situ_glu with beta 2^64, no linear bound), 1 = SiTU
+    float situ_beta, situ_linear_beta;
+};
+
+int k3xr_decode_mxfp4(const std::uint8_t* packed, const std::uint8_t* scales,
+                      std::size_t rows, std::size_t cols, std::size_t group,
+                      float* out) {
+    auto r = k3x::decode_mxfp4(bytes(packed, rows * cols / 2),
+                               bytes(scales, rows * cols / group), rows, cols, group);
+    if (r) std::copy(r.value().begin(), r.value().end(), out);
+    return code(r);
+}
+
+int k3xr_mxfp4_matmul(const float* x, const std::uint8_t* packed,
+                      const std::uint8_t* scales, std::size_t rows,
+                      std::size_t cols, std::size_t group, float* out) {
+    auto r = k3x::mxfp4_matmul({x, cols}, bytes(packed, rows * cols / 2),
+                               bytes(scales, rows * cols / group), rows, cols, group);
+    if (r) std::copy(r.value().begin(), r.value().end(), out);
+    return code(r);
+}
+
+void k3xr_situ_glu(float* out, const float* gate, const float* up, std::size_t n,
+                   float beta, float linear_beta) {
+    k3x::situ_glu({out, n}, {gate, n}, {up, n}, beta, linear(linear_beta));
+}
+
+int k3xr_route_official_moe(const float* hidden, const std::uint16_t* router,
+                            std::size_t experts, std::size_t hidden_size,
+                            const float* correction, std::size_t top_k,
+                            std::uint32_t* ids, float* contributions, float* scores) {
+    k3x::Bf16WeightView view{{router, experts * hidden_size}, experts, hidden_size, 0};
+    auto r = k3x::route_official_moe({hidden, hidden_size}, view,
+                                     {correction, experts}, top_k);
+    if (r) {
+        std::copy(r.value().expert_ids.begin(), r.value().expert_ids.end(), ids);
+        std::copy(r.value().contributions.begin(), r.value().contributions.end(),
+                  contributions);
+        if (scores) std::copy(r.value().scores.begin(), r.value().scores.end(), scores);
+    }
+    return code(r);
+}
+
+int k3xr_route_official_moe_logits(const float* logits, const float* correction,
+                                   std::size_t experts, std::size_t top_k,
+                                   std::uint32_t* ids, float* contributions,
+                                   float* scores) {
+    auto r = k3x::route_official_moe_logits({logits, experts}, {correction, experts}, top_k);
+    if (r) {
+        std::copy(r.value().expert_ids.begin(), r.value().expert_ids.end(), ids);
+        std::copy(r.value().contributions.begin(), r.value().contributions.end(),
+                  contributions);
+        if (scores) std::copy(r.value().scores.begin(), r.value().scores.end(), scores);
+    }
+    return code(r);
+}
+
+// Routes are given per token as (ids, contributions) of width counts[t].
+int k3xr_expert_major_plan(const std::uint32_t* ids, const float* contributions,
+                           const std::uint32_t* counts, std::size_t tokens,
+                           std::uint32_t* group_expert, std::uint32_t* group_offset,
+                           std::uint32_t* assign_token, std::uint32_t* assign_slot,
+                           float* assign_contrib, std::size_t* group_count) {
+    std::vector<k3x::ExpertMajorTokenRoute> routes(tokens);
+    std::size_t at = 0;
+    for (std::size_t t = 0; t < tokens; ++t) {
+        routes[t].expert_ids.assign(ids + at, ids + at + counts[t]);
+        routes[t].contributions.assign(contributions + at, contributions + at + counts[t]);
+        at += counts[t];
+    }
+    auto r = k3x::build_expert_major_plan(routes);
+    if (!r) return code(r);
+    std::size_t pos = 0;
+    const auto& plan = r.value();
+    for (std::size_t g = 0; g < plan.groups.size(); ++g) {
+        group_expert[g] = plan.groups[g].expert_id;
+        group_offset[g] = static_cast<std::uint32_t>(pos);
+        for (const auto& a : plan.groups[g].assignments) {
+            assign_token[pos] = static_cast<std::uint32_t>(a.token_index);
+            assign_slot[pos] = static_cast<std::uint32_t>(a.router_slot);
+            assign_contrib[pos] = a.contribution;
+            ++pos;
+        }
+    }
+    group_offset[plan.groups.size()] = static_cast<std::uint32_t>(pos);
+    *group_count = plan.groups.size();
+    return 0;
+}
+
+int k3xr_verify_greedy_target_block(std::uint32_t anchor, const std::uint32_t* drafts,
+                                    std::size_t count, std::size_t max_draft,
+                                    std::size_t vocab, const std::uint32_t* targets,
+                                    std::size_t* accepted, std::uint32_t* committed,
+                                    std::size_t* committed_count, int* all_accepted) {
+    k3x::DraftProposal proposal{anchor, std::vector<std::uint32_t>(drafts, drafts + count)};
+    auto r = k3x::verify_greedy_target_block(proposal, max_draft, vocab,
+                                             {targets, count + 1});
+    if (!r) return code(r);
+    *accepted = r.value().accepted_draft_tokens;
+    *committed_count = r.value().committed_tokens.size();
+    std::copy(r.value().committed_tokens.begin(), r.value().committed_tokens.end(), committed);
+    *all_accepted = r.value().all_draft_tokens_accepted ? 1 : 0;
+    return 0;
+}
+
+typedef int (*k3xr_target_step_fn)(void* user, std::uint32_t input, std::uint32_t* output);
+
+int k3xr_verify_greedy_draft(std::uint32_t anchor, const std::uint32_t* drafts,
+                             std::size_t count, std::size_t max_draft, std::size_t vocab,
+                             k3xr_target_step_fn step, void* user, std::size_t* accepted,
+                             std::uint32_t* committed, std::size_t* committed_count,
+                             int* all_accepted) {
+    k3x::DraftProposal proposal{anchor, std::vector<std::uint32_t>(drafts, drafts + count)};
+    k3x::GreedyTargetStep target;
+    if (step) {
+        target = [step, user](std::uint32_t input) {
+            std::uint32_t out = 0;
+            int status = step(user, input, &out);
+            if (status) return k3x::Result<std::uint32_t>::failure(static_cast<ErrorCode>(status));
+            return k3x::Result<std::uint32_t>::success(out);
+        };
+    }
+    auto r = k3x::verify_greedy_draft(proposal, max_draft, vocab, target);
+    if (!r) return code(r);
+    *accepted = r.value().accepted_draft_tokens;
+    *committed_count = r.value().committed_tokens.size();
+    std::copy(r.value().committed_tokens.begin(), r.value().committed_tokens.end(), committed);
+    *all_accepted = r.value().all_draft_tokens_accepted ? 1 : 0;
+    return 0;
+}
+
+// One routed expert through the reference primitives used by expert_ffn
+// (official_moe.cpp:82-103): mxfp4_matmul, situ_glu, mxfp4_matmul, bf16 round.
+static int expert_ffn(const k3xr_moe_layer& L, std::size_t e, const float* x, float* y) {
+    const std::size_t H = L.hidden, I = L.inter;
+    auto gate = k3x::mxfp4_matmul({x, H}, bytes(L.gate_packed + e * I * H / 2, I * H / 2),
+                                  bytes(L.gate_scales + e * I * H / 32, I * H / 32), I, H, 32);
+    auto up = k3x::mxfp4_matmul({x, H}, bytes(L.up_packed + e * I * H / 2, I * H / 2),
+                                bytes(L.up_scales + e * I * H / 32, I * H / 32), I, H, 32);
+    if (!gate) return code(gate);
+    if (!up) return code(up);
+    std::vector<float> act(I);
+    if (L.activation == 1)
+        k3x::situ_glu(act, gate.value(), up.value(), L.situ_beta, linear(L.situ_linear_beta));
+    else
+        k3x::situ_glu(act, gate.value(), up.value(), 0x1p64F, std::nullopt);
+    auto down = k3x::mxfp4_matmul(act, bytes(L.down_packed + e * H * I / 2, H * I / 2),
+                                  bytes(L.down_scales + e * H * I / 32, H * I / 32), H, I, 32);
+    if (!down) return code(down);
+    for (std::size_t i = 0; i < H; ++i) y[i] = round_bf16(down.value()[i]);
+    return 0;
+}
+
+static int bf16_matvec(const float* x, const std::uint16_t* w, std::size_t rows,
+                       std::size_t cols, float* out) {
+    for (std::size_t r = 0; r < rows; ++r) {
+        double sum = 0.0;
+        for (std::size_t c = 0; c < cols; ++c)
+            sum += static_cast<double>(k3x::decode_bf16_word(w[r * cols + c])) * x[c];
+        out[r] = round_bf16(static_cast<float>(sum));
+    }
+    return 0;
+}
+
+// Plain (hidden-space) MoE layer composed of the reference's routing,
+// expert primitives and its slot-ordered combine rule
+// (official_moe.cpp:271-344 without the latent projections). Tokens
+// [token_begin, token_end) are processed with up to `threads` workers.
+int k3xr_moe_layer_forward(const k3xr_moe_layer* layer, const float* hidden,
+                           std::size_t token_begin, std::size_t token_end,
+                           float* out, std::uint32_t* ids, float* contributions,
+                           int threads) {
+    const auto& L = *layer;
+    const std::size_t H = L.hidden, K = L.top_k;
+    std::atomic<std::size_t> next{token_begin};
+    std::atomic<int> status{0};
+    auto worker = [&]() {
+        std::vector<float> y(K * H), mixed(H), shared(L.hidden);
+        std::vector<float> g(L.shared_inter), u(L.shared_inter), a(L.shared_inter);
+        for (;;) {
+            std::size_t t = next.fetch_add(1);
+            if (t >= token_end || status.load()) break;
+            const float* x = hidden + t * H;
+            int st = k3xr_route_official_moe(x, L.router, L.experts, H, L.correction, K,
+                                             ids + t * K, contributions + t * K, nullptr);
+            for (std::size_t s = 0; s < K && !st; ++s)
+                st = expert_ffn(L, ids[t * K + s], x, y.data() + s * H);
+            if (st) { status.store(st); break; }
+            std::fill(mixed.begin(), mixed.end(), 0.0F);
+            for (std::size_t s = 0; s < K; ++s)
+                for (std::size_t i = 0; i < H; ++i)
+                    mixed[i] += contributions[t * K + s] * y[s * H + i];
+            for (auto& v : mixed) v = round_bf16(v);
+            if (L.shared_gate) {
+                bf16_matvec(x, L.shared_gate, L.shared_inter, H, g.data());
+                bf16_matvec(x, L.shared_up, L.shared_inter, H, u.data());
+                if (L.activation == 1)
+                    k3x::situ_glu(a, g, u, L.situ_beta, linear(L.situ_linear_beta));
+                else
+                    k3x::situ_glu(a, g, u, 0x1p64F, std::nullopt);
+                bf16_matvec(a.data(), L.shared_down, H, L.shared_inter, shared.data());
+            } else {
+                std::fill(shared.begin(), shared.end(), 0.0F);
+            }
+            for (std::size_t i = 0; i < H; ++i) out[t * H + i] = round_bf16(mixed[i] + shared[i]);
+        }
+    };
+    if (threads < 1) threads = 1;
+    std::vector<std::thread> pool;
+    for (int i = 1; i < threads; ++i) pool.emplace_back(worker);
+    worker();
+    for (auto& th : pool) th.join();
+    return status.load();
+}
+
+struct k3xr_kda_weights {
+    std::size_t hidden, heads, head_dim, conv_width;
+    float eps, gate_lower_bound;
+    const std::uint16_t *q_proj, *k_proj, *v_proj;
+    const float *q_conv, *k_conv, *v_conv;
+    const std::uint16_t* f_a_proj;
+    const std::uint16_t* f_b_proj;
+    const float* a_log;
+    const float* dt_bias;
+    const std::uint16_t* b_proj;
+    const std::uint16_t* g_proj;
+    const float* o_norm;
+    const std::uint16_t* o_proj;
+};
+
+// official_kda_cpu over `tokens` positions; state arrays are updated in place.
+int k3xr_official_kda_cpu(const k3xr_kda_weights* w, const float* hidden,
+                          std::size_t tokens, std::uint16_t* conv_q,
+                          std::uint16_t* conv_k, std::uint16_t* conv_v,
+                          float* recurrent, float* out) {
+    const std::size_t H = w->hidden, h = w->heads, d = w->head_dim, P = h * d;
+    const std::size_t W = w->conv_width;
+    k3x::OfficialKdaConfig config{H, h, d, W, w->eps, w->gate_lower_bound};
+    auto mat = [](const std::uint16_t* p, std::size_t rows, std::size_t cols) {
+        return k3x::Bf16WeightView{{p, rows * cols}, rows, cols, 0};
+    };
+    k3x::OfficialKdaWeightsView view{
+        mat(w->q_proj, P, H), mat(w->k_proj, P, H), mat(w->v_proj, P, H),
+        {w->q_conv, P * W}, {w->k_conv, P * W}, {w->v_conv, P * W},
+        mat(w->f_a_proj, d, H), mat(w->f_b_proj, P, d),
+        {w->a_log, d}, {w->dt_bias, P},
+        mat(w->b_proj, h, H), mat(w->g_proj, P, H),
+        {w->o_norm, d}, mat(w->o_proj, H, P)};
+    const std::size_t hist = (W - 1) * P;
+    k3x::OfficialKdaState state{
+        std::vector<std::uint16_t>(conv_q, conv_q + hist),
+        std::vector<std::uint16_t>(conv_k, conv_k + hist),
+        std::vector<std::uint16_t>(conv_v, conv_v + hist),
+        std::vector<float>(recurrent, recurrent + h * d * d)};
+    auto r = k3x::official_kda_cpu({hidden, tokens * H}, view, state, config);
+    if (!r) return code(r);
+    const auto& s = r.value().state;
+    std::copy(s.conv_q.begin(), s.conv_q.end(), conv_q);
+    std::copy(s.conv_k.begin(), s.conv_k.end(), conv_k);
+    std::copy(s.conv_v.begin(), s.conv_v.end(), conv_v);
+    std::copy(s.recurrent_v_first.begin(), s.recurrent_v_first.end(), recurrent);
+    std::copy(r.value().output.begin(), r.value().output.end(), out);
+    return 0;
+}
+
+}  // extern "C"

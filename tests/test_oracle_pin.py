@@ -1,0 +1,371 @@
+"""Pins the C restatement (oracle/k3x_oracle.c) before anything is checked
+against it:
+  * against the reference's golden literals and known-answer tests
+    (tests/cpp/test_official_moe.cpp, test_expert_major.cpp,
+    test_speculative.cpp, reference/k3x_ref/fixtures.py), and
+  * bit for bit against the reference's own compiled CPU code
+    (oracle/_ref/libk3x_ref.so) on seeded random inputs.
+CPU only.
+"""
+import numpy as np
+import pytest
+
+from oracle import (ACT_SITU, ACT_SWIGLU, OracleError, bf16_normal, bf16_values, bf16_words,
+                    make_moe_layer)
+
+
+# ---------------------------------------------------------------- MXFP4 ----
+
+def test_mxfp4_known_answer(rs):
+    # reference/k3x_ref/fixtures.py:265 — 0x10 then zeros, scale 127, 1x32
+    packed = np.array([0x10] + [0] * 15, np.uint8)
+    out = rs.decode_mxfp4(packed, np.array([127], np.uint8), 1, 32)
+    assert out[0, 0] == 0.0 and out[0, 1] == 0.5 and not out[0, 2:].any()
+
+
+def test_mxfp4_reserved_scale_rejected(rs):
+    # ops.cpp:46-48: scale byte 0xFF is reserved
+    packed = np.zeros(16, np.uint8)
+    with pytest.raises(OracleError) as e:
+        rs.decode_mxfp4(packed, np.array([0xFF], np.uint8), 1, 32)
+    assert e.value.status == 15
+    with pytest.raises(OracleError):
+        rs.mxfp4_matmul(np.zeros(32, np.float32), packed, np.array([0xFF], np.uint8), 1, 32)
+
+
+def test_mxfp4_bad_extent_rejected(rs):
+    with pytest.raises(OracleError):
+        rs.decode_mxfp4(np.zeros(8, np.uint8), np.zeros(1, np.uint8), 1, 17, 17)
+
+
+def test_mxfp4_decode_and_matmul_match_reference(rs, ref):
+    g = np.random.default_rng(11)
+    rows, cols = 48, 256
+    packed = g.integers(0, 256, size=rows * cols // 2, dtype=np.uint8)
+    scales = g.integers(100, 140, size=rows * cols // 32, dtype=np.uint8)
+    x = g.normal(size=cols).astype(np.float32)
+    np.testing.assert_array_equal(rs.decode_mxfp4(packed, scales, rows, cols),
+                                  ref.decode_mxfp4(packed, scales, rows, cols))
+    np.testing.assert_array_equal(rs.mxfp4_matmul(x, packed, scales, rows, cols),
+                                  ref.mxfp4_matmul(x, packed, scales, rows, cols))
+
+
+def test_quantizer_roundtrip_bounds(rs):
+    g = np.random.default_rng(3)
+    w = g.normal(0, 0.02, size=(64, 256)).astype(np.float32)
+    packed, scales = rs.quantize_mxfp4(w)
+    dec = rs.decode_mxfp4(packed, scales, 64, 256)
+    blocks = np.abs(w).reshape(64, 8, 32).max(axis=2)
+    step = np.ldexp(1.0, scales.astype(np.int32) - 127)           # 2^s
+    # amax <= 6 * 2^s and not representable one exponent lower
+    assert np.all(blocks <= 6 * step) and np.all(blocks > 3 * step)
+    # error at most half the coarsest grid spacing (2 * 2^s) per block
+    err = np.abs(dec - w).reshape(64, 8, 32).max(axis=2)
+    assert np.all(err <= step)
+
+
+def test_e2m1_terms_exact_decomposition(rs):
+    g = np.random.default_rng(5)
+    for scale in (1.0, 1e-3, 37.0):
+        x = (g.normal(size=32) * scale).astype(np.float32)
+        for nterms in (1, 2, 4, 6, 8):
+            packed, scales, res = rs.e2m1_terms(x, nterms)
+            recon = np.zeros(32, np.float64)
+            for t in range(nterms):
+                recon += rs.decode_mxfp4(packed[t], scales[t:t + 1], 1, 32)[0].astype(np.float64)
+            resid = np.abs(x.astype(np.float64) - recon).max()
+            assert resid == pytest.approx(res, rel=0, abs=0)
+            # each term removes at least two bits of the block maximum
+            assert resid <= np.abs(x).max() * 2.0 ** (-2 * nterms + 1)
+
+
+# ---------------------------------------------------------- activations ----
+
+def test_situ_glu_matches_reference(rs, ref):
+    g = np.random.default_rng(7)
+    gate = (g.normal(size=1000) * 4).astype(np.float32)
+    up = (g.normal(size=1000) * 40).astype(np.float32)
+    np.testing.assert_array_equal(rs.situ_glu(gate, up, 4.0, 25.0), ref.situ_glu(gate, up, 4.0, 25.0))
+    np.testing.assert_array_equal(rs.situ_glu(gate, up, 4.0), ref.situ_glu(gate, up, 4.0))
+
+
+def test_swiglu_is_situ_limit(rs, ref):
+    # SwiGLU = situ_glu(beta = 2^64, no linear bound), bit for bit
+    g = np.random.default_rng(8)
+    gate = (g.normal(size=4096) * 3).astype(np.float32)
+    up = g.normal(size=4096).astype(np.float32)
+    np.testing.assert_array_equal(rs.swiglu(gate, up), ref.situ_glu(gate, up, 2.0 ** 64))
+
+
+def test_situ_literal(rs):
+    # fixtures.py:263 situ_glu([[-1, 2]], [[3, 4]], 1, 1) — recomputed here in float64
+    gate = np.array([-1.0, 2.0], np.float32)
+    up = np.array([3.0, 4.0], np.float32)
+    out = rs.situ_glu(gate, up, 1.0, 1.0)
+    sig = 1 / (1 + np.exp(-gate.astype(np.float64)))
+    expect = np.tanh(gate) * sig * np.tanh(up)
+    np.testing.assert_allclose(out, expect, rtol=1e-6)
+
+
+# --------------------------------------------------------------- router ----
+
+ROUTER = np.array([0x3F80, 0x0000, 0x0000, 0x3F80, 0xBF80, 0x3F80], np.uint16).reshape(3, 2)
+CORRECTION = np.array([0.0, 0.1, -0.05], np.float32)
+HIDDEN = np.array([1.2578125, -0.32421875], np.float32)
+
+
+def test_route_literals(rs):
+    # test_official_moe.cpp:86-91
+    ids, contrib = rs.route(HIDDEN, ROUTER, CORRECTION, 2)
+    assert ids.tolist() == [0, 1]
+    assert abs(contrib[0] - 0.6497964859) <= 1e-6 and abs(contrib[1] - 0.3502035439) <= 1e-6
+    # :92-100 logits entry point gives identical ids/scores/contributions
+    logits = np.array([1.2578125, -0.32421875, -1.58203125], np.float32)
+    ids2, c2, s2 = rs.route_logits(logits, CORRECTION, 2, want_scores=True)
+    assert ids2.tolist() == ids.tolist() and np.array_equal(c2, contrib)
+    # :101-109 ties break to the lower index
+    ids3, c3, s3 = rs.route_logits(np.zeros(3, np.float32), np.zeros(3, np.float32), 2,
+                                   want_scores=True)
+    assert ids3.tolist() == [0, 1] and s3.tolist() == [0.5] * 3 and c3.tolist() == [0.5, 0.5]
+
+
+@pytest.mark.parametrize("logits,corr,k", [
+    ([0.0, np.inf, 0.0], [0, 0, 0], 2),       # non-finite logit
+    ([0.0, 0.0, 0.0], [0, 0, 0], 0),          # top_k == 0
+    ([0.0, 0.0, 0.0], [0, 0, 0], 4),          # top_k > experts
+    ([-3.4028235e38] * 3, [0, 0, 0], 2),      # zero mass
+])
+def test_route_rejects(rs, logits, corr, k):
+    # test_official_moe.cpp:110-127
+    with pytest.raises(OracleError):
+        rs.route_logits(np.array(logits, np.float32), np.array(corr, np.float32), k)
+
+
+def test_route_matches_reference_random(rs, ref):
+    g = np.random.default_rng(12)
+    E, H, K = 64, 512, 8
+    router = bf16_words(g.normal(0, 0.02, size=(E, H)))
+    corr = g.normal(0, 0.02, size=E).astype(np.float32)
+    for _ in range(20):
+        x = bf16_normal(g, H)
+        a = rs.route(x, router, corr, K)
+        b = ref.route(x, router, corr, K)
+        assert a[0].tolist() == b[0].tolist()
+        np.testing.assert_array_equal(a[1], b[1])
+
+
+# ---------------------------------------------------------- bucketing ----
+
+def test_expert_major_known_answers(rs):
+    # test_expert_major.cpp:24-51
+    plan = rs.expert_major_plan(np.array([[2, 1], [1, 3]]), np.array([[0.6, 0.4], [0.7, 0.3]]))
+    assert plan["group_expert"].tolist() == [2, 1, 3]
+    assert plan["group_offset"].tolist() == [0, 1, 3, 4]
+    assert plan["assign_token"].tolist() == [0, 0, 1, 1]
+    assert plan["assign_slot"].tolist() == [0, 1, 0, 1]
+    assert plan["assign_contrib"].tolist() == pytest.approx([0.6, 0.4, 0.7, 0.3])
+    # :52-62
+    plan = rs.expert_major_plan(np.array([[4], [5]]), np.array([[1.0], [1.0]]))
+    assert plan["group_expert"].tolist() == [4, 5]
+
+
+@pytest.mark.parametrize("ids,contrib,status", [
+    ([[1, 1]], [[0.5, 0.5]], 16),                 # duplicate expert (:81-86)
+    ([[1]], [[np.nan]], 16),                      # NaN contribution (:87-93)
+    ([[1]], [[np.inf]], 16),                      # Inf contribution (:94-100)
+])
+def test_expert_major_rejects(rs, ids, contrib, status):
+    with pytest.raises(OracleError) as e:
+        rs.expert_major_plan(np.array(ids), np.array(contrib, np.float32))
+    assert e.value.status == status
+
+
+def test_expert_major_matches_reference_random(rs, ref):
+    g = np.random.default_rng(13)
+    T, E, K = 64, 384, 16
+    ids = np.stack([g.choice(E, K, replace=False) for _ in range(T)]).astype(np.uint32)
+    con = g.random(size=(T, K)).astype(np.float32)
+    a = rs.expert_major_plan(ids, con)
+    b = ref.expert_major_plan(ids.tolist(), con.tolist())
+    for key in a:
+        np.testing.assert_array_equal(a[key], b[key])
+
+
+# ---------------------------------------------------- expert FFN literals --
+
+def test_official_expert_literals(rs):
+    # test_official_moe.cpp:57-63 and :134-136 — 2x2 experts, group 2, SiTU(4, 25)
+    latent = HIDDEN
+    scales = np.array([127, 127], np.uint8)
+    experts = {0: ([0x12, 0x21], [0x22, 0x31], [0x12, 0x21]),
+               1: ([0x21, 0x12], [0x12, 0x23], [0x12, 0x12])}
+    expect = {0: [0.76171875, 0.3984375], 1: [0.81640625, 0.81640625]}
+    outs = []
+    for e, (gp, up, dp) in experts.items():
+        gate = rs.mxfp4_matmul(latent, np.array(gp, np.uint8), scales, 2, 2, 2)
+        upv = rs.mxfp4_matmul(latent, np.array(up, np.uint8), scales, 2, 2, 2)
+        act = rs.situ_glu(gate, upv, 4.0, 25.0)
+        y = rs.round_bf16(rs.mxfp4_matmul(act, np.array(dp, np.uint8), scales, 2, 2, 2))
+        assert np.abs(y - expect[e]).max() <= 1e-6
+        outs.append(y)
+    # :136 mixed_latent
+    _, contrib = rs.route(HIDDEN, ROUTER, CORRECTION, 2)
+    mixed = rs.routed_combine(np.stack(outs), contrib)
+    assert np.abs(mixed - [0.78125, 0.54296875]).max() <= 1e-6
+
+
+def test_moe_layer_matches_reference_random(rs, ref):
+    for act in (ACT_SWIGLU, ACT_SITU):
+        layer = make_moe_layer(rs, 21 + act, hidden=128, inter=64, experts=12, top_k=4,
+                               shared_inter=64, activation=act)
+        x = bf16_normal(np.random.default_rng(22), (6, 128))
+        a = rs.moe_layer(layer, x)
+        b = ref.moe_layer(layer, x, threads=2)
+        for u, v in zip(a, b):
+            np.testing.assert_array_equal(u, v)
+
+
+# ------------------------------------------------------------------ KDA ----
+
+def _kda_weights(g, H, h, d, W=4):
+    P = h * d
+    n = lambda *s: bf16_words(g.normal(0, 0.1, size=s))
+    return dict(hidden=H, heads=h, head_dim=d, conv_width=W, eps=1e-5, gate_lower_bound=-5.0,
+                q_proj=n(P, H), k_proj=n(P, H), v_proj=n(P, H),
+                q_conv=g.normal(0, 0.5, size=(P, W)).astype(np.float32),
+                k_conv=g.normal(0, 0.5, size=(P, W)).astype(np.float32),
+                v_conv=g.normal(0, 0.5, size=(P, W)).astype(np.float32),
+                f_a_proj=n(d, H), f_b_proj=n(P, d),
+                a_log=g.normal(0, 0.3, size=d).astype(np.float32),
+                dt_bias=g.normal(0, 0.3, size=P).astype(np.float32),
+                b_proj=n(h, H), g_proj=n(P, H),
+                o_norm=(1 + g.normal(0, 0.1, size=d)).astype(np.float32), o_proj=n(H, P))
+
+
+def test_kda_block_matches_reference(rs, ref):
+    g = np.random.default_rng(31)
+    H, h, d, W = 64, 2, 16, 4
+    w = _kda_weights(g, H, h, d, W)
+    P = h * d
+    state = [np.zeros((W - 1) * P, np.uint16)] * 3 + [np.zeros(h * d * d, np.float32)]
+    for _ in range(2):   # two chunks: the second continues from the first's state
+        x = g.normal(size=(5, H)).astype(np.float32)
+        a_out, a_state = rs.kda_block(w, x, *state)
+        b_out, b_state = ref.kda_block(w, x, *state)
+        np.testing.assert_array_equal(a_out, b_out)
+        for u, v in zip(a_state, b_state):
+            np.testing.assert_array_equal(u, v)
+        state = list(a_state)
+
+
+def test_kda_tree_linear_chain_equals_steps(rs):
+    g = np.random.default_rng(33)
+    h, d, n = 2, 8, 5
+    s0 = g.normal(0, 0.1, size=(h, d, d)).astype(np.float32)
+    q, k, v = (g.normal(size=(n, h * d)).astype(np.float32) for _ in range(3))
+    ld = -np.abs(g.normal(size=(n, h * d))).astype(np.float32)
+    be = g.random(size=(n, h)).astype(np.float32)
+    out, states = rs.kda_tree(s0, np.arange(-1, n - 1), q, k, v, ld, be, h, d, want_states=True)
+    s = s0
+    for i in range(n):
+        s, o = rs.kda_step(s, q[i], k[i], v[i], ld[i], be[i], h, d)
+        np.testing.assert_array_equal(o, out[i])
+        np.testing.assert_array_equal(s, states[i])
+
+
+def test_kda_tree_rejects_forward_parent(rs):
+    with pytest.raises(OracleError):
+        z = np.zeros((2, 8), np.float32)
+        rs.kda_tree(np.zeros((1, 8, 8), np.float32), np.array([-1, 1]), z, z, z, z,
+                    np.zeros((2, 1), np.float32), 1, 8)
+
+
+# ----------------------------------------------------------- acceptance ----
+
+@pytest.mark.parametrize("anchor,drafts,maxd,targets,expect", [
+    (10, [11, 12], 2, [11, 12, 13], (2, [11, 12, 13], True)),        # test_speculative.cpp:155-165
+    (10, [99, 100], 2, [11, 12, 13], (0, [11], False)),             # :166-176
+    (10, [11, 99], 2, [11, 12, 13], (1, [11, 12], False)),          # :177-187
+    (10, [11, 12, 99], 3, [11, 12, 13, 14], (2, [11, 12, 13], False)),  # :188-199
+    (10, [], 0, [11], (0, [11], True)),                              # :200-209
+])
+def test_greedy_block_known_answers(rs, ref, anchor, drafts, maxd, targets, expect):
+    got = rs.verify_greedy_block(anchor, np.array(drafts, np.uint32), maxd, 128,
+                                 np.array(targets, np.uint32))
+    assert got == expect
+    assert ref.verify_greedy_block(anchor, np.array(drafts, np.uint32), maxd, 128,
+                                   np.array(targets, np.uint32)) == expect
+
+
+@pytest.mark.parametrize("anchor,drafts,maxd,status", [
+    (10, [11, 12], 1, 9),     # too many drafts (invalid_extent)
+    (128, [], 0, 9),          # anchor out of vocabulary
+    (10, [128], 1, 9),        # draft out of vocabulary
+])
+def test_greedy_block_rejects(rs, anchor, drafts, maxd, status):
+    with pytest.raises(OracleError) as e:
+        rs.verify_greedy_block(anchor, np.array(drafts, np.uint32), maxd, 128,
+                               np.arange(11, 11 + len(drafts) + 1, dtype=np.uint32))
+    assert e.value.status == status
+
+
+def test_greedy_block_target_out_of_vocab(rs):
+    # :235-242 target token >= vocabulary -> invalid_state
+    with pytest.raises(OracleError) as e:
+        rs.verify_greedy_block(10, np.array([11], np.uint32), 1, 128, np.array([11, 128], np.uint32))
+    assert e.value.status == 16
+
+
+def test_greedy_block_equals_token_major(ref):
+    # verify_greedy_draft (token-major, target callback) and the block form agree
+    g = np.random.default_rng(41)
+    V = 50
+    table = g.integers(0, V, size=V)
+    for _ in range(50):
+        anchor = int(g.integers(V))
+        p = int(g.integers(0, 6))
+        drafts = g.integers(0, V, size=p).astype(np.uint32)
+        # make some prefixes accepted
+        tok = anchor
+        for i in range(p):
+            if g.random() < 0.6:
+                drafts[i] = table[tok]
+            tok = drafts[i]
+        targets = [int(table[anchor])] + [int(table[t]) for t in drafts]
+        a = ref.verify_greedy_draft(anchor, drafts, p, V, lambda t: (0, int(table[t])))
+        b = ref.verify_greedy_block(anchor, drafts, p, V, np.array(targets, np.uint32))
+        assert a == b
+
+
+def test_argmax_first_maximum(rs):
+    x = np.array([1.0, 3.0, 2.0, 3.0], np.float32)
+    assert rs.argmax(x) == 1
+
+
+def test_rejection_sampling_distribution(rs):
+    # The residual rule makes the committed token at the first position
+    # distributed as p, whatever q is: check empirically on a tiny vocab.
+    V = 6
+    g = np.random.default_rng(51)
+    tl = g.normal(size=(2, V)).astype(np.float32)
+    dl = g.normal(size=(1, V)).astype(np.float32)
+    p = np.exp(tl[0] - tl[0].max()); p /= p.sum()
+    q = np.exp(dl[0] - dl[0].max()); q /= q.sum()
+    counts = np.zeros(V)
+    n = 6000
+    for s in range(n):
+        d = int(g.choice(V, p=q))
+        _, com = rs.verify_rejection(tl, dl, np.array([d], np.uint32), 1.0, 1234, s)
+        counts[com[0]] += 1
+    assert np.abs(counts / n - p).max() < 0.03
+
+
+def test_rejection_deterministic(rs):
+    g = np.random.default_rng(52)
+    V = 300
+    tl = g.normal(size=(4, V)).astype(np.float32)
+    dl = g.normal(size=(3, V)).astype(np.float32)
+    d = np.array([int(np.argmax(tl[i])) for i in range(3)], np.uint32)
+    a = rs.verify_rejection(tl, dl, d, 1.0, 9, 3)
+    b = rs.verify_rejection(tl, dl, d, 1.0, 9, 3)
+    assert a == b and 1 <= len(a[1]) <= 4
