@@ -1,0 +1,408 @@
+"""Benchmark of the B200 speculative-verification path (driver contract).
+
+Workload ("c2"): one released-shape MoE layer,
+expert-major verification of 64 verify tokens (8 sequences x 8 drafts):
+hidden 7168, 384 routed experts + 1 shared (SwiGLU, intermediate 2048),
+Top-16 sigmoid router with per-expert bias, experts MXFP4 from N(0, 0.02),
+hidden states bf16 N(0, 1), seed 1. Synthetic data generated on the GPU.
+
+A step = route -> expert-major plan -> grouped expert FFN -> slot-ordered
+combine + shared expert, for all 64 tokens (one KDA+MoE layer's MoE half;
+the metric is tokens verified per step / step time x layers).
+
+`value` times the device entry point with inputs resident in HBM; `e2e`
+times k3xb_moe_layer_forward_host (pinned host hidden in, output + routes
+out, copies inside the timed region). Every step streams ~8.4 GB of expert
+weights, far above the 126 MB L2, so no flush is needed.
+
+--impl reference times the reference's own CPU code (oracle/_ref, compiled
+from the reference sources) on a bounded sample of the same tokens using all
+host threads.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "project-k3x_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+METRIC = "verified draft tokens/s per KDA+MoE layer"
+C2 = dict(hidden=7168, inter=2048, experts=384, top_k=16, shared_inter=2048, tokens=64, seed=1,
+          sequences=8, drafts=8)
+EXPERT_BYTES = 3 * 7168 * 2048 * (0.5 + 1 / 32)   # S_e = 23,396,352 B per expert
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """Samples nvidia-smi during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._thread.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 5 + i and s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def dist_setup(n_gpus):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def make_c2_layer(ctx, torch, cfg, engine, act_terms):
+    import k3xb
+    H, I, E, Is = cfg["hidden"], cfg["inter"], cfg["experts"], cfg["shared_inter"]
+    seed = cfg["seed"]
+    u8 = lambda *s: torch.empty(s, dtype=torch.uint8, device="cuda")
+    w = dict(hidden=H, inter=I, experts=E, top_k=cfg["top_k"], shared_inter=Is,
+             activation=k3xb.ACT_SWIGLU)
+    w["gate_packed"], w["gate_scales"] = u8(E, I, H // 2), u8(E, I, H // 32)
+    w["up_packed"], w["up_scales"] = u8(E, I, H // 2), u8(E, I, H // 32)
+    w["down_packed"], w["down_scales"] = u8(E, H, I // 2), u8(E, H, I // 32)
+    ctx.fill_normal_mxfp4(w["gate_packed"], w["gate_scales"], E * I, H, seed, 10, 0.02)
+    ctx.fill_normal_mxfp4(w["up_packed"], w["up_scales"], E * I, H, seed, 11, 0.02)
+    ctx.fill_normal_mxfp4(w["down_packed"], w["down_scales"], E * H, I, seed, 12, 0.02)
+    w["router"] = torch.empty((E, H), dtype=torch.int16, device="cuda")
+    ctx.fill_normal_bf16(w["router"], seed, 20, 0.02)
+    w["correction"] = torch.empty(E, dtype=torch.float32, device="cuda")
+    ctx.fill_normal_f32(w["correction"], seed, 21, 0.0, 0.02)
+    for i, name in enumerate(("shared_gate", "shared_up")):
+        w[name] = torch.empty((Is, H), dtype=torch.int16, device="cuda")
+        ctx.fill_normal_bf16(w[name], seed, 22 + i, 0.02)
+    w["shared_down"] = torch.empty((H, Is), dtype=torch.int16, device="cuda")
+    ctx.fill_normal_bf16(w["shared_down"], seed, 24, 0.02)
+    words = torch.empty((cfg["tokens"], H), dtype=torch.int16, device="cuda")
+    ctx.fill_normal_bf16(words, seed, 30, 1.0)
+    hidden = (words.to(torch.int32) << 16).view(torch.float32).contiguous()
+    if engine == k3xb.ENGINE_MXF4:
+        ctx.prepare_layer_scales(w)   # one-time tcgen05 scale layout of the resident weights
+    desc = k3xb.moe_layer_desc(w, engine=engine, act_terms=act_terms)
+    return w, desc, hidden
+
+
+def run_ours(args):
+    import torch
+
+    import k3xb
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    cfg = dict(C2)
+    ctx = k3xb.Context(local)
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
+    ctx.use_stream(stream)
+    engine = k3xb.ENGINE_SIMT if args.engine == "simt" else k3xb.ENGINE_MXF4
+    w, desc, hidden = make_c2_layer(ctx, torch, cfg, engine, args.act_terms)
+    T, H, K, E = cfg["tokens"], cfg["hidden"], cfg["top_k"], cfg["experts"]
+    out = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    con = torch.empty((T, K), dtype=torch.float32, device="cuda")
+
+    def step():
+        ctx.moe_layer_forward(desc, hidden, out, ids, con)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    # unique experts of this workload (for the algorithmic byte count)
+    unique = int(torch.unique(ids).numel())
+
+    barrier(world)
+    torch.cuda.synchronize()
+    launches0 = ctx.stats()["kernel_launches"]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = ctx.stats()["kernel_launches"] - launches0
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_max = max_over_ranks(ms, world)
+    barrier(world)
+
+    # dominant kernel(s): the grouped expert FFN, timed alone on the same stream
+    plan = dict(group_expert=torch.empty(E, dtype=torch.int32, device="cuda"),
+                group_offset=torch.empty(E + 1, dtype=torch.int32, device="cuda"),
+                assign_token=torch.empty(T * K, dtype=torch.int32, device="cuda"),
+                assign_slot=torch.empty(T * K, dtype=torch.int32, device="cuda"),
+                assign_contrib=torch.empty(T * K, dtype=torch.float32, device="cuda"),
+                group_count=torch.empty(1, dtype=torch.int32, device="cuda"),
+                status=torch.zeros(1, dtype=torch.int32, device="cuda"))
+    ctx.expert_major_plan(ids, con, E, plan)
+    slot_out = torch.empty((T * K, H), dtype=torch.float32, device="cuda")
+    pl = k3xb.Plan(*(k3xb._p(plan[k]) for k in ("group_expert", "group_offset", "assign_token",
+                                                  "assign_slot", "assign_contrib", "group_count", "status")))
+    import ctypes as C
+
+    def experts():
+        ctx._check(ctx.lib.k3xb_moe_experts(ctx.h, C.byref(desc), k3xb._p(hidden), T, C.byref(pl),
+                                            k3xb._p(slot_out)), "moe_experts")
+
+    for _ in range(2):
+        experts()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(3, args.steps)
+    e0.record(stream)
+    for _ in range(reps):
+        experts()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    exp_ms = e0.elapsed_time(e1) / reps
+    alg_bytes = unique * EXPERT_BYTES + T * H * 2 + T * H * 4
+    hbm, peak_kind = peaks()
+    achieved = alg_bytes / (exp_ms * 1e-3) / 1e9
+
+    # e2e through the host-buffer C-ABI entry point (pinned host memory)
+    h_host = hidden.cpu().pin_memory()
+    o_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    i_host = torch.empty((T, K), dtype=torch.int32).pin_memory()
+    c_host = torch.empty((T, K), dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        ctx.moe_layer_forward_host(desc, h_host, o_host, i_host, c_host)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(args.steps):
+        ctx.moe_layer_forward_host(desc, h_host, o_host, i_host, c_host)
+    s1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(s0.elapsed_time(s1) / args.steps, world)
+    wall_e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+
+    total_tokens = sum_over_ranks(T, world)
+    result = {
+        "metric": METRIC,
+        "value": total_tokens / (ms_max * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_max,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "mxfp4 weights (e2m1+e8m0) x e2m1-term activations, fp32 accumulate",
+        "data": "synthetic (seeded, generated on the GPU)",
+        "config": {"workload": "c2: single released-shape MoE layer, expert-major verify",
+                   "hidden": H, "experts": E, "top_k": K, "inter": cfg["inter"],
+                   "shared_inter": cfg["shared_inter"], "verify_tokens": T,
+                   "sequences_x_drafts": "8x8", "layers": 1, "engine": args.engine,
+                   "act_terms": args.act_terms if args.engine == "mxf4" else None,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "no flush: each step streams ~8.4 GB of expert weights (>> 126 MB L2)"},
+        "e2e": {"value": total_tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4 + 2 * T * K * 4,
+                "wall_ms_per_step": wall_e2e_ms},
+        "roofline": {"bound": "hbm", "kernel": f"expert FFN ({args.engine})", "achieved": achieved,
+                     "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                     "alg_bytes_per_launch": alg_bytes, "unique_experts": unique,
+                     "launch_ms": exp_ms, "traffic": None},
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(w, hidden, cfg, args)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def host_layer(w, cfg):
+    """Copies the device-generated layer to host numpy for the CPU reference."""
+    import numpy as np
+    L = dict(hidden=cfg["hidden"], inter=cfg["inter"], experts=cfg["experts"], top_k=cfg["top_k"],
+             shared_inter=cfg["shared_inter"], activation=0, situ_beta=4.0, situ_linear_beta=0.0)
+    for k in ("gate_packed", "gate_scales", "up_packed", "up_scales", "down_packed", "down_scales"):
+        L[k] = w[k].cpu().numpy()
+    for k in ("router", "shared_gate", "shared_up", "shared_down"):
+        L[k] = w[k].cpu().numpy().view(np.uint16)
+    L["correction"] = w["correction"].cpu().numpy()
+    return L
+
+
+def cpu_sample_tokens(cores):
+    # ~7.7 s of single-core work per token at c2 (48 matvecs of 2048x7168)
+    return max(1, min(64, cores))
+
+
+def cpu_baseline(w, hidden, cfg, args):
+    import numpy as np
+
+    from oracle import Reference, have_reference
+    if not have_reference():
+        return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
+                "sample": "unavailable: oracle/_ref not built"}
+    ref = Reference()
+    L = host_layer(w, cfg)
+    x = hidden.cpu().numpy()
+    cores = max(1, os.cpu_count() or 1)
+    n = cpu_sample_tokens(cores)
+    t0 = time.perf_counter()
+    ref.moe_layer(L, x, 0, n, threads=cores)
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": "reference",
+            "sample": f"{n} of the 64 c2 tokens through the reference CPU functions "
+                      f"(route_official_moe, mxfp4_matmul, situ_glu) on {cores} threads, {dt:.1f} s"}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU implementation of the path."""
+    import numpy as np
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import Reference, have_reference, make_moe_layer  # noqa: F401
+    if not have_reference():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libk3x_ref.so was not built"}))
+        return
+    import torch
+
+    import k3xb
+    cfg = dict(C2)
+    # same synthetic workload as our arm (generated with the same seeds)
+    ctx = k3xb.Context(0)
+    ctx.use_stream()
+    w, desc, hidden = make_c2_layer(ctx, torch, cfg, k3xb.ENGINE_SIMT, 6)
+    torch.cuda.synchronize()
+    L = host_layer(w, cfg)
+    x = hidden.cpu().numpy()
+    del w
+    ref = Reference()
+    cores = max(1, os.cpu_count() or 1)
+    n = cpu_sample_tokens(cores)
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        ref.moe_layer(L, x, 0, n, threads=cores)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    dt = statistics.mean(times)
+    value = n / dt
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 64 / value * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32/fp64 (reference CPU)", "data": "synthetic (same seeds as our arm)",
+        "config": {"workload": "c2: single released-shape MoE layer, expert-major verify",
+                   "hidden": cfg["hidden"], "experts": cfg["experts"], "top_k": cfg["top_k"],
+                   "inter": cfg["inter"], "verify_tokens": cfg["tokens"], "layers": 1},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "reference",
+                         "sample": f"{n} of 64 tokens per step on {cores} threads"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--engine", choices=["mxf4", "simt"], default=os.environ.get("K3XB_ENGINE", "mxf4"))
+    ap.add_argument("--act-terms", type=int, default=6)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

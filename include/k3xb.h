@@ -1,0 +1,231 @@
+/*
+ * k3xb.h — C ABI of the B200-native K3X speculative-verification library
+ * (libk3xb.so, built from project-k3x_b200/csrc for sm_100a).
+ *
+ * Plain pointers and sizes only. Unless a name ends in _host, every array
+ * argument is DEVICE memory on the context's GPU and the call is
+ * asynchronous on the context's current stream (k3xb_set_stream). All
+ * entry points return a status that mirrors k3x::ErrorCode
+ * (runtime/include/k3x/status.hpp:9-30); k3xb_last_error() gives the
+ * message of the last failure on a context. There is no CPU fallback: a
+ * missing or unsupported device returns K3XB_BACKEND_UNAVAILABLE or
+ * K3XB_UNSUPPORTED_ARCHITECTURE.
+ *
+ * Each entry point names the reference interface it replaces. The C++20
+ * adapter (project-k3x_b200/cpp/b200_backend.cpp) maps k3x::ComputeBackend
+ * (runtime/include/k3x/backend.hpp:326-462) and the free verification
+ * functions onto these calls.
+ */
+#ifndef K3XB_H
+#define K3XB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes: runtime/include/k3x/status.hpp:9-30 ---------------- */
+enum {
+    K3XB_OK = 0,
+    K3XB_INVALID_EXTENT = 9,
+    K3XB_INVALID_MXFP4 = 15,
+    K3XB_INVALID_STATE = 16,
+    K3XB_BACKEND_UNAVAILABLE = 17,
+    K3XB_UNSUPPORTED_ARCHITECTURE = 19,
+};
+
+/* Expert / shared-expert activation. SwiGLU is situ_glu's beta -> inf limit
+ * without a linear bound; SiTU is runtime/src/ops.cpp:20-30. */
+enum { K3XB_ACT_SWIGLU = 0, K3XB_ACT_SITU = 1 };
+
+/* Expert GEMM engine. MXF4 = tcgen05 block-scaled kind::mxf4 tensor cores
+ * (E2M1 weights and activation terms, E8M0 per-32 scales, TMEM
+ * accumulators); SIMT = CUDA-core FP4 decode + FP32 FMA (cross-check). */
+enum { K3XB_ENGINE_MXF4 = 0, K3XB_ENGINE_SIMT = 1 };
+
+typedef struct k3xb_ctx k3xb_ctx;
+
+/* ---- context ------------------------------------------------------------ */
+/* Replaces make_cuda_backend (runtime/include/k3x/backend.hpp:465-466):
+ * requires compute capability 10.x (B200) and returns
+ * K3XB_UNSUPPORTED_ARCHITECTURE otherwise. */
+int k3xb_create(int device, k3xb_ctx** out);
+int k3xb_destroy(k3xb_ctx* ctx);
+/* Copies the last error message (NUL-terminated, truncated to len). */
+int k3xb_last_error(const k3xb_ctx* ctx, char* buf, size_t len);
+/* Stream for subsequent calls (a cudaStream_t); NULL = the context's own
+ * non-blocking stream (backend_cuda.cu:5344-5348 keeps one stream too). */
+int k3xb_set_stream(k3xb_ctx* ctx, void* stream);
+int k3xb_sync(k3xb_ctx* ctx);
+
+/* Counters in the spirit of k3x::BackendRuntimeStats (backend.hpp:50-129). */
+typedef struct {
+    uint64_t kernel_launches;
+    uint64_t route_calls;
+    uint64_t moe_layer_calls;
+    uint64_t moe_layer_experts;
+    uint64_t kda_calls;
+    uint64_t accept_calls;
+    uint64_t scratch_bytes;
+    uint64_t peak_scratch_bytes;
+    uint64_t h2d_bytes;
+    uint64_t d2h_bytes;
+} k3xb_stats;
+int k3xb_get_stats(const k3xb_ctx* ctx, k3xb_stats* out);
+
+/* ---- (a) router ---------------------------------------------------------- */
+/* route_official_moe (runtime/src/official_moe.cpp:247-269) for T tokens:
+ * logits = float(sum_h double(bf16 W[e][h]) * hidden[t][h]) summed in h
+ * order (bit-identical to the reference), scores = sigmoid, Top-k by
+ * (score + correction) desc / index asc, contributions = score / double
+ * sum. ids/contributions are [T][k]; scores [T][E] may be NULL. */
+int k3xb_route(k3xb_ctx* ctx, const float* hidden, uint32_t tokens,
+               uint32_t hidden_size, const uint16_t* router,
+               const float* correction, uint32_t experts, uint32_t top_k,
+               uint32_t* ids, float* contributions, float* scores);
+
+/* build_expert_major_plan (runtime/src/expert_major.cpp:10-54): groups in
+ * first-use order, assignments in (token, slot) order inside a group.
+ * group_offset has room for experts+1 entries; the used prefix is
+ * group_count[0]+1. Duplicate ids in a token or non-finite contributions
+ * set status[0] = K3XB_INVALID_STATE (device-side; read it after sync). */
+typedef struct {
+    uint32_t* group_expert;    /* [experts] */
+    uint32_t* group_offset;    /* [experts + 1] */
+    uint32_t* assign_token;    /* [T * k] */
+    uint32_t* assign_slot;     /* [T * k] */
+    float* assign_contrib;     /* [T * k] */
+    uint32_t* group_count;     /* [1] */
+    int32_t* status;           /* [1] */
+} k3xb_plan;
+int k3xb_expert_major_plan(k3xb_ctx* ctx, const uint32_t* ids,
+                           const float* contributions, uint32_t tokens,
+                           uint32_t top_k, uint32_t experts,
+                           const k3xb_plan* plan);
+
+/* ---- (b)+(c) resident MoE layer ----------------------------------------- */
+/* Plain (hidden-space) MoE layer over device-resident weights: route ->
+ * expert-major plan -> grouped expert FFN -> slot-ordered weighted combine
+ * -> + shared expert. Replaces resident_mxfp4_moe_layer /
+ * official_mxfp4_moe_ffn (backend.hpp:369-397; official_moe.cpp:271-344
+ * without the latent projections). Expert weights are stacked:
+ * gate/up [E][I][H/2] (+ scales [E][I][H/32]), down [E][H][I/2] (+ scales
+ * [E][H][I/32]), reference MXFP4 layout (low nibble = even column). */
+typedef struct {
+    uint32_t hidden, inter, experts, top_k, shared_inter;
+    const uint16_t* router;        /* [E][H] bf16 */
+    const float* correction;       /* [E] */
+    const uint8_t* gate_packed;
+    const uint8_t* gate_scales;
+    const uint8_t* up_packed;
+    const uint8_t* up_scales;
+    const uint8_t* down_packed;
+    const uint8_t* down_scales;
+    const uint16_t* shared_gate;   /* [Is][H] bf16, or NULL */
+    const uint16_t* shared_up;     /* [Is][H] */
+    const uint16_t* shared_down;   /* [H][Is] */
+    int32_t activation;            /* K3XB_ACT_* */
+    float situ_beta, situ_linear_beta;  /* linear_beta <= 0: none */
+    int32_t engine;                /* K3XB_ENGINE_* */
+    int32_t act_terms;             /* E2M1 activation terms (MXF4 engine), 0 = 6 */
+    /* Optional copies of the three scale arrays in the tcgen05 layout made by
+     * k3xb_prepare_mxfp4_scales (same byte count). When NULL the MXF4 engine
+     * re-lays the scales into its scratch on every call. */
+    const uint8_t* gate_scales_tc;
+    const uint8_t* up_scales_tc;
+    const uint8_t* down_scales_tc;
+} k3xb_moe_layer;
+
+/* Re-lays MXFP4 scales [rows][cols/32] (rows % 128 == 0, cols % 128 == 0)
+ * into the layout the tcgen05 block-scaled MMA reads: 512-byte atoms of 128
+ * rows x 4 scale blocks, atoms[rows/128][cols/128]. Done once per resident
+ * weight, like the reference's one-time resident upload (resident_weights.cuh). */
+int k3xb_prepare_mxfp4_scales(k3xb_ctx* ctx, const uint8_t* scales, size_t rows,
+                              size_t cols, uint8_t* out);
+
+/* out [T][H] = round_bf16(mixed + shared); ids/contributions [T][k] and
+ * plan_out may be NULL. */
+int k3xb_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* layer,
+                           const float* hidden, uint32_t tokens, float* out,
+                           uint32_t* ids, float* contributions);
+/* Same with HOST hidden/out/ids/contributions: copies in, runs, copies out
+ * and synchronises (the reference's resident layer returns by value). */
+int k3xb_moe_layer_forward_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer,
+                                const float* hidden_host, uint32_t tokens,
+                                float* out_host, uint32_t* ids_host,
+                                float* contributions_host);
+
+/* Expert FFN only, for an existing plan (mxfp4_situ_mlp_grid,
+ * backend.hpp:357-363): y[t][slot][H] = round_bf16(expert(hidden[t])). */
+int k3xb_moe_experts(k3xb_ctx* ctx, const k3xb_moe_layer* layer,
+                     const float* hidden, uint32_t tokens,
+                     const k3xb_plan* plan, float* slot_out);
+
+/* ---- (d) KDA recurrence -------------------------------------------------- */
+/* official_kda.cpp:319-369 applied over a draft tree for S sequences that
+ * share the topology: node n continues from parent[n]'s state
+ * (parent[n] = -1: the prefix state; parent[n] < n). A linear draft is
+ * parent[n] = n - 1. parent is a HOST array. Device arrays:
+ * state [S][h][d][d] (V-first), q/k/v/log_decay [S][N][h*d],
+ * beta [S][N][h], out [S][N][h*d]. */
+int k3xb_kda_tree(k3xb_ctx* ctx, const float* state, const int32_t* parent,
+                  uint32_t nodes, uint32_t sequences, uint32_t heads,
+                  uint32_t head_dim, const float* q, const float* k,
+                  const float* v, const float* log_decay, const float* beta,
+                  float* out);
+/* Replays root..commit_node[s] and writes that node's state to state_out
+ * (bit-identical to the state k3xb_kda_tree computed for it);
+ * commit_node[s] = -1 copies the prefix state. commit_node is HOST. */
+int k3xb_kda_commit(k3xb_ctx* ctx, const float* state, const int32_t* parent,
+                    uint32_t nodes, uint32_t sequences, uint32_t heads,
+                    uint32_t head_dim, const float* q, const float* k,
+                    const float* v, const float* log_decay, const float* beta,
+                    const int32_t* commit_node, float* state_out);
+
+/* ---- (e) acceptance ------------------------------------------------------- */
+/* verify_greedy_target_block (runtime/src/speculative.cpp:74-112) for S
+ * sequences of p drafts: targets = first-max argmax of logits
+ * [S][p+1][V] (model.cpp:1174-1176); accepted [S], committed [S][p+1],
+ * committed_count [S], targets [S][p+1] (may be NULL). */
+int k3xb_accept_greedy(k3xb_ctx* ctx, const float* logits,
+                       const uint32_t* drafts, uint32_t sequences,
+                       uint32_t drafts_per_sequence, uint32_t vocab,
+                       uint32_t* targets, uint32_t* accepted,
+                       uint32_t* committed, uint32_t* committed_count);
+/* Seeded speculative rejection sampling (no reference counterpart): accept
+ * draft i if u_i * q_i(d_i) < p_i(d_i) (softmax at `temperature`, FP64);
+ * at the first rejection sample norm(max(0, p - q)), else a bonus from p.
+ * Canonical FP64 reduction order and RNG are those of oracle/k3x_oracle.c.
+ * draft_logits [S][p][V]. */
+int k3xb_accept_rejection(k3xb_ctx* ctx, const float* target_logits,
+                          const float* draft_logits, const uint32_t* drafts,
+                          uint32_t sequences, uint32_t drafts_per_sequence,
+                          uint32_t vocab, float temperature, uint64_t seed,
+                          uint64_t sequence_base, uint32_t* accepted,
+                          uint32_t* committed, uint32_t* committed_count);
+
+/* ---- synthetic data and MXFP4 preparation -------------------------------- */
+/* N(mean, sigma) from a counter-based generator (SplitMix64 + Box-Muller),
+ * deterministic in (seed, stream, index). */
+int k3xb_fill_normal_f32(k3xb_ctx* ctx, float* out, size_t count,
+                         uint64_t seed, uint64_t stream, float mean,
+                         float sigma);
+/* Same values rounded to bf16 (as float values or as bf16 words). */
+int k3xb_fill_normal_bf16(k3xb_ctx* ctx, uint16_t* out, size_t count,
+                          uint64_t seed, uint64_t stream, float sigma);
+/* MXFP4 quantiser (no reference counterpart; the reference only decodes):
+ * per 32-block s = smallest integer with amax <= 6*2^s, E2M1 codes by
+ * round-to-nearest-even. x [rows][cols] float, cols % 32 == 0. */
+int k3xb_quantize_mxfp4(k3xb_ctx* ctx, const float* x, size_t rows,
+                        size_t cols, uint8_t* packed, uint8_t* scales);
+/* Generates N(0, sigma) weights and quantises them without a float copy. */
+int k3xb_fill_normal_mxfp4(k3xb_ctx* ctx, uint8_t* packed, uint8_t* scales,
+                           size_t rows, size_t cols, uint64_t seed,
+                           uint64_t stream, float sigma);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

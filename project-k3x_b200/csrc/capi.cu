@@ -1,0 +1,485 @@
+// capi.cu — the extern "C" boundary of libk3xb (include/k3xb.h).
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace k3xb {
+
+int fail(k3xb_ctx* ctx, int status, const std::string& message) {
+    if (ctx) ctx->error = message;
+    return status;
+}
+
+int cuda_fail(k3xb_ctx* ctx, cudaError_t err, const char* where) {
+    std::string msg = std::string(where) + ": " + cudaGetErrorName(err) + " (" + cudaGetErrorString(err) + ")";
+    return fail(ctx, K3XB_BACKEND_UNAVAILABLE, msg);
+}
+
+int ensure_scratch(k3xb_ctx* ctx, size_t bytes, void** out) {
+    if (bytes > ctx->scratch_bytes) {
+        K3XB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+        if (ctx->scratch) K3XB_CUDA(ctx, cudaFree(ctx->scratch));
+        ctx->scratch = nullptr;
+        ctx->scratch_bytes = 0;
+        const size_t grown = bytes + bytes / 4 + (1u << 20);
+        K3XB_CUDA(ctx, cudaMalloc(&ctx->scratch, grown));
+        ctx->scratch_bytes = grown;
+        ctx->stats.scratch_bytes = grown;
+        if (grown > ctx->stats.peak_scratch_bytes) ctx->stats.peak_scratch_bytes = grown;
+    }
+    *out = ctx->scratch;
+    return K3XB_OK;
+}
+
+namespace {
+
+struct MoeScratch {
+    float* logits;
+    uint32_t* ids;
+    float* contrib;
+    k3xb_plan plan;
+    float* act;
+    float* slot_out;
+    float* sg;
+    float* su;
+    float* sa;
+    float* shared_out;
+    float* hidden;   // host path only
+    float* out;      // host path only
+};
+
+template <typename A>
+void layout_moe(A& a, const k3xb_moe_layer& L, uint32_t T, bool host, MoeScratch* s) {
+    const size_t E = L.experts, K = L.top_k, H = L.hidden, I = L.inter, Is = L.shared_inter;
+    MoeScratch tmp{};
+    MoeScratch& r = s ? *s : tmp;
+    r.logits = a.template take<float>(T * E);
+    r.ids = a.template take<uint32_t>(T * K);
+    r.contrib = a.template take<float>(T * K);
+    r.plan.group_expert = a.template take<uint32_t>(E);
+    r.plan.group_offset = a.template take<uint32_t>(E + 1);
+    r.plan.assign_token = a.template take<uint32_t>(T * K);
+    r.plan.assign_slot = a.template take<uint32_t>(T * K);
+    r.plan.assign_contrib = a.template take<float>(T * K);
+    r.plan.group_count = a.template take<uint32_t>(1);
+    r.act = L.engine == K3XB_ENGINE_SIMT ? a.template take<float>(T * K * I) : nullptr;
+    r.slot_out = a.template take<float>(T * K * H);
+    r.sg = a.template take<float>(T * Is);
+    r.su = a.template take<float>(T * Is);
+    r.sa = a.template take<float>(T * Is);
+    r.shared_out = a.template take<float>(T * H);
+    r.hidden = host ? a.template take<float>(T * H) : nullptr;
+    r.out = host ? a.template take<float>(T * H) : nullptr;
+}
+
+int validate_layer(k3xb_ctx* ctx, const k3xb_moe_layer* L) {
+    if (!L) return fail(ctx, K3XB_INVALID_EXTENT, "null layer");
+    if (!L->hidden || !L->inter || !L->experts || !L->top_k || L->top_k > L->experts)
+        return fail(ctx, K3XB_INVALID_EXTENT, "layer dimensions");
+    if (L->hidden % 32 || L->inter % 32)
+        return fail(ctx, K3XB_INVALID_MXFP4, "hidden and inter must be multiples of the MXFP4 group (32)");
+    if (!L->router || !L->correction || !L->gate_packed || !L->gate_scales || !L->up_packed ||
+        !L->up_scales || !L->down_packed || !L->down_scales)
+        return fail(ctx, K3XB_INVALID_EXTENT, "missing layer weights");
+    if (L->shared_gate && (!L->shared_up || !L->shared_down || !L->shared_inter))
+        return fail(ctx, K3XB_INVALID_EXTENT, "incomplete shared expert");
+    if (L->activation != K3XB_ACT_SWIGLU && L->activation != K3XB_ACT_SITU)
+        return fail(ctx, K3XB_INVALID_STATE, "unknown activation");
+    if (L->activation == K3XB_ACT_SITU && !(L->situ_beta > 0.0f))
+        return fail(ctx, K3XB_INVALID_STATE, "SiTU beta must be positive");
+    if (L->engine != K3XB_ENGINE_SIMT && L->engine != K3XB_ENGINE_MXF4)
+        return fail(ctx, K3XB_INVALID_STATE, "unknown expert engine");
+    return K3XB_OK;
+}
+
+int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T,
+                       float* out, uint32_t* ids_out, float* contrib_out, MoeScratch& s) {
+    const uint32_t E = L.experts, K = L.top_k, H = L.hidden;
+    uint32_t* ids = ids_out ? ids_out : s.ids;
+    float* contrib = contrib_out ? contrib_out : s.contrib;
+    s.plan.status = ctx->status_word;
+    int st;
+    if ((st = launch_router_logits(ctx, hidden, T, H, L.router, E, s.logits))) return st;
+    if ((st = launch_topk(ctx, s.logits, L.correction, T, E, K, ids, contrib, nullptr, s.plan.status))) return st;
+    if ((st = launch_plan(ctx, ids, contrib, T, K, E, s.plan))) return st;
+    if (L.engine == K3XB_ENGINE_SIMT) {
+        if ((st = launch_simt_experts(ctx, L, hidden, T, s.plan, s.act, s.slot_out))) return st;
+    } else {
+        if ((st = launch_mxf4_experts(ctx, L, hidden, T, s.plan, s.slot_out))) return st;
+    }
+    const float* shared = nullptr;
+    if (L.shared_gate) {
+        const uint32_t Is = L.shared_inter;
+        if ((st = launch_bf16_rows(ctx, hidden, L.shared_gate, T, Is, H, s.sg))) return st;
+        if ((st = launch_bf16_rows(ctx, hidden, L.shared_up, T, Is, H, s.su))) return st;
+        if ((st = launch_act(ctx, s.sg, s.su, static_cast<size_t>(T) * Is, L.activation, L.situ_beta,
+                             L.situ_linear_beta, s.sa))) return st;
+        if ((st = launch_bf16_rows(ctx, s.sa, L.shared_down, T, H, Is, s.shared_out))) return st;
+        shared = s.shared_out;
+    }
+    if ((st = launch_combine(ctx, s.slot_out, contrib, shared, T, K, H, out))) return st;
+    ++ctx->stats.moe_layer_calls;
+    return K3XB_OK;
+}
+
+}  // namespace
+
+}  // namespace k3xb
+
+using namespace k3xb;
+
+extern "C" {
+
+int k3xb_create(int device, k3xb_ctx** out) {
+    if (!out) return K3XB_INVALID_EXTENT;
+    *out = nullptr;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) return K3XB_BACKEND_UNAVAILABLE;
+    if (device < 0 || device >= count) return K3XB_INVALID_EXTENT;
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return K3XB_BACKEND_UNAVAILABLE;
+    if (prop.major != 10) return K3XB_UNSUPPORTED_ARCHITECTURE;   // sm_100a code only
+    k3xb_ctx* ctx = new (std::nothrow) k3xb_ctx();
+    if (!ctx) return K3XB_BACKEND_UNAVAILABLE;
+    ctx->device = device;
+    ctx->sm_count = prop.multiProcessorCount;
+    if (cudaSetDevice(device) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&ctx->status_word, sizeof(int32_t)) != cudaSuccess ||
+        cudaMemset(ctx->status_word, 0, sizeof(int32_t)) != cudaSuccess) {
+        k3xb_destroy(ctx);
+        return K3XB_BACKEND_UNAVAILABLE;
+    }
+    ctx->stream = ctx->own_stream;
+    *out = ctx;
+    return K3XB_OK;
+}
+
+int k3xb_destroy(k3xb_ctx* ctx) {
+    if (!ctx) return K3XB_OK;
+    cudaSetDevice(ctx->device);
+    if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->status_word) cudaFree(ctx->status_word);
+    release_mxf4_resources(ctx);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return K3XB_OK;
+}
+
+int k3xb_last_error(const k3xb_ctx* ctx, char* buf, size_t len) {
+    if (!ctx || !buf || !len) return K3XB_INVALID_EXTENT;
+    std::snprintf(buf, len, "%s", ctx->error.c_str());
+    return K3XB_OK;
+}
+
+int k3xb_set_stream(k3xb_ctx* ctx, void* stream) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+    return K3XB_OK;
+}
+
+int k3xb_sync(k3xb_ctx* ctx) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    int32_t st = 0;
+    K3XB_CUDA(ctx, cudaMemcpy(&st, ctx->status_word, sizeof st, cudaMemcpyDeviceToHost));
+    if (st) {
+        K3XB_CUDA(ctx, cudaMemset(ctx->status_word, 0, sizeof st));
+        return fail(ctx, st, "device-side validation failed (route/plan input)");
+    }
+    return K3XB_OK;
+}
+
+int k3xb_get_stats(const k3xb_ctx* ctx, k3xb_stats* out) {
+    if (!ctx || !out) return K3XB_INVALID_EXTENT;
+    *out = ctx->stats;
+    return K3XB_OK;
+}
+
+int k3xb_route(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_t H, const uint16_t* router,
+               const float* correction, uint32_t E, uint32_t K, uint32_t* ids, float* contrib,
+               float* scores) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!T || !H || !E || !K || K > E || !hidden || !router || !correction || !ids || !contrib)
+        return fail(ctx, K3XB_INVALID_EXTENT, "route arguments");
+    void* base;
+    Sizer sz;
+    sz.take<float>(static_cast<size_t>(T) * E);
+    int st = ensure_scratch(ctx, sz.used, &base);
+    if (st) return st;
+    Carver c(base);
+    float* logits = c.take<float>(static_cast<size_t>(T) * E);
+    if ((st = launch_router_logits(ctx, hidden, T, H, router, E, logits))) return st;
+    if ((st = launch_topk(ctx, logits, correction, T, E, K, ids, contrib, scores, ctx->status_word))) return st;
+    ++ctx->stats.route_calls;
+    return K3XB_OK;
+}
+
+int k3xb_expert_major_plan(k3xb_ctx* ctx, const uint32_t* ids, const float* contrib, uint32_t T,
+                           uint32_t K, uint32_t E, const k3xb_plan* plan) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!plan || !ids || !contrib) return fail(ctx, K3XB_INVALID_EXTENT, "plan arguments");
+    if (!T || !K) return fail(ctx, K3XB_INVALID_EXTENT, "empty routes");   // expert_major.cpp:12-14
+    k3xb_plan p = *plan;
+    if (!p.status) p.status = ctx->status_word;
+    return launch_plan(ctx, ids, contrib, T, K, E, p);
+}
+
+int k3xb_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const float* hidden, uint32_t T,
+                           float* out, uint32_t* ids, float* contrib) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    int st = validate_layer(ctx, layer);
+    if (st) return st;
+    if (!T || !hidden || !out) return fail(ctx, K3XB_INVALID_EXTENT, "moe forward arguments");
+    Sizer sz;
+    layout_moe(sz, *layer, T, false, nullptr);
+    sz.used += mxf4_scratch_bytes(*layer, T);
+    void* base;
+    if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
+    Carver c(base);
+    MoeScratch s{};
+    layout_moe(c, *layer, T, false, &s);
+    set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
+    return moe_forward_device(ctx, *layer, hidden, T, out, ids, contrib, s);
+}
+
+int k3xb_moe_layer_forward_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const float* hidden_host,
+                                uint32_t T, float* out_host, uint32_t* ids_host, float* contrib_host) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    int st = validate_layer(ctx, layer);
+    if (st) return st;
+    if (!T || !hidden_host || !out_host) return fail(ctx, K3XB_INVALID_EXTENT, "moe forward arguments");
+    Sizer sz;
+    layout_moe(sz, *layer, T, true, nullptr);
+    sz.used += mxf4_scratch_bytes(*layer, T);
+    void* base;
+    if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
+    Carver c(base);
+    MoeScratch s{};
+    layout_moe(c, *layer, T, true, &s);
+    set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
+    const size_t hbytes = sizeof(float) * T * layer->hidden;
+    K3XB_CUDA(ctx, cudaMemcpyAsync(s.hidden, hidden_host, hbytes, cudaMemcpyHostToDevice, ctx->stream));
+    ctx->stats.h2d_bytes += hbytes;
+    if ((st = moe_forward_device(ctx, *layer, s.hidden, T, s.out, nullptr, nullptr, s))) return st;
+    K3XB_CUDA(ctx, cudaMemcpyAsync(out_host, s.out, hbytes, cudaMemcpyDeviceToHost, ctx->stream));
+    ctx->stats.d2h_bytes += hbytes;
+    const size_t rbytes = static_cast<size_t>(T) * layer->top_k * 4;
+    if (ids_host) {
+        K3XB_CUDA(ctx, cudaMemcpyAsync(ids_host, s.ids, rbytes, cudaMemcpyDeviceToHost, ctx->stream));
+        ctx->stats.d2h_bytes += rbytes;
+    }
+    if (contrib_host) {
+        K3XB_CUDA(ctx, cudaMemcpyAsync(contrib_host, s.contrib, rbytes, cudaMemcpyDeviceToHost, ctx->stream));
+        ctx->stats.d2h_bytes += rbytes;
+    }
+    return k3xb_sync(ctx);
+}
+
+int k3xb_moe_experts(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const float* hidden, uint32_t T,
+                     const k3xb_plan* plan, float* slot_out) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    int st = validate_layer(ctx, layer);
+    if (st) return st;
+    if (!T || !hidden || !plan || !slot_out) return fail(ctx, K3XB_INVALID_EXTENT, "experts arguments");
+    Sizer sz;
+    sz.take<float>(static_cast<size_t>(T) * layer->top_k * layer->inter);
+    sz.used += mxf4_scratch_bytes(*layer, T);
+    void* base;
+    if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
+    Carver c(base);
+    float* act = c.take<float>(static_cast<size_t>(T) * layer->top_k * layer->inter);
+    set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
+    if (layer->engine == K3XB_ENGINE_SIMT) return launch_simt_experts(ctx, *layer, hidden, T, *plan, act, slot_out);
+    return launch_mxf4_experts(ctx, *layer, hidden, T, *plan, slot_out);
+}
+
+// ---- KDA -------------------------------------------------------------------
+
+namespace {
+
+struct KdaSchedule {
+    std::vector<int32_t> order, depth, from_stack;
+    uint32_t levels = 0;
+};
+
+// DFS preorder of the draft forest (roots = parent -1, children in index
+// order); from_stack marks nodes whose parent is not the node visited just
+// before them.
+int schedule_tree(k3xb_ctx* ctx, const int32_t* parent, uint32_t n, KdaSchedule& out) {
+    std::vector<std::vector<int32_t>> children(n);
+    std::vector<int32_t> roots;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (parent[i] < -1 || parent[i] >= static_cast<int32_t>(i))
+            return fail(ctx, K3XB_INVALID_EXTENT, "draft tree: parent[n] must be -1 or < n");
+        if (parent[i] < 0) roots.push_back(static_cast<int32_t>(i));
+        else children[parent[i]].push_back(static_cast<int32_t>(i));
+    }
+    std::vector<int32_t> dep(n, 0);
+    std::vector<std::pair<int32_t, int32_t>> stack;   // (node, depth)
+    for (auto it = roots.rbegin(); it != roots.rend(); ++it) stack.push_back({*it, 1});
+    int32_t prev = -1;
+    while (!stack.empty()) {
+        auto [node, d] = stack.back();
+        stack.pop_back();
+        out.order.push_back(node);
+        out.depth.push_back(d);
+        // the registers hold the prefix state before the first node and the
+        // previous node's state afterwards
+        const bool reload = parent[node] != prev;
+        out.from_stack.push_back(reload ? 1 : 0);
+        if (reload) out.levels = std::max<uint32_t>(out.levels, static_cast<uint32_t>(d));
+        for (auto c = children[node].rbegin(); c != children[node].rend(); ++c) stack.push_back({*c, d + 1});
+        prev = node;
+    }
+    return K3XB_OK;
+}
+
+int kda_common(k3xb_ctx* ctx, const float* state, uint32_t nodes, uint32_t S, uint32_t heads,
+               uint32_t head_dim, const float* q, const float* k, const float* v, const float* ld,
+               const float* beta, float* out, float* state_out, const KdaSchedule& sch) {
+    const size_t visit = sch.order.size();
+    Sizer sz;
+    sz.take<int32_t>(3 * visit + 3);
+    void* base;
+    int st = ensure_scratch(ctx, sz.used, &base);
+    if (st) return st;
+    Carver c(base);
+    int32_t* d = c.take<int32_t>(3 * visit + 3);
+    std::vector<int32_t> packed;
+    packed.insert(packed.end(), sch.order.begin(), sch.order.end());
+    packed.insert(packed.end(), sch.depth.begin(), sch.depth.end());
+    packed.insert(packed.end(), sch.from_stack.begin(), sch.from_stack.end());
+    if (!packed.empty())
+        K3XB_CUDA(ctx, cudaMemcpyAsync(d, packed.data(), packed.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
+    st = launch_kda(ctx, state, d, d + visit, d + 2 * visit, static_cast<uint32_t>(visit), nodes, S, heads,
+                    head_dim, q, k, v, ld, beta, out, state_out, sch.levels);
+    ++ctx->stats.kda_calls;
+    return st;
+}
+
+}  // namespace
+
+int k3xb_kda_tree(k3xb_ctx* ctx, const float* state, const int32_t* parent, uint32_t nodes,
+                  uint32_t S, uint32_t heads, uint32_t head_dim, const float* q, const float* k,
+                  const float* v, const float* ld, const float* beta, float* out) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!state || !parent || !nodes || !S || !heads || !q || !k || !v || !ld || !beta || !out)
+        return fail(ctx, K3XB_INVALID_EXTENT, "kda_tree arguments");
+    KdaSchedule sch;
+    int st = schedule_tree(ctx, parent, nodes, sch);
+    if (st) return st;
+    return kda_common(ctx, state, nodes, S, heads, head_dim, q, k, v, ld, beta, out, nullptr, sch);
+}
+
+int k3xb_kda_commit(k3xb_ctx* ctx, const float* state, const int32_t* parent, uint32_t nodes, uint32_t S,
+                    uint32_t heads, uint32_t head_dim, const float* q, const float* k, const float* v,
+                    const float* ld, const float* beta, const int32_t* commit_node, float* state_out) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!state || !parent || !S || !heads || !commit_node || !state_out)
+        return fail(ctx, K3XB_INVALID_EXTENT, "kda_commit arguments");
+    for (uint32_t i = 0; i < nodes; ++i)
+        if (parent[i] < -1 || parent[i] >= static_cast<int32_t>(i))
+            return fail(ctx, K3XB_INVALID_EXTENT, "draft tree: parent[n] must be -1 or < n");
+    // sequences may commit different nodes: group them by path
+    const size_t sstride = static_cast<size_t>(heads) * head_dim * head_dim;
+    for (uint32_t s = 0; s < S; ++s) {
+        const int32_t node = commit_node[s];
+        if (node < -1 || node >= static_cast<int32_t>(nodes))
+            return fail(ctx, K3XB_INVALID_EXTENT, "commit node out of range");
+        KdaSchedule sch;
+        std::vector<int32_t> path;
+        for (int32_t x = node; x >= 0; x = parent[x]) path.push_back(x);
+        for (size_t i = 0; i < path.size(); ++i) {
+            sch.order.push_back(path[path.size() - 1 - i]);
+            sch.depth.push_back(static_cast<int32_t>(i + 1));
+            sch.from_stack.push_back(0);
+        }
+        const size_t io = static_cast<size_t>(s) * nodes * heads * head_dim;
+        int st = kda_common(ctx, state + s * sstride, nodes, 1, heads, head_dim, q + io, k + io, v + io,
+                            ld + io, beta + static_cast<size_t>(s) * nodes * heads, nullptr,
+                            state_out + s * sstride, sch);
+        if (st) return st;
+    }
+    return K3XB_OK;
+}
+
+// ---- acceptance --------------------------------------------------------------
+
+int k3xb_accept_greedy(k3xb_ctx* ctx, const float* logits, const uint32_t* drafts, uint32_t S, uint32_t p,
+                       uint32_t V, uint32_t* targets, uint32_t* accepted, uint32_t* committed,
+                       uint32_t* count) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!logits || (!drafts && p) || !S || !V || !accepted || !committed || !count)
+        return fail(ctx, K3XB_INVALID_EXTENT, "accept_greedy arguments");
+    uint32_t* t = targets;
+    if (!t) {
+        void* base;
+        int st = ensure_scratch(ctx, sizeof(uint32_t) * S * (p + 1) + 256, &base);
+        if (st) return st;
+        t = static_cast<uint32_t*>(base);
+    }
+    ++ctx->stats.accept_calls;
+    return launch_accept_greedy(ctx, logits, drafts, S, p, V, t, accepted, committed, count);
+}
+
+int k3xb_accept_rejection(k3xb_ctx* ctx, const float* tl, const float* dl, const uint32_t* drafts, uint32_t S,
+                          uint32_t p, uint32_t V, float temperature, uint64_t seed, uint64_t seq_base,
+                          uint32_t* accepted, uint32_t* committed, uint32_t* count) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!tl || (p && (!dl || !drafts)) || !S || !V || !accepted || !committed || !count)
+        return fail(ctx, K3XB_INVALID_EXTENT, "accept_rejection arguments");
+    if (!(temperature > 0.0f)) return fail(ctx, K3XB_INVALID_EXTENT, "temperature must be positive");
+    void* base;
+    int st = ensure_scratch(ctx, sizeof(double) * 2 * S * (p + 1) + 512, &base);
+    if (st) return st;
+    Carver c(base);
+    double* pd = c.take<double>(static_cast<size_t>(S) * (p + 1));
+    double* qd = c.take<double>(static_cast<size_t>(S) * (p + 1));
+    ++ctx->stats.accept_calls;
+    return launch_accept_rejection(ctx, tl, dl, drafts, S, p, V, temperature, seed, seq_base, pd, qd,
+                                   accepted, committed, count);
+}
+
+// ---- synthetic data --------------------------------------------------------------
+
+int k3xb_fill_normal_f32(k3xb_ctx* ctx, float* out, size_t n, uint64_t seed, uint64_t stream, float mean,
+                         float sigma) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!out || !n) return fail(ctx, K3XB_INVALID_EXTENT, "fill arguments");
+    return launch_fill_normal_f32(ctx, out, n, seed, stream, mean, sigma);
+}
+
+int k3xb_fill_normal_bf16(k3xb_ctx* ctx, uint16_t* out, size_t n, uint64_t seed, uint64_t stream, float sigma) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!out || !n) return fail(ctx, K3XB_INVALID_EXTENT, "fill arguments");
+    return launch_fill_normal_bf16(ctx, out, n, seed, stream, sigma);
+}
+
+int k3xb_quantize_mxfp4(k3xb_ctx* ctx, const float* x, size_t rows, size_t cols, uint8_t* packed,
+                        uint8_t* scales) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!x || !packed || !scales || !rows || !cols || cols % 32)
+        return fail(ctx, K3XB_INVALID_MXFP4, "quantize arguments (cols % 32 == 0)");
+    return launch_quantize_mxfp4(ctx, x, rows, cols, packed, scales);
+}
+
+int k3xb_prepare_mxfp4_scales(k3xb_ctx* ctx, const uint8_t* scales, size_t rows, size_t cols, uint8_t* out) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    return prepare_mxfp4_scales(ctx, scales, rows, cols, out);
+}
+
+int k3xb_fill_normal_mxfp4(k3xb_ctx* ctx, uint8_t* packed, uint8_t* scales, size_t rows, size_t cols,
+                           uint64_t seed, uint64_t stream, float sigma) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!packed || !scales || !rows || !cols || cols % 32)
+        return fail(ctx, K3XB_INVALID_MXFP4, "fill arguments (cols % 32 == 0)");
+    return launch_fill_normal_mxfp4(ctx, packed, scales, rows, cols, seed, stream, sigma);
+}
+
+}  // extern "C"

@@ -1,0 +1,64 @@
+// kernels.cuh — host-side launchers implemented by the .cu files of libk3xb.
+#pragma once
+
+#include "common.cuh"
+
+namespace k3xb {
+
+// router.cu
+size_t plan_smem_bytes(uint32_t T, uint32_t E);
+int launch_router_logits(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_t H,
+                         const uint16_t* W, uint32_t E, float* logits);
+int launch_topk(k3xb_ctx* ctx, const float* logits, const float* correction, uint32_t T,
+                uint32_t E, uint32_t K, uint32_t* ids, float* contrib, float* scores,
+                int32_t* status);
+int launch_plan(k3xb_ctx* ctx, const uint32_t* ids, const float* contrib, uint32_t T,
+                uint32_t K, uint32_t E, const k3xb_plan& plan);
+
+// experts_simt.cu
+int launch_simt_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T,
+                        const k3xb_plan& plan, float* act_buf, float* slot_out);
+int launch_combine(k3xb_ctx* ctx, const float* slot_out, const float* contrib, const float* shared,
+                   uint32_t T, uint32_t K, uint32_t H, float* out);
+int launch_bf16_rows(k3xb_ctx* ctx, const float* x, const uint16_t* W, uint32_t T, uint32_t rows,
+                     uint32_t cols, float* out);
+int launch_act(k3xb_ctx* ctx, const float* g, const float* u, size_t n, int act, float beta,
+               float lbeta, float* out);
+
+// kda.cu
+int launch_kda(k3xb_ctx* ctx, const float* state, const int32_t* order, const int32_t* depth,
+               const int32_t* from_stack, uint32_t visit, uint32_t nodes, uint32_t sequences,
+               uint32_t heads, uint32_t head_dim, const float* q, const float* k, const float* v,
+               const float* log_decay, const float* beta, float* out, float* state_out,
+               uint32_t levels);
+
+// accept.cu
+int launch_accept_greedy(k3xb_ctx* ctx, const float* logits, const uint32_t* drafts, uint32_t S,
+                         uint32_t p, uint32_t V, uint32_t* targets, uint32_t* accepted,
+                         uint32_t* committed, uint32_t* count);
+int launch_accept_rejection(k3xb_ctx* ctx, const float* tl, const float* dl, const uint32_t* drafts,
+                            uint32_t S, uint32_t p, uint32_t V, float temperature, uint64_t seed,
+                            uint64_t seq_base, double* pd, double* qd, uint32_t* accepted,
+                            uint32_t* committed, uint32_t* count);
+
+// synth.cu
+int launch_fill_normal_f32(k3xb_ctx* ctx, float* out, size_t n, uint64_t seed, uint64_t stream,
+                           float mean, float sigma);
+int launch_fill_normal_bf16(k3xb_ctx* ctx, uint16_t* out, size_t n, uint64_t seed, uint64_t stream,
+                            float sigma);
+int launch_quantize_mxfp4(k3xb_ctx* ctx, const float* x, size_t rows, size_t cols, uint8_t* packed,
+                          uint8_t* scales);
+int launch_fill_normal_mxfp4(k3xb_ctx* ctx, uint8_t* packed, uint8_t* scales, size_t rows, size_t cols,
+                             uint64_t seed, uint64_t stream, float sigma);
+
+}  // namespace k3xb
+
+namespace k3xb {
+// experts_mxf4.cu — tcgen05 block-scaled expert engine
+size_t mxf4_scratch_bytes(const k3xb_moe_layer& L, uint32_t T);
+void set_mxf4_scratch(k3xb_ctx* ctx, void* region);
+int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T,
+                        const k3xb_plan& plan, float* slot_out);
+void release_mxf4_resources(k3xb_ctx* ctx);
+int prepare_mxfp4_scales(k3xb_ctx* ctx, const uint8_t* scales, size_t rows, size_t cols, uint8_t* out);
+}  // namespace k3xb

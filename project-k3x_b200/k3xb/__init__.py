@@ -1,0 +1,266 @@
+"""Python binding of libk3xb (include/k3xb.h) over ctypes.
+
+Device arrays are passed as torch CUDA tensors (torch supplies memory and
+streams; all compute is in libk3xb.so). There is no CPU fallback: if the
+library or a B200 is missing, every entry point raises K3xbError.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libk3xb.so")
+
+OK = 0
+INVALID_EXTENT = 9
+INVALID_MXFP4 = 15
+INVALID_STATE = 16
+BACKEND_UNAVAILABLE = 17
+UNSUPPORTED_ARCHITECTURE = 19
+
+ACT_SWIGLU = 0
+ACT_SITU = 1
+ENGINE_MXF4 = 0
+ENGINE_SIMT = 1
+
+STATUS_NAMES = {0: "OK", 9: "INVALID_EXTENT", 15: "INVALID_MXFP4", 16: "INVALID_STATE",
+                17: "BACKEND_UNAVAILABLE", 19: "UNSUPPORTED_ARCHITECTURE"}
+
+
+class K3xbError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class Plan(C.Structure):
+    _fields_ = [("group_expert", C.c_void_p), ("group_offset", C.c_void_p),
+                ("assign_token", C.c_void_p), ("assign_slot", C.c_void_p),
+                ("assign_contrib", C.c_void_p), ("group_count", C.c_void_p),
+                ("status", C.c_void_p)]
+
+
+class MoeLayer(C.Structure):
+    _fields_ = [("hidden", C.c_uint32), ("inter", C.c_uint32), ("experts", C.c_uint32),
+                ("top_k", C.c_uint32), ("shared_inter", C.c_uint32),
+                ("router", C.c_void_p), ("correction", C.c_void_p),
+                ("gate_packed", C.c_void_p), ("gate_scales", C.c_void_p),
+                ("up_packed", C.c_void_p), ("up_scales", C.c_void_p),
+                ("down_packed", C.c_void_p), ("down_scales", C.c_void_p),
+                ("shared_gate", C.c_void_p), ("shared_up", C.c_void_p), ("shared_down", C.c_void_p),
+                ("activation", C.c_int32), ("situ_beta", C.c_float),
+                ("situ_linear_beta", C.c_float), ("engine", C.c_int32), ("act_terms", C.c_int32),
+                ("gate_scales_tc", C.c_void_p), ("up_scales_tc", C.c_void_p),
+                ("down_scales_tc", C.c_void_p)]
+
+
+class Stats(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in (
+        "kernel_launches", "route_calls", "moe_layer_calls", "moe_layer_experts", "kda_calls",
+        "accept_calls", "scratch_bytes", "peak_scratch_bytes", "h2d_bytes", "d2h_bytes")]
+
+
+_lib = None
+
+
+def library() -> C.CDLL:
+    """Loads libk3xb.so; raises if it was not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise K3xbError(BACKEND_UNAVAILABLE, f"{LIB_PATH} is missing: run project-k3x_b200/build.py")
+        lib = C.CDLL(LIB_PATH)
+        vp, u32, u64, sz, f32 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_size_t, C.c_float
+        sigs = {
+            "k3xb_create": [C.c_int, C.POINTER(vp)],
+            "k3xb_destroy": [vp],
+            "k3xb_last_error": [vp, C.c_char_p, sz],
+            "k3xb_set_stream": [vp, vp],
+            "k3xb_sync": [vp],
+            "k3xb_get_stats": [vp, C.POINTER(Stats)],
+            "k3xb_route": [vp, vp, u32, u32, vp, vp, u32, u32, vp, vp, vp],
+            "k3xb_expert_major_plan": [vp, vp, vp, u32, u32, u32, C.POINTER(Plan)],
+            "k3xb_moe_layer_forward": [vp, C.POINTER(MoeLayer), vp, u32, vp, vp, vp],
+            "k3xb_moe_layer_forward_host": [vp, C.POINTER(MoeLayer), vp, u32, vp, vp, vp],
+            "k3xb_moe_experts": [vp, C.POINTER(MoeLayer), vp, u32, C.POINTER(Plan), vp],
+            "k3xb_kda_tree": [vp, vp, vp, u32, u32, u32, u32, vp, vp, vp, vp, vp, vp],
+            "k3xb_kda_commit": [vp, vp, vp, u32, u32, u32, u32, vp, vp, vp, vp, vp, vp, vp],
+            "k3xb_accept_greedy": [vp, vp, vp, u32, u32, u32, vp, vp, vp, vp],
+            "k3xb_accept_rejection": [vp, vp, vp, vp, u32, u32, u32, f32, u64, u64, vp, vp, vp],
+            "k3xb_fill_normal_f32": [vp, vp, sz, u64, u64, f32, f32],
+            "k3xb_fill_normal_bf16": [vp, vp, sz, u64, u64, f32],
+            "k3xb_quantize_mxfp4": [vp, vp, sz, sz, vp, vp],
+            "k3xb_fill_normal_mxfp4": [vp, vp, vp, sz, sz, u64, u64, f32],
+            "k3xb_prepare_mxfp4_scales": [vp, vp, sz, sz, vp],
+        }
+        for name, args in sigs.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = C.c_int
+        _lib = lib
+    return _lib
+
+
+def _p(t):
+    """Device pointer of a torch tensor (None -> NULL)."""
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise K3xbError(INVALID_EXTENT, "expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise K3xbError(INVALID_EXTENT, "expected a contiguous tensor")
+    return C.c_void_p(t.data_ptr())
+
+
+class Context:
+    """One k3xb context per GPU; calls run on torch's current stream unless
+    `stream` is given."""
+
+    def __init__(self, device: int = 0):
+        self.lib = library()
+        h = C.c_void_p()
+        st = self.lib.k3xb_create(device, C.byref(h))
+        if st != OK:
+            raise K3xbError(st, f"k3xb_create(device={device})")
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.k3xb_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, st, where):
+        if st != OK:
+            buf = C.create_string_buffer(512)
+            self.lib.k3xb_last_error(self.h, buf, 512)
+            raise K3xbError(st, f"{where}: {buf.value.decode(errors='replace')}")
+
+    def use_stream(self, stream=None):
+        """Binds a torch.cuda.Stream (default: torch's current stream)."""
+        import torch
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        self._check(self.lib.k3xb_set_stream(self.h, C.c_void_p(s.cuda_stream)), "set_stream")
+
+    def sync(self):
+        self._check(self.lib.k3xb_sync(self.h), "sync")
+
+    def stats(self) -> dict:
+        s = Stats()
+        self._check(self.lib.k3xb_get_stats(self.h, C.byref(s)), "stats")
+        return {n: getattr(s, n) for n, _ in Stats._fields_}
+
+    # ---- (a) ------------------------------------------------------------------
+    def route(self, hidden, router, correction, top_k, ids, contrib, scores=None):
+        T, H = hidden.shape
+        E = router.shape[0]
+        self._check(self.lib.k3xb_route(self.h, _p(hidden), T, H, _p(router), _p(correction), E, top_k,
+                                        _p(ids), _p(contrib), _p(scores)), "route")
+
+    def expert_major_plan(self, ids, contrib, experts, plan: dict):
+        T, K = ids.shape
+        pl = Plan(*(_p(plan[k]) for k in ("group_expert", "group_offset", "assign_token", "assign_slot",
+                                          "assign_contrib", "group_count", "status")))
+        self._check(self.lib.k3xb_expert_major_plan(self.h, _p(ids), _p(contrib), T, K, experts,
+                                                    C.byref(pl)), "expert_major_plan")
+
+    # ---- (b)+(c) ----------------------------------------------------------------
+    def moe_layer_forward(self, layer: MoeLayer, hidden, out, ids=None, contrib=None):
+        self._check(self.lib.k3xb_moe_layer_forward(self.h, C.byref(layer), _p(hidden), hidden.shape[0],
+                                                    _p(out), _p(ids), _p(contrib)), "moe_layer_forward")
+
+    def moe_layer_forward_host(self, layer: MoeLayer, hidden, out, ids=None, contrib=None):
+        """hidden/out/ids/contrib are CPU tensors (pinned for async copies)."""
+        ptr = lambda t: None if t is None else C.c_void_p(t.data_ptr())
+        self._check(self.lib.k3xb_moe_layer_forward_host(self.h, C.byref(layer), ptr(hidden),
+                                                         hidden.shape[0], ptr(out), ptr(ids),
+                                                         ptr(contrib)), "moe_layer_forward_host")
+
+    # ---- (d) --------------------------------------------------------------------
+    def kda_tree(self, state, parent, q, k, v, log_decay, beta, out):
+        S, N = q.shape[0], q.shape[1]
+        heads, d = state.shape[1], state.shape[2]
+        par = (C.c_int32 * N)(*[int(x) for x in parent])
+        self._check(self.lib.k3xb_kda_tree(self.h, _p(state), par, N, S, heads, d, _p(q), _p(k), _p(v),
+                                           _p(log_decay), _p(beta), _p(out)), "kda_tree")
+
+    def kda_commit(self, state, parent, q, k, v, log_decay, beta, commit_node, state_out):
+        S, N = q.shape[0], q.shape[1]
+        heads, d = state.shape[1], state.shape[2]
+        par = (C.c_int32 * N)(*[int(x) for x in parent])
+        com = (C.c_int32 * S)(*[int(x) for x in commit_node])
+        self._check(self.lib.k3xb_kda_commit(self.h, _p(state), par, N, S, heads, d, _p(q), _p(k), _p(v),
+                                             _p(log_decay), _p(beta), com, _p(state_out)), "kda_commit")
+
+    # ---- (e) --------------------------------------------------------------------
+    def accept_greedy(self, logits, drafts, accepted, committed, count, targets=None):
+        S, P1, V = logits.shape
+        self._check(self.lib.k3xb_accept_greedy(self.h, _p(logits), _p(drafts), S, P1 - 1, V, _p(targets),
+                                                _p(accepted), _p(committed), _p(count)), "accept_greedy")
+
+    def accept_rejection(self, target_logits, draft_logits, drafts, temperature, seed, seq_base,
+                         accepted, committed, count):
+        S, P1, V = target_logits.shape
+        self._check(self.lib.k3xb_accept_rejection(self.h, _p(target_logits), _p(draft_logits), _p(drafts),
+                                                   S, P1 - 1, V, temperature, seed, seq_base,
+                                                   _p(accepted), _p(committed), _p(count)),
+                    "accept_rejection")
+
+    # ---- synthetic ----------------------------------------------------------------
+    def fill_normal_f32(self, out, seed, stream, mean=0.0, sigma=1.0):
+        self._check(self.lib.k3xb_fill_normal_f32(self.h, _p(out), out.numel(), seed, stream, mean, sigma),
+                    "fill_normal_f32")
+
+    def fill_normal_bf16(self, out, seed, stream, sigma=1.0):
+        self._check(self.lib.k3xb_fill_normal_bf16(self.h, _p(out), out.numel(), seed, stream, sigma),
+                    "fill_normal_bf16")
+
+    def quantize_mxfp4(self, x, packed, scales):
+        rows, cols = x.shape
+        self._check(self.lib.k3xb_quantize_mxfp4(self.h, _p(x), rows, cols, _p(packed), _p(scales)),
+                    "quantize_mxfp4")
+
+    def prepare_mxfp4_scales(self, scales, rows, cols, out):
+        self._check(self.lib.k3xb_prepare_mxfp4_scales(self.h, _p(scales), rows, cols, _p(out)),
+                    "prepare_mxfp4_scales")
+
+    def prepare_layer_scales(self, w: dict):
+        """Adds tcgen05-layout copies of the three expert scale arrays to a
+        layer dict (one-time, for resident weights)."""
+        import torch
+        E, H, I = w["experts"], w["hidden"], w["inter"]
+        for name, rows, cols in (("gate", E * I, H), ("up", E * I, H), ("down", E * H, I)):
+            out = torch.empty_like(w[f"{name}_scales"])
+            self.prepare_mxfp4_scales(w[f"{name}_scales"], rows, cols, out)
+            w[f"{name}_scales_tc"] = out
+        return w
+
+    def fill_normal_mxfp4(self, packed, scales, rows, cols, seed, stream, sigma):
+        self._check(self.lib.k3xb_fill_normal_mxfp4(self.h, _p(packed), _p(scales), rows, cols, seed, stream,
+                                                    sigma), "fill_normal_mxfp4")
+
+
+def moe_layer_desc(w: dict, engine=ENGINE_SIMT, act_terms=6) -> MoeLayer:
+    """Builds the C descriptor from a dict of torch CUDA tensors + dims
+    (keeps no references: the caller keeps the tensors alive)."""
+    L = MoeLayer()
+    L.hidden, L.inter, L.experts, L.top_k = w["hidden"], w["inter"], w["experts"], w["top_k"]
+    L.shared_inter = w.get("shared_inter", 0)
+    for name in ("router", "correction", "gate_packed", "gate_scales", "up_packed", "up_scales",
+                 "down_packed", "down_scales", "shared_gate", "shared_up", "shared_down",
+                 "gate_scales_tc", "up_scales_tc", "down_scales_tc"):
+        t = w.get(name)
+        setattr(L, name, None if t is None else t.data_ptr())
+    L.activation = w.get("activation", ACT_SWIGLU)
+    L.situ_beta = w.get("situ_beta", 4.0)
+    L.situ_linear_beta = w.get("situ_linear_beta", 0.0)
+    L.engine = engine
+    L.act_terms = act_terms
+    return L

@@ -1,0 +1,114 @@
+"""Parity of the tcgen05 kind::mxf4 expert engine (through the C ABI).
+
+Against the CPU oracle at small shapes, and against the SIMT engine (itself
+pinned to the oracle) at the released c2 shape. Tolerance: the north-star
+rel 2e-2 / abs 1e-3 on hidden states; routes bit-exact.
+"""
+import numpy as np
+import pytest
+
+from gpu_util import from_dev, layer_to_dev, to_dev, torch_cuda
+from oracle import ACT_SITU, ACT_SWIGLU, bf16_normal, make_moe_layer
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch():
+    return torch_cuda()
+
+
+@pytest.fixture(scope="module")
+def ctx(torch):
+    import k3xb
+    c = k3xb.Context(0)
+    c.use_stream()
+    yield c
+    c.close()
+
+
+def _run(torch, ctx, d, hidden_dev, T, engine, terms=6):
+    import k3xb
+    desc = k3xb.moe_layer_desc(d, engine=engine, act_terms=terms)
+    out = torch.empty((T, d["hidden"]), dtype=torch.float32, device="cuda")
+    ids = torch.empty((T, d["top_k"]), dtype=torch.int32, device="cuda")
+    ctx.moe_layer_forward(desc, hidden_dev, out, ids)
+    ctx.sync()
+    return out.cpu().numpy(), ids.cpu().numpy().view(np.uint32)
+
+
+def _report(got, want):
+    err = np.abs(got - want)
+    tol = 1e-3 + 2e-2 * np.abs(want)
+    return f"max|err| {err.max():.3e}, violations {(err > tol).sum()}/{err.size}"
+
+
+@pytest.mark.parametrize("act", [ACT_SWIGLU, ACT_SITU])
+@pytest.mark.parametrize("dims", [(256, 128, 16, 4, 5), (512, 256, 32, 8, 40), (384, 640, 12, 3, 9)])
+def test_mxf4_matches_oracle(torch, ctx, rs, act, dims):
+    import k3xb
+    H, I, E, K, T = dims
+    layer = make_moe_layer(rs, H + I + act, hidden=H, inter=I, experts=E, top_k=K, shared_inter=128,
+                           activation=act)
+    hidden = bf16_normal(np.random.default_rng(H), (T, H))
+    d = layer_to_dev(torch, layer)
+    got, ids = _run(torch, ctx, d, to_dev(torch, hidden), T, k3xb.ENGINE_MXF4)
+    want, want_ids, _ = rs.moe_layer(layer, hidden)
+    np.testing.assert_array_equal(ids, want_ids)
+    np.testing.assert_allclose(got, want, rtol=2e-2, atol=1e-3, err_msg=_report(got, want))
+
+
+def test_mxf4_prepared_scales_identical(torch, ctx, rs):
+    """Scales re-laid once (k3xb_prepare_mxfp4_scales) give bit-identical
+    results to the per-call re-layout."""
+    import k3xb
+    layer = make_moe_layer(rs, 17, hidden=256, inter=256, experts=8, top_k=2, shared_inter=0)
+    hidden = bf16_normal(np.random.default_rng(18), (6, 256))
+    d = layer_to_dev(torch, layer)
+    a, _ = _run(torch, ctx, d, to_dev(torch, hidden), 6, k3xb.ENGINE_MXF4)
+    ctx.prepare_layer_scales(d)
+    b, _ = _run(torch, ctx, d, to_dev(torch, hidden), 6, k3xb.ENGINE_MXF4)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_mxf4_term_count_converges(torch, ctx, rs):
+    """More E2M1 terms -> closer to the FP64 oracle (the split is exact in
+    the limit); 2 terms must already be within 10x of the tolerance."""
+    import k3xb
+    layer = make_moe_layer(rs, 5, hidden=512, inter=256, experts=16, top_k=4, shared_inter=0)
+    hidden = bf16_normal(np.random.default_rng(6), (8, 512))
+    d = layer_to_dev(torch, layer)
+    want, _, _ = rs.moe_layer(layer, hidden)
+    errs = []
+    for terms in (2, 4, 8):
+        got, _ = _run(torch, ctx, d, to_dev(torch, hidden), 8, k3xb.ENGINE_MXF4, terms)
+        errs.append(np.abs(got - want).max())
+    assert errs[2] <= errs[0], errs
+
+
+def test_mxf4_matches_simt_at_c2_shape(torch, ctx):
+    """Full released shape (H 7168, E 384, I 2048, Top-16, 64 tokens) on
+    device-generated weights: MXF4 engine vs SIMT engine."""
+    import k3xb
+    H, I, E, K, T = 7168, 2048, 384, 16, 64
+    u8 = lambda *s: torch.empty(s, dtype=torch.uint8, device="cuda")
+    d = dict(hidden=H, inter=I, experts=E, top_k=K, shared_inter=0, activation=k3xb.ACT_SWIGLU)
+    d["gate_packed"], d["gate_scales"] = u8(E, I, H // 2), u8(E, I, H // 32)
+    d["up_packed"], d["up_scales"] = u8(E, I, H // 2), u8(E, I, H // 32)
+    d["down_packed"], d["down_scales"] = u8(E, H, I // 2), u8(E, H, I // 32)
+    ctx.fill_normal_mxfp4(d["gate_packed"], d["gate_scales"], E * I, H, 1, 10, 0.02)
+    ctx.fill_normal_mxfp4(d["up_packed"], d["up_scales"], E * I, H, 1, 11, 0.02)
+    ctx.fill_normal_mxfp4(d["down_packed"], d["down_scales"], E * H, I, 1, 12, 0.02)
+    d["router"] = torch.empty((E, H), dtype=torch.int16, device="cuda")
+    ctx.fill_normal_bf16(d["router"], 1, 20, 0.02)
+    d["correction"] = torch.empty(E, dtype=torch.float32, device="cuda")
+    ctx.fill_normal_f32(d["correction"], 1, 21, 0.0, 0.02)
+    words = torch.empty((T, H), dtype=torch.int16, device="cuda")
+    ctx.fill_normal_bf16(words, 1, 30, 1.0)
+    hidden = (words.to(torch.int32) << 16).view(torch.float32).contiguous()
+    a, ia = _run(torch, ctx, d, hidden, T, k3xb.ENGINE_MXF4)
+    b, ib = _run(torch, ctx, d, hidden, T, k3xb.ENGINE_SIMT)
+    np.testing.assert_array_equal(ia, ib)
+    np.testing.assert_allclose(a, b, rtol=2e-2, atol=1e-3, err_msg=_report(a, b))
+    del d
+    torch.cuda.empty_cache()

@@ -1,0 +1,331 @@
+"""GPU parity of the CUDA path (through the C ABI) against the CPU oracle.
+
+Bars (north star): bit-exact selected expert ids, bucketing and accepted
+token counts; hidden states within rel 2e-2 / abs 1e-3; KDA within 1e-4.
+Router scores/contributions: the GPU sigmoid uses a correctly rounded expf
+while glibc's expf (the reference's std::exp) is off by one ulp on ~0.06% of
+inputs, so those two are compared to 1 ulp (rtol 2.4e-7 * few).
+"""
+import numpy as np
+import pytest
+
+from gpu_util import from_dev, layer_to_dev, to_dev, torch_cuda
+from oracle import ACT_SITU, ACT_SWIGLU, bf16_normal, bf16_words, make_moe_layer
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch():
+    return torch_cuda()
+
+
+@pytest.fixture(scope="module")
+def ctx(torch):
+    import k3xb
+    c = k3xb.Context(0)
+    c.use_stream()
+    yield c
+    c.close()
+
+
+# ----------------------------------------------------------------- (a) -----
+
+@pytest.mark.parametrize("T,E,H,K", [(5, 16, 256, 4), (64, 384, 7168, 16), (3, 3, 2, 2)])
+def test_route_parity(torch, ctx, rs, T, E, H, K):
+    g = np.random.default_rng(100 + T)
+    if H == 2:   # test_official_moe.cpp:50-52 literal router
+        router = np.array([0x3F80, 0, 0, 0x3F80, 0xBF80, 0x3F80], np.uint16).reshape(3, 2)
+        corr = np.array([0.0, 0.1, -0.05], np.float32)
+        hidden = np.tile(np.array([1.2578125, -0.32421875], np.float32), (T, 1))
+    else:
+        router = bf16_words(g.normal(0, 0.02, size=(E, H)))
+        corr = g.normal(0, 0.02, size=E).astype(np.float32)
+        hidden = bf16_normal(g, (T, H))
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    con = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    sco = torch.empty((T, E), dtype=torch.float32, device="cuda")
+    ctx.route(to_dev(torch, hidden), to_dev(torch, router), to_dev(torch, corr), K, ids, con, sco)
+    ctx.sync()
+    gi, gc, gs = from_dev(ids, np.uint32), from_dev(con, np.float32), from_dev(sco, np.float32)
+    for t in range(T):
+        logits = rs.router_logits(hidden[t], router)
+        oi, oc, os_ = rs.route_logits(logits, corr, K, want_scores=True)
+        assert gi[t].tolist() == oi.tolist(), f"token {t}: ids differ"
+        np.testing.assert_allclose(gs[t], os_, rtol=3e-7, atol=0)
+        np.testing.assert_allclose(gc[t], oc, rtol=1e-6, atol=0)
+    if H == 2:
+        assert gi[0].tolist() == [0, 1]
+        assert abs(gc[0, 0] - 0.6497964859) <= 1e-6
+
+
+def test_route_ties_lower_index(torch, ctx):
+    router = np.zeros((8, 64), np.uint16)
+    hidden = np.zeros((2, 64), np.float32)
+    corr = np.zeros(8, np.float32)
+    ids = torch.empty((2, 3), dtype=torch.int32, device="cuda")
+    con = torch.empty((2, 3), dtype=torch.float32, device="cuda")
+    ctx.route(to_dev(torch, hidden), to_dev(torch, router), to_dev(torch, corr), 3, ids, con)
+    ctx.sync()
+    assert from_dev(ids, np.uint32).tolist() == [[0, 1, 2]] * 2
+    assert np.all(from_dev(con, np.float32) == np.float32(1 / 3))
+
+
+def _plan_dev(torch, T, K, E):
+    z = lambda n, dt: torch.zeros(n, dtype=dt, device="cuda")
+    return dict(group_expert=z(E, torch.int32), group_offset=z(E + 1, torch.int32),
+                assign_token=z(T * K, torch.int32), assign_slot=z(T * K, torch.int32),
+                assign_contrib=z(T * K, torch.float32), group_count=z(1, torch.int32),
+                status=z(1, torch.int32))
+
+
+@pytest.mark.parametrize("T,K,E", [(2, 2, 4), (64, 16, 384), (576, 16, 384), (1, 1, 1)])
+def test_plan_parity(torch, ctx, rs, T, K, E):
+    g = np.random.default_rng(T * 7 + K)
+    if T == 2:   # test_expert_major.cpp:25-28
+        ids = np.array([[2, 1], [1, 3]], np.uint32)
+        con = np.array([[0.6, 0.4], [0.7, 0.3]], np.float32)
+    else:
+        ids = np.stack([g.choice(E, K, replace=False) for _ in range(T)]).astype(np.uint32)
+        con = g.random(size=(T, K)).astype(np.float32)
+    plan = _plan_dev(torch, T, K, E)
+    ctx.expert_major_plan(to_dev(torch, ids.view(np.int32)), to_dev(torch, con), E, plan)
+    ctx.sync()
+    want = rs.expert_major_plan(ids, con)
+    ng = int(plan["group_count"].item())
+    assert int(plan["status"].item()) == 0
+    assert ng == len(want["group_expert"])
+    np.testing.assert_array_equal(from_dev(plan["group_expert"], np.uint32)[:ng], want["group_expert"])
+    np.testing.assert_array_equal(from_dev(plan["group_offset"], np.uint32)[:ng + 1], want["group_offset"])
+    for key, dt in (("assign_token", np.uint32), ("assign_slot", np.uint32), ("assign_contrib", np.float32)):
+        np.testing.assert_array_equal(from_dev(plan[key], dt), want[key])
+
+
+def test_plan_rejects_duplicate_expert(torch, ctx):
+    import k3xb
+    ids = np.array([[1, 1]], np.int32)
+    con = np.array([[0.5, 0.5]], np.float32)
+    plan = _plan_dev(torch, 1, 2, 4)
+    ctx.expert_major_plan(to_dev(torch, ids), to_dev(torch, con), 4, plan)
+    torch.cuda.synchronize()
+    assert int(plan["status"].item()) == k3xb.INVALID_STATE
+
+
+# ------------------------------------------------------------- (b)+(c) -----
+
+def _moe_parity(torch, ctx, rs, layer, hidden, engine, act_terms=6):
+    import k3xb
+    d = layer_to_dev(torch, layer)
+    desc = k3xb.moe_layer_desc(d, engine=engine, act_terms=act_terms)
+    T, K = hidden.shape[0], layer["top_k"]
+    out = torch.empty((T, layer["hidden"]), dtype=torch.float32, device="cuda")
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    con = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    ctx.moe_layer_forward(desc, to_dev(torch, hidden), out, ids, con)
+    ctx.sync()
+    o_out, o_ids, o_con = rs.moe_layer(layer, hidden)
+    np.testing.assert_array_equal(from_dev(ids, np.uint32), o_ids)
+    np.testing.assert_allclose(from_dev(con, np.float32), o_con, rtol=1e-6)
+    return from_dev(out, np.float32), o_out
+
+
+@pytest.mark.parametrize("act", [ACT_SWIGLU, ACT_SITU])
+def test_moe_layer_simt_c1_dims(torch, ctx, rs, act):
+    import k3xb
+    layer = make_moe_layer(rs, 7 + act, hidden=256, inter=128, experts=16, top_k=4, shared_inter=128,
+                           activation=act)
+    hidden = bf16_normal(np.random.default_rng(8), (5, 256))
+    got, want = _moe_parity(torch, ctx, rs, layer, hidden, k3xb.ENGINE_SIMT)
+    np.testing.assert_allclose(got, want, rtol=2e-2, atol=1e-3)
+
+
+def test_moe_layer_simt_many_tokens(torch, ctx, rs):
+    import k3xb
+    layer = make_moe_layer(rs, 9, hidden=512, inter=256, experts=32, top_k=8, shared_inter=0)
+    hidden = bf16_normal(np.random.default_rng(10), (40, 512))
+    got, want = _moe_parity(torch, ctx, rs, layer, hidden, k3xb.ENGINE_SIMT)
+    np.testing.assert_allclose(got, want, rtol=2e-2, atol=1e-3)
+
+
+def test_moe_layer_host_entry_matches_device(torch, ctx, rs):
+    import k3xb
+    layer = make_moe_layer(rs, 11, hidden=256, inter=128, experts=16, top_k=4, shared_inter=128)
+    hidden = bf16_normal(np.random.default_rng(12), (5, 256))
+    d = layer_to_dev(torch, layer)
+    desc = k3xb.moe_layer_desc(d, engine=k3xb.ENGINE_SIMT)
+    out_d = torch.empty((5, 256), dtype=torch.float32, device="cuda")
+    ctx.moe_layer_forward(desc, to_dev(torch, hidden), out_d)
+    ctx.sync()
+    h = torch.from_numpy(hidden).pin_memory()
+    out_h = torch.empty((5, 256), dtype=torch.float32).pin_memory()
+    ids_h = torch.empty((5, 4), dtype=torch.int32).pin_memory()
+    ctx.moe_layer_forward_host(desc, h, out_h, ids_h)
+    np.testing.assert_array_equal(out_h.numpy(), out_d.cpu().numpy())
+
+
+# ----------------------------------------------------------------- (d) -----
+
+def _tree(seed, n=32, depth=4):
+    """BFS tree with branching in {2,3} until n nodes, depth <= 4 (c3)."""
+    g = np.random.default_rng(seed)
+    parent = []
+    level = [-1]
+    d = 0
+    while len(parent) < n and d < depth:
+        nxt = []
+        for p in level:
+            for _ in range(int(g.integers(2, 4))):
+                if len(parent) < n:
+                    parent.append(p)
+                    nxt.append(len(parent) - 1)
+        level = nxt
+        d += 1
+    return np.array(parent, np.int32)
+
+
+def _kda_inputs(g, S, N, h, d):
+    q = bf16_normal(g, (S, N, h, d))
+    k = bf16_normal(g, (S, N, h, d))
+    k = k / np.linalg.norm(k, axis=-1, keepdims=True)
+    q = q / np.linalg.norm(q, axis=-1, keepdims=True) / np.sqrt(d)
+    v = bf16_normal(g, (S, N, h, d))
+    ld = np.log(1 / (1 + np.exp(-g.normal(size=(S, N, h, d))))).astype(np.float32)
+    be = (1 / (1 + np.exp(-g.normal(size=(S, N, h))))).astype(np.float32)
+    f = lambda a: np.ascontiguousarray(a.reshape(S, N, h * d).astype(np.float32))
+    return f(q), f(k), f(v), f(ld), be.astype(np.float32)
+
+
+@pytest.mark.parametrize("shape", ["tree_c3", "linear", "forest"])
+def test_kda_tree_parity(torch, ctx, rs, shape):
+    g = np.random.default_rng(2)
+    if shape == "tree_c3":
+        S, h, d = 1, 32, 128
+        parent = _tree(2)
+    elif shape == "linear":
+        S, h, d = 3, 4, 64
+        parent = np.arange(-1, 8, dtype=np.int32)
+    else:
+        S, h, d = 2, 2, 32
+        parent = np.array([-1, 0, -1, 1, 2, 0, 3], np.int32)
+    N = parent.size
+    state = (g.normal(0, 0.05, size=(S, h, d, d))).astype(np.float32)
+    q, k, v, ld, be = _kda_inputs(g, S, N, h, d)
+    out = torch.empty((S, N, h * d), dtype=torch.float32, device="cuda")
+    dev = [to_dev(torch, a) for a in (state, q, k, v, ld, be)]
+    ctx.kda_tree(dev[0], parent, *dev[1:], out)
+    ctx.sync()
+    got = from_dev(out, np.float32)
+    for s in range(S):
+        want, states = rs.kda_tree(state[s], parent, q[s], k[s], v[s], ld[s], be[s], h, d, want_states=True)
+        np.testing.assert_allclose(got[s], want, rtol=0, atol=1e-4)
+        # commit: replay to a node and compare the state with the oracle's
+    commit = [N - 1 - s for s in range(S)]
+    st_out = torch.empty_like(dev[0])
+    ctx.kda_commit(dev[0], parent, *dev[1:], commit, st_out)
+    ctx.sync()
+    got_state = from_dev(st_out, np.float32)
+    for s in range(S):
+        _, states = rs.kda_tree(state[s], parent, q[s], k[s], v[s], ld[s], be[s], h, d, want_states=True)
+        np.testing.assert_allclose(got_state[s], states[commit[s]], rtol=0, atol=1e-4)
+    # -1 commits the prefix state unchanged
+    ctx.kda_commit(dev[0], parent, *dev[1:], [-1] * S, st_out)
+    ctx.sync()
+    np.testing.assert_array_equal(from_dev(st_out, np.float32), state)
+
+
+def test_kda_commit_bit_identical_to_tree_pass(torch, ctx):
+    """The committed state replays exactly the ops of the verify pass: a
+    second tree pass continuing from the committed state equals the
+    continuation computed inside one longer chain."""
+    g = np.random.default_rng(5)
+    S, h, d, N = 1, 2, 64, 6
+    parent = np.arange(-1, N - 1, dtype=np.int32)
+    state = g.normal(0, 0.05, size=(S, h, d, d)).astype(np.float32)
+    q, k, v, ld, be = _kda_inputs(g, S, N, h, d)
+    dev = [to_dev(torch, a) for a in (state, q, k, v, ld, be)]
+    full = torch.empty((S, N, h * d), dtype=torch.float32, device="cuda")
+    ctx.kda_tree(dev[0], parent, *dev[1:], full)
+    mid = torch.empty_like(dev[0])
+    ctx.kda_commit(dev[0], parent, *dev[1:], [2], mid)
+    tail = [t[:, 3:].contiguous() for t in dev[1:]]
+    rest = torch.empty((S, N - 3, h * d), dtype=torch.float32, device="cuda")
+    ctx.kda_tree(mid, np.arange(-1, N - 4, dtype=np.int32), *tail, rest)
+    ctx.sync()
+    np.testing.assert_array_equal(rest.cpu().numpy(), full[:, 3:].cpu().numpy())
+
+
+# ----------------------------------------------------------------- (e) -----
+
+@pytest.mark.parametrize("S,p,V", [(16, 8, 129280), (4, 0, 1000), (3, 4, 50)])
+def test_accept_greedy_parity(torch, ctx, rs, S, p, V):
+    g = np.random.default_rng(S + p)
+    logits = g.normal(size=(S, p + 1, V)).astype(np.float32)
+    drafts = np.zeros((S, max(p, 1)), np.uint32)
+    for s in range(S):   # accept a random prefix
+        cut = int(g.integers(0, p + 1))
+        for i in range(p):
+            drafts[s, i] = rs.argmax(logits[s, i]) if i < cut else int(g.integers(V))
+    if V == 50:
+        logits[0, 0, :] = 1.0   # all-equal row: first index wins
+    acc = torch.empty(S, dtype=torch.int32, device="cuda")
+    com = torch.empty((S, p + 1), dtype=torch.int32, device="cuda")
+    cnt = torch.empty(S, dtype=torch.int32, device="cuda")
+    tgt = torch.empty((S, p + 1), dtype=torch.int32, device="cuda")
+    ctx.accept_greedy(to_dev(torch, logits), to_dev(torch, drafts[:, :p].copy().view(np.int32)) if p
+                      else to_dev(torch, np.zeros(1, np.int32)), acc, com, cnt, tgt)
+    ctx.sync()
+    for s in range(S):
+        targets = np.array([rs.argmax(logits[s, i]) for i in range(p + 1)], np.uint32)
+        assert from_dev(tgt, np.uint32)[s].tolist() == targets.tolist()
+        a, committed, _ = rs.verify_greedy_block(0, drafts[s, :p], p, V, targets)
+        assert int(acc[s]) == a and int(cnt[s]) == len(committed)
+        assert from_dev(com, np.uint32)[s, :len(committed)].tolist() == committed
+
+
+@pytest.mark.parametrize("S,p,V", [(16, 8, 129280), (6, 3, 300), (2, 0, 64)])
+def test_accept_rejection_parity(torch, ctx, rs, S, p, V):
+    g = np.random.default_rng(40 + S)
+    tl = g.normal(size=(S, p + 1, V)).astype(np.float32)
+    dl = g.normal(size=(S, max(p, 1), V)).astype(np.float32)
+    drafts = g.integers(0, V, size=(S, max(p, 1))).astype(np.uint32)
+    for s in range(S):   # drafts likely under p so some get accepted
+        for i in range(p):
+            if g.random() < 0.5:
+                drafts[s, i] = int(np.argmax(tl[s, i]))
+    acc = torch.empty(S, dtype=torch.int32, device="cuda")
+    com = torch.empty((S, p + 1), dtype=torch.int32, device="cuda")
+    cnt = torch.empty(S, dtype=torch.int32, device="cuda")
+    ctx.accept_rejection(to_dev(torch, tl), to_dev(torch, dl[:, :max(p, 1)]),
+                         to_dev(torch, drafts.view(np.int32)), 1.0, 1234, 77, acc, com, cnt)
+    ctx.sync()
+    for s in range(S):
+        a, committed = rs.verify_rejection(tl[s], dl[s, :p], drafts[s, :p], 1.0, 1234, 77 + s)
+        assert int(acc[s]) == a
+        assert from_dev(com, np.uint32)[s, :len(committed)].tolist() == committed
+
+
+# ----------------------------------------------------------- synthetic -----
+
+def test_quantizer_bit_exact(torch, ctx, rs):
+    g = np.random.default_rng(3)
+    x = (g.normal(size=(64, 512)) * np.exp(g.normal(size=(64, 1)) * 3)).astype(np.float32)
+    x[0, :32] = 0.0
+    x[1, 5] = 0.25   # ties
+    x[1, 6] = 0.75
+    packed = torch.empty((64, 256), dtype=torch.uint8, device="cuda")
+    scales = torch.empty((64, 16), dtype=torch.uint8, device="cuda")
+    ctx.quantize_mxfp4(to_dev(torch, x), packed, scales)
+    ctx.sync()
+    wp, ws = rs.quantize_mxfp4(x)
+    np.testing.assert_array_equal(packed.cpu().numpy(), wp)
+    np.testing.assert_array_equal(scales.cpu().numpy(), ws)
+
+
+def test_fill_normal_mxfp4_statistics(torch, ctx, rs):
+    rows, cols = 256, 1024
+    packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device="cuda")
+    scales = torch.empty((rows, cols // 32), dtype=torch.uint8, device="cuda")
+    ctx.fill_normal_mxfp4(packed, scales, rows, cols, 1, 0, 0.02)
+    ctx.sync()
+    w = rs.decode_mxfp4(packed.cpu().numpy(), scales.cpu().numpy(), rows, cols)
+    assert abs(w.mean()) < 1e-3 and 0.018 < w.std() < 0.022
