@@ -86,6 +86,24 @@ int k3xb_route(k3xb_ctx* ctx, const float* hidden, uint32_t tokens,
                const float* correction, uint32_t experts, uint32_t top_k,
                uint32_t* ids, float* contributions, float* scores);
 
+/* Same routing as k3xb_route for callers that may not allocate device
+ * memory while they run (a serving loop that reserved all of HBM up front,
+ * an application whose own allocator owns the device, a latency-critical
+ * loop where cudaMalloc/cudaFree would synchronise the device). No
+ * counterpart in the reference. Needs no context: the logits live in a
+ * 1 MiB array compiled into the library (one per GPU, held until exit), so
+ * tokens * experts must be <= 262144, else K3XB_INVALID_EXTENT. Runs on
+ * `stream` (a cudaStream_t, NULL = legacy default stream) of the current
+ * device and returns before the work finishes. `status` (device int32, may
+ * be NULL) receives K3XB_INVALID_EXTENT for non-finite inputs. All calls on
+ * a device share the array, so calls that overlap on the GPU race. The
+ * first call on each device looks the array up once; make it before any
+ * stream capture starts. */
+int k3xb_route_static(const float* hidden, uint32_t tokens, uint32_t hidden_size,
+                      const uint16_t* router, const float* correction,
+                      uint32_t experts, uint32_t top_k, uint32_t* ids,
+                      float* contributions, int32_t* status, void* stream);
+
 /* build_expert_major_plan (runtime/src/expert_major.cpp:10-54): groups in
  * first-use order, assignments in (token, slot) order inside a group.
  * group_offset has room for experts+1 entries; the used prefix is
