@@ -156,6 +156,17 @@ typedef struct {
     const uint8_t* down_scales_tc;
 } k3xb_moe_layer;
 
+/* bf16_matvec (runtime/src/official_moe.cpp:39-59) for many tokens on
+ * tcgen05 kind::f16 tensor cores: out[t][r] = sum_k W[r][k] * x[t][k],
+ * rounded to bf16 when round_output != 0. W [out_features][in_features]
+ * bf16 words, x [tokens][in_features] float, out [tokens][out_features].
+ * FP32 accumulation (the reference accumulates in FP64); x is carried as
+ * two bf16 terms, exact for bf16-valued x. in_features % 8 == 0. Used for
+ * the LM head and the KDA projections. */
+int k3xb_linear_bf16(k3xb_ctx* ctx, const float* x, uint32_t tokens,
+                     uint32_t in_features, const uint16_t* weight,
+                     uint32_t out_features, int32_t round_output, float* out);
+
 /* Re-lays MXFP4 scales [rows][cols/32] (rows % 128 == 0, cols % 128 == 0)
  * into the layout the tcgen05 block-scaled MMA reads: 512-byte atoms of 128
  * rows x 4 scale blocks, atoms[rows/128][cols/128]. Done once per resident

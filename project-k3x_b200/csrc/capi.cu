@@ -48,6 +48,8 @@ struct MoeScratch {
     float* su;
     float* sa;
     float* shared_out;
+    uint16_t* sxb;   // tensor-core shared expert: input terms [2T][H]
+    uint16_t* sbd;   // tensor-core shared expert: down operand [2T][Is]
     float* hidden;   // host path only
     float* out;      // host path only
 };
@@ -72,6 +74,9 @@ void layout_moe(A& a, const k3xb_moe_layer& L, uint32_t T, bool host, MoeScratch
     r.su = a.template take<float>(T * Is);
     r.sa = a.template take<float>(T * Is);
     r.shared_out = a.template take<float>(T * H);
+    const bool tc_shared = L.engine == K3XB_ENGINE_MXF4 && L.shared_gate;
+    r.sxb = tc_shared ? a.template take<uint16_t>(2 * T * H) : nullptr;
+    r.sbd = tc_shared ? a.template take<uint16_t>(2 * T * Is) : nullptr;
     r.hidden = host ? a.template take<float>(T * H) : nullptr;
     r.out = host ? a.template take<float>(T * H) : nullptr;
 }
@@ -112,7 +117,10 @@ int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidd
         if ((st = launch_mxf4_experts(ctx, L, hidden, T, s.plan, s.slot_out))) return st;
     }
     const float* shared = nullptr;
-    if (L.shared_gate) {
+    if (L.shared_gate && L.engine == K3XB_ENGINE_MXF4) {
+        if ((st = launch_shared_tc(ctx, L, hidden, T, s.sxb, s.sbd, s.shared_out))) return st;
+        shared = s.shared_out;
+    } else if (L.shared_gate) {
         const uint32_t Is = L.shared_inter;
         if ((st = launch_bf16_rows(ctx, hidden, L.shared_gate, T, Is, H, s.sg))) return st;
         if ((st = launch_bf16_rows(ctx, hidden, L.shared_up, T, Is, H, s.su))) return st;
@@ -467,6 +475,18 @@ int k3xb_quantize_mxfp4(k3xb_ctx* ctx, const float* x, size_t rows, size_t cols,
     if (!x || !packed || !scales || !rows || !cols || cols % 32)
         return fail(ctx, K3XB_INVALID_MXFP4, "quantize arguments (cols % 32 == 0)");
     return launch_quantize_mxfp4(ctx, x, rows, cols, packed, scales);
+}
+
+int k3xb_linear_bf16(k3xb_ctx* ctx, const float* x, uint32_t tokens, uint32_t in_features, const uint16_t* weight,
+                     uint32_t out_features, int32_t round_output, float* out) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!x || !weight || !out || !tokens || !in_features || !out_features)
+        return fail(ctx, K3XB_INVALID_EXTENT, "linear arguments");
+    void* base;
+    int st = ensure_scratch(ctx, linear_scratch_bytes(tokens, in_features), &base);
+    if (st) return st;
+    return launch_linear_bf16(ctx, x, weight, tokens, out_features, in_features, round_output,
+                              static_cast<uint16_t*>(base), out);
 }
 
 int k3xb_prepare_mxfp4_scales(k3xb_ctx* ctx, const uint8_t* scales, size_t rows, size_t cols, uint8_t* out) {

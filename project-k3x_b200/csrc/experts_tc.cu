@@ -1,0 +1,682 @@
+// experts_tc.cu — (b)+(c) the MoE expert FFNs on tcgen05 tensor cores.
+//
+// Routed experts: block-scaled kind::mxf4 (E2M1 x E2M1, UE8M0 per-32
+// scales, FP32 accumulation in TMEM). Weights are consumed in the
+// reference's own MXFP4 layout — packed [rows][K/2] bytes, low nibble = even
+// column (runtime/src/ops.cpp:32-55) — and TMA-loaded straight from HBM into
+// 128B-swizzled shared memory (0.53 B per weight, no dequantisation). Only
+// the E8M0 scales are re-laid once into the 128-row x 4-block atoms that
+// tcgen05.cp moves into TMEM.
+//
+// The activation operand must be E2M1 as well, so each activation row is
+// split exactly into `terms` E2M1 rows with their own E8M0 block scales
+// (x = sum_t q_t + r, |r| shrinks >= 4x per term; 6 terms reproduce bf16
+// inputs exactly and fp32 SwiGLU outputs to ~2^-12 of the block maximum).
+// A token's terms are consecutive B rows (the MMA N dimension) and the
+// epilogue adds their accumulator columns.
+//
+// Shared expert: kind::f16 (bf16 weights x bf16 activation terms).
+//
+// Launches per MoE layer (routed):
+//   worklist       tiles of <= floor(128/terms) tokens per expert group and
+//                  one 16-byte descriptor per (tile, 128-row m-tile) item
+//   split_tokens   E2M1-term split of every hidden row, once per token
+//   gather_gu      tile-major gate/up B operand + scale atoms
+//   gateup         gate and up share the B tile; the epilogue applies
+//                  SwiGLU / SiTU (official_moe.cpp:95-96) and splits the result
+//                  into the down projection's E2M1 operand and scales
+//   down           the epilogue sums term columns, rounds to bf16
+//                  (official_moe.cpp:101) and scatters each row to its
+//                  (token, slot) for the ordered combine (c)
+#include "common.cuh"
+#include "kernels.cuh"
+#include "tc_pipeline.cuh"
+
+namespace k3xb {
+
+namespace {
+
+using tcp::kAtomBytes;
+using tcp::kBlockM;
+using tcp::kThreads;
+
+constexpr uint32_t kNMax = 128;         // activation rows (tokens x terms) per tile
+constexpr uint32_t kStagesGU = 4;
+constexpr uint32_t kStagesD = 6;
+
+constexpr uint32_t round16(uint32_t x) { return (x + 15u) / 16u * 16u; }
+
+// ---------------------------------------------------------------------------
+// one-time scale re-layout: [rows][K/32] -> atoms[rows/128][K/128][512]
+__global__ void sf_relayout_kernel(const uint8_t* __restrict__ in, size_t rows, uint32_t K,
+                                   uint8_t* __restrict__ out) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const uint32_t kb_count = K / 32;
+    if (i >= rows * kb_count) return;
+    const size_t r = i / kb_count;
+    const uint32_t kb = static_cast<uint32_t>(i % kb_count);
+    const size_t atom = (r / 128) * (K / 128) + kb / 4;
+    const uint32_t rr = static_cast<uint32_t>(r % 128);
+    out[atom * kAtomBytes + (rr % 32) * 16 + (rr / 32) * 4 + kb % 4] = in[i];
+}
+
+// ---------------------------------------------------------------------------
+struct Tables {
+    uint32_t* counts;       // [0] tiles, [1] gate/up items, [2] down items
+    uint32_t* tile_ntok;
+    uint32_t* tile_tok0;    // index into the plan's assignment arrays
+    uint4* desc_gu;         // {a_row, b_row, n | ntok << 16, tok0}
+    uint4* desc_d;
+};
+
+// One CTA of 1024 threads: one thread per group, Hillis-Steele scan of the
+// per-group tile counts, then each group writes its tiles and descriptors
+// (group-major, then m-tile, then n-tile, so the n-tiles that share a
+// weight tile run back to back and the second read hits L2).
+__global__ void __launch_bounds__(1024) worklist_kernel(const uint32_t* group_count, const uint32_t* group_offset,
+                                                        const uint32_t* group_expert, uint32_t terms, uint32_t H,
+                                                        uint32_t I, Tables t) {
+    __shared__ uint32_t scan[2][1024];
+    __shared__ uint32_t tile_base[1025];
+    const uint32_t ng = *group_count;
+    const uint32_t tpt = kNMax / terms;
+    const uint32_t mt_gu = I / kBlockM, mt_d = H / kBlockM;
+    const uint32_t g = threadIdx.x;
+    scan[0][g] = g < ng ? (group_offset[g + 1] - group_offset[g] + tpt - 1) / tpt : 0u;
+    __syncthreads();
+    uint32_t src = 0;
+    for (uint32_t off = 1; off < 1024; off <<= 1) {
+        scan[src ^ 1u][g] = scan[src][g] + (g >= off ? scan[src][g - off] : 0u);
+        src ^= 1u;
+        __syncthreads();
+    }
+    tile_base[g + 1] = scan[src][g];
+    if (g == 0) tile_base[0] = 0;
+    __syncthreads();
+    if (g == 0) {
+        t.counts[0] = tile_base[ng];
+        t.counts[1] = tile_base[ng] * mt_gu;
+        t.counts[2] = tile_base[ng] * mt_d;
+    }
+    if (g >= ng) return;
+    const uint32_t ntok_g = group_offset[g + 1] - group_offset[g];
+    const uint32_t tb = tile_base[g], nt = tile_base[g + 1] - tb;
+    const uint32_t e = group_expert[g];
+    for (uint32_t j = 0; j < nt; ++j) {
+        const uint32_t ntok = min(tpt, ntok_g - j * tpt), tok0 = group_offset[g] + j * tpt;
+        t.tile_ntok[tb + j] = ntok;
+        t.tile_tok0[tb + j] = tok0;
+        const uint32_t nz = round16(ntok * terms) | (ntok << 16);
+        for (uint32_t mt = 0; mt < mt_gu; ++mt)
+            t.desc_gu[tb * mt_gu + mt * nt + j] = make_uint4(e * I + mt * kBlockM, (tb + j) * kNMax, nz, tok0);
+        for (uint32_t mt = 0; mt < mt_d; ++mt)
+            t.desc_d[tb * mt_d + mt * nt + j] = make_uint4(e * H + mt * kBlockM, (tb + j) * kNMax, nz, tok0);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// E2M1-term split (bit-identical to oracle/k3x_oracle.c:k3xo_e2m1_terms).
+// Every token's hidden row once: tsplit[t][term][H/2], tsf[t][term][H/32].
+__global__ void __launch_bounds__(256) split_tokens_kernel(const float* __restrict__ hidden, uint32_t T,
+                                                           uint32_t H, uint32_t terms,
+                                                           uint8_t* __restrict__ tsplit,
+                                                           uint8_t* __restrict__ tsf) {
+    const uint32_t kbc = H / 32;
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<size_t>(T) * kbc) return;
+    const uint32_t t = static_cast<uint32_t>(i / kbc), kb = static_cast<uint32_t>(i % kbc);
+    const float* x = hidden + static_cast<size_t>(t) * H + kb * 32;
+    float r[32];
+#pragma unroll
+    for (int q = 0; q < 32; q += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(x + q);
+        r[q] = v.x; r[q + 1] = v.y; r[q + 2] = v.z; r[q + 3] = v.w;
+    }
+    for (uint32_t term = 0; term < terms; ++term) {
+        float amax = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(r[e]));
+        const int s = amax > 0.0f ? e2m1_block_exponent(amax) : 0;
+        const float inv = exp2i(-s), scl = exp2i(s);
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint32_t acc = 0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float v = r[8 * q + e];
+                const uint32_t code = e2m1_code(fabsf(v) * inv);
+                const bool neg = signbit(v) && code;
+                acc |= (code | (neg ? 8u : 0u)) << (4 * e);
+                const float qv = e2m1_magnitude(code) * scl;
+                r[8 * q + e] = neg ? __fadd_rn(v, qv) : __fsub_rn(v, qv);
+            }
+            w[q] = acc;
+        }
+        const size_t row = static_cast<size_t>(t) * terms + term;
+        *reinterpret_cast<uint4*>(tsplit + row * (H / 2) + kb * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        tsf[row * kbc + kb] = static_cast<uint8_t>(s + 127);
+    }
+}
+
+// Tile-major gate/up B operand (+ scale atoms) gathered from the per-token
+// split; zero rows pad the MMA N to a 16-multiple.
+__global__ void __launch_bounds__(256) gather_gu_kernel(const uint8_t* __restrict__ tsplit,
+                                                        const uint8_t* __restrict__ tsf, uint32_t H,
+                                                        const uint32_t* __restrict__ assign_token, Tables tb,
+                                                        uint32_t terms, uint8_t* __restrict__ b,
+                                                        uint8_t* __restrict__ sfb) {
+    const uint32_t tile = blockIdx.x;
+    if (tile >= tb.counts[0]) return;
+    const uint32_t ntok = tb.tile_ntok[tile], tok0 = tb.tile_tok0[tile];
+    const uint32_t used = ntok * terms, n = round16(used);
+    const uint32_t kbc = H / 32;
+    const size_t row_stride = H / 2;
+    uint8_t* base = b + static_cast<size_t>(tile) * kNMax * row_stride;
+    uint8_t* atoms = sfb + static_cast<size_t>(tile) * (kbc / 4) * kAtomBytes;
+    for (uint32_t i = threadIdx.x; i < n * kbc; i += blockDim.x) {
+        const uint32_t r = i / kbc, v = i % kbc;
+        uint4 val = make_uint4(0, 0, 0, 0);
+        uint8_t sf = 127;
+        if (r < used) {
+            const size_t src = static_cast<size_t>(assign_token[tok0 + r / terms]) * terms + r % terms;
+            val = *reinterpret_cast<const uint4*>(tsplit + src * row_stride + v * 16);
+            sf = tsf[src * kbc + v];
+        }
+        *reinterpret_cast<uint4*>(base + static_cast<size_t>(r) * row_stride + v * 16) = val;
+        atoms[(v / 4) * kAtomBytes + (r % 32) * 16 + (r / 32) * 4 + v % 4] = sf;
+    }
+}
+
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float activate(float g, float u, int act, float beta, float lbeta) {
+    // SwiGLU: (g * sigmoid(g)) * u; SiTU: runtime/src/ops.cpp:20-30.
+    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+    if (act == K3XB_ACT_SITU) {
+        const float bg = __fmul_rn(__fmul_rn(beta, tanhf(__fdiv_rn(g, beta))), sig);
+        const float bu = lbeta > 0.0f ? __fmul_rn(lbeta, tanhf(__fdiv_rn(u, lbeta))) : u;
+        return __fmul_rn(bg, bu);
+    }
+    return __fmul_rn(__fmul_rn(g, sig), u);
+}
+
+struct GuParams {
+    const uint4* desc;
+    const uint32_t* n_items;
+    const uint8_t* sfa_gate;
+    const uint8_t* sfa_up;
+    const uint8_t* sfb;       // gather_gu scales
+    uint8_t* b_down;          // epilogue outputs: the down projection's B operand
+    uint8_t* sfb_down;
+    uint32_t H, I, terms;
+    int act;
+    float beta, lbeta;
+    int* error;
+};
+
+struct DParams {
+    const uint4* desc;
+    const uint32_t* n_items;
+    const uint32_t* assign_token;
+    const uint32_t* assign_slot;
+    const uint8_t* sfa;
+    const uint8_t* sfb;
+    float* slot_out;
+    uint32_t H, I, terms, top_k;
+    int* error;
+};
+
+// TMEM columns
+constexpr uint32_t kColAccGate = 0, kColAccUp = 128, kColSfaGate = 256, kColSfaUp = 264, kColSfbGU = 272;
+constexpr uint32_t kColAccD = 0, kColSfaD = 256, kColSfbD = 264;   // down: two accumulator buffers at 0/128
+
+__global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_constant__ CUtensorMap map_gate,
+                                                              const __grid_constant__ CUtensorMap map_up,
+                                                              const __grid_constant__ CUtensorMap map_b,
+                                                              const GuParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    auto& sm = tcp::smem_from<kStagesGU, 2>(smem_raw);
+    const uint32_t terms = p.terms;
+    const uint32_t mtc = p.I / kBlockM;
+    auto get_desc = [&](uint32_t item) { return __ldg(p.desc + item); };
+    auto epilogue = [&](const uint4& d, uint32_t tmem, uint32_t q, uint32_t lane) {
+        const uint32_t tile = d.y / kNMax, mt = (d.x / kBlockM) % mtc;
+        const uint32_t ntok = tcp::desc_ntok(d);
+        const uint32_t used = ntok * terms, n = tcp::desc_n(d);
+        const uint32_t lane_base = (32u * q) << 16;
+        const size_t row_stride = p.I / 2;
+        uint8_t* brow = p.b_down + static_cast<size_t>(tile) * kNMax * row_stride + mt * 64 + q * 16;
+        uint8_t* sfbase = p.sfb_down + (static_cast<size_t>(tile) * (p.I / 128) + mt) * kAtomBytes + q;
+        float gs = 0.0f, us = 0.0f;
+        uint32_t tcount = 0, j = 0;
+        for (uint32_t c0 = 0; c0 < used; c0 += 16) {
+            float vg[16], vu[16];
+            tc::tmem_ld16(tmem + lane_base + kColAccGate + c0, vg);
+            tc::tmem_ld16(tmem + lane_base + kColAccUp + c0, vu);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (c0 + i >= used) break;
+                gs = __fadd_rn(gs, vg[i]);
+                us = __fadd_rn(us, vu[i]);
+                if (++tcount < terms) continue;
+                // token j done: a = act(g, u), split over this warp's 32 rows
+                // (one MX block of the down projection's K)
+                float r = activate(gs, us, p.act, p.beta, p.lbeta);
+                for (uint32_t t = 0; t < terms; ++t) {
+                    const float amax = warp_max(fabsf(r));
+                    const int s = amax > 0.0f ? e2m1_block_exponent(amax) : 0;
+                    const uint32_t cd = e2m1_code(fabsf(r) * exp2i(-s));
+                    const bool neg = signbit(r) && cd;
+                    const float qv = e2m1_magnitude(cd) * exp2i(s);
+                    r = neg ? __fadd_rn(r, qv) : __fsub_rn(r, qv);
+                    uint32_t word = (cd | (neg ? 8u : 0u)) << (4 * (lane % 8));
+                    word |= __shfl_xor_sync(0xffffffffu, word, 1);
+                    word |= __shfl_xor_sync(0xffffffffu, word, 2);
+                    word |= __shfl_xor_sync(0xffffffffu, word, 4);
+                    const uint32_t row = j * terms + t;
+                    if (lane % 8 == 0)
+                        *reinterpret_cast<uint32_t*>(brow + static_cast<size_t>(row) * row_stride + (lane / 8) * 4) = word;
+                    if (lane == 0) sfbase[(row % 32) * 16 + (row / 32) * 4] = static_cast<uint8_t>(s + 127);
+                }
+                gs = us = 0.0f;
+                tcount = 0;
+                ++j;
+            }
+        }
+        for (uint32_t row = used; row < n; ++row) {   // zero padding rows
+            if (lane % 8 == 0) *reinterpret_cast<uint32_t*>(brow + static_cast<size_t>(row) * row_stride + (lane / 8) * 4) = 0u;
+            if (lane == 0) sfbase[(row % 32) * 16 + (row / 32) * 4] = 127;
+        }
+    };
+    const uint8_t* sfa[2] = {p.sfa_gate, p.sfa_up};
+    const tcp::Config cfg{p.H, *p.n_items, 512, kColAccGate, kColAccUp, 0, kColSfaGate, kColSfaUp, kColSfbGU};
+    tcp::run_pipeline<kStagesGU, 2, false, 1>(sm, &map_gate, &map_up, &map_b, cfg, sfa, p.sfb, p.error, get_desc,
+                                              epilogue);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) down_kernel(const __grid_constant__ CUtensorMap map_down,
+                                                            const __grid_constant__ CUtensorMap map_b,
+                                                            const DParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    auto& sm = tcp::smem_from<kStagesD, 1>(smem_raw);
+    const uint32_t terms = p.terms;
+    const uint32_t mtc = p.H / kBlockM;
+    auto get_desc = [&](uint32_t item) { return __ldg(p.desc + item); };
+    auto epilogue = [&](const uint4& d, uint32_t tmem, uint32_t q, uint32_t lane) {
+        const uint32_t mt = (d.x / kBlockM) % mtc, tok0 = d.w;
+        const uint32_t used = tcp::desc_ntok(d) * terms;
+        const uint32_t lane_base = (32u * q) << 16;
+        const uint32_t h = mt * kBlockM + 32u * q + lane;
+        float ys = 0.0f;
+        uint32_t tcount = 0, j = 0;
+        for (uint32_t c0 = 0; c0 < used; c0 += 16) {
+            float v[16];
+            tc::tmem_ld16(tmem + lane_base + kColAccD + c0, v);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (c0 + i >= used) break;
+                ys = __fadd_rn(ys, v[i]);
+                if (++tcount < terms) continue;
+                const uint32_t a = tok0 + j;
+                const size_t dst = static_cast<size_t>(__ldg(p.assign_token + a)) * p.top_k + __ldg(p.assign_slot + a);
+                p.slot_out[dst * p.H + h] = round_bf16(ys);
+                ys = 0.0f;
+                tcount = 0;
+                ++j;
+            }
+        }
+    };
+    const uint8_t* sfa[1] = {p.sfa};
+    const tcp::Config cfg{p.I, *p.n_items, 512, kColAccD, kColAccD, 128, kColSfaD, kColSfaD, kColSfbD};
+    tcp::run_pipeline<kStagesD, 1, false, 2>(sm, &map_down, &map_down, &map_b, cfg, sfa, p.sfb, p.error, get_desc,
+                                             epilogue);
+}
+
+// ---------------------------------------------------------------------------
+// Shared expert on kind::f16 (shared_ffn, official_moe.cpp:105-117): bf16
+// weights, FP32 accumulation. Activations enter as two bf16 terms per token
+// (hi = bf16(x), lo = bf16(x - hi)), rows token*2 + t, so any float input is
+// carried to ~16 bits and bf16-valued inputs exactly. Tiles are 64 tokens
+// (N = 128). gate/up epilogue: g, u rounded to bf16 (bf16_matvec,
+// official_moe.cpp:56), activation, split into the down operand's two
+// terms. down epilogue: sum of the two term columns, rounded to bf16.
+constexpr uint32_t kSharedTok = 64;
+
+struct SharedParams {
+    uint32_t T, H, Is, items;
+    uint16_t* b_down;   // [2T][Is] bf16 words
+    float* out;         // [T][H]
+    int act;
+    float beta, lbeta;
+    int* error;
+};
+
+__device__ __forceinline__ uint16_t bf16_word(float v) { return static_cast<uint16_t>(__float_as_uint(v) >> 16); }
+
+__global__ void split_bf16_kernel(const float* __restrict__ x, size_t n, uint32_t H, uint16_t* __restrict__ out) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const size_t t = i / H, h = i % H;
+    const float hi = round_bf16(x[i]);
+    const float lo = round_bf16(__fsub_rn(x[i], hi));
+    out[(2 * t) * H + h] = bf16_word(hi);
+    out[(2 * t + 1) * H + h] = bf16_word(lo);
+}
+
+__device__ __forceinline__ uint4 shared_desc(uint32_t item, uint32_t mtc, uint32_t T) {
+    const uint32_t tile = item / mtc, mt = item % mtc;
+    const uint32_t ntok = min(kSharedTok, T - tile * kSharedTok);
+    return make_uint4(mt * kBlockM, tile * 2 * kSharedTok, round16(2 * ntok) | (ntok << 16), tile * kSharedTok);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) shared_gateup_kernel(const __grid_constant__ CUtensorMap map_gate,
+                                                                     const __grid_constant__ CUtensorMap map_up,
+                                                                     const __grid_constant__ CUtensorMap map_x,
+                                                                     const SharedParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    auto& sm = tcp::smem_from<kStagesGU, 2>(smem_raw);
+    const uint32_t mtc = p.Is / kBlockM;
+    auto get_desc = [&](uint32_t item) { return shared_desc(item, mtc, p.T); };
+    auto epilogue = [&](const uint4& d, uint32_t tmem, uint32_t q, uint32_t lane) {
+        const uint32_t used = 2 * tcp::desc_ntok(d);
+        const uint32_t lane_base = (32u * q) << 16;
+        const uint32_t m = d.x + 32u * q + lane;
+        for (uint32_t c0 = 0; c0 < used; c0 += 16) {
+            float vg[16], vu[16];
+            tc::tmem_ld16(tmem + lane_base + kColAccGate + c0, vg);
+            tc::tmem_ld16(tmem + lane_base + kColAccUp + c0, vu);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) {
+                if (c0 + i >= used) break;
+                const float g = round_bf16(__fadd_rn(vg[i], vg[i + 1]));
+                const float u = round_bf16(__fadd_rn(vu[i], vu[i + 1]));
+                const float a = activate(g, u, p.act, p.beta, p.lbeta);
+                const float hi = round_bf16(a);
+                const float lo = round_bf16(__fsub_rn(a, hi));
+                const size_t tok = d.w + (c0 + i) / 2;
+                p.b_down[(2 * tok) * p.Is + m] = bf16_word(hi);
+                p.b_down[(2 * tok + 1) * p.Is + m] = bf16_word(lo);
+            }
+        }
+    };
+    const uint8_t* none[2] = {nullptr, nullptr};
+    const tcp::Config cfg{p.H, p.items, 256, kColAccGate, kColAccUp, 0, 0, 0, 0};
+    tcp::run_pipeline<kStagesGU, 2, true, 1>(sm, &map_gate, &map_up, &map_x, cfg, none, nullptr, p.error, get_desc,
+                                             epilogue);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) shared_down_kernel(const __grid_constant__ CUtensorMap map_down,
+                                                                   const __grid_constant__ CUtensorMap map_b,
+                                                                   const SharedParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    auto& sm = tcp::smem_from<kStagesD, 1>(smem_raw);
+    const uint32_t mtc = p.H / kBlockM;
+    auto get_desc = [&](uint32_t item) { return shared_desc(item, mtc, p.T); };
+    auto epilogue = [&](const uint4& d, uint32_t tmem, uint32_t q, uint32_t lane) {
+        const uint32_t used = 2 * tcp::desc_ntok(d);
+        const uint32_t lane_base = (32u * q) << 16;
+        const uint32_t h = d.x + 32u * q + lane;
+        for (uint32_t c0 = 0; c0 < used; c0 += 16) {
+            float v[16];
+            tc::tmem_ld16(tmem + lane_base + kColAccD + c0, v);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) {
+                if (c0 + i >= used) break;
+                const size_t tok = d.w + (c0 + i) / 2;
+                p.out[tok * p.H + h] = round_bf16(__fadd_rn(v[i], v[i + 1]));
+            }
+        }
+    };
+    const uint8_t* none[1] = {nullptr};
+    const tcp::Config cfg{p.Is, p.items, 256, kColAccD, kColAccD, 128, 0, 0, 0};
+    tcp::run_pipeline<kStagesD, 1, true, 2>(sm, &map_down, &map_down, &map_b, cfg, none, nullptr, p.error, get_desc,
+                                            epilogue);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct TcState {
+    EncodeFn encode = nullptr;
+    bool configured = false;
+    bool configured_shared = false;
+};
+
+TcState* state_of(k3xb_ctx* ctx) {
+    if (!ctx->mxf4_state) ctx->mxf4_state = new TcState();
+    return static_cast<TcState*>(ctx->mxf4_state);
+}
+
+int get_encode(k3xb_ctx* ctx, EncodeFn* out) {
+    TcState* s = state_of(ctx);
+    if (!s->encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        K3XB_CUDA(ctx, cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (!fn || q != cudaDriverEntryPointSuccess)
+            return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "cuTensorMapEncodeTiled unavailable");
+        s->encode = reinterpret_cast<EncodeFn>(fn);
+    }
+    *out = s->encode;
+    return K3XB_OK;
+}
+
+// 2-D byte tensor [rows][row_bytes], box {128 B, box_rows}, 128B swizzle.
+// Every TMA x coordinate used with these maps is a multiple of 128 bytes.
+int make_map(k3xb_ctx* ctx, CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows,
+             uint32_t box_rows) {
+    EncodeFn encode;
+    int st = get_encode(ctx, &encode);
+    if (st) return st;
+    if (reinterpret_cast<uintptr_t>(base) % 16 || row_bytes % 16)
+        return fail(ctx, K3XB_INVALID_EXTENT, "tensor-core operands need 16-byte aligned rows");
+    const cuuint64_t dims[2] = {row_bytes, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {128, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "cuTensorMapEncodeTiled failed");
+    return K3XB_OK;
+}
+
+int relayout(k3xb_ctx* ctx, const uint8_t* scales, size_t rows, uint32_t K, uint8_t* out) {
+    const size_t n = rows * (K / 32);
+    sf_relayout_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(scales, rows, K, out);
+    K3XB_LAUNCHED(ctx);
+    return K3XB_OK;
+}
+
+struct Layout {
+    uint32_t terms, tpt, max_tiles, mt_gu, mt_d;
+    size_t b_gu, sfb_gu, b_d, sfb_d;
+    size_t sf_gate, sf_up, sf_down;   // per-call re-laid scales (0 when prepared)
+    size_t tsplit, tsf;               // per-token E2M1 split of the hidden rows
+};
+
+Layout layout_of(const k3xb_moe_layer& L, uint32_t T) {
+    Layout l{};
+    l.terms = L.act_terms > 0 ? static_cast<uint32_t>(L.act_terms) : 6u;
+    l.tpt = kNMax / l.terms;
+    const uint32_t assigns = T * L.top_k;
+    l.max_tiles = std::min(L.experts, assigns) + (assigns + l.tpt - 1) / l.tpt;
+    l.mt_gu = L.inter / kBlockM;
+    l.mt_d = L.hidden / kBlockM;
+    l.b_gu = static_cast<size_t>(l.max_tiles) * kNMax * (L.hidden / 2);
+    l.sfb_gu = static_cast<size_t>(l.max_tiles) * (L.hidden / 128) * kAtomBytes;
+    l.b_d = static_cast<size_t>(l.max_tiles) * kNMax * (L.inter / 2);
+    l.sfb_d = static_cast<size_t>(l.max_tiles) * (L.inter / 128) * kAtomBytes;
+    const size_t sf_gu = static_cast<size_t>(L.experts) * L.inter * (L.hidden / 32);
+    l.sf_gate = L.gate_scales_tc ? 0 : sf_gu;
+    l.sf_up = L.up_scales_tc ? 0 : sf_gu;
+    l.sf_down = L.down_scales_tc ? 0 : sf_gu;
+    l.tsplit = static_cast<size_t>(T) * l.terms * (L.hidden / 2);
+    l.tsf = static_cast<size_t>(T) * l.terms * (L.hidden / 32);
+    return l;
+}
+
+struct Buffers {
+    Tables tb;
+    uint8_t *b_gu, *sfb_gu, *b_d, *sfb_d, *sf[3], *tsplit, *tsf;
+};
+
+template <typename A>
+void carve(A& a, const Layout& l, Buffers* out) {
+    Buffers tmp;
+    Buffers& r = out ? *out : tmp;
+    r.tb.counts = a.template take<uint32_t>(4);
+    r.tb.tile_ntok = a.template take<uint32_t>(l.max_tiles);
+    r.tb.tile_tok0 = a.template take<uint32_t>(l.max_tiles);
+    r.tb.desc_gu = a.template take<uint4>(static_cast<size_t>(l.max_tiles) * l.mt_gu);
+    r.tb.desc_d = a.template take<uint4>(static_cast<size_t>(l.max_tiles) * l.mt_d);
+    r.b_gu = a.template take<uint8_t>(l.b_gu, 1024);
+    r.sfb_gu = a.template take<uint8_t>(l.sfb_gu, 1024);
+    r.b_d = a.template take<uint8_t>(l.b_d, 1024);
+    r.sfb_d = a.template take<uint8_t>(l.sfb_d, 1024);
+    r.sf[0] = a.template take<uint8_t>(l.sf_gate, 1024);
+    r.sf[1] = a.template take<uint8_t>(l.sf_up, 1024);
+    r.sf[2] = a.template take<uint8_t>(l.sf_down, 1024);
+    r.tsplit = a.template take<uint8_t>(l.tsplit, 1024);
+    r.tsf = a.template take<uint8_t>(l.tsf, 1024);
+}
+
+}  // namespace
+
+int make_byte_map(k3xb_ctx* ctx, void* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows) {
+    return make_map(ctx, static_cast<CUtensorMap*>(map), base, row_bytes, rows, box_rows);
+}
+
+int prepare_mxfp4_scales(k3xb_ctx* ctx, const uint8_t* scales, size_t rows, size_t cols, uint8_t* out) {
+    if (!scales || !out || !rows || rows % 128 || !cols || cols % 128)
+        return fail(ctx, K3XB_INVALID_MXFP4, "prepare scales: rows and cols must be multiples of 128");
+    return relayout(ctx, scales, rows, static_cast<uint32_t>(cols), out);
+}
+
+size_t mxf4_scratch_bytes(const k3xb_moe_layer& L, uint32_t T) {
+    if (L.engine != K3XB_ENGINE_MXF4) return 0;
+    Sizer s;
+    carve(s, layout_of(L, T), nullptr);
+    return s.used + 1024;
+}
+
+void set_mxf4_scratch(k3xb_ctx* ctx, void* region) { ctx->mxf4_scratch = region; }
+
+int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T,
+                        const k3xb_plan& plan, float* slot_out) {
+    const uint32_t H = L.hidden, I = L.inter;
+    if (H % 128 || I % 128)
+        return fail(ctx, K3XB_INVALID_EXTENT, "MXF4 engine needs hidden and inter multiples of 128");
+    if (L.act_terms < 0 || L.act_terms > 16)
+        return fail(ctx, K3XB_INVALID_EXTENT, "act_terms must be in [1, 16] (0 = default 6)");
+    if (L.experts > 1024) return fail(ctx, K3XB_INVALID_EXTENT, "MXF4 engine supports <= 1024 experts");
+    const Layout l = layout_of(L, T);
+    if (static_cast<uint64_t>(l.max_tiles) * kNMax >= (1ull << 31))
+        return fail(ctx, K3XB_INVALID_EXTENT, "MXF4 work list too large");
+    int st;
+    Carver c(reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ctx->mxf4_scratch) + 1023) & ~uintptr_t(1023)));
+    Buffers bf;
+    carve(c, l, &bf);
+    const uint8_t* sfa_gate = L.gate_scales_tc;
+    const uint8_t* sfa_up = L.up_scales_tc;
+    const uint8_t* sfa_down = L.down_scales_tc;
+    const size_t rows_gu = static_cast<size_t>(L.experts) * I, rows_d = static_cast<size_t>(L.experts) * H;
+    if (!sfa_gate) { if ((st = relayout(ctx, L.gate_scales, rows_gu, H, bf.sf[0]))) return st; sfa_gate = bf.sf[0]; }
+    if (!sfa_up) { if ((st = relayout(ctx, L.up_scales, rows_gu, H, bf.sf[1]))) return st; sfa_up = bf.sf[1]; }
+    if (!sfa_down) { if ((st = relayout(ctx, L.down_scales, rows_d, I, bf.sf[2]))) return st; sfa_down = bf.sf[2]; }
+
+    CUtensorMap map_gate, map_up, map_down, map_bgu, map_bd;
+    if ((st = make_map(ctx, &map_gate, L.gate_packed, H / 2, static_cast<uint64_t>(L.experts) * I, 128))) return st;
+    if ((st = make_map(ctx, &map_up, L.up_packed, H / 2, static_cast<uint64_t>(L.experts) * I, 128))) return st;
+    if ((st = make_map(ctx, &map_down, L.down_packed, I / 2, static_cast<uint64_t>(L.experts) * H, 128))) return st;
+    if ((st = make_map(ctx, &map_bgu, bf.b_gu, H / 2, static_cast<uint64_t>(l.max_tiles) * kNMax, 16))) return st;
+    if ((st = make_map(ctx, &map_bd, bf.b_d, I / 2, static_cast<uint64_t>(l.max_tiles) * kNMax, 16))) return st;
+
+    TcState* s = state_of(ctx);
+    const size_t smem_gu = tcp::smem_bytes<kStagesGU, 2>();
+    const size_t smem_d = tcp::smem_bytes<kStagesD, 1>();
+    if (!s->configured) {
+        K3XB_CUDA(ctx, cudaFuncSetAttribute(gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem_gu)));
+        K3XB_CUDA(ctx, cudaFuncSetAttribute(down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem_d)));
+        s->configured = true;
+    }
+
+    worklist_kernel<<<1, 1024, 0, ctx->stream>>>(plan.group_count, plan.group_offset, plan.group_expert, l.terms, H,
+                                                 I, bf.tb);
+    K3XB_LAUNCHED(ctx);
+    {
+        const size_t n = static_cast<size_t>(T) * (H / 32);
+        split_tokens_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(hidden, T, H, l.terms,
+                                                                                          bf.tsplit, bf.tsf);
+        K3XB_LAUNCHED(ctx);
+    }
+    gather_gu_kernel<<<l.max_tiles, 256, 0, ctx->stream>>>(bf.tsplit, bf.tsf, H, plan.assign_token, bf.tb, l.terms,
+                                                           bf.b_gu, bf.sfb_gu);
+    K3XB_LAUNCHED(ctx);
+
+    GuParams gp{bf.tb.desc_gu, bf.tb.counts + 1, sfa_gate, sfa_up, bf.sfb_gu, bf.b_d, bf.sfb_d, H, I, l.terms,
+                L.activation, L.situ_beta, L.situ_linear_beta, ctx->status_word};
+    gateup_kernel<<<ctx->sm_count, kThreads, smem_gu, ctx->stream>>>(map_gate, map_up, map_bgu, gp);
+    K3XB_LAUNCHED(ctx);
+    DParams dp{bf.tb.desc_d, bf.tb.counts + 2, plan.assign_token, plan.assign_slot, sfa_down, bf.sfb_d, slot_out,
+               H, I, l.terms, L.top_k, ctx->status_word};
+    down_kernel<<<ctx->sm_count, kThreads, smem_d, ctx->stream>>>(map_down, map_bd, dp);
+    K3XB_LAUNCHED(ctx);
+    return K3XB_OK;
+}
+
+int launch_shared_tc(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T, uint16_t* xb,
+                     uint16_t* bd, float* out) {
+    const uint32_t H = L.hidden, Is = L.shared_inter;
+    if (H % 128 || Is % 128)
+        return fail(ctx, K3XB_INVALID_EXTENT, "tensor-core shared expert needs hidden and shared_inter multiples of 128");
+    int st;
+    CUtensorMap map_gate, map_up, map_x, map_down, map_b;
+    if ((st = make_map(ctx, &map_gate, L.shared_gate, static_cast<uint64_t>(H) * 2, Is, 128))) return st;
+    if ((st = make_map(ctx, &map_up, L.shared_up, static_cast<uint64_t>(H) * 2, Is, 128))) return st;
+    if ((st = make_map(ctx, &map_x, xb, static_cast<uint64_t>(H) * 2, 2ull * T, 16))) return st;
+    if ((st = make_map(ctx, &map_down, L.shared_down, static_cast<uint64_t>(Is) * 2, H, 128))) return st;
+    if ((st = make_map(ctx, &map_b, bd, static_cast<uint64_t>(Is) * 2, 2ull * T, 16))) return st;
+    TcState* s = state_of(ctx);
+    const size_t smem_gu = tcp::smem_bytes<kStagesGU, 2>();
+    const size_t smem_d = tcp::smem_bytes<kStagesD, 1>();
+    if (!s->configured_shared) {
+        K3XB_CUDA(ctx, cudaFuncSetAttribute(shared_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem_gu)));
+        K3XB_CUDA(ctx, cudaFuncSetAttribute(shared_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem_d)));
+        s->configured_shared = true;
+    }
+    const size_t n = static_cast<size_t>(T) * H;
+    split_bf16_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(hidden, n, H, xb);
+    K3XB_LAUNCHED(ctx);
+    const uint32_t tiles = (T + kSharedTok - 1) / kSharedTok;
+    SharedParams p{T, H, Is, tiles * (Is / kBlockM), bd, out, L.activation, L.situ_beta, L.situ_linear_beta,
+                   ctx->status_word};
+    shared_gateup_kernel<<<std::min<uint32_t>(ctx->sm_count, p.items), kThreads, smem_gu, ctx->stream>>>(
+        map_gate, map_up, map_x, p);
+    K3XB_LAUNCHED(ctx);
+    p.items = tiles * (H / kBlockM);
+    shared_down_kernel<<<std::min<uint32_t>(ctx->sm_count, p.items), kThreads, smem_d, ctx->stream>>>(map_down,
+                                                                                                    map_b, p);
+    K3XB_LAUNCHED(ctx);
+    return K3XB_OK;
+}
+
+void release_mxf4_resources(k3xb_ctx* ctx) {
+    if (!ctx->mxf4_state) return;
+    delete static_cast<TcState*>(ctx->mxf4_state);
+    ctx->mxf4_state = nullptr;
+}
+
+}  // namespace k3xb

@@ -61,4 +61,13 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
                         const k3xb_plan& plan, float* slot_out);
 void release_mxf4_resources(k3xb_ctx* ctx);
 int prepare_mxfp4_scales(k3xb_ctx* ctx, const uint8_t* scales, size_t rows, size_t cols, uint8_t* out);
+// 2-D byte tensor map (128B swizzle, box {128 B, box_rows}); map is a CUtensorMap*
+int make_byte_map(k3xb_ctx* ctx, void* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows);
+// linear_tc.cu — out[T][rows] = (round_bf16)(W . x), x split into two bf16 terms
+size_t linear_scratch_bytes(uint32_t T, uint32_t K);
+int launch_linear_bf16(k3xb_ctx* ctx, const float* x, const uint16_t* W, uint32_t T, uint32_t rows, uint32_t K,
+                       int round_out, uint16_t* xterms, float* out);
+// shared expert on kind::f16 tensor cores; xb [2T][H], bd [2T][Is] bf16 scratch
+int launch_shared_tc(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T, uint16_t* xb,
+                     uint16_t* bd, float* out);
 }  // namespace k3xb

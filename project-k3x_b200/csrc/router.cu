@@ -17,133 +17,190 @@ namespace k3xb {
 
 namespace {
 
-constexpr int kTok = 8;
+// CTA tile: 32 experts (one per lane) x 16 tokens (4 per warp, 4 warps).
+// W and x stream through a double-buffered shared-memory chunk of kChunk
+// hidden columns: W transposed to [h][expert] (float, exact from bf16) so
+// lanes read consecutive words, x as double [h][token] so a warp's 4 tokens
+// are one broadcast 32-byte read. Padding (h >= H) is zero, and adding
+// fma(0, 0, acc) = acc leaves each chain bit-identical.
+constexpr int kExp = 32;
+constexpr int kTokCta = 16;
+constexpr int kChunk = 256;
+constexpr size_t kLogitsSmem = 2 * kChunk * kExp * sizeof(float) + 2 * kChunk * kTokCta * sizeof(double);
 
 __global__ void __launch_bounds__(128) router_logits_kernel(
     const float* __restrict__ hidden, const uint16_t* __restrict__ W, uint32_t T,
     uint32_t H, uint32_t E, float* __restrict__ logits) {
-    const uint32_t e = blockIdx.x * blockDim.x + threadIdx.x;
-    const uint32_t t0 = blockIdx.y * kTok;
-    if (e >= E) return;
-    double acc[kTok];
-    const float* x[kTok];
-#pragma unroll
-    for (int j = 0; j < kTok; ++j) {
-        acc[j] = 0.0;
-        const uint32_t t = (t0 + j < T) ? t0 + j : T - 1;
-        x[j] = hidden + static_cast<size_t>(t) * H;
-    }
-    const uint16_t* w = W + static_cast<size_t>(e) * H;
+    extern __shared__ __align__(16) unsigned char router_smem[];
+    float* ws = reinterpret_cast<float*>(router_smem);                        // [2][kChunk][kExp]
+    double* xs = reinterpret_cast<double*>(ws + 2 * kChunk * kExp);           // [2][kChunk][kTokCta]
+    const uint32_t tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+    const uint32_t e0 = blockIdx.x * kExp, t0 = blockIdx.y * kTokCta;
+
+    // Stage registers: 8 x (8 bf16 of one expert row) and 8 x (4 floats of
+    // one token row) per thread, loaded for chunk c+1 while chunk c computes.
+    // Vector path when rows are 16-byte aligned; element path otherwise.
     const bool vec = (H % 8 == 0) && ((reinterpret_cast<uintptr_t>(W) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(hidden) & 15) == 0);
-    uint32_t h = 0;
-    if (vec) {
-        for (; h < H; h += 8) {
-            const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + h));
-            float wf[8];
-            wf[0] = __uint_as_float(wv.x << 16); wf[1] = __uint_as_float(wv.x & 0xffff0000u);
-            wf[2] = __uint_as_float(wv.y << 16); wf[3] = __uint_as_float(wv.y & 0xffff0000u);
-            wf[4] = __uint_as_float(wv.z << 16); wf[5] = __uint_as_float(wv.z & 0xffff0000u);
-            wf[6] = __uint_as_float(wv.w << 16); wf[7] = __uint_as_float(wv.w & 0xffff0000u);
+    const uint32_t we = e0 + tid % kExp, wseg = tid / kExp;         // W: segments wseg + 4k
+    const uint32_t xt = t0 + tid % kTokCta, xseg = tid / kTokCta;   // x: segments xseg + 8k
+    uint4 wr[8];
+    float4 xr[8];
+    auto fetch = [&](uint32_t h0) {
 #pragma unroll
-            for (int j = 0; j < kTok; ++j) {
-                const float4 a = __ldg(reinterpret_cast<const float4*>(x[j] + h));
-                const float4 b = __ldg(reinterpret_cast<const float4*>(x[j] + h + 4));
-                acc[j] = fma(static_cast<double>(wf[0]), static_cast<double>(a.x), acc[j]);
-                acc[j] = fma(static_cast<double>(wf[1]), static_cast<double>(a.y), acc[j]);
-                acc[j] = fma(static_cast<double>(wf[2]), static_cast<double>(a.z), acc[j]);
-                acc[j] = fma(static_cast<double>(wf[3]), static_cast<double>(a.w), acc[j]);
-                acc[j] = fma(static_cast<double>(wf[4]), static_cast<double>(b.x), acc[j]);
-                acc[j] = fma(static_cast<double>(wf[5]), static_cast<double>(b.y), acc[j]);
-                acc[j] = fma(static_cast<double>(wf[6]), static_cast<double>(b.z), acc[j]);
-                acc[j] = fma(static_cast<double>(wf[7]), static_cast<double>(b.w), acc[j]);
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t hw = h0 + (wseg + 4 * k) * 8;
+            wr[k] = make_uint4(0, 0, 0, 0);
+            if (we < E && hw < H) {
+                const uint16_t* src = W + static_cast<size_t>(we) * H + hw;
+                if (vec) {
+                    wr[k] = __ldg(reinterpret_cast<const uint4*>(src));
+                } else {
+                    uint16_t v[8];
+                    for (int i = 0; i < 8; ++i) v[i] = hw + i < H ? src[i] : 0;
+                    wr[k] = make_uint4(v[0] | (v[1] << 16), v[2] | (v[3] << 16), v[4] | (v[5] << 16),
+                                       v[6] | (v[7] << 16));
+                }
+            }
+            const uint32_t hx = h0 + (xseg + 8 * k) * 4;
+            xr[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (xt < T && hx < H) {
+                const float* src = hidden + static_cast<size_t>(xt) * H + hx;
+                if (vec) {
+                    xr[k] = __ldg(reinterpret_cast<const float4*>(src));
+                } else {
+                    xr[k].x = src[0];
+                    xr[k].y = hx + 1 < H ? src[1] : 0.f;
+                    xr[k].z = hx + 2 < H ? src[2] : 0.f;
+                    xr[k].w = hx + 3 < H ? src[3] : 0.f;
+                }
             }
         }
-    } else {
-        for (; h < H; ++h) {
-            const double wd = decode_bf16(w[h]);
+    };
+    auto stash = [&](uint32_t buf) {
+        float* wdst = ws + buf * kChunk * kExp;
+        double* xdst = xs + buf * kChunk * kTokCta;
 #pragma unroll
-            for (int j = 0; j < kTok; ++j) acc[j] = fma(wd, static_cast<double>(x[j][h]), acc[j]);
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t hw = (wseg + 4 * k) * 8;
+            const uint32_t q[4] = {wr[k].x, wr[k].y, wr[k].z, wr[k].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                wdst[(hw + 2 * i) * kExp + tid % kExp] = __uint_as_float(q[i] << 16);
+                wdst[(hw + 2 * i + 1) * kExp + tid % kExp] = __uint_as_float(q[i] & 0xffff0000u);
+            }
+            const uint32_t hx = (xseg + 8 * k) * 4;
+            xdst[(hx + 0) * kTokCta + tid % kTokCta] = xr[k].x;
+            xdst[(hx + 1) * kTokCta + tid % kTokCta] = xr[k].y;
+            xdst[(hx + 2) * kTokCta + tid % kTokCta] = xr[k].z;
+            xdst[(hx + 3) * kTokCta + tid % kTokCta] = xr[k].w;
         }
+    };
+
+    double acc[4] = {0.0, 0.0, 0.0, 0.0};
+    const uint32_t chunks = (H + kChunk - 1) / kChunk;
+    fetch(0);
+    stash(0);
+    __syncthreads();
+    for (uint32_t c = 0; c < chunks; ++c) {
+        const uint32_t buf = c & 1u;
+        if (c + 1 < chunks) fetch((c + 1) * kChunk);
+        const float* wb = ws + buf * kChunk * kExp;
+        const double* xb = xs + buf * kChunk * kTokCta + 4 * warp;
+#pragma unroll 8
+        for (uint32_t h = 0; h < kChunk; ++h) {
+            const double w = static_cast<double>(wb[h * kExp + lane]);
+            const double2 xa = *reinterpret_cast<const double2*>(xb + h * kTokCta);
+            const double2 xc = *reinterpret_cast<const double2*>(xb + h * kTokCta + 2);
+            acc[0] = fma(w, xa.x, acc[0]);
+            acc[1] = fma(w, xa.y, acc[1]);
+            acc[2] = fma(w, xc.x, acc[2]);
+            acc[3] = fma(w, xc.y, acc[3]);
+        }
+        if (c + 1 < chunks) stash(buf ^ 1u);
+        __syncthreads();
     }
+    const uint32_t e = e0 + lane;
 #pragma unroll
-    for (int j = 0; j < kTok; ++j)
-        if (t0 + j < T) logits[static_cast<size_t>(t0 + j) * E + e] = static_cast<float>(acc[j]);
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t t = t0 + 4 * warp + j;
+        if (e < E && t < T) logits[static_cast<size_t>(t) * E + e] = static_cast<float>(acc[j]);
+    }
 }
 
-// route_official_moe_logits (official_moe.cpp:211-245), one warp per token.
-// sigmoid = 1 / (1 + expf(-l)) in float; expf is evaluated as the correctly
-// rounded float(exp(double)).
+// route_official_moe_logits (official_moe.cpp:211-245), one CTA per token:
+// all threads compute sigmoid scores (1 / (1 + expf(-l)) in float, with expf
+// evaluated as the correctly rounded float(exp(double))), then warp 0 picks
+// the Top-k under (adjusted desc, index asc) and forms the contributions.
 constexpr int kMaxPerLane = 32;   // E <= 1024
+constexpr int kTopkThreads = 128;
 
-__global__ void __launch_bounds__(256) topk_kernel(
+__global__ void __launch_bounds__(kTopkThreads) topk_kernel(
     const float* __restrict__ logits, const float* __restrict__ correction, uint32_t T,
     uint32_t E, uint32_t K, uint32_t* __restrict__ ids, float* __restrict__ contrib,
     float* __restrict__ scores_out, int32_t* __restrict__ status) {
-    const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
-    const uint32_t lane = threadIdx.x % 32;
-    if (warp >= T) return;
-    const float* l = logits + static_cast<size_t>(warp) * E;
-    float score[kMaxPerLane], adj[kMaxPerLane];
-    bool bad = false;
+    __shared__ float s_score[32 * kMaxPerLane], s_adj[32 * kMaxPerLane];
+    __shared__ float sel_score[32];
+    __shared__ uint32_t sel_id[32];
+    const uint32_t token = blockIdx.x, tid = threadIdx.x, lane = tid % 32;
+    if (token >= T) return;
+    const float* l = logits + static_cast<size_t>(token) * E;
+    int bad = 0;
+    for (uint32_t e = tid; e < E; e += blockDim.x) {
+        const float x = l[e];
+        const float c = correction[e];
+        bad |= !isfinite(x) || !isfinite(c);
+        const float ex = static_cast<float>(exp(-static_cast<double>(x)));
+        const float sc = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
+        s_score[e] = sc;
+        s_adj[e] = __fadd_rn(sc, c);
+        if (scores_out) scores_out[static_cast<size_t>(token) * E + e] = sc;
+    }
+    if (__syncthreads_or(bad)) {
+        if (tid == 0) atomicExch(status, K3XB_INVALID_EXTENT);
+        return;
+    }
+    if (tid >= 32) return;
+    float adj[kMaxPerLane];
 #pragma unroll
     for (int i = 0; i < kMaxPerLane; ++i) {
         const uint32_t e = lane + 32u * i;
-        score[i] = 0.0f;
-        adj[i] = -INFINITY;
-        if (e < E) {
-            const float x = l[e];
-            const float c = correction[e];
-            bad |= !isfinite(x) || !isfinite(c);
-            const float ex = static_cast<float>(exp(-static_cast<double>(x)));
-            score[i] = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
-            adj[i] = __fadd_rn(score[i], c);
-            if (scores_out) scores_out[static_cast<size_t>(warp) * E + e] = score[i];
-        }
-    }
-    if (__any_sync(0xffffffffu, bad)) {
-        if (lane == 0) atomicExch(status, K3XB_INVALID_EXTENT);
-        return;
+        adj[i] = e < E ? s_adj[e] : -INFINITY;
     }
     uint32_t taken = 0;   // bit i: this lane's entry i is selected
     double total = 0.0;
-    float sel_score[32];
-    uint32_t sel_id[32];
     for (uint32_t slot = 0; slot < K; ++slot) {
-        // lane-local best under (adjusted desc, index asc)
         float bv = -INFINITY;
         uint32_t bi = 0xffffffffu;
-        float bs = 0.0f;
 #pragma unroll
         for (int i = 0; i < kMaxPerLane; ++i) {
             const uint32_t e = lane + 32u * i;
             if (e < E && !(taken >> i & 1u)) {
-                if (bi == 0xffffffffu || adj[i] > bv) { bv = adj[i]; bi = e; bs = score[i]; }
+                if (bi == 0xffffffffu || adj[i] > bv) { bv = adj[i]; bi = e; }
             }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
             const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            const float os = __shfl_xor_sync(0xffffffffu, bs, o);
             const bool better = (oi != 0xffffffffu) &&
                                 (bi == 0xffffffffu || ov > bv || (ov == bv && oi < bi));
-            if (better) { bv = ov; bi = oi; bs = os; }
+            if (better) { bv = ov; bi = oi; }
         }
         if ((bi % 32) == lane) taken |= 1u << (bi / 32);
-        if (slot < 32) { sel_score[slot] = bs; sel_id[slot] = bi; }
+        const float bs = s_score[bi];
+        if (lane == 0) { sel_score[slot] = bs; sel_id[slot] = bi; }
         total += static_cast<double>(bs);   // slot order, like the reference
     }
+    __syncwarp();
     if (!isfinite(total) || total <= 0.0) {
         if (lane == 0) atomicExch(status, K3XB_INVALID_EXTENT);
         return;
     }
-    if (lane == 0) {
-        for (uint32_t slot = 0; slot < K && slot < 32; ++slot) {
-            ids[static_cast<size_t>(warp) * K + slot] = sel_id[slot];
-            contrib[static_cast<size_t>(warp) * K + slot] =
-                static_cast<float>(static_cast<double>(sel_score[slot]) / total);
-        }
+    if (lane < K) {
+        ids[static_cast<size_t>(token) * K + lane] = sel_id[lane];
+        contrib[static_cast<size_t>(token) * K + lane] =
+            static_cast<float>(static_cast<double>(sel_score[lane]) / total);
     }
 }
 
@@ -236,8 +293,14 @@ size_t plan_smem_bytes(uint32_t T, uint32_t E) {
 
 int launch_router_logits(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_t H,
                          const uint16_t* W, uint32_t E, float* logits) {
-    dim3 grid((E + 127) / 128, (T + kTok - 1) / kTok);
-    router_logits_kernel<<<grid, 128, 0, ctx->stream>>>(hidden, W, T, H, E, logits);
+    static bool configured = false;
+    if (!configured) {
+        K3XB_CUDA(ctx, cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(kLogitsSmem)));
+        configured = true;
+    }
+    dim3 grid((E + kExp - 1) / kExp, (T + kTokCta - 1) / kTokCta);
+    router_logits_kernel<<<grid, 128, kLogitsSmem, ctx->stream>>>(hidden, W, T, H, E, logits);
     K3XB_LAUNCHED(ctx);
     return K3XB_OK;
 }
@@ -247,9 +310,7 @@ int launch_topk(k3xb_ctx* ctx, const float* logits, const float* correction, uin
                 int32_t* status) {
     if (E > 32u * kMaxPerLane || K == 0 || K > E || K > 32)
         return fail(ctx, K3XB_INVALID_EXTENT, "route: need 0 < top_k <= min(32, experts) and experts <= 1024");
-    const uint32_t warps_per_block = 8;
-    topk_kernel<<<(T + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0,
-                  ctx->stream>>>(logits, correction, T, E, K, ids, contrib, scores, status);
+    topk_kernel<<<T, kTopkThreads, 0, ctx->stream>>>(logits, correction, T, E, K, ids, contrib, scores, status);
     K3XB_LAUNCHED(ctx);
     return K3XB_OK;
 }

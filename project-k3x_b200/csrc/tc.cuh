@@ -127,6 +127,17 @@ __device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t adesc, uint64
         : "memory");
 }
 
+// Single thread: D(tmem) (+)= A x B^T, kind::f16 (bf16 inputs, fp32 accum), M=128, K=16.
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Single thread: arrive on `bar` when all prior tcgen05 ops of this thread finish.
 __device__ __forceinline__ void commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -173,6 +184,12 @@ __device__ __forceinline__ uint64_t desc_sf_atom(const void* smem) {
 __host__ __device__ __forceinline__ uint32_t idesc_mxf4(uint32_t n, uint32_t a_sf_id, uint32_t b_sf_id) {
     return (b_sf_id << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
            (a_sf_id << 29);
+}
+
+// Instruction descriptor, kind::f16: FP32 accumulator, BF16 A and B (format
+// 1), K-major both, M = 128, N = n.
+__host__ __device__ __forceinline__ uint32_t idesc_bf16(uint32_t n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((128u >> 4) << 24);
 }
 
 }  // namespace tc

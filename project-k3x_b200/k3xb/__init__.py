@@ -93,6 +93,7 @@ def library() -> C.CDLL:
             "k3xb_quantize_mxfp4": [vp, vp, sz, sz, vp, vp],
             "k3xb_fill_normal_mxfp4": [vp, vp, vp, sz, sz, u64, u64, f32],
             "k3xb_prepare_mxfp4_scales": [vp, vp, sz, sz, vp],
+            "k3xb_linear_bf16": [vp, vp, u32, u32, vp, u32, C.c_int32, vp],
         }
         for name, args in sigs.items():
             fn = getattr(lib, name)
@@ -147,7 +148,11 @@ class Context:
         """Binds a torch.cuda.Stream (default: torch's current stream)."""
         import torch
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
-        self._check(self.lib.k3xb_set_stream(self.h, C.c_void_p(s.cuda_stream)), "set_stream")
+        # torch's default stream has handle 0, which the C ABI reads as "the
+        # context's own stream"; pass cudaStreamLegacy (0x1) so work stays
+        # ordered with torch's default-stream work.
+        handle = s.cuda_stream if s.cuda_stream else 0x1
+        self._check(self.lib.k3xb_set_stream(self.h, C.c_void_p(handle)), "set_stream")
 
     def sync(self):
         self._check(self.lib.k3xb_sync(self.h), "sync")
@@ -226,6 +231,13 @@ class Context:
         rows, cols = x.shape
         self._check(self.lib.k3xb_quantize_mxfp4(self.h, _p(x), rows, cols, _p(packed), _p(scales)),
                     "quantize_mxfp4")
+
+    def linear_bf16(self, x, weight, out, round_output=True):
+        """out[T][rows] = (round_bf16)(weight[rows][K] . x[T][K]) on kind::f16."""
+        T, K = x.shape
+        rows = weight.shape[0]
+        self._check(self.lib.k3xb_linear_bf16(self.h, _p(x), T, K, _p(weight), rows,
+                                              1 if round_output else 0, _p(out)), "linear_bf16")
 
     def prepare_mxfp4_scales(self, scales, rows, cols, out):
         self._check(self.lib.k3xb_prepare_mxfp4_scales(self.h, _p(scales), rows, cols, _p(out)),

@@ -31,3 +31,25 @@ def layer_to_dev(torch, layer: dict) -> dict:
 def assert_close_bf16(actual, expected, rtol=2e-2, atol=1e-3):
     """The north-star tolerance for hidden states and logits."""
     np.testing.assert_allclose(actual, expected, rtol=rtol, atol=atol)
+
+
+def bf16_step(x):
+    """One bf16 step at the binade of |x|."""
+    return np.ldexp(1.0, np.floor(np.log2(np.abs(x) + 1e-30)).astype(int) - 7)
+
+
+def assert_hidden_close(actual, expected, operand_scale, max_flip_fraction=0.01):
+    """North-star tolerance (rel 2e-2 / abs 1e-3) with one allowance: the
+    reference rounds to bf16 at fixed points (each bf16_matvec output, the
+    slot mix, mixed + shared); FP32-vs-FP64 accumulation moves a value across
+    a rounding midpoint now and then, and where addends cancel that one-step
+    flip of an operand (size `operand_scale`) lands in a small output. Such
+    elements may differ by up to two bf16 steps of the operand scale, and
+    must be rare."""
+    err = np.abs(actual - expected)
+    strict = 1e-3 + 2e-2 * np.abs(expected)
+    loose = strict + 2 * bf16_step(operand_scale)
+    bad = np.nonzero(err > loose)
+    assert bad[0].size == 0, (f"{bad[0].size} elements beyond tolerance; first {[b[:3] for b in bad]}: "
+                              f"got {actual[bad][:3]} want {expected[bad][:3]}")
+    assert (err > strict).mean() <= max_flip_fraction, f"{(err > strict).mean():.4f} of elements need the allowance"
