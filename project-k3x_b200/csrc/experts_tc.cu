@@ -40,8 +40,20 @@ using tcp::kAtomBytes;
 using tcp::kBlockM;
 using tcp::kThreads;
 
-constexpr uint32_t kNMax = 128;         // activation rows (tokens x terms) per tile
-constexpr uint32_t kStagesGU = 4;
+// B-tile height NM (activation rows = tokens x terms per tile) is 64 or 128.
+// With few tokens per expert (c2: ~3) a 64-row B slot leaves room for more
+// weight stages in shared memory — bytes in flight are what bound an
+// HBM-streaming GEMM — and for a double-buffered gate/up accumulator.
+template <uint32_t NM> struct RoutedCfg;
+template <> struct RoutedCfg<64> {
+    static constexpr uint32_t kStagesGU = 5, kStagesD = 8, kAccbGU = 2;
+    static constexpr uint32_t kColUp = 64, kStrideGU = 128;
+};
+template <> struct RoutedCfg<128> {
+    static constexpr uint32_t kStagesGU = 4, kStagesD = 6, kAccbGU = 1;
+    static constexpr uint32_t kColUp = 128, kStrideGU = 0;
+};
+constexpr uint32_t kStagesGU = 4;   // shared expert (kind::f16) pipelines
 constexpr uint32_t kStagesD = 6;
 
 constexpr uint32_t round16(uint32_t x) { return (x + 15u) / 16u * 16u; }
@@ -75,11 +87,11 @@ struct Tables {
 // weight tile run back to back and the second read hits L2).
 __global__ void __launch_bounds__(1024) worklist_kernel(const uint32_t* group_count, const uint32_t* group_offset,
                                                         const uint32_t* group_expert, uint32_t terms, uint32_t H,
-                                                        uint32_t I, Tables t) {
+                                                        uint32_t I, uint32_t nmax, Tables t) {
     __shared__ uint32_t scan[2][1024];
     __shared__ uint32_t tile_base[1025];
     const uint32_t ng = *group_count;
-    const uint32_t tpt = kNMax / terms;
+    const uint32_t tpt = nmax / terms;
     const uint32_t mt_gu = I / kBlockM, mt_d = H / kBlockM;
     const uint32_t g = threadIdx.x;
     scan[0][g] = g < ng ? (group_offset[g + 1] - group_offset[g] + tpt - 1) / tpt : 0u;
@@ -108,9 +120,9 @@ __global__ void __launch_bounds__(1024) worklist_kernel(const uint32_t* group_co
         t.tile_tok0[tb + j] = tok0;
         const uint32_t nz = round16(ntok * terms) | (ntok << 16);
         for (uint32_t mt = 0; mt < mt_gu; ++mt)
-            t.desc_gu[tb * mt_gu + mt * nt + j] = make_uint4(e * I + mt * kBlockM, (tb + j) * kNMax, nz, tok0);
+            t.desc_gu[tb * mt_gu + mt * nt + j] = make_uint4(e * I + mt * kBlockM, (tb + j) * nmax, nz, tok0);
         for (uint32_t mt = 0; mt < mt_d; ++mt)
-            t.desc_d[tb * mt_d + mt * nt + j] = make_uint4(e * H + mt * kBlockM, (tb + j) * kNMax, nz, tok0);
+            t.desc_d[tb * mt_d + mt * nt + j] = make_uint4(e * H + mt * kBlockM, (tb + j) * nmax, nz, tok0);
     }
 }
 
@@ -164,7 +176,7 @@ __global__ void __launch_bounds__(256) split_tokens_kernel(const float* __restri
 __global__ void __launch_bounds__(256) gather_gu_kernel(const uint8_t* __restrict__ tsplit,
                                                         const uint8_t* __restrict__ tsf, uint32_t H,
                                                         const uint32_t* __restrict__ assign_token, Tables tb,
-                                                        uint32_t terms, uint8_t* __restrict__ b,
+                                                        uint32_t terms, uint32_t nmax, uint8_t* __restrict__ b,
                                                         uint8_t* __restrict__ sfb) {
     const uint32_t tile = blockIdx.x;
     if (tile >= tb.counts[0]) return;
@@ -172,7 +184,7 @@ __global__ void __launch_bounds__(256) gather_gu_kernel(const uint8_t* __restric
     const uint32_t used = ntok * terms, n = round16(used);
     const uint32_t kbc = H / 32;
     const size_t row_stride = H / 2;
-    uint8_t* base = b + static_cast<size_t>(tile) * kNMax * row_stride;
+    uint8_t* base = b + static_cast<size_t>(tile) * nmax * row_stride;
     uint8_t* atoms = sfb + static_cast<size_t>(tile) * (kbc / 4) * kAtomBytes;
     for (uint32_t i = threadIdx.x; i < n * kbc; i += blockDim.x) {
         const uint32_t r = i / kbc, v = i % kbc;
@@ -226,33 +238,36 @@ struct DParams {
     int* error;
 };
 
-// TMEM columns
+// TMEM columns. Routed gate/up: gate accumulator at 0, up at RoutedCfg::kColUp,
+// second buffer (NM = 64) kStrideGU further; block scales from 256.
 constexpr uint32_t kColAccGate = 0, kColAccUp = 128, kColSfaGate = 256, kColSfaUp = 264, kColSfbGU = 272;
 constexpr uint32_t kColAccD = 0, kColSfaD = 256, kColSfbD = 264;   // down: two accumulator buffers at 0/128
 
+template <uint32_t NM>
 __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_constant__ CUtensorMap map_gate,
                                                               const __grid_constant__ CUtensorMap map_up,
                                                               const __grid_constant__ CUtensorMap map_b,
                                                               const GuParams p) {
+    using RC = RoutedCfg<NM>;
     extern __shared__ uint8_t smem_raw[];
-    auto& sm = tcp::smem_from<kStagesGU, 2>(smem_raw);
+    auto& sm = tcp::smem_from<RC::kStagesGU, 2, NM>(smem_raw);
     const uint32_t terms = p.terms;
     const uint32_t mtc = p.I / kBlockM;
     auto get_desc = [&](uint32_t item) { return __ldg(p.desc + item); };
     auto epilogue = [&](const uint4& d, uint32_t tmem, uint32_t q, uint32_t lane) {
-        const uint32_t tile = d.y / kNMax, mt = (d.x / kBlockM) % mtc;
+        const uint32_t tile = d.y / NM, mt = (d.x / kBlockM) % mtc;
         const uint32_t ntok = tcp::desc_ntok(d);
         const uint32_t used = ntok * terms, n = tcp::desc_n(d);
         const uint32_t lane_base = (32u * q) << 16;
         const size_t row_stride = p.I / 2;
-        uint8_t* brow = p.b_down + static_cast<size_t>(tile) * kNMax * row_stride + mt * 64 + q * 16;
+        uint8_t* brow = p.b_down + static_cast<size_t>(tile) * NM * row_stride + mt * 64 + q * 16;
         uint8_t* sfbase = p.sfb_down + (static_cast<size_t>(tile) * (p.I / 128) + mt) * kAtomBytes + q;
         float gs = 0.0f, us = 0.0f;
         uint32_t tcount = 0, j = 0;
         for (uint32_t c0 = 0; c0 < used; c0 += 16) {
             float vg[16], vu[16];
             tc::tmem_ld16(tmem + lane_base + kColAccGate + c0, vg);
-            tc::tmem_ld16(tmem + lane_base + kColAccUp + c0, vu);
+            tc::tmem_ld16(tmem + lane_base + RC::kColUp + c0, vu);
             tc::tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -290,16 +305,19 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_consta
         }
     };
     const uint8_t* sfa[2] = {p.sfa_gate, p.sfa_up};
-    const tcp::Config cfg{p.H, *p.n_items, 512, kColAccGate, kColAccUp, 0, kColSfaGate, kColSfaUp, kColSfbGU};
-    tcp::run_pipeline<kStagesGU, 2, false, 1>(sm, &map_gate, &map_up, &map_b, cfg, sfa, p.sfb, p.error, get_desc,
-                                              epilogue);
+    const tcp::Config cfg{p.H, *p.n_items, 512, kColAccGate, RC::kColUp, RC::kStrideGU, kColSfaGate, kColSfaUp,
+                          kColSfbGU};
+    tcp::run_pipeline<RC::kStagesGU, 2, false, RC::kAccbGU>(sm, &map_gate, &map_up, &map_b, cfg, sfa, p.sfb,
+                                                            p.error, get_desc, epilogue);
 }
 
+template <uint32_t NM>
 __global__ void __launch_bounds__(kThreads, 1) down_kernel(const __grid_constant__ CUtensorMap map_down,
                                                             const __grid_constant__ CUtensorMap map_b,
                                                             const DParams p) {
+    using RC = RoutedCfg<NM>;
     extern __shared__ uint8_t smem_raw[];
-    auto& sm = tcp::smem_from<kStagesD, 1>(smem_raw);
+    auto& sm = tcp::smem_from<RC::kStagesD, 1, NM>(smem_raw);
     const uint32_t terms = p.terms;
     const uint32_t mtc = p.H / kBlockM;
     auto get_desc = [&](uint32_t item) { return __ldg(p.desc + item); };
@@ -330,8 +348,8 @@ __global__ void __launch_bounds__(kThreads, 1) down_kernel(const __grid_constant
     };
     const uint8_t* sfa[1] = {p.sfa};
     const tcp::Config cfg{p.I, *p.n_items, 512, kColAccD, kColAccD, 128, kColSfaD, kColSfaD, kColSfbD};
-    tcp::run_pipeline<kStagesD, 1, false, 2>(sm, &map_down, &map_down, &map_b, cfg, sfa, p.sfb, p.error, get_desc,
-                                             epilogue);
+    tcp::run_pipeline<RC::kStagesD, 1, false, 2>(sm, &map_down, &map_down, &map_b, cfg, sfa, p.sfb, p.error,
+                                                 get_desc, epilogue);
 }
 
 // ---------------------------------------------------------------------------
@@ -497,7 +515,7 @@ int relayout(k3xb_ctx* ctx, const uint8_t* scales, size_t rows, uint32_t K, uint
 }
 
 struct Layout {
-    uint32_t terms, tpt, max_tiles, mt_gu, mt_d;
+    uint32_t terms, nmax, tpt, max_tiles, mt_gu, mt_d;
     size_t b_gu, sfb_gu, b_d, sfb_d;
     size_t sf_gate, sf_up, sf_down;   // per-call re-laid scales (0 when prepared)
     size_t tsplit, tsf;               // per-token E2M1 split of the hidden rows
@@ -506,14 +524,18 @@ struct Layout {
 Layout layout_of(const k3xb_moe_layer& L, uint32_t T) {
     Layout l{};
     l.terms = L.act_terms > 0 ? static_cast<uint32_t>(L.act_terms) : 6u;
-    l.tpt = kNMax / l.terms;
     const uint32_t assigns = T * L.top_k;
+    // 64-row B tiles when an average expert gets at most 64 rows of terms
+    // (c2: ~3 tokens x 6 terms), otherwise 128
+    const uint32_t avg_rows = (assigns + L.experts - 1) / L.experts * l.terms;
+    l.nmax = (avg_rows <= 64 && l.terms <= 64) ? 64u : 128u;
+    l.tpt = l.nmax / l.terms;
     l.max_tiles = std::min(L.experts, assigns) + (assigns + l.tpt - 1) / l.tpt;
     l.mt_gu = L.inter / kBlockM;
     l.mt_d = L.hidden / kBlockM;
-    l.b_gu = static_cast<size_t>(l.max_tiles) * kNMax * (L.hidden / 2);
+    l.b_gu = static_cast<size_t>(l.max_tiles) * l.nmax * (L.hidden / 2);
     l.sfb_gu = static_cast<size_t>(l.max_tiles) * (L.hidden / 128) * kAtomBytes;
-    l.b_d = static_cast<size_t>(l.max_tiles) * kNMax * (L.inter / 2);
+    l.b_d = static_cast<size_t>(l.max_tiles) * l.nmax * (L.inter / 2);
     l.sfb_d = static_cast<size_t>(l.max_tiles) * (L.inter / 128) * kAtomBytes;
     const size_t sf_gu = static_cast<size_t>(L.experts) * L.inter * (L.hidden / 32);
     l.sf_gate = L.gate_scales_tc ? 0 : sf_gu;
@@ -549,6 +571,27 @@ void carve(A& a, const Layout& l, Buffers* out) {
     r.tsf = a.template take<uint8_t>(l.tsf, 1024);
 }
 
+template <uint32_t NM>
+int launch_routed(k3xb_ctx* ctx, const CUtensorMap& map_gate, const CUtensorMap& map_up, const CUtensorMap& map_bgu,
+                  const CUtensorMap& map_down, const CUtensorMap& map_bd, const GuParams& gp, const DParams& dp) {
+    using RC = RoutedCfg<NM>;
+    const size_t smem_gu = tcp::smem_bytes<RC::kStagesGU, 2, NM>();
+    const size_t smem_d = tcp::smem_bytes<RC::kStagesD, 1, NM>();
+    static bool configured = false;   // per template instance
+    if (!configured) {
+        K3XB_CUDA(ctx, cudaFuncSetAttribute(gateup_kernel<NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem_gu)));
+        K3XB_CUDA(ctx, cudaFuncSetAttribute(down_kernel<NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem_d)));
+        configured = true;
+    }
+    gateup_kernel<NM><<<ctx->sm_count, kThreads, smem_gu, ctx->stream>>>(map_gate, map_up, map_bgu, gp);
+    K3XB_LAUNCHED(ctx);
+    down_kernel<NM><<<ctx->sm_count, kThreads, smem_d, ctx->stream>>>(map_down, map_bd, dp);
+    K3XB_LAUNCHED(ctx);
+    return K3XB_OK;
+}
+
 }  // namespace
 
 int make_byte_map(k3xb_ctx* ctx, void* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows) {
@@ -579,7 +622,7 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
         return fail(ctx, K3XB_INVALID_EXTENT, "act_terms must be in [1, 16] (0 = default 6)");
     if (L.experts > 1024) return fail(ctx, K3XB_INVALID_EXTENT, "MXF4 engine supports <= 1024 experts");
     const Layout l = layout_of(L, T);
-    if (static_cast<uint64_t>(l.max_tiles) * kNMax >= (1ull << 31))
+    if (static_cast<uint64_t>(l.max_tiles) * l.nmax >= (1ull << 31))
         return fail(ctx, K3XB_INVALID_EXTENT, "MXF4 work list too large");
     int st;
     Carver c(reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ctx->mxf4_scratch) + 1023) & ~uintptr_t(1023)));
@@ -597,22 +640,11 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
     if ((st = make_map(ctx, &map_gate, L.gate_packed, H / 2, static_cast<uint64_t>(L.experts) * I, 128))) return st;
     if ((st = make_map(ctx, &map_up, L.up_packed, H / 2, static_cast<uint64_t>(L.experts) * I, 128))) return st;
     if ((st = make_map(ctx, &map_down, L.down_packed, I / 2, static_cast<uint64_t>(L.experts) * H, 128))) return st;
-    if ((st = make_map(ctx, &map_bgu, bf.b_gu, H / 2, static_cast<uint64_t>(l.max_tiles) * kNMax, 16))) return st;
-    if ((st = make_map(ctx, &map_bd, bf.b_d, I / 2, static_cast<uint64_t>(l.max_tiles) * kNMax, 16))) return st;
-
-    TcState* s = state_of(ctx);
-    const size_t smem_gu = tcp::smem_bytes<kStagesGU, 2>();
-    const size_t smem_d = tcp::smem_bytes<kStagesD, 1>();
-    if (!s->configured) {
-        K3XB_CUDA(ctx, cudaFuncSetAttribute(gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(smem_gu)));
-        K3XB_CUDA(ctx, cudaFuncSetAttribute(down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(smem_d)));
-        s->configured = true;
-    }
+    if ((st = make_map(ctx, &map_bgu, bf.b_gu, H / 2, static_cast<uint64_t>(l.max_tiles) * l.nmax, 16))) return st;
+    if ((st = make_map(ctx, &map_bd, bf.b_d, I / 2, static_cast<uint64_t>(l.max_tiles) * l.nmax, 16))) return st;
 
     worklist_kernel<<<1, 1024, 0, ctx->stream>>>(plan.group_count, plan.group_offset, plan.group_expert, l.terms, H,
-                                                 I, bf.tb);
+                                                 I, l.nmax, bf.tb);
     K3XB_LAUNCHED(ctx);
     {
         const size_t n = static_cast<size_t>(T) * (H / 32);
@@ -621,18 +653,15 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
         K3XB_LAUNCHED(ctx);
     }
     gather_gu_kernel<<<l.max_tiles, 256, 0, ctx->stream>>>(bf.tsplit, bf.tsf, H, plan.assign_token, bf.tb, l.terms,
-                                                           bf.b_gu, bf.sfb_gu);
+                                                           l.nmax, bf.b_gu, bf.sfb_gu);
     K3XB_LAUNCHED(ctx);
 
     GuParams gp{bf.tb.desc_gu, bf.tb.counts + 1, sfa_gate, sfa_up, bf.sfb_gu, bf.b_d, bf.sfb_d, H, I, l.terms,
                 L.activation, L.situ_beta, L.situ_linear_beta, ctx->status_word};
-    gateup_kernel<<<ctx->sm_count, kThreads, smem_gu, ctx->stream>>>(map_gate, map_up, map_bgu, gp);
-    K3XB_LAUNCHED(ctx);
     DParams dp{bf.tb.desc_d, bf.tb.counts + 2, plan.assign_token, plan.assign_slot, sfa_down, bf.sfb_d, slot_out,
                H, I, l.terms, L.top_k, ctx->status_word};
-    down_kernel<<<ctx->sm_count, kThreads, smem_d, ctx->stream>>>(map_down, map_bd, dp);
-    K3XB_LAUNCHED(ctx);
-    return K3XB_OK;
+    return l.nmax == 64 ? launch_routed<64>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, dp)
+                        : launch_routed<128>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, dp);
 }
 
 int launch_shared_tc(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T, uint16_t* xb,

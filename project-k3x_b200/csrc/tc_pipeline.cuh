@@ -31,10 +31,12 @@ constexpr uint32_t kTileBytes = kBlockM * 128;   // 16 KB A tile per stage
 constexpr uint32_t kAtomBytes = 512;    // 128 rows x 4 E8M0 scale blocks
 constexpr uint32_t kThreads = 192;
 
-template <uint32_t S, uint32_t NA>
+// BROWS = rows of the B (activation) tile per stage; a stage holds NA A
+// tiles (16 KB each), BROWS x 128 B of B and the stage's block scales.
+template <uint32_t S, uint32_t NA, uint32_t BROWS = 128>
 struct __align__(1024) Smem {
     uint8_t a[NA][S][kTileBytes];
-    uint8_t b[S][kTileBytes];
+    uint8_t b[S][BROWS * 128];
     uint8_t sfa[NA][S][2 * kAtomBytes];
     uint8_t sfb[S][2 * kAtomBytes];
     uint64_t full[S], empty[S], tmem_full[2], tmem_empty[2], teardown;
@@ -42,13 +44,13 @@ struct __align__(1024) Smem {
     int abort;
 };
 
-template <uint32_t S, uint32_t NA>
-__device__ __forceinline__ Smem<S, NA>& smem_from(uint8_t* raw) {
-    return *reinterpret_cast<Smem<S, NA>*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+template <uint32_t S, uint32_t NA, uint32_t BROWS = 128>
+__device__ __forceinline__ Smem<S, NA, BROWS>& smem_from(uint8_t* raw) {
+    return *reinterpret_cast<Smem<S, NA, BROWS>*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
 }
 
-template <uint32_t S, uint32_t NA>
-constexpr size_t smem_bytes() { return sizeof(Smem<S, NA>) + 1024; }
+template <uint32_t S, uint32_t NA, uint32_t BROWS = 128>
+constexpr size_t smem_bytes() { return sizeof(Smem<S, NA, BROWS>) + 1024; }
 
 struct Config {
     uint32_t K;             // reduction length in elements
@@ -62,8 +64,8 @@ struct Config {
 __device__ __forceinline__ uint32_t desc_n(const uint4& d) { return d.z & 0xffffu; }
 __device__ __forceinline__ uint32_t desc_ntok(const uint4& d) { return d.z >> 16; }
 
-template <uint32_t S, uint32_t NA, bool F16, uint32_t ACCB, typename GetDesc, typename Epilogue>
-__device__ __forceinline__ void run_pipeline(Smem<S, NA>& sm, const CUtensorMap* map_a0, const CUtensorMap* map_a1,
+template <uint32_t S, uint32_t NA, bool F16, uint32_t ACCB, uint32_t BROWS, typename GetDesc, typename Epilogue>
+__device__ __forceinline__ void run_pipeline(Smem<S, NA, BROWS>& sm, const CUtensorMap* map_a0, const CUtensorMap* map_a1,
                                              const CUtensorMap* map_b, const Config cfg,
                                              const uint8_t* const* sfa_src, const uint8_t* sfb_src, int* error,
                                              GetDesc get_desc, Epilogue epilogue) {
@@ -122,7 +124,8 @@ __device__ __forceinline__ void run_pipeline(Smem<S, NA>& sm, const CUtensorMap*
                     for (uint32_t m = 0; m < NA; ++m)
                         tc::bulk_load(sm.sfa[m][st], sfa_src[m] + a_atom * kAtomBytes, atoms * kAtomBytes,
                                       &sm.full[st]);
-                    const size_t b_atom = static_cast<size_t>(b_row / 128) * atoms_per_row + 2 * s;
+                    // one scale-atom column per B tile (BROWS rows padded to the atom's 128)
+                    const size_t b_atom = static_cast<size_t>(b_row / BROWS) * atoms_per_row + 2 * s;
                     tc::bulk_load(sm.sfb[st], sfb_src + b_atom * kAtomBytes, atoms * kAtomBytes, &sm.full[st]);
                 }
             }

@@ -46,7 +46,9 @@ def _report(got, want):
 
 
 @pytest.mark.parametrize("act", [ACT_SWIGLU, ACT_SITU])
-@pytest.mark.parametrize("dims", [(256, 128, 16, 4, 5), (512, 256, 32, 8, 40), (384, 640, 12, 3, 9)])
+@pytest.mark.parametrize("dims", [(256, 128, 16, 4, 5), (512, 256, 32, 8, 40), (384, 640, 12, 3, 9),
+                                  # ~25 rows per expert x 6 terms: 128-row activation tiles
+                                  (256, 384, 8, 2, 100)])
 def test_mxf4_matches_oracle(torch, ctx, rs, act, dims):
     import k3xb
     H, I, E, K, T = dims
