@@ -326,6 +326,13 @@ __global__ void __launch_bounds__(kThreads, 1) down_kernel(const __grid_constant
         const uint32_t used = tcp::desc_ntok(d) * terms;
         const uint32_t lane_base = (32u * q) << 16;
         const uint32_t h = mt * kBlockM + 32u * q + lane;
+        const uint32_t ntok = tcp::desc_ntok(d);
+        // destination rows of up to 32 tokens per round trip (lane j holds token j's)
+        auto fetch_dst = [&](uint32_t j0) {
+            const uint32_t a = tok0 + j0 + lane;
+            return j0 + lane < ntok ? __ldg(p.assign_token + a) * p.top_k + __ldg(p.assign_slot + a) : 0u;
+        };
+        uint32_t dsts = fetch_dst(0);
         float ys = 0.0f;
         uint32_t tcount = 0, j = 0;
         for (uint32_t c0 = 0; c0 < used; c0 += 16) {
@@ -337,8 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1) down_kernel(const __grid_constant
                 if (c0 + i >= used) break;
                 ys = __fadd_rn(ys, v[i]);
                 if (++tcount < terms) continue;
-                const uint32_t a = tok0 + j;
-                const size_t dst = static_cast<size_t>(__ldg(p.assign_token + a)) * p.top_k + __ldg(p.assign_slot + a);
+                if (j % 32 == 0 && j) dsts = fetch_dst(j);
+                const size_t dst = __shfl_sync(0xffffffffu, dsts, j % 32);
                 p.slot_out[dst * p.H + h] = round_bf16(ys);
                 ys = 0.0f;
                 tcount = 0;

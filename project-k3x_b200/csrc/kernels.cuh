@@ -54,7 +54,7 @@ int launch_fill_normal_mxfp4(k3xb_ctx* ctx, uint8_t* packed, uint8_t* scales, si
 }  // namespace k3xb
 
 namespace k3xb {
-// experts_mxf4.cu — tcgen05 block-scaled expert engine
+// experts_tc.cu — tcgen05 block-scaled expert engine
 size_t mxf4_scratch_bytes(const k3xb_moe_layer& L, uint32_t T);
 void set_mxf4_scratch(k3xb_ctx* ctx, void* region);
 int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T,

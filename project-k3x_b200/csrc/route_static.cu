@@ -81,6 +81,11 @@ extern "C" int k3xb_route_static(const float* hidden, uint32_t tokens, uint32_t 
     k3xb_ctx launch;   // carries the stream for the shared launchers; owns no device memory
     launch.device = device;
     launch.stream = s;
-    if ((st = launch_router_logits(&launch, hidden, tokens, hidden_size, router, experts, logits))) return st;
+    if (cudaDeviceGetAttribute(&launch.sm_count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+        return K3XB_BACKEND_UNAVAILABLE;
+    launch.status_word = word;
+    st = launch_router_logits(&launch, hidden, tokens, hidden_size, router, experts, logits);
+    release_mxf4_resources(&launch);   // host-side tensor-map state of the local context
+    if (st) return st;
     return launch_topk(&launch, logits, correction, tokens, experts, top_k, ids, contributions, nullptr, word);
 }

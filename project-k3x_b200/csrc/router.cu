@@ -5,11 +5,12 @@
 // the float result is bit-identical to the reference. A bf16 x float
 // product is exact in FP64, so fma(w, x, acc) rounds exactly like the
 // reference's `sum += double(w) * x`. Chains are independent per (token,
-// expert); a thread carries TOK of them for ILP. The kernel is bound by
-// the FP64 dependency chain (H sequential adds), not by HBM: W_r is 5.5 MB
-// at the released shape and is read once per TOK tokens from L2.
+// expert); a thread carries several of them for ILP. The kernels are bound
+// by the FP64 dependency chain (H sequential FMAs), not by HBM: W_r is
+// 5.5 MB at the released shape and is re-read from L2 per token group.
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tc.cuh"
 
 #include <cfloat>
 
@@ -125,6 +126,120 @@ __global__ void __launch_bounds__(128) router_logits_kernel(
     for (int j = 0; j < 4; ++j) {
         const uint32_t t = t0 + 4 * warp + j;
         if (e < E && t < T) logits[static_cast<size_t>(t) * E + e] = static_cast<float>(acc[j]);
+    }
+}
+
+// TMA variant (rows 16-byte aligned, H % 64 == 0, the CTA's TW token rows
+// fit in shared memory): lane = expert, a CTA's 4 warps cover 128 experts.
+// The TW tokens' hidden rows are staged once as double [h][TW]; the 128
+// expert rows stream through kRtStages shared-memory stages of 64 weights,
+// each one 2D TMA box (128 rows x 128 B, 128B-swizzled so a warp's 16-byte
+// reads hit distinct banks). A chain step is a conversion (float -> double,
+// exact), one broadcast shared load and TW independent FMAs; thread 0 also
+// refills each stage once all 128 threads have released it.
+constexpr int kRtStages = 4;
+constexpr uint32_t kRtStageBytes = 128 * 128;
+constexpr size_t kRtSmemMax = 220 * 1024;
+
+struct RtBars {
+    uint64_t full[kRtStages], empty[kRtStages];
+    int abort;
+};
+
+constexpr size_t rt_smem_bytes(uint32_t H, int tw) {
+    return 1024 + kRtStages * kRtStageBytes + static_cast<size_t>(H) * tw * sizeof(double) + sizeof(RtBars);
+}
+
+template <int TW>
+__global__ void __launch_bounds__(128) router_tma_kernel(const __grid_constant__ CUtensorMap map_w,
+                                                         const float* __restrict__ hidden, uint32_t T, uint32_t H,
+                                                         uint32_t E, float* __restrict__ logits, int* error) {
+    extern __shared__ __align__(16) unsigned char router_smem[];
+    uint8_t* wst = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(router_smem) + 1023) & ~uintptr_t(1023));
+    double* xs = reinterpret_cast<double*>(wst + kRtStages * kRtStageBytes);   // [H][TW]
+    RtBars* bars = reinterpret_cast<RtBars*>(xs + static_cast<size_t>(H) * TW);
+    volatile int* abort = &bars->abort;
+    const uint32_t tid = threadIdx.x;
+    const uint32_t e0 = blockIdx.x * 128;
+    const uint32_t nst = H / 64;
+    if (tid == 0) {
+        for (int s = 0; s < kRtStages; ++s) {
+            tc::mbar_init(&bars->full[s], 1);
+            tc::mbar_init(&bars->empty[s], 128);
+        }
+        bars->abort = 0;
+        tc::fence_barrier_init();
+    }
+    __syncthreads();
+    uint32_t issued = 0;
+    auto load_stage = [&](uint32_t st) {
+        const uint32_t slot = st % kRtStages;
+        tc::mbar_arrive_expect_tx(&bars->full[slot], kRtStageBytes);
+        tc::tma_load_2d(wst + slot * kRtStageBytes, &map_w, &bars->full[slot], static_cast<int>(st * 128),
+                        static_cast<int>(e0));
+        ++issued;
+    };
+    if (tid == 0) {
+        tc::prefetch_tensormap(&map_w);
+        for (uint32_t st = 0; st < kRtStages && st < nst; ++st) load_stage(st);
+    }
+    const uint32_t t0 = blockIdx.y * TW;
+    for (uint32_t i = tid; i < H * TW; i += blockDim.x) {
+        const uint32_t h = i / TW, j = i % TW;
+        xs[i] = t0 + j < T ? static_cast<double>(hidden[static_cast<size_t>(t0 + j) * H + h]) : 0.0;
+    }
+    __syncthreads();
+
+    double acc[TW];
+#pragma unroll
+    for (int j = 0; j < TW; ++j) acc[j] = 0.0;
+    for (uint32_t st = 0; st < nst; ++st) {
+        if (tid == 0 && st >= 1 && st - 1 + kRtStages < nst) {
+            const uint32_t prev = st - 1;
+            if (tc::mbar_wait(&bars->empty[prev % kRtStages], (prev / kRtStages) & 1u, abort))
+                load_stage(prev + kRtStages);
+        }
+        const uint32_t slot = st % kRtStages;
+        if (!tc::mbar_wait(&bars->full[slot], (st / kRtStages) & 1u, abort)) break;
+        const uint8_t* row = wst + slot * kRtStageBytes + tid * 128;
+        const double* xp = xs + static_cast<size_t>(st) * 64 * TW;
+#pragma unroll
+        for (uint32_t c = 0; c < 8; ++c) {
+            const uint4 cur = *reinterpret_cast<const uint4*>(row + ((c ^ (tid & 7u)) << 4));
+            const uint32_t q[4] = {cur.x, cur.y, cur.z, cur.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t f = (i & 1) ? (q[i / 2] & 0xffff0000u) : (q[i / 2] << 16);
+                const double w = static_cast<double>(__uint_as_float(f));
+                const double* x = xp + (c * 8 + i) * TW;
+                if (TW % 2 == 0) {
+#pragma unroll
+                    for (int j = 0; j < TW; j += 2) {
+                        const double2 xv = *reinterpret_cast<const double2*>(x + j);
+                        acc[j] = fma(w, xv.x, acc[j]);
+                        acc[j + 1] = fma(w, xv.y, acc[j + 1]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < TW; ++j) acc[j] = fma(w, x[j], acc[j]);
+                }
+            }
+        }
+        tc::mbar_arrive(&bars->empty[slot]);
+    }
+    if (tid == 0 && *abort) {
+        // let every issued copy land before the shared memory is released
+        volatile int never = 0;
+        for (uint32_t st = 0; st < issued; ++st) tc::mbar_wait(&bars->full[st % kRtStages], (st / kRtStages) & 1u, &never, 200000000ull);
+        if (error) atomicExch(error, K3XB_BACKEND_UNAVAILABLE);
+    }
+    __syncthreads();
+    if (*abort) return;
+    const uint32_t e = e0 + tid;
+    if (e < E) {
+#pragma unroll
+        for (int j = 0; j < TW; ++j)
+            if (t0 + j < T) logits[static_cast<size_t>(t0 + j) * E + e] = static_cast<float>(acc[j]);
     }
 }
 
@@ -293,6 +408,39 @@ size_t plan_smem_bytes(uint32_t T, uint32_t E) {
 
 int launch_router_logits(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_t H,
                          const uint16_t* W, uint32_t E, float* logits) {
+    // TMA kernel: the smallest TW that keeps about one warp per SM
+    // sub-partition (a chain step's latency is paid once per TW FMAs).
+    const bool aligned = H % 64 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0;
+    int tw = 0;
+    for (int c : {1, 2, 4}) {
+        if (rt_smem_bytes(H, c) > kRtSmemMax) break;
+        tw = c;
+        const uint64_t warps = static_cast<uint64_t>((E + 127) / 128) * 4 * ((T + c - 1) / c);
+        if (warps <= 4ull * ctx->sm_count) break;
+    }
+    if (aligned && tw > 0) {
+        CUtensorMap map;
+        int st = make_byte_map(ctx, &map, W, static_cast<uint64_t>(H) * 2, E, 128);
+        if (st) return st;
+        static bool tma_configured = false;
+        if (!tma_configured) {
+            K3XB_CUDA(ctx, cudaFuncSetAttribute(router_tma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(kRtSmemMax)));
+            K3XB_CUDA(ctx, cudaFuncSetAttribute(router_tma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(kRtSmemMax)));
+            K3XB_CUDA(ctx, cudaFuncSetAttribute(router_tma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(kRtSmemMax)));
+            tma_configured = true;
+        }
+        const dim3 grid((E + 127) / 128, (T + tw - 1) / tw);
+        const size_t smem = rt_smem_bytes(H, tw);
+        int* err = ctx->status_word;
+        if (tw == 1) router_tma_kernel<1><<<grid, 128, smem, ctx->stream>>>(map, hidden, T, H, E, logits, err);
+        else if (tw == 2) router_tma_kernel<2><<<grid, 128, smem, ctx->stream>>>(map, hidden, T, H, E, logits, err);
+        else router_tma_kernel<4><<<grid, 128, smem, ctx->stream>>>(map, hidden, T, H, E, logits, err);
+        K3XB_LAUNCHED(ctx);
+        return K3XB_OK;
+    }
     static bool configured = false;
     if (!configured) {
         K3XB_CUDA(ctx, cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -131,9 +131,10 @@ __device__ __forceinline__ void run_pipeline(Smem<S, NA, BROWS>& sm, const CUten
             }
             d = nd;
         }
+        volatile int never = 0;   // these waits must not be cut short by the abort flag
         for (uint32_t k = 0; k < S && k < it; ++k) {   // copies still in flight
             const uint32_t j = it - 1 - k;
-            tc::mbar_wait(&sm.full[j % S], (j / S) & 1u, abort, 200000000ull);
+            tc::mbar_wait(&sm.full[j % S], (j / S) & 1u, &never, 200000000ull);
         }
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer ----------------
@@ -193,8 +194,9 @@ __device__ __forceinline__ void run_pipeline(Smem<S, NA, BROWS>& sm, const CUten
             d = nd;
         }
         if (issued) {   // all issued MMAs finish before TMEM is freed
+            volatile int never = 0;
             tc::commit(&sm.teardown);
-            tc::mbar_wait(&sm.teardown, 0, abort, 200000000ull);
+            tc::mbar_wait(&sm.teardown, 0, &never, 200000000ull);
         }
     } else if (warp >= 2) {
         // ---------------- epilogue (4 warps = 128 TMEM lanes) ----------------
