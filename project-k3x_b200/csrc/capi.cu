@@ -108,6 +108,16 @@ int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidd
     float* contrib = contrib_out ? contrib_out : s.contrib;
     s.plan.status = ctx->status_word;
     int st;
+    if (L.shared_gate && L.engine == K3XB_ENGINE_MXF4) {
+        K3XB_CUDA(ctx, cudaEventRecord(ctx->ev_fork, ctx->stream));
+        K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->side_stream, ctx->ev_fork, 0));
+        cudaStream_t main = ctx->stream;
+        ctx->stream = ctx->side_stream;
+        st = launch_shared_tc(ctx, L, hidden, T, s.sxb, s.sbd, s.shared_out);
+        ctx->stream = main;
+        if (st) return st;
+        K3XB_CUDA(ctx, cudaEventRecord(ctx->ev_join, ctx->side_stream));
+    }
     if ((st = launch_router_logits(ctx, hidden, T, H, L.router, E, s.logits))) return st;
     if ((st = launch_topk(ctx, s.logits, L.correction, T, E, K, ids, contrib, nullptr, s.plan.status))) return st;
     if ((st = launch_plan(ctx, ids, contrib, T, K, E, s.plan))) return st;
@@ -118,7 +128,10 @@ int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidd
     }
     const float* shared = nullptr;
     if (L.shared_gate && L.engine == K3XB_ENGINE_MXF4) {
-        if ((st = launch_shared_tc(ctx, L, hidden, T, s.sxb, s.sbd, s.shared_out))) return st;
+        // the shared expert depends on the hidden rows only: it runs on the
+        // side stream, forked before the router, on the SMs the router leaves
+        // free; the main stream joins it before the combine
+        K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
         shared = s.shared_out;
     } else if (L.shared_gate) {
         const uint32_t Is = L.shared_inter;
@@ -157,6 +170,9 @@ int k3xb_create(int device, k3xb_ctx** out) {
     ctx->sm_count = prop.multiProcessorCount;
     if (cudaSetDevice(device) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&ctx->side_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_join, cudaEventDisableTiming) != cudaSuccess ||
         cudaMalloc(&ctx->status_word, sizeof(int32_t)) != cudaSuccess ||
         cudaMemset(ctx->status_word, 0, sizeof(int32_t)) != cudaSuccess) {
         k3xb_destroy(ctx);
@@ -171,10 +187,14 @@ int k3xb_destroy(k3xb_ctx* ctx) {
     if (!ctx) return K3XB_OK;
     cudaSetDevice(ctx->device);
     if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
+    if (ctx->side_stream) cudaStreamSynchronize(ctx->side_stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->status_word) cudaFree(ctx->status_word);
     release_mxf4_resources(ctx);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    if (ctx->side_stream) cudaStreamDestroy(ctx->side_stream);
+    if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
+    if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
     delete ctx;
     return K3XB_OK;
 }

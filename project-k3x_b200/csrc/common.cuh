@@ -13,6 +13,8 @@ struct k3xb_ctx {
     int sm_count = 0;
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
+    cudaStream_t side_stream = nullptr;   // work forked off `stream` within one call
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     std::string error;
     void* scratch = nullptr;
     size_t scratch_bytes = 0;

@@ -137,9 +137,10 @@ __global__ void __launch_bounds__(128) router_logits_kernel(
 // reads hit distinct banks). A chain step is a conversion (float -> double,
 // exact), one broadcast shared load and TW independent FMAs; thread 0 also
 // refills each stage once all 128 threads have released it.
-constexpr int kRtStages = 4;
+constexpr int kRtStages = 6;
 constexpr uint32_t kRtStageBytes = 128 * 128;
 constexpr size_t kRtSmemMax = 220 * 1024;
+constexpr uint32_t kRtThreads = 160;   // 4 consumer warps (one expert row per thread) + 1 producer warp
 
 struct RtBars {
     uint64_t full[kRtStages], empty[kRtStages];
@@ -151,9 +152,10 @@ constexpr size_t rt_smem_bytes(uint32_t H, int tw) {
 }
 
 template <int TW>
-__global__ void __launch_bounds__(128) router_tma_kernel(const __grid_constant__ CUtensorMap map_w,
-                                                         const float* __restrict__ hidden, uint32_t T, uint32_t H,
-                                                         uint32_t E, float* __restrict__ logits, int* error) {
+__global__ void __launch_bounds__(kRtThreads) router_tma_kernel(const __grid_constant__ CUtensorMap map_w,
+                                                                const float* __restrict__ hidden, uint32_t T,
+                                                                uint32_t H, uint32_t E, float* __restrict__ logits,
+                                                                int* error) {
     extern __shared__ __align__(16) unsigned char router_smem[];
     uint8_t* wst = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(router_smem) + 1023) & ~uintptr_t(1023));
     double* xs = reinterpret_cast<double*>(wst + kRtStages * kRtStageBytes);   // [H][TW]
@@ -171,34 +173,51 @@ __global__ void __launch_bounds__(128) router_tma_kernel(const __grid_constant__
         tc::fence_barrier_init();
     }
     __syncthreads();
-    uint32_t issued = 0;
-    auto load_stage = [&](uint32_t st) {
-        const uint32_t slot = st % kRtStages;
-        tc::mbar_arrive_expect_tx(&bars->full[slot], kRtStageBytes);
-        tc::tma_load_2d(wst + slot * kRtStageBytes, &map_w, &bars->full[slot], static_cast<int>(st * 128),
-                        static_cast<int>(e0));
-        ++issued;
-    };
-    if (tid == 0) {
+    if (tid == 128) {
+        // ---- producer: one TMA box per stage, refilled once all 128 consumers released it
         tc::prefetch_tensormap(&map_w);
-        for (uint32_t st = 0; st < kRtStages && st < nst; ++st) load_stage(st);
+        uint32_t issued = 0;
+        for (uint32_t st = 0; st < nst; ++st) {
+            const uint32_t slot = st % kRtStages;
+            if (st >= kRtStages && !tc::mbar_wait(&bars->empty[slot], ((st / kRtStages) & 1u) ^ 1u, abort)) break;
+            tc::mbar_arrive_expect_tx(&bars->full[slot], kRtStageBytes);
+            tc::tma_load_2d(wst + slot * kRtStageBytes, &map_w, &bars->full[slot], static_cast<int>(st * 128),
+                            static_cast<int>(e0));
+            ++issued;
+        }
+        volatile int never = 0;   // copies in flight land before the CTA exits, abort or not
+        for (uint32_t k = 0; k < kRtStages && k < issued; ++k) {
+            const uint32_t j = issued - 1 - k;
+            tc::mbar_wait(&bars->full[j % kRtStages], (j / kRtStages) & 1u, &never, 200000000ull);
+        }
+        if (*abort && error) atomicExch(error, K3XB_BACKEND_UNAVAILABLE);
+        return;
     }
+    if (tid >= 128) return;
+    // ---- consumers. Stage x: 4 hidden columns of every token per thread and
+    // iteration, several 16-byte loads in flight (rows 16-byte aligned).
     const uint32_t t0 = blockIdx.y * TW;
-    for (uint32_t i = tid; i < H * TW; i += blockDim.x) {
-        const uint32_t h = i / TW, j = i % TW;
-        xs[i] = t0 + j < T ? static_cast<double>(hidden[static_cast<size_t>(t0 + j) * H + h]) : 0.0;
+#pragma unroll 4
+    for (uint32_t h4 = tid; h4 < H / 4; h4 += 128) {
+        float4 v[TW];
+#pragma unroll
+        for (int j = 0; j < TW; ++j)
+            v[j] = t0 + j < T ? __ldg(reinterpret_cast<const float4*>(hidden + static_cast<size_t>(t0 + j) * H) + h4)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < TW; ++j) {
+            xs[(4 * h4 + 0) * TW + j] = v[j].x;
+            xs[(4 * h4 + 1) * TW + j] = v[j].y;
+            xs[(4 * h4 + 2) * TW + j] = v[j].z;
+            xs[(4 * h4 + 3) * TW + j] = v[j].w;
+        }
     }
-    __syncthreads();
+    asm volatile("bar.sync 1, 128;" ::: "memory");   // consumers only
 
     double acc[TW];
 #pragma unroll
     for (int j = 0; j < TW; ++j) acc[j] = 0.0;
     for (uint32_t st = 0; st < nst; ++st) {
-        if (tid == 0 && st >= 1 && st - 1 + kRtStages < nst) {
-            const uint32_t prev = st - 1;
-            if (tc::mbar_wait(&bars->empty[prev % kRtStages], (prev / kRtStages) & 1u, abort))
-                load_stage(prev + kRtStages);
-        }
         const uint32_t slot = st % kRtStages;
         if (!tc::mbar_wait(&bars->full[slot], (st / kRtStages) & 1u, abort)) break;
         const uint8_t* row = wst + slot * kRtStageBytes + tid * 128;
@@ -227,13 +246,6 @@ __global__ void __launch_bounds__(128) router_tma_kernel(const __grid_constant__
         }
         tc::mbar_arrive(&bars->empty[slot]);
     }
-    if (tid == 0 && *abort) {
-        // let every issued copy land before the shared memory is released
-        volatile int never = 0;
-        for (uint32_t st = 0; st < issued; ++st) tc::mbar_wait(&bars->full[st % kRtStages], (st / kRtStages) & 1u, &never, 200000000ull);
-        if (error) atomicExch(error, K3XB_BACKEND_UNAVAILABLE);
-    }
-    __syncthreads();
     if (*abort) return;
     const uint32_t e = e0 + tid;
     if (e < E) {
@@ -410,7 +422,8 @@ int launch_router_logits(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_
                          const uint16_t* W, uint32_t E, float* logits) {
     // TMA kernel: the smallest TW that keeps about one warp per SM
     // sub-partition (a chain step's latency is paid once per TW FMAs).
-    const bool aligned = H % 64 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0;
+    const bool aligned = H % 64 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(hidden) & 15) == 0;
     int tw = 0;
     for (int c : {1, 2, 4}) {
         if (rt_smem_bytes(H, c) > kRtSmemMax) break;
@@ -435,9 +448,9 @@ int launch_router_logits(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_
         const dim3 grid((E + 127) / 128, (T + tw - 1) / tw);
         const size_t smem = rt_smem_bytes(H, tw);
         int* err = ctx->status_word;
-        if (tw == 1) router_tma_kernel<1><<<grid, 128, smem, ctx->stream>>>(map, hidden, T, H, E, logits, err);
-        else if (tw == 2) router_tma_kernel<2><<<grid, 128, smem, ctx->stream>>>(map, hidden, T, H, E, logits, err);
-        else router_tma_kernel<4><<<grid, 128, smem, ctx->stream>>>(map, hidden, T, H, E, logits, err);
+        if (tw == 1) router_tma_kernel<1><<<grid, kRtThreads, smem, ctx->stream>>>(map, hidden, T, H, E, logits, err);
+        else if (tw == 2) router_tma_kernel<2><<<grid, kRtThreads, smem, ctx->stream>>>(map, hidden, T, H, E, logits, err);
+        else router_tma_kernel<4><<<grid, kRtThreads, smem, ctx->stream>>>(map, hidden, T, H, E, logits, err);
         K3XB_LAUNCHED(ctx);
         return K3XB_OK;
     }
