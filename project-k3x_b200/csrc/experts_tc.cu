@@ -18,16 +18,18 @@
 // Shared expert: kind::f16 (bf16 weights x bf16 activation terms).
 //
 // Launches per MoE layer (routed):
-//   worklist       tiles of <= floor(128/terms) tokens per expert group and
-//                  one 16-byte descriptor per (tile, 128-row m-tile) item
+//   worklist       tiles of <= floor(NM/terms) tokens per expert group and
+//                  one 16-byte descriptor per work item: (tile, 128-row
+//                  m-tile) for gate/up, (tile, 256-row m-tile pair) for down
 //   split_tokens   E2M1-term split of every hidden row, once per token
 //   gather_gu      tile-major gate/up B operand + scale atoms
 //   gateup         gate and up share the B tile; the epilogue applies
 //                  SwiGLU / SiTU (official_moe.cpp:95-96) and splits the result
 //                  into the down projection's E2M1 operand and scales
-//   down           the epilogue sums term columns, rounds to bf16
-//                  (official_moe.cpp:101) and scatters each row to its
-//                  (token, slot) for the ordered combine (c)
+//   down           two weight tiles per item; the epilogue sums term
+//                  columns, rounds to bf16 (official_moe.cpp:101) and
+//                  scatters each row to its (token, slot) for the ordered
+//                  combine (c)
 #include "common.cuh"
 #include "kernels.cuh"
 #include "tc_pipeline.cuh"
@@ -46,11 +48,11 @@ using tcp::kThreads;
 // HBM-streaming GEMM — and for a double-buffered gate/up accumulator.
 template <uint32_t NM> struct RoutedCfg;
 template <> struct RoutedCfg<64> {
-    static constexpr uint32_t kStagesGU = 5, kStagesD = 8, kAccbGU = 2;
+    static constexpr uint32_t kStagesGU = 5, kAccbGU = 2;
     static constexpr uint32_t kColUp = 64, kStrideGU = 128;
 };
 template <> struct RoutedCfg<128> {
-    static constexpr uint32_t kStagesGU = 4, kStagesD = 6, kAccbGU = 1;
+    static constexpr uint32_t kStagesGU = 4, kAccbGU = 1;
     static constexpr uint32_t kColUp = 128, kStrideGU = 0;
 };
 constexpr uint32_t kStagesGU = 4;   // shared expert (kind::f16) pipelines
@@ -92,7 +94,7 @@ __global__ void __launch_bounds__(1024) worklist_kernel(const uint32_t* group_co
     __shared__ uint32_t tile_base[1025];
     const uint32_t ng = *group_count;
     const uint32_t tpt = nmax / terms;
-    const uint32_t mt_gu = I / kBlockM, mt_d = H / kBlockM;
+    const uint32_t mt_gu = I / kBlockM, mt_d = (H + 2 * kBlockM - 1) / (2 * kBlockM);   // down: 256-row pairs
     const uint32_t g = threadIdx.x;
     scan[0][g] = g < ng ? (group_offset[g + 1] - group_offset[g] + tpt - 1) / tpt : 0u;
     __syncthreads();
@@ -122,7 +124,7 @@ __global__ void __launch_bounds__(1024) worklist_kernel(const uint32_t* group_co
         for (uint32_t mt = 0; mt < mt_gu; ++mt)
             t.desc_gu[tb * mt_gu + mt * nt + j] = make_uint4(e * I + mt * kBlockM, (tb + j) * nmax, nz, tok0);
         for (uint32_t mt = 0; mt < mt_d; ++mt)
-            t.desc_d[tb * mt_d + mt * nt + j] = make_uint4(e * H + mt * kBlockM, (tb + j) * nmax, nz, tok0);
+            t.desc_d[tb * mt_d + mt * nt + j] = make_uint4(e * H + mt * 2 * kBlockM, (tb + j) * nmax, nz, tok0);
     }
 }
 
@@ -236,12 +238,12 @@ struct DParams {
     float* slot_out;
     uint32_t H, I, terms, top_k;
     int* error;
+    uint32_t rowblocks;       // 128-row blocks of the stacked down weights (E * H / 128)
 };
 
 // TMEM columns. Routed gate/up: gate accumulator at 0, up at RoutedCfg::kColUp,
 // second buffer (NM = 64) kStrideGU further; block scales from 256.
 constexpr uint32_t kColAccGate = 0, kColAccUp = 128, kColSfaGate = 256, kColSfaUp = 264, kColSfbGU = 272;
-constexpr uint32_t kColAccD = 0, kColSfaD = 256, kColSfbD = 264;   // down: two accumulator buffers at 0/128
 
 template <uint32_t NM>
 __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_constant__ CUtensorMap map_gate,
@@ -306,57 +308,65 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_consta
     };
     const uint8_t* sfa[2] = {p.sfa_gate, p.sfa_up};
     const tcp::Config cfg{p.H, *p.n_items, 512, kColAccGate, RC::kColUp, RC::kStrideGU, kColSfaGate, kColSfaUp,
-                          kColSfbGU};
+                          kColSfbGU, 0, NM};
     tcp::run_pipeline<RC::kStagesGU, 2, false, RC::kAccbGU>(sm, &map_gate, &map_up, &map_b, cfg, sfa, p.sfb,
                                                             p.error, get_desc, epilogue);
 }
 
+// Down projection: an item is a PAIR of 128-row weight tiles (rows r0 and
+// r0 + 128 of one expert) sharing the activation tile, so a pipeline stage
+// moves 32 KB of weights per handful of TMA instructions. When H is an odd
+// multiple of 128 the second tile of an expert's last pair is discarded.
 template <uint32_t NM>
 __global__ void __launch_bounds__(kThreads, 1) down_kernel(const __grid_constant__ CUtensorMap map_down,
                                                             const __grid_constant__ CUtensorMap map_b,
                                                             const DParams p) {
     using RC = RoutedCfg<NM>;
     extern __shared__ uint8_t smem_raw[];
-    auto& sm = tcp::smem_from<RC::kStagesD, 1, NM>(smem_raw);
+    auto& sm = tcp::smem_from<RC::kStagesGU, 2, NM>(smem_raw);
     const uint32_t terms = p.terms;
-    const uint32_t mtc = p.H / kBlockM;
     auto get_desc = [&](uint32_t item) { return __ldg(p.desc + item); };
     auto epilogue = [&](const uint4& d, uint32_t tmem, uint32_t q, uint32_t lane) {
-        const uint32_t mt = (d.x / kBlockM) % mtc, tok0 = d.w;
-        const uint32_t used = tcp::desc_ntok(d) * terms;
-        const uint32_t lane_base = (32u * q) << 16;
-        const uint32_t h = mt * kBlockM + 32u * q + lane;
+        const uint32_t r0 = d.x % p.H, tok0 = d.w;
+        const bool second = r0 + kBlockM < p.H;
         const uint32_t ntok = tcp::desc_ntok(d);
+        const uint32_t used = ntok * terms;
+        const uint32_t lane_base = (32u * q) << 16;
+        const uint32_t h0 = r0 + 32u * q + lane, h1 = h0 + kBlockM;
         // destination rows of up to 32 tokens per round trip (lane j holds token j's)
         auto fetch_dst = [&](uint32_t j0) {
             const uint32_t a = tok0 + j0 + lane;
             return j0 + lane < ntok ? __ldg(p.assign_token + a) * p.top_k + __ldg(p.assign_slot + a) : 0u;
         };
         uint32_t dsts = fetch_dst(0);
-        float ys = 0.0f;
+        float y0 = 0.0f, y1 = 0.0f;
         uint32_t tcount = 0, j = 0;
         for (uint32_t c0 = 0; c0 < used; c0 += 16) {
-            float v[16];
-            tc::tmem_ld16(tmem + lane_base + kColAccD + c0, v);
+            float v0[16], v1[16];
+            tc::tmem_ld16(tmem + lane_base + kColAccGate + c0, v0);
+            if (second) tc::tmem_ld16(tmem + lane_base + RC::kColUp + c0, v1);
             tc::tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 if (c0 + i >= used) break;
-                ys = __fadd_rn(ys, v[i]);
+                y0 = __fadd_rn(y0, v0[i]);
+                if (second) y1 = __fadd_rn(y1, v1[i]);
                 if (++tcount < terms) continue;
                 if (j % 32 == 0 && j) dsts = fetch_dst(j);
                 const size_t dst = __shfl_sync(0xffffffffu, dsts, j % 32);
-                p.slot_out[dst * p.H + h] = round_bf16(ys);
-                ys = 0.0f;
+                p.slot_out[dst * p.H + h0] = round_bf16(y0);
+                if (second) p.slot_out[dst * p.H + h1] = round_bf16(y1);
+                y0 = y1 = 0.0f;
                 tcount = 0;
                 ++j;
             }
         }
     };
-    const uint8_t* sfa[1] = {p.sfa};
-    const tcp::Config cfg{p.I, *p.n_items, 512, kColAccD, kColAccD, 128, kColSfaD, kColSfaD, kColSfbD};
-    tcp::run_pipeline<RC::kStagesD, 1, false, 2>(sm, &map_down, &map_down, &map_b, cfg, sfa, p.sfb, p.error,
-                                                 get_desc, epilogue);
+    const uint8_t* sfa[2] = {p.sfa, p.sfa};
+    const tcp::Config cfg{p.I, *p.n_items, 512, kColAccGate, RC::kColUp, RC::kStrideGU, kColSfaGate, kColSfaUp,
+                          kColSfbGU, kBlockM, NM, p.rowblocks};
+    tcp::run_pipeline<RC::kStagesGU, 2, false, RC::kAccbGU>(sm, &map_down, &map_down, &map_b, cfg, sfa, p.sfb,
+                                                            p.error, get_desc, epilogue);
 }
 
 // ---------------------------------------------------------------------------
@@ -446,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1) shared_down_kernel(const __grid_c
         const uint32_t h = d.x + 32u * q + lane;
         for (uint32_t c0 = 0; c0 < used; c0 += 16) {
             float v[16];
-            tc::tmem_ld16(tmem + lane_base + kColAccD + c0, v);
+            tc::tmem_ld16(tmem + lane_base + kColAccGate + c0, v);
             tc::tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; i += 2) {
@@ -457,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1) shared_down_kernel(const __grid_c
         }
     };
     const uint8_t* none[1] = {nullptr};
-    const tcp::Config cfg{p.Is, p.items, 256, kColAccD, kColAccD, 128, 0, 0, 0};
+    const tcp::Config cfg{p.Is, p.items, 256, kColAccGate, kColAccGate, 128, 0, 0, 0};
     tcp::run_pipeline<kStagesD, 1, true, 2>(sm, &map_down, &map_down, &map_b, cfg, none, nullptr, p.error, get_desc,
                                             epilogue);
 }
@@ -539,7 +549,7 @@ Layout layout_of(const k3xb_moe_layer& L, uint32_t T) {
     l.tpt = l.nmax / l.terms;
     l.max_tiles = std::min(L.experts, assigns) + (assigns + l.tpt - 1) / l.tpt;
     l.mt_gu = L.inter / kBlockM;
-    l.mt_d = L.hidden / kBlockM;
+    l.mt_d = (L.hidden + 2 * kBlockM - 1) / (2 * kBlockM);
     l.b_gu = static_cast<size_t>(l.max_tiles) * l.nmax * (L.hidden / 2);
     l.sfb_gu = static_cast<size_t>(l.max_tiles) * (L.hidden / 128) * kAtomBytes;
     l.b_d = static_cast<size_t>(l.max_tiles) * l.nmax * (L.inter / 2);
@@ -583,7 +593,7 @@ int launch_routed(k3xb_ctx* ctx, const CUtensorMap& map_gate, const CUtensorMap&
                   const CUtensorMap& map_down, const CUtensorMap& map_bd, const GuParams& gp, const DParams& dp) {
     using RC = RoutedCfg<NM>;
     const size_t smem_gu = tcp::smem_bytes<RC::kStagesGU, 2, NM>();
-    const size_t smem_d = tcp::smem_bytes<RC::kStagesD, 1, NM>();
+    const size_t smem_d = tcp::smem_bytes<RC::kStagesGU, 2, NM>();
     static bool configured = false;   // per template instance
     if (!configured) {
         K3XB_CUDA(ctx, cudaFuncSetAttribute(gateup_kernel<NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -647,8 +657,8 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
     if ((st = make_map(ctx, &map_gate, L.gate_packed, H / 2, static_cast<uint64_t>(L.experts) * I, 128))) return st;
     if ((st = make_map(ctx, &map_up, L.up_packed, H / 2, static_cast<uint64_t>(L.experts) * I, 128))) return st;
     if ((st = make_map(ctx, &map_down, L.down_packed, I / 2, static_cast<uint64_t>(L.experts) * H, 128))) return st;
-    if ((st = make_map(ctx, &map_bgu, bf.b_gu, H / 2, static_cast<uint64_t>(l.max_tiles) * l.nmax, 16))) return st;
-    if ((st = make_map(ctx, &map_bd, bf.b_d, I / 2, static_cast<uint64_t>(l.max_tiles) * l.nmax, 16))) return st;
+    if ((st = make_map(ctx, &map_bgu, bf.b_gu, H / 2, static_cast<uint64_t>(l.max_tiles) * l.nmax, l.nmax))) return st;
+    if ((st = make_map(ctx, &map_bd, bf.b_d, I / 2, static_cast<uint64_t>(l.max_tiles) * l.nmax, l.nmax))) return st;
 
     worklist_kernel<<<1, 1024, 0, ctx->stream>>>(plan.group_count, plan.group_offset, plan.group_expert, l.terms, H,
                                                  I, l.nmax, bf.tb);
@@ -666,7 +676,7 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
     GuParams gp{bf.tb.desc_gu, bf.tb.counts + 1, sfa_gate, sfa_up, bf.sfb_gu, bf.b_d, bf.sfb_d, H, I, l.terms,
                 L.activation, L.situ_beta, L.situ_linear_beta, ctx->status_word};
     DParams dp{bf.tb.desc_d, bf.tb.counts + 2, plan.assign_token, plan.assign_slot, sfa_down, bf.sfb_d, slot_out,
-               H, I, l.terms, L.top_k, ctx->status_word};
+               H, I, l.terms, L.top_k, ctx->status_word, static_cast<uint32_t>(static_cast<size_t>(L.experts) * H / kBlockM)};
     return l.nmax == 64 ? launch_routed<64>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, dp)
                         : launch_routed<128>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, dp);
 }

@@ -59,6 +59,9 @@ struct Config {
     uint32_t col_acc0, col_acc1;   // accumulator column of A0 / A1 (buffer 0)
     uint32_t acc_stride;    // column distance between accumulator buffers
     uint32_t col_sfa0, col_sfa1, col_sfb;
+    uint32_t a1_row_off = 0;          // A1 tile rows = A0 rows + a1_row_off (same tensor map allowed)
+    uint32_t b_box = 16;              // B rows per TMA box (the B tensor map's box height)
+    uint32_t a_rowblocks = 0xffffffffu;   // 128-row scale blocks of A (clamps the A1 scale row)
 };
 
 __device__ __forceinline__ uint32_t desc_n(const uint4& d) { return d.z & 0xffffu; }
@@ -112,18 +115,23 @@ __device__ __forceinline__ void run_pipeline(Smem<S, NA, BROWS>& sm, const CUten
                 const uint32_t st = it % S, ph = (it / S) & 1u;
                 if (!tc::mbar_wait(&sm.empty[st], ph ^ 1u, abort)) break;
                 const uint32_t atoms = F16 ? 0u : min(2u, (K - s * kStepElems) / 128u);
-                const uint32_t bytes = NA * kTileBytes + n * 128u + (NA + 1) * atoms * kAtomBytes;
+                const uint32_t b_loads = (n + cfg.b_box - 1) / cfg.b_box;
+                const uint32_t bytes = NA * kTileBytes + b_loads * cfg.b_box * 128u + (NA + 1) * atoms * kAtomBytes;
                 tc::mbar_arrive_expect_tx(&sm.full[st], bytes);
                 const int x = static_cast<int>(s * 128u);
                 tc::tma_load_2d(sm.a[0][st], map_a0, &sm.full[st], x, static_cast<int>(a_row));
-                if (NA == 2) tc::tma_load_2d(sm.a[NA - 1][st], map_a1, &sm.full[st], x, static_cast<int>(a_row));
-                for (uint32_t r = 0; r < n; r += 16)
-                    tc::tma_load_2d(sm.b[st] + r * 128u, map_b, &sm.full[st], x, static_cast<int>(b_row + r));
+                if (NA == 2)
+                    tc::tma_load_2d(sm.a[NA - 1][st], map_a1, &sm.full[st], x, static_cast<int>(a_row + cfg.a1_row_off));
+                for (uint32_t r = 0; r < b_loads; ++r)
+                    tc::tma_load_2d(sm.b[st] + r * cfg.b_box * 128u, map_b, &sm.full[st], x,
+                                    static_cast<int>(b_row + r * cfg.b_box));
                 if (!F16) {
-                    const size_t a_atom = static_cast<size_t>(a_row / 128) * atoms_per_row + 2 * s;
-                    for (uint32_t m = 0; m < NA; ++m)
+                    for (uint32_t m = 0; m < NA; ++m) {
+                        const uint32_t rb = min((a_row + (m ? cfg.a1_row_off : 0u)) / 128u, cfg.a_rowblocks - 1u);
+                        const size_t a_atom = static_cast<size_t>(rb) * atoms_per_row + 2 * s;
                         tc::bulk_load(sm.sfa[m][st], sfa_src[m] + a_atom * kAtomBytes, atoms * kAtomBytes,
                                       &sm.full[st]);
+                    }
                     // one scale-atom column per B tile (BROWS rows padded to the atom's 128)
                     const size_t b_atom = static_cast<size_t>(b_row / BROWS) * atoms_per_row + 2 * s;
                     tc::bulk_load(sm.sfb[st], sfb_src + b_atom * kAtomBytes, atoms * kAtomBytes, &sm.full[st]);
