@@ -11,8 +11,8 @@
  * missing or unsupported device returns K3XB_BACKEND_UNAVAILABLE or
  * K3XB_UNSUPPORTED_ARCHITECTURE.
  *
- * Each entry point names the reference interface it replaces. The C++20
- * adapter (project-k3x_b200/cpp/b200_backend.cpp) maps k3x::ComputeBackend
+ * Each entry point names the reference interface it replaces; a C++20
+ * adapter on the reference side maps k3x::ComputeBackend
  * (runtime/include/k3x/backend.hpp:326-462) and the free verification
  * functions onto these calls.
  */
@@ -212,6 +212,103 @@ int k3xb_kda_commit(k3xb_ctx* ctx, const float* state, const int32_t* parent,
                     uint32_t head_dim, const float* q, const float* k,
                     const float* v, const float* log_decay, const float* beta,
                     const int32_t* commit_node, float* state_out);
+
+/* ---- full KDA block and the KDA + MoE layer -------------------------------- */
+/* Weights of one official KDA block (official_kda.hpp / official_kda.cpp:
+ * 198-426), bf16 words unless marked float. P = heads * head_dim, H the
+ * model width, w = conv_width. */
+typedef struct {
+    uint32_t heads, head_dim, conv_width;
+    float eps, gate_lower_bound;
+    const uint16_t* q_proj;     /* [P][H] */
+    const uint16_t* k_proj;     /* [P][H] */
+    const uint16_t* v_proj;     /* [P][H] */
+    const float* q_conv;        /* [P][w] float */
+    const float* k_conv;        /* [P][w] float */
+    const float* v_conv;        /* [P][w] float */
+    const uint16_t* f_a_proj;   /* [d][H] */
+    const uint16_t* f_b_proj;   /* [P][d] */
+    const float* a_log;         /* [d] float */
+    const float* dt_bias;       /* [P] float */
+    const uint16_t* b_proj;     /* [h][H] */
+    const uint16_t* g_proj;     /* [P][H] */
+    const float* o_norm;        /* [d] float */
+    const uint16_t* o_proj;     /* [H][P] */
+} k3xb_kda_layer;
+
+/* Device bytes of the trace k3xb_kda_block leaves for a later commit: the
+ * recurrence inputs q, k, v, log-decay, beta and the projected q, k, v of
+ * every node. */
+size_t k3xb_kda_trace_bytes(const k3xb_kda_layer* w, uint32_t nodes,
+                            uint32_t sequences);
+
+/* official_kda_cpu (official_kda.cpp:198-426) over a draft topology shared
+ * by S sequences (parent is a HOST array, as for k3xb_kda_tree): node n's
+ * short-conv window and recurrent state continue from its ancestors, and
+ * from the sequence's prefix state below the roots. A linear draft is
+ * parent[n] = n - 1. hidden [S][N][H]; conv [S][3][w-1][P] bf16 words (the
+ * q, k, v histories, oldest row first); recurrent [S][h][d][d]. Neither
+ * state is modified. out [S][N][H]. trace (k3xb_kda_trace_bytes) may be
+ * NULL when no commit follows. */
+int k3xb_kda_block(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t hidden,
+                   const float* x, const int32_t* parent, uint32_t nodes,
+                   uint32_t sequences, const uint16_t* conv,
+                   const float* recurrent, float* out, void* trace);
+
+/* The state after node commit_node[s] (HOST; -1 keeps the prefix state)
+ * from a k3xb_kda_block trace, as Engine::forward_expert_major_block's
+ * commit (model.cpp:1660-1664) keeps the last committed position: the
+ * recurrent state replayed along the path (bit-identical to the verify
+ * pass) and the conv windows ending at that node. conv_out may alias conv;
+ * recurrent_out must not alias recurrent. */
+int k3xb_kda_block_commit(k3xb_ctx* ctx, const k3xb_kda_layer* w,
+                          const void* trace, const int32_t* parent,
+                          uint32_t nodes, uint32_t sequences,
+                          const int32_t* commit_node, const uint16_t* conv,
+                          const float* recurrent, uint16_t* conv_out,
+                          float* recurrent_out);
+
+/* prepare_official_moe_input (official_moe.cpp:156-209) and the layer's
+ * input path (official_layer.cpp:159-172): attention_residual of the two
+ * sources (official_layer.cpp:42-102), then rms_norm (:104-125) with
+ * post_norm. With delta != NULL the first source is round_bf16(round_bf16(a)
+ * + delta) (official_layer.cpp:190-193), written to prefix_out. Rows [T][H];
+ * norm/proj/post_norm [H] bf16 words. */
+int k3xb_attention_residual_norm(k3xb_ctx* ctx, const float* a,
+                                 const float* delta, const float* block,
+                                 const uint16_t* residual_norm,
+                                 const uint16_t* residual_proj,
+                                 const uint16_t* post_norm, uint32_t tokens,
+                                 uint32_t hidden, float eps,
+                                 float* prefix_out, float* out);
+
+/* One KDA + MoE layer: official_layer_cpu (official_layer.cpp:134-244) with
+ * the plain hidden-space MoE (official_moe.cpp:271-344 without the latent
+ * steps :296, :323-331): out = round_bf16(round_bf16(prefix) +
+ * round_bf16(routed + shared)). moe.hidden must equal hidden. */
+typedef struct {
+    uint32_t hidden;
+    float rms_eps;
+    const uint16_t* self_residual_norm;   /* [H] */
+    const uint16_t* self_residual_proj;   /* [H] */
+    const uint16_t* input_norm;           /* [H] */
+    const uint16_t* moe_residual_norm;    /* [H] */
+    const uint16_t* moe_residual_proj;    /* [H] */
+    const uint16_t* post_norm;            /* [H] */
+    k3xb_kda_layer kda;
+    k3xb_moe_layer moe;
+} k3xb_layer;
+
+/* The layer over S sequences x N draft nodes (parent HOST, as above):
+ * hidden_in and block_source [S][N][H] -> hidden_out [S][N][H]; KDA state
+ * as k3xb_kda_block (unchanged; commit with k3xb_kda_block_commit and the
+ * trace). expert_ids [S*N][top_k] may be NULL. */
+int k3xb_layer_forward(k3xb_ctx* ctx, const k3xb_layer* layer,
+                       const float* hidden_in, const float* block_source,
+                       const int32_t* parent, uint32_t nodes,
+                       uint32_t sequences, const uint16_t* conv,
+                       const float* recurrent, float* hidden_out,
+                       uint32_t* expert_ids, void* kda_trace);
 
 /* ---- (e) acceptance ------------------------------------------------------- */
 /* verify_greedy_target_block (runtime/src/speculative.cpp:74-112) for S

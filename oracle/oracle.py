@@ -128,6 +128,8 @@ class Restatement:
         L.k3xo_kda_tree.argtypes = [_f32p, _i32p, _sz, _f32p, _f32p, _f32p, _f32p, _f32p,
                                     _sz, _sz, _f32p, C.c_void_p]
         L.k3xo_kda_block.argtypes = [C.c_void_p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p, _f32p]
+        L.k3xo_rms_norm_bf16.argtypes = [_f32p, _u16p, _sz, C.c_float, _f32p]
+        L.k3xo_attention_residual.argtypes = [_f32p, _f32p, _u16p, _u16p, _sz, C.c_float, _f32p]
         L.k3xo_argmax.restype = C.c_uint32
         L.k3xo_argmax.argtypes = [_f32p, _sz]
         L.k3xo_verify_greedy_block.argtypes = [C.c_uint32, _u32p, _sz, _sz, _sz, _u32p,
@@ -286,6 +288,79 @@ class Restatement:
         del keep
         return out.reshape(T, weights["hidden"]), (cq, ck, cv, rec)
 
+    # -- layer composition ------------------------------------------------------
+    def rms_norm(self, x, weight, eps):
+        x = _c(x, np.float32)
+        out = np.empty_like(x)
+        self._check(self.lib.k3xo_rms_norm_bf16(x, _c(weight, np.uint16), x.size, eps, out), "rms_norm")
+        return out
+
+    def attention_residual(self, prefix, block, norm, proj, eps):
+        prefix = _c(prefix, np.float32)
+        out = np.empty_like(prefix)
+        self._check(self.lib.k3xo_attention_residual(prefix, _c(block, np.float32), _c(norm, np.uint16),
+                                                     _c(proj, np.uint16), prefix.size, eps, out),
+                    "attention_residual")
+        return out
+
+    def prepare_input(self, prefix, block, norm, proj, post, eps):
+        """prepare_official_moe_input (official_moe.cpp:156-209) for one row:
+        attention residual then RMSNorm."""
+        return self.rms_norm(self.attention_residual(prefix, block, norm, proj, eps), post, eps)
+
+    def kda_block_path(self, weights: dict, x, path, conv, recurrent):
+        """The official block over the nodes of one root-to-node path (a
+        linear sequence): outputs for those nodes and the state after the
+        last. conv = (q, k, v) histories [(w-1)*P] bf16 words."""
+        if len(path) == 0:
+            return np.zeros((0, weights["hidden"]), np.float32), (*conv, recurrent)
+        return self.kda_block(weights, x[list(path)], *conv, recurrent)
+
+    @staticmethod
+    def _path(parent, node):
+        p = []
+        while node >= 0:
+            p.append(int(node))
+            node = int(parent[node])
+        return p[::-1]
+
+    def kda_block_tree(self, weights: dict, x, parent, conv, recurrent):
+        """Draft-tree semantics of the block (new; official_kda.cpp:198-426
+        per path): node n's output is the block's output for n over the path
+        root..n from the prefix state. Runs one path per leaf."""
+        n = len(parent)
+        has_child = np.zeros(n, bool)
+        for i in range(n):
+            if parent[i] >= 0:
+                has_child[parent[i]] = True
+        out = np.full((n, weights["hidden"]), np.nan, np.float32)
+        for leaf in np.nonzero(~has_child)[0]:
+            path = self._path(parent, leaf)
+            o, _ = self.kda_block_path(weights, x, path, conv, recurrent)
+            out[path] = o
+        return out
+
+    def kda_block_commit(self, weights: dict, x, parent, node, conv, recurrent):
+        _, st = self.kda_block_path(weights, x, self._path(parent, node), conv, recurrent)
+        return st
+
+    def layer_forward(self, layer: dict, hidden_in, block, parent, conv, recurrent):
+        """official_layer_cpu (official_layer.cpp:134-244) with the plain MoE
+        (official_moe.cpp:271-344 minus :296, :323-331) for one sequence's
+        draft nodes [N][H]. Returns (out, expert ids, moe input)."""
+        eps = layer["rms_eps"]
+        N = hidden_in.shape[0]
+        xin = np.stack([self.prepare_input(hidden_in[i], block[i], layer["self_residual_norm"],
+                                           layer["self_residual_proj"], layer["input_norm"], eps)
+                        for i in range(N)])
+        kda_out = self.kda_block_tree(layer["kda"], xin, parent, conv, recurrent)
+        prefix = self.round_bf16(self.round_bf16(hidden_in) + kda_out)
+        moe_in = np.stack([self.prepare_input(prefix[i], block[i], layer["moe_residual_norm"],
+                                              layer["moe_residual_proj"], layer["post_norm"], eps)
+                           for i in range(N)])
+        combined, ids, _ = self.moe_layer(layer["moe"], moe_in)
+        return self.round_bf16(self.round_bf16(prefix) + combined), ids, moe_in
+
     def argmax(self, logits):
         logits = _c(logits, np.float32)
         return int(self.lib.k3xo_argmax(logits, logits.size))
@@ -345,6 +420,7 @@ class Reference:
                                              C.c_int]
         L.k3xr_official_kda_cpu.argtypes = [C.c_void_p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p,
                                             _f32p]
+        L.k3xr_prepare_moe_input.argtypes = [_f32p, _f32p, _u16p, _u16p, _u16p, _sz, C.c_float, _f32p]
 
     def decode_mxfp4(self, packed, scales, rows, cols, group=32):
         out = np.empty(rows * cols, np.float32)
@@ -461,6 +537,14 @@ class Reference:
             raise OracleError(st, "ref moe layer")
         return out, ids, contrib
 
+    def prepare_input(self, prefix, block, norm, proj, post, eps):
+        out = np.empty(len(prefix), np.float32)
+        st = self.lib.k3xr_prepare_moe_input(_c(prefix, np.float32), _c(block, np.float32), _c(norm, np.uint16),
+                                             _c(proj, np.uint16), _c(post, np.uint16), len(prefix), eps, out)
+        if st:
+            raise OracleError(st, "prepare_official_moe_input")
+        return out
+
     def kda_block(self, weights: dict, hidden, conv_q, conv_k, conv_v, recurrent):
         s, keep = kda_struct(weights)
         hidden = _c(hidden, np.float32)
@@ -527,3 +611,35 @@ def make_moe_layer(rs: Restatement, seed, hidden, inter, experts, top_k, shared_
 
 def bf16_normal(g, shape, sigma=1.0):
     return bf16_values(bf16_words(g.normal(0.0, sigma, size=shape).astype(np.float32)))
+
+
+def make_kda_weights(g, hidden, heads, head_dim, conv_width=4, sigma=0.02):
+    """Synthetic official KDA block weights (the dict kda_struct reads):
+    projections N(0, sigma) in bf16, conv taps and gate parameters float."""
+    P = heads * head_dim
+    n = lambda *s: bf16_words(g.normal(0.0, sigma, size=s))
+    return dict(hidden=hidden, heads=heads, head_dim=head_dim, conv_width=conv_width, eps=1e-5,
+                gate_lower_bound=-5.0,
+                q_proj=n(P, hidden), k_proj=n(P, hidden), v_proj=n(P, hidden),
+                q_conv=g.normal(0.0, 0.5, size=(P, conv_width)).astype(np.float32),
+                k_conv=g.normal(0.0, 0.5, size=(P, conv_width)).astype(np.float32),
+                v_conv=g.normal(0.0, 0.5, size=(P, conv_width)).astype(np.float32),
+                f_a_proj=n(head_dim, hidden), f_b_proj=bf16_words(g.normal(0.0, 0.1, size=(P, head_dim))),
+                a_log=g.normal(0.0, 0.3, size=head_dim).astype(np.float32),
+                dt_bias=g.normal(0.0, 0.3, size=P).astype(np.float32),
+                b_proj=n(heads, hidden), g_proj=n(P, hidden),
+                o_norm=np.ones(head_dim, np.float32), o_proj=n(hidden, P))
+
+
+def make_layer(rs: Restatement, seed, hidden, heads, head_dim, experts, top_k, inter, shared_inter,
+               conv_width=4, sigma=0.02):
+    """Synthetic KDA + MoE layer (BASELINE configs[0] recipe: N(0, sigma)
+    weights, norms = 1, residual projections N(0, sigma), MXFP4 experts)."""
+    g = np.random.default_rng(seed)
+    ones = bf16_words(np.ones(hidden, np.float32))
+    return dict(hidden=hidden, rms_eps=1e-6,
+                self_residual_norm=ones, self_residual_proj=bf16_words(g.normal(0.0, sigma, size=hidden)),
+                input_norm=ones, moe_residual_norm=ones,
+                moe_residual_proj=bf16_words(g.normal(0.0, sigma, size=hidden)), post_norm=ones,
+                kda=make_kda_weights(g, hidden, heads, head_dim, conv_width, sigma),
+                moe=make_moe_layer(rs, seed + 1000, hidden, inter, experts, top_k, shared_inter, sigma))

@@ -97,6 +97,25 @@ void k3xr_situ_glu(float* out, const float* gate, const float* up, std::size_t n
     k3x::situ_glu({out, n}, {gate, n}, {up, n}, beta, linear(linear_beta));
 }
 
+// prepare_official_moe_input (official_moe.cpp:156-209): attention residual
+// of {block, prefix} then RMSNorm with post_norm; only the three weights it
+// reads are set.
+int k3xr_prepare_moe_input(const float* prefix, const float* block, const std::uint16_t* residual_norm,
+                           const std::uint16_t* residual_proj, const std::uint16_t* post_norm, std::size_t n,
+                           float eps, float* out) {
+    k3x::OfficialMoeWeights w{};
+    w.residual_norm.values = {residual_norm, n};
+    w.residual_proj.values = {residual_proj, n};
+    w.residual_proj.rows = 1;
+    w.residual_proj.cols = n;
+    w.post_norm.values = {post_norm, n};
+    const k3x::OfficialMoeInput input{std::vector<float>(prefix, prefix + n), std::vector<float>(block, block + n)};
+    auto r = k3x::prepare_official_moe_input(input, w, eps);
+    if (!r) return code(r);
+    std::copy(r.value().begin(), r.value().end(), out);
+    return 0;
+}
+
 int k3xr_route_official_moe(const float* hidden, const std::uint16_t* router,
                             std::size_t experts, std::size_t hidden_size,
                             const float* correction, std::size_t top_k,

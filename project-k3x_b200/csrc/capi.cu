@@ -523,3 +523,294 @@ int k3xb_fill_normal_mxfp4(k3xb_ctx* ctx, uint8_t* packed, uint8_t* scales, size
 }
 
 }  // extern "C"
+
+// ---- full KDA block and the KDA + MoE layer ----------------------------------
+
+namespace {
+
+// Per-node values a commit replays (recurrence inputs) and reads (projected
+// q, k, v for the conv windows).
+struct KdaTrace {
+    float *qn, *kn, *cv, *ld, *be, *pq, *pk, *pv;
+};
+
+template <typename A>
+void layout_trace(A& a, size_t T, size_t P, size_t h, KdaTrace* out) {
+    KdaTrace tmp{};
+    KdaTrace& r = out ? *out : tmp;
+    r.qn = a.template take<float>(T * P);
+    r.kn = a.template take<float>(T * P);
+    r.cv = a.template take<float>(T * P);
+    r.ld = a.template take<float>(T * P);
+    r.be = a.template take<float>(T * h);
+    r.pq = a.template take<float>(T * P);
+    r.pk = a.template take<float>(T * P);
+    r.pv = a.template take<float>(T * P);
+}
+
+struct KdaWork {
+    float *xr, *og, *fl, *bp, *fg, *cq, *ck, *ro, *gt;
+    uint16_t *xt_h, *xt_d, *xt_p;
+    int32_t* tables;   // anc [N][w-1], then the recurrence schedule
+};
+
+template <typename A>
+void layout_kda_work(A& a, size_t T, size_t H, size_t P, size_t d, size_t h, size_t table_ints, KdaWork* out) {
+    KdaWork tmp{};
+    KdaWork& r = out ? *out : tmp;
+    r.xr = a.template take<float>(T * H);
+    r.og = a.template take<float>(T * P);
+    r.fl = a.template take<float>(T * d);
+    r.bp = a.template take<float>(T * h);
+    r.fg = a.template take<float>(T * P);
+    r.cq = a.template take<float>(T * P);
+    r.ck = a.template take<float>(T * P);
+    r.ro = a.template take<float>(T * P);
+    r.gt = a.template take<float>(T * P);
+    r.xt_h = a.template take<uint16_t>(2 * T * H, 1024);
+    r.xt_d = a.template take<uint16_t>(2 * T * d, 1024);
+    r.xt_p = a.template take<uint16_t>(2 * T * P, 1024);
+    r.tables = a.template take<int32_t>(table_ints);
+}
+
+int validate_kda(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t H) {
+    if (!w) return fail(ctx, K3XB_INVALID_EXTENT, "null KDA weights");
+    if (!w->heads || !w->head_dim || w->conv_width < 2 || !H)
+        return fail(ctx, K3XB_INVALID_EXTENT, "KDA dimensions (conv_width >= 2)");
+    if (H % 8 || w->head_dim % 8)
+        return fail(ctx, K3XB_INVALID_EXTENT, "KDA projections need hidden and head_dim multiples of 8");
+    if (w->head_dim > 128) return fail(ctx, K3XB_INVALID_EXTENT, "KDA head_dim <= 128");
+    if (!w->q_proj || !w->k_proj || !w->v_proj || !w->q_conv || !w->k_conv || !w->v_conv || !w->f_a_proj ||
+        !w->f_b_proj || !w->a_log || !w->dt_bias || !w->b_proj || !w->g_proj || !w->o_norm || !w->o_proj)
+        return fail(ctx, K3XB_INVALID_EXTENT, "missing KDA weights");
+    if (!(w->eps > 0.0f)) return fail(ctx, K3XB_INVALID_EXTENT, "KDA eps must be positive");
+    return K3XB_OK;
+}
+
+// anc[n][j-1]: node n's j-th ancestor (j = 1..w-1), or -(r+1) for conv
+// history row r once the path leaves the tree (the row before a root is
+// the newest, w-2).
+void ancestor_table(const int32_t* parent, uint32_t N, uint32_t w, int32_t* anc) {
+    for (uint32_t n = 0; n < N; ++n) {
+        int32_t x = static_cast<int32_t>(n);
+        uint32_t inside = 0;   // ancestors met inside the tree
+        for (uint32_t j = 1; j < w; ++j) {
+            if (x >= 0) x = parent[x];
+            if (x >= 0) {
+                ++inside;
+                anc[n * (w - 1) + j - 1] = x;
+            } else {
+                const int32_t row = static_cast<int32_t>(w - 1) - static_cast<int32_t>(j - inside);
+                anc[n * (w - 1) + j - 1] = -(row + 1);
+            }
+        }
+    }
+}
+
+int kda_block_device(k3xb_ctx* ctx, const k3xb_kda_layer& w, uint32_t H, const float* x, bool x_is_bf16,
+                     uint32_t N, uint32_t S, const uint16_t* conv, const float* rec, const KdaSchedule& sch,
+                     const KdaTrace& tr, const KdaWork& wk, float* out) {
+    const uint32_t T = N * S, h = w.heads, d = w.head_dim, P = h * d, cw = w.conv_width;
+    int st;
+    const float* xin = x;
+    if (!x_is_bf16) {   // the block rounds its input first (official_kda.cpp:235-240)
+        if ((st = launch_residual_round(ctx, x, static_cast<size_t>(T) * H, wk.xr))) return st;
+        xin = wk.xr;
+    }
+    if ((st = launch_split_terms(ctx, xin, T, H, wk.xt_h))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_h, w.q_proj, T, P, H, 1, tr.pq))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_h, w.k_proj, T, P, H, 1, tr.pk))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_h, w.v_proj, T, P, H, 1, tr.pv))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_h, w.g_proj, T, P, H, 1, wk.og))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_h, w.f_a_proj, T, d, H, 1, wk.fl))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_h, w.b_proj, T, h, H, 1, wk.bp))) return st;
+    if ((st = launch_split_terms(ctx, wk.fl, T, d, wk.xt_d))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_d, w.f_b_proj, T, P, d, 1, wk.fg))) return st;
+    const float* proj[3] = {tr.pq, tr.pk, tr.pv};
+    const float* cwt[3] = {w.q_conv, w.k_conv, w.v_conv};
+    float* const co[3] = {wk.cq, wk.ck, tr.cv};
+    if ((st = launch_short_conv(ctx, proj, cwt, conv, wk.tables, S, N, P, cw, co))) return st;
+    if ((st = launch_qk_gates(ctx, wk.cq, wk.ck, wk.fg, wk.bp, w.a_log, w.dt_bias, w.gate_lower_bound, T, h, d,
+                              tr.qn, tr.kn, tr.ld, tr.be)))
+        return st;
+    const int32_t* sched = wk.tables + static_cast<size_t>(N) * (cw - 1);
+    const size_t visit = sch.order.size();
+    if ((st = launch_kda(ctx, rec, sched, sched + visit, sched + 2 * visit, static_cast<uint32_t>(visit), N, S, h, d,
+                         tr.qn, tr.kn, tr.cv, tr.ld, tr.be, wk.ro, nullptr, sch.levels)))
+        return st;
+    if ((st = launch_gated_norm(ctx, wk.ro, wk.og, w.o_norm, w.eps, T, h, d, wk.gt))) return st;
+    if ((st = launch_split_terms(ctx, wk.gt, T, P, wk.xt_p))) return st;
+    ++ctx->stats.kda_calls;
+    return launch_linear_terms(ctx, wk.xt_p, w.o_proj, T, H, P, 1, out);
+}
+
+// anc table + schedule packed for one upload
+std::vector<int32_t> kda_tables(const int32_t* parent, uint32_t N, uint32_t cw, const KdaSchedule& sch) {
+    std::vector<int32_t> t(static_cast<size_t>(N) * (cw - 1));
+    ancestor_table(parent, N, cw, t.data());
+    t.insert(t.end(), sch.order.begin(), sch.order.end());
+    t.insert(t.end(), sch.depth.begin(), sch.depth.end());
+    t.insert(t.end(), sch.from_stack.begin(), sch.from_stack.end());
+    return t;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t k3xb_kda_trace_bytes(const k3xb_kda_layer* w, uint32_t nodes, uint32_t S) {
+    if (!w) return 0;
+    Sizer sz;
+    layout_trace(sz, static_cast<size_t>(nodes) * S, static_cast<size_t>(w->heads) * w->head_dim, w->heads, nullptr);
+    return sz.used;
+}
+
+int k3xb_kda_block(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t H, const float* x, const int32_t* parent,
+                   uint32_t N, uint32_t S, const uint16_t* conv, const float* rec, float* out, void* trace) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    int st = validate_kda(ctx, w, H);
+    if (st) return st;
+    if (!x || !parent || !N || !S || !conv || !rec || !out) return fail(ctx, K3XB_INVALID_EXTENT, "kda_block arguments");
+    KdaSchedule sch;
+    if ((st = schedule_tree(ctx, parent, N, sch))) return st;
+    const std::vector<int32_t> tables = kda_tables(parent, N, w->conv_width, sch);
+    const size_t T = static_cast<size_t>(N) * S, P = static_cast<size_t>(w->heads) * w->head_dim;
+    Sizer sz;
+    if (!trace) layout_trace(sz, T, P, w->heads, nullptr);
+    layout_kda_work(sz, T, H, P, w->head_dim, w->heads, tables.size(), nullptr);
+    void* base;
+    if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
+    Carver c(base);
+    KdaTrace tr{};
+    if (trace) {
+        Carver t(trace);
+        layout_trace(t, T, P, w->heads, &tr);
+    } else {
+        layout_trace(c, T, P, w->heads, &tr);
+    }
+    KdaWork wk{};
+    layout_kda_work(c, T, H, P, w->head_dim, w->heads, tables.size(), &wk);
+    K3XB_CUDA(ctx, cudaMemcpyAsync(wk.tables, tables.data(), tables.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                   ctx->stream));
+    return kda_block_device(ctx, *w, H, x, false, N, S, conv, rec, sch, tr, wk, out);
+}
+
+int k3xb_kda_block_commit(k3xb_ctx* ctx, const k3xb_kda_layer* w, const void* trace, const int32_t* parent,
+                          uint32_t N, uint32_t S, const int32_t* commit_node, const uint16_t* conv, const float* rec,
+                          uint16_t* conv_out, float* rec_out) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!w || !trace || !parent || !N || !S || !commit_node || !conv || !rec || !conv_out || !rec_out)
+        return fail(ctx, K3XB_INVALID_EXTENT, "kda_block_commit arguments");
+    if (rec_out == rec) return fail(ctx, K3XB_INVALID_EXTENT, "recurrent_out must not alias recurrent");
+    const uint32_t cw = w->conv_width, h = w->heads, d = w->head_dim;
+    if (cw < 2) return fail(ctx, K3XB_INVALID_EXTENT, "conv_width >= 2");
+    for (uint32_t i = 0; i < N; ++i)
+        if (parent[i] < -1 || parent[i] >= static_cast<int32_t>(i))
+            return fail(ctx, K3XB_INVALID_EXTENT, "draft tree: parent[n] must be -1 or < n");
+    // anc_commit[s][j]: the commit node (j = 0) and its ancestors, else history rows
+    std::vector<int32_t> anc(static_cast<size_t>(S) * (cw - 1));
+    for (uint32_t s = 0; s < S; ++s) {
+        const int32_t node = commit_node[s];
+        if (node < -1 || node >= static_cast<int32_t>(N)) return fail(ctx, K3XB_INVALID_EXTENT, "commit node out of range");
+        int32_t x = node;
+        uint32_t inside = 0;
+        for (uint32_t j = 0; j + 1 < cw; ++j) {
+            if (j > 0 && x >= 0) x = parent[x];
+            if (x >= 0) {
+                ++inside;
+                anc[static_cast<size_t>(s) * (cw - 1) + j] = x;
+            } else {
+                const int32_t row = static_cast<int32_t>(cw) - 2 - static_cast<int32_t>(j - inside);
+                anc[static_cast<size_t>(s) * (cw - 1) + j] = -(row + 1);
+            }
+        }
+    }
+    const size_t T = static_cast<size_t>(N) * S, P = static_cast<size_t>(h) * d;
+    KdaTrace tr{};
+    Carver t(const_cast<void*>(trace));
+    layout_trace(t, T, P, h, &tr);
+    void* base;
+    int st = ensure_scratch(ctx, anc.size() * sizeof(int32_t), &base);
+    if (st) return st;
+    K3XB_CUDA(ctx, cudaMemcpyAsync(base, anc.data(), anc.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                   ctx->stream));
+    const float* proj[3] = {tr.pq, tr.pk, tr.pv};
+    if ((st = launch_conv_commit(ctx, proj, conv, static_cast<const int32_t*>(base), S, N, static_cast<uint32_t>(P),
+                                 cw, conv_out)))
+        return st;
+    return k3xb_kda_commit(ctx, rec, parent, N, S, h, d, tr.qn, tr.kn, tr.cv, tr.ld, tr.be, commit_node, rec_out);
+}
+
+int k3xb_attention_residual_norm(k3xb_ctx* ctx, const float* a, const float* delta, const float* block,
+                                 const uint16_t* rnorm, const uint16_t* rproj, const uint16_t* post, uint32_t T,
+                                 uint32_t H, float eps, float* prefix_out, float* out) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!a || !block || !rnorm || !rproj || !post || !T || !H || !out || (delta && !prefix_out))
+        return fail(ctx, K3XB_INVALID_EXTENT, "attention residual arguments");
+    if (!(eps > 0.0f)) return fail(ctx, K3XB_INVALID_EXTENT, "eps must be positive");
+    return launch_attnres_norm(ctx, a, delta, block, rnorm, rproj, post, T, H, eps, prefix_out, out);
+}
+
+int k3xb_layer_forward(k3xb_ctx* ctx, const k3xb_layer* L, const float* hidden_in, const float* block,
+                       const int32_t* parent, uint32_t N, uint32_t S, const uint16_t* conv, const float* rec,
+                       float* hidden_out, uint32_t* ids_out, void* trace) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!L) return fail(ctx, K3XB_INVALID_EXTENT, "null layer");
+    const uint32_t H = L->hidden;
+    int st = validate_kda(ctx, &L->kda, H);
+    if (st) return st;
+    if ((st = validate_layer(ctx, &L->moe))) return st;
+    if (L->moe.hidden != H) return fail(ctx, K3XB_INVALID_EXTENT, "moe.hidden must equal the layer width");
+    if (!L->self_residual_norm || !L->self_residual_proj || !L->input_norm || !L->moe_residual_norm ||
+        !L->moe_residual_proj || !L->post_norm || !(L->rms_eps > 0.0f))
+        return fail(ctx, K3XB_INVALID_EXTENT, "missing layer norms");
+    if (!hidden_in || !block || !parent || !N || !S || !conv || !rec || !hidden_out)
+        return fail(ctx, K3XB_INVALID_EXTENT, "layer arguments");
+    const k3xb_kda_layer& w = L->kda;
+    KdaSchedule sch;
+    if ((st = schedule_tree(ctx, parent, N, sch))) return st;
+    const std::vector<int32_t> tables = kda_tables(parent, N, w.conv_width, sch);
+    const uint32_t T = N * S;
+    const size_t P = static_cast<size_t>(w.heads) * w.head_dim, TH = static_cast<size_t>(T) * H;
+    Sizer sz;
+    if (!trace) layout_trace(sz, T, P, w.heads, nullptr);
+    layout_kda_work(sz, T, H, P, w.head_dim, w.heads, tables.size(), nullptr);
+    for (int i = 0; i < 4; ++i) sz.take<float>(TH);   // xin, kda_out, prefix, moe_in
+    layout_moe(sz, L->moe, T, false, nullptr);
+    sz.used += mxf4_scratch_bytes(L->moe, T);
+    void* base;
+    if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
+    Carver c(base);
+    KdaTrace tr{};
+    if (trace) {
+        Carver t(trace);
+        layout_trace(t, T, P, w.heads, &tr);
+    } else {
+        layout_trace(c, T, P, w.heads, &tr);
+    }
+    KdaWork wk{};
+    layout_kda_work(c, T, H, P, w.head_dim, w.heads, tables.size(), &wk);
+    float* xin = c.take<float>(TH);
+    float* kda_out = c.take<float>(TH);
+    float* prefix = c.take<float>(TH);
+    float* moe_in = c.take<float>(TH);
+    MoeScratch ms{};
+    layout_moe(c, L->moe, T, false, &ms);
+    set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
+    K3XB_CUDA(ctx, cudaMemcpyAsync(wk.tables, tables.data(), tables.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                   ctx->stream));
+    // official_layer.cpp:159-172: attention residual + input norm
+    if ((st = launch_attnres_norm(ctx, hidden_in, nullptr, block, L->self_residual_norm, L->self_residual_proj,
+                                  L->input_norm, T, H, L->rms_eps, nullptr, xin)))
+        return st;
+    if ((st = kda_block_device(ctx, w, H, xin, true, N, S, conv, rec, sch, tr, wk, kda_out))) return st;
+    // :190-205: prefix, MoE input preparation
+    if ((st = launch_attnres_norm(ctx, hidden_in, kda_out, block, L->moe_residual_norm, L->moe_residual_proj,
+                                  L->post_norm, T, H, L->rms_eps, prefix, moe_in)))
+        return st;
+    // plain MoE: combined = round_bf16(routed + shared) into hidden_out, then the residual
+    if ((st = moe_forward_device(ctx, L->moe, moe_in, T, hidden_out, ids_out, nullptr, ms))) return st;
+    return launch_residual(ctx, prefix, hidden_out, TH, hidden_out);
+}
+
+}  // extern "C"

@@ -67,6 +67,26 @@ int make_byte_map(k3xb_ctx* ctx, void* map, const void* base, uint64_t row_bytes
 size_t linear_scratch_bytes(uint32_t T, uint32_t K);
 int launch_linear_bf16(k3xb_ctx* ctx, const float* x, const uint16_t* W, uint32_t T, uint32_t rows, uint32_t K,
                        int round_out, uint16_t* xterms, float* out);
+// the same with the two-term split done once for several weights of one x
+int launch_split_terms(k3xb_ctx* ctx, const float* x, uint32_t T, uint32_t K, uint16_t* xterms);
+int launch_linear_terms(k3xb_ctx* ctx, const uint16_t* xterms, const uint16_t* W, uint32_t T, uint32_t rows,
+                        uint32_t K, int round_out, float* out);
+// layer.cu — KDA block and layer steps around the GEMMs
+size_t attnres_smem_bytes(uint32_t H);
+int launch_attnres_norm(k3xb_ctx* ctx, const float* a, const float* delta, const float* block, const uint16_t* rnorm,
+                        const uint16_t* rproj, const uint16_t* post, uint32_t T, uint32_t H, float eps,
+                        float* prefix_out, float* out);
+int launch_short_conv(k3xb_ctx* ctx, const float* const proj[3], const float* const weight[3], const uint16_t* conv,
+                      const int32_t* anc, uint32_t S, uint32_t N, uint32_t P, uint32_t w, float* const out[3]);
+int launch_qk_gates(k3xb_ctx* ctx, const float* cq, const float* ck, const float* fg, const float* bp,
+                    const float* a_log, const float* dt_bias, float glb, uint32_t T, uint32_t h, uint32_t d,
+                    float* qn, float* kn, float* ld, float* be);
+int launch_gated_norm(k3xb_ctx* ctx, const float* ro, const float* og, const float* o_norm, float eps, uint32_t T,
+                      uint32_t h, uint32_t d, float* gt);
+int launch_residual(k3xb_ctx* ctx, const float* a, const float* b, size_t n, float* out);
+int launch_residual_round(k3xb_ctx* ctx, const float* a, size_t n, float* out);   // out = round_bf16(a)
+int launch_conv_commit(k3xb_ctx* ctx, const float* const proj[3], const uint16_t* conv_in, const int32_t* anc_commit,
+                       uint32_t S, uint32_t N, uint32_t P, uint32_t w, uint16_t* conv_out);
 // shared expert on kind::f16 tensor cores; xb [2T][H], bd [2T][Is] bf16 scratch
 int launch_shared_tc(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T, uint16_t* xb,
                      uint16_t* bd, float* out);

@@ -78,8 +78,8 @@ int make_byte_map(k3xb_ctx* ctx, void* map, const void* base, uint64_t row_bytes
 
 size_t linear_scratch_bytes(uint32_t T, uint32_t K) { return static_cast<size_t>(2) * T * K * 2 + 1024; }
 
-int launch_linear_bf16(k3xb_ctx* ctx, const float* x, const uint16_t* W, uint32_t T, uint32_t rows, uint32_t K,
-                       int round_out, uint16_t* xterms, float* out) {
+int launch_linear_terms(k3xb_ctx* ctx, const uint16_t* xterms, const uint16_t* W, uint32_t T, uint32_t rows,
+                        uint32_t K, int round_out, float* out) {
     if (K % 8) return fail(ctx, K3XB_INVALID_EXTENT, "bf16 linear needs K % 8 == 0");
     int st;
     CUtensorMap map_w, map_x;
@@ -92,14 +92,26 @@ int launch_linear_bf16(k3xb_ctx* ctx, const float* x, const uint16_t* W, uint32_
                                             static_cast<int>(smem)));
         configured = true;
     }
-    const size_t n = static_cast<size_t>(T) * K;
-    split2_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(x, n, K, xterms);
-    K3XB_LAUNCHED(ctx);
     const uint32_t items = ((T + kTok - 1) / kTok) * ((rows + kBlockM - 1) / kBlockM);
     LinParams p{T, rows, K, items, static_cast<uint32_t>(round_out ? 1 : 0), out, ctx->status_word};
     linear_bf16_kernel<<<std::min<uint32_t>(ctx->sm_count, items), kThreads, smem, ctx->stream>>>(map_w, map_x, p);
     K3XB_LAUNCHED(ctx);
     return K3XB_OK;
+}
+
+int launch_split_terms(k3xb_ctx* ctx, const float* x, uint32_t T, uint32_t K, uint16_t* xterms) {
+    const size_t n = static_cast<size_t>(T) * K;
+    split2_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(x, n, K, xterms);
+    K3XB_LAUNCHED(ctx);
+    return K3XB_OK;
+}
+
+int launch_linear_bf16(k3xb_ctx* ctx, const float* x, const uint16_t* W, uint32_t T, uint32_t rows, uint32_t K,
+                       int round_out, uint16_t* xterms, float* out) {
+    if (K % 8) return fail(ctx, K3XB_INVALID_EXTENT, "bf16 linear needs K % 8 == 0");
+    int st = launch_split_terms(ctx, x, T, K, xterms);
+    if (st) return st;
+    return launch_linear_terms(ctx, xterms, W, T, rows, K, round_out, out);
 }
 
 }  // namespace k3xb

@@ -55,6 +55,20 @@ class MoeLayer(C.Structure):
                 ("down_scales_tc", C.c_void_p)]
 
 
+class KdaLayer(C.Structure):
+    _fields_ = [("heads", C.c_uint32), ("head_dim", C.c_uint32), ("conv_width", C.c_uint32),
+                ("eps", C.c_float), ("gate_lower_bound", C.c_float)] + [
+        (n, C.c_void_p) for n in ("q_proj", "k_proj", "v_proj", "q_conv", "k_conv", "v_conv", "f_a_proj",
+                                  "f_b_proj", "a_log", "dt_bias", "b_proj", "g_proj", "o_norm", "o_proj")]
+
+
+class Layer(C.Structure):
+    _fields_ = [("hidden", C.c_uint32), ("rms_eps", C.c_float)] + [
+        (n, C.c_void_p) for n in ("self_residual_norm", "self_residual_proj", "input_norm",
+                                  "moe_residual_norm", "moe_residual_proj", "post_norm")] + [
+        ("kda", KdaLayer), ("moe", MoeLayer)]
+
+
 class Stats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in (
         "kernel_launches", "route_calls", "moe_layer_calls", "moe_layer_experts", "kda_calls",
@@ -94,11 +108,17 @@ def library() -> C.CDLL:
             "k3xb_fill_normal_mxfp4": [vp, vp, vp, sz, sz, u64, u64, f32],
             "k3xb_prepare_mxfp4_scales": [vp, vp, sz, sz, vp],
             "k3xb_linear_bf16": [vp, vp, u32, u32, vp, u32, C.c_int32, vp],
+            "k3xb_kda_block": [vp, C.POINTER(KdaLayer), u32, vp, vp, u32, u32, vp, vp, vp, vp],
+            "k3xb_kda_block_commit": [vp, C.POINTER(KdaLayer), vp, vp, u32, u32, vp, vp, vp, vp, vp],
+            "k3xb_attention_residual_norm": [vp, vp, vp, vp, vp, vp, vp, u32, u32, f32, vp, vp],
+            "k3xb_layer_forward": [vp, C.POINTER(Layer), vp, vp, vp, u32, u32, vp, vp, vp, vp, vp],
         }
         for name, args in sigs.items():
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = C.c_int
+        lib.k3xb_kda_trace_bytes.argtypes = [C.POINTER(KdaLayer), u32, u32]
+        lib.k3xb_kda_trace_bytes.restype = sz
         _lib = lib
     return _lib
 
@@ -204,6 +224,40 @@ class Context:
         self._check(self.lib.k3xb_kda_commit(self.h, _p(state), par, N, S, heads, d, _p(q), _p(k), _p(v),
                                              _p(log_decay), _p(beta), com, _p(state_out)), "kda_commit")
 
+    # ---- full KDA block and the layer ----------------------------------------
+    def kda_trace_bytes(self, kda: "KdaLayer", nodes, sequences):
+        return self.lib.k3xb_kda_trace_bytes(C.byref(kda), nodes, sequences)
+
+    def kda_block(self, kda: "KdaLayer", x, parent, conv, recurrent, out, trace=None):
+        """x/out [S][N][H]; conv [S][3][w-1][P] int16 (bf16 words); recurrent [S][h][d][d]."""
+        S, N, H = x.shape
+        par = (C.c_int32 * N)(*[int(v) for v in parent])
+        self._check(self.lib.k3xb_kda_block(self.h, C.byref(kda), H, _p(x), par, N, S, _p(conv), _p(recurrent),
+                                            _p(out), _p(trace)), "kda_block")
+
+    def kda_block_commit(self, kda: "KdaLayer", trace, parent, sequences, commit_node, conv, recurrent,
+                         conv_out, recurrent_out):
+        N = len(parent)
+        par = (C.c_int32 * N)(*[int(v) for v in parent])
+        com = (C.c_int32 * sequences)(*[int(v) for v in commit_node])
+        self._check(self.lib.k3xb_kda_block_commit(self.h, C.byref(kda), _p(trace), par, N, sequences, com,
+                                                   _p(conv), _p(recurrent), _p(conv_out), _p(recurrent_out)),
+                    "kda_block_commit")
+
+    def attention_residual_norm(self, a, block, norm, proj, post, eps, out, delta=None, prefix_out=None):
+        T, H = a.shape
+        self._check(self.lib.k3xb_attention_residual_norm(self.h, _p(a), _p(delta), _p(block), _p(norm), _p(proj),
+                                                          _p(post), T, H, eps, _p(prefix_out), _p(out)),
+                    "attention_residual_norm")
+
+    def layer_forward(self, layer: "Layer", hidden_in, block, parent, conv, recurrent, hidden_out,
+                      expert_ids=None, trace=None):
+        S, N, H = hidden_in.shape
+        par = (C.c_int32 * N)(*[int(v) for v in parent])
+        self._check(self.lib.k3xb_layer_forward(self.h, C.byref(layer), _p(hidden_in), _p(block), par, N, S,
+                                                _p(conv), _p(recurrent), _p(hidden_out), _p(expert_ids),
+                                                _p(trace)), "layer_forward")
+
     # ---- (e) --------------------------------------------------------------------
     def accept_greedy(self, logits, drafts, accepted, committed, count, targets=None):
         S, P1, V = logits.shape
@@ -275,4 +329,29 @@ def moe_layer_desc(w: dict, engine=ENGINE_SIMT, act_terms=6) -> MoeLayer:
     L.situ_linear_beta = w.get("situ_linear_beta", 0.0)
     L.engine = engine
     L.act_terms = act_terms
+    return L
+
+
+def kda_layer_desc(w: dict) -> KdaLayer:
+    """C descriptor of a KDA block from a dict of torch CUDA tensors + dims."""
+    K = KdaLayer()
+    K.heads, K.head_dim, K.conv_width = w["heads"], w["head_dim"], w["conv_width"]
+    K.eps, K.gate_lower_bound = w["eps"], w["gate_lower_bound"]
+    for name in ("q_proj", "k_proj", "v_proj", "q_conv", "k_conv", "v_conv", "f_a_proj", "f_b_proj", "a_log",
+                 "dt_bias", "b_proj", "g_proj", "o_norm", "o_proj"):
+        setattr(K, name, w[name].data_ptr())
+    return K
+
+
+def layer_desc(w: dict, engine=ENGINE_MXF4, act_terms=6) -> Layer:
+    """C descriptor of a KDA + MoE layer: w["kda"], w["moe"] sub-dicts and
+    the six [H] bf16 norm/projection vectors."""
+    L = Layer()
+    L.hidden = w["hidden"]
+    L.rms_eps = w["rms_eps"]
+    for name in ("self_residual_norm", "self_residual_proj", "input_norm", "moe_residual_norm",
+                 "moe_residual_proj", "post_norm"):
+        setattr(L, name, w[name].data_ptr())
+    L.kda = kda_layer_desc(w["kda"])
+    L.moe = moe_layer_desc(w["moe"], engine=engine, act_terms=act_terms)
     return L

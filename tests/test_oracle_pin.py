@@ -369,3 +369,39 @@ def test_rejection_deterministic(rs):
     a = rs.verify_rejection(tl, dl, d, 1.0, 9, 3)
     b = rs.verify_rejection(tl, dl, d, 1.0, 9, 3)
     assert a == b and 1 <= len(a[1]) <= 4
+
+
+def test_prepare_input_matches_reference(rs, ref):
+    """attention_residual + rms_norm (official_layer.cpp:42-125) composed in
+    the restatement == the reference's prepare_official_moe_input."""
+    g = np.random.default_rng(41)
+    for n in (64, 256, 7168):
+        prefix = bf16_normal(g, n)
+        block = (g.normal(size=n) * 3).astype(np.float32)
+        norm = bf16_words(1 + g.normal(0, 0.1, size=n))
+        proj = bf16_words(g.normal(0, 0.05, size=n))
+        post = bf16_words(1 + g.normal(0, 0.1, size=n))
+        a = rs.prepare_input(prefix, block, norm, proj, post, 1e-6)
+        b = ref.prepare_input(prefix, block, norm, proj, post, 1e-6)
+        np.testing.assert_array_equal(a, b)
+
+
+def test_kda_block_tree_on_a_chain_is_the_block(rs):
+    g = np.random.default_rng(43)
+    H, h, d, W, N = 64, 2, 16, 4, 5
+    w = _kda_weights(g, H, h, d, W)
+    P = h * d
+    conv = tuple(bf16_words(g.normal(0, 0.5, size=(W - 1) * P)) for _ in range(3))
+    rec = g.normal(0, 0.1, size=h * d * d).astype(np.float32)
+    x = g.normal(size=(N, H)).astype(np.float32)
+    want, st = rs.kda_block(w, x, *conv, rec)
+    got = rs.kda_block_tree(w, x, np.arange(-1, N - 1), conv, rec)
+    np.testing.assert_array_equal(got, want)
+    # a branch sees only its own ancestors: node 3 hangs off node 1
+    parent = np.array([-1, 0, 1, 1])
+    tree = rs.kda_block_tree(w, x[:4], parent, conv, rec)
+    alt, _ = rs.kda_block(w, x[[0, 1, 3]], *conv, rec)
+    np.testing.assert_array_equal(tree[3], alt[2])
+    c = rs.kda_block_commit(w, x, np.arange(-1, N - 1), N - 1, conv, rec)
+    for u, v in zip(c, st):
+        np.testing.assert_array_equal(u, v)
