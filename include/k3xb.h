@@ -310,6 +310,58 @@ int k3xb_layer_forward(k3xb_ctx* ctx, const k3xb_layer* layer,
                        const float* recurrent, float* hidden_out,
                        uint32_t* expert_ids, void* kda_trace);
 
+/* ---- the verify step: layer stack + LM head + acceptance + commit -------- */
+/* A stack of KDA + MoE layers with its LM head (model.cpp:376-386,
+ * :456-459, :1174-1176). layer is a HOST array of `layers` descriptors that
+ * share hidden, heads, head_dim and conv_width. embedding [V][H] bf16 may be
+ * NULL (the caller passes embedded hidden states); final_norm [H] bf16 may
+ * be NULL (no final RMSNorm); lm_head [V][H] bf16. */
+typedef struct {
+    uint32_t layers, vocab;
+    const k3xb_layer* layer;
+    const uint16_t* embedding;
+    const uint16_t* final_norm;
+    float final_eps;
+    const uint16_t* lm_head;
+} k3xb_verify_model;
+
+enum { K3XB_ACCEPT_GREEDY = 0, K3XB_ACCEPT_REJECTION = 1 };
+
+/* One call's device arrays. S sequences verify p linear drafts each; node 0
+ * of a sequence is its anchor, node i its draft i. tokens [S][p+1] (anchor
+ * then drafts; with an embedding), hidden_in [S][p+1][H] (without one),
+ * block_source [S][p+1][H] (NULL: the embedded/given input), drafts [S][p].
+ * conv [layers][S][3][w-1][P] and recurrent [layers][S][h][d][d] are the
+ * per-layer KDA states, advanced IN PLACE to the last accepted position
+ * (node accepted[s]). logits [S][p+1][V] (may be NULL) receives the
+ * bf16-rounded LM-head logits. draft_logits [S][p][V], temperature, seed and
+ * sequence_base are read for K3XB_ACCEPT_REJECTION. */
+typedef struct {
+    uint32_t sequences, drafts;
+    const uint32_t* tokens;
+    const float* hidden_in;
+    const float* block_source;
+    const uint32_t* draft_tokens;
+    uint16_t* conv;
+    float* recurrent;
+    int32_t mode;
+    const float* draft_logits;
+    float temperature;
+    uint64_t seed, sequence_base;
+    float* logits;
+    uint32_t* accepted;
+    uint32_t* committed;
+    uint32_t* committed_count;
+} k3xb_verify_io;
+
+/* Engine::forward_expert_major_block + verify_greedy_target_block +
+ * commit (model.cpp:133-420, :1660-1664; speculative.cpp:74-112), or the
+ * seeded rejection rule (no reference counterpart), as one device-side call:
+ * no host synchronisation between the layers, the LM head, the acceptance
+ * and the state commit. */
+int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* model,
+                     const k3xb_verify_io* io);
+
 /* ---- (e) acceptance ------------------------------------------------------- */
 /* verify_greedy_target_block (runtime/src/speculative.cpp:74-112) for S
  * sequences of p drafts: targets = first-max argmax of logits

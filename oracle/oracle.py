@@ -344,7 +344,7 @@ class Restatement:
         _, st = self.kda_block_path(weights, x, self._path(parent, node), conv, recurrent)
         return st
 
-    def layer_forward(self, layer: dict, hidden_in, block, parent, conv, recurrent):
+    def layer_forward(self, layer: dict, hidden_in, block, parent, conv, recurrent, want_xin=False):
         """official_layer_cpu (official_layer.cpp:134-244) with the plain MoE
         (official_moe.cpp:271-344 minus :296, :323-331) for one sequence's
         draft nodes [N][H]. Returns (out, expert ids, moe input)."""
@@ -359,7 +359,30 @@ class Restatement:
                                               layer["moe_residual_proj"], layer["post_norm"], eps)
                            for i in range(N)])
         combined, ids, _ = self.moe_layer(layer["moe"], moe_in)
-        return self.round_bf16(self.round_bf16(prefix) + combined), ids, moe_in
+        out = self.round_bf16(self.round_bf16(prefix) + combined)
+        return (out, ids, moe_in, xin) if want_xin else (out, ids, moe_in)
+
+    def verify_greedy_stack(self, layers, lm_head, final_norm, final_eps, hidden_in, block, drafts, conv, rec):
+        """One sequence's verify step (model.cpp:133-420 layer-major over the
+        anchor + p linear drafts, LM head as bf16_matvec, targets by
+        first-max argmax, speculative.cpp:74-112, then each layer's KDA state
+        committed at node `accepted`). conv/rec: per-layer lists. Returns
+        (logits [p+1][V], targets, accepted, committed, states)."""
+        N = hidden_in.shape[0]
+        parent = np.arange(-1, N - 1)
+        x, xins = hidden_in, []
+        for l, layer in enumerate(layers):
+            x, _, _, xin = self.layer_forward(layer, x, block, parent, conv[l], rec[l], want_xin=True)
+            xins.append(xin)
+        if final_norm is not None:
+            x = np.stack([self.rms_norm(x[i], final_norm, final_eps) for i in range(N)])
+        logits = np.stack([self.bf16_matvec(x[i], lm_head) for i in range(N)])
+        targets = np.array([self.argmax(logits[i]) for i in range(N)], np.uint32)
+        V = lm_head.shape[0]
+        accepted, committed = self.verify_greedy_block(0, drafts, len(drafts), V, targets)[:2]
+        states = [self.kda_block_commit(layer["kda"], xins[l], parent, accepted, conv[l], rec[l])
+                  for l, layer in enumerate(layers)]
+        return logits, targets, accepted, committed, states
 
     def argmax(self, logits):
         logits = _c(logits, np.float32)

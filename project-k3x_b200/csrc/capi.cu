@@ -644,6 +644,77 @@ int kda_block_device(k3xb_ctx* ctx, const k3xb_kda_layer& w, uint32_t H, const f
     return launch_linear_terms(ctx, wk.xt_p, w.o_proj, T, H, P, 1, out);
 }
 
+int validate_full_layer(k3xb_ctx* ctx, const k3xb_layer* L) {
+    if (!L) return fail(ctx, K3XB_INVALID_EXTENT, "null layer");
+    int st = validate_kda(ctx, &L->kda, L->hidden);
+    if (st) return st;
+    if ((st = validate_layer(ctx, &L->moe))) return st;
+    if (L->moe.hidden != L->hidden) return fail(ctx, K3XB_INVALID_EXTENT, "moe.hidden must equal the layer width");
+    if (!L->self_residual_norm || !L->self_residual_proj || !L->input_norm || !L->moe_residual_norm ||
+        !L->moe_residual_proj || !L->post_norm || !(L->rms_eps > 0.0f))
+        return fail(ctx, K3XB_INVALID_EXTENT, "missing layer norms");
+    if (attnres_smem_bytes(L->hidden) > 200 * 1024) return fail(ctx, K3XB_INVALID_EXTENT, "hidden too large");
+    return K3XB_OK;
+}
+
+// Scratch of one layer forward (its region starts at the scratch base).
+template <typename A>
+void layout_layer(A& a, const k3xb_layer& L, uint32_t N, uint32_t S, bool own_trace, KdaTrace* tr, KdaWork* wk,
+                  float** bufs, MoeScratch* ms) {
+    const size_t T = static_cast<size_t>(N) * S, H = L.hidden;
+    const size_t P = static_cast<size_t>(L.kda.heads) * L.kda.head_dim;
+    if (own_trace) layout_trace(a, T, P, L.kda.heads, tr);
+    layout_kda_work(a, T, H, P, L.kda.head_dim, L.kda.heads, 0, wk);
+    for (int i = 0; i < 4; ++i) {   // xin, kda_out, prefix, moe_in
+        float* b = a.template take<float>(T * H);
+        if (bufs) bufs[i] = b;
+    }
+    layout_moe(a, L.moe, static_cast<uint32_t>(T), false, ms);
+}
+
+size_t layer_work_bytes(const k3xb_layer& L, uint32_t N, uint32_t S, bool own_trace) {
+    Sizer sz;
+    layout_layer(sz, L, N, S, own_trace, nullptr, nullptr, nullptr, nullptr);
+    return sz.used + mxf4_scratch_bytes(L.moe, N * S) + 1024;
+}
+
+// official_layer_cpu with the plain MoE; d_tables = device anc table +
+// recurrence schedule for `sch`.
+int layer_forward_impl(k3xb_ctx* ctx, const k3xb_layer& L, const float* hidden_in, const float* block, uint32_t N,
+                       uint32_t S, const uint16_t* conv, const float* rec, float* hidden_out, uint32_t* ids_out,
+                       void* trace, const KdaSchedule& sch, const int32_t* d_tables) {
+    const uint32_t T = N * S, H = L.hidden;
+    const size_t P = static_cast<size_t>(L.kda.heads) * L.kda.head_dim;
+    void* base;
+    int st = ensure_scratch(ctx, layer_work_bytes(L, N, S, trace == nullptr), &base);
+    if (st) return st;
+    Carver c(base);
+    KdaTrace tr{};
+    KdaWork wk{};
+    float* bufs[4];
+    MoeScratch ms{};
+    layout_layer(c, L, N, S, trace == nullptr, &tr, &wk, bufs, &ms);
+    if (trace) {
+        Carver t(trace);
+        layout_trace(t, T, P, L.kda.heads, &tr);
+    }
+    set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
+    wk.tables = const_cast<int32_t*>(d_tables);
+    float *xin = bufs[0], *kda_out = bufs[1], *prefix = bufs[2], *moe_in = bufs[3];
+    // official_layer.cpp:159-172: attention residual + input norm
+    if ((st = launch_attnres_norm(ctx, hidden_in, nullptr, block, L.self_residual_norm, L.self_residual_proj,
+                                  L.input_norm, T, H, L.rms_eps, nullptr, xin)))
+        return st;
+    if ((st = kda_block_device(ctx, L.kda, H, xin, true, N, S, conv, rec, sch, tr, wk, kda_out))) return st;
+    // :190-205: prefix, MoE input preparation
+    if ((st = launch_attnres_norm(ctx, hidden_in, kda_out, block, L.moe_residual_norm, L.moe_residual_proj,
+                                  L.post_norm, T, H, L.rms_eps, prefix, moe_in)))
+        return st;
+    // plain MoE: combined = round_bf16(routed + shared), then the residual (official_moe.cpp:336-341)
+    if ((st = moe_forward_device(ctx, L.moe, moe_in, T, hidden_out, ids_out, nullptr, ms))) return st;
+    return launch_residual(ctx, prefix, hidden_out, static_cast<size_t>(T) * H, hidden_out);
+}
+
 // anc table + schedule packed for one upload
 std::vector<int32_t> kda_tables(const int32_t* parent, uint32_t N, uint32_t cw, const KdaSchedule& sch) {
     std::vector<int32_t> t(static_cast<size_t>(N) * (cw - 1));
@@ -755,62 +826,129 @@ int k3xb_layer_forward(k3xb_ctx* ctx, const k3xb_layer* L, const float* hidden_i
                        const int32_t* parent, uint32_t N, uint32_t S, const uint16_t* conv, const float* rec,
                        float* hidden_out, uint32_t* ids_out, void* trace) {
     if (!ctx) return K3XB_INVALID_EXTENT;
-    if (!L) return fail(ctx, K3XB_INVALID_EXTENT, "null layer");
-    const uint32_t H = L->hidden;
-    int st = validate_kda(ctx, &L->kda, H);
+    int st = validate_full_layer(ctx, L);
     if (st) return st;
-    if ((st = validate_layer(ctx, &L->moe))) return st;
-    if (L->moe.hidden != H) return fail(ctx, K3XB_INVALID_EXTENT, "moe.hidden must equal the layer width");
-    if (!L->self_residual_norm || !L->self_residual_proj || !L->input_norm || !L->moe_residual_norm ||
-        !L->moe_residual_proj || !L->post_norm || !(L->rms_eps > 0.0f))
-        return fail(ctx, K3XB_INVALID_EXTENT, "missing layer norms");
     if (!hidden_in || !block || !parent || !N || !S || !conv || !rec || !hidden_out)
         return fail(ctx, K3XB_INVALID_EXTENT, "layer arguments");
-    const k3xb_kda_layer& w = L->kda;
     KdaSchedule sch;
     if ((st = schedule_tree(ctx, parent, N, sch))) return st;
-    const std::vector<int32_t> tables = kda_tables(parent, N, w.conv_width, sch);
-    const uint32_t T = N * S;
-    const size_t P = static_cast<size_t>(w.heads) * w.head_dim, TH = static_cast<size_t>(T) * H;
+    const std::vector<int32_t> tables = kda_tables(parent, N, L->kda.conv_width, sch);
+    // the layer's own region first, the topology tables after it
+    const size_t own = layer_work_bytes(*L, N, S, trace == nullptr);
+    void* base;
+    if ((st = ensure_scratch(ctx, own + tables.size() * sizeof(int32_t) + 256, &base))) return st;
+    int32_t* d_tables = reinterpret_cast<int32_t*>((reinterpret_cast<uintptr_t>(base) + own + 255) & ~uintptr_t(255));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(d_tables, tables.data(), tables.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                   ctx->stream));
+    return layer_forward_impl(ctx, *L, hidden_in, block, N, S, conv, rec, hidden_out, ids_out, trace, sch, d_tables);
+}
+
+int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verify_io* io) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!m || !io || !m->layers || !m->layer || !m->vocab || !m->lm_head)
+        return fail(ctx, K3XB_INVALID_EXTENT, "verify model");
+    int st;
+    const k3xb_layer& L0 = m->layer[0];
+    for (uint32_t l = 0; l < m->layers; ++l) {
+        if ((st = validate_full_layer(ctx, &m->layer[l]))) return st;
+        const k3xb_layer& L = m->layer[l];
+        if (L.hidden != L0.hidden || L.kda.heads != L0.kda.heads || L.kda.head_dim != L0.kda.head_dim ||
+            L.kda.conv_width != L0.kda.conv_width)
+            return fail(ctx, K3XB_INVALID_EXTENT, "verify layers must share hidden, heads, head_dim, conv_width");
+    }
+    const uint32_t S = io->sequences, p = io->drafts, N = p + 1, T = S * N, H = L0.hidden, V = m->vocab;
+    if (!S || !io->conv || !io->recurrent || !io->accepted || !io->committed || !io->committed_count ||
+        (p && !io->draft_tokens))
+        return fail(ctx, K3XB_INVALID_EXTENT, "verify io");
+    if (m->embedding ? !io->tokens : !io->hidden_in) return fail(ctx, K3XB_INVALID_EXTENT, "verify inputs");
+    if (io->mode != K3XB_ACCEPT_GREEDY && io->mode != K3XB_ACCEPT_REJECTION)
+        return fail(ctx, K3XB_INVALID_EXTENT, "acceptance mode");
+    if (io->mode == K3XB_ACCEPT_REJECTION && ((p && !io->draft_logits) || !(io->temperature > 0.0f)))
+        return fail(ctx, K3XB_INVALID_EXTENT, "rejection sampling needs draft logits and temperature > 0");
+    if (H % 8) return fail(ctx, K3XB_INVALID_EXTENT, "LM head needs hidden % 8 == 0");
+    std::vector<int32_t> parent(N);
+    for (uint32_t i = 0; i < N; ++i) parent[i] = static_cast<int32_t>(i) - 1;
+    KdaSchedule sch;
+    if ((st = schedule_tree(ctx, parent.data(), N, sch))) return st;
+    const uint32_t cw = L0.kda.conv_width, h = L0.kda.heads, d = L0.kda.head_dim, P = h * d;
+    const std::vector<int32_t> tables = kda_tables(parent.data(), N, cw, sch);
+    size_t own = 0;
+    for (uint32_t l = 0; l < m->layers; ++l) own = std::max(own, layer_work_bytes(m->layer[l], N, S, false));
+    const size_t TH = static_cast<size_t>(T) * H, trace_bytes = k3xb_kda_trace_bytes(&L0.kda, N, S);
     Sizer sz;
-    if (!trace) layout_trace(sz, T, P, w.heads, nullptr);
-    layout_kda_work(sz, T, H, P, w.head_dim, w.heads, tables.size(), nullptr);
-    for (int i = 0; i < 4; ++i) sz.take<float>(TH);   // xin, kda_out, prefix, moe_in
-    layout_moe(sz, L->moe, T, false, nullptr);
-    sz.used += mxf4_scratch_bytes(L->moe, T);
+    sz.take<uint8_t>(own);
+    sz.take<int32_t>(tables.size());
+    for (uint32_t l = 0; l < m->layers; ++l) sz.take<uint8_t>(trace_bytes, 1024);
+    for (int i = 0; i < 3; ++i) sz.take<float>(TH);   // x0, ping, pong
+    sz.take<uint16_t>(2 * TH, 1024);                   // LM-head operand terms
+    if (!io->logits) sz.take<float>(static_cast<size_t>(T) * V);
+    sz.take<uint32_t>(T);                              // greedy targets
+    sz.take<double>(2 * static_cast<size_t>(T));       // rejection sums
     void* base;
     if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
     Carver c(base);
-    KdaTrace tr{};
-    if (trace) {
-        Carver t(trace);
-        layout_trace(t, T, P, w.heads, &tr);
-    } else {
-        layout_trace(c, T, P, w.heads, &tr);
-    }
-    KdaWork wk{};
-    layout_kda_work(c, T, H, P, w.head_dim, w.heads, tables.size(), &wk);
-    float* xin = c.take<float>(TH);
-    float* kda_out = c.take<float>(TH);
-    float* prefix = c.take<float>(TH);
-    float* moe_in = c.take<float>(TH);
-    MoeScratch ms{};
-    layout_moe(c, L->moe, T, false, &ms);
-    set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
-    K3XB_CUDA(ctx, cudaMemcpyAsync(wk.tables, tables.data(), tables.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+    c.take<uint8_t>(own);
+    int32_t* d_tables = c.take<int32_t>(tables.size());
+    std::vector<void*> traces(m->layers);
+    for (uint32_t l = 0; l < m->layers; ++l) traces[l] = c.take<uint8_t>(trace_bytes, 1024);
+    float* x0 = c.take<float>(TH);
+    float* buf[2] = {c.take<float>(TH), c.take<float>(TH)};
+    uint16_t* xt = c.take<uint16_t>(2 * TH, 1024);
+    float* logits = io->logits ? io->logits : c.take<float>(static_cast<size_t>(T) * V);
+    uint32_t* targets = c.take<uint32_t>(T);
+    double* pd = c.take<double>(T);
+    double* qd = c.take<double>(T);
+    K3XB_CUDA(ctx, cudaMemcpyAsync(d_tables, tables.data(), tables.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
                                    ctx->stream));
-    // official_layer.cpp:159-172: attention residual + input norm
-    if ((st = launch_attnres_norm(ctx, hidden_in, nullptr, block, L->self_residual_norm, L->self_residual_proj,
-                                  L->input_norm, T, H, L->rms_eps, nullptr, xin)))
-        return st;
-    if ((st = kda_block_device(ctx, w, H, xin, true, N, S, conv, rec, sch, tr, wk, kda_out))) return st;
-    // :190-205: prefix, MoE input preparation
-    if ((st = launch_attnres_norm(ctx, hidden_in, kda_out, block, L->moe_residual_norm, L->moe_residual_proj,
-                                  L->post_norm, T, H, L->rms_eps, prefix, moe_in)))
-        return st;
-    // plain MoE: combined = round_bf16(routed + shared) into hidden_out, then the residual
-    if ((st = moe_forward_device(ctx, L->moe, moe_in, T, hidden_out, ids_out, nullptr, ms))) return st;
-    return launch_residual(ctx, prefix, hidden_out, TH, hidden_out);
+    const float* x = io->hidden_in;
+    if (m->embedding) {
+        if ((st = launch_embed(ctx, io->tokens, m->embedding, V, T, H, x0))) return st;
+        x = x0;
+    }
+    const float* block = io->block_source ? io->block_source : x;
+    const size_t conv_stride = static_cast<size_t>(S) * 3 * (cw - 1) * P;
+    const size_t rec_stride = static_cast<size_t>(S) * h * d * d;
+    for (uint32_t l = 0; l < m->layers; ++l) {
+        float* out = buf[l & 1u];
+        if ((st = layer_forward_impl(ctx, m->layer[l], x, block, N, S, io->conv + l * conv_stride,
+                                     io->recurrent + l * rec_stride, out, nullptr, traces[l], sch, d_tables)))
+            return st;
+        x = out;
+    }
+    if (m->final_norm) {
+        float* y = buf[m->layers & 1u];
+        if ((st = launch_rms_norm(ctx, x, m->final_norm, T, H, m->final_eps, y))) return st;
+        x = y;
+    }
+    // LM head: bf16 matvec semantics (official_moe.cpp:39-59), logits rounded to bf16
+    if ((st = launch_split_terms(ctx, x, T, H, xt))) return st;
+    if ((st = launch_linear_terms(ctx, xt, m->lm_head, T, V, H, 1, logits))) return st;
+    if (io->mode == K3XB_ACCEPT_GREEDY) {
+        st = launch_accept_greedy(ctx, logits, io->draft_tokens, S, p, V, targets, io->accepted, io->committed,
+                                  io->committed_count);
+    } else {
+        st = launch_accept_rejection(ctx, logits, io->draft_logits, io->draft_tokens, S, p, V, io->temperature,
+                                     io->seed, io->sequence_base, pd, qd, io->accepted, io->committed,
+                                     io->committed_count);
+    }
+    if (st) return st;
+    ++ctx->stats.accept_calls;
+    // commit every layer at node accepted[s] (model.cpp:1660-1664), on the device
+    const int32_t* sched = d_tables + static_cast<size_t>(N) * (cw - 1);
+    for (uint32_t l = 0; l < m->layers; ++l) {
+        KdaTrace tr{};
+        Carver t(traces[l]);
+        layout_trace(t, T, P, h, &tr);
+        const float* proj[3] = {tr.pq, tr.pk, tr.pv};
+        uint16_t* conv = io->conv + l * conv_stride;
+        float* rec = io->recurrent + l * rec_stride;
+        if ((st = launch_conv_commit_linear(ctx, proj, conv, io->accepted, S, N, P, cw, conv))) return st;
+        // in place: each warp reads its state rows before it writes them
+        if ((st = launch_kda(ctx, rec, sched, sched + N, sched + 2 * N, N, N, S, h, d, tr.qn, tr.kn, tr.cv, tr.ld,
+                             tr.be, nullptr, rec, sch.levels, reinterpret_cast<const int32_t*>(io->accepted))))
+            return st;
+    }
+    return K3XB_OK;
 }
 
 }  // extern "C"

@@ -14,7 +14,9 @@
 // otherwise the parent's state is reloaded from a per-warp shared-memory
 // stack indexed by depth (the prefix state is depth 0). Linear drafts never
 // touch the stack. Commit mode replays a root..node path and writes that
-// node's state, bit-identical to what the tree pass computed for it.
+// node's state, bit-identical to what the tree pass computed for it; with a
+// device commit array the pass writes the state after commit[s] instead
+// (linear drafts committed from device-side acceptance).
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -31,7 +33,7 @@ __global__ void __launch_bounds__(128) kda_tree_kernel(
     uint32_t nodes, uint32_t heads, const float* __restrict__ q, const float* __restrict__ k,
     const float* __restrict__ v, const float* __restrict__ log_decay,
     const float* __restrict__ beta, float* __restrict__ out, float* __restrict__ state_out,
-    uint32_t levels) {
+    uint32_t levels, const int32_t* __restrict__ commit) {
     constexpr int D = 32 * KPL;
     extern __shared__ float stack[];   // [warps][levels][kRows][D]; level 0 = prefix
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -44,6 +46,17 @@ __global__ void __launch_bounds__(128) kda_tree_kernel(
 
     float st[kRows][KPL];
     const float* src = state + static_cast<size_t>(s) * heads * D * D + static_cast<size_t>(h) * D * D;
+    float* dst = state_out ? state_out + static_cast<size_t>(s) * heads * D * D + static_cast<size_t>(h) * D * D
+                           : nullptr;
+    // commit (device array, per sequence): state_out receives the state after
+    // node commit[s] (the prefix state for -1) instead of after the last node
+    const int32_t keep = commit ? commit[s] : INT32_MIN;
+    auto save = [&]() {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r)
+#pragma unroll
+            for (int i = 0; i < KPL; ++i) dst[static_cast<size_t>(v0 + r) * D + lane * KPL + i] = st[r][i];
+    };
 #pragma unroll
     for (int r = 0; r < kRows; ++r)
 #pragma unroll
@@ -51,6 +64,7 @@ __global__ void __launch_bounds__(128) kda_tree_kernel(
             st[r][i] = src[static_cast<size_t>(v0 + r) * D + lane * KPL + i];
             if (levels) my_stack[r * D + lane * KPL + i] = st[r][i];
         }
+    if (dst && keep == -1) save();
 
     for (uint32_t it = 0; it < visit; ++it) {
         const int32_t n = order[it];
@@ -94,14 +108,9 @@ __global__ void __launch_bounds__(128) kda_tree_kernel(
                 for (int i = 0; i < KPL; ++i)
                     my_stack[(static_cast<size_t>(dn) * kRows + r) * D + lane * KPL + i] = st[r][i];
         }
+        if (dst && n == keep) save();
     }
-    if (state_out) {
-        float* dst = state_out + static_cast<size_t>(s) * heads * D * D + static_cast<size_t>(h) * D * D;
-#pragma unroll
-        for (int r = 0; r < kRows; ++r)
-#pragma unroll
-            for (int i = 0; i < KPL; ++i) dst[static_cast<size_t>(v0 + r) * D + lane * KPL + i] = st[r][i];
-    }
+    if (dst && !commit) save();
 }
 
 }  // namespace
@@ -110,7 +119,7 @@ int launch_kda(k3xb_ctx* ctx, const float* state, const int32_t* order, const in
                const int32_t* from_stack, uint32_t visit, uint32_t nodes, uint32_t sequences,
                uint32_t heads, uint32_t head_dim, const float* q, const float* k, const float* v,
                const float* log_decay, const float* beta, float* out, float* state_out,
-               uint32_t levels) {
+               uint32_t levels, const int32_t* commit) {
     const uint32_t warps = 4;
     const size_t smem = static_cast<size_t>(warps) * levels * kRows * head_dim * sizeof(float);
     if (smem > 200 * 1024) return fail(ctx, K3XB_INVALID_EXTENT, "KDA draft tree too deep for the state stack");
@@ -123,7 +132,7 @@ int launch_kda(k3xb_ctx* ctx, const float* state, const int32_t* order, const in
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); \
         kda_tree_kernel<KPL><<<grid, 32 * warps, smem, ctx->stream>>>(                          \
             state, order, depth, from_stack, visit, nodes, heads, q, k, v, log_decay, beta, out, \
-            state_out, levels);                                                            \
+            state_out, levels, commit);                                                    \
         break;
         K3XB_KDA_CASE(1)
         K3XB_KDA_CASE(2)

@@ -30,7 +30,7 @@ int launch_kda(k3xb_ctx* ctx, const float* state, const int32_t* order, const in
                const int32_t* from_stack, uint32_t visit, uint32_t nodes, uint32_t sequences,
                uint32_t heads, uint32_t head_dim, const float* q, const float* k, const float* v,
                const float* log_decay, const float* beta, float* out, float* state_out,
-               uint32_t levels);
+               uint32_t levels, const int32_t* commit = nullptr);
 
 // accept.cu
 int launch_accept_greedy(k3xb_ctx* ctx, const float* logits, const uint32_t* drafts, uint32_t S,
@@ -87,6 +87,12 @@ int launch_residual(k3xb_ctx* ctx, const float* a, const float* b, size_t n, flo
 int launch_residual_round(k3xb_ctx* ctx, const float* a, size_t n, float* out);   // out = round_bf16(a)
 int launch_conv_commit(k3xb_ctx* ctx, const float* const proj[3], const uint16_t* conv_in, const int32_t* anc_commit,
                        uint32_t S, uint32_t N, uint32_t P, uint32_t w, uint16_t* conv_out);
+int launch_conv_commit_linear(k3xb_ctx* ctx, const float* const proj[3], const uint16_t* conv_in,
+                              const uint32_t* commit, uint32_t S, uint32_t N, uint32_t P, uint32_t w,
+                              uint16_t* conv_out);
+int launch_rms_norm(k3xb_ctx* ctx, const float* x, const uint16_t* w, uint32_t T, uint32_t H, float eps, float* out);
+int launch_embed(k3xb_ctx* ctx, const uint32_t* tokens, const uint16_t* table, uint32_t V, uint32_t T, uint32_t H,
+                 float* out);
 // shared expert on kind::f16 tensor cores; xb [2T][H], bd [2T][Is] bf16 scratch
 int launch_shared_tc(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T, uint16_t* xb,
                      uint16_t* bd, float* out);

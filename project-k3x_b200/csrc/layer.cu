@@ -222,7 +222,85 @@ __global__ void conv_commit_kernel(ConvArgs args, const uint16_t* __restrict__ c
     }
 }
 
+// rms_norm (official_layer.cpp:104-125): one CTA per row.
+__global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__ x, const uint16_t* __restrict__ w,
+                                                       uint32_t H, float eps, float* __restrict__ out) {
+    __shared__ double red[32];
+    const size_t row = blockIdx.x;
+    const float* px = x + row * H;
+    double sq = 0.0;
+    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x)
+        sq = fma(static_cast<double>(px[i]), static_cast<double>(px[i]), sq);
+    sq = block_sum_d(sq, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(sq / H), eps)));
+    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x)
+        out[row * H + i] = round_bf16(__fmul_rn(__fmul_rn(px[i], inv), decode_bf16(w[i])));
+}
+
+// Embedding rows of token ids (bf16 table [V][H]); an id >= V zeroes the
+// row and sets the status word.
+__global__ void embed_kernel(const uint32_t* __restrict__ tokens, const uint16_t* __restrict__ table, uint32_t V,
+                             uint32_t H, size_t n, float* __restrict__ out, int* status) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint32_t tok = tokens[i / H];
+    if (tok >= V) {
+        out[i] = 0.0f;
+        if (status) atomicExch(status, K3XB_INVALID_EXTENT);
+        return;
+    }
+    out[i] = decode_bf16(table[static_cast<size_t>(tok) * H + i % H]);
+}
+
+// Conv histories after a device-chosen node of a LINEAR draft (node c =
+// commit[s]): row r is node c - (w-2-r) when >= 0, else input history row
+// w-1-j+c for j = w-2-r steps back.
+__global__ void conv_commit_linear_kernel(ConvArgs args, const uint16_t* __restrict__ conv_in,
+                                          const uint32_t* __restrict__ commit, uint32_t S, uint32_t N, uint32_t P,
+                                          uint32_t w, uint16_t* __restrict__ conv_out) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<size_t>(S) * 3 * P) return;
+    const uint32_t c = static_cast<uint32_t>(i % P);
+    const uint32_t type = static_cast<uint32_t>((i / P) % 3), s = static_cast<uint32_t>(i / P / 3);
+    const int32_t node = static_cast<int32_t>(min(commit[s], N - 1));
+    const uint16_t* hin = conv_in + (static_cast<size_t>(s) * 3 + type) * (w - 1) * P;
+    uint16_t* hout = conv_out + (static_cast<size_t>(s) * 3 + type) * (w - 1) * P;
+    for (uint32_t r = 0; r + 1 < w; ++r) {   // increasing rows: in-place safe
+        const int32_t j = static_cast<int32_t>(w) - 2 - static_cast<int32_t>(r);
+        const int32_t a = node - j;
+        hout[static_cast<size_t>(r) * P + c] =
+            a >= 0 ? encode_bf16(args.proj[type][(static_cast<size_t>(s) * N + a) * P + c])
+                   : hin[static_cast<size_t>(static_cast<int32_t>(w) - 1 - j + node) * P + c];
+    }
+}
+
 }  // namespace
+
+int launch_rms_norm(k3xb_ctx* ctx, const float* x, const uint16_t* w, uint32_t T, uint32_t H, float eps, float* out) {
+    rms_norm_kernel<<<T, 256, 0, ctx->stream>>>(x, w, H, eps, out);
+    K3XB_LAUNCHED(ctx);
+    return K3XB_OK;
+}
+
+int launch_embed(k3xb_ctx* ctx, const uint32_t* tokens, const uint16_t* table, uint32_t V, uint32_t T, uint32_t H,
+                 float* out) {
+    const size_t n = static_cast<size_t>(T) * H;
+    embed_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(tokens, table, V, H, n, out,
+                                                                                  ctx->status_word);
+    K3XB_LAUNCHED(ctx);
+    return K3XB_OK;
+}
+
+int launch_conv_commit_linear(k3xb_ctx* ctx, const float* const proj[3], const uint16_t* conv_in,
+                              const uint32_t* commit, uint32_t S, uint32_t N, uint32_t P, uint32_t w,
+                              uint16_t* conv_out) {
+    ConvArgs args{{proj[0], proj[1], proj[2]}, {nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr}};
+    const size_t n = static_cast<size_t>(S) * 3 * P;
+    conv_commit_linear_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(args, conv_in, commit,
+                                                                                               S, N, P, w, conv_out);
+    K3XB_LAUNCHED(ctx);
+    return K3XB_OK;
+}
 
 size_t attnres_smem_bytes(uint32_t H) { return 2ull * H * sizeof(float); }
 

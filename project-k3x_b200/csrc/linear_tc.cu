@@ -36,8 +36,12 @@ __global__ void split2_kernel(const float* __restrict__ x, size_t n, uint32_t K,
     out[(2 * t + 1) * K + k] = static_cast<uint16_t>(__float_as_uint(lo) >> 16);
 }
 
-__device__ __forceinline__ uint4 lin_desc(uint32_t item, uint32_t mtc, uint32_t T) {
-    const uint32_t tile = item / mtc, mt = item % mtc;
+// Weight-tile-major item order: the token tiles of one 128-row weight tile
+// are consecutive items, run by neighbouring CTAs at about the same time, so
+// the weight tile comes from HBM once and from L2 for the other token tiles.
+__device__ __forceinline__ uint4 lin_desc(uint32_t item, uint32_t T) {
+    const uint32_t tiles = (T + kTok - 1) / kTok;
+    const uint32_t tile = item % tiles, mt = item / tiles;
     const uint32_t ntok = min(kTok, T - tile * kTok);
     return make_uint4(mt * kBlockM, tile * 2 * kTok, ((2 * ntok + 15) / 16 * 16) | (ntok << 16), tile * kTok);
 }
@@ -47,8 +51,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_bf16_kernel(const __grid_c
                                                                    const LinParams p) {
     extern __shared__ uint8_t smem_raw[];
     auto& sm = tcp::smem_from<kStages, 1>(smem_raw);
-    const uint32_t mtc = (p.rows + kBlockM - 1) / kBlockM;
-    auto get_desc = [&](uint32_t item) { return lin_desc(item, mtc, p.T); };
+    auto get_desc = [&](uint32_t item) { return lin_desc(item, p.T); };
     auto epilogue = [&](const uint4& d, uint32_t tmem, uint32_t q, uint32_t lane) {
         const uint32_t used = 2 * tcp::desc_ntok(d);
         const uint32_t lane_base = (32u * q) << 16;

@@ -69,6 +69,20 @@ class Layer(C.Structure):
         ("kda", KdaLayer), ("moe", MoeLayer)]
 
 
+class VerifyModel(C.Structure):
+    _fields_ = [("layers", C.c_uint32), ("vocab", C.c_uint32), ("layer", C.POINTER(Layer)),
+                ("embedding", C.c_void_p), ("final_norm", C.c_void_p), ("final_eps", C.c_float),
+                ("lm_head", C.c_void_p)]
+
+
+class VerifyIO(C.Structure):
+    _fields_ = [("sequences", C.c_uint32), ("drafts", C.c_uint32)] + [
+        (n, C.c_void_p) for n in ("tokens", "hidden_in", "block_source", "draft_tokens", "conv", "recurrent")] + [
+        ("mode", C.c_int32), ("draft_logits", C.c_void_p), ("temperature", C.c_float),
+        ("seed", C.c_uint64), ("sequence_base", C.c_uint64)] + [
+        (n, C.c_void_p) for n in ("logits", "accepted", "committed", "committed_count")]
+
+
 class Stats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in (
         "kernel_launches", "route_calls", "moe_layer_calls", "moe_layer_experts", "kda_calls",
@@ -112,6 +126,7 @@ def library() -> C.CDLL:
             "k3xb_kda_block_commit": [vp, C.POINTER(KdaLayer), vp, vp, u32, u32, vp, vp, vp, vp, vp],
             "k3xb_attention_residual_norm": [vp, vp, vp, vp, vp, vp, vp, u32, u32, f32, vp, vp],
             "k3xb_layer_forward": [vp, C.POINTER(Layer), vp, vp, vp, u32, u32, vp, vp, vp, vp, vp],
+            "k3xb_verify_step": [vp, C.POINTER(VerifyModel), C.POINTER(VerifyIO)],
         }
         for name, args in sigs.items():
             fn = getattr(lib, name)
@@ -258,6 +273,9 @@ class Context:
                                                 _p(conv), _p(recurrent), _p(hidden_out), _p(expert_ids),
                                                 _p(trace)), "layer_forward")
 
+    def verify_step(self, model: "VerifyModel", io: "VerifyIO"):
+        self._check(self.lib.k3xb_verify_step(self.h, C.byref(model), C.byref(io)), "verify_step")
+
     # ---- (e) --------------------------------------------------------------------
     def accept_greedy(self, logits, drafts, accepted, committed, count, targets=None):
         S, P1, V = logits.shape
@@ -355,3 +373,37 @@ def layer_desc(w: dict, engine=ENGINE_MXF4, act_terms=6) -> Layer:
     L.kda = kda_layer_desc(w["kda"])
     L.moe = moe_layer_desc(w["moe"], engine=engine, act_terms=act_terms)
     return L
+
+
+ACCEPT_GREEDY = 0
+ACCEPT_REJECTION = 1
+
+
+def verify_model_desc(layers, vocab, lm_head, embedding=None, final_norm=None, final_eps=1e-6):
+    """C descriptor of a verify stack; `layers` is a list of Layer
+    descriptors (kept alive by the returned object)."""
+    arr = (Layer * len(layers))(*layers)
+    m = VerifyModel()
+    m.layers, m.vocab = len(layers), vocab
+    m.layer = C.cast(arr, C.POINTER(Layer))
+    m.embedding = None if embedding is None else embedding.data_ptr()
+    m.final_norm = None if final_norm is None else final_norm.data_ptr()
+    m.final_eps = final_eps
+    m.lm_head = lm_head.data_ptr()
+    m._keep = arr
+    return m
+
+
+def verify_io_desc(sequences, drafts, conv, recurrent, accepted, committed, committed_count, draft_tokens,
+                   tokens=None, hidden_in=None, block_source=None, logits=None, mode=ACCEPT_GREEDY,
+                   draft_logits=None, temperature=1.0, seed=0, sequence_base=0):
+    io = VerifyIO()
+    io.sequences, io.drafts = sequences, drafts
+    ptr = lambda t: None if t is None else t.data_ptr()
+    io.tokens, io.hidden_in, io.block_source = ptr(tokens), ptr(hidden_in), ptr(block_source)
+    io.draft_tokens, io.conv, io.recurrent = ptr(draft_tokens), ptr(conv), ptr(recurrent)
+    io.mode, io.draft_logits, io.temperature = mode, ptr(draft_logits), temperature
+    io.seed, io.sequence_base = seed, sequence_base
+    io.logits, io.accepted, io.committed = ptr(logits), ptr(accepted), ptr(committed)
+    io.committed_count = ptr(committed_count)
+    return io

@@ -194,3 +194,84 @@ def test_layer_forward_c1_vs_oracle(torch, ctx, rs):
         agree += same.sum()
         assert_mostly_close(got[s][same], want[same], what=f"layer output, sequence {s}")
     assert agree >= 0.9 * S * N, f"expert ids agree on {agree}/{S * N} tokens"
+
+
+def _layer_dev(torch, layer):
+    dl = dict(layer)
+    dl["kda"] = _kda_dev(torch, layer["kda"])
+    dl["moe"] = layer_to_dev(torch, layer["moe"])
+    for k in ("self_residual_norm", "self_residual_proj", "input_norm", "moe_residual_norm", "moe_residual_proj",
+              "post_norm"):
+        dl[k] = to_dev(torch, layer[k])
+    return dl
+
+
+def test_verify_step_c1_vs_oracle(torch, ctx, rs):
+    """BASELINE configs[0] shapes end to end: embedding, 2 KDA+MoE layers,
+    final norm, V 1024 LM head, greedy acceptance, device-side commit.
+    Sequence 0's first two drafts are the oracle's own greedy continuation,
+    so acceptance is exercised past the first draft."""
+    import k3xb
+    c = C1
+    L, S, p, V, H = 2, 2, 4, 1024, c["hidden"]
+    N, P = p + 1, c["heads"] * c["head_dim"]
+    layers = [make_layer(rs, 10 + l, H, c["heads"], c["head_dim"], c["experts"], c["top_k"], c["inter"],
+                         c["shared_inter"]) for l in range(L)]
+    g = np.random.default_rng(3)
+    emb = bf16_words(g.normal(0, 1.0, size=(V, H)))
+    lm = bf16_words(g.normal(0, 0.02, size=(V, H)))
+    fnorm = bf16_words(np.ones(H, np.float32))
+    states = [_states(g, S, c["heads"], c["head_dim"], 4, P) for _ in range(L)]
+    conv = np.stack([st[0] for st in states])     # [L][S][3][(w-1)P]
+    rec = np.stack([st[1] for st in states])      # [L][S][h][d][d]
+    embf = (emb.astype(np.uint32) << 16).view(np.float32)
+    tokens = g.integers(0, V, size=(S, N)).astype(np.uint32)
+
+    def oracle(s, toks):
+        x = embf[toks]
+        return rs.verify_greedy_stack(layers, lm, fnorm, 1e-6, x, x, toks[1:],
+                                      [tuple(conv[l, s, i] for i in range(3)) for l in range(L)],
+                                      [rec[l, s].ravel() for l in range(L)])
+
+    for i in range(1, 3):   # sequence 0: drafts 1, 2 follow the oracle's targets
+        tokens[0, i] = oracle(0, tokens[0, :i + 1])[1][i - 1]
+    want = [oracle(s, tokens[s]) for s in range(S)]
+
+    dls = [_layer_dev(torch, layer) for layer in layers]
+    emb_d, lm_d, fnorm_d = to_dev(torch, emb), to_dev(torch, lm), to_dev(torch, fnorm)   # kept alive
+    model = k3xb.verify_model_desc([k3xb.layer_desc(d) for d in dls], V, lm_d, embedding=emb_d,
+                                   final_norm=fnorm_d)
+    u32 = lambda *shape: torch.zeros(shape, dtype=torch.int32, device="cuda")
+    conv_d, rec_d = to_dev(torch, conv), to_dev(torch, rec)
+    tok_d = to_dev(torch, tokens.view(np.int32))
+    drafts_d = to_dev(torch, np.ascontiguousarray(tokens[:, 1:]).view(np.int32))
+    logits = torch.empty((S, N, V), dtype=torch.float32, device="cuda")
+    acc, com, cnt = u32(S), u32(S, N), u32(S)
+    io = k3xb.verify_io_desc(S, p, conv_d, rec_d, acc, com, cnt, drafts_d, tokens=tok_d, logits=logits)
+    ctx.verify_step(model, io)
+    ctx.sync()
+    gl = logits.cpu().numpy()
+    ga, gc, gn = acc.cpu().numpy(), com.cpu().numpy().view(np.uint32), cnt.cpu().numpy()
+    gconv, grec = conv_d.cpu().numpy().view(np.uint16), rec_d.cpu().numpy()
+    for s in range(S):
+        wl, wt, wa, wc, wst = want[s]
+        assert_mostly_close(gl[s], wl, what=f"logits, sequence {s}")
+        # acceptance on the GPU's own logits is bit-exact (speculative.cpp:74-112)
+        targets = np.array([rs.argmax(gl[s, i]) for i in range(N)], np.uint32)
+        a, cm, _ = rs.verify_greedy_block(0, tokens[s, 1:], p, V, targets)
+        assert ga[s] == a and gn[s] == len(cm) and gc[s, :len(cm)].tolist() == cm
+        if s == 0:
+            assert ga[s] >= 2 or not np.array_equal(targets[:2], wt[:2])
+        # committed state at the GPU's accepted node vs the oracle's commit there
+        x = embf[tokens[s]]
+        xl, parent = x, np.arange(-1, N - 1)
+        for l in range(L):
+            out, _, _, xin = rs.layer_forward(layers[l], xl, x, parent,
+                                              tuple(conv[l, s, i] for i in range(3)), rec[l, s].ravel(),
+                                              want_xin=True)
+            cq, ck, cv, r = rs.kda_block_commit(layers[l]["kda"], xin, parent, int(ga[s]),
+                                                tuple(conv[l, s, i] for i in range(3)), rec[l, s].ravel())
+            for i, rows in enumerate((cq, ck, cv)):
+                assert_mostly_close(bf16_to_f32(gconv[l, s, i]), bf16_to_f32(rows), what=f"layer {l} conv {i}")
+            assert_mostly_close(grec[l, s].ravel(), r, what=f"layer {l} recurrent state")
+            xl = out
