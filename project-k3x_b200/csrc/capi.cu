@@ -617,15 +617,15 @@ int kda_block_device(k3xb_ctx* ctx, const k3xb_kda_layer& w, uint32_t H, const f
         if ((st = launch_residual_round(ctx, x, static_cast<size_t>(T) * H, wk.xr))) return st;
         xin = wk.xr;
     }
-    if ((st = launch_split_terms(ctx, xin, T, H, wk.xt_h))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_h, w.q_proj, T, P, H, 1, tr.pq))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_h, w.k_proj, T, P, H, 1, tr.pk))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_h, w.v_proj, T, P, H, 1, tr.pv))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_h, w.g_proj, T, P, H, 1, wk.og))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_h, w.f_a_proj, T, d, H, 1, wk.fl))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_h, w.b_proj, T, h, H, 1, wk.bp))) return st;
-    if ((st = launch_split_terms(ctx, wk.fl, T, d, wk.xt_d))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_d, w.f_b_proj, T, P, d, 1, wk.fg))) return st;
+    if ((st = launch_split_terms(ctx, xin, T, H, 1, wk.xt_h))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.q_proj, T, P, H, 1, tr.pq))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.k_proj, T, P, H, 1, tr.pk))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.v_proj, T, P, H, 1, tr.pv))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.g_proj, T, P, H, 1, wk.og))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.f_a_proj, T, d, H, 1, wk.fl))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.b_proj, T, h, H, 1, wk.bp))) return st;
+    if ((st = launch_split_terms(ctx, wk.fl, T, d, 1, wk.xt_d))) return st;
+    if ((st = launch_linear_terms(ctx, wk.xt_d, 1, w.f_b_proj, T, P, d, 1, wk.fg))) return st;
     const float* proj[3] = {tr.pq, tr.pk, tr.pv};
     const float* cwt[3] = {w.q_conv, w.k_conv, w.v_conv};
     float* const co[3] = {wk.cq, wk.ck, tr.cv};
@@ -639,9 +639,9 @@ int kda_block_device(k3xb_ctx* ctx, const k3xb_kda_layer& w, uint32_t H, const f
                          tr.qn, tr.kn, tr.cv, tr.ld, tr.be, wk.ro, nullptr, sch.levels)))
         return st;
     if ((st = launch_gated_norm(ctx, wk.ro, wk.og, w.o_norm, w.eps, T, h, d, wk.gt))) return st;
-    if ((st = launch_split_terms(ctx, wk.gt, T, P, wk.xt_p))) return st;
+    if ((st = launch_split_terms(ctx, wk.gt, T, P, 1, wk.xt_p))) return st;
     ++ctx->stats.kda_calls;
-    return launch_linear_terms(ctx, wk.xt_p, w.o_proj, T, H, P, 1, out);
+    return launch_linear_terms(ctx, wk.xt_p, 1, w.o_proj, T, H, P, 1, out);
 }
 
 int validate_full_layer(k3xb_ctx* ctx, const k3xb_layer* L) {
@@ -921,8 +921,8 @@ int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verif
         x = y;
     }
     // LM head: bf16 matvec semantics (official_moe.cpp:39-59), logits rounded to bf16
-    if ((st = launch_split_terms(ctx, x, T, H, xt))) return st;
-    if ((st = launch_linear_terms(ctx, xt, m->lm_head, T, V, H, 1, logits))) return st;
+    if ((st = launch_split_terms(ctx, x, T, H, 1, xt))) return st;
+    if ((st = launch_linear_terms(ctx, xt, 1, m->lm_head, T, V, H, 1, logits))) return st;
     if (io->mode == K3XB_ACCEPT_GREEDY) {
         st = launch_accept_greedy(ctx, logits, io->draft_tokens, S, p, V, targets, io->accepted, io->committed,
                                   io->committed_count);

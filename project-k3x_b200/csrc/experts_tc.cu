@@ -438,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1) shared_gateup_kernel(const __grid
         }
     };
     const uint8_t* none[2] = {nullptr, nullptr};
-    const tcp::Config cfg{p.H, p.items, 256, kColAccGate, kColAccUp, 0, 0, 0, 0};
+    const tcp::Config cfg{p.H, p.items, 256, kColAccGate, kColAccUp, 0, 0, 0, 0, 0, 2 * kSharedTok};
     tcp::run_pipeline<kStagesGU, 2, true, 1>(sm, &map_gate, &map_up, &map_x, cfg, none, nullptr, p.error, get_desc,
                                              epilogue);
 }
@@ -467,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1) shared_down_kernel(const __grid_c
         }
     };
     const uint8_t* none[1] = {nullptr};
-    const tcp::Config cfg{p.Is, p.items, 256, kColAccGate, kColAccGate, 128, 0, 0, 0};
+    const tcp::Config cfg{p.Is, p.items, 256, kColAccGate, kColAccGate, 128, 0, 0, 0, 0, 2 * kSharedTok};
     tcp::run_pipeline<kStagesD, 1, true, 2>(sm, &map_down, &map_down, &map_b, cfg, none, nullptr, p.error, get_desc,
                                             epilogue);
 }
@@ -690,9 +690,9 @@ int launch_shared_tc(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden
     CUtensorMap map_gate, map_up, map_x, map_down, map_b;
     if ((st = make_map(ctx, &map_gate, L.shared_gate, static_cast<uint64_t>(H) * 2, Is, 128))) return st;
     if ((st = make_map(ctx, &map_up, L.shared_up, static_cast<uint64_t>(H) * 2, Is, 128))) return st;
-    if ((st = make_map(ctx, &map_x, xb, static_cast<uint64_t>(H) * 2, 2ull * T, 16))) return st;
+    if ((st = make_map(ctx, &map_x, xb, static_cast<uint64_t>(H) * 2, 2ull * T, 2 * kSharedTok))) return st;
     if ((st = make_map(ctx, &map_down, L.shared_down, static_cast<uint64_t>(Is) * 2, H, 128))) return st;
-    if ((st = make_map(ctx, &map_b, bd, static_cast<uint64_t>(Is) * 2, 2ull * T, 16))) return st;
+    if ((st = make_map(ctx, &map_b, bd, static_cast<uint64_t>(Is) * 2, 2ull * T, 2 * kSharedTok))) return st;
     TcState* s = state_of(ctx);
     const size_t smem_gu = tcp::smem_bytes<kStagesGU, 2>();
     const size_t smem_d = tcp::smem_bytes<kStagesD, 1>();

@@ -68,9 +68,10 @@ size_t linear_scratch_bytes(uint32_t T, uint32_t K);
 int launch_linear_bf16(k3xb_ctx* ctx, const float* x, const uint16_t* W, uint32_t T, uint32_t rows, uint32_t K,
                        int round_out, uint16_t* xterms, float* out);
 // the same with the two-term split done once for several weights of one x
-int launch_split_terms(k3xb_ctx* ctx, const float* x, uint32_t T, uint32_t K, uint16_t* xterms);
-int launch_linear_terms(k3xb_ctx* ctx, const uint16_t* xterms, const uint16_t* W, uint32_t T, uint32_t rows,
-                        uint32_t K, int round_out, float* out);
+// terms = 1: x is bf16-valued (one row per token); 2: hi/lo split of any float
+int launch_split_terms(k3xb_ctx* ctx, const float* x, uint32_t T, uint32_t K, uint32_t terms, uint16_t* xterms);
+int launch_linear_terms(k3xb_ctx* ctx, const uint16_t* xterms, uint32_t terms, const uint16_t* W, uint32_t T,
+                        uint32_t rows, uint32_t K, int round_out, float* out);
 // layer.cu — KDA block and layer steps around the GEMMs
 size_t attnres_smem_bytes(uint32_t H);
 int launch_attnres_norm(k3xb_ctx* ctx, const float* a, const float* delta, const float* block, const uint16_t* rnorm,
