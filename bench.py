@@ -409,6 +409,99 @@ def run_c3(args, rank, world, local, ctx, stream):
         print(json.dumps(result), flush=True)
 
 
+def run_c2_ep(args, rank, world, local, ctx, stream, cfg):
+    """c2 at N > 1: expert parallelism. Rank r holds experts [r*E/N, ...) and
+    the hidden rows of its 8/N sequences; tokens reach the experts' ranks and
+    come back by NCCL all-to-all (k3xb_ep_moe_layer_forward). Total work is
+    fixed (64 verify tokens): strong scaling."""
+    import torch
+    import torch.distributed as dist
+
+    import k3xb
+    E, T, H, K = cfg["experts"], cfg["tokens"], cfg["hidden"], cfg["top_k"]
+    if T % world or E % world:
+        raise SystemExit(f"c2 expert parallelism needs tokens ({T}) and experts ({E}) divisible by {world}")
+    w, _, hidden = make_c2_layer(ctx, torch, cfg, k3xb.ENGINE_MXF4, args.act_terms)
+    lw = k3xb.ep_local_layer(w, rank, world)
+    desc = k3xb.moe_layer_desc(lw, engine=k3xb.ENGINE_MXF4, act_terms=args.act_terms)
+    Tr = T // world
+    x = hidden[rank * Tr:(rank + 1) * Tr].contiguous()
+    uid = [k3xb.ep_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    ctx.ep_init(uid[0], rank, world)
+    out = torch.empty((Tr, H), dtype=torch.float32, device="cuda")
+    ids = torch.empty((Tr, K), dtype=torch.int32, device="cuda")
+    con = torch.empty((Tr, K), dtype=torch.float32, device="cuda")
+
+    def step():
+        ctx.ep_moe_layer_forward(desc, E, x, out, ids, con)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    all_ids = [torch.empty_like(ids) for _ in range(world)]
+    dist.all_gather(all_ids, ids)
+    unique = int(torch.unique(torch.cat(all_ids)).numel())
+    barrier(world)
+    torch.cuda.synchronize()
+    launches0 = ctx.stats()["kernel_launches"]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = ctx.stats()["kernel_launches"] - launches0
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+    # e2e: pinned host rows in, layer output out, copies inside the timed region
+    x_h = x.cpu().pin_memory()
+    o_h = torch.empty((Tr, H), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        x.copy_(x_h, non_blocking=True)
+        step()
+        o_h.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(s0.elapsed_time(s1) / args.steps, world)
+    hbm, peak_kind = peaks()
+    alg = unique * EXPERT_BYTES + T * H * 6
+    achieved = alg / (ms * 1e-3) / 1e9
+    result = {
+        "metric": METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "mxfp4 weights (e2m1+e8m0) x e2m1-term activations, fp32 accumulate",
+        "data": "synthetic (seeded, generated on the GPU)",
+        "config": {"workload": "c2: single released-shape MoE layer, expert-major verify",
+                   "hidden": H, "experts": E, "top_k": K, "inter": cfg["inter"],
+                   "shared_inter": cfg["shared_inter"], "verify_tokens": T, "sequences_x_drafts": "8x8",
+                   "layers": 1, "engine": "mxf4", "act_terms": args.act_terms,
+                   "parallelism": f"expert parallel x{world} (NCCL all-to-all), {Tr} tokens per rank",
+                   "l2": "no flush: each step streams ~8.4 GB of expert weights (>> 126 MB L2)"},
+        "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
+                "d2h_bytes_per_step": T * H * 4},
+        "roofline": {"bound": "hbm", "kernel": "whole EP layer (weights of the used experts, all ranks)",
+                     "achieved": achieved, "peak": hbm * world, "unit": "GB/s", "frac": achieved / (hbm * world),
+                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs x {world} ({peak_kind})",
+                     "alg_bytes_per_launch": alg, "unique_experts": unique, "traffic": None},
+        "gpu_launches": launches, "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    ctx.ep_finalize()
+
+
 def run_ours(args):
     import torch
 
@@ -416,6 +509,10 @@ def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
     cfg = dict(C2)
+    if args.experts:   # reduced c2 case for profiler captures (a few GB on the device)
+        cfg["experts"] = args.experts
+    if args.tokens:
+        cfg["tokens"] = args.tokens
     ctx = k3xb.Context(local)
     stream = torch.cuda.Stream(device=local)
     torch.cuda.set_stream(stream)
@@ -425,6 +522,9 @@ def run_ours(args):
         return finish(ctx, world)
     if args.config == "c3":
         run_c3(args, rank, world, local, ctx, stream)
+        return finish(ctx, world)
+    if world > 1:
+        run_c2_ep(args, rank, world, local, ctx, stream, cfg)
         return finish(ctx, world)
     engine = k3xb.ENGINE_SIMT if args.engine == "simt" else k3xb.ENGINE_MXF4
     w, desc, hidden = make_c2_layer(ctx, torch, cfg, engine, args.act_terms)
@@ -523,7 +623,8 @@ def run_ours(args):
         "vs_baseline": None,
         "dtype": "mxfp4 weights (e2m1+e8m0) x e2m1-term activations, fp32 accumulate",
         "data": "synthetic (seeded, generated on the GPU)",
-        "config": {"workload": "c2: single released-shape MoE layer, expert-major verify",
+        "config": {"workload": "c2: single released-shape MoE layer, expert-major verify"
+                   + ("" if (E, T) == (C2["experts"], C2["tokens"]) else f" (reduced: {E} experts, {T} tokens)"),
                    "hidden": H, "experts": E, "top_k": K, "inter": cfg["inter"],
                    "shared_inter": cfg["shared_inter"], "verify_tokens": T,
                    "sequences_x_drafts": "8x8", "layers": 1, "engine": args.engine,
@@ -653,6 +754,8 @@ def main():
                     help="c2 (default, the headline line), c3 KDA tree, c4 two-layer verify step")
     ap.add_argument("--accept", choices=["greedy", "rejection"], default="greedy", help="c4 acceptance rule")
     ap.add_argument("--sequences", type=int, default=1, help="c3: sequences sharing the draft tree")
+    ap.add_argument("--experts", type=int, default=0, help="c2 with fewer experts (small profiler case)")
+    ap.add_argument("--tokens", type=int, default=0, help="c2 with another verify-token count")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

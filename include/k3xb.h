@@ -362,6 +362,29 @@ typedef struct {
 int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* model,
                      const k3xb_verify_io* io);
 
+/* ---- expert parallelism (NCCL over NVLink) ---------------------------------- */
+/* 128-byte NCCL unique id, made on one rank and handed to all (any
+ * transport: a store, a file, a broadcast). No reference counterpart: the
+ * reference runs one process on one GPU. */
+int k3xb_ep_unique_id(uint8_t* unique_id);
+/* Joins this context (its GPU) to a world of `world` ranks. */
+int k3xb_ep_init(k3xb_ctx* ctx, const uint8_t* unique_id, int32_t rank,
+                 int32_t world);
+int k3xb_ep_finalize(k3xb_ctx* ctx);
+/* The MoE layer of k3xb_moe_layer_forward with the routed experts sharded:
+ * this rank holds experts [rank*E/world, (rank+1)*E/world) in `local`
+ * (local->experts == E / world; router [E][H], correction [E] and the shared
+ * expert are the full, replicated ones) and `tokens` tokens of its own
+ * sequences, the same count on every rank. Tokens reach the experts' ranks
+ * and the outputs come back by NCCL all-to-all; the combine runs on the
+ * token's rank with the one-GPU arithmetic, so out/ids/contributions equal
+ * the single-GPU layer's bit for bit. Every rank calls it with the same
+ * shapes (a collective). MXF4 engine only. */
+int k3xb_ep_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* local,
+                              uint32_t experts_total, const float* hidden,
+                              uint32_t tokens, float* out, uint32_t* ids,
+                              float* contributions);
+
 /* ---- (e) acceptance ------------------------------------------------------- */
 /* verify_greedy_target_block (runtime/src/speculative.cpp:74-112) for S
  * sequences of p drafts: targets = first-max argmax of logits

@@ -48,8 +48,7 @@ def build(verbose: bool = False, extra=()) -> str:
                 print(" ".join(cmd), flush=True)
             subprocess.run(cmd, check=True)
     if _stale(LIB, objs):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-cudart", "static", "-lcuda" if False else ""]
-        cmd = [c for c in cmd if c]
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-cudart", "static", "-ldl"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

@@ -191,6 +191,7 @@ int k3xb_destroy(k3xb_ctx* ctx) {
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->status_word) cudaFree(ctx->status_word);
     release_mxf4_resources(ctx);
+    release_ep(ctx);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     if (ctx->side_stream) cudaStreamDestroy(ctx->side_stream);
     if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
@@ -948,6 +949,62 @@ int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verif
                              tr.be, nullptr, rec, sch.levels, reinterpret_cast<const int32_t*>(io->accepted))))
             return st;
     }
+    return K3XB_OK;
+}
+
+int k3xb_ep_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* local, uint32_t E, const float* hidden,
+                              uint32_t T, float* out, uint32_t* ids_out, float* contrib_out) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    int st = validate_layer(ctx, local);
+    if (st) return st;
+    const int G = ep_world(ctx);
+    if (G < 1) return fail(ctx, K3XB_INVALID_STATE, "expert parallelism not initialised (k3xb_ep_init)");
+    if (local->engine != K3XB_ENGINE_MXF4) return fail(ctx, K3XB_INVALID_STATE, "expert parallelism runs the MXF4 engine");
+    if (!E || E % static_cast<uint32_t>(G) || local->experts != E / static_cast<uint32_t>(G))
+        return fail(ctx, K3XB_INVALID_EXTENT, "experts must split evenly: local.experts == experts_total / world");
+    if (local->top_k > E || local->top_k > 32 || E > 1024 || local->top_k > 255)
+        return fail(ctx, K3XB_INVALID_EXTENT, "route: need top_k <= 32 and experts <= 1024");
+    if (!T || !hidden || !out) return fail(ctx, K3XB_INVALID_EXTENT, "ep forward arguments");
+    const uint32_t K = local->top_k, H = local->hidden, Is = local->shared_inter;
+    const bool shared = local->shared_gate != nullptr;
+    Sizer sz;
+    sz.take<float>(static_cast<size_t>(T) * E);
+    sz.take<uint32_t>(static_cast<size_t>(T) * K);
+    sz.take<float>(static_cast<size_t>(T) * K);
+    sz.take<float>(static_cast<size_t>(T) * H);
+    sz.take<uint16_t>(2ull * T * H);
+    sz.take<uint16_t>(2ull * T * (Is ? Is : 1));
+    sz.take<uint8_t>(ep_scratch_bytes(G, T, K, H, local->experts), 1024);
+    sz.used += mxf4_scratch_bytes(*local, static_cast<uint32_t>(G) * T);
+    void* base;
+    if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
+    Carver c(base);
+    float* logits = c.take<float>(static_cast<size_t>(T) * E);
+    uint32_t* ids = ids_out ? ids_out : c.take<uint32_t>(static_cast<size_t>(T) * K);
+    if (ids_out) c.take<uint32_t>(static_cast<size_t>(T) * K);
+    float* contrib = contrib_out ? contrib_out : c.take<float>(static_cast<size_t>(T) * K);
+    if (contrib_out) c.take<float>(static_cast<size_t>(T) * K);
+    float* shared_out = c.take<float>(static_cast<size_t>(T) * H);
+    uint16_t* sxb = c.take<uint16_t>(2ull * T * H);
+    uint16_t* sbd = c.take<uint16_t>(2ull * T * (Is ? Is : 1));
+    void* region = c.take<uint8_t>(ep_scratch_bytes(G, T, K, H, local->experts), 1024);
+    set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
+    if (shared) {   // side stream, as in the one-GPU layer
+        K3XB_CUDA(ctx, cudaEventRecord(ctx->ev_fork, ctx->stream));
+        K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->side_stream, ctx->ev_fork, 0));
+        cudaStream_t main = ctx->stream;
+        ctx->stream = ctx->side_stream;
+        st = launch_shared_tc(ctx, *local, hidden, T, sxb, sbd, shared_out);
+        ctx->stream = main;
+        if (st) return st;
+        K3XB_CUDA(ctx, cudaEventRecord(ctx->ev_join, ctx->side_stream));
+    }
+    if ((st = launch_router_logits(ctx, hidden, T, H, local->router, E, logits))) return st;
+    if ((st = launch_topk(ctx, logits, local->correction, T, E, K, ids, contrib, nullptr, ctx->status_word))) return st;
+    if (shared) K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
+    if ((st = ep_moe_forward(ctx, *local, E, hidden, T, ids, contrib, shared ? shared_out : nullptr, region, out)))
+        return st;
+    ++ctx->stats.moe_layer_calls;
     return K3XB_OK;
 }
 

@@ -22,6 +22,7 @@ struct k3xb_ctx {
     int32_t* status_word = nullptr;   // device-side validation status (route, plan)
     void* mxf4_scratch = nullptr;     // MXF4-engine region inside `scratch`
     void* mxf4_state = nullptr;       // MXF4-engine resources (tensor maps, attributes)
+    void* ep_state = nullptr;         // expert parallelism: NCCL communicator
 };
 
 namespace k3xb {

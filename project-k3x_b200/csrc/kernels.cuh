@@ -94,6 +94,12 @@ int launch_conv_commit_linear(k3xb_ctx* ctx, const float* const proj[3], const u
 int launch_rms_norm(k3xb_ctx* ctx, const float* x, const uint16_t* w, uint32_t T, uint32_t H, float eps, float* out);
 int launch_embed(k3xb_ctx* ctx, const uint32_t* tokens, const uint16_t* table, uint32_t V, uint32_t T, uint32_t H,
                  float* out);
+// ep.cu — expert parallelism (NCCL all-to-all dispatch / combine)
+void release_ep(k3xb_ctx* ctx);
+size_t ep_scratch_bytes(uint32_t G, uint32_t T, uint32_t K, uint32_t H, uint32_t E_r);
+int ep_moe_forward(k3xb_ctx* ctx, const k3xb_moe_layer& local, uint32_t E, const float* hidden, uint32_t T,
+                   const uint32_t* ids, const float* contrib, const float* shared, void* region, float* out);
+int ep_world(const k3xb_ctx* ctx);   // 0 when expert parallelism is not initialised
 // shared expert on kind::f16 tensor cores; xb [2T][H], bd [2T][Is] bf16 scratch
 int launch_shared_tc(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T, uint16_t* xb,
                      uint16_t* bd, float* out);

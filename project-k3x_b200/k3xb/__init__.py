@@ -127,6 +127,10 @@ def library() -> C.CDLL:
             "k3xb_attention_residual_norm": [vp, vp, vp, vp, vp, vp, vp, u32, u32, f32, vp, vp],
             "k3xb_layer_forward": [vp, C.POINTER(Layer), vp, vp, vp, u32, u32, vp, vp, vp, vp, vp],
             "k3xb_verify_step": [vp, C.POINTER(VerifyModel), C.POINTER(VerifyIO)],
+            "k3xb_ep_unique_id": [vp],
+            "k3xb_ep_init": [vp, vp, C.c_int32, C.c_int32],
+            "k3xb_ep_finalize": [vp],
+            "k3xb_ep_moe_layer_forward": [vp, C.POINTER(MoeLayer), u32, vp, u32, vp, vp, vp],
         }
         for name, args in sigs.items():
             fn = getattr(lib, name)
@@ -273,6 +277,19 @@ class Context:
                                                 _p(conv), _p(recurrent), _p(hidden_out), _p(expert_ids),
                                                 _p(trace)), "layer_forward")
 
+    # ---- expert parallelism ------------------------------------------------
+    def ep_init(self, unique_id: bytes, rank: int, world: int):
+        buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
+        self._check(self.lib.k3xb_ep_init(self.h, buf, rank, world), "ep_init")
+
+    def ep_finalize(self):
+        self._check(self.lib.k3xb_ep_finalize(self.h), "ep_finalize")
+
+    def ep_moe_layer_forward(self, local: "MoeLayer", experts_total, hidden, out, ids=None, contrib=None):
+        self._check(self.lib.k3xb_ep_moe_layer_forward(self.h, C.byref(local), experts_total, _p(hidden),
+                                                       hidden.shape[0], _p(out), _p(ids), _p(contrib)),
+                    "ep_moe_layer_forward")
+
     def verify_step(self, model: "VerifyModel", io: "VerifyIO"):
         self._check(self.lib.k3xb_verify_step(self.h, C.byref(model), C.byref(io)), "verify_step")
 
@@ -407,3 +424,32 @@ def verify_io_desc(sequences, drafts, conv, recurrent, accepted, committed, comm
     io.logits, io.accepted, io.committed = ptr(logits), ptr(accepted), ptr(committed)
     io.committed_count = ptr(committed_count)
     return io
+
+
+def ep_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for k3xb_ep_init on every rank."""
+    buf = (C.c_uint8 * 128)()
+    st = library().k3xb_ep_unique_id(buf)
+    if st != OK:
+        raise K3xbError(st, "ep_unique_id")
+    return bytes(buf)
+
+
+def ep_local_layer(w: dict, rank: int, world: int) -> dict:
+    """The expert shard of rank `rank`: experts [rank*E/world, ...) of the
+    stacked MXFP4 arrays (views, no copies), router/correction/shared kept
+    whole."""
+    E = w["experts"]
+    if E % world:
+        raise K3xbError(INVALID_EXTENT, "experts must divide evenly over the world")
+    n = E // world
+    lo, hi = rank * n, (rank + 1) * n
+    out = dict(w, experts=n)
+    for k in ("gate_packed", "gate_scales", "up_packed", "up_scales", "down_packed", "down_scales"):
+        out[k] = w[k][lo:hi]
+    I, H = w["inter"], w["hidden"]
+    for k, rows in (("gate_scales_tc", I), ("up_scales_tc", I), ("down_scales_tc", H)):
+        if w.get(k) is not None:   # atoms [E*rows/128][K/128][512]: whole experts are contiguous
+            per = w[k].numel() // E
+            out[k] = w[k].view(-1)[lo * per:hi * per]
+    return out
