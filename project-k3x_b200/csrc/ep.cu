@@ -13,7 +13,7 @@
 //   local plan      expert-major over the received rows (ascending local
 //                   expert, (row, slot) order inside a group)
 //   experts         the tcgen05 engine (experts_tc.cu) on the local experts
-//   all-to-all #2   each (row, slot) output back to the home rank
+//   all-to-all #2   each (row, slot) output back to the home rank (bf16)
 //   combine         slot-ordered weighted sum + shared expert (the single-GPU
 //                   arithmetic, official_moe.cpp:313-322), so the output is
 //                   bit-identical to the one-GPU layer for any world size
@@ -157,8 +157,9 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const uint32_t* __restric
 }
 
 // combine (official_moe.cpp:313-322, then + shared): slot j's output comes
-// from the rank that owns expert ids[t][j]: y[g][t][j][H].
-__global__ void ep_combine_kernel(const float* __restrict__ y, const uint32_t* __restrict__ ids,
+// from the rank that owns expert ids[t][j]: y[g][t][j][H] (bf16 words; the
+// expert outputs are bf16-rounded, so the words are exact).
+__global__ void ep_combine_kernel(const uint16_t* __restrict__ y, const uint32_t* __restrict__ ids,
                                   const float* __restrict__ contrib, const float* __restrict__ shared, uint32_t T,
                                   uint32_t K, uint32_t H, uint32_t E_r, float* __restrict__ out) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -167,7 +168,7 @@ __global__ void ep_combine_kernel(const float* __restrict__ y, const uint32_t* _
     float mixed = 0.0f;
     for (uint32_t j = 0; j < K; ++j) {
         const uint32_t g = ids[t * K + j] / E_r;
-        const float v = y[((static_cast<size_t>(g) * T + t) * K + j) * H + h];
+        const float v = decode_bf16(y[((static_cast<size_t>(g) * T + t) * K + j) * H + h]);
         mixed = __fadd_rn(mixed, __fmul_rn(contrib[t * K + j], v));
     }
     mixed = round_bf16(mixed);
@@ -213,8 +214,8 @@ size_t ep_scratch_bytes(uint32_t G, uint32_t T, uint32_t K, uint32_t H, uint32_t
     s.take<float>(static_cast<size_t>(G) * T * H);       // recv_x
     s.take<uint32_t>(static_cast<size_t>(G) * T * K);    // send_meta
     s.take<uint32_t>(static_cast<size_t>(G) * T * K);    // recv_meta
-    s.take<float>(static_cast<size_t>(G) * T * K * H);   // y (rows received, per slot)
-    s.take<float>(static_cast<size_t>(G) * T * K * H);   // y_home
+    s.take<uint16_t>(static_cast<size_t>(G) * T * K * H);   // y (rows received, per slot)
+    s.take<uint16_t>(static_cast<size_t>(G) * T * K * H);   // y_home
     s.take<uint32_t>(E_r + 1);                           // plan
     s.take<uint32_t>(E_r + 1);
     s.take<uint32_t>(static_cast<size_t>(G) * T * K);
@@ -233,8 +234,8 @@ int ep_moe_forward(k3xb_ctx* ctx, const k3xb_moe_layer& L, uint32_t E, const flo
     float* recv_x = c.take<float>(static_cast<size_t>(G) * T * H);
     uint32_t* send_meta = c.take<uint32_t>(static_cast<size_t>(G) * T * K);
     uint32_t* recv_meta = c.take<uint32_t>(static_cast<size_t>(G) * T * K);
-    float* y = c.take<float>(static_cast<size_t>(G) * T * K * H);
-    float* y_home = c.take<float>(static_cast<size_t>(G) * T * K * H);
+    uint16_t* y = c.take<uint16_t>(static_cast<size_t>(G) * T * K * H);
+    uint16_t* y_home = c.take<uint16_t>(static_cast<size_t>(G) * T * K * H);
     k3xb_plan plan{};
     plan.group_expert = c.take<uint32_t>(E_r + 1);
     plan.group_offset = c.take<uint32_t>(E_r + 1);
@@ -250,12 +251,22 @@ int ep_moe_forward(k3xb_ctx* ctx, const k3xb_moe_layer& L, uint32_t E, const flo
     ep_rows_kernel<<<dim3(T, G), 256, 0, ctx->stream>>>(hidden, T, H, send_x);
     K3XB_LAUNCHED(ctx);
     int st;
-    if ((st = all_to_all(ctx, send_meta, recv_meta, static_cast<size_t>(T) * K, ncclUint32, 4))) return st;
-    if ((st = all_to_all(ctx, send_x, recv_x, static_cast<size_t>(T) * H, ncclFloat32, 4))) return st;
+    {   // metadata and rows in one NCCL group
+        const NcclApi& api = nccl();
+        K3XB_NCCL(ctx, api.group_start());
+        for (uint32_t g = 0; g < G; ++g) {
+            const size_t nm_g = static_cast<size_t>(T) * K, nx_g = static_cast<size_t>(T) * H;
+            K3XB_NCCL(ctx, api.send(send_meta + g * nm_g, nm_g, ncclUint32, g, ep->comm, ctx->stream));
+            K3XB_NCCL(ctx, api.recv(recv_meta + g * nm_g, nm_g, ncclUint32, g, ep->comm, ctx->stream));
+            K3XB_NCCL(ctx, api.send(send_x + g * nx_g, nx_g, ncclFloat32, g, ep->comm, ctx->stream));
+            K3XB_NCCL(ctx, api.recv(recv_x + g * nx_g, nx_g, ncclFloat32, g, ep->comm, ctx->stream));
+        }
+        K3XB_NCCL(ctx, api.group_end());
+    }
     ep_plan_kernel<<<1, 1024, (E_r + 1) * sizeof(uint32_t), ctx->stream>>>(recv_meta, G * T, K, E_r, plan);
     K3XB_LAUNCHED(ctx);
-    if ((st = launch_mxf4_experts(ctx, L, recv_x, G * T, plan, y))) return st;
-    if ((st = all_to_all(ctx, y, y_home, static_cast<size_t>(T) * K * H, ncclFloat32, 4))) return st;
+    if ((st = launch_mxf4_experts(ctx, L, recv_x, G * T, plan, nullptr, y))) return st;
+    if ((st = all_to_all(ctx, y, y_home, static_cast<size_t>(T) * K * H, ncclBfloat16, 2))) return st;
     const size_t n = static_cast<size_t>(T) * H;
     ep_combine_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(y_home, ids, contrib, shared,
                                                                                        T, K, H, E_r, out);

@@ -131,45 +131,32 @@ __global__ void __launch_bounds__(1024) worklist_kernel(const uint32_t* group_co
 // ---------------------------------------------------------------------------
 // E2M1-term split (bit-identical to oracle/k3x_oracle.c:k3xo_e2m1_terms).
 // Every token's hidden row once: tsplit[t][term][H/2], tsf[t][term][H/32].
+// One warp per (row, 32-element block), lane = element: the block maximum
+// is a warp max (exact), each lane codes and subtracts its own element, and
+// groups of 8 lanes OR their nibbles into one 32-bit word.
 __global__ void __launch_bounds__(256) split_tokens_kernel(const float* __restrict__ hidden, uint32_t T,
                                                            uint32_t H, uint32_t terms,
                                                            uint8_t* __restrict__ tsplit,
                                                            uint8_t* __restrict__ tsf) {
-    const uint32_t kbc = H / 32;
-    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= static_cast<size_t>(T) * kbc) return;
-    const uint32_t t = static_cast<uint32_t>(i / kbc), kb = static_cast<uint32_t>(i % kbc);
-    const float* x = hidden + static_cast<size_t>(t) * H + kb * 32;
-    float r[32];
-#pragma unroll
-    for (int q = 0; q < 32; q += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(x + q);
-        r[q] = v.x; r[q + 1] = v.y; r[q + 2] = v.z; r[q + 3] = v.w;
-    }
+    const uint32_t kbc = H / 32, lane = threadIdx.x % 32;
+    const size_t w = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
+    if (w >= static_cast<size_t>(T) * kbc) return;
+    const uint32_t t = static_cast<uint32_t>(w / kbc), kb = static_cast<uint32_t>(w % kbc);
+    float r = hidden[static_cast<size_t>(t) * H + kb * 32 + lane];
     for (uint32_t term = 0; term < terms; ++term) {
-        float amax = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(r[e]));
+        const float amax = warp_max(fabsf(r));
         const int s = amax > 0.0f ? e2m1_block_exponent(amax) : 0;
-        const float inv = exp2i(-s), scl = exp2i(s);
-        uint32_t w[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            uint32_t acc = 0;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float v = r[8 * q + e];
-                const uint32_t code = e2m1_code(fabsf(v) * inv);
-                const bool neg = signbit(v) && code;
-                acc |= (code | (neg ? 8u : 0u)) << (4 * e);
-                const float qv = e2m1_magnitude(code) * scl;
-                r[8 * q + e] = neg ? __fadd_rn(v, qv) : __fsub_rn(v, qv);
-            }
-            w[q] = acc;
-        }
+        const uint32_t code = e2m1_code(fabsf(r) * exp2i(-s));
+        const bool neg = signbit(r) && code;
+        const float qv = e2m1_magnitude(code) * exp2i(s);
+        r = neg ? __fadd_rn(r, qv) : __fsub_rn(r, qv);
+        uint32_t word = (code | (neg ? 8u : 0u)) << (4 * (lane % 8));
+        word |= __shfl_xor_sync(0xffffffffu, word, 1);
+        word |= __shfl_xor_sync(0xffffffffu, word, 2);
+        word |= __shfl_xor_sync(0xffffffffu, word, 4);
         const size_t row = static_cast<size_t>(t) * terms + term;
-        *reinterpret_cast<uint4*>(tsplit + row * (H / 2) + kb * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-        tsf[row * kbc + kb] = static_cast<uint8_t>(s + 127);
+        if (lane % 8 == 0) *reinterpret_cast<uint32_t*>(tsplit + row * (H / 2) + kb * 16 + (lane / 8) * 4) = word;
+        if (lane == 0) tsf[row * kbc + kb] = static_cast<uint8_t>(s + 127);
     }
 }
 
@@ -239,6 +226,7 @@ struct DParams {
     uint32_t H, I, terms, top_k;
     int* error;
     uint32_t rowblocks;       // 128-row blocks of the stacked down weights (E * H / 128)
+    uint16_t* slot_out16;     // when set: bf16 words instead of slot_out floats
 };
 
 // TMEM columns. Routed gate/up: gate accumulator at 0, up at RoutedCfg::kColUp,
@@ -354,8 +342,13 @@ __global__ void __launch_bounds__(kThreads, 1) down_kernel(const __grid_constant
                 if (++tcount < terms) continue;
                 if (j % 32 == 0 && j) dsts = fetch_dst(j);
                 const size_t dst = __shfl_sync(0xffffffffu, dsts, j % 32);
-                p.slot_out[dst * p.H + h0] = round_bf16(y0);
-                if (second) p.slot_out[dst * p.H + h1] = round_bf16(y1);
+                if (p.slot_out16) {
+                    p.slot_out16[dst * p.H + h0] = encode_bf16(y0);
+                    if (second) p.slot_out16[dst * p.H + h1] = encode_bf16(y1);
+                } else {
+                    p.slot_out[dst * p.H + h0] = round_bf16(y0);
+                    if (second) p.slot_out[dst * p.H + h1] = round_bf16(y1);
+                }
                 y0 = y1 = 0.0f;
                 tcount = 0;
                 ++j;
@@ -631,7 +624,7 @@ size_t mxf4_scratch_bytes(const k3xb_moe_layer& L, uint32_t T) {
 void set_mxf4_scratch(k3xb_ctx* ctx, void* region) { ctx->mxf4_scratch = region; }
 
 int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T,
-                        const k3xb_plan& plan, float* slot_out) {
+                        const k3xb_plan& plan, float* slot_out, uint16_t* slot_out16) {
     const uint32_t H = L.hidden, I = L.inter;
     if (H % 128 || I % 128)
         return fail(ctx, K3XB_INVALID_EXTENT, "MXF4 engine needs hidden and inter multiples of 128");
@@ -665,7 +658,7 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
     K3XB_LAUNCHED(ctx);
     {
         const size_t n = static_cast<size_t>(T) * (H / 32);
-        split_tokens_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(hidden, T, H, l.terms,
+        split_tokens_kernel<<<static_cast<unsigned>((n * 32 + 255) / 256), 256, 0, ctx->stream>>>(hidden, T, H, l.terms,
                                                                                           bf.tsplit, bf.tsf);
         K3XB_LAUNCHED(ctx);
     }
@@ -676,7 +669,8 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
     GuParams gp{bf.tb.desc_gu, bf.tb.counts + 1, sfa_gate, sfa_up, bf.sfb_gu, bf.b_d, bf.sfb_d, H, I, l.terms,
                 L.activation, L.situ_beta, L.situ_linear_beta, ctx->status_word};
     DParams dp{bf.tb.desc_d, bf.tb.counts + 2, plan.assign_token, plan.assign_slot, sfa_down, bf.sfb_d, slot_out,
-               H, I, l.terms, L.top_k, ctx->status_word, static_cast<uint32_t>(static_cast<size_t>(L.experts) * H / kBlockM)};
+               H, I, l.terms, L.top_k, ctx->status_word, static_cast<uint32_t>(static_cast<size_t>(L.experts) * H / kBlockM),
+               slot_out16};
     return l.nmax == 64 ? launch_routed<64>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, dp)
                         : launch_routed<128>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, dp);
 }

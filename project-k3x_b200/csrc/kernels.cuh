@@ -57,8 +57,9 @@ namespace k3xb {
 // experts_tc.cu — tcgen05 block-scaled expert engine
 size_t mxf4_scratch_bytes(const k3xb_moe_layer& L, uint32_t T);
 void set_mxf4_scratch(k3xb_ctx* ctx, void* region);
+// slot_out [T*k][H] float, or bf16 words in slot_out16 when that is given
 int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T,
-                        const k3xb_plan& plan, float* slot_out);
+                        const k3xb_plan& plan, float* slot_out, uint16_t* slot_out16 = nullptr);
 void release_mxf4_resources(k3xb_ctx* ctx);
 int prepare_mxfp4_scales(k3xb_ctx* ctx, const uint8_t* scales, size_t rows, size_t cols, uint8_t* out);
 // 2-D byte tensor map (128B swizzle, box {128 B, box_rows}); map is a CUtensorMap*
