@@ -134,6 +134,27 @@ def sum_over_ranks(x, world):
     return float(t.item())
 
 
+def graphed(torch, ctx, step, stream, enabled):
+    """Counts the library's kernel launches of one eager step, then (when
+    enabled) captures the step into a CUDA graph on `stream` so the timed
+    loop replays it without host launch overhead. Returns (run, launches per
+    step, graph used). Only for steps without NCCL calls: a graph holding
+    collectives would have to be released before the communicator is."""
+    l0 = ctx.stats()["kernel_launches"]
+    step()
+    torch.cuda.synchronize()
+    per = ctx.stats()["kernel_launches"] - l0
+    if not enabled:
+        return step, per, False
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step()
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    return g.replay, per, True
+
+
 def make_c2_layer(ctx, torch, cfg, engine, act_terms):
     import k3xb
     H, I, E, Is = cfg["hidden"], cfg["inter"], cfg["experts"], cfg["shared_inter"]
@@ -442,17 +463,20 @@ def run_c2_ep(args, rank, world, local, ctx, stream, cfg):
     all_ids = [torch.empty_like(ids) for _ in range(world)]
     dist.all_gather(all_ids, ids)
     unique = int(torch.unique(torch.cat(all_ids)).numel())
+    # eager launches: a CUDA graph that holds NCCL calls must be released
+    # before the communicator and the process group are destroyed; this
+    # path keeps the collectives out of graphs altogether
+    run, per_step, used_graph = graphed(torch, ctx, step, stream, False)
     barrier(world)
     torch.cuda.synchronize()
-    launches0 = ctx.stats()["kernel_launches"]
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         ev0.record(stream)
         for _ in range(args.steps):
-            step()
+            run()
         ev1.record(stream)
         torch.cuda.synchronize()
-    launches = ctx.stats()["kernel_launches"] - launches0
+    launches = per_step * args.steps
     ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
     # e2e: pinned host rows in, layer output out, copies inside the timed region
     x_h = x.cpu().pin_memory()
@@ -488,6 +512,7 @@ def run_c2_ep(args, rank, world, local, ctx, stream, cfg):
                    "shared_inter": cfg["shared_inter"], "verify_tokens": T, "sequences_x_drafts": "8x8",
                    "layers": 1, "engine": "mxf4", "act_terms": args.act_terms,
                    "parallelism": f"expert parallel x{world} (NCCL all-to-all), {Tr} tokens per rank",
+                   "cuda_graph": used_graph,
                    "l2": "no flush: each step streams ~8.4 GB of expert weights (>> 126 MB L2)"},
         "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
                 "d2h_bytes_per_step": T * H * 4},
@@ -541,18 +566,18 @@ def run_ours(args):
     ctx.sync()
     # unique experts of this workload (for the algorithmic byte count)
     unique = int(torch.unique(ids).numel())
+    run, per_step, used_graph = graphed(torch, ctx, step, stream, not args.no_graph)
 
     barrier(world)
     torch.cuda.synchronize()
-    launches0 = ctx.stats()["kernel_launches"]
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         ev0.record(stream)
         for _ in range(args.steps):
-            step()
+            run()
         ev1.record(stream)
         torch.cuda.synchronize()
-    launches = ctx.stats()["kernel_launches"] - launches0
+    launches = per_step * args.steps
     ms = ev0.elapsed_time(ev1) / args.steps
     ms_max = max_over_ranks(ms, world)
     barrier(world)
@@ -630,6 +655,7 @@ def run_ours(args):
                    "sequences_x_drafts": "8x8", "layers": 1, "engine": args.engine,
                    "act_terms": args.act_terms if args.engine == "mxf4" else None,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "cuda_graph": used_graph,
                    "l2": "no flush: each step streams ~8.4 GB of expert weights (>> 126 MB L2)"},
         "e2e": {"value": total_tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4 + 2 * T * K * 4,
@@ -756,6 +782,7 @@ def main():
     ap.add_argument("--sequences", type=int, default=1, help="c3: sequences sharing the draft tree")
     ap.add_argument("--experts", type=int, default=0, help="c2 with fewer experts (small profiler case)")
     ap.add_argument("--tokens", type=int, default=0, help="c2 with another verify-token count")
+    ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a CUDA graph replay")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
