@@ -36,6 +36,12 @@ METRIC = "verified draft tokens/s per KDA+MoE layer"
 C2 = dict(hidden=7168, inter=2048, experts=384, top_k=16, shared_inter=2048, tokens=64, seed=1,
           sequences=8, drafts=8)
 EXPERT_BYTES = 3 * 7168 * 2048 * (0.5 + 1 / 32)   # S_e = 23,396,352 B per expert
+# DRAM bytes (read + write) of the routed gate/up + down kernels per
+# algorithmic byte, from one ncu capture of a reduced c2 case (128 experts,
+# 24 tokens): 2963.3 MB against 2872 MB algorithmic (expected 122.8 unique
+# experts). Traffic grows with the unique experts, so a full-size launch is
+# this ratio times its algorithmic bytes (profiles/expert_ffn_traffic_128x24.md).
+EXPERT_TRAFFIC_RATIO = (1969.4 + 7.3 + 976.3 + 10.3) / (122.8 * 3 * 7168 * 2048 * 0.53125 / 1e6)
 
 
 def peaks():
@@ -664,7 +670,9 @@ def run_ours(args):
                      "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
                      "alg_bytes_per_launch": alg_bytes, "unique_experts": unique,
-                     "launch_ms": exp_ms, "traffic": None},
+                     "launch_ms": exp_ms, "traffic": unique * EXPERT_BYTES * EXPERT_TRAFFIC_RATIO,
+                     "traffic_source": "ncu dram__bytes_read+write of gate/up + down on a reduced c2 case, "
+                                       "scaled by unique experts (profiles/expert_ffn_traffic_128x24.md)"},
         "gpu_launches": launches,
         "clocks": clk.summary(),
     }
