@@ -104,6 +104,32 @@ int k3xb_route_static(const float* hidden, uint32_t tokens, uint32_t hidden_size
                       uint32_t experts, uint32_t top_k, uint32_t* ids,
                       float* contributions, int32_t* status, void* stream);
 
+/* select_routing (runtime/src/routing_policy.cpp:31-159), the synthetic
+ * engine's routing policy (model.cpp:245, :925) over sigmoid scores:
+ * natural Top-k, a fixed K from the ladder {4, 6, 8, 12, 16}, or an
+ * adaptive K (natural Top-16 cut at the first ladder K that reaches
+ * mass_target, covers the entropy support exp(H) and clears
+ * minimum_boundary_gap), raised to quality_floor_k (0 = none). */
+enum { K3XB_ROUTING_NATURAL = 0, K3XB_ROUTING_FIXED = 1, K3XB_ROUTING_ADAPTIVE = 2 };
+typedef struct {
+    int32_t mode;              /* K3XB_ROUTING_* */
+    uint32_t fixed_k;
+    float mass_target;         /* (0, 1] */
+    float minimum_gap;         /* [0, 1] */
+    uint32_t quality_floor_k;
+} k3xb_routing_policy;
+/* scores [T][E] in [0, 1], bias [E]; natural_k <= min(32, E), E <= 1024.
+ * Outputs [T][natural_k]: expert_ids (UINT32_MAX past the selected K) and
+ * normalized weights (0 there); selected_k [T]; escalated [T] (may be NULL:
+ * the floor raised K); stats [T][4] (may be NULL): normalized entropy,
+ * entropy support, selected mass, boundary confidence. Policy errors return
+ * K3XB_INVALID_STATE; invalid scores set the device status word to it. */
+int k3xb_select_routing(k3xb_ctx* ctx, const float* scores, uint32_t tokens,
+                        uint32_t experts, const float* bias, uint32_t natural_k,
+                        const k3xb_routing_policy* policy, uint32_t* expert_ids,
+                        float* weights, uint32_t* selected_k, uint32_t* escalated,
+                        float* stats);
+
 /* build_expert_major_plan (runtime/src/expert_major.cpp:10-54): groups in
  * first-use order, assignments in (token, slot) order inside a group.
  * group_offset has room for experts+1 entries; the used prefix is

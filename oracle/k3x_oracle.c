@@ -12,6 +12,7 @@
  */
 #include "k3x_oracle.h"
 
+#include <float.h>
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -367,6 +368,123 @@ int k3xo_route_logits(const float* logits, const float* correction,
     }
     free(scores);
     free(adjusted);
+    return status;
+}
+
+/* routing_policy.cpp:12-29 */
+static int routing_k_allowed(size_t k)
+{
+    return k == 4 || k == 6 || k == 8 || k == 12 || k == 16;
+}
+
+static float routing_boundary(const float* probs, size_t n, size_t k)
+{
+    if (k >= n) return 1.0f;
+    float gap = probs[k - 1] - probs[k];
+    if (gap < 0.0f) gap = 0.0f;
+    float top = probs[0] > FLT_MIN ? probs[0] : FLT_MIN;
+    return gap / top;
+}
+
+/* routing_policy.cpp:109-128: first ladder K past the floor that reaches the
+ * mass target, the entropy support and the boundary gap; else natural_k */
+static size_t routing_adaptive_k(const float* probs, size_t n, float support, float mass_target,
+                                 float minimum_gap, size_t floor_k)
+{
+    const float eps = 1.0e-5f;
+    float cumulative = 0.0f;
+    for (size_t slot = 0; slot < n; ++slot) {
+        cumulative += probs[slot];
+        size_t k = slot + 1;
+        if (!routing_k_allowed(k) || k < floor_k) continue;
+        float confidence = routing_boundary(probs, n, k);
+        if (cumulative + eps >= mass_target && (float)k + eps >= support && confidence + eps >= minimum_gap)
+            return k;
+    }
+    return n;
+}
+
+/* routing_policy.cpp:31-159 */
+int k3xo_select_routing(const float* scores, const float* bias, size_t E, size_t K, int mode,
+                        size_t fixed_k, float mass_target, float minimum_gap, size_t floor_k,
+                        uint32_t* full_order, uint32_t* expert_ids, float* weights,
+                        size_t* selected_k, float* stats, int* escalated)
+{
+    if (!E || !K || K > E) return K3XO_INVALID_STATE;
+    for (size_t e = 0; e < E; ++e)
+        if (!isfinite(scores[e]) || scores[e] < 0.0f || scores[e] > 1.0f || !isfinite(bias[e]))
+            return K3XO_INVALID_STATE;
+    if (!isfinite(mass_target) || mass_target <= 0.0f || mass_target > 1.0f || !isfinite(minimum_gap) ||
+        minimum_gap < 0.0f || minimum_gap > 1.0f)
+        return K3XO_INVALID_STATE;
+    if (floor_k != 0 && (!routing_k_allowed(floor_k) || (mode != 0 && floor_k > K))) return K3XO_INVALID_STATE;
+    if (mode == 1 && (!routing_k_allowed(fixed_k) || fixed_k > K)) return K3XO_INVALID_STATE;
+    if (mode == 2 && K != 16) return K3XO_INVALID_STATE;
+    if (mode < 0 || mode > 2) return K3XO_INVALID_STATE;
+    float* adjusted = (float*)malloc(E * sizeof(float));
+    uint32_t* order = (uint32_t*)malloc(E * sizeof(uint32_t));
+    float* probs = (float*)malloc(K * sizeof(float));
+    int status = K3XO_OK;
+    for (size_t e = 0; e < E; ++e) {
+        adjusted[e] = scores[e] + bias[e];
+        if (!isfinite(adjusted[e])) status = K3XO_INVALID_STATE;
+    }
+    if (status == K3XO_OK) {
+        /* stable order: adjusted descending, index ascending on ties */
+        for (size_t e = 0; e < E; ++e) {
+            size_t pos = e;
+            order[e] = (uint32_t)e;
+            while (pos > 0 && adjusted[order[pos - 1]] < adjusted[e]) {
+                order[pos] = order[pos - 1];
+                --pos;
+            }
+            order[pos] = (uint32_t)e;
+        }
+        float denom = 0.0f;
+        for (size_t slot = 0; slot < K; ++slot) denom += scores[order[slot]];
+        if (!isfinite(denom) || denom <= 0.0f) status = K3XO_INVALID_STATE;
+    }
+    if (status == K3XO_OK) {
+        float denom = 0.0f;
+        for (size_t slot = 0; slot < K; ++slot) denom += scores[order[slot]];
+        float entropy = 0.0f;
+        for (size_t slot = 0; slot < K; ++slot) {
+            probs[slot] = scores[order[slot]] / denom;
+            if (probs[slot] > 0.0f) entropy -= probs[slot] * logf(probs[slot]);
+        }
+        float support = expf(entropy);
+        size_t chosen = K, unfloored = K;
+        if (mode == 1) {
+            unfloored = fixed_k;
+            chosen = fixed_k > floor_k ? fixed_k : floor_k;
+        } else if (mode == 2) {
+            unfloored = routing_adaptive_k(probs, K, support, mass_target, minimum_gap, 0);
+            chosen = routing_adaptive_k(probs, K, support, mass_target, minimum_gap, floor_k);
+        }
+        float mass = 0.0f, sel = 0.0f;
+        for (size_t slot = 0; slot < chosen; ++slot) {
+            mass += probs[slot];
+            sel += scores[order[slot]];
+        }
+        if (!isfinite(sel) || sel <= 0.0f) {
+            status = K3XO_INVALID_STATE;
+        } else {
+            for (size_t slot = 0; slot < chosen; ++slot) {
+                expert_ids[slot] = order[slot];
+                weights[slot] = scores[order[slot]] / sel;
+            }
+            *selected_k = chosen;
+            stats[0] = K == 1 ? 0.0f : entropy / logf((float)K);
+            stats[1] = support;
+            stats[2] = mass;
+            stats[3] = routing_boundary(probs, K, chosen);
+            *escalated = chosen > unfloored;
+            if (full_order) memcpy(full_order, order, E * sizeof(uint32_t));
+        }
+    }
+    free(adjusted);
+    free(order);
+    free(probs);
     return status;
 }
 

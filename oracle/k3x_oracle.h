@@ -88,6 +88,22 @@ int k3xo_router_logits(const float* hidden, const uint16_t* w, size_t experts,
 int k3xo_route_logits(const float* logits, const float* correction,
                       size_t experts, size_t top_k, uint32_t* ids,
                       float* contributions, float* scores);
+/* select_routing (routing_policy.cpp:31-159): the synthetic engine's
+ * routing policy over sigmoid scores in [0,1]. mode 0 natural (Top-k),
+ * 1 fixed (fixed_k from the ladder {4,6,8,12,16}), 2 adaptive (natural
+ * Top-16 cut at the first ladder K that reaches the mass target, covers the
+ * entropy support and clears the boundary gap); quality_floor_k (0 = none)
+ * raises the choice. Outputs: full_order [E] (may be NULL), expert_ids and
+ * weights [selected_k] (room for natural_k), *selected_k, stats[4] =
+ * {normalized entropy, entropy support, selected mass, boundary
+ * confidence}, *escalated. Invalid input: K3XO_INVALID_STATE. */
+int k3xo_select_routing(const float* scores, const float* bias, size_t experts,
+                        size_t natural_k, int mode, size_t fixed_k,
+                        float mass_target, float minimum_gap,
+                        size_t quality_floor_k, uint32_t* full_order,
+                        uint32_t* expert_ids, float* weights,
+                        size_t* selected_k, float* stats, int* escalated);
+
 /* expert_major.cpp:10-54: stable first-use grouping. Outputs:
  * group_expert[g], group_offset[g..g+1] into the assignment arrays,
  * assign_token/assign_slot/assign_contrib in (token, slot) order per group. */

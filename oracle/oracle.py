@@ -27,6 +27,32 @@ _szp = C.POINTER(C.c_size_t)
 ACT_SWIGLU = 0
 ACT_SITU = 1
 
+ROUTING_NATURAL, ROUTING_FIXED, ROUTING_ADAPTIVE = 0, 1, 2
+_SELECT_ROUTING_ARGS = [_f32p, _f32p, _sz, _sz, C.c_int, _sz, C.c_float, C.c_float, _sz, C.c_void_p,
+                        _u32p, _f32p, _szp, _f32p, C.POINTER(C.c_int)]
+
+
+def _select_routing(fn, scores, bias, natural_k, mode=ROUTING_NATURAL, fixed_k=0, mass_target=0.9,
+                    minimum_gap=0.0, quality_floor_k=0):
+    """Shared wrapper of k3xo_/k3xr_select_routing: (status, dict)."""
+    scores = _c(scores, np.float32)
+    bias = _c(bias, np.float32)
+    E = scores.size
+    order = np.zeros(E, np.uint32)
+    ids = np.zeros(max(natural_k, 1), np.uint32)
+    w = np.zeros(max(natural_k, 1), np.float32)
+    k = C.c_size_t()
+    stats = np.zeros(4, np.float32)
+    esc = C.c_int()
+    st = fn(scores, bias, E, natural_k, mode, fixed_k, mass_target, minimum_gap, quality_floor_k,
+            order.ctypes.data_as(C.c_void_p), ids, w, C.byref(k), stats, C.byref(esc))
+    if st:
+        return st, None
+    n = k.value
+    return 0, dict(full_order=order, expert_ids=ids[:n], weights=w[:n], selected_k=n,
+                   normalized_entropy=stats[0], support=stats[1], mass=stats[2], boundary=stats[3],
+                   escalated=bool(esc.value))
+
 
 class OracleError(RuntimeError):
     def __init__(self, status: int, where: str):
@@ -129,6 +155,7 @@ class Restatement:
                                     _sz, _sz, _f32p, C.c_void_p]
         L.k3xo_kda_block.argtypes = [C.c_void_p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p, _f32p]
         L.k3xo_rms_norm_bf16.argtypes = [_f32p, _u16p, _sz, C.c_float, _f32p]
+        L.k3xo_select_routing.argtypes = _SELECT_ROUTING_ARGS
         L.k3xo_attention_residual.argtypes = [_f32p, _f32p, _u16p, _u16p, _sz, C.c_float, _f32p]
         L.k3xo_argmax.restype = C.c_uint32
         L.k3xo_argmax.argtypes = [_f32p, _sz]
@@ -288,6 +315,9 @@ class Restatement:
         del keep
         return out.reshape(T, weights["hidden"]), (cq, ck, cv, rec)
 
+    def select_routing(self, scores, bias, natural_k, **policy):
+        return _select_routing(self.lib.k3xo_select_routing, scores, bias, natural_k, **policy)
+
     # -- layer composition ------------------------------------------------------
     def rms_norm(self, x, weight, eps):
         x = _c(x, np.float32)
@@ -444,6 +474,7 @@ class Reference:
         L.k3xr_official_kda_cpu.argtypes = [C.c_void_p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p,
                                             _f32p]
         L.k3xr_prepare_moe_input.argtypes = [_f32p, _f32p, _u16p, _u16p, _u16p, _sz, C.c_float, _f32p]
+        L.k3xr_select_routing.argtypes = _SELECT_ROUTING_ARGS
 
     def decode_mxfp4(self, packed, scales, rows, cols, group=32):
         out = np.empty(rows * cols, np.float32)
@@ -559,6 +590,9 @@ class Reference:
         if st:
             raise OracleError(st, "ref moe layer")
         return out, ids, contrib
+
+    def select_routing(self, scores, bias, natural_k, **policy):
+        return _select_routing(self.lib.k3xr_select_routing, scores, bias, natural_k, **policy)
 
     def prepare_input(self, prefix, block, norm, proj, post, eps):
         out = np.empty(len(prefix), np.float32)

@@ -11,6 +11,7 @@
 #include "k3x/expert_major.hpp"
 #include "k3x/official_kda.hpp"
 #include "k3x/official_moe.hpp"
+#include "k3x/routing_policy.hpp"
 #include "k3x/ops.hpp"
 #include "k3x/speculative.hpp"
 
@@ -113,6 +114,36 @@ int k3xr_prepare_moe_input(const float* prefix, const float* block, const std::u
     auto r = k3x::prepare_official_moe_input(input, w, eps);
     if (!r) return code(r);
     std::copy(r.value().begin(), r.value().end(), out);
+    return 0;
+}
+
+// select_routing (routing_policy.cpp:31-159) with the outputs flattened.
+int k3xr_select_routing(const float* scores, const float* bias, std::size_t experts, std::size_t natural_k,
+                        int mode, std::size_t fixed_k, float mass_target, float minimum_gap,
+                        std::size_t quality_floor_k, std::uint32_t* full_order, std::uint32_t* expert_ids,
+                        float* weights, std::size_t* selected_k, float* stats, int* escalated) {
+    k3x::RoutingPolicyConfig config{};
+    config.mode = mode == 1 ? k3x::RoutingMode::fixed
+                            : mode == 2 ? k3x::RoutingMode::adaptive : k3x::RoutingMode::natural;
+    config.fixed_k = fixed_k;
+    config.mass_target = mass_target;
+    config.minimum_boundary_gap = minimum_gap;
+    config.quality_floor_k = quality_floor_k;
+    auto r = k3x::select_routing({scores, experts}, {bias, experts}, natural_k, config);
+    if (!r) return code(r);
+    const auto& d = r.value();
+    if (full_order)
+        for (std::size_t i = 0; i < d.full_order.size(); ++i) full_order[i] = static_cast<std::uint32_t>(d.full_order[i]);
+    for (std::size_t i = 0; i < d.selected_k; ++i) {
+        expert_ids[i] = static_cast<std::uint32_t>(d.expert_ids[i]);
+        weights[i] = d.normalized_weights[i];
+    }
+    *selected_k = d.selected_k;
+    stats[0] = d.normalized_entropy;
+    stats[1] = d.entropy_effective_support;
+    stats[2] = d.selected_cumulative_mass;
+    stats[3] = d.boundary_confidence;
+    *escalated = d.quality_floor_escalated ? 1 : 0;
     return 0;
 }
 

@@ -1,4 +1,5 @@
 // capi.cu — the extern "C" boundary of libk3xb (include/k3xb.h).
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <new>
@@ -247,6 +248,33 @@ int k3xb_route(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_t H, const
     if ((st = launch_topk(ctx, logits, correction, T, E, K, ids, contrib, scores, ctx->status_word))) return st;
     ++ctx->stats.route_calls;
     return K3XB_OK;
+}
+
+int k3xb_select_routing(k3xb_ctx* ctx, const float* scores, uint32_t T, uint32_t E, const float* bias, uint32_t K,
+                        const k3xb_routing_policy* policy, uint32_t* ids, float* weights, uint32_t* selected,
+                        uint32_t* escalated, float* stats) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!scores || !bias || !policy || !ids || !weights || !selected || !T)
+        return fail(ctx, K3XB_INVALID_EXTENT, "select_routing arguments");
+    // routing_policy.cpp:38-72
+    auto allowed = [](uint32_t k) { return k == 4 || k == 6 || k == 8 || k == 12 || k == 16; };
+    const k3xb_routing_policy& p = *policy;
+    if (!E || !K || K > E) return fail(ctx, K3XB_INVALID_STATE, "invalid routing dimensions");
+    if (K > 32 || E > 1024) return fail(ctx, K3XB_INVALID_EXTENT, "select_routing: natural_k <= 32, experts <= 1024");
+    if (p.mode < K3XB_ROUTING_NATURAL || p.mode > K3XB_ROUTING_ADAPTIVE)
+        return fail(ctx, K3XB_INVALID_STATE, "unknown routing mode");
+    if (!std::isfinite(p.mass_target) || p.mass_target <= 0.0f || p.mass_target > 1.0f ||
+        !std::isfinite(p.minimum_gap) || p.minimum_gap < 0.0f || p.minimum_gap > 1.0f)
+        return fail(ctx, K3XB_INVALID_STATE, "invalid adaptive routing threshold");
+    if (p.quality_floor_k != 0 &&
+        (!allowed(p.quality_floor_k) || (p.mode != K3XB_ROUTING_NATURAL && p.quality_floor_k > K)))
+        return fail(ctx, K3XB_INVALID_STATE, "invalid routing quality floor");
+    if (p.mode == K3XB_ROUTING_FIXED && (!allowed(p.fixed_k) || p.fixed_k > K))
+        return fail(ctx, K3XB_INVALID_STATE, "invalid fixed routing K");
+    if (p.mode == K3XB_ROUTING_ADAPTIVE && K != 16)
+        return fail(ctx, K3XB_INVALID_STATE, "adaptive routing requires natural Top-16");
+    ++ctx->stats.route_calls;
+    return launch_select_routing(ctx, scores, T, E, bias, K, p, ids, weights, selected, escalated, stats);
 }
 
 int k3xb_expert_major_plan(k3xb_ctx* ctx, const uint32_t* ids, const float* contrib, uint32_t T,

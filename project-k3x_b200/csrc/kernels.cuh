@@ -12,6 +12,9 @@ int launch_router_logits(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_
 int launch_topk(k3xb_ctx* ctx, const float* logits, const float* correction, uint32_t T,
                 uint32_t E, uint32_t K, uint32_t* ids, float* contrib, float* scores,
                 int32_t* status);
+int launch_select_routing(k3xb_ctx* ctx, const float* scores, uint32_t T, uint32_t E, const float* bias, uint32_t K,
+                          const k3xb_routing_policy& policy, uint32_t* ids, float* weights, uint32_t* selected,
+                          uint32_t* escalated, float* stats);
 int launch_plan(k3xb_ctx* ctx, const uint32_t* ids, const float* contrib, uint32_t T,
                 uint32_t K, uint32_t E, const k3xb_plan& plan);
 

@@ -331,6 +331,142 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(
     }
 }
 
+// select_routing (routing_policy.cpp:31-159), one CTA per token: the first
+// natural_k entries of the stable order (adjusted score desc, index asc) by
+// warp selection as in topk_kernel, then lane 0 runs the policy over at most
+// 32 slots in the reference's float order. logf/expf of the entropy are the
+// correctly rounded values (float of the double function).
+struct RoutingArgs {
+    int32_t mode;
+    uint32_t fixed_k, floor_k;
+    float mass_target, minimum_gap;
+};
+
+__device__ __forceinline__ bool routing_allowed(uint32_t k) {
+    return k == 4 || k == 6 || k == 8 || k == 12 || k == 16;
+}
+
+__device__ float routing_boundary(const float* probs, uint32_t n, uint32_t k) {
+    if (k >= n) return 1.0f;
+    const float gap = fmaxf(0.0f, __fsub_rn(probs[k - 1], probs[k]));
+    return __fdiv_rn(gap, fmaxf(probs[0], FLT_MIN));
+}
+
+__device__ uint32_t routing_adaptive(const float* probs, uint32_t n, float support, const RoutingArgs& a,
+                                     uint32_t floor_k) {
+    const float eps = 1.0e-5f;
+    float cumulative = 0.0f;
+    for (uint32_t slot = 0; slot < n; ++slot) {
+        cumulative = __fadd_rn(cumulative, probs[slot]);
+        const uint32_t k = slot + 1;
+        if (!routing_allowed(k) || k < floor_k) continue;
+        const float confidence = routing_boundary(probs, n, k);
+        if (__fadd_rn(cumulative, eps) >= a.mass_target && __fadd_rn(static_cast<float>(k), eps) >= support &&
+            __fadd_rn(confidence, eps) >= a.minimum_gap)
+            return k;
+    }
+    return n;
+}
+
+__global__ void __launch_bounds__(kTopkThreads) select_routing_kernel(
+    const float* __restrict__ scores, const float* __restrict__ bias, uint32_t T, uint32_t E, uint32_t K,
+    RoutingArgs args, uint32_t* __restrict__ ids, float* __restrict__ weights, uint32_t* __restrict__ selected,
+    uint32_t* __restrict__ escalated, float* __restrict__ stats, int32_t* __restrict__ status) {
+    __shared__ float s_score[32 * kMaxPerLane], s_adj[32 * kMaxPerLane];
+    __shared__ float sel_score[32];
+    __shared__ uint32_t sel_id[32];
+    const uint32_t token = blockIdx.x, tid = threadIdx.x, lane = tid % 32;
+    if (token >= T) return;
+    const float* sc = scores + static_cast<size_t>(token) * E;
+    int bad = 0;
+    for (uint32_t e = tid; e < E; e += blockDim.x) {
+        const float x = sc[e], b = bias[e];
+        const float adj = __fadd_rn(x, b);
+        bad |= !isfinite(x) || x < 0.0f || x > 1.0f || !isfinite(b) || !isfinite(adj);
+        s_score[e] = x;
+        s_adj[e] = adj;
+    }
+    if (__syncthreads_or(bad)) {
+        if (tid == 0) atomicExch(status, K3XB_INVALID_STATE);
+        return;
+    }
+    if (tid >= 32) return;
+    float adj[kMaxPerLane];
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+        const uint32_t e = lane + 32u * i;
+        adj[i] = e < E ? s_adj[e] : -INFINITY;
+    }
+    uint32_t taken = 0;
+    for (uint32_t slot = 0; slot < K; ++slot) {
+        float bv = -INFINITY;
+        uint32_t bi = 0xffffffffu;
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) {
+            const uint32_t e = lane + 32u * i;
+            if (e < E && !(taken >> i & 1u)) {
+                if (bi == 0xffffffffu || adj[i] > bv) { bv = adj[i]; bi = e; }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            const bool better = (oi != 0xffffffffu) && (bi == 0xffffffffu || ov > bv || (ov == bv && oi < bi));
+            if (better) { bv = ov; bi = oi; }
+        }
+        if ((bi % 32) == lane) taken |= 1u << (bi / 32);
+        if (lane == 0) { sel_score[slot] = s_score[bi]; sel_id[slot] = bi; }
+    }
+    __syncwarp();
+    if (lane != 0) return;
+    float denom = 0.0f;
+    for (uint32_t slot = 0; slot < K; ++slot) denom = __fadd_rn(denom, sel_score[slot]);
+    if (!isfinite(denom) || denom <= 0.0f) {
+        atomicExch(status, K3XB_INVALID_STATE);
+        return;
+    }
+    float probs[32];
+    float entropy = 0.0f;
+    for (uint32_t slot = 0; slot < K; ++slot) {
+        probs[slot] = __fdiv_rn(sel_score[slot], denom);
+        if (probs[slot] > 0.0f)
+            entropy = __fsub_rn(entropy, __fmul_rn(probs[slot], static_cast<float>(log(static_cast<double>(probs[slot])))));
+    }
+    const float support = static_cast<float>(exp(static_cast<double>(entropy)));
+    uint32_t chosen = K, unfloored = K;
+    if (args.mode == K3XB_ROUTING_FIXED) {
+        unfloored = args.fixed_k;
+        chosen = max(args.fixed_k, args.floor_k);
+    } else if (args.mode == K3XB_ROUTING_ADAPTIVE) {
+        unfloored = routing_adaptive(probs, K, support, args, 0);
+        chosen = routing_adaptive(probs, K, support, args, args.floor_k);
+    }
+    float mass = 0.0f, sel = 0.0f;
+    for (uint32_t slot = 0; slot < chosen; ++slot) {
+        mass = __fadd_rn(mass, probs[slot]);
+        sel = __fadd_rn(sel, sel_score[slot]);
+    }
+    if (!isfinite(sel) || sel <= 0.0f) {
+        atomicExch(status, K3XB_INVALID_STATE);
+        return;
+    }
+    const size_t o = static_cast<size_t>(token) * K;
+    for (uint32_t slot = 0; slot < K; ++slot) {
+        ids[o + slot] = slot < chosen ? sel_id[slot] : 0xffffffffu;
+        weights[o + slot] = slot < chosen ? __fdiv_rn(sel_score[slot], sel) : 0.0f;
+    }
+    selected[token] = chosen;
+    if (escalated) escalated[token] = chosen > unfloored ? 1u : 0u;
+    if (stats) {
+        float* st = stats + static_cast<size_t>(token) * 4;
+        st[0] = K == 1 ? 0.0f : __fdiv_rn(entropy, static_cast<float>(log(static_cast<double>(K))));
+        st[1] = support;
+        st[2] = mass;
+        st[3] = routing_boundary(probs, K, chosen);
+    }
+}
+
 // build_expert_major_plan (expert_major.cpp:10-54) in one CTA. A bitmap
 // bits[e][t/32] marks which tokens chose expert e; the in-group index of
 // (t, e) is the number of set bits below t, which reproduces the
@@ -472,6 +608,17 @@ int launch_topk(k3xb_ctx* ctx, const float* logits, const float* correction, uin
     if (E > 32u * kMaxPerLane || K == 0 || K > E || K > 32)
         return fail(ctx, K3XB_INVALID_EXTENT, "route: need 0 < top_k <= min(32, experts) and experts <= 1024");
     topk_kernel<<<T, kTopkThreads, 0, ctx->stream>>>(logits, correction, T, E, K, ids, contrib, scores, status);
+    K3XB_LAUNCHED(ctx);
+    return K3XB_OK;
+}
+
+int launch_select_routing(k3xb_ctx* ctx, const float* scores, uint32_t T, uint32_t E, const float* bias, uint32_t K,
+                          const k3xb_routing_policy& policy, uint32_t* ids, float* weights, uint32_t* selected,
+                          uint32_t* escalated, float* stats) {
+    const RoutingArgs args{policy.mode, policy.fixed_k, policy.quality_floor_k, policy.mass_target,
+                           policy.minimum_gap};
+    select_routing_kernel<<<T, kTopkThreads, 0, ctx->stream>>>(scores, bias, T, E, K, args, ids, weights, selected,
+                                                               escalated, stats, ctx->status_word);
     K3XB_LAUNCHED(ctx);
     return K3XB_OK;
 }

@@ -83,6 +83,14 @@ class VerifyIO(C.Structure):
         (n, C.c_void_p) for n in ("logits", "accepted", "committed", "committed_count")]
 
 
+class RoutingPolicy(C.Structure):
+    _fields_ = [("mode", C.c_int32), ("fixed_k", C.c_uint32), ("mass_target", C.c_float),
+                ("minimum_gap", C.c_float), ("quality_floor_k", C.c_uint32)]
+
+
+ROUTING_NATURAL, ROUTING_FIXED, ROUTING_ADAPTIVE = 0, 1, 2
+
+
 class Stats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in (
         "kernel_launches", "route_calls", "moe_layer_calls", "moe_layer_experts", "kda_calls",
@@ -109,6 +117,7 @@ def library() -> C.CDLL:
             "k3xb_get_stats": [vp, C.POINTER(Stats)],
             "k3xb_route": [vp, vp, u32, u32, vp, vp, u32, u32, vp, vp, vp],
             "k3xb_expert_major_plan": [vp, vp, vp, u32, u32, u32, C.POINTER(Plan)],
+            "k3xb_select_routing": [vp, vp, u32, u32, vp, u32, C.POINTER(RoutingPolicy), vp, vp, vp, vp, vp],
             "k3xb_moe_layer_forward": [vp, C.POINTER(MoeLayer), vp, u32, vp, vp, vp],
             "k3xb_moe_layer_forward_host": [vp, C.POINTER(MoeLayer), vp, u32, vp, vp, vp],
             "k3xb_moe_experts": [vp, C.POINTER(MoeLayer), vp, u32, C.POINTER(Plan), vp],
@@ -242,6 +251,15 @@ class Context:
         com = (C.c_int32 * S)(*[int(x) for x in commit_node])
         self._check(self.lib.k3xb_kda_commit(self.h, _p(state), par, N, S, heads, d, _p(q), _p(k), _p(v),
                                              _p(log_decay), _p(beta), com, _p(state_out)), "kda_commit")
+
+    def select_routing(self, scores, bias, natural_k, ids, weights, selected, escalated=None, stats=None,
+                       mode=ROUTING_NATURAL, fixed_k=0, mass_target=0.9, minimum_gap=0.0, quality_floor_k=0):
+        """select_routing (routing_policy.cpp:31-159) for scores [T][E]."""
+        T, E = scores.shape
+        pol = RoutingPolicy(mode, fixed_k, mass_target, minimum_gap, quality_floor_k)
+        self._check(self.lib.k3xb_select_routing(self.h, _p(scores), T, E, _p(bias), natural_k, C.byref(pol),
+                                                 _p(ids), _p(weights), _p(selected), _p(escalated), _p(stats)),
+                    "select_routing")
 
     # ---- full KDA block and the layer ----------------------------------------
     def kda_trace_bytes(self, kda: "KdaLayer", nodes, sequences):

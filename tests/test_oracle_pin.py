@@ -405,3 +405,74 @@ def test_kda_block_tree_on_a_chain_is_the_block(rs):
     c = rs.kda_block_commit(w, x, np.arange(-1, N - 1), N - 1, conv, rec)
     for u, v in zip(c, st):
         np.testing.assert_array_equal(u, v)
+
+
+# ------------------------------------------------------ routing policy ----
+
+def _same_routing(a, b):
+    assert a[0] == b[0]
+    if a[0]:
+        return
+    x, y = a[1], b[1]
+    for k in ("full_order", "expert_ids", "weights"):
+        np.testing.assert_array_equal(x[k], y[k])
+    for k in ("selected_k", "escalated", "normalized_entropy", "support", "mass", "boundary"):
+        assert x[k] == y[k], k
+
+
+@pytest.mark.parametrize("mode,kw", [
+    (0, {}), (0, dict(quality_floor_k=16)),
+    (1, dict(fixed_k=4)), (1, dict(fixed_k=8, quality_floor_k=12)),
+    (2, dict(mass_target=0.75, minimum_gap=0.1)), (2, dict(mass_target=0.9, quality_floor_k=12)),
+    (2, dict(mass_target=0.5, minimum_gap=0.0)),
+])
+def test_select_routing_matches_reference(rs, ref, mode, kw):
+    """select_routing (routing_policy.cpp:31-159): restatement == reference
+    build, bit for bit, on random sigmoid scores with ties and biases."""
+    g = np.random.default_rng(100 + mode)
+    for trial in range(40):
+        E = int(g.choice([16, 32, 64, 384]))
+        scores = (1 / (1 + np.exp(-g.normal(0, 2, size=E)))).astype(np.float32)
+        if trial % 4 == 0:   # exact ties broken by index
+            scores[: E // 2] = scores[0]
+        bias = (g.normal(0, 0.05, size=E) * (trial % 3 != 0)).astype(np.float32)
+        K = 16 if mode == 2 else int(g.choice([4, 8, 16]))
+        _same_routing(rs.select_routing(scores, bias, K, mode=mode, **kw),
+                      ref.select_routing(scores, bias, K, mode=mode, **kw))
+
+
+def test_select_routing_reference_cases(rs):
+    """The cases of the reference's test_routing_policy.cpp, on the restatement."""
+    close = lambda a, b: abs(a - b) <= 1e-6
+    s = np.array([0.8, 0.8, 0.4, 0.7, 0.2, 0.1], np.float32)
+    b = np.array([0, 0, 0.5, 0, 0, 0], np.float32)
+    st, d = rs.select_routing(s, b, 4)
+    assert st == 0 and d["full_order"].tolist() == [2, 0, 1, 3, 4, 5] and d["expert_ids"].tolist() == [2, 0, 1, 3]
+    assert all(close(w, v) for w, v in zip(d["weights"], np.float32([0.4, 0.8, 0.8, 0.7]) / np.float32(2.7)))
+    assert close(d["mass"], 1.0)
+    st, d = rs.select_routing(s, b, 4, quality_floor_k=16)
+    assert st == 0 and d["selected_k"] == 4 and not d["escalated"]
+    desc = (1 - np.arange(16) * 0.04).astype(np.float32)
+    zero = np.zeros(16, np.float32)
+    st, d = rs.select_routing(desc, zero, 16, mode=1, fixed_k=4)
+    assert st == 0 and d["selected_k"] == 4 and d["expert_ids"].tolist() == [0, 1, 2, 3]
+    assert close(float(np.sum(d["weights"], dtype=np.float32)), 1.0) and d["mass"] < 1.0
+    eight = np.full(16, 1e-9, np.float32)
+    eight[:8] = 1.0
+    st, d = rs.select_routing(eight, zero, 16, mode=2, mass_target=0.75, minimum_gap=0.1)
+    assert st == 0 and d["selected_k"] == 8 and d["support"] <= 8.0001 and d["boundary"] > 0.9
+    st, d = rs.select_routing(eight, zero, 16, mode=2, mass_target=0.75, minimum_gap=0.0, quality_floor_k=12)
+    assert st == 0 and d["selected_k"] == 12 and d["escalated"]
+    weak = np.full(16, 1e-9, np.float32)
+    weak[:8] = 1.0
+    weak[8:13] = 0.1
+    st, d = rs.select_routing(weak, zero, 16, mode=2, mass_target=0.8, minimum_gap=0.2)
+    assert st == 0 and d["selected_k"] == 16
+    assert rs.select_routing(desc, zero, 16, mode=1, fixed_k=2)[0] != 0
+    assert rs.select_routing(desc, zero, 12, mode=1, fixed_k=16)[0] != 0
+    assert rs.select_routing(desc, zero, 16, mode=2, mass_target=float("nan"))[0] != 0
+    bad = desc.copy()
+    bad[0] = 1.1
+    assert rs.select_routing(bad, zero, 16)[0] != 0
+    assert rs.select_routing(zero, zero, 16)[0] != 0
+    assert rs.select_routing(desc, zero, 16, mode=2, quality_floor_k=5)[0] != 0
