@@ -72,6 +72,13 @@ typedef struct {
     uint64_t peak_scratch_bytes;
     uint64_t h2d_bytes;
     uint64_t d2h_bytes;
+    /* resident weights (k3xb_acquire_weight / k3xb_acquire_expert_stack) */
+    uint64_t weight_cache_hits;
+    uint64_t weight_cache_misses;
+    uint64_t weight_cache_bypasses;
+    uint64_t resident_weight_bytes;
+    uint64_t peak_resident_weight_bytes;
+    uint64_t weight_h2d_bytes;
 } k3xb_stats;
 int k3xb_get_stats(const k3xb_ctx* ctx, k3xb_stats* out);
 
@@ -217,6 +224,86 @@ int k3xb_moe_layer_forward_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer,
 int k3xb_moe_experts(k3xb_ctx* ctx, const k3xb_moe_layer* layer,
                      const float* hidden, uint32_t tokens,
                      const k3xb_plan* plan, float* slot_out);
+
+/* ---- resident weights ------------------------------------------------------ */
+/* Device copies of HOST weights, kept by the context and keyed by tensor id:
+ * the reference's ResidentWeightTable (runtime/cuda/resident_weights.cuh:
+ * 17-47, acquire in resident_weights.cu:104-166), which its CUDA backend
+ * fills from the host views Bf16WeightView / Mxfp4WeightView
+ * (backend.hpp:131-158). Same rules: a payload that does not match its key
+ * or a tensor id seen with another shape is K3XB_INVALID_EXTENT; a held key
+ * is a HIT (no copy); a new entry that would pass the capacity is a BYPASS
+ * (K3XB_OK, null pointers, nothing kept); otherwise ADMITTED. In addition,
+ * MXFP4 scales are checked at admission (0xFF -> K3XB_INVALID_MXFP4) and
+ * MXFP4 entries with rows and cols multiples of 128 also hold the scales in
+ * the tcgen05 layout (scales_tc). Copies are issued on the context's stream;
+ * the host arrays may be reused when the call returns. */
+enum {
+    K3XB_WEIGHT_F32 = 0,           /* values [rows][cols] float */
+    K3XB_WEIGHT_BF16 = 1,          /* values [rows][cols] bf16 words */
+    K3XB_WEIGHT_MXFP4 = 2,         /* packed [rows][cols/2] + scales [rows][cols/group] */
+    K3XB_WEIGHT_EXPERT_STACK = 3   /* k3xb_acquire_expert_stack */
+};
+enum { K3XB_RESIDENT_HIT = 0, K3XB_RESIDENT_ADMITTED = 1, K3XB_RESIDENT_BYPASS = 2 };
+
+typedef struct {
+    int32_t disposition;           /* K3XB_RESIDENT_* */
+    const void* primary;           /* values / MXFP4 packed (device) */
+    const void* secondary;         /* MXFP4 scales (device), else NULL */
+    const void* scales_tc;         /* MXFP4 scales in the tcgen05 layout, or NULL */
+    uint64_t uploaded_bytes;       /* host->device bytes of this call */
+} k3xb_resident;
+
+/* Bytes the table may hold (default: no bound but device memory). Entries
+ * already held stay. */
+int k3xb_set_resident_capacity(k3xb_ctx* ctx, uint64_t bytes);
+/* primary_bytes / secondary_bytes must be what (representation, rows,
+ * cols, group_size) imply: f32 rows*cols*4, bf16 rows*cols*2 (group 0, no
+ * secondary), MXFP4 rows*cols/2 and rows*cols/group_size. */
+int k3xb_acquire_weight(k3xb_ctx* ctx, uint64_t tensor_id, int32_t representation,
+                        uint64_t rows, uint64_t cols, uint64_t group_size,
+                        const void* primary, size_t primary_bytes,
+                        const void* secondary, size_t secondary_bytes,
+                        k3xb_resident* out);
+
+/* One expert's HOST MXFP4 arrays (gate/up [I][H/2] + [I][H/32], down
+ * [H][I/2] + [H][I/32]): an element of the Mxfp4MlpView list the
+ * reference's MoE methods take (backend.hpp:315-319). */
+typedef struct {
+    const uint8_t* gate_packed;
+    const uint8_t* gate_scales;
+    const uint8_t* up_packed;
+    const uint8_t* up_scales;
+    const uint8_t* down_packed;
+    const uint8_t* down_scales;
+} k3xb_mxfp4_expert_host;
+
+/* Device pointers of a resident expert stack, ready for the expert fields
+ * of k3xb_moe_layer (including the *_scales_tc copies). */
+typedef struct {
+    int32_t disposition;           /* K3XB_RESIDENT_* */
+    const uint8_t* gate_packed;
+    const uint8_t* gate_scales;
+    const uint8_t* up_packed;
+    const uint8_t* up_scales;
+    const uint8_t* down_packed;
+    const uint8_t* down_scales;
+    const uint8_t* gate_scales_tc;
+    const uint8_t* up_scales_tc;
+    const uint8_t* down_scales_tc;
+    uint64_t uploaded_bytes;
+} k3xb_resident_stack;
+
+/* Uploads `experts` experts into one resident stack in the stacked layout
+ * of k3xb_moe_layer, keyed by stack_id (same table, capacity and
+ * counters; hidden and inter multiples of 128). A BYPASS leaves the
+ * pointers NULL. */
+int k3xb_acquire_expert_stack(k3xb_ctx* ctx, uint64_t stack_id, uint32_t experts,
+                              uint32_t hidden, uint32_t inter,
+                              const k3xb_mxfp4_expert_host* host,
+                              k3xb_resident_stack* out);
+/* Frees every resident entry (pointers handed out before become invalid). */
+int k3xb_release_resident(k3xb_ctx* ctx);
 
 /* ---- (d) KDA recurrence -------------------------------------------------- */
 /* official_kda.cpp:319-369 applied over a draft tree for S sequences that

@@ -37,7 +37,8 @@ def _stale(target, deps):
 
 def build(verbose: bool = False, extra=()) -> str:
     os.makedirs(OBJ_DIR, exist_ok=True)
-    headers = glob.glob(os.path.join(CSRC, "*.cuh")) + [os.path.join(ROOT, "include", "k3xb.h")]
+    headers = (glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.hpp")) +
+               [os.path.join(ROOT, "include", "k3xb.h")])
     objs = []
     for src in sorted(glob.glob(os.path.join(CSRC, "*.cu"))):
         obj = os.path.join(OBJ_DIR, os.path.basename(src) + ".o")

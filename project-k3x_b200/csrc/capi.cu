@@ -192,6 +192,7 @@ int k3xb_destroy(k3xb_ctx* ctx) {
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->status_word) cudaFree(ctx->status_word);
     release_mxf4_resources(ctx);
+    release_resident(ctx);
     release_ep(ctx);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     if (ctx->side_stream) cudaStreamDestroy(ctx->side_stream);
@@ -228,6 +229,7 @@ int k3xb_sync(k3xb_ctx* ctx) {
 int k3xb_get_stats(const k3xb_ctx* ctx, k3xb_stats* out) {
     if (!ctx || !out) return K3XB_INVALID_EXTENT;
     *out = ctx->stats;
+    resident_stats(ctx, out);
     return K3XB_OK;
 }
 

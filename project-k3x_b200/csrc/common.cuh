@@ -23,6 +23,7 @@ struct k3xb_ctx {
     void* mxf4_scratch = nullptr;     // MXF4-engine region inside `scratch`
     void* mxf4_state = nullptr;       // MXF4-engine resources (tensor maps, attributes)
     void* ep_state = nullptr;         // expert parallelism: NCCL communicator
+    void* resident = nullptr;         // resident weight table (resident.cu)
 };
 
 namespace k3xb {

@@ -94,7 +94,29 @@ ROUTING_NATURAL, ROUTING_FIXED, ROUTING_ADAPTIVE = 0, 1, 2
 class Stats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in (
         "kernel_launches", "route_calls", "moe_layer_calls", "moe_layer_experts", "kda_calls",
-        "accept_calls", "scratch_bytes", "peak_scratch_bytes", "h2d_bytes", "d2h_bytes")]
+        "accept_calls", "scratch_bytes", "peak_scratch_bytes", "h2d_bytes", "d2h_bytes",
+        "weight_cache_hits", "weight_cache_misses", "weight_cache_bypasses", "resident_weight_bytes",
+        "peak_resident_weight_bytes", "weight_h2d_bytes")]
+
+
+WEIGHT_F32, WEIGHT_BF16, WEIGHT_MXFP4, WEIGHT_EXPERT_STACK = 0, 1, 2, 3
+RESIDENT_HIT, RESIDENT_ADMITTED, RESIDENT_BYPASS = 0, 1, 2
+
+
+class Resident(C.Structure):
+    _fields_ = [("disposition", C.c_int32), ("primary", C.c_void_p), ("secondary", C.c_void_p),
+                ("scales_tc", C.c_void_p), ("uploaded_bytes", C.c_uint64)]
+
+
+class ExpertHost(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("gate_packed", "gate_scales", "up_packed", "up_scales",
+                                          "down_packed", "down_scales")]
+
+
+class ResidentStack(C.Structure):
+    _fields_ = [("disposition", C.c_int32)] + [(n, C.c_void_p) for n in (
+        "gate_packed", "gate_scales", "up_packed", "up_scales", "down_packed", "down_scales",
+        "gate_scales_tc", "up_scales_tc", "down_scales_tc")] + [("uploaded_bytes", C.c_uint64)]
 
 
 _lib = None
@@ -140,6 +162,11 @@ def library() -> C.CDLL:
             "k3xb_ep_init": [vp, vp, C.c_int32, C.c_int32],
             "k3xb_ep_finalize": [vp],
             "k3xb_ep_moe_layer_forward": [vp, C.POINTER(MoeLayer), u32, vp, u32, vp, vp, vp],
+            "k3xb_set_resident_capacity": [vp, u64],
+            "k3xb_acquire_weight": [vp, u64, C.c_int32, u64, u64, u64, vp, sz, vp, sz, C.POINTER(Resident)],
+            "k3xb_acquire_expert_stack": [vp, u64, u32, u32, u32, C.POINTER(ExpertHost),
+                                          C.POINTER(ResidentStack)],
+            "k3xb_release_resident": [vp],
         }
         for name, args in sigs.items():
             fn = getattr(lib, name)
@@ -350,6 +377,39 @@ class Context:
         self._check(self.lib.k3xb_prepare_mxfp4_scales(self.h, _p(scales), rows, cols, _p(out)),
                     "prepare_mxfp4_scales")
 
+    # ---- resident weights (host arrays -> device copies keyed by tensor id) ----
+    def set_resident_capacity(self, nbytes: int):
+        self._check(self.lib.k3xb_set_resident_capacity(self.h, nbytes), "set_resident_capacity")
+
+    def acquire_weight(self, tensor_id, representation, rows, cols, group_size, primary, secondary=None):
+        """primary / secondary are HOST numpy arrays; returns a Resident."""
+        import numpy as np
+        primary = np.ascontiguousarray(primary)
+        sec = None if secondary is None else np.ascontiguousarray(secondary)
+        out = Resident()
+        self._check(self.lib.k3xb_acquire_weight(
+            self.h, tensor_id, representation, rows, cols, group_size, primary.ctypes.data, primary.nbytes,
+            None if sec is None else sec.ctypes.data, 0 if sec is None else sec.nbytes, C.byref(out)),
+            "acquire_weight")
+        return out
+
+    def acquire_expert_stack(self, stack_id, hidden, inter, experts):
+        """experts: list of dicts of HOST uint8 arrays (gate_packed, gate_scales,
+        up_packed, up_scales, down_packed, down_scales). Returns a ResidentStack."""
+        import numpy as np
+        keep = [{k: np.ascontiguousarray(v) for k, v in e.items()} for e in experts]
+        views = (ExpertHost * len(keep))()
+        for i, e in enumerate(keep):
+            for name, _ in ExpertHost._fields_:
+                setattr(views[i], name, e[name].ctypes.data)
+        out = ResidentStack()
+        self._check(self.lib.k3xb_acquire_expert_stack(self.h, stack_id, len(keep), hidden, inter, views,
+                                                       C.byref(out)), "acquire_expert_stack")
+        return out
+
+    def release_resident(self):
+        self._check(self.lib.k3xb_release_resident(self.h), "release_resident")
+
     def prepare_layer_scales(self, w: dict):
         """Adds tcgen05-layout copies of the three expert scale arrays to a
         layer dict (one-time, for resident weights)."""
@@ -382,6 +442,19 @@ def moe_layer_desc(w: dict, engine=ENGINE_SIMT, act_terms=6) -> MoeLayer:
     L.situ_linear_beta = w.get("situ_linear_beta", 0.0)
     L.engine = engine
     L.act_terms = act_terms
+    return L
+
+
+def stack_layer_desc(stack: ResidentStack, w: dict, engine=ENGINE_MXF4, act_terms=6) -> MoeLayer:
+    """moe_layer_desc with the expert arrays taken from a resident stack
+    (k3xb_acquire_expert_stack); router, correction and the shared expert
+    still come from the dict."""
+    if stack.disposition == RESIDENT_BYPASS:
+        raise K3xbError(INVALID_STATE, "expert stack was not admitted (resident capacity)")
+    L = moe_layer_desc(w, engine=engine, act_terms=act_terms)
+    for name, _ in ResidentStack._fields_:
+        if name not in ("disposition", "uploaded_bytes"):
+            setattr(L, name, getattr(stack, name))
     return L
 
 

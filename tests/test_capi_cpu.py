@@ -45,3 +45,26 @@ def test_null_context_rejected():
     lib = k3xb.library()
     assert lib.k3xb_sync(None) == k3xb.INVALID_EXTENT
     assert lib.k3xb_destroy(None) == k3xb.OK
+
+
+def test_resident_entry_points_marshal_and_reject_null_context():
+    """The ctypes structs of the resident-weight calls marshal (the same
+    code the GPU tests use) and a null context is refused before any CUDA
+    call."""
+    import ctypes as C
+
+    import numpy as np
+
+    import k3xb
+    lib = k3xb.library()
+    assert C.sizeof(k3xb.Stats) == 16 * 8
+    words = np.zeros((4, 8), np.uint16)
+    out = k3xb.Resident()
+    assert lib.k3xb_acquire_weight(None, 1, k3xb.WEIGHT_BF16, 4, 8, 0, words.ctypes.data, words.nbytes, None, 0,
+                                   C.byref(out)) == k3xb.INVALID_EXTENT
+    views = (k3xb.ExpertHost * 2)()
+    views[1].down_scales = words.ctypes.data
+    stack = k3xb.ResidentStack()
+    assert lib.k3xb_acquire_expert_stack(None, 1, 2, 128, 128, views, C.byref(stack)) == k3xb.INVALID_EXTENT
+    assert lib.k3xb_set_resident_capacity(None, 0) == k3xb.INVALID_EXTENT
+    assert lib.k3xb_release_resident(None) == k3xb.INVALID_EXTENT
