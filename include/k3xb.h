@@ -305,6 +305,21 @@ int k3xb_acquire_expert_stack(k3xb_ctx* ctx, uint64_t stack_id, uint32_t experts
 /* Frees every resident entry (pointers handed out before become invalid). */
 int k3xb_release_resident(k3xb_ctx* ctx);
 
+/* mxfp4_situ_mlp_grid (backend.hpp:357-363, CPU semantics
+ * backend_cpu.cpp:191-262) over a stack of experts: out[j][t][H] =
+ * expert_{expert_ids[j]}(inputs[t]) for j < n, t < tokens: gate/up MXFP4
+ * products, the layer's activation, down product rounded to bf16 as
+ * expert_ffn (official_moe.cpp:82-103) does (the reference backend's
+ * per-token methods return it unrounded, a difference inside their 2e-2
+ * CUDA tolerance). Only the dims, expert arrays, activation, act_terms and
+ * engine of `layer` are read; expert ids must be distinct (at most 32).
+ * HOST inputs [tokens][H], out [n][tokens][H] and expert_ids; returns after
+ * the results are on the host. */
+int k3xb_expert_grid_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer,
+                          const uint32_t* expert_ids, uint32_t n,
+                          const float* inputs_host, uint32_t tokens,
+                          float* out_host);
+
 /* ---- (d) KDA recurrence -------------------------------------------------- */
 /* official_kda.cpp:319-369 applied over a draft tree for S sequences that
  * share the topology: node n continues from parent[n]'s state
@@ -380,6 +395,18 @@ int k3xb_kda_block_commit(k3xb_ctx* ctx, const k3xb_kda_layer* w,
                           const int32_t* commit_node, const uint16_t* conv,
                           const float* recurrent, uint16_t* conv_out,
                           float* recurrent_out);
+
+/* official_kda (backend.hpp:402-408) in its host-roundtrip state mode
+ * (OfficialKdaStateMode::host_roundtrip): one sequence's `tokens`
+ * positions of HOST x [tokens][H] run as a chain through the KDA block;
+ * out [tokens][H] (HOST); the state after the last position replaces
+ * conv [3][w-1][P] (bf16 words: the q, k, v histories of
+ * OfficialKdaCudaStateView, oldest row first) and recurrent [h][d][d]
+ * (V-first). Weights are device arrays (e.g. resident, k3xb_acquire_weight).
+ * Returns after the results are on the host. */
+int k3xb_kda_block_host(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t hidden,
+                        const float* x_host, uint32_t tokens, uint16_t* conv_host,
+                        float* recurrent_host, float* out_host);
 
 /* prepare_official_moe_input (official_moe.cpp:156-209) and the layer's
  * input path (official_layer.cpp:159-172): attention_residual of the two

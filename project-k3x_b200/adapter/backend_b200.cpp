@@ -1,0 +1,457 @@
+// backend_b200.cpp — B200Backend: k3x::ComputeBackend over the C ABI of
+// libk3xb (see backend_b200.hpp for the method split).
+#include "backend_b200.hpp"
+
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <unordered_set>
+#include <utility>
+#include <vector>
+
+namespace k3x {
+namespace {
+
+// The C ABI's status values are the values of k3x::ErrorCode
+// (runtime/include/k3x/status.hpp:9-30), so a status converts by value.
+static_assert(static_cast<int>(ErrorCode::ok) == K3XB_OK);
+static_assert(static_cast<int>(ErrorCode::invalid_extent) == K3XB_INVALID_EXTENT);
+static_assert(static_cast<int>(ErrorCode::invalid_mxfp4) == K3XB_INVALID_MXFP4);
+static_assert(static_cast<int>(ErrorCode::invalid_state) == K3XB_INVALID_STATE);
+static_assert(static_cast<int>(ErrorCode::backend_unavailable) == K3XB_BACKEND_UNAVAILABLE);
+static_assert(static_cast<int>(ErrorCode::unsupported_architecture) == K3XB_UNSUPPORTED_ARCHITECTURE);
+
+template <class T>
+Result<T> unavailable(const char* what) {
+    return Result<T>::failure(ErrorCode::backend_unavailable, what);
+}
+
+const std::uint8_t* bytes_of(std::span<const std::byte> s) {
+    return reinterpret_cast<const std::uint8_t*>(s.data());
+}
+
+// One MXFP4 matrix of `rows` x `cols`, group 32 (the engine's block size).
+bool valid_matrix(const Mxfp4WeightView& w, std::size_t rows, std::size_t cols) {
+    return w.tensor_id != 0 && w.rows == rows && w.cols == cols && w.group_size == 32 && cols % 32 == 0 &&
+           w.packed.size() == rows * cols / 2 && w.scales.size() == rows * cols / 32;
+}
+
+// Same dimensions for every expert, as the reference's grid checks
+// (backend_cpu.cpp:215-234): gate/up [I][H], down [H][I].
+bool valid_experts(std::span<const Mxfp4MlpView> experts, std::size_t* H, std::size_t* I) {
+    if (experts.empty()) return false;
+    *H = experts.front().gate.cols;
+    *I = experts.front().gate.rows;
+    for (const auto& e : experts)
+        if (!valid_matrix(e.gate, *I, *H) || !valid_matrix(e.up, *I, *H) || !valid_matrix(e.down, *H, *I))
+            return false;
+    return *H > 0 && *I > 0;
+}
+
+bool valid_activation(float beta, std::optional<float> linear) {
+    return std::isfinite(beta) && beta > 0.0F && (!linear || (std::isfinite(*linear) && *linear > 0.0F));
+}
+
+class B200Backend final : public ComputeBackend {
+public:
+    B200Backend(const BackendOptions& options, k3xb_ctx* ctx, std::unique_ptr<ComputeBackend> rest)
+        : options_(options), ctx_(ctx), rest_(std::move(rest)) {
+        if (ctx_ && options_.cuda_weights == CudaWeightMode::resident && options_.cuda_resident_bytes)
+            k3xb_set_resident_capacity(ctx_, options_.cuda_resident_bytes);
+    }
+    ~B200Backend() override {
+        if (ctx_) k3xb_destroy(ctx_);
+    }
+    B200Backend(const B200Backend&) = delete;
+    B200Backend& operator=(const B200Backend&) = delete;
+
+    BackendKind kind() const noexcept override { return BackendKind::cuda_custom; }
+    const BackendOptions& options() const noexcept override { return options_; }
+    std::string_view device_name() const noexcept override { return "NVIDIA B200 (libk3xb, sm_100a)"; }
+
+    BackendRuntimeStats runtime_stats() const noexcept override {
+        BackendRuntimeStats r = rest_ ? rest_->runtime_stats() : BackendRuntimeStats{};
+        k3xb_stats s{};
+        if (ctx_ && k3xb_get_stats(ctx_, &s) == K3XB_OK) {
+            r.weight_cache_hits += s.weight_cache_hits;
+            r.weight_cache_misses += s.weight_cache_misses;
+            r.weight_cache_bypasses += s.weight_cache_bypasses;
+            r.resident_weight_bytes += s.resident_weight_bytes;
+            r.peak_resident_weight_bytes += s.peak_resident_weight_bytes;
+            r.weight_h2d_bytes += s.weight_h2d_bytes;
+            r.activation_h2d_bytes += s.h2d_bytes - s.weight_h2d_bytes;
+            r.device_to_host_bytes += s.d2h_bytes;
+            r.scratch_bytes += s.scratch_bytes;
+            r.peak_scratch_bytes += s.peak_scratch_bytes;
+        }
+        r.batched_expert_ffn_calls += grid_calls_;
+        r.batched_expert_ffn_tokens += grid_tokens_;
+        r.fused_moe_calls += moe_calls_;
+        r.official_kda_calls += kda_calls_;
+        return r;
+    }
+
+    BackendMemoryStats memory_stats() const noexcept override {
+        BackendMemoryStats m = rest_ ? rest_->memory_stats() : BackendMemoryStats{};
+        k3xb_stats s{};
+        if (ctx_ && k3xb_get_stats(ctx_, &s) == K3XB_OK) {
+            m.current_device_bytes += s.resident_weight_bytes + s.scratch_bytes;
+            m.peak_device_bytes += s.peak_resident_weight_bytes + s.peak_scratch_bytes;
+        }
+        return m;
+    }
+
+    // ---- not on the B200 path: the maintainer's other backend -------------
+    Result<std::vector<float>> dense_matvec(std::span<const float> input, DenseWeightView weight,
+                                            std::uint32_t layer, ProfilePhase phase) override {
+        if (!rest_) return unavailable<std::vector<float>>("dense_matvec is not on the B200 path");
+        return rest_->dense_matvec(input, weight, layer, phase);
+    }
+    Result<std::vector<float>> mxfp4_matvec(std::span<const float> input, Mxfp4WeightView weight,
+                                            std::uint32_t layer, ProfilePhase phase) override {
+        if (!rest_) return unavailable<std::vector<float>>("mxfp4_matvec is not on the B200 path");
+        return rest_->mxfp4_matvec(input, weight, layer, phase);
+    }
+    Result<std::vector<std::vector<float>>> dense_matvec_group(std::span<const float> input,
+                                                               std::span<const DenseWeightView> weights,
+                                                               std::uint32_t layer, ProfilePhase phase) override {
+        if (!rest_) return unavailable<std::vector<std::vector<float>>>("dense_matvec_group is not on the B200 path");
+        return rest_->dense_matvec_group(input, weights, layer, phase);
+    }
+    Result<std::vector<std::vector<float>>> mxfp4_matvec_group(std::span<const float> input,
+                                                               std::span<const Mxfp4WeightView> weights,
+                                                               std::uint32_t layer, ProfilePhase phase) override {
+        if (!rest_) return unavailable<std::vector<std::vector<float>>>("mxfp4_matvec_group is not on the B200 path");
+        return rest_->mxfp4_matvec_group(input, weights, layer, phase);
+    }
+    Result<std::vector<float>> dense_situ_mlp(std::span<const float> input, DenseMlpView weights, float situ_beta,
+                                              std::optional<float> situ_linear, std::uint32_t layer,
+                                              ProfilePhase phase) override {
+        if (!rest_) return unavailable<std::vector<float>>("dense_situ_mlp is not on the B200 path");
+        return rest_->dense_situ_mlp(input, weights, situ_beta, situ_linear, layer, phase);
+    }
+    // The latent-space MoE of the reference's official/resident layers
+    // (routed_down / routed_norm / routed_up) is not the plain hidden-space
+    // MoE this library runs.
+    Result<ResidentMoeLayerResult> resident_mxfp4_moe_layer(std::span<const float> input, ResidentMoeLayerView w,
+                                                            std::span<const Mxfp4MlpView> experts,
+                                                            std::span<const float> contributions, float epsilon,
+                                                            float beta, std::optional<float> linear,
+                                                            std::uint32_t layer, ProfilePhase phase) override {
+        if (!rest_) return unavailable<ResidentMoeLayerResult>("latent MoE layer is not on the B200 path");
+        return rest_->resident_mxfp4_moe_layer(input, w, experts, contributions, epsilon, beta, linear, layer,
+                                               phase);
+    }
+    Result<OfficialMoeFfnResult> official_mxfp4_moe_ffn(std::span<const float> hidden, std::span<const float> prefix,
+                                                        OfficialMoeFfnView w, std::span<const Mxfp4MlpView> experts,
+                                                        std::span<const std::uint32_t> ids,
+                                                        std::span<const float> contributions, float epsilon,
+                                                        float beta, std::optional<float> linear,
+                                                        std::uint32_t layer, ProfilePhase phase) override {
+        if (!rest_) return unavailable<OfficialMoeFfnResult>("latent MoE FFN is not on the B200 path");
+        return rest_->official_mxfp4_moe_ffn(hidden, prefix, w, experts, ids, contributions, epsilon, beta, linear,
+                                             layer, phase);
+    }
+
+    // ---- expert FFNs on tcgen05 (k3xb_expert_grid_host) --------------------
+    Result<std::vector<std::vector<float>>> mxfp4_situ_mlp_group(std::span<const float> input,
+                                                                 std::span<const Mxfp4MlpView> experts,
+                                                                 float situ_beta, std::optional<float> situ_linear,
+                                                                 std::uint32_t, ProfilePhase) override {
+        std::size_t H = 0, I = 0;
+        if (!valid_experts(experts, &H, &I) || input.size() != H || !valid_activation(situ_beta, situ_linear))
+            return Result<std::vector<std::vector<float>>>::failure(ErrorCode::invalid_mxfp4);
+        std::vector<std::vector<float>> out;
+        out.reserve(experts.size());
+        for (const auto& e : experts) {
+            auto y = run_expert(e, H, I, input.data(), 1, situ_beta, situ_linear);
+            if (!y) return Result<std::vector<std::vector<float>>>::failure(y.error(), y.message());
+            out.push_back(std::move(y.value()));
+        }
+        return Result<std::vector<std::vector<float>>>::success(std::move(out));
+    }
+
+    Result<std::vector<std::vector<float>>> mxfp4_situ_mlp_batch(std::span<const float> inputs,
+                                                                 std::size_t batch_size, Mxfp4MlpView expert,
+                                                                 float situ_beta, std::optional<float> situ_linear,
+                                                                 std::uint32_t, ProfilePhase) override {
+        std::size_t H = 0, I = 0;
+        if (!batch_size || !valid_experts(std::span<const Mxfp4MlpView>(&expert, 1), &H, &I) ||
+            inputs.size() != batch_size * H || !valid_activation(situ_beta, situ_linear))
+            return Result<std::vector<std::vector<float>>>::failure(ErrorCode::invalid_mxfp4);
+        auto y = run_expert(expert, H, I, inputs.data(), batch_size, situ_beta, situ_linear);
+        if (!y) return Result<std::vector<std::vector<float>>>::failure(y.error(), y.message());
+        std::vector<std::vector<float>> out(batch_size);
+        for (std::size_t t = 0; t < batch_size; ++t)
+            out[t].assign(y.value().begin() + static_cast<std::ptrdiff_t>(t * H),
+                          y.value().begin() + static_cast<std::ptrdiff_t>((t + 1) * H));
+        return Result<std::vector<std::vector<float>>>::success(std::move(out));
+    }
+
+    // outputs[expert] = [token][H] (backend_cpu.cpp:241-262)
+    Result<std::vector<std::vector<float>>> mxfp4_situ_mlp_grid(std::span<const float> inputs,
+                                                                std::size_t token_count,
+                                                                std::span<const Mxfp4MlpView> experts,
+                                                                float situ_beta, std::optional<float> situ_linear,
+                                                                std::uint32_t, ProfilePhase) override {
+        std::size_t H = 0, I = 0;
+        if (!token_count || !valid_experts(experts, &H, &I) || inputs.size() != token_count * H ||
+            !valid_activation(situ_beta, situ_linear) || !distinct_ids(experts))
+            return Result<std::vector<std::vector<float>>>::failure(ErrorCode::invalid_mxfp4);
+        std::vector<std::vector<float>> out;
+        out.reserve(experts.size());
+        for (const auto& e : experts) {
+            auto y = run_expert(e, H, I, inputs.data(), token_count, situ_beta, situ_linear);
+            if (!y) return Result<std::vector<std::vector<float>>>::failure(y.error(), y.message());
+            out.push_back(std::move(y.value()));
+        }
+        return Result<std::vector<std::vector<float>>>::success(std::move(out));
+    }
+
+    // mixed = sum_slot contribution * y_slot in float, slot order
+    // (backend_cpu.cpp:266-303; official_moe.cpp:313-322).
+    Result<std::vector<float>> mxfp4_situ_moe(std::span<const float> input, std::span<const Mxfp4MlpView> experts,
+                                              std::span<const float> contributions, float situ_beta,
+                                              std::optional<float> situ_linear, std::uint32_t layer,
+                                              ProfilePhase phase) override {
+        if (experts.empty() || experts.size() != contributions.size())
+            return Result<std::vector<float>>::failure(ErrorCode::invalid_mxfp4);
+        for (const float c : contributions)
+            if (!std::isfinite(c)) return Result<std::vector<float>>::failure(ErrorCode::invalid_mxfp4);
+        auto ys = mxfp4_situ_mlp_group(input, experts, situ_beta, situ_linear, layer, phase);
+        if (!ys) return Result<std::vector<float>>::failure(ys.error(), ys.message());
+        ++moe_calls_;
+        return Result<std::vector<float>>::success(mix(ys.value(), contributions));
+    }
+
+    // Prefetch = upload the experts now (the resident stacks), keep the list
+    // for the _prepared call that follows.
+    Result<Mxfp4PrefetchToken> prefetch_mxfp4_situ_mlp_group(std::span<const Mxfp4MlpView> experts,
+                                                             std::uint64_t use_sequence, std::uint32_t,
+                                                             ProfilePhase) override {
+        std::size_t H = 0, I = 0;
+        if (!valid_experts(experts, &H, &I)) return Result<Mxfp4PrefetchToken>::failure(ErrorCode::invalid_mxfp4);
+        for (const auto& e : experts) {
+            k3xb_moe_layer L{};
+            if (auto st = stack_of(e, H, I, &L); st != ErrorCode::ok) return Result<Mxfp4PrefetchToken>::failure(st);
+        }
+        const std::uint64_t id = ++next_token_;
+        prefetched_[id] = std::vector<Mxfp4MlpView>(experts.begin(), experts.end());
+        return Result<Mxfp4PrefetchToken>::success({id, use_sequence});
+    }
+
+    Result<std::vector<std::vector<float>>> mxfp4_situ_mlp_group_prepared(std::span<const float> input,
+                                                                          Mxfp4PrefetchToken token, float beta,
+                                                                          std::optional<float> linear,
+                                                                          std::uint32_t layer,
+                                                                          ProfilePhase phase) override {
+        auto it = prefetched_.find(token.value);
+        if (it == prefetched_.end())
+            return Result<std::vector<std::vector<float>>>::failure(ErrorCode::invalid_state, "unknown prefetch token");
+        const std::vector<Mxfp4MlpView> experts = std::move(it->second);
+        prefetched_.erase(it);
+        return mxfp4_situ_mlp_group(input, experts, beta, linear, layer, phase);
+    }
+
+    Result<std::vector<float>> mxfp4_situ_moe_prepared(std::span<const float> input, Mxfp4PrefetchToken token,
+                                                       std::span<const float> contributions, float beta,
+                                                       std::optional<float> linear, std::uint32_t layer,
+                                                       ProfilePhase phase) override {
+        auto it = prefetched_.find(token.value);
+        if (it == prefetched_.end())
+            return Result<std::vector<float>>::failure(ErrorCode::invalid_state, "unknown prefetch token");
+        const std::vector<Mxfp4MlpView> experts = std::move(it->second);
+        prefetched_.erase(it);
+        return mxfp4_situ_moe(input, experts, contributions, beta, linear, layer, phase);
+    }
+
+    // ---- KDA block (k3xb_kda_block_host) -----------------------------------
+    Result<OfficialKdaCudaResult> official_kda(std::span<const float> input, OfficialKdaCudaView w,
+                                               OfficialKdaCudaStateView state, OfficialKdaCudaConfig config,
+                                               std::uint32_t layer, ProfilePhase phase,
+                                               OfficialKdaStateControl control) override {
+        if (control.mode != OfficialKdaStateMode::host_roundtrip) {
+            // device-held state between calls is the verify step's job here
+            if (!rest_) return unavailable<OfficialKdaCudaResult>("device KDA state modes are not on the B200 path");
+            return rest_->official_kda(input, w, state, config, layer, phase, control);
+        }
+        const std::size_t H = config.hidden_size, h = config.heads, d = config.head_dim, cw = config.conv_width;
+        const std::size_t P = h * d;
+        if (!H || !h || !d || cw < 2 || !std::isfinite(config.rms_norm_epsilon) || config.rms_norm_epsilon <= 0.0F ||
+            !std::isfinite(config.gate_lower_bound) || config.gate_lower_bound >= 0.0F || input.empty() ||
+            input.size() % H || state.conv_q.size() != (cw - 1) * P || state.conv_k.size() != (cw - 1) * P ||
+            state.conv_v.size() != (cw - 1) * P || state.recurrent_v_first.size() != h * d * d)
+            return Result<OfficialKdaCudaResult>::failure(ErrorCode::invalid_extent);
+        k3xb_kda_layer K{};
+        K.heads = static_cast<std::uint32_t>(h);
+        K.head_dim = static_cast<std::uint32_t>(d);
+        K.conv_width = static_cast<std::uint32_t>(cw);
+        K.eps = config.rms_norm_epsilon;
+        K.gate_lower_bound = config.gate_lower_bound;
+        ErrorCode st = ErrorCode::ok;
+        const auto bf16 = [&](const Bf16WeightView& v, std::size_t rows, std::size_t cols) -> const std::uint16_t* {
+            if (st != ErrorCode::ok) return nullptr;
+            if (v.rows != rows || v.cols != cols || v.values.size() != rows * cols) {
+                st = ErrorCode::invalid_extent;
+                return nullptr;
+            }
+            return static_cast<const std::uint16_t*>(resident(v.tensor_id, K3XB_WEIGHT_BF16, rows, cols,
+                                                              v.values.data(), v.values.size() * 2, &st));
+        };
+        const auto f32 = [&](std::uint64_t id, std::span<const float> v, std::size_t rows,
+                             std::size_t cols) -> const float* {
+            if (st != ErrorCode::ok) return nullptr;
+            if (v.size() != rows * cols) {
+                st = ErrorCode::invalid_extent;
+                return nullptr;
+            }
+            return static_cast<const float*>(resident(id, K3XB_WEIGHT_F32, rows, cols, v.data(), v.size() * 4, &st));
+        };
+        K.q_proj = bf16(w.q_proj, P, H);
+        K.k_proj = bf16(w.k_proj, P, H);
+        K.v_proj = bf16(w.v_proj, P, H);
+        K.q_conv = f32(w.q_conv.tensor_id, w.q_conv.values, P, cw);
+        K.k_conv = f32(w.k_conv.tensor_id, w.k_conv.values, P, cw);
+        K.v_conv = f32(w.v_conv.tensor_id, w.v_conv.values, P, cw);
+        K.f_a_proj = bf16(w.f_a_proj, d, H);
+        K.f_b_proj = bf16(w.f_b_proj, P, d);
+        K.a_log = f32(w.a_log.tensor_id, w.a_log.values, 1, d);
+        K.dt_bias = f32(w.dt_bias.tensor_id, w.dt_bias.values, 1, P);
+        K.b_proj = bf16(w.b_proj, h, H);
+        K.g_proj = bf16(w.g_proj, P, H);
+        K.o_norm = f32(w.o_norm.tensor_id, w.o_norm.values, 1, d);
+        K.o_proj = bf16(w.o_proj, H, P);
+        if (st != ErrorCode::ok) return Result<OfficialKdaCudaResult>::failure(st, last_error());
+
+        const std::size_t hist = (cw - 1) * P;
+        std::vector<std::uint16_t> conv(3 * hist);
+        std::memcpy(conv.data(), state.conv_q.data(), hist * 2);
+        std::memcpy(conv.data() + hist, state.conv_k.data(), hist * 2);
+        std::memcpy(conv.data() + 2 * hist, state.conv_v.data(), hist * 2);
+        OfficialKdaCudaResult r;
+        r.recurrent_v_first.assign(state.recurrent_v_first.begin(), state.recurrent_v_first.end());
+        r.output.resize(input.size());
+        const int rc = k3xb_kda_block_host(ctx_, &K, static_cast<std::uint32_t>(H), input.data(),
+                                           static_cast<std::uint32_t>(input.size() / H), conv.data(),
+                                           r.recurrent_v_first.data(), r.output.data());
+        if (rc != K3XB_OK) return Result<OfficialKdaCudaResult>::failure(static_cast<ErrorCode>(rc), last_error());
+        r.conv_q.assign(conv.begin(), conv.begin() + static_cast<std::ptrdiff_t>(hist));
+        r.conv_k.assign(conv.begin() + static_cast<std::ptrdiff_t>(hist),
+                        conv.begin() + static_cast<std::ptrdiff_t>(2 * hist));
+        r.conv_v.assign(conv.begin() + static_cast<std::ptrdiff_t>(2 * hist), conv.end());
+        r.executed = true;
+        ++kda_calls_;
+        return Result<OfficialKdaCudaResult>::success(std::move(r));
+    }
+
+private:
+    std::string last_error() const {
+        char buf[512] = {0};
+        if (ctx_) k3xb_last_error(ctx_, buf, sizeof buf);
+        return buf;
+    }
+
+    static bool distinct_ids(std::span<const Mxfp4MlpView> experts) {
+        std::unordered_set<std::uint64_t> ids;
+        for (const auto& e : experts)
+            for (const auto id : {e.gate.tensor_id, e.up.tensor_id, e.down.tensor_id})
+                if (!ids.insert(id).second) return false;
+        return true;
+    }
+
+    static std::vector<float> mix(const std::vector<std::vector<float>>& ys, std::span<const float> contributions) {
+        std::vector<float> mixed(ys.front().size(), 0.0F);
+        for (std::size_t slot = 0; slot < ys.size(); ++slot)
+            for (std::size_t row = 0; row < mixed.size(); ++row) mixed[row] += contributions[slot] * ys[slot][row];
+        return mixed;
+    }
+
+    // A device copy of one host weight; records a failure in *st.
+    const void* resident(std::uint64_t id, std::int32_t kind, std::size_t rows, std::size_t cols, const void* data,
+                         std::size_t bytes, ErrorCode* st) {
+        k3xb_resident r{};
+        const int rc = k3xb_acquire_weight(ctx_, id, kind, rows, cols, 0, data, bytes, nullptr, 0, &r);
+        if (rc != K3XB_OK) {
+            *st = static_cast<ErrorCode>(rc);
+            return nullptr;
+        }
+        if (r.disposition == K3XB_RESIDENT_BYPASS) {
+            *st = ErrorCode::backend_unavailable;   // over cuda_resident_bytes: the kernels read device copies
+            return nullptr;
+        }
+        return r.primary;
+    }
+
+    // The expert as a resident stack of one, keyed by its gate tensor id.
+    ErrorCode stack_of(const Mxfp4MlpView& e, std::size_t H, std::size_t I, k3xb_moe_layer* L) {
+        if (H % 128 || I % 128) return ErrorCode::backend_unavailable;   // the tcgen05 tiles
+        const k3xb_mxfp4_expert_host host{bytes_of(e.gate.packed), bytes_of(e.gate.scales), bytes_of(e.up.packed),
+                                          bytes_of(e.up.scales),   bytes_of(e.down.packed), bytes_of(e.down.scales)};
+        k3xb_resident_stack s{};
+        const int rc = k3xb_acquire_expert_stack(ctx_, e.gate.tensor_id, 1, static_cast<std::uint32_t>(H),
+                                                 static_cast<std::uint32_t>(I), &host, &s);
+        if (rc != K3XB_OK) return static_cast<ErrorCode>(rc);
+        if (s.disposition == K3XB_RESIDENT_BYPASS) return ErrorCode::backend_unavailable;
+        *L = k3xb_moe_layer{};
+        L->hidden = static_cast<std::uint32_t>(H);
+        L->inter = static_cast<std::uint32_t>(I);
+        L->experts = 1;
+        L->top_k = 1;
+        L->gate_packed = s.gate_packed;
+        L->gate_scales = s.gate_scales;
+        L->up_packed = s.up_packed;
+        L->up_scales = s.up_scales;
+        L->down_packed = s.down_packed;
+        L->down_scales = s.down_scales;
+        L->gate_scales_tc = s.gate_scales_tc;
+        L->up_scales_tc = s.up_scales_tc;
+        L->down_scales_tc = s.down_scales_tc;
+        L->engine = K3XB_ENGINE_MXF4;
+        return ErrorCode::ok;
+    }
+
+    // y [tokens][H] of one expert (gate/up, SiTU, down on tcgen05).
+    Result<std::vector<float>> run_expert(const Mxfp4MlpView& e, std::size_t H, std::size_t I, const float* x,
+                                          std::size_t tokens, float beta, std::optional<float> linear) {
+        k3xb_moe_layer L{};
+        if (auto st = stack_of(e, H, I, &L); st != ErrorCode::ok)
+            return Result<std::vector<float>>::failure(st, last_error());
+        L.activation = K3XB_ACT_SITU;
+        L.situ_beta = beta;
+        L.situ_linear_beta = linear ? *linear : 0.0F;
+        std::vector<float> y(tokens * H);
+        const std::uint32_t zero = 0;
+        const int rc = k3xb_expert_grid_host(ctx_, &L, &zero, 1, x, static_cast<std::uint32_t>(tokens), y.data());
+        if (rc != K3XB_OK) return Result<std::vector<float>>::failure(static_cast<ErrorCode>(rc), last_error());
+        ++grid_calls_;
+        grid_tokens_ += tokens;
+        return Result<std::vector<float>>::success(std::move(y));
+    }
+
+    BackendOptions options_;
+    k3xb_ctx* ctx_;
+    std::unique_ptr<ComputeBackend> rest_;
+    std::map<std::uint64_t, std::vector<Mxfp4MlpView>> prefetched_;
+    std::uint64_t next_token_ = 0;
+    std::uint64_t grid_calls_ = 0, grid_tokens_ = 0, moe_calls_ = 0, kda_calls_ = 0;
+};
+
+}  // namespace
+
+std::unique_ptr<ComputeBackend> wrap_b200_context(const BackendOptions& options, k3xb_ctx* ctx,
+                                                  std::unique_ptr<ComputeBackend> rest) {
+    return std::make_unique<B200Backend>(options, ctx, std::move(rest));
+}
+
+Result<std::unique_ptr<ComputeBackend>> make_b200_backend(const BackendOptions& options, int device,
+                                                          std::unique_ptr<ComputeBackend> rest) {
+    k3xb_ctx* ctx = nullptr;
+    const int rc = k3xb_create(device, &ctx);
+    if (rc != K3XB_OK)
+        return Result<std::unique_ptr<ComputeBackend>>::failure(static_cast<ErrorCode>(rc),
+                                                                "B200 backend: k3xb_create failed");
+    return Result<std::unique_ptr<ComputeBackend>>::success(wrap_b200_context(options, ctx, std::move(rest)));
+}
+
+}  // namespace k3x

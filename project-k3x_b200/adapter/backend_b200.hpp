@@ -1,0 +1,42 @@
+// backend_b200.hpp — a k3x::ComputeBackend for B200 over libk3xb.
+//
+// The reference's own CUDA backend refuses compute capability 10.0
+// (make_cuda_backend, runtime/cuda/backend_cuda.cu:5317-5329). This backend
+// is what a maintainer adds next to it (runtime/src/backend_b200.cpp, linked
+// with libk3xb.so): the hot-path methods of ComputeBackend
+// (runtime/include/k3x/backend.hpp:326-462) run on the B200 through the C
+// ABI of k3xb.h, everything else goes to a backend the maintainer passes
+// in (`rest`, e.g. the reference's CPU or dense CUDA backend) or returns
+// backend_unavailable when there is none. A failing hot-path call is
+// returned as it is; it is never retried on `rest`.
+//
+// On the B200:
+//   mxfp4_situ_mlp_group / _batch / _grid, mxfp4_situ_moe and their
+//   prefetch / _prepared forms  -> k3xb_acquire_expert_stack + k3xb_expert_grid_host
+//   official_kda (host-roundtrip state)  -> k3xb_acquire_weight + k3xb_kda_block_host
+// Weights are uploaded once, keyed by tensor id (BackendOptions::
+// cuda_resident_bytes bounds them when cuda_weights is resident).
+//
+// The batched verify step (k3xb_verify_step) has no ComputeBackend method:
+// it replaces Engine::forward_expert_major_block as a whole and is called
+// directly.
+#pragma once
+
+#include <memory>
+
+#include "k3x/backend.hpp"
+#include "k3xb.h"
+
+namespace k3x {
+
+// Creates a context on `device` (k3xb_create: compute capability 10.x only)
+// and wraps it. Fails with the C ABI's status (backend_unavailable without a
+// GPU, unsupported_architecture on other GPUs).
+Result<std::unique_ptr<ComputeBackend>> make_b200_backend(const BackendOptions& options, int device = 0,
+                                                          std::unique_ptr<ComputeBackend> rest = nullptr);
+
+// Wraps an existing context and takes ownership of it.
+std::unique_ptr<ComputeBackend> wrap_b200_context(const BackendOptions& options, k3xb_ctx* ctx,
+                                                  std::unique_ptr<ComputeBackend> rest = nullptr);
+
+}  // namespace k3x

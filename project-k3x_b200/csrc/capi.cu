@@ -36,6 +36,20 @@ int ensure_scratch(k3xb_ctx* ctx, size_t bytes, void** out) {
     return K3XB_OK;
 }
 
+int ensure_io(k3xb_ctx* ctx, size_t bytes, void** out) {
+    if (bytes > ctx->io_bytes) {
+        K3XB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+        if (ctx->io) K3XB_CUDA(ctx, cudaFree(ctx->io));
+        ctx->io = nullptr;
+        ctx->io_bytes = 0;
+        const size_t grown = bytes + bytes / 4 + (1u << 20);
+        K3XB_CUDA(ctx, cudaMalloc(&ctx->io, grown));
+        ctx->io_bytes = grown;
+    }
+    *out = ctx->io;
+    return K3XB_OK;
+}
+
 namespace {
 
 struct MoeScratch {
@@ -190,6 +204,7 @@ int k3xb_destroy(k3xb_ctx* ctx) {
     if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
     if (ctx->side_stream) cudaStreamSynchronize(ctx->side_stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->io) cudaFree(ctx->io);
     if (ctx->status_word) cudaFree(ctx->status_word);
     release_mxf4_resources(ctx);
     release_resident(ctx);
@@ -356,6 +371,69 @@ int k3xb_moe_experts(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const float* hi
     set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
     if (layer->engine == K3XB_ENGINE_SIMT) return launch_simt_experts(ctx, *layer, hidden, T, *plan, act, slot_out);
     return launch_mxf4_experts(ctx, *layer, hidden, T, *plan, slot_out);
+}
+
+int k3xb_expert_grid_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const uint32_t* expert_ids, uint32_t n,
+                          const float* inputs_host, uint32_t T, float* out_host) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!layer || !expert_ids || !inputs_host || !out_host || !T || !n)
+        return fail(ctx, K3XB_INVALID_EXTENT, "expert grid arguments");
+    k3xb_moe_layer L = *layer;
+    L.top_k = n;   // every token through each listed expert: one routing slot per expert
+    L.shared_gate = L.shared_up = L.shared_down = nullptr;
+    L.shared_inter = 0;
+    if (!L.hidden || !L.inter || !L.experts || n > L.experts || n > 32)
+        return fail(ctx, K3XB_INVALID_EXTENT, "expert grid: 1 <= experts listed <= min(32, stack size)");
+    if (L.hidden % 32 || L.inter % 32)
+        return fail(ctx, K3XB_INVALID_MXFP4, "hidden and inter must be multiples of the MXFP4 group (32)");
+    if (!L.gate_packed || !L.gate_scales || !L.up_packed || !L.up_scales || !L.down_packed || !L.down_scales)
+        return fail(ctx, K3XB_INVALID_EXTENT, "missing expert weights");
+    if (L.activation != K3XB_ACT_SWIGLU && L.activation != K3XB_ACT_SITU)
+        return fail(ctx, K3XB_INVALID_STATE, "unknown activation");
+    if (L.activation == K3XB_ACT_SITU && !(L.situ_beta > 0.0f))
+        return fail(ctx, K3XB_INVALID_STATE, "SiTU beta must be positive");
+    if (L.engine != K3XB_ENGINE_SIMT && L.engine != K3XB_ENGINE_MXF4)
+        return fail(ctx, K3XB_INVALID_STATE, "unknown expert engine");
+    // the reference rejects a repeated expert (backend_cpu.cpp:226-233 by tensor id)
+    std::vector<uint8_t> seen(L.experts, 0);
+    for (uint32_t j = 0; j < n; ++j) {
+        if (expert_ids[j] >= L.experts || seen[expert_ids[j]])
+            return fail(ctx, K3XB_INVALID_MXFP4, "expert grid: expert ids must be distinct and in the stack");
+        seen[expert_ids[j]] = 1;
+    }
+    const size_t H = L.hidden;
+    Sizer sz;
+    layout_moe(sz, L, T, true, nullptr);
+    sz.used += mxf4_scratch_bytes(L, T);
+    void* base;
+    int st;
+    if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
+    Carver c(base);
+    MoeScratch s{};
+    layout_moe(c, L, T, true, &s);
+    set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
+    std::vector<uint32_t> ids(static_cast<size_t>(T) * n);
+    std::vector<float> contrib(static_cast<size_t>(T) * n, 1.0f);
+    for (uint32_t t = 0; t < T; ++t)
+        for (uint32_t j = 0; j < n; ++j) ids[static_cast<size_t>(t) * n + j] = expert_ids[j];
+    const size_t hbytes = sizeof(float) * T * H;
+    K3XB_CUDA(ctx, cudaMemcpyAsync(s.hidden, inputs_host, hbytes, cudaMemcpyHostToDevice, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(s.ids, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(s.contrib, contrib.data(), contrib.size() * 4, cudaMemcpyHostToDevice,
+                                   ctx->stream));
+    ctx->stats.h2d_bytes += hbytes + ids.size() * 8;
+    s.plan.status = ctx->status_word;
+    if ((st = launch_plan(ctx, s.ids, s.contrib, T, n, L.experts, s.plan))) return st;
+    st = L.engine == K3XB_ENGINE_SIMT ? launch_simt_experts(ctx, L, s.hidden, T, s.plan, s.act, s.slot_out)
+                                      : launch_mxf4_experts(ctx, L, s.hidden, T, s.plan, s.slot_out);
+    if (st) return st;
+    // slot_out [T][n][H] -> out [n][T][H]
+    for (uint32_t j = 0; j < n; ++j)
+        K3XB_CUDA(ctx, cudaMemcpy2DAsync(out_host + static_cast<size_t>(j) * T * H, H * sizeof(float),
+                                         s.slot_out + static_cast<size_t>(j) * H, n * H * sizeof(float),
+                                         H * sizeof(float), T, cudaMemcpyDeviceToHost, ctx->stream));
+    ctx->stats.d2h_bytes += static_cast<uint64_t>(n) * hbytes;
+    return k3xb_sync(ctx);
 }
 
 // ---- KDA -------------------------------------------------------------------
@@ -841,6 +919,50 @@ int k3xb_kda_block_commit(k3xb_ctx* ctx, const k3xb_kda_layer* w, const void* tr
                                  cw, conv_out)))
         return st;
     return k3xb_kda_commit(ctx, rec, parent, N, S, h, d, tr.qn, tr.kn, tr.cv, tr.ld, tr.be, commit_node, rec_out);
+}
+
+int k3xb_kda_block_host(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t H, const float* x_host, uint32_t T,
+                        uint16_t* conv_host, float* rec_host, float* out_host) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    int st = validate_kda(ctx, w, H);
+    if (st) return st;
+    if (!x_host || !T || !conv_host || !rec_host || !out_host)
+        return fail(ctx, K3XB_INVALID_EXTENT, "kda_block_host arguments");
+    const size_t P = static_cast<size_t>(w->heads) * w->head_dim;
+    const size_t conv_n = 3 * static_cast<size_t>(w->conv_width - 1) * P;
+    const size_t rec_n = static_cast<size_t>(w->heads) * w->head_dim * w->head_dim;
+    const size_t xbytes = sizeof(float) * T * H;
+    Sizer sz;
+    sz.take<float>(static_cast<size_t>(T) * H);
+    sz.take<float>(static_cast<size_t>(T) * H);
+    sz.take<uint16_t>(2 * conv_n);
+    sz.take<float>(2 * rec_n);
+    sz.take<uint8_t>(k3xb_kda_trace_bytes(w, T, 1));
+    void* base;
+    if ((st = ensure_io(ctx, sz.used, &base))) return st;
+    Carver c(base);
+    float* x = c.take<float>(static_cast<size_t>(T) * H);
+    float* out = c.take<float>(static_cast<size_t>(T) * H);
+    uint16_t* conv = c.take<uint16_t>(2 * conv_n);
+    float* rec = c.take<float>(2 * rec_n);
+    void* trace = c.take<uint8_t>(k3xb_kda_trace_bytes(w, T, 1));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(x, x_host, xbytes, cudaMemcpyHostToDevice, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(conv, conv_host, conv_n * 2, cudaMemcpyHostToDevice, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(rec, rec_host, rec_n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    ctx->stats.h2d_bytes += xbytes + conv_n * 2 + rec_n * 4;
+    // the positions are a chain; its last node is the state the call publishes
+    std::vector<int32_t> parent(T);
+    for (uint32_t n = 0; n < T; ++n) parent[n] = static_cast<int32_t>(n) - 1;
+    const int32_t last = static_cast<int32_t>(T) - 1;
+    if ((st = k3xb_kda_block(ctx, w, H, x, parent.data(), T, 1, conv, rec, out, trace))) return st;
+    if ((st = k3xb_kda_block_commit(ctx, w, trace, parent.data(), T, 1, &last, conv, rec, conv + conv_n,
+                                    rec + rec_n)))
+        return st;
+    K3XB_CUDA(ctx, cudaMemcpyAsync(out_host, out, xbytes, cudaMemcpyDeviceToHost, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(conv_host, conv + conv_n, conv_n * 2, cudaMemcpyDeviceToHost, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(rec_host, rec + rec_n, rec_n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    ctx->stats.d2h_bytes += xbytes + conv_n * 2 + rec_n * 4;
+    return k3xb_sync(ctx);
 }
 
 int k3xb_attention_residual_norm(k3xb_ctx* ctx, const float* a, const float* delta, const float* block,

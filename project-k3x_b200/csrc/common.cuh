@@ -18,6 +18,8 @@ struct k3xb_ctx {
     std::string error;
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
+    void* io = nullptr;               // device side of the host-I/O entry points (*_host)
+    size_t io_bytes = 0;
     k3xb_stats stats{};
     int32_t* status_word = nullptr;   // device-side validation status (route, plan)
     void* mxf4_scratch = nullptr;     // MXF4-engine region inside `scratch`
@@ -35,6 +37,10 @@ int cuda_fail(k3xb_ctx* ctx, cudaError_t err, const char* where);
 // Grow-only device scratch (the reference's device_memory.cu keeps a
 // grow-only scratch too). Growing synchronises the stream first.
 int ensure_scratch(k3xb_ctx* ctx, size_t bytes, void** out);
+// Grow-only device buffer for the inputs and results of the host-I/O entry
+// points, apart from `scratch` so the device entry points they call may
+// grow the scratch.
+int ensure_io(k3xb_ctx* ctx, size_t bytes, void** out);
 
 #define K3XB_CUDA(ctx, call)                                        \
     do {                                                            \

@@ -167,6 +167,8 @@ def library() -> C.CDLL:
             "k3xb_acquire_expert_stack": [vp, u64, u32, u32, u32, C.POINTER(ExpertHost),
                                           C.POINTER(ResidentStack)],
             "k3xb_release_resident": [vp],
+            "k3xb_expert_grid_host": [vp, C.POINTER(MoeLayer), vp, u32, vp, u32, vp],
+            "k3xb_kda_block_host": [vp, C.POINTER(KdaLayer), u32, vp, u32, vp, vp, vp],
         }
         for name, args in sigs.items():
             fn = getattr(lib, name)
@@ -405,6 +407,33 @@ class Context:
         out = ResidentStack()
         self._check(self.lib.k3xb_acquire_expert_stack(self.h, stack_id, len(keep), hidden, inter, views,
                                                        C.byref(out)), "acquire_expert_stack")
+        return out
+
+    def expert_grid_host(self, layer: MoeLayer, expert_ids, inputs):
+        """HOST inputs [T][H] float32 through each listed expert of the
+        layer's stack -> HOST [n][T][H] (k3xb_expert_grid_host)."""
+        import numpy as np
+        x = np.ascontiguousarray(inputs, dtype=np.float32)
+        ids = np.ascontiguousarray(expert_ids, dtype=np.uint32)
+        out = np.empty((ids.size, x.shape[0], layer.hidden), np.float32)
+        self._check(self.lib.k3xb_expert_grid_host(self.h, C.byref(layer), ids.ctypes.data, ids.size,
+                                                   x.ctypes.data, x.shape[0], out.ctypes.data),
+                    "expert_grid_host")
+        return out
+
+    def kda_block_host(self, w: KdaLayer, hidden, x, conv, recurrent):
+        """One sequence through the KDA block with HOST arrays: x [T][H]
+        float32 -> out [T][H]; conv [3][w-1][P] uint16 and recurrent
+        [h][d][d] float32 are replaced by the state after the last position."""
+        import numpy as np
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        for a, dt in ((conv, np.uint16), (recurrent, np.float32)):
+            if a.dtype != dt or not a.flags.c_contiguous:
+                raise K3xbError(INVALID_EXTENT, "conv must be contiguous uint16 and recurrent float32")
+        out = np.empty((x.shape[0], hidden), np.float32)
+        self._check(self.lib.k3xb_kda_block_host(self.h, C.byref(w), hidden, x.ctypes.data, x.shape[0],
+                                                 conv.ctypes.data, recurrent.ctypes.data, out.ctypes.data),
+                    "kda_block_host")
         return out
 
     def release_resident(self):

@@ -1,0 +1,242 @@
+// Host-side checks of B200Backend (project-k3x_b200/adapter/backend_b200.cpp)
+// compiled against the reference's own ComputeBackend header: the method
+// split (hot path to libk3xb, the rest to the maintainer's backend), the
+// reference's argument checks, statuses passed through by value, and no
+// retry of a failed hot-path call on the other backend. A context of NULL
+// stands for "no GPU": every C ABI call then returns INVALID_EXTENT, which
+// shows the call reached the library.
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <vector>
+
+#include "backend_b200.hpp"
+
+#define CHECK(cond)                                                              \
+    do {                                                                         \
+        if (!(cond)) {                                                           \
+            std::fprintf(stderr, "check failed: %s (line %d)\n", #cond, __LINE__); \
+            return 1;                                                            \
+        }                                                                        \
+    } while (0)
+
+namespace {
+
+using namespace k3x;
+
+// Stands in for the maintainer's other backend; counts what reaches it.
+class FakeRest final : public ComputeBackend {
+public:
+    int calls = 0;
+    BackendOptions opts;
+    BackendKind kind() const noexcept override { return BackendKind::cpu; }
+    const BackendOptions& options() const noexcept override { return opts; }
+    BackendRuntimeStats runtime_stats() const noexcept override {
+        BackendRuntimeStats s{};
+        s.weight_cache_hits = 5;
+        return s;
+    }
+    BackendMemoryStats memory_stats() const noexcept override { return {3, 4}; }
+    std::string_view device_name() const noexcept override { return "fake"; }
+    Result<std::vector<float>> dense_matvec(std::span<const float>, DenseWeightView, std::uint32_t,
+                                            ProfilePhase) override {
+        ++calls;
+        return Result<std::vector<float>>::success({42.0F});
+    }
+    Result<std::vector<float>> mxfp4_matvec(std::span<const float>, Mxfp4WeightView, std::uint32_t,
+                                            ProfilePhase) override {
+        ++calls;
+        return Result<std::vector<float>>::success({43.0F});
+    }
+    Result<std::vector<std::vector<float>>> dense_matvec_group(std::span<const float>,
+                                                               std::span<const DenseWeightView>, std::uint32_t,
+                                                               ProfilePhase) override {
+        ++calls;
+        return Result<std::vector<std::vector<float>>>::success({});
+    }
+    Result<std::vector<std::vector<float>>> mxfp4_matvec_group(std::span<const float>,
+                                                               std::span<const Mxfp4WeightView>, std::uint32_t,
+                                                               ProfilePhase) override {
+        ++calls;
+        return Result<std::vector<std::vector<float>>>::success({});
+    }
+    Result<std::vector<float>> dense_situ_mlp(std::span<const float>, DenseMlpView, float, std::optional<float>,
+                                              std::uint32_t, ProfilePhase) override {
+        ++calls;
+        return Result<std::vector<float>>::success({});
+    }
+    Result<std::vector<std::vector<float>>> mxfp4_situ_mlp_group(std::span<const float>,
+                                                                 std::span<const Mxfp4MlpView>, float,
+                                                                 std::optional<float>, std::uint32_t,
+                                                                 ProfilePhase) override {
+        ++calls;
+        return Result<std::vector<std::vector<float>>>::success({});
+    }
+    Result<std::vector<std::vector<float>>> mxfp4_situ_mlp_batch(std::span<const float>, std::size_t,
+                                                                 Mxfp4MlpView, float, std::optional<float>,
+                                                                 std::uint32_t, ProfilePhase) override {
+        ++calls;
+        return Result<std::vector<std::vector<float>>>::success({});
+    }
+    Result<std::vector<float>> mxfp4_situ_moe(std::span<const float>, std::span<const Mxfp4MlpView>,
+                                              std::span<const float>, float, std::optional<float>, std::uint32_t,
+                                              ProfilePhase) override {
+        ++calls;
+        return Result<std::vector<float>>::success({});
+    }
+    Result<Mxfp4PrefetchToken> prefetch_mxfp4_situ_mlp_group(std::span<const Mxfp4MlpView>, std::uint64_t,
+                                                             std::uint32_t, ProfilePhase) override {
+        ++calls;
+        return Result<Mxfp4PrefetchToken>::success({});
+    }
+    Result<std::vector<std::vector<float>>> mxfp4_situ_mlp_group_prepared(std::span<const float>,
+                                                                          Mxfp4PrefetchToken, float,
+                                                                          std::optional<float>, std::uint32_t,
+                                                                          ProfilePhase) override {
+        ++calls;
+        return Result<std::vector<std::vector<float>>>::success({});
+    }
+    Result<std::vector<float>> mxfp4_situ_moe_prepared(std::span<const float>, Mxfp4PrefetchToken,
+                                                       std::span<const float>, float, std::optional<float>,
+                                                       std::uint32_t, ProfilePhase) override {
+        ++calls;
+        return Result<std::vector<float>>::success({});
+    }
+    Result<OfficialKdaCudaResult> official_kda(std::span<const float>, OfficialKdaCudaView,
+                                               OfficialKdaCudaStateView, OfficialKdaCudaConfig, std::uint32_t,
+                                               ProfilePhase, OfficialKdaStateControl) override {
+        ++calls;
+        OfficialKdaCudaResult r;
+        r.executed = true;
+        r.output = {7.0F};
+        return Result<OfficialKdaCudaResult>::success(std::move(r));
+    }
+};
+
+// One expert's views over host buffers (rows x cols MXFP4, group 32).
+struct ExpertBuffers {
+    std::vector<std::byte> gp, gs, up, us, dp, ds;
+    Mxfp4MlpView view{};
+    ExpertBuffers(std::size_t H, std::size_t I, std::uint64_t id)
+        : gp(I * H / 2), gs(I * H / 32), up(I * H / 2), us(I * H / 32), dp(H * I / 2), ds(H * I / 32) {
+        view.gate = {id, gp, gs, I, H, 32};
+        view.up = {id + 1, up, us, I, H, 32};
+        view.down = {id + 2, dp, ds, H, I, 32};
+    }
+};
+
+int factory() {
+    BackendOptions o{};
+    o.kind = BackendKind::cuda_custom;
+    auto b = make_b200_backend(o, 0);
+    if (b) {   // a B200 is present
+        CHECK(b.value()->kind() == BackendKind::cuda_custom);
+    } else {
+        CHECK(b.error() == ErrorCode::backend_unavailable || b.error() == ErrorCode::unsupported_architecture);
+    }
+    return 0;
+}
+
+int split_and_forwarding() {
+    BackendOptions o{};
+    auto rest = std::make_unique<FakeRest>();
+    FakeRest* fake = rest.get();
+    auto b = wrap_b200_context(o, nullptr, std::move(rest));
+    CHECK(b->kind() == BackendKind::cuda_custom && !b->device_name().empty());
+    CHECK(b->runtime_stats().weight_cache_hits == 5 && b->memory_stats().current_device_bytes == 3);
+    const std::vector<float> x(128, 1.0F);
+    // not on the path: forwarded
+    auto d = b->dense_matvec(x, DenseWeightView{1, x, 1, 128}, 0, ProfilePhase::decode);
+    CHECK(d && d.value().size() == 1 && d.value()[0] == 42.0F && fake->calls == 1);
+    // on the path: reaches the C ABI (NULL context -> invalid_extent), never the other backend
+    ExpertBuffers e(128, 128, 10);
+    const std::vector<Mxfp4MlpView> experts{e.view};
+    auto g = b->mxfp4_situ_mlp_group(x, experts, 1.0e6F, std::nullopt, 0, ProfilePhase::decode);
+    CHECK(!g && g.error() == ErrorCode::invalid_extent && fake->calls == 1);
+    const std::vector<float> c{1.0F};
+    auto m = b->mxfp4_situ_moe(x, experts, c, 1.0e6F, std::nullopt, 0, ProfilePhase::decode);
+    CHECK(!m && m.error() == ErrorCode::invalid_extent && fake->calls == 1);
+    // device KDA state modes go to the other backend
+    OfficialKdaStateControl ctl{};
+    ctl.mode = OfficialKdaStateMode::device_seed;
+    auto k = b->official_kda(x, OfficialKdaCudaView{}, OfficialKdaCudaStateView{}, OfficialKdaCudaConfig{}, 0,
+                             ProfilePhase::decode, ctl);
+    CHECK(k && k.value().output.size() == 1 && fake->calls == 2);
+    return 0;
+}
+
+int no_rest() {
+    BackendOptions o{};
+    auto b = wrap_b200_context(o, nullptr);
+    const std::vector<float> x(128, 1.0F);
+    auto d = b->dense_matvec(x, DenseWeightView{1, x, 1, 128}, 0, ProfilePhase::decode);
+    CHECK(!d && d.error() == ErrorCode::backend_unavailable);
+    auto r = b->resident_mxfp4_moe_layer(x, ResidentMoeLayerView{}, {}, {}, 1e-6F, 1.0F, std::nullopt, 0,
+                                         ProfilePhase::decode);
+    CHECK(!r && r.error() == ErrorCode::backend_unavailable);
+    OfficialKdaStateControl ctl{};
+    ctl.mode = OfficialKdaStateMode::device_continue;
+    auto k = b->official_kda(x, OfficialKdaCudaView{}, OfficialKdaCudaStateView{}, OfficialKdaCudaConfig{}, 0,
+                             ProfilePhase::decode, ctl);
+    CHECK(!k && k.error() == ErrorCode::backend_unavailable);
+    return 0;
+}
+
+int argument_checks() {
+    BackendOptions o{};
+    auto b = wrap_b200_context(o, nullptr);
+    const std::vector<float> x(128, 1.0F);
+    ExpertBuffers e(128, 128, 10), f(128, 128, 20);
+    const std::vector<Mxfp4MlpView> one{e.view}, two{e.view, f.view}, dup{e.view, e.view};
+    const std::vector<float> c1{1.0F}, c2{0.5F, 0.5F}, bad{NAN};
+    const auto P = ProfilePhase::decode;
+    // contributions must match the experts and be finite (backend_cpu.cpp:270-280)
+    CHECK(b->mxfp4_situ_moe(x, two, c1, 1.0F, std::nullopt, 0, P).error() == ErrorCode::invalid_mxfp4);
+    CHECK(b->mxfp4_situ_moe(x, one, bad, 1.0F, std::nullopt, 0, P).error() == ErrorCode::invalid_mxfp4);
+    // SiTU parameters (backend_cpu.cpp:200-208)
+    CHECK(b->mxfp4_situ_mlp_group(x, one, 0.0F, std::nullopt, 0, P).error() == ErrorCode::invalid_mxfp4);
+    CHECK(b->mxfp4_situ_mlp_group(x, one, 1.0F, -1.0F, 0, P).error() == ErrorCode::invalid_mxfp4);
+    // input width, token counts, distinct tensor ids in a grid
+    CHECK(b->mxfp4_situ_mlp_group(std::span<const float>(x).first(64), one, 1.0F, std::nullopt, 0, P).error() ==
+          ErrorCode::invalid_mxfp4);
+    CHECK(b->mxfp4_situ_mlp_grid(x, 0, one, 1.0F, std::nullopt, 0, P).error() == ErrorCode::invalid_mxfp4);
+    CHECK(b->mxfp4_situ_mlp_grid(x, 1, dup, 1.0F, std::nullopt, 0, P).error() == ErrorCode::invalid_mxfp4);
+    CHECK(b->mxfp4_situ_mlp_batch(x, 2, e.view, 1.0F, std::nullopt, 0, P).error() == ErrorCode::invalid_mxfp4);
+    // malformed MXFP4 views
+    ExpertBuffers g(128, 128, 30);
+    g.view.down.group_size = 16;
+    CHECK(b->mxfp4_situ_mlp_group(x, std::vector<Mxfp4MlpView>{g.view}, 1.0F, std::nullopt, 0, P).error() ==
+          ErrorCode::invalid_mxfp4);
+    // shapes the tcgen05 tiles cannot take: backend_unavailable, before any device call
+    ExpertBuffers h(96, 128, 40);
+    const std::vector<float> x96(96, 1.0F);
+    CHECK(b->mxfp4_situ_mlp_group(x96, std::vector<Mxfp4MlpView>{h.view}, 1.0F, std::nullopt, 0, P).error() ==
+          ErrorCode::backend_unavailable);
+    // prefetch tokens
+    CHECK(b->mxfp4_situ_mlp_group_prepared(x, Mxfp4PrefetchToken{99, 0}, 1.0F, std::nullopt, 0, P).error() ==
+          ErrorCode::invalid_state);
+    // KDA, host-roundtrip: config and state extents (official_kda.cpp:150-180)
+    OfficialKdaCudaConfig cfg{128, 2, 64, 4, 1e-5F, -5.0F};
+    const std::vector<std::uint16_t> hist(3 * 128);
+    const std::vector<float> rec(2 * 64 * 64);
+    OfficialKdaCudaStateView st{hist, hist, hist, rec};
+    const std::vector<float> x3(3 * 128, 0.0F);
+    CHECK(b->official_kda(std::span<const float>(x3).first(100), OfficialKdaCudaView{}, st, cfg, 0, P).error() ==
+          ErrorCode::invalid_extent);
+    OfficialKdaCudaConfig pos = cfg;
+    pos.gate_lower_bound = 1.0F;
+    CHECK(b->official_kda(x3, OfficialKdaCudaView{}, st, pos, 0, P).error() == ErrorCode::invalid_extent);
+    OfficialKdaCudaStateView short_state{std::span<const std::uint16_t>(hist).first(10), hist, hist, rec};
+    CHECK(b->official_kda(x3, OfficialKdaCudaView{}, short_state, cfg, 0, P).error() == ErrorCode::invalid_extent);
+    // weight views of the wrong shape
+    CHECK(b->official_kda(x3, OfficialKdaCudaView{}, st, cfg, 0, P).error() == ErrorCode::invalid_extent);
+    return 0;
+}
+
+}  // namespace
+
+int main() {
+    if (factory() || split_and_forwarding() || no_rest() || argument_checks()) return 1;
+    std::printf("backend adapter ok\n");
+    return 0;
+}

@@ -1,0 +1,49 @@
+"""B200Backend, the k3x::ComputeBackend over libk3xb
+(project-k3x_b200/adapter/), compiled against the reference's own
+interface headers with -Wall -Wextra -Werror and linked with libk3xb.so:
+the proof that it is a drop-in for backend.hpp:326-462. Its host-side
+behaviour (method split, argument checks, statuses, no retry on the other
+backend) runs here; its device calls are the C ABI entry points the GPU
+tests cover (test_gpu_host_io.py, test_gpu_resident.py).
+
+The reference tree is found through K3X_REFERENCE or the REF default of
+oracle/Makefile; without it the test skips."""
+import os
+import re
+import shutil
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIBDIR = os.path.join(ROOT, "project-k3x_b200", "k3xb")
+ADAPTER = os.path.join(ROOT, "project-k3x_b200", "adapter")
+
+
+def reference_include():
+    ref = os.environ.get("K3X_REFERENCE")
+    if not ref:
+        m = re.search(r"^REF \?= (\S+)", open(os.path.join(ROOT, "oracle", "Makefile")).read(), re.M)
+        ref = m.group(1) if m else ""
+    inc = os.path.join(ref, "runtime", "include")
+    return inc if os.path.exists(os.path.join(inc, "k3x", "backend.hpp")) else None
+
+
+def test_backend_adapter_against_reference_interface(tmp_path):
+    cxx = shutil.which("g++")
+    if not cxx:
+        pytest.skip("no C++ compiler")
+    inc = reference_include()
+    if not inc:
+        pytest.skip("reference headers absent")
+    if not os.path.exists(os.path.join(LIBDIR, "libk3xb.so")):
+        pytest.fail("libk3xb.so is not built (project-k3x_b200/build.py)")
+    exe = tmp_path / "backend_adapter_check"
+    subprocess.run([cxx, "-std=c++20", "-O1", "-Wall", "-Wextra", "-Werror", "-isystem", inc,
+                    "-I", os.path.join(ROOT, "include"), "-I", ADAPTER,
+                    os.path.join(ADAPTER, "backend_b200.cpp"),
+                    os.path.join(ROOT, "tests", "cpp", "backend_adapter_check.cpp"),
+                    "-L", LIBDIR, "-lk3xb", f"-Wl,-rpath,{LIBDIR}", "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.startswith("backend adapter ok"), out.stdout

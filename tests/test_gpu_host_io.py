@@ -1,0 +1,115 @@
+"""Host-I/O entry points a ComputeBackend adapter calls with the reference's
+host views (backend.hpp:326-462): k3xb_expert_grid_host
+(mxfp4_situ_mlp_grid / _group / _batch / mxfp4_situ_moe) and
+k3xb_kda_block_host (official_kda, host-roundtrip state). Each must equal
+the device entry points it is made of, bit for bit, also when its weights
+come from the resident table (k3xb_acquire_*), and the grid must equal the
+oracle's expert FFN within the north-star tolerance."""
+import numpy as np
+import pytest
+
+from gpu_util import assert_close_bf16, layer_to_dev, to_dev, torch_cuda
+from oracle import bf16_normal, bf16_words, make_kda_weights, make_moe_layer
+
+pytestmark = pytest.mark.gpu
+
+DIMS = dict(hidden=256, inter=128, experts=8, top_k=2, shared_inter=0)
+
+
+@pytest.fixture(scope="module")
+def torch():
+    return torch_cuda()
+
+
+@pytest.fixture(scope="module")
+def ctx(torch):
+    import k3xb
+    c = k3xb.Context(0)
+    c.use_stream()
+    yield c
+    c.close()
+
+
+def _expert(rs, L, e, x):
+    H, I = L["hidden"], L["inter"]
+    g = rs.mxfp4_matmul(x, L["gate_packed"][e], L["gate_scales"][e], I, H)
+    u = rs.mxfp4_matmul(x, L["up_packed"][e], L["up_scales"][e], I, H)
+    return rs.round_bf16(rs.mxfp4_matmul(rs.swiglu(g, u), L["down_packed"][e], L["down_scales"][e], H, I))
+
+
+def test_expert_grid_host_vs_oracle_and_single_expert_stacks(torch, ctx, rs):
+    import k3xb
+    d = DIMS
+    L = make_moe_layer(rs, 81, d["hidden"], d["inter"], d["experts"], d["top_k"])
+    x = bf16_normal(np.random.default_rng(82), (5, d["hidden"]))
+    desc = k3xb.moe_layer_desc(layer_to_dev(torch, L), engine=k3xb.ENGINE_MXF4)
+    ids = [3, 0, 7]
+    got = ctx.expert_grid_host(desc, ids, x)
+    assert got.shape == (3, 5, d["hidden"])
+    for j, e in enumerate(ids):
+        want = np.stack([_expert(rs, L, e, x[t]) for t in range(x.shape[0])])
+        assert_close_bf16(got[j], want)
+    # the adapter's layout: every expert its own resident stack of one
+    names = ("gate_packed", "gate_scales", "up_packed", "up_scales", "down_packed", "down_scales")
+    for j, e in enumerate(ids):
+        stack = ctx.acquire_expert_stack(1000 + e, d["hidden"], d["inter"], [{n: L[n][e] for n in names}])
+        one = dict(hidden=d["hidden"], inter=d["inter"], experts=1, top_k=1)
+        single = ctx.expert_grid_host(k3xb.stack_layer_desc(stack, one), [0], x)
+        np.testing.assert_array_equal(single[0], got[j])
+    with pytest.raises(k3xb.K3xbError, match="INVALID_MXFP4"):
+        ctx.expert_grid_host(desc, [1, 1], x)
+
+
+def test_kda_block_host_equals_device_chain_and_resident_weights(torch, ctx, rs):
+    import k3xb
+    g = np.random.default_rng(83)
+    H, h, dh, W, T = 256, 2, 64, 4, 5
+    P = h * dh
+    w = make_kda_weights(g, H, h, dh, W)
+    conv = np.stack([bf16_words(g.normal(0, 0.5, size=(W - 1) * P)) for _ in range(3)])   # [3][(w-1)*P]
+    rec = g.normal(0, 0.05, size=(h, dh, dh)).astype(np.float32)
+    x = bf16_normal(g, (T, H))
+
+    wd = {k: (to_dev(torch, v) if isinstance(v, np.ndarray) else v) for k, v in w.items()}
+    desc = k3xb.kda_layer_desc(wd)
+    parent = list(range(-1, T - 1))
+    out_d = torch.empty((1, T, H), dtype=torch.float32, device="cuda")
+    trace = torch.empty(ctx.kda_trace_bytes(desc, T, 1), dtype=torch.uint8, device="cuda")
+    conv_d, rec_d = to_dev(torch, conv[None]), to_dev(torch, rec[None])
+    ctx.kda_block(desc, to_dev(torch, x[None]), parent, conv_d, rec_d, out_d, trace)
+    conv_o, rec_o = torch.empty_like(conv_d), torch.empty_like(rec_d)
+    ctx.kda_block_commit(desc, trace, parent, 1, [T - 1], conv_d, rec_d, conv_o, rec_o)
+    ctx.sync()
+    want_out = out_d.cpu().numpy()[0]
+    want_conv = conv_o.cpu().numpy().view(np.uint16)[0]
+    want_rec = rec_o.cpu().numpy()[0]
+
+    c1, r1 = conv.copy(), rec.copy()
+    got = ctx.kda_block_host(desc, H, x, c1, r1)
+    np.testing.assert_array_equal(got, want_out)
+    np.testing.assert_array_equal(c1, want_conv)
+    np.testing.assert_array_equal(r1, want_rec)
+
+    # the same block with every weight uploaded through the resident table
+    res = dict(w)
+    keep = []
+    for tensor_id, (name, v) in enumerate(w.items(), start=5000):
+        if not isinstance(v, np.ndarray):
+            continue
+        rows, cols = (v.shape if v.ndim == 2 else (1, v.shape[0]))
+        kind = k3xb.WEIGHT_BF16 if v.dtype == np.uint16 else k3xb.WEIGHT_F32
+        r = ctx.acquire_weight(tensor_id, kind, rows, cols, 0, v)
+        assert r.disposition == k3xb.RESIDENT_ADMITTED
+        keep.append(r)
+        res[name] = r.primary
+    K = k3xb.KdaLayer()
+    K.heads, K.head_dim, K.conv_width, K.eps, K.gate_lower_bound = h, dh, W, w["eps"], w["gate_lower_bound"]
+    for name in ("q_proj", "k_proj", "v_proj", "q_conv", "k_conv", "v_conv", "f_a_proj", "f_b_proj", "a_log",
+                 "dt_bias", "b_proj", "g_proj", "o_norm", "o_proj"):
+        setattr(K, name, res[name])
+    c2, r2 = conv.copy(), rec.copy()
+    got2 = ctx.kda_block_host(K, H, x, c2, r2)
+    np.testing.assert_array_equal(got2, want_out)
+    np.testing.assert_array_equal(c2, want_conv)
+    np.testing.assert_array_equal(r2, want_rec)
+    ctx.release_resident()
