@@ -31,3 +31,21 @@ def ref():
     if not have_reference():
         pytest.skip("oracle/_ref/libk3x_ref.so not built (reference tree absent)")
     return Reference()
+
+
+# GPU files in dependency order: the kernels first, then what is composed of
+# them or added on top (golden end-to-end cases, the routing policy, expert
+# parallelism, the host-I/O entry points, resident weights), so that a run which stops at the first failure
+# stops at the lowest broken layer. Files not listed keep their place after
+# these; test_zz_no_alloc.py stays last.
+_GPU_ORDER = ["test_gpu_parity", "test_gpu_mxf4", "test_gpu_linear", "test_gpu_layer", "test_gpu_golden",
+              "test_gpu_routing_policy", "test_gpu_ep", "test_gpu_host_io", "test_gpu_resident"]
+
+
+def pytest_collection_modifyitems(session, config, items):
+    def rank(item):
+        name = item.module.__name__.rsplit(".", 1)[-1] if item.module else ""
+        if name.startswith("test_zz"):
+            return len(_GPU_ORDER) + 1
+        return _GPU_ORDER.index(name) if name in _GPU_ORDER else len(_GPU_ORDER)
+    items.sort(key=rank)   # stable: order inside a file is kept

@@ -1,0 +1,176 @@
+"""Generates the golden fixtures in this folder from the reference's own CPU
+code: oracle/_ref/libk3x_ref.so, compiled by `make -C oracle` from the
+reference's unmodified runtime sources (ops.cpp, official_moe.cpp,
+official_kda.cpp, expert_major.cpp, speculative.cpp, routing_policy.cpp)
+where they lie. Inputs are seeded synthetic data at the c1 dimensions; each
+fixture stores inputs and the reference's outputs, so the oracle pin
+(tests/test_golden.py) and the GPU parity tests (tests/test_gpu_golden.py)
+run where neither the reference tree nor its build exists.
+
+Run from the repository root: python tests/golden/make_golden.py
+"""
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path[:0] = [os.path.join(ROOT, "oracle")]
+
+from oracle import (ROUTING_ADAPTIVE, ROUTING_FIXED, ROUTING_NATURAL, Reference, Restatement,  # noqa: E402
+                    bf16_normal, bf16_words, make_kda_weights, make_moe_layer)
+
+MOE = dict(hidden=256, inter=128, experts=8, top_k=2, shared_inter=128)
+KDA = dict(hidden=256, heads=2, head_dim=64, conv_width=4, tokens=5)
+
+
+def save(name, **arrays):
+    path = os.path.join(HERE, name)
+    np.savez_compressed(path, **{k: np.asarray(v) for k, v in arrays.items()})
+    print(f"{name}: {os.path.getsize(path)} bytes")
+
+
+def route(ref):
+    """route_official_moe (official_moe.cpp:247-269) for 6 tokens."""
+    g = np.random.default_rng(1001)
+    T, E, H, K = 6, 16, 256, 4
+    hidden = bf16_normal(g, (T, H))
+    router = bf16_words(g.normal(0, 0.02, size=(E, H)))
+    correction = g.normal(0, 0.02, size=E).astype(np.float32)
+    ids, con, sco = zip(*(ref.route(hidden[t], router, correction, K, want_scores=True) for t in range(T)))
+    save("route.npz", hidden=hidden, router=router, correction=correction, top_k=K,
+         ids=np.stack(ids), contributions=np.stack(con), scores=np.stack(sco))
+
+
+def expert_major(ref):
+    """build_expert_major_plan (expert_major.cpp:10-54) for 12 tokens x 3 slots."""
+    g = np.random.default_rng(1002)
+    T, K, E = 12, 3, 10
+    ids = np.stack([g.choice(E, size=K, replace=False) for _ in range(T)]).astype(np.uint32)
+    con = g.random((T, K)).astype(np.float32)
+    p = ref.expert_major_plan(ids.tolist(), con.tolist())
+    save("expert_major.npz", ids=ids, contributions=con, experts=E, **p)
+
+
+def mxfp4(ref, rs):
+    """decode_mxfp4 / mxfp4_matmul (ops.cpp:32-76) of a 64 x 256 matrix."""
+    g = np.random.default_rng(1003)
+    rows, cols = 64, 256
+    packed, scales = rs.quantize_mxfp4(g.normal(0, 0.02, size=(rows, cols)).astype(np.float32))
+    x = bf16_normal(g, (cols,))
+    save("mxfp4.npz", packed=packed, scales=scales, x=x,
+         decoded=ref.decode_mxfp4(packed, scales, rows, cols), y=ref.mxfp4_matmul(x, packed, scales, rows, cols))
+
+
+def moe_layer(ref, rs):
+    """The plain hidden-space MoE layer (official_moe.cpp:271-344 without the
+    latent steps) composed from the reference's exported functions."""
+    d = MOE
+    layer = make_moe_layer(rs, 1004, d["hidden"], d["inter"], d["experts"], d["top_k"], d["shared_inter"])
+    hidden = bf16_normal(np.random.default_rng(1005), (5, d["hidden"]))
+    out, ids, con = ref.moe_layer(layer, hidden)
+    arrays = {k: v for k, v in layer.items() if isinstance(v, np.ndarray)}
+    dims = {k: v for k, v in layer.items() if not isinstance(v, np.ndarray)}
+    save("moe_layer.npz", hidden=hidden, out=out, ids=ids, contributions=con,
+         **arrays, **{f"dim_{k}": v for k, v in dims.items()})
+
+
+def kda_block(ref):
+    """official_kda_cpu (official_kda.cpp:198-426) over 5 positions from a
+    non-zero state."""
+    d = KDA
+    g = np.random.default_rng(1006)
+    P = d["heads"] * d["head_dim"]
+    w = make_kda_weights(g, d["hidden"], d["heads"], d["head_dim"], d["conv_width"])
+    conv = [bf16_words(g.normal(0, 0.5, size=(d["conv_width"] - 1) * P)) for _ in range(3)]
+    rec = g.normal(0, 0.05, size=(d["heads"], d["head_dim"], d["head_dim"])).astype(np.float32)
+    x = bf16_normal(g, (d["tokens"], d["hidden"]))
+    out, (cq, ck, cv, r) = ref.kda_block(w, x, conv[0], conv[1], conv[2], rec.ravel())
+    arrays = {f"w_{k}": v for k, v in w.items() if isinstance(v, np.ndarray)}
+    dims = {f"dim_{k}": v for k, v in w.items() if not isinstance(v, np.ndarray)}
+    save("kda_block.npz", x=x, conv_q=conv[0], conv_k=conv[1], conv_v=conv[2], recurrent=rec, out=out,
+         next_conv_q=cq, next_conv_k=ck, next_conv_v=cv, next_recurrent=r.reshape(rec.shape), **arrays, **dims)
+
+
+def prepare_input(ref):
+    """prepare_official_moe_input (official_moe.cpp:156-209) for 4 rows."""
+    g = np.random.default_rng(1007)
+    T, H, eps = 4, 256, 1e-6
+    prefix, block = bf16_normal(g, (T, H)), bf16_normal(g, (T, H))
+    norm = bf16_words(1.0 + g.normal(0, 0.1, size=H))
+    proj = bf16_words(g.normal(0, 0.02, size=H))
+    post = bf16_words(1.0 + g.normal(0, 0.1, size=H))
+    out = np.stack([ref.prepare_input(prefix[t], block[t], norm, proj, post, eps) for t in range(T)])
+    save("prepare_input.npz", prefix=prefix, block=block, norm=norm, proj=proj, post=post, eps=eps, out=out)
+
+
+POLICIES = [
+    dict(mode=ROUTING_NATURAL),
+    dict(mode=ROUTING_FIXED, fixed_k=8),
+    dict(mode=ROUTING_FIXED, fixed_k=4, quality_floor_k=6),
+    dict(mode=ROUTING_ADAPTIVE, mass_target=0.5, minimum_gap=0.0),
+    dict(mode=ROUTING_ADAPTIVE, mass_target=0.9, minimum_gap=0.02, quality_floor_k=8),
+]
+
+
+def select_routing(ref):
+    """select_routing (routing_policy.cpp:31-159): 8 tokens x 64 experts,
+    natural Top-16, each policy of POLICIES."""
+    g = np.random.default_rng(1008)
+    T, E, K = 8, 64, 16
+    scores = (1.0 / (1.0 + np.exp(-g.normal(0, 1.5, size=(T, E))))).astype(np.float32)
+    bias = g.normal(0, 0.05, size=E).astype(np.float32)
+    arrays = dict(scores=scores, bias=bias, natural_k=K)
+    for i, pol in enumerate(POLICIES):
+        ids = np.full((T, K), 0xFFFFFFFF, np.uint32)
+        wts = np.zeros((T, K), np.float32)
+        sel = np.zeros(T, np.uint32)
+        esc = np.zeros(T, np.uint32)
+        stats = np.zeros((T, 4), np.float32)
+        for t in range(T):
+            st, r = ref.select_routing(scores[t], bias, K, **pol)
+            assert st == 0, st
+            n = r["selected_k"]
+            ids[t, :n], wts[t, :n], sel[t], esc[t] = r["expert_ids"], r["weights"], n, r["escalated"]
+            stats[t] = (r["normalized_entropy"], r["support"], r["mass"], r["boundary"])
+        arrays.update({f"p{i}_ids": ids, f"p{i}_weights": wts, f"p{i}_selected": sel, f"p{i}_escalated": esc,
+                       f"p{i}_stats": stats})
+    save("select_routing.npz", **arrays)
+
+
+def verify_greedy(ref):
+    """verify_greedy_target_block (speculative.cpp:74-112): 6 sequences of
+    anchor + 5 drafts over vocab 1000, accepting 0..5 drafts."""
+    g = np.random.default_rng(1009)
+    S, p, V = 6, 5, 1000
+    drafts = g.integers(0, V, size=(S, p)).astype(np.uint32)
+    targets = g.integers(0, V, size=(S, p + 1)).astype(np.uint32)
+    accepted = np.zeros(S, np.uint32)
+    committed = np.zeros((S, p + 1), np.uint32)
+    count = np.zeros(S, np.uint32)
+    for s in range(S):
+        targets[s, :s] = drafts[s, :s]            # sequence s accepts exactly s drafts
+        if s < p:
+            targets[s, s] = (drafts[s, s] + 1) % V
+        a, com, _ = ref.verify_greedy_block(0, drafts[s], p, V, targets[s])
+        accepted[s], count[s] = a, len(com)
+        committed[s, :len(com)] = com
+    save("verify_greedy.npz", drafts=drafts, targets=targets, vocab=V, accepted=accepted, committed=committed,
+         count=count)
+
+
+def main():
+    ref, rs = Reference(), Restatement()
+    route(ref)
+    expert_major(ref)
+    mxfp4(ref, rs)
+    moe_layer(ref, rs)
+    kda_block(ref)
+    prepare_input(ref)
+    select_routing(ref)
+    verify_greedy(ref)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,45 @@
+"""Loads the golden fixtures of tests/golden/ (made by
+tests/golden/make_golden.py from the reference's own CPU build)."""
+import os
+
+import numpy as np
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def load(name):
+    with np.load(os.path.join(GOLDEN, name)) as f:
+        return {k: f[k] for k in f.files}
+
+
+def _scalar(v):
+    v = np.asarray(v)
+    return v.item() if v.ndim == 0 else v
+
+
+def moe_layer():
+    """(layer dict in make_moe_layer's form, hidden, out, ids, contributions)."""
+    f = load("moe_layer.npz")
+    layer = {k[4:]: _scalar(v) for k, v in f.items() if k.startswith("dim_")}
+    for k, v in f.items():
+        if not k.startswith("dim_") and k not in ("hidden", "out", "ids", "contributions"):
+            layer[k] = v
+    for k in ("hidden", "inter", "experts", "top_k", "shared_inter", "activation"):
+        layer[k] = int(layer[k])
+    for k in ("situ_beta", "situ_linear_beta"):
+        layer[k] = float(layer[k])
+    return layer, f["hidden"], f["out"], f["ids"], f["contributions"]
+
+
+def kda_block():
+    """(weights dict in make_kda_weights's form, fixture dict)."""
+    f = load("kda_block.npz")
+    w = {k[2:]: v for k, v in f.items() if k.startswith("w_")}
+    for k, v in f.items():
+        if k.startswith("dim_"):
+            w[k[4:]] = _scalar(v)
+    for k in ("hidden", "heads", "head_dim", "conv_width"):
+        w[k] = int(w[k])
+    for k in ("eps", "gate_lower_bound"):
+        w[k] = float(w[k])
+    return w, f

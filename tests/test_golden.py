@@ -1,0 +1,94 @@
+"""The oracle restatement (oracle/k3x_oracle.c) against the golden fixtures
+that the reference's own CPU code produced (tests/golden/make_golden.py):
+bit for bit, with no reference tree or build needed. This is the pin that
+travels: tests/test_oracle_pin.py checks the same functions against the
+live reference build where it exists."""
+import numpy as np
+
+import golden_util as gu
+from golden.make_golden import POLICIES
+
+
+def test_route(rs):
+    f = gu.load("route.npz")
+    K = int(f["top_k"])
+    for t in range(f["hidden"].shape[0]):
+        ids, con, sco = rs.route_logits(rs.router_logits(f["hidden"][t], f["router"]), f["correction"], K,
+                                        want_scores=True)
+        np.testing.assert_array_equal(ids, f["ids"][t])
+        np.testing.assert_array_equal(con, f["contributions"][t])
+        np.testing.assert_array_equal(sco, f["scores"][t])
+
+
+def test_expert_major_plan(rs):
+    f = gu.load("expert_major.npz")
+    p = rs.expert_major_plan(f["ids"], f["contributions"])
+    for k in ("group_expert", "group_offset", "assign_token", "assign_slot", "assign_contrib"):
+        np.testing.assert_array_equal(p[k], f[k], err_msg=k)
+
+
+def test_mxfp4(rs):
+    f = gu.load("mxfp4.npz")
+    rows, cols = f["decoded"].shape
+    np.testing.assert_array_equal(rs.decode_mxfp4(f["packed"], f["scales"], rows, cols), f["decoded"])
+    np.testing.assert_array_equal(rs.mxfp4_matmul(f["x"], f["packed"], f["scales"], rows, cols), f["y"])
+
+
+def test_moe_layer(rs):
+    layer, hidden, out, ids, con = gu.moe_layer()
+    got_out, got_ids, got_con = rs.moe_layer(layer, hidden)
+    np.testing.assert_array_equal(got_ids, ids)
+    np.testing.assert_array_equal(got_con, con)
+    np.testing.assert_array_equal(got_out, out)
+
+
+def test_kda_block(rs):
+    w, f = gu.kda_block()
+    out, (cq, ck, cv, r) = rs.kda_block(w, f["x"], f["conv_q"], f["conv_k"], f["conv_v"], f["recurrent"].ravel())
+    np.testing.assert_array_equal(out, f["out"])
+    np.testing.assert_array_equal(cq, f["next_conv_q"])
+    np.testing.assert_array_equal(ck, f["next_conv_k"])
+    np.testing.assert_array_equal(cv, f["next_conv_v"])
+    np.testing.assert_array_equal(r.reshape(f["next_recurrent"].shape), f["next_recurrent"])
+
+
+def test_kda_block_tree_restatement_on_the_chain(rs):
+    """The draft-tree composition the GPU path is checked against, on a
+    chain, reproduces the reference block's outputs."""
+    w, f = gu.kda_block()
+    T = f["x"].shape[0]
+    got = rs.kda_block_tree(w, f["x"], np.arange(-1, T - 1), (f["conv_q"], f["conv_k"], f["conv_v"]),
+                            f["recurrent"].ravel())
+    np.testing.assert_array_equal(got, f["out"])
+
+
+def test_prepare_input(rs):
+    f = gu.load("prepare_input.npz")
+    for t in range(f["prefix"].shape[0]):
+        got = rs.prepare_input(f["prefix"][t], f["block"][t], f["norm"], f["proj"], f["post"], float(f["eps"]))
+        np.testing.assert_array_equal(got, f["out"][t])
+
+
+def test_select_routing(rs):
+    f = gu.load("select_routing.npz")
+    K = int(f["natural_k"])
+    for i, pol in enumerate(POLICIES):
+        for t in range(f["scores"].shape[0]):
+            st, r = rs.select_routing(f["scores"][t], f["bias"], K, **pol)
+            assert st == 0
+            n = int(f[f"p{i}_selected"][t])
+            assert r["selected_k"] == n, (i, t)
+            np.testing.assert_array_equal(r["expert_ids"], f[f"p{i}_ids"][t, :n])
+            np.testing.assert_array_equal(r["weights"], f[f"p{i}_weights"][t, :n])
+            assert r["escalated"] == bool(f[f"p{i}_escalated"][t])
+            stats = (r["normalized_entropy"], r["support"], r["mass"], r["boundary"])
+            np.testing.assert_array_equal(np.array(stats, np.float32), f[f"p{i}_stats"][t])
+
+
+def test_verify_greedy(rs):
+    f = gu.load("verify_greedy.npz")
+    p = f["drafts"].shape[1]
+    for s in range(f["drafts"].shape[0]):
+        a, com, _ = rs.verify_greedy_block(0, f["drafts"][s], p, int(f["vocab"]), f["targets"][s])
+        assert a == f["accepted"][s]
+        assert com == f["committed"][s, :f["count"][s]].tolist()
