@@ -161,6 +161,21 @@ def graphed(torch, ctx, step, stream, enabled):
     return g.replay, per, True
 
 
+def phase_profile(ctx, torch, step, steps):
+    """Device ms per step of each phase of the path (the library's phase
+    timing, k3xb_set_profiling), over `steps` eager steps run after the timed
+    region: the events it records never touch the reported numbers."""
+    ctx.set_profiling(True)
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize()
+    prof = ctx.profile()
+    ctx.set_profiling(False)
+    dropped = prof.pop("dropped")
+    return {"steps": steps, "dropped": dropped, "source": "CUDA events per phase (k3xb_get_profile), eager",
+            "ms_per_step": {k: round(v[0] / steps, 4) for k, v in prof.items()}}
+
+
 def make_c2_layer(ctx, torch, cfg, engine, act_terms):
     import k3xb
     H, I, E, Is = cfg["hidden"], cfg["inter"], cfg["experts"], cfg["shared_inter"]
@@ -357,6 +372,8 @@ def run_c4(args, rank, world, local, ctx, stream):
         "gpu_launches": launches, "clocks": clk.summary(),
         "accepted_mean": float(acc.float().mean().item()),
     }
+    if args.profile:
+        result["phases"] = phase_profile(ctx, torch, step, max(3, args.steps))
     if rank == 0:
         print(json.dumps(result), flush=True)
 
@@ -528,6 +545,8 @@ def run_c2_ep(args, rank, world, local, ctx, stream, cfg):
                      "alg_bytes_per_launch": alg, "unique_experts": unique, "traffic": None},
         "gpu_launches": launches, "clocks": clk.summary(),
     }
+    if args.profile:   # every rank takes the same profiled steps (same collectives)
+        result["phases"] = phase_profile(ctx, torch, step, max(3, args.steps))
     if rank == 0:
         print(json.dumps(result), flush=True)
     ctx.ep_finalize()
@@ -676,6 +695,8 @@ def run_ours(args):
         "gpu_launches": launches,
         "clocks": clk.summary(),
     }
+    if args.profile:
+        result["phases"] = phase_profile(ctx, torch, step, max(3, args.steps))
     if rank == 0 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(w, hidden, cfg, args)
     if rank == 0:
@@ -791,6 +812,8 @@ def main():
     ap.add_argument("--experts", type=int, default=0, help="c2 with fewer experts (small profiler case)")
     ap.add_argument("--tokens", type=int, default=0, help="c2 with another verify-token count")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a CUDA graph replay")
+    ap.add_argument("--profile", action="store_true",
+                    help="after the timed region, add per-phase device times (rank 0's) to the JSON line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -82,6 +82,49 @@ typedef struct {
 } k3xb_stats;
 int k3xb_get_stats(const k3xb_ctx* ctx, k3xb_stats* out);
 
+/* Device time per phase of the path (the reference's Profiler,
+ * runtime/include/k3x/profile.hpp:32-63, and the CUDA events its backend
+ * records around each operation). Every phase is also an NVTX range. With
+ * profiling on, each phase records a pair of CUDA events on its stream
+ * (none while a stream is captured into a graph); k3xb_get_profile waits
+ * for them and adds their elapsed time to the phase's total. Phases on the
+ * side stream (the shared expert) overlap others, so totals can sum to more
+ * than the call's wall time. */
+enum {
+    K3XB_PHASE_ROUTE = 0,          /* router logits + Top-k */
+    K3XB_PHASE_PLAN,               /* expert-major bucketing */
+    K3XB_PHASE_EXPERT_PREP,        /* work list, activation split, row gather */
+    K3XB_PHASE_EXPERT_GATEUP,      /* gate/up grouped GEMM + activation */
+    K3XB_PHASE_EXPERT_DOWN,        /* down grouped GEMM + scatter */
+    K3XB_PHASE_SHARED,             /* shared expert */
+    K3XB_PHASE_COMBINE,            /* slot-ordered combine (+ shared) */
+    K3XB_PHASE_EP_DISPATCH,        /* expert parallelism: send buffers */
+    K3XB_PHASE_EP_EXCHANGE,        /* rows + metadata all-to-all */
+    K3XB_PHASE_EP_RETURN,          /* expert outputs back to their tokens */
+    K3XB_PHASE_ATTN_RESIDUAL,      /* attention residual + RMSNorm */
+    K3XB_PHASE_KDA_PROJECT,        /* q/k/v/f/b/g projections */
+    K3XB_PHASE_KDA_CONV,           /* short conv, q/k norm, gates */
+    K3XB_PHASE_KDA_RECURRENCE,     /* gated delta rule over the draft tree */
+    K3XB_PHASE_KDA_OUTPUT,         /* gated norm + output projection */
+    K3XB_PHASE_EMBED,              /* token embedding */
+    K3XB_PHASE_LM_HEAD,            /* final norm + LM head */
+    K3XB_PHASE_ACCEPT,             /* greedy / rejection acceptance */
+    K3XB_PHASE_COMMIT,             /* state commit of the accepted path */
+    K3XB_PHASE_COUNT
+};
+typedef struct {
+    double device_ms;   /* summed over calls */
+    uint64_t calls;
+} k3xb_phase_time;
+/* enable != 0 starts recording; either way the totals are cleared. */
+int k3xb_set_profiling(k3xb_ctx* ctx, int enable);
+/* Synchronises with the recorded events and copies K3XB_PHASE_COUNT totals
+ * to out. dropped (may be NULL): phases not timed because more than 4096
+ * were pending; read the profile at least every few thousand phases. */
+int k3xb_get_profile(k3xb_ctx* ctx, k3xb_phase_time* out, uint64_t* dropped);
+/* Name of a K3XB_PHASE_* value ("route", "expert_gateup", ...), or NULL. */
+const char* k3xb_phase_name(int phase);
+
 /* ---- (a) router ---------------------------------------------------------- */
 /* route_official_moe (runtime/src/official_moe.cpp:247-269) for T tokens:
  * logits = float(sum_h double(bf16 W[e][h]) * hidden[t][h]) summed in h

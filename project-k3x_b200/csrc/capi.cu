@@ -7,6 +7,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "profile.cuh"
 
 namespace k3xb {
 
@@ -128,15 +129,26 @@ int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidd
         K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->side_stream, ctx->ev_fork, 0));
         cudaStream_t main = ctx->stream;
         ctx->stream = ctx->side_stream;
-        st = launch_shared_tc(ctx, L, hidden, T, s.sxb, s.sbd, s.shared_out);
+        {
+            PhaseScope ph(ctx, K3XB_PHASE_SHARED);
+            st = launch_shared_tc(ctx, L, hidden, T, s.sxb, s.sbd, s.shared_out);
+        }
         ctx->stream = main;
         if (st) return st;
         K3XB_CUDA(ctx, cudaEventRecord(ctx->ev_join, ctx->side_stream));
     }
-    if ((st = launch_router_logits(ctx, hidden, T, H, L.router, E, s.logits))) return st;
-    if ((st = launch_topk(ctx, s.logits, L.correction, T, E, K, ids, contrib, nullptr, s.plan.status))) return st;
-    if ((st = launch_plan(ctx, ids, contrib, T, K, E, s.plan))) return st;
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_ROUTE);
+        if ((st = launch_router_logits(ctx, hidden, T, H, L.router, E, s.logits))) return st;
+        if ((st = launch_topk(ctx, s.logits, L.correction, T, E, K, ids, contrib, nullptr, s.plan.status)))
+            return st;
+    }
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_PLAN);
+        if ((st = launch_plan(ctx, ids, contrib, T, K, E, s.plan))) return st;
+    }
     if (L.engine == K3XB_ENGINE_SIMT) {
+        PhaseScope ph(ctx, K3XB_PHASE_EXPERT_GATEUP);
         if ((st = launch_simt_experts(ctx, L, hidden, T, s.plan, s.act, s.slot_out))) return st;
     } else {
         if ((st = launch_mxf4_experts(ctx, L, hidden, T, s.plan, s.slot_out))) return st;
@@ -149,6 +161,7 @@ int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidd
         K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
         shared = s.shared_out;
     } else if (L.shared_gate) {
+        PhaseScope ph(ctx, K3XB_PHASE_SHARED);
         const uint32_t Is = L.shared_inter;
         if ((st = launch_bf16_rows(ctx, hidden, L.shared_gate, T, Is, H, s.sg))) return st;
         if ((st = launch_bf16_rows(ctx, hidden, L.shared_up, T, Is, H, s.su))) return st;
@@ -157,7 +170,10 @@ int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidd
         if ((st = launch_bf16_rows(ctx, s.sa, L.shared_down, T, H, Is, s.shared_out))) return st;
         shared = s.shared_out;
     }
-    if ((st = launch_combine(ctx, s.slot_out, contrib, shared, T, K, H, out))) return st;
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_COMBINE);
+        if ((st = launch_combine(ctx, s.slot_out, contrib, shared, T, K, H, out))) return st;
+    }
     ++ctx->stats.moe_layer_calls;
     return K3XB_OK;
 }
@@ -208,6 +224,7 @@ int k3xb_destroy(k3xb_ctx* ctx) {
     if (ctx->status_word) cudaFree(ctx->status_word);
     release_mxf4_resources(ctx);
     release_resident(ctx);
+    release_profiler(ctx);
     release_ep(ctx);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     if (ctx->side_stream) cudaStreamDestroy(ctx->side_stream);
@@ -261,6 +278,7 @@ int k3xb_route(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_t H, const
     if (st) return st;
     Carver c(base);
     float* logits = c.take<float>(static_cast<size_t>(T) * E);
+    PhaseScope ph(ctx, K3XB_PHASE_ROUTE);
     if ((st = launch_router_logits(ctx, hidden, T, H, router, E, logits))) return st;
     if ((st = launch_topk(ctx, logits, correction, T, E, K, ids, contrib, scores, ctx->status_word))) return st;
     ++ctx->stats.route_calls;
@@ -301,6 +319,7 @@ int k3xb_expert_major_plan(k3xb_ctx* ctx, const uint32_t* ids, const float* cont
     if (!T || !K) return fail(ctx, K3XB_INVALID_EXTENT, "empty routes");   // expert_major.cpp:12-14
     k3xb_plan p = *plan;
     if (!p.status) p.status = ctx->status_word;
+    PhaseScope ph(ctx, K3XB_PHASE_PLAN);
     return launch_plan(ctx, ids, contrib, T, K, E, p);
 }
 
@@ -511,6 +530,7 @@ int k3xb_kda_tree(k3xb_ctx* ctx, const float* state, const int32_t* parent, uint
     KdaSchedule sch;
     int st = schedule_tree(ctx, parent, nodes, sch);
     if (st) return st;
+    PhaseScope ph(ctx, K3XB_PHASE_KDA_RECURRENCE);
     return kda_common(ctx, state, nodes, S, heads, head_dim, q, k, v, ld, beta, out, nullptr, sch);
 }
 
@@ -524,6 +544,7 @@ int k3xb_kda_commit(k3xb_ctx* ctx, const float* state, const int32_t* parent, ui
         if (parent[i] < -1 || parent[i] >= static_cast<int32_t>(i))
             return fail(ctx, K3XB_INVALID_EXTENT, "draft tree: parent[n] must be -1 or < n");
     // sequences may commit different nodes: group them by path
+    PhaseScope ph(ctx, K3XB_PHASE_COMMIT);
     const size_t sstride = static_cast<size_t>(heads) * head_dim * head_dim;
     for (uint32_t s = 0; s < S; ++s) {
         const int32_t node = commit_node[s];
@@ -562,6 +583,7 @@ int k3xb_accept_greedy(k3xb_ctx* ctx, const float* logits, const uint32_t* draft
         t = static_cast<uint32_t*>(base);
     }
     ++ctx->stats.accept_calls;
+    PhaseScope ph(ctx, K3XB_PHASE_ACCEPT);
     return launch_accept_greedy(ctx, logits, drafts, S, p, V, t, accepted, committed, count);
 }
 
@@ -579,6 +601,7 @@ int k3xb_accept_rejection(k3xb_ctx* ctx, const float* tl, const float* dl, const
     double* pd = c.take<double>(static_cast<size_t>(S) * (p + 1));
     double* qd = c.take<double>(static_cast<size_t>(S) * (p + 1));
     ++ctx->stats.accept_calls;
+    PhaseScope ph(ctx, K3XB_PHASE_ACCEPT);
     return launch_accept_rejection(ctx, tl, dl, drafts, S, p, V, temperature, seed, seq_base, pd, qd,
                                    accepted, committed, count);
 }
@@ -722,31 +745,41 @@ int kda_block_device(k3xb_ctx* ctx, const k3xb_kda_layer& w, uint32_t H, const f
     const uint32_t T = N * S, h = w.heads, d = w.head_dim, P = h * d, cw = w.conv_width;
     int st;
     const float* xin = x;
-    if (!x_is_bf16) {   // the block rounds its input first (official_kda.cpp:235-240)
-        if ((st = launch_residual_round(ctx, x, static_cast<size_t>(T) * H, wk.xr))) return st;
-        xin = wk.xr;
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_KDA_PROJECT);
+        if (!x_is_bf16) {   // the block rounds its input first (official_kda.cpp:235-240)
+            if ((st = launch_residual_round(ctx, x, static_cast<size_t>(T) * H, wk.xr))) return st;
+            xin = wk.xr;
+        }
+        if ((st = launch_split_terms(ctx, xin, T, H, 1, wk.xt_h))) return st;
+        if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.q_proj, T, P, H, 1, tr.pq))) return st;
+        if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.k_proj, T, P, H, 1, tr.pk))) return st;
+        if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.v_proj, T, P, H, 1, tr.pv))) return st;
+        if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.g_proj, T, P, H, 1, wk.og))) return st;
+        if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.f_a_proj, T, d, H, 1, wk.fl))) return st;
+        if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.b_proj, T, h, H, 1, wk.bp))) return st;
+        if ((st = launch_split_terms(ctx, wk.fl, T, d, 1, wk.xt_d))) return st;
+        if ((st = launch_linear_terms(ctx, wk.xt_d, 1, w.f_b_proj, T, P, d, 1, wk.fg))) return st;
     }
-    if ((st = launch_split_terms(ctx, xin, T, H, 1, wk.xt_h))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.q_proj, T, P, H, 1, tr.pq))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.k_proj, T, P, H, 1, tr.pk))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.v_proj, T, P, H, 1, tr.pv))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.g_proj, T, P, H, 1, wk.og))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.f_a_proj, T, d, H, 1, wk.fl))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.b_proj, T, h, H, 1, wk.bp))) return st;
-    if ((st = launch_split_terms(ctx, wk.fl, T, d, 1, wk.xt_d))) return st;
-    if ((st = launch_linear_terms(ctx, wk.xt_d, 1, w.f_b_proj, T, P, d, 1, wk.fg))) return st;
-    const float* proj[3] = {tr.pq, tr.pk, tr.pv};
-    const float* cwt[3] = {w.q_conv, w.k_conv, w.v_conv};
-    float* const co[3] = {wk.cq, wk.ck, tr.cv};
-    if ((st = launch_short_conv(ctx, proj, cwt, conv, wk.tables, S, N, P, cw, co))) return st;
-    if ((st = launch_qk_gates(ctx, wk.cq, wk.ck, wk.fg, wk.bp, w.a_log, w.dt_bias, w.gate_lower_bound, T, h, d,
-                              tr.qn, tr.kn, tr.ld, tr.be)))
-        return st;
-    const int32_t* sched = wk.tables + static_cast<size_t>(N) * (cw - 1);
-    const size_t visit = sch.order.size();
-    if ((st = launch_kda(ctx, rec, sched, sched + visit, sched + 2 * visit, static_cast<uint32_t>(visit), N, S, h, d,
-                         tr.qn, tr.kn, tr.cv, tr.ld, tr.be, wk.ro, nullptr, sch.levels)))
-        return st;
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_KDA_CONV);
+        const float* proj[3] = {tr.pq, tr.pk, tr.pv};
+        const float* cwt[3] = {w.q_conv, w.k_conv, w.v_conv};
+        float* const co[3] = {wk.cq, wk.ck, tr.cv};
+        if ((st = launch_short_conv(ctx, proj, cwt, conv, wk.tables, S, N, P, cw, co))) return st;
+        if ((st = launch_qk_gates(ctx, wk.cq, wk.ck, wk.fg, wk.bp, w.a_log, w.dt_bias, w.gate_lower_bound, T, h, d,
+                                  tr.qn, tr.kn, tr.ld, tr.be)))
+            return st;
+    }
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_KDA_RECURRENCE);
+        const int32_t* sched = wk.tables + static_cast<size_t>(N) * (cw - 1);
+        const size_t visit = sch.order.size();
+        if ((st = launch_kda(ctx, rec, sched, sched + visit, sched + 2 * visit, static_cast<uint32_t>(visit), N, S, h,
+                             d, tr.qn, tr.kn, tr.cv, tr.ld, tr.be, wk.ro, nullptr, sch.levels)))
+            return st;
+    }
+    PhaseScope ph(ctx, K3XB_PHASE_KDA_OUTPUT);
     if ((st = launch_gated_norm(ctx, wk.ro, wk.og, w.o_norm, w.eps, T, h, d, wk.gt))) return st;
     if ((st = launch_split_terms(ctx, wk.gt, T, P, 1, wk.xt_p))) return st;
     ++ctx->stats.kda_calls;
@@ -810,15 +843,19 @@ int layer_forward_impl(k3xb_ctx* ctx, const k3xb_layer& L, const float* hidden_i
     set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
     wk.tables = const_cast<int32_t*>(d_tables);
     float *xin = bufs[0], *kda_out = bufs[1], *prefix = bufs[2], *moe_in = bufs[3];
-    // official_layer.cpp:159-172: attention residual + input norm
-    if ((st = launch_attnres_norm(ctx, hidden_in, nullptr, block, L.self_residual_norm, L.self_residual_proj,
-                                  L.input_norm, T, H, L.rms_eps, nullptr, xin)))
-        return st;
+    {   // official_layer.cpp:159-172: attention residual + input norm
+        PhaseScope ph(ctx, K3XB_PHASE_ATTN_RESIDUAL);
+        if ((st = launch_attnres_norm(ctx, hidden_in, nullptr, block, L.self_residual_norm, L.self_residual_proj,
+                                      L.input_norm, T, H, L.rms_eps, nullptr, xin)))
+            return st;
+    }
     if ((st = kda_block_device(ctx, L.kda, H, xin, true, N, S, conv, rec, sch, tr, wk, kda_out))) return st;
-    // :190-205: prefix, MoE input preparation
-    if ((st = launch_attnres_norm(ctx, hidden_in, kda_out, block, L.moe_residual_norm, L.moe_residual_proj,
-                                  L.post_norm, T, H, L.rms_eps, prefix, moe_in)))
-        return st;
+    {   // :190-205: prefix, MoE input preparation
+        PhaseScope ph(ctx, K3XB_PHASE_ATTN_RESIDUAL);
+        if ((st = launch_attnres_norm(ctx, hidden_in, kda_out, block, L.moe_residual_norm, L.moe_residual_proj,
+                                      L.post_norm, T, H, L.rms_eps, prefix, moe_in)))
+            return st;
+    }
     // plain MoE: combined = round_bf16(routed + shared), then the residual (official_moe.cpp:336-341)
     if ((st = moe_forward_device(ctx, L.moe, moe_in, T, hidden_out, ids_out, nullptr, ms))) return st;
     return launch_residual(ctx, prefix, hidden_out, static_cast<size_t>(T) * H, hidden_out);
@@ -915,9 +952,12 @@ int k3xb_kda_block_commit(k3xb_ctx* ctx, const k3xb_kda_layer* w, const void* tr
     K3XB_CUDA(ctx, cudaMemcpyAsync(base, anc.data(), anc.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
                                    ctx->stream));
     const float* proj[3] = {tr.pq, tr.pk, tr.pv};
-    if ((st = launch_conv_commit(ctx, proj, conv, static_cast<const int32_t*>(base), S, N, static_cast<uint32_t>(P),
-                                 cw, conv_out)))
-        return st;
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_COMMIT);
+        if ((st = launch_conv_commit(ctx, proj, conv, static_cast<const int32_t*>(base), S, N,
+                                     static_cast<uint32_t>(P), cw, conv_out)))
+            return st;
+    }
     return k3xb_kda_commit(ctx, rec, parent, N, S, h, d, tr.qn, tr.kn, tr.cv, tr.ld, tr.be, commit_node, rec_out);
 }
 
@@ -1055,6 +1095,7 @@ int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verif
                                    ctx->stream));
     const float* x = io->hidden_in;
     if (m->embedding) {
+        PhaseScope ph(ctx, K3XB_PHASE_EMBED);
         if ((st = launch_embed(ctx, io->tokens, m->embedding, V, T, H, x0))) return st;
         x = x0;
     }
@@ -1068,25 +1109,32 @@ int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verif
             return st;
         x = out;
     }
-    if (m->final_norm) {
-        float* y = buf[m->layers & 1u];
-        if ((st = launch_rms_norm(ctx, x, m->final_norm, T, H, m->final_eps, y))) return st;
-        x = y;
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_LM_HEAD);
+        if (m->final_norm) {
+            float* y = buf[m->layers & 1u];
+            if ((st = launch_rms_norm(ctx, x, m->final_norm, T, H, m->final_eps, y))) return st;
+            x = y;
+        }
+        // LM head: bf16 matvec semantics (official_moe.cpp:39-59), logits rounded to bf16
+        if ((st = launch_split_terms(ctx, x, T, H, 1, xt))) return st;
+        if ((st = launch_linear_terms(ctx, xt, 1, m->lm_head, T, V, H, 1, logits))) return st;
     }
-    // LM head: bf16 matvec semantics (official_moe.cpp:39-59), logits rounded to bf16
-    if ((st = launch_split_terms(ctx, x, T, H, 1, xt))) return st;
-    if ((st = launch_linear_terms(ctx, xt, 1, m->lm_head, T, V, H, 1, logits))) return st;
-    if (io->mode == K3XB_ACCEPT_GREEDY) {
-        st = launch_accept_greedy(ctx, logits, io->draft_tokens, S, p, V, targets, io->accepted, io->committed,
-                                  io->committed_count);
-    } else {
-        st = launch_accept_rejection(ctx, logits, io->draft_logits, io->draft_tokens, S, p, V, io->temperature,
-                                     io->seed, io->sequence_base, pd, qd, io->accepted, io->committed,
-                                     io->committed_count);
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_ACCEPT);
+        if (io->mode == K3XB_ACCEPT_GREEDY) {
+            st = launch_accept_greedy(ctx, logits, io->draft_tokens, S, p, V, targets, io->accepted,
+                                      io->committed, io->committed_count);
+        } else {
+            st = launch_accept_rejection(ctx, logits, io->draft_logits, io->draft_tokens, S, p, V, io->temperature,
+                                         io->seed, io->sequence_base, pd, qd, io->accepted, io->committed,
+                                         io->committed_count);
+        }
     }
     if (st) return st;
     ++ctx->stats.accept_calls;
     // commit every layer at node accepted[s] (model.cpp:1660-1664), on the device
+    PhaseScope commit_phase(ctx, K3XB_PHASE_COMMIT);
     const int32_t* sched = d_tables + static_cast<size_t>(N) * (cw - 1);
     for (uint32_t l = 0; l < m->layers; ++l) {
         KdaTrace tr{};
@@ -1146,13 +1194,20 @@ int k3xb_ep_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* local, uint32
         K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->side_stream, ctx->ev_fork, 0));
         cudaStream_t main = ctx->stream;
         ctx->stream = ctx->side_stream;
-        st = launch_shared_tc(ctx, *local, hidden, T, sxb, sbd, shared_out);
+        {
+            PhaseScope ph(ctx, K3XB_PHASE_SHARED);
+            st = launch_shared_tc(ctx, *local, hidden, T, sxb, sbd, shared_out);
+        }
         ctx->stream = main;
         if (st) return st;
         K3XB_CUDA(ctx, cudaEventRecord(ctx->ev_join, ctx->side_stream));
     }
-    if ((st = launch_router_logits(ctx, hidden, T, H, local->router, E, logits))) return st;
-    if ((st = launch_topk(ctx, logits, local->correction, T, E, K, ids, contrib, nullptr, ctx->status_word))) return st;
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_ROUTE);
+        if ((st = launch_router_logits(ctx, hidden, T, H, local->router, E, logits))) return st;
+        if ((st = launch_topk(ctx, logits, local->correction, T, E, K, ids, contrib, nullptr, ctx->status_word)))
+            return st;
+    }
     if (shared) K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
     if ((st = ep_moe_forward(ctx, *local, E, hidden, T, ids, contrib, shared ? shared_out : nullptr, region, out)))
         return st;

@@ -26,6 +26,7 @@ struct k3xb_ctx {
     void* mxf4_state = nullptr;       // MXF4-engine resources (tensor maps, attributes)
     void* ep_state = nullptr;         // expert parallelism: NCCL communicator
     void* resident = nullptr;         // resident weight table (resident.cu)
+    void* profiler = nullptr;         // phase timing (profile.cu), NULL when off
 };
 
 namespace k3xb {

@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "profile.cuh"
 
 namespace k3xb {
 
@@ -245,13 +246,17 @@ int ep_moe_forward(k3xb_ctx* ctx, const k3xb_moe_layer& L, uint32_t E, const flo
     plan.group_count = c.take<uint32_t>(1);
     plan.status = ctx->status_word;
     const size_t nm = static_cast<size_t>(G) * T * K;
-    ep_dispatch_kernel<<<static_cast<unsigned>((nm + 255) / 256), 256, 0, ctx->stream>>>(ids, T, K, E_r, G,
-                                                                                         send_meta);
-    K3XB_LAUNCHED(ctx);
-    ep_rows_kernel<<<dim3(T, G), 256, 0, ctx->stream>>>(hidden, T, H, send_x);
-    K3XB_LAUNCHED(ctx);
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_EP_DISPATCH);
+        ep_dispatch_kernel<<<static_cast<unsigned>((nm + 255) / 256), 256, 0, ctx->stream>>>(ids, T, K, E_r, G,
+                                                                                             send_meta);
+        K3XB_LAUNCHED(ctx);
+        ep_rows_kernel<<<dim3(T, G), 256, 0, ctx->stream>>>(hidden, T, H, send_x);
+        K3XB_LAUNCHED(ctx);
+    }
     int st;
     {   // metadata and rows in one NCCL group
+        PhaseScope ph(ctx, K3XB_PHASE_EP_EXCHANGE);
         const NcclApi& api = nccl();
         K3XB_NCCL(ctx, api.group_start());
         for (uint32_t g = 0; g < G; ++g) {
@@ -263,11 +268,18 @@ int ep_moe_forward(k3xb_ctx* ctx, const k3xb_moe_layer& L, uint32_t E, const flo
         }
         K3XB_NCCL(ctx, api.group_end());
     }
-    ep_plan_kernel<<<1, 1024, (E_r + 1) * sizeof(uint32_t), ctx->stream>>>(recv_meta, G * T, K, E_r, plan);
-    K3XB_LAUNCHED(ctx);
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_PLAN);
+        ep_plan_kernel<<<1, 1024, (E_r + 1) * sizeof(uint32_t), ctx->stream>>>(recv_meta, G * T, K, E_r, plan);
+        K3XB_LAUNCHED(ctx);
+    }
     if ((st = launch_mxf4_experts(ctx, L, recv_x, G * T, plan, nullptr, y))) return st;
-    if ((st = all_to_all(ctx, y, y_home, static_cast<size_t>(T) * K * H, ncclBfloat16, 2))) return st;
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_EP_RETURN);
+        if ((st = all_to_all(ctx, y, y_home, static_cast<size_t>(T) * K * H, ncclBfloat16, 2))) return st;
+    }
     const size_t n = static_cast<size_t>(T) * H;
+    PhaseScope ph(ctx, K3XB_PHASE_COMBINE);
     ep_combine_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(y_home, ids, contrib, shared,
                                                                                        T, K, H, E_r, out);
     K3XB_LAUNCHED(ctx);

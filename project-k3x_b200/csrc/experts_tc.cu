@@ -32,6 +32,7 @@
 //                  combine (c)
 #include "common.cuh"
 #include "kernels.cuh"
+#include "profile.cuh"
 #include "tc_pipeline.cuh"
 
 namespace k3xb {
@@ -595,8 +596,12 @@ int launch_routed(k3xb_ctx* ctx, const CUtensorMap& map_gate, const CUtensorMap&
                                             static_cast<int>(smem_d)));
         configured = true;
     }
-    gateup_kernel<NM><<<ctx->sm_count, kThreads, smem_gu, ctx->stream>>>(map_gate, map_up, map_bgu, gp);
-    K3XB_LAUNCHED(ctx);
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_EXPERT_GATEUP);
+        gateup_kernel<NM><<<ctx->sm_count, kThreads, smem_gu, ctx->stream>>>(map_gate, map_up, map_bgu, gp);
+        K3XB_LAUNCHED(ctx);
+    }
+    PhaseScope ph(ctx, K3XB_PHASE_EXPERT_DOWN);
     down_kernel<NM><<<ctx->sm_count, kThreads, smem_d, ctx->stream>>>(map_down, map_bd, dp);
     K3XB_LAUNCHED(ctx);
     return K3XB_OK;
@@ -638,6 +643,7 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
     Carver c(reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ctx->mxf4_scratch) + 1023) & ~uintptr_t(1023)));
     Buffers bf;
     carve(c, l, &bf);
+    PhaseScope prep(ctx, K3XB_PHASE_EXPERT_PREP);
     const uint8_t* sfa_gate = L.gate_scales_tc;
     const uint8_t* sfa_up = L.up_scales_tc;
     const uint8_t* sfa_down = L.down_scales_tc;
@@ -665,6 +671,7 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
     gather_gu_kernel<<<l.max_tiles, 256, 0, ctx->stream>>>(bf.tsplit, bf.tsf, H, plan.assign_token, bf.tb, l.terms,
                                                            l.nmax, bf.b_gu, bf.sfb_gu);
     K3XB_LAUNCHED(ctx);
+    prep.end();
 
     GuParams gp{bf.tb.desc_gu, bf.tb.counts + 1, sfa_gate, sfa_up, bf.sfb_gu, bf.b_d, bf.sfb_d, H, I, l.terms,
                 L.activation, L.situ_beta, L.situ_linear_beta, ctx->status_word};

@@ -99,6 +99,13 @@ class Stats(C.Structure):
         "peak_resident_weight_bytes", "weight_h2d_bytes")]
 
 
+PHASE_COUNT = 19   # K3XB_PHASE_COUNT
+
+
+class PhaseTime(C.Structure):
+    _fields_ = [("device_ms", C.c_double), ("calls", C.c_uint64)]
+
+
 WEIGHT_F32, WEIGHT_BF16, WEIGHT_MXFP4, WEIGHT_EXPERT_STACK = 0, 1, 2, 3
 RESIDENT_HIT, RESIDENT_ADMITTED, RESIDENT_BYPASS = 0, 1, 2
 
@@ -168,6 +175,8 @@ def library() -> C.CDLL:
                                           C.POINTER(ResidentStack)],
             "k3xb_release_resident": [vp],
             "k3xb_expert_grid_host": [vp, C.POINTER(MoeLayer), vp, u32, vp, u32, vp],
+            "k3xb_set_profiling": [vp, C.c_int],
+            "k3xb_get_profile": [vp, C.POINTER(PhaseTime), C.POINTER(u64)],
             "k3xb_kda_block_host": [vp, C.POINTER(KdaLayer), u32, vp, u32, vp, vp, vp],
         }
         for name, args in sigs.items():
@@ -176,6 +185,8 @@ def library() -> C.CDLL:
             fn.restype = C.c_int
         lib.k3xb_kda_trace_bytes.argtypes = [C.POINTER(KdaLayer), u32, u32]
         lib.k3xb_kda_trace_bytes.restype = sz
+        lib.k3xb_phase_name.argtypes = [C.c_int]
+        lib.k3xb_phase_name.restype = C.c_char_p
         _lib = lib
     return _lib
 
@@ -379,6 +390,21 @@ class Context:
         self._check(self.lib.k3xb_prepare_mxfp4_scales(self.h, _p(scales), rows, cols, _p(out)),
                     "prepare_mxfp4_scales")
 
+    # ---- phase profile ----------------------------------------------------------
+    def set_profiling(self, on: bool):
+        """Starts (or stops) per-phase device timing; clears the totals."""
+        self._check(self.lib.k3xb_set_profiling(self.h, 1 if on else 0), "set_profiling")
+
+    def profile(self) -> dict:
+        """{phase name: (device ms summed, calls)} for phases that ran, and
+        "dropped": phases not timed."""
+        arr = (PhaseTime * PHASE_COUNT)()
+        dropped = C.c_uint64()
+        self._check(self.lib.k3xb_get_profile(self.h, arr, C.byref(dropped)), "get_profile")
+        out = {phase_name(i): (arr[i].device_ms, arr[i].calls) for i in range(PHASE_COUNT) if arr[i].calls}
+        out["dropped"] = dropped.value
+        return out
+
     # ---- resident weights (host arrays -> device copies keyed by tensor id) ----
     def set_resident_capacity(self, nbytes: int):
         self._check(self.lib.k3xb_set_resident_capacity(self.h, nbytes), "set_resident_capacity")
@@ -472,6 +498,11 @@ def moe_layer_desc(w: dict, engine=ENGINE_SIMT, act_terms=6) -> MoeLayer:
     L.engine = engine
     L.act_terms = act_terms
     return L
+
+
+def phase_name(i: int) -> str:
+    n = library().k3xb_phase_name(i)
+    return n.decode() if n else None
 
 
 def stack_layer_desc(stack: ResidentStack, w: dict, engine=ENGINE_MXF4, act_terms=6) -> MoeLayer:

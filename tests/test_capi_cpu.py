@@ -68,3 +68,21 @@ def test_resident_entry_points_marshal_and_reject_null_context():
     assert lib.k3xb_acquire_expert_stack(None, 1, 2, 128, 128, views, C.byref(stack)) == k3xb.INVALID_EXTENT
     assert lib.k3xb_set_resident_capacity(None, 0) == k3xb.INVALID_EXTENT
     assert lib.k3xb_release_resident(None) == k3xb.INVALID_EXTENT
+
+
+def test_profiling_entry_points():
+    """Phase names cover every K3XB_PHASE_* value of the header; the calls
+    refuse a null context before any CUDA call."""
+    import re
+
+    import k3xb
+    lib = k3xb.library()
+    header = open(HEADER).read()
+    block = header[header.index("K3XB_PHASE_ROUTE = 0"):header.index("K3XB_PHASE_COUNT")]
+    assert len(re.findall(r"K3XB_PHASE_\w+", block)) == k3xb.PHASE_COUNT
+    names = [k3xb.phase_name(i) for i in range(k3xb.PHASE_COUNT)]
+    assert all(names) and len(set(names)) == k3xb.PHASE_COUNT and names[0] == "route"
+    assert k3xb.phase_name(k3xb.PHASE_COUNT) is None and k3xb.phase_name(-1) is None
+    arr = (k3xb.PhaseTime * k3xb.PHASE_COUNT)()
+    assert lib.k3xb_set_profiling(None, 1) == k3xb.INVALID_EXTENT
+    assert lib.k3xb_get_profile(None, arr, None) == k3xb.INVALID_EXTENT
