@@ -110,6 +110,7 @@ enum {
     K3XB_PHASE_LM_HEAD,            /* final norm + LM head */
     K3XB_PHASE_ACCEPT,             /* greedy / rejection acceptance */
     K3XB_PHASE_COMMIT,             /* state commit of the accepted path */
+    K3XB_PHASE_LATENT,             /* LatentMoE projections and routed norm */
     K3XB_PHASE_COUNT
 };
 typedef struct {
@@ -230,6 +231,18 @@ typedef struct {
     const uint8_t* gate_scales_tc;
     const uint8_t* up_scales_tc;
     const uint8_t* down_scales_tc;
+    /* LatentMoE (official_moe_cpu, official_moe.cpp:271-344 with :296 and
+     * :322-331): latent = round_bf16(routed_down . hidden) [L]; the experts
+     * work on the latent row (their stacks are gate/up [E][I][L/2], down
+     * [E][L][I/2]); mixed = round_bf16(slot-ordered combine) [L]; routed =
+     * round_bf16(routed_up . rms_norm(mixed, routed_norm, latent_eps)) [H];
+     * out = round_bf16(routed + shared). latent = 0: the plain MoE above.
+     * The router still reads the hidden row. */
+    uint32_t latent;
+    const uint16_t* routed_down;   /* [L][H] bf16 */
+    const uint16_t* routed_norm;   /* [L] bf16 */
+    const uint16_t* routed_up;     /* [H][L] bf16 */
+    float latent_eps;
 } k3xb_moe_layer;
 
 /* bf16_matvec (runtime/src/official_moe.cpp:39-59) for many tokens on
@@ -263,7 +276,9 @@ int k3xb_moe_layer_forward_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer,
                                 float* contributions_host);
 
 /* Expert FFN only, for an existing plan (mxfp4_situ_mlp_grid,
- * backend.hpp:357-363): y[t][slot][H] = round_bf16(expert(hidden[t])). */
+ * backend.hpp:357-363): y[t][slot][D] = round_bf16(expert(hidden[t])), D the
+ * experts' width (the latent width of a LatentMoE layer, whose rows the
+ * caller then passes as `hidden`). */
 int k3xb_moe_experts(k3xb_ctx* ctx, const k3xb_moe_layer* layer,
                      const float* hidden, uint32_t tokens,
                      const k3xb_plan* plan, float* slot_out);
@@ -349,7 +364,8 @@ int k3xb_acquire_expert_stack(k3xb_ctx* ctx, uint64_t stack_id, uint32_t experts
 int k3xb_release_resident(k3xb_ctx* ctx);
 
 /* mxfp4_situ_mlp_grid (backend.hpp:357-363, CPU semantics
- * backend_cpu.cpp:191-262) over a stack of experts: out[j][t][H] =
+ * backend_cpu.cpp:191-262) over a stack of experts (rows of the experts'
+ * width H: the latent width for a LatentMoE layer): out[j][t][H] =
  * expert_{expert_ids[j]}(inputs[t]) for j < n, t < tokens: gate/up MXFP4
  * products, the layer's activation, down product rounded to bf16 as
  * expert_ffn (official_moe.cpp:82-103) does (the reference backend's

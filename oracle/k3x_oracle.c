@@ -594,27 +594,43 @@ int k3xo_moe_layer_forward(const k3xo_moe_layer* L, const float* hidden,
                            float* contributions)
 {
     const size_t H = L->hidden, I = L->inter, E = L->experts, K = L->top_k;
+    const size_t D = L->latent ? L->latent : H;   /* the experts' width */
     float* logits = (float*)malloc(E * sizeof(float));
-    float* y = (float*)malloc(K * H * sizeof(float));
-    float* mixed = (float*)malloc(H * sizeof(float));
+    float* y = (float*)malloc(K * D * sizeof(float));
+    float* mixed = (float*)malloc(D * sizeof(float));
     float* shared = (float*)malloc(H * sizeof(float));
+    float* lat = (float*)malloc(D * sizeof(float));
+    float* normed = (float*)malloc(D * sizeof(float));
+    float* routed = (float*)malloc(H * sizeof(float));
     int st = K3XO_OK;
     for (size_t t = 0; t < tokens && st == K3XO_OK; ++t) {
         const float* x = hidden + t * H;
+        const float* xe = x;
         st = k3xo_router_logits(x, L->router, E, H, logits);
         if (st == K3XO_OK)
             st = k3xo_route_logits(logits, L->correction, E, K, ids + t * K,
                                    contributions + t * K, NULL);
+        if (st == K3XO_OK && L->latent) {   /* official_moe.cpp:296 */
+            st = k3xo_bf16_matvec(x, L->routed_down, D, H, lat);
+            xe = lat;
+        }
         for (size_t s = 0; s < K && st == K3XO_OK; ++s) {
             size_t e = ids[t * K + s];
-            k3xo_mxfp4 g = {L->gate_packed + e * I * H / 2, L->gate_scales + e * I * H / 32};
-            k3xo_mxfp4 u = {L->up_packed + e * I * H / 2, L->up_scales + e * I * H / 32};
-            k3xo_mxfp4 d = {L->down_packed + e * H * I / 2, L->down_scales + e * H * I / 32};
-            st = k3xo_expert_ffn(x, g, u, d, H, I, L->activation, L->situ_beta,
-                                 L->situ_linear_beta, y + s * H);
+            k3xo_mxfp4 g = {L->gate_packed + e * I * D / 2, L->gate_scales + e * I * D / 32};
+            k3xo_mxfp4 u = {L->up_packed + e * I * D / 2, L->up_scales + e * I * D / 32};
+            k3xo_mxfp4 d = {L->down_packed + e * D * I / 2, L->down_scales + e * D * I / 32};
+            st = k3xo_expert_ffn(xe, g, u, d, D, I, L->activation, L->situ_beta,
+                                 L->situ_linear_beta, y + s * D);
         }
         if (st != K3XO_OK) break;
-        k3xo_routed_combine(y, contributions + t * K, K, H, mixed);
+        k3xo_routed_combine(y, contributions + t * K, K, D, mixed);
+        if (L->latent) {   /* :323-331: normalized(mixed, routed_norm), routed_up */
+            st = k3xo_rms_norm_bf16(mixed, L->routed_norm, D, L->latent_eps, normed);
+            if (st == K3XO_OK) st = k3xo_bf16_matvec(normed, L->routed_up, H, D, routed);
+            if (st != K3XO_OK) break;
+        } else {
+            for (size_t i = 0; i < H; ++i) routed[i] = mixed[i];
+        }
         if (L->shared_gate) {
             st = k3xo_shared_ffn(x, L->shared_gate, L->shared_up, L->shared_down, H,
                                  L->shared_inter, L->activation, L->situ_beta,
@@ -623,12 +639,15 @@ int k3xo_moe_layer_forward(const k3xo_moe_layer* L, const float* hidden,
             for (size_t i = 0; i < H; ++i) shared[i] = 0.0f;
         }
         /* official_moe.cpp:336: combined = round_bf16(routed + shared) */
-        for (size_t i = 0; i < H; ++i) out[t * H + i] = k3xo_round_bf16(mixed[i] + shared[i]);
+        for (size_t i = 0; i < H; ++i) out[t * H + i] = k3xo_round_bf16(routed[i] + shared[i]);
     }
     free(logits);
     free(y);
     free(mixed);
     free(shared);
+    free(lat);
+    free(normed);
+    free(routed);
     return st;
 }
 

@@ -132,11 +132,17 @@ int k3xo_shared_ffn(const float* x, const uint16_t* gate, const uint16_t* up,
                     const uint16_t* down, size_t hidden, size_t inter,
                     int activation, float beta, float linear_beta, float* y);
 
-/* Plain (hidden-space) MoE layer: official_moe.cpp:271-344 without the
- * latent steps (:296, :323-331). Experts are stacked: gate/up
- * [E][inter][hidden/2], down [E][hidden][inter/2], scales likewise with /32.
- * shared_* may be NULL (no shared expert). out[t] = round_bf16(mixed +
- * shared). ids/contrib (T*k) receive the routes. */
+/* MoE layer of official_moe.cpp:271-344 after the input preparation: route
+ * on the hidden row, experts, slot-ordered combine, shared expert,
+ * out[t] = round_bf16(routed + shared) (the prefix residual, :337-341, is
+ * the caller's). latent == 0: the plain hidden-space MoE (routed = mixed,
+ * no :296 / :323-331). latent = L: LatentMoE — latent = bf16_matvec(hidden,
+ * routed_down) (:296), experts on the latent row, mixed rounded (:322),
+ * normalized by routed_norm with latent_eps (:323), routed =
+ * bf16_matvec(normalized, routed_up) (:328). Experts are stacked over their
+ * width D (H, or L): gate/up [E][inter][D/2], down [E][D][inter/2], scales
+ * likewise with /32. shared_* may be NULL (no shared expert). ids/contrib
+ * (T*k) receive the routes. */
 typedef struct {
     size_t hidden, inter, experts, top_k, shared_inter;
     const uint16_t* router;       /* [E][H] bf16 */
@@ -152,6 +158,11 @@ typedef struct {
     const uint16_t* shared_down;  /* [H][Is] */
     int activation;
     float situ_beta, situ_linear_beta;
+    size_t latent;                /* 0: plain MoE */
+    const uint16_t* routed_down;  /* [L][H] */
+    const uint16_t* routed_norm;  /* [L] */
+    const uint16_t* routed_up;    /* [H][L] */
+    float latent_eps;
 } k3xo_moe_layer;
 
 int k3xo_moe_layer_forward(const k3xo_moe_layer* layer, const float* hidden,

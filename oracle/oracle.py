@@ -78,6 +78,8 @@ class _MoeLayer(C.Structure):
         ("down_packed", C.c_void_p), ("down_scales", C.c_void_p),
         ("shared_gate", C.c_void_p), ("shared_up", C.c_void_p), ("shared_down", C.c_void_p),
         ("activation", C.c_int), ("situ_beta", C.c_float), ("situ_linear_beta", C.c_float),
+        ("latent", _sz), ("routed_down", C.c_void_p), ("routed_norm", C.c_void_p), ("routed_up", C.c_void_p),
+        ("latent_eps", C.c_float),
     ]
 
 
@@ -110,6 +112,10 @@ def moe_struct(layer: dict):
     s.activation = keep.get("activation", ACT_SWIGLU)
     s.situ_beta = keep.get("situ_beta", 4.0)
     s.situ_linear_beta = keep.get("situ_linear_beta", 0.0)
+    s.latent = keep.get("latent", 0)
+    for name in ("routed_down", "routed_norm", "routed_up"):
+        setattr(s, name, _ptr(keep.get(name)))
+    s.latent_eps = keep.get("latent_eps", 1e-6)
     return s, keep
 
 
@@ -475,6 +481,8 @@ class Reference:
                                             _f32p]
         L.k3xr_prepare_moe_input.argtypes = [_f32p, _f32p, _u16p, _u16p, _u16p, _sz, C.c_float, _f32p]
         L.k3xr_select_routing.argtypes = _SELECT_ROUTING_ARGS
+        L.k3xr_official_moe.argtypes = [C.c_void_p, _f32p, _f32p, _u16p, _u16p, _u16p, C.c_float, _sz, _f32p,
+                                        _u32p, _f32p]
 
     def decode_mxfp4(self, packed, scales, rows, cols, group=32):
         out = np.empty(rows * cols, np.float32)
@@ -594,6 +602,23 @@ class Reference:
     def select_routing(self, scores, bias, natural_k, **policy):
         return _select_routing(self.lib.k3xr_select_routing, scores, bias, natural_k, **policy)
 
+    def official_moe(self, layer: dict, prefix, block, residual_norm, residual_proj, post_norm, eps):
+        """official_moe_cpu (LatentMoE) for T positions with its own input
+        preparation and routing: (out with the prefix residual, ids, contributions)."""
+        prefix, block = _c(prefix, np.float32), _c(block, np.float32)
+        T, H = prefix.shape
+        s, keep = moe_struct(layer)
+        out = np.zeros((T, H), np.float32)
+        ids = np.zeros((T, layer["top_k"]), np.uint32)
+        con = np.zeros((T, layer["top_k"]), np.float32)
+        st = self.lib.k3xr_official_moe(C.byref(s), prefix, block, _c(residual_norm, np.uint16),
+                                        _c(residual_proj, np.uint16), _c(post_norm, np.uint16), eps, T, out, ids,
+                                        con)
+        del keep
+        if st:
+            raise OracleError(st, "ref official_moe_cpu")
+        return out, ids, con
+
     def prepare_input(self, prefix, block, norm, proj, post, eps):
         out = np.empty(len(prefix), np.float32)
         st = self.lib.k3xr_prepare_moe_input(_c(prefix, np.float32), _c(block, np.float32), _c(norm, np.uint16),
@@ -636,10 +661,13 @@ def bf16_values(words):
 
 
 def make_moe_layer(rs: Restatement, seed, hidden, inter, experts, top_k, shared_inter=0,
-                   sigma=0.02, activation=ACT_SWIGLU):
-    """Synthetic plain MoE layer: N(0, sigma) weights, experts quantised to
-    MXFP4 with the restated quantiser, router/shared in bf16."""
+                   sigma=0.02, activation=ACT_SWIGLU, latent=0):
+    """Synthetic MoE layer: N(0, sigma) weights, experts quantised to MXFP4
+    with the restated quantiser, router/shared in bf16. latent > 0 makes a
+    LatentMoE layer: routed_down [L][H], routed_norm [L] (1 + N(0, 0.1)),
+    routed_up [H][L] in bf16, experts of width L."""
     g = np.random.default_rng(seed)
+    D = latent or hidden
 
     def mx(rows, cols):
         w = g.normal(0.0, sigma, size=(rows, cols)).astype(np.float32)
@@ -647,9 +675,9 @@ def make_moe_layer(rs: Restatement, seed, hidden, inter, experts, top_k, shared_
 
     gp, gs, up_, us, dp, ds = [], [], [], [], [], []
     for _ in range(experts):
-        a, b = mx(inter, hidden); gp.append(a); gs.append(b)
-        a, b = mx(inter, hidden); up_.append(a); us.append(b)
-        a, b = mx(hidden, inter); dp.append(a); ds.append(b)
+        a, b = mx(inter, D); gp.append(a); gs.append(b)
+        a, b = mx(inter, D); up_.append(a); us.append(b)
+        a, b = mx(D, inter); dp.append(a); ds.append(b)
     layer = dict(
         hidden=hidden, inter=inter, experts=experts, top_k=top_k, shared_inter=shared_inter,
         router=bf16_words(g.normal(0.0, sigma, size=(experts, hidden))),
@@ -663,6 +691,12 @@ def make_moe_layer(rs: Restatement, seed, hidden, inter, experts, top_k, shared_
         layer["shared_gate"] = bf16_words(g.normal(0.0, sigma, size=(shared_inter, hidden)))
         layer["shared_up"] = bf16_words(g.normal(0.0, sigma, size=(shared_inter, hidden)))
         layer["shared_down"] = bf16_words(g.normal(0.0, sigma, size=(hidden, shared_inter)))
+    if latent:
+        layer["latent"] = latent
+        layer["latent_eps"] = 1e-6
+        layer["routed_down"] = bf16_words(g.normal(0.0, 1.0 / np.sqrt(hidden), size=(latent, hidden)))
+        layer["routed_norm"] = bf16_words(1.0 + g.normal(0.0, 0.1, size=latent))
+        layer["routed_up"] = bf16_words(g.normal(0.0, sigma, size=(hidden, latent)))
     return layer
 
 

@@ -73,6 +73,11 @@ struct k3xr_moe_layer {
     const std::uint16_t* shared_down;
     int activation;  // 0 = SwiGLU (situ_glu with beta 2^64, no linear bound), 1 = SiTU
     float situ_beta, situ_linear_beta;
+    std::size_t latent;                 // LatentMoE width (0: plain; k3xr_official_moe needs > 0)
+    const std::uint16_t* routed_down;   // [L][H]
+    const std::uint16_t* routed_norm;   // [L]
+    const std::uint16_t* routed_up;     // [H][L]
+    float latent_eps;
 };
 
 int k3xr_decode_mxfp4(const std::uint8_t* packed, const std::uint8_t* scales,
@@ -333,6 +338,61 @@ int k3xr_moe_layer_forward(const k3xr_moe_layer* layer, const float* hidden,
     worker();
     for (auto& th : pool) th.join();
     return status.load();
+}
+
+// official_moe_cpu itself (official_moe.cpp:271-344, LatentMoE) for T
+// positions: each position's input is {prefix, block}, its hidden row the
+// reference's prepare_official_moe_input (with residual_norm/proj and
+// post_norm), its route route_official_moe on that row. out [T][H] is the
+// reference's `output` (with the prefix residual); ids/contributions [T][k].
+int k3xr_official_moe(const k3xr_moe_layer* layer, const float* prefix, const float* block,
+                      const std::uint16_t* residual_norm, const std::uint16_t* residual_proj,
+                      const std::uint16_t* post_norm, float eps, std::size_t T, float* out,
+                      std::uint32_t* ids, float* contributions) {
+    const auto& L = *layer;
+    const std::size_t H = L.hidden, I = L.inter, D = L.latent, E = L.experts;
+    if (!D || L.activation != 0) return static_cast<int>(ErrorCode::invalid_state);
+    const auto w16 = [](const std::uint16_t* p, std::size_t n) { return std::span<const std::uint16_t>(p, n); };
+    std::vector<k3x::OfficialExpertView> experts(E);
+    for (std::size_t e = 0; e < E; ++e) {
+        experts[e].expert_id = static_cast<std::uint32_t>(e);
+        experts[e].weights.gate = {e * 3 + 1, bytes(L.gate_packed + e * I * D / 2, I * D / 2),
+                                   bytes(L.gate_scales + e * I * D / 32, I * D / 32), I, D, 32};
+        experts[e].weights.up = {e * 3 + 2, bytes(L.up_packed + e * I * D / 2, I * D / 2),
+                                 bytes(L.up_scales + e * I * D / 32, I * D / 32), I, D, 32};
+        experts[e].weights.down = {e * 3 + 3, bytes(L.down_packed + e * D * I / 2, D * I / 2),
+                                   bytes(L.down_scales + e * D * I / 32, D * I / 32), D, I, 32};
+    }
+    k3x::OfficialMoeWeights w{};
+    w.residual_norm = {w16(residual_norm, H), 1};
+    w.residual_proj = {w16(residual_proj, H), 1, H, 2};
+    w.post_norm = {w16(post_norm, H), 3};
+    w.router = {w16(L.router, E * H), E, H, 4};
+    w.correction = {L.correction, E};
+    w.routed_down = {w16(L.routed_down, D * H), D, H, 5};
+    w.routed_norm = {w16(L.routed_norm, D), 6};
+    w.routed_up = {w16(L.routed_up, H * D), H, D, 7};
+    if (L.shared_gate) {
+        w.shared.gate = {w16(L.shared_gate, L.shared_inter * H), L.shared_inter, H, 8};
+        w.shared.up = {w16(L.shared_up, L.shared_inter * H), L.shared_inter, H, 9};
+        w.shared.down = {w16(L.shared_down, H * L.shared_inter), H, L.shared_inter, 10};
+    }
+    w.experts = experts;
+    for (std::size_t t = 0; t < T; ++t) {
+        k3x::OfficialMoeInput in{std::vector<float>(prefix + t * H, prefix + (t + 1) * H),
+                                 std::vector<float>(block + t * H, block + (t + 1) * H)};
+        auto hidden = k3x::prepare_official_moe_input(in, w, eps);
+        if (!hidden) return code(hidden);
+        auto route = k3x::route_official_moe(hidden.value(), w.router, w.correction, L.top_k);
+        if (!route) return code(route);
+        auto r = k3x::official_moe_cpu(in, w, route.value(), eps, 0x1p64F, std::nullopt);
+        if (!r) return code(r);
+        std::copy(r.value().output.begin(), r.value().output.end(), out + t * H);
+        std::copy(route.value().expert_ids.begin(), route.value().expert_ids.end(), ids + t * L.top_k);
+        std::copy(route.value().contributions.begin(), route.value().contributions.end(),
+                  contributions + t * L.top_k);
+    }
+    return 0;
 }
 
 struct k3xr_kda_weights {

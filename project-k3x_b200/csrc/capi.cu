@@ -68,11 +68,27 @@ struct MoeScratch {
     uint16_t* sbd;   // tensor-core shared expert: down operand [2T][Is]
     float* hidden;   // host path only
     float* out;      // host path only
+    // LatentMoE only
+    float* lat;      // [T][L] latent rows (the experts' input)
+    float* mixed;    // [T][L]
+    float* normed;   // [T][L]
+    float* routed;   // [T][H]
+    uint16_t* xt;    // linear input terms [2][T][max(H, L)]
 };
+
+// The experts' view of a layer: its width is the latent width for a
+// LatentMoE layer, the hidden width otherwise.
+k3xb_moe_layer expert_view(const k3xb_moe_layer& L) {
+    k3xb_moe_layer v = L;
+    if (L.latent) v.hidden = L.latent;
+    v.latent = 0;
+    return v;
+}
 
 template <typename A>
 void layout_moe(A& a, const k3xb_moe_layer& L, uint32_t T, bool host, MoeScratch* s) {
     const size_t E = L.experts, K = L.top_k, H = L.hidden, I = L.inter, Is = L.shared_inter;
+    const size_t D = L.latent ? L.latent : H;   // the experts' width
     MoeScratch tmp{};
     MoeScratch& r = s ? *s : tmp;
     r.logits = a.template take<float>(T * E);
@@ -85,7 +101,7 @@ void layout_moe(A& a, const k3xb_moe_layer& L, uint32_t T, bool host, MoeScratch
     r.plan.assign_contrib = a.template take<float>(T * K);
     r.plan.group_count = a.template take<uint32_t>(1);
     r.act = L.engine == K3XB_ENGINE_SIMT ? a.template take<float>(T * K * I) : nullptr;
-    r.slot_out = a.template take<float>(T * K * H);
+    r.slot_out = a.template take<float>(T * K * D);
     r.sg = a.template take<float>(T * Is);
     r.su = a.template take<float>(T * Is);
     r.sa = a.template take<float>(T * Is);
@@ -95,6 +111,12 @@ void layout_moe(A& a, const k3xb_moe_layer& L, uint32_t T, bool host, MoeScratch
     r.sbd = tc_shared ? a.template take<uint16_t>(2 * T * Is) : nullptr;
     r.hidden = host ? a.template take<float>(T * H) : nullptr;
     r.out = host ? a.template take<float>(T * H) : nullptr;
+    const bool latent = L.latent != 0;
+    r.lat = latent ? a.template take<float>(T * D) : nullptr;
+    r.mixed = latent ? a.template take<float>(T * D) : nullptr;
+    r.normed = latent ? a.template take<float>(T * D) : nullptr;
+    r.routed = latent ? a.template take<float>(T * H) : nullptr;
+    r.xt = latent ? a.template take<uint16_t>(2 * T * (H > D ? H : D)) : nullptr;
 }
 
 int validate_layer(k3xb_ctx* ctx, const k3xb_moe_layer* L) {
@@ -114,6 +136,15 @@ int validate_layer(k3xb_ctx* ctx, const k3xb_moe_layer* L) {
         return fail(ctx, K3XB_INVALID_STATE, "SiTU beta must be positive");
     if (L->engine != K3XB_ENGINE_SIMT && L->engine != K3XB_ENGINE_MXF4)
         return fail(ctx, K3XB_INVALID_STATE, "unknown expert engine");
+    if (L->latent) {   // official_moe.cpp:296, :323-331
+        if (L->latent % 32)
+            return fail(ctx, K3XB_INVALID_MXFP4, "latent must be a multiple of the MXFP4 group (32)");
+        if (L->hidden % 8 || L->latent % 8)
+            return fail(ctx, K3XB_INVALID_EXTENT, "latent projections need hidden and latent multiples of 8");
+        if (!L->routed_down || !L->routed_norm || !L->routed_up)
+            return fail(ctx, K3XB_INVALID_EXTENT, "missing latent projections");
+        if (!(L->latent_eps > 0.0f)) return fail(ctx, K3XB_INVALID_EXTENT, "latent_eps must be positive");
+    }
     return K3XB_OK;
 }
 
@@ -147,11 +178,19 @@ int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidd
         PhaseScope ph(ctx, K3XB_PHASE_PLAN);
         if ((st = launch_plan(ctx, ids, contrib, T, K, E, s.plan))) return st;
     }
+    const k3xb_moe_layer LE = expert_view(L);
+    const uint32_t D = LE.hidden;
+    const float* xe = hidden;
+    if (L.latent) {   // official_moe.cpp:296: latent = bf16_matvec(hidden, routed_down)
+        PhaseScope ph(ctx, K3XB_PHASE_LATENT);
+        if ((st = launch_linear_bf16(ctx, hidden, L.routed_down, T, D, H, 1, s.xt, s.lat))) return st;
+        xe = s.lat;
+    }
     if (L.engine == K3XB_ENGINE_SIMT) {
         PhaseScope ph(ctx, K3XB_PHASE_EXPERT_GATEUP);
-        if ((st = launch_simt_experts(ctx, L, hidden, T, s.plan, s.act, s.slot_out))) return st;
+        if ((st = launch_simt_experts(ctx, LE, xe, T, s.plan, s.act, s.slot_out))) return st;
     } else {
-        if ((st = launch_mxf4_experts(ctx, L, hidden, T, s.plan, s.slot_out))) return st;
+        if ((st = launch_mxf4_experts(ctx, LE, xe, T, s.plan, s.slot_out))) return st;
     }
     const float* shared = nullptr;
     if (L.shared_gate && L.engine == K3XB_ENGINE_MXF4) {
@@ -170,7 +209,20 @@ int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidd
         if ((st = launch_bf16_rows(ctx, s.sa, L.shared_down, T, H, Is, s.shared_out))) return st;
         shared = s.shared_out;
     }
-    {
+    if (L.latent) {
+        {   // :313-322: mixed = round_bf16(slot-ordered combine), in the latent width
+            PhaseScope ph(ctx, K3XB_PHASE_COMBINE);
+            if ((st = launch_combine(ctx, s.slot_out, contrib, nullptr, T, K, D, s.mixed))) return st;
+        }
+        // :323-331: routed = bf16_matvec(normalized(mixed, routed_norm), routed_up); then
+        // :336 combined = round_bf16(routed + shared)
+        PhaseScope ph(ctx, K3XB_PHASE_LATENT);
+        if ((st = launch_rms_norm(ctx, s.mixed, L.routed_norm, T, D, L.latent_eps, s.normed))) return st;
+        if ((st = launch_linear_bf16(ctx, s.normed, L.routed_up, T, H, D, 1, s.xt, s.routed))) return st;
+        const size_t n = static_cast<size_t>(T) * H;
+        st = shared ? launch_residual(ctx, s.routed, shared, n, out) : launch_residual_round(ctx, s.routed, n, out);
+        if (st) return st;
+    } else {
         PhaseScope ph(ctx, K3XB_PHASE_COMBINE);
         if ((st = launch_combine(ctx, s.slot_out, contrib, shared, T, K, H, out))) return st;
     }
@@ -331,7 +383,7 @@ int k3xb_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const flo
     if (!T || !hidden || !out) return fail(ctx, K3XB_INVALID_EXTENT, "moe forward arguments");
     Sizer sz;
     layout_moe(sz, *layer, T, false, nullptr);
-    sz.used += mxf4_scratch_bytes(*layer, T);
+    sz.used += mxf4_scratch_bytes(expert_view(*layer), T);
     void* base;
     if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
     Carver c(base);
@@ -349,7 +401,7 @@ int k3xb_moe_layer_forward_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer, cons
     if (!T || !hidden_host || !out_host) return fail(ctx, K3XB_INVALID_EXTENT, "moe forward arguments");
     Sizer sz;
     layout_moe(sz, *layer, T, true, nullptr);
-    sz.used += mxf4_scratch_bytes(*layer, T);
+    sz.used += mxf4_scratch_bytes(expert_view(*layer), T);
     void* base;
     if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
     Carver c(base);
@@ -382,14 +434,15 @@ int k3xb_moe_experts(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const float* hi
     if (!T || !hidden || !plan || !slot_out) return fail(ctx, K3XB_INVALID_EXTENT, "experts arguments");
     Sizer sz;
     sz.take<float>(static_cast<size_t>(T) * layer->top_k * layer->inter);
-    sz.used += mxf4_scratch_bytes(*layer, T);
+    sz.used += mxf4_scratch_bytes(expert_view(*layer), T);
     void* base;
     if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
     Carver c(base);
     float* act = c.take<float>(static_cast<size_t>(T) * layer->top_k * layer->inter);
     set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
-    if (layer->engine == K3XB_ENGINE_SIMT) return launch_simt_experts(ctx, *layer, hidden, T, *plan, act, slot_out);
-    return launch_mxf4_experts(ctx, *layer, hidden, T, *plan, slot_out);
+    const k3xb_moe_layer LE = expert_view(*layer);   // rows of the experts' width (latent rows for LatentMoE)
+    if (layer->engine == K3XB_ENGINE_SIMT) return launch_simt_experts(ctx, LE, hidden, T, *plan, act, slot_out);
+    return launch_mxf4_experts(ctx, LE, hidden, T, *plan, slot_out);
 }
 
 int k3xb_expert_grid_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const uint32_t* expert_ids, uint32_t n,
@@ -397,7 +450,7 @@ int k3xb_expert_grid_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const uint
     if (!ctx) return K3XB_INVALID_EXTENT;
     if (!layer || !expert_ids || !inputs_host || !out_host || !T || !n)
         return fail(ctx, K3XB_INVALID_EXTENT, "expert grid arguments");
-    k3xb_moe_layer L = *layer;
+    k3xb_moe_layer L = expert_view(*layer);   // inputs are rows of the experts' width
     L.top_k = n;   // every token through each listed expert: one routing slot per expert
     L.shared_gate = L.shared_up = L.shared_down = nullptr;
     L.shared_inter = 0;
@@ -817,7 +870,7 @@ void layout_layer(A& a, const k3xb_layer& L, uint32_t N, uint32_t S, bool own_tr
 size_t layer_work_bytes(const k3xb_layer& L, uint32_t N, uint32_t S, bool own_trace) {
     Sizer sz;
     layout_layer(sz, L, N, S, own_trace, nullptr, nullptr, nullptr, nullptr);
-    return sz.used + mxf4_scratch_bytes(L.moe, N * S) + 1024;
+    return sz.used + mxf4_scratch_bytes(expert_view(L.moe), N * S) + 1024;
 }
 
 // official_layer_cpu with the plain MoE; d_tables = device anc table +
@@ -1167,15 +1220,24 @@ int k3xb_ep_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* local, uint32
     if (!T || !hidden || !out) return fail(ctx, K3XB_INVALID_EXTENT, "ep forward arguments");
     const uint32_t K = local->top_k, H = local->hidden, Is = local->shared_inter;
     const bool shared = local->shared_gate != nullptr;
+    // a LatentMoE layer sends, computes and returns latent rows (width D)
+    const k3xb_moe_layer LE = expert_view(*local);
+    const uint32_t D = LE.hidden;
+    const size_t TD = static_cast<size_t>(T) * D, TH = static_cast<size_t>(T) * H;
     Sizer sz;
     sz.take<float>(static_cast<size_t>(T) * E);
     sz.take<uint32_t>(static_cast<size_t>(T) * K);
     sz.take<float>(static_cast<size_t>(T) * K);
-    sz.take<float>(static_cast<size_t>(T) * H);
+    sz.take<float>(TH);
     sz.take<uint16_t>(2ull * T * H);
     sz.take<uint16_t>(2ull * T * (Is ? Is : 1));
-    sz.take<uint8_t>(ep_scratch_bytes(G, T, K, H, local->experts), 1024);
-    sz.used += mxf4_scratch_bytes(*local, static_cast<uint32_t>(G) * T);
+    sz.take<uint8_t>(ep_scratch_bytes(G, T, K, D, local->experts), 1024);
+    if (local->latent) {
+        sz.take<float>(3 * TD);
+        sz.take<float>(TH);
+        sz.take<uint16_t>(2ull * T * (H > D ? H : D));
+    }
+    sz.used += mxf4_scratch_bytes(LE, static_cast<uint32_t>(G) * T);
     void* base;
     if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
     Carver c(base);
@@ -1187,7 +1249,16 @@ int k3xb_ep_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* local, uint32
     float* shared_out = c.take<float>(static_cast<size_t>(T) * H);
     uint16_t* sxb = c.take<uint16_t>(2ull * T * H);
     uint16_t* sbd = c.take<uint16_t>(2ull * T * (Is ? Is : 1));
-    void* region = c.take<uint8_t>(ep_scratch_bytes(G, T, K, H, local->experts), 1024);
+    void* region = c.take<uint8_t>(ep_scratch_bytes(G, T, K, D, local->experts), 1024);
+    float *lat = nullptr, *mixed = nullptr, *normed = nullptr, *routed = nullptr;
+    uint16_t* xt = nullptr;
+    if (local->latent) {
+        lat = c.take<float>(TD);
+        mixed = c.take<float>(TD);
+        normed = c.take<float>(TD);
+        routed = c.take<float>(TH);
+        xt = c.take<uint16_t>(2ull * T * (H > D ? H : D));
+    }
     set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
     if (shared) {   // side stream, as in the one-GPU layer
         K3XB_CUDA(ctx, cudaEventRecord(ctx->ev_fork, ctx->stream));
@@ -1208,9 +1279,24 @@ int k3xb_ep_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* local, uint32
         if ((st = launch_topk(ctx, logits, local->correction, T, E, K, ids, contrib, nullptr, ctx->status_word)))
             return st;
     }
-    if (shared) K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
-    if ((st = ep_moe_forward(ctx, *local, E, hidden, T, ids, contrib, shared ? shared_out : nullptr, region, out)))
-        return st;
+    if (!local->latent) {
+        if (shared) K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
+        if ((st = ep_moe_forward(ctx, *local, E, hidden, T, ids, contrib, shared ? shared_out : nullptr, region,
+                                 out)))
+            return st;
+    } else {   // official_moe.cpp:296, then the experts on latent rows, then :322-336
+        {
+            PhaseScope ph(ctx, K3XB_PHASE_LATENT);
+            if ((st = launch_linear_bf16(ctx, hidden, local->routed_down, T, D, H, 1, xt, lat))) return st;
+        }
+        if ((st = ep_moe_forward(ctx, LE, E, lat, T, ids, contrib, nullptr, region, mixed))) return st;
+        PhaseScope ph(ctx, K3XB_PHASE_LATENT);
+        if ((st = launch_rms_norm(ctx, mixed, local->routed_norm, T, D, local->latent_eps, normed))) return st;
+        if ((st = launch_linear_bf16(ctx, normed, local->routed_up, T, H, D, 1, xt, routed))) return st;
+        if (shared) K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
+        st = shared ? launch_residual(ctx, routed, shared_out, TH, out) : launch_residual_round(ctx, routed, TH, out);
+        if (st) return st;
+    }
     ++ctx->stats.moe_layer_calls;
     return K3XB_OK;
 }

@@ -13,7 +13,7 @@ constexpr int kMaxPending = 4096;
 const char* const kNames[] = {"route",         "plan",          "expert_prep",   "expert_gateup", "expert_down",
                               "shared",        "combine",       "ep_dispatch",   "ep_exchange",   "ep_return",
                               "attn_residual", "kda_project",   "kda_conv",      "kda_recurrence", "kda_output",
-                              "embed",         "lm_head",       "accept",        "commit"};
+                              "embed",         "lm_head",       "accept",        "commit",        "latent"};
 static_assert(sizeof(kNames) / sizeof(kNames[0]) == K3XB_PHASE_COUNT, "one name per phase");
 
 struct Profiler {

@@ -52,7 +52,9 @@ class MoeLayer(C.Structure):
                 ("activation", C.c_int32), ("situ_beta", C.c_float),
                 ("situ_linear_beta", C.c_float), ("engine", C.c_int32), ("act_terms", C.c_int32),
                 ("gate_scales_tc", C.c_void_p), ("up_scales_tc", C.c_void_p),
-                ("down_scales_tc", C.c_void_p)]
+                ("down_scales_tc", C.c_void_p),
+                ("latent", C.c_uint32), ("routed_down", C.c_void_p), ("routed_norm", C.c_void_p),
+                ("routed_up", C.c_void_p), ("latent_eps", C.c_float)]
 
 
 class KdaLayer(C.Structure):
@@ -99,7 +101,7 @@ class Stats(C.Structure):
         "peak_resident_weight_bytes", "weight_h2d_bytes")]
 
 
-PHASE_COUNT = 19   # K3XB_PHASE_COUNT
+PHASE_COUNT = 20   # K3XB_PHASE_COUNT
 
 
 class PhaseTime(C.Structure):
@@ -469,7 +471,7 @@ class Context:
         """Adds tcgen05-layout copies of the three expert scale arrays to a
         layer dict (one-time, for resident weights)."""
         import torch
-        E, H, I = w["experts"], w["hidden"], w["inter"]
+        E, H, I = w["experts"], w.get("latent") or w["hidden"], w["inter"]   # H: the experts' width
         for name, rows, cols in (("gate", E * I, H), ("up", E * I, H), ("down", E * H, I)):
             out = torch.empty_like(w[f"{name}_scales"])
             self.prepare_mxfp4_scales(w[f"{name}_scales"], rows, cols, out)
@@ -497,6 +499,11 @@ def moe_layer_desc(w: dict, engine=ENGINE_SIMT, act_terms=6) -> MoeLayer:
     L.situ_linear_beta = w.get("situ_linear_beta", 0.0)
     L.engine = engine
     L.act_terms = act_terms
+    L.latent = w.get("latent", 0)   # LatentMoE width (0: plain MoE)
+    for name in ("routed_down", "routed_norm", "routed_up"):
+        t = w.get(name)
+        setattr(L, name, None if t is None else t.data_ptr())
+    L.latent_eps = w.get("latent_eps", 1e-6)
     return L
 
 

@@ -76,6 +76,25 @@ def moe_layer(ref, rs):
          **arrays, **{f"dim_{k}": v for k, v in dims.items()})
 
 
+def latent_moe(ref, rs):
+    """official_moe_cpu (official_moe.cpp:271-344, LatentMoE) with its own
+    input preparation and routing, for 4 positions."""
+    d = dict(MOE, experts=8, top_k=2, latent=128)
+    layer = make_moe_layer(rs, 1011, d["hidden"], d["inter"], d["experts"], d["top_k"], d["shared_inter"],
+                           latent=d["latent"])
+    g = np.random.default_rng(1012)
+    T, H, eps = 4, d["hidden"], 1e-6
+    prefix, block = bf16_normal(g, (T, H)), bf16_normal(g, (T, H))
+    norm = bf16_words(1.0 + g.normal(0, 0.1, size=H))
+    proj = bf16_words(g.normal(0, 0.05, size=H))
+    post = bf16_words(1.0 + g.normal(0, 0.1, size=H))
+    out, ids, con = ref.official_moe(layer, prefix, block, norm, proj, post, eps)
+    arrays = {k: v for k, v in layer.items() if isinstance(v, np.ndarray)}
+    dims = {k: v for k, v in layer.items() if not isinstance(v, np.ndarray)}
+    save("latent_moe.npz", prefix=prefix, block=block, residual_norm=norm, residual_proj=proj, post_norm=post,
+         eps=eps, out=out, ids=ids, contributions=con, **arrays, **{f"dim_{k}": v for k, v in dims.items()})
+
+
 def kda_block(ref):
     """official_kda_cpu (official_kda.cpp:198-426) over 5 positions from a
     non-zero state."""
@@ -166,6 +185,7 @@ def main():
     expert_major(ref)
     mxfp4(ref, rs)
     moe_layer(ref, rs)
+    latent_moe(ref, rs)
     kda_block(ref)
     prepare_input(ref)
     select_routing(ref)

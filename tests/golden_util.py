@@ -31,6 +31,21 @@ def moe_layer():
     return layer, f["hidden"], f["out"], f["ids"], f["contributions"]
 
 
+def latent_moe():
+    """(layer dict with latent fields, fixture dict)."""
+    f = load("latent_moe.npz")
+    skip = ("prefix", "block", "residual_norm", "residual_proj", "post_norm", "eps", "out", "ids", "contributions")
+    layer = {k[4:]: _scalar(v) for k, v in f.items() if k.startswith("dim_")}
+    for k, v in f.items():
+        if not k.startswith("dim_") and k not in skip:
+            layer[k] = v
+    for k in ("hidden", "inter", "experts", "top_k", "shared_inter", "activation", "latent"):
+        layer[k] = int(layer[k])
+    for k in ("situ_beta", "situ_linear_beta", "latent_eps"):
+        layer[k] = float(layer[k])
+    return layer, f
+
+
 def kda_block():
     """(weights dict in make_kda_weights's form, fixture dict)."""
     f = load("kda_block.npz")

@@ -92,3 +92,18 @@ def test_verify_greedy(rs):
         a, com, _ = rs.verify_greedy_block(0, f["drafts"][s], p, int(f["vocab"]), f["targets"][s])
         assert a == f["accepted"][s]
         assert com == f["committed"][s, :f["count"][s]].tolist()
+
+
+def test_latent_moe(rs):
+    """LatentMoE: input preparation, routing, the latent layer and the
+    prefix residual, restated, against official_moe_cpu's output."""
+    layer, f = gu.latent_moe()
+    eps = float(f["eps"])
+    layer["latent_eps"] = eps
+    T = f["prefix"].shape[0]
+    hidden = np.stack([rs.prepare_input(f["prefix"][t], f["block"][t], f["residual_norm"], f["residual_proj"],
+                                        f["post_norm"], eps) for t in range(T)])
+    moe, ids, con = rs.moe_layer(layer, hidden)
+    np.testing.assert_array_equal(ids, f["ids"])
+    np.testing.assert_array_equal(con, f["contributions"])
+    np.testing.assert_array_equal(rs.round_bf16(rs.round_bf16(f["prefix"]) + moe), f["out"])

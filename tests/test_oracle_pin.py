@@ -476,3 +476,26 @@ def test_select_routing_reference_cases(rs):
     assert rs.select_routing(bad, zero, 16)[0] != 0
     assert rs.select_routing(zero, zero, 16)[0] != 0
     assert rs.select_routing(desc, zero, 16, mode=2, quality_floor_k=5)[0] != 0
+
+
+def test_latent_moe_matches_reference(rs, ref):
+    """LatentMoE: the restatement (prepare_input, then the latent layer, then
+    the prefix residual) equals the reference's official_moe_cpu
+    (official_moe.cpp:271-344) with its own preparation and routing, bit for
+    bit."""
+    from oracle import bf16_normal, bf16_words, make_moe_layer
+    g = np.random.default_rng(61)
+    H, L, T, eps = 256, 128, 4, 1e-6
+    layer = make_moe_layer(rs, 62, H, 128, 16, 4, shared_inter=128, latent=L)
+    prefix, block = bf16_normal(g, (T, H)), bf16_normal(g, (T, H))
+    norm = bf16_words(1 + g.normal(0, 0.1, size=H))
+    proj = bf16_words(g.normal(0, 0.05, size=H))
+    post = bf16_words(1 + g.normal(0, 0.1, size=H))
+    want, want_ids, want_con = ref.official_moe(layer, prefix, block, norm, proj, post, eps)
+    layer["latent_eps"] = eps
+    hidden = np.stack([rs.prepare_input(prefix[t], block[t], norm, proj, post, eps) for t in range(T)])
+    moe, ids, con = rs.moe_layer(layer, hidden)
+    got = rs.round_bf16(rs.round_bf16(prefix) + moe)
+    np.testing.assert_array_equal(ids, want_ids)
+    np.testing.assert_array_equal(con, want_con)
+    np.testing.assert_array_equal(got, want)
