@@ -561,6 +561,52 @@ typedef struct {
 int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* model,
                      const k3xb_verify_io* io);
 
+/* The AURORA reduced-Top-K self-draft on the device (the draft side of
+ * AuroraPersistentDraftProvider, aurora.cpp:206-383, with the draft
+ * session's fixed routing of K in {4, 6, 8, 12}, aurora.cpp:10-12): from
+ * each sequence's committed KDA state, `drafts` greedy decode steps of the
+ * same layer stack with every MoE layer's top_k replaced by draft_top_k.
+ * Step i feeds the token step i-1 produced (step 0 the anchor) and its
+ * argmax becomes draft i. The target's state arrays are read, not changed:
+ * the draft runs on its own copy, so nothing needs rolling back after
+ * verification (the job of IncrementalDraftCursor, model.cpp:1179-1409).
+ * The model needs its embedding. Device arrays: anchors [S], conv
+ * [layers][S][3][w-1][P], recurrent [layers][S][h][d][d] (as
+ * k3xb_verify_io), draft_tokens [S][drafts]. */
+typedef struct {
+    uint32_t sequences, drafts, draft_top_k;
+    const uint32_t* anchors;
+    const uint16_t* conv;
+    const float* recurrent;
+    uint32_t* draft_tokens;
+} k3xb_draft_io;
+int k3xb_draft_greedy(k3xb_ctx* ctx, const k3xb_verify_model* model,
+                      const k3xb_draft_io* io);
+
+/* One speculative round with the drafter on the device (the propose /
+ * verify / update loop of generate_speculative, model.cpp:1507, with
+ * AuroraPersistentDraftProvider as the drafter): k3xb_draft_greedy from
+ * the anchors and the committed state, then k3xb_verify_step (greedy) of
+ * anchor + drafts with the full model, which advances the state to the
+ * accepted position, then anchors <- each sequence's last committed token.
+ * No host synchronisation inside: rounds can be queued back to back.
+ * Device arrays: anchors [S] (in/out); conv, recurrent as k3xb_verify_io
+ * (in/out); draft_tokens [S][p], accepted [S], committed [S][p+1],
+ * committed_count [S] (out); logits [S][p+1][V] (out, may be NULL). */
+typedef struct {
+    uint32_t sequences, drafts, draft_top_k;
+    uint32_t* anchors;
+    uint16_t* conv;
+    float* recurrent;
+    uint32_t* draft_tokens;
+    uint32_t* accepted;
+    uint32_t* committed;
+    uint32_t* committed_count;
+    float* logits;
+} k3xb_speculative_io;
+int k3xb_speculative_step(k3xb_ctx* ctx, const k3xb_verify_model* model,
+                          const k3xb_speculative_io* io);
+
 /* ---- expert parallelism (NCCL over NVLink) ---------------------------------- */
 /* 128-byte NCCL unique id, made on one rank and handed to all (any
  * transport: a store, a file, a broadcast). No reference counterpart: the

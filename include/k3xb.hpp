@@ -14,8 +14,12 @@
 // (speculative.hpp:58-64), so an adapter can copy fields one to one.
 #pragma once
 
+#include <algorithm>
+#include <array>
 #include <cstddef>
 #include <cstdint>
+#include <limits>
+#include <optional>
 #include <span>
 #include <string>
 #include <utility>
@@ -183,6 +187,16 @@ public:
         return check(k3xb_verify_step(h_, &model, &io));
     }
 
+    // AURORA reduced-Top-K drafts on the device, and a whole on-device round
+    // (draft, verify, advance the state, next anchors); the length comes
+    // from a DraftLengthScheduler on the host.
+    Outcome draft(const k3xb_verify_model& model, const k3xb_draft_io& io) {
+        return check(k3xb_draft_greedy(h_, &model, &io));
+    }
+    Outcome speculative_step(const k3xb_verify_model& model, const k3xb_speculative_io& io) {
+        return check(k3xb_speculative_step(h_, &model, &io));
+    }
+
     // Expert parallelism over the GPUs of one box.
     Outcome ep_init(std::span<const std::uint8_t, 128> unique_id, int rank, int world) {
         return check(k3xb_ep_init(h_, unique_id.data(), rank, world));
@@ -257,6 +271,153 @@ class Verifier {
 public:
     virtual ~Verifier() = default;
     virtual Result<std::vector<Verification>> verify(std::span<const Draft> drafts) = 0;
+};
+
+// ---- draft length -----------------------------------------------------------
+
+// How many tokens to draft next: the AURORA ladder of 1, 2 or 4 drafts
+// (AdaptiveDraftScheduler, aurora_scheduler.cpp:37-199). `fixed` always
+// takes the longest rung within the caps. `adaptive` climbs one rung at a
+// time while the Laplace-smoothed survival of the last drafted position,
+// (accepted there + 1) / (tried there + 2), stays at or above
+// minimum_prefix_survival and the rung's unique-expert loads per
+// assignment stay at or below maximum_unique_load_ratio; a rejection caps
+// the next choice one rung lower (none after a rejection at rung 1, then
+// one retry of rung 1).
+enum class DraftPolicy { fixed, adaptive };
+
+struct DraftSchedulerConfig {
+    DraftPolicy policy = DraftPolicy::fixed;
+    std::size_t maximum_length = 1;            // 1, 2 or 4
+    double minimum_prefix_survival = 0.5;      // [0, 1]
+    double maximum_unique_load_ratio = 0.9;    // [0, 1]
+};
+
+// What one verification of `proposed` drafts reported (the fields of
+// k3x::DraftVerification the schedule reads, speculative.hpp:25-35).
+struct DraftObservation {
+    std::size_t proposed = 0, accepted = 0;
+    std::size_t positions_evaluated = 0, positions_discarded = 0;
+    std::size_t expert_loads = 0, expert_assignments = 0;   // unique experts loaded, (token, slot) pairs
+};
+
+struct DraftSchedulerStats {
+    std::uint64_t selected_1 = 0, selected_2 = 0, selected_4 = 0;
+    std::uint64_t growths = 0, backoffs = 0;
+};
+
+class DraftLengthScheduler {
+public:
+    static Result<DraftLengthScheduler> create(const DraftSchedulerConfig& c) {
+        const auto unit = [](double v) { return v == v && v >= 0.0 && v <= 1.0; };   // finite, in [0, 1]
+        if (!rung_of(c.maximum_length) || !unit(c.minimum_prefix_survival) || !unit(c.maximum_unique_load_ratio))
+            return Outcome(Status::invalid_extent, "draft scheduler: maximum_length in {1, 2, 4}, ratios in [0, 1]");
+        DraftLengthScheduler s;
+        s.cfg_ = c;
+        return s;
+    }
+    DraftLengthScheduler() = default;
+
+    const DraftSchedulerStats& stats() const noexcept { return stats_; }
+
+    // Drafts to propose when the caller allows at most `request_maximum`.
+    Result<std::size_t> select(std::size_t request_maximum) {
+        if (request_maximum == 0) return std::size_t{0};
+        std::size_t cap = std::min(request_maximum, cfg_.maximum_length);
+        if (has_cap_) cap = std::min(cap, cap_after_reject_);
+        if (cap == 0) {   // only a rejection at rung 1 gets here: retry rung 1 next time
+            if (has_cap_ && cap_after_reject_ == 0) {
+                has_cap_ = false;
+                retry_first_ = true;
+            }
+            return std::size_t{0};
+        }
+        if (cfg_.policy == DraftPolicy::fixed) {
+            for (std::size_t r = kRungs.size(); r-- > 0;)
+                if (kRungs[r] <= cap) return take(r);
+            return std::size_t{0};
+        }
+        if (retry_first_) {
+            retry_first_ = false;
+            return take(0);
+        }
+        const std::size_t top = has_qualified_ ? std::min(qualified_ + 1, *rung_of(cfg_.maximum_length)) : 0;
+        for (std::size_t r = top + 1; r-- > 0;) {
+            if (kRungs[r] > cap) continue;
+            if (seen_[r] && !(survival(kRungs[r] - 1) >= cfg_.minimum_prefix_survival && cost_ok(r))) continue;
+            return take(r);
+        }
+        return std::size_t{0};
+    }
+
+    // Learns from one verification of the drafts select() chose.
+    Outcome observe(const DraftObservation& o) {
+        if (o.proposed == 0) {
+            if (o.accepted || o.expert_loads || o.expert_assignments || o.positions_discarded > o.positions_evaluated)
+                return Outcome(Status::invalid_extent, "draft scheduler: an empty proposal reports nothing");
+            return {};
+        }
+        const auto rung = rung_of(o.proposed);
+        if (!rung || o.proposed > cfg_.maximum_length || o.accepted > o.proposed ||
+            o.positions_discarded > o.positions_evaluated || (o.expert_loads && !o.expert_assignments) ||
+            o.expert_loads > o.expert_assignments)
+            return Outcome(Status::invalid_extent, "draft scheduler: inconsistent observation");
+        const std::size_t r = *rung;
+        constexpr auto kMax = std::numeric_limits<std::uint64_t>::max();
+        for (std::size_t i = 0; i < o.proposed; ++i)
+            if (tried_[i] == kMax) return Outcome(Status::invalid_state, "draft scheduler: counter overflow");
+        if (o.expert_loads > kMax - loads_[r] || o.expert_assignments > kMax - assignments_[r])
+            return Outcome(Status::invalid_state, "draft scheduler: counter overflow");
+        for (std::size_t i = 0; i < o.proposed; ++i) {
+            ++tried_[i];
+            if (o.accepted > i) ++survived_[i];
+        }
+        loads_[r] += o.expert_loads;
+        assignments_[r] += o.expert_assignments;
+        seen_[r] = true;
+        if (cfg_.policy == DraftPolicy::fixed) return {};
+        if (o.accepted < o.proposed) {   // back off one rung (to none from rung 1)
+            has_cap_ = true;
+            cap_after_reject_ = r == 0 ? 0 : kRungs[r - 1];
+            ++stats_.backoffs;
+            return {};
+        }
+        has_cap_ = false;
+        if (survival(o.proposed - 1) >= cfg_.minimum_prefix_survival && cost_ok(r) &&
+            (!has_qualified_ || r > qualified_)) {
+            has_qualified_ = true;
+            qualified_ = r;
+            if (r + 1 < kRungs.size()) ++stats_.growths;
+        }
+        return {};
+    }
+
+private:
+    static constexpr std::array<std::size_t, 3> kRungs{1, 2, 4};
+    static std::optional<std::size_t> rung_of(std::size_t length) {
+        for (std::size_t r = 0; r < kRungs.size(); ++r)
+            if (kRungs[r] == length) return r;
+        return std::nullopt;
+    }
+    double survival(std::size_t position) const {
+        return static_cast<double>(survived_[position] + 1) / static_cast<double>(tried_[position] + 2);
+    }
+    bool cost_ok(std::size_t r) const {
+        return assignments_[r] == 0 ||
+               static_cast<double>(loads_[r]) / static_cast<double>(assignments_[r]) <= cfg_.maximum_unique_load_ratio;
+    }
+    std::size_t take(std::size_t r) {
+        (r == 0 ? stats_.selected_1 : r == 1 ? stats_.selected_2 : stats_.selected_4) += 1;
+        return kRungs[r];
+    }
+
+    DraftSchedulerConfig cfg_{};
+    std::array<std::uint64_t, 4> tried_{}, survived_{};   // per drafted position
+    std::array<std::uint64_t, 3> loads_{}, assignments_{};   // per rung
+    std::array<bool, 3> seen_{};
+    bool has_qualified_ = false, has_cap_ = false, retry_first_ = false;
+    std::size_t qualified_ = 0, cap_after_reject_ = 0;
+    DraftSchedulerStats stats_{};
 };
 
 // One speculative round: ask the drafter, verify, report back; returns the

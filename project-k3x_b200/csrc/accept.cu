@@ -279,7 +279,24 @@ __global__ void __launch_bounds__(kChunks) rejection_decide_kernel(
     }
 }
 
+// Next round's anchor of each sequence: its last committed token
+// (committed[s][count[s] - 1], the target token after the accepted drafts).
+__global__ void next_round_kernel(const uint32_t* __restrict__ committed, const uint32_t* __restrict__ count,
+                                  uint32_t S, uint32_t stride, uint32_t* __restrict__ anchors) {
+    const uint32_t s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= S) return;
+    const uint32_t n = count[s];
+    anchors[s] = committed[static_cast<size_t>(s) * stride + (n ? min(n, stride) - 1 : 0)];
+}
+
 }  // namespace
+
+int launch_next_anchor(k3xb_ctx* ctx, const uint32_t* committed, const uint32_t* count, uint32_t S, uint32_t stride,
+                       uint32_t* anchors) {
+    next_round_kernel<<<(S + 127) / 128, 128, 0, ctx->stream>>>(committed, count, S, stride, anchors);
+    K3XB_LAUNCHED(ctx);
+    return K3XB_OK;
+}
 
 int launch_accept_greedy(k3xb_ctx* ctx, const float* logits, const uint32_t* drafts, uint32_t S,
                          uint32_t p, uint32_t V, uint32_t* targets, uint32_t* accepted,

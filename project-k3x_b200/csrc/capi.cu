@@ -2,6 +2,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <memory>
 #include <new>
 #include <vector>
 
@@ -1203,6 +1204,98 @@ int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verif
             return st;
     }
     return K3XB_OK;
+}
+
+int k3xb_draft_greedy(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_draft_io* io) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!m || !io || !m->layers || !m->layer || !m->embedding)
+        return fail(ctx, K3XB_INVALID_EXTENT, "draft model (needs its embedding)");
+    const uint32_t S = io->sequences, p = io->drafts, K = io->draft_top_k;
+    if (!S || !p || !io->anchors || !io->conv || !io->recurrent || !io->draft_tokens)
+        return fail(ctx, K3XB_INVALID_EXTENT, "draft io");
+    // the draft model: every MoE layer routed with draft_top_k experts
+    std::unique_ptr<k3xb_layer[]> layers(new (std::nothrow) k3xb_layer[m->layers]);
+    if (!layers) return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "draft: out of host memory");
+    for (uint32_t l = 0; l < m->layers; ++l) {
+        layers[l] = m->layer[l];
+        if (!K || K > layers[l].moe.top_k) return fail(ctx, K3XB_INVALID_EXTENT, "draft_top_k must be in [1, top_k]");
+        layers[l].moe.top_k = K;
+    }
+    k3xb_verify_model dm = *m;
+    dm.layer = layers.get();
+    const k3xb_layer& L0 = layers[0];
+    const size_t P = static_cast<size_t>(L0.kda.heads) * L0.kda.head_dim;
+    const size_t conv_n = static_cast<size_t>(m->layers) * S * 3 * (L0.kda.conv_width ? L0.kda.conv_width - 1 : 0) * P;
+    const size_t rec_n = static_cast<size_t>(m->layers) * S * L0.kda.heads * L0.kda.head_dim * L0.kda.head_dim;
+    Sizer sz;
+    sz.take<uint16_t>(conv_n);
+    sz.take<float>(rec_n);
+    sz.take<uint32_t>(4ull * S);
+    void* base;
+    int st = ensure_io(ctx, sz.used, &base);
+    if (st) return st;
+    Carver c(base);
+    uint16_t* conv = c.take<uint16_t>(conv_n);
+    float* rec = c.take<float>(rec_n);
+    uint32_t* tok = c.take<uint32_t>(S);
+    uint32_t* acc = c.take<uint32_t>(S);
+    uint32_t* com = c.take<uint32_t>(S);
+    uint32_t* cnt = c.take<uint32_t>(S);
+    // the draft continues from the committed state on a copy of it
+    K3XB_CUDA(ctx, cudaMemcpyAsync(conv, io->conv, conv_n * sizeof(uint16_t), cudaMemcpyDeviceToDevice, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(rec, io->recurrent, rec_n * sizeof(float), cudaMemcpyDeviceToDevice, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(tok, io->anchors, S * sizeof(uint32_t), cudaMemcpyDeviceToDevice, ctx->stream));
+    k3xb_verify_io v{};
+    v.sequences = S;
+    v.drafts = 0;   // one position per sequence: a greedy decode step
+    v.tokens = tok;
+    v.conv = conv;
+    v.recurrent = rec;
+    v.mode = K3XB_ACCEPT_GREEDY;
+    v.accepted = acc;
+    v.committed = com;
+    v.committed_count = cnt;
+    for (uint32_t i = 0; i < p; ++i) {
+        if ((st = k3xb_verify_step(ctx, &dm, &v))) return st;
+        // committed[s][0] is the argmax after the fed token: draft i, and the next input
+        K3XB_CUDA(ctx, cudaMemcpy2DAsync(io->draft_tokens + i, p * sizeof(uint32_t), com, sizeof(uint32_t),
+                                         sizeof(uint32_t), S, cudaMemcpyDeviceToDevice, ctx->stream));
+        K3XB_CUDA(ctx, cudaMemcpyAsync(tok, com, S * sizeof(uint32_t), cudaMemcpyDeviceToDevice, ctx->stream));
+    }
+    return K3XB_OK;
+}
+
+int k3xb_speculative_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_speculative_io* io) {
+    if (!ctx) return K3XB_INVALID_EXTENT;
+    if (!m || !io || !io->anchors || !io->conv || !io->recurrent || !io->draft_tokens || !io->accepted ||
+        !io->committed || !io->committed_count || !io->sequences || !io->drafts)
+        return fail(ctx, K3XB_INVALID_EXTENT, "speculative io");
+    const uint32_t S = io->sequences, p = io->drafts;
+    k3xb_draft_io d{S, p, io->draft_top_k, io->anchors, io->conv, io->recurrent, io->draft_tokens};
+    int st = k3xb_draft_greedy(ctx, m, &d);
+    if (st) return st;
+    // anchor + drafts, per sequence (the drafter's own buffers are done with)
+    void* base;
+    if ((st = ensure_io(ctx, sizeof(uint32_t) * S * (p + 1), &base))) return st;
+    uint32_t* tokens = static_cast<uint32_t*>(base);
+    K3XB_CUDA(ctx, cudaMemcpy2DAsync(tokens, (p + 1) * sizeof(uint32_t), io->anchors, sizeof(uint32_t),
+                                     sizeof(uint32_t), S, cudaMemcpyDeviceToDevice, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpy2DAsync(tokens + 1, (p + 1) * sizeof(uint32_t), io->draft_tokens, p * sizeof(uint32_t),
+                                     p * sizeof(uint32_t), S, cudaMemcpyDeviceToDevice, ctx->stream));
+    k3xb_verify_io v{};
+    v.sequences = S;
+    v.drafts = p;
+    v.tokens = tokens;
+    v.draft_tokens = io->draft_tokens;
+    v.conv = io->conv;
+    v.recurrent = io->recurrent;
+    v.mode = K3XB_ACCEPT_GREEDY;
+    v.logits = io->logits;
+    v.accepted = io->accepted;
+    v.committed = io->committed;
+    v.committed_count = io->committed_count;
+    if ((st = k3xb_verify_step(ctx, m, &v))) return st;
+    return launch_next_anchor(ctx, io->committed, io->committed_count, S, p + 1, io->anchors);
 }
 
 int k3xb_ep_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* local, uint32_t E, const float* hidden,

@@ -44,6 +44,10 @@ int launch_accept_rejection(k3xb_ctx* ctx, const float* tl, const float* dl, con
                             uint64_t seq_base, double* pd, double* qd, uint32_t* accepted,
                             uint32_t* committed, uint32_t* count);
 
+// anchors[s] = committed[s][count[s] - 1] (the next round's anchor)
+int launch_next_anchor(k3xb_ctx* ctx, const uint32_t* committed, const uint32_t* count, uint32_t S, uint32_t stride,
+                       uint32_t* anchors);
+
 // synth.cu
 int launch_fill_normal_f32(k3xb_ctx* ctx, float* out, size_t n, uint64_t seed, uint64_t stream,
                            float mean, float sigma);

@@ -85,6 +85,17 @@ class VerifyIO(C.Structure):
         (n, C.c_void_p) for n in ("logits", "accepted", "committed", "committed_count")]
 
 
+class DraftIO(C.Structure):
+    _fields_ = [("sequences", C.c_uint32), ("drafts", C.c_uint32), ("draft_top_k", C.c_uint32)] + [
+        (n, C.c_void_p) for n in ("anchors", "conv", "recurrent", "draft_tokens")]
+
+
+class SpeculativeIO(C.Structure):
+    _fields_ = [("sequences", C.c_uint32), ("drafts", C.c_uint32), ("draft_top_k", C.c_uint32)] + [
+        (n, C.c_void_p) for n in ("anchors", "conv", "recurrent", "draft_tokens", "accepted", "committed",
+                                  "committed_count", "logits")]
+
+
 class RoutingPolicy(C.Structure):
     _fields_ = [("mode", C.c_int32), ("fixed_k", C.c_uint32), ("mass_target", C.c_float),
                 ("minimum_gap", C.c_float), ("quality_floor_k", C.c_uint32)]
@@ -167,6 +178,8 @@ def library() -> C.CDLL:
             "k3xb_attention_residual_norm": [vp, vp, vp, vp, vp, vp, vp, u32, u32, f32, vp, vp],
             "k3xb_layer_forward": [vp, C.POINTER(Layer), vp, vp, vp, u32, u32, vp, vp, vp, vp, vp],
             "k3xb_verify_step": [vp, C.POINTER(VerifyModel), C.POINTER(VerifyIO)],
+            "k3xb_draft_greedy": [vp, C.POINTER(VerifyModel), C.POINTER(DraftIO)],
+            "k3xb_speculative_step": [vp, C.POINTER(VerifyModel), C.POINTER(SpeculativeIO)],
             "k3xb_ep_unique_id": [vp],
             "k3xb_ep_init": [vp, vp, C.c_int32, C.c_int32],
             "k3xb_ep_finalize": [vp],
@@ -352,6 +365,22 @@ class Context:
 
     def verify_step(self, model: "VerifyModel", io: "VerifyIO"):
         self._check(self.lib.k3xb_verify_step(self.h, C.byref(model), C.byref(io)), "verify_step")
+
+    def draft_greedy(self, model: "VerifyModel", anchors, conv, recurrent, draft_tokens, draft_top_k):
+        """AURORA reduced-Top-K self-draft: draft_tokens [S][p] (device int32)
+        from anchors [S] and the committed states (read, not changed)."""
+        S, p = draft_tokens.shape
+        io = DraftIO(S, p, draft_top_k, _p(anchors), _p(conv), _p(recurrent), _p(draft_tokens))
+        self._check(self.lib.k3xb_draft_greedy(self.h, C.byref(model), C.byref(io)), "draft_greedy")
+
+    def speculative_step(self, model: "VerifyModel", anchors, conv, recurrent, draft_tokens, accepted, committed,
+                         committed_count, draft_top_k, logits=None):
+        """One on-device round: draft, verify, advance the state, anchors <-
+        last committed tokens (all device tensors)."""
+        S, p = draft_tokens.shape
+        io = SpeculativeIO(S, p, draft_top_k, _p(anchors), _p(conv), _p(recurrent), _p(draft_tokens), _p(accepted),
+                           _p(committed), _p(committed_count), _p(logits))
+        self._check(self.lib.k3xb_speculative_step(self.h, C.byref(model), C.byref(io)), "speculative_step")
 
     # ---- (e) --------------------------------------------------------------------
     def accept_greedy(self, logits, drafts, accepted, committed, count, targets=None):

@@ -86,3 +86,12 @@ def test_profiling_entry_points():
     arr = (k3xb.PhaseTime * k3xb.PHASE_COUNT)()
     assert lib.k3xb_set_profiling(None, 1) == k3xb.INVALID_EXTENT
     assert lib.k3xb_get_profile(None, arr, None) == k3xb.INVALID_EXTENT
+
+
+def test_draft_entry_point_rejects_null_context():
+    import ctypes as C
+
+    import k3xb
+    lib = k3xb.library()
+    io = k3xb.DraftIO(1, 1, 1, None, None, None, None)
+    assert lib.k3xb_draft_greedy(None, C.byref(k3xb.VerifyModel()), C.byref(io)) == k3xb.INVALID_EXTENT
