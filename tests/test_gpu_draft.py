@@ -137,11 +137,12 @@ def test_reduced_k_first_draft_is_the_reduced_argmax(rs):
         ctx.close()
 
 
-def test_on_device_rounds_follow_the_greedy_decode(rs):
-    """Two on-device rounds (draft with the full K, verify, advance, next
-    anchor) commit exactly the target's greedy decode: every draft is
-    accepted, and the committed tokens of round 1 then round 2 are the
-    2(p+1) tokens a plain greedy decode from the same state produces."""
+def test_on_device_steps_follow_the_greedy_decode(rs):
+    """Two on-device speculative steps (draft with the full K, verify,
+    advance, next anchor) commit exactly the target's greedy decode: every
+    draft is accepted, and the committed tokens of the first step then the
+    second are the 2(p+1) tokens a plain greedy decode from the same state
+    produces."""
     import k3xb
     torch = torch_cuda()
     S, p = 2, 3
