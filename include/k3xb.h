@@ -2,19 +2,21 @@
  * k3xb.h — C ABI of the B200-native K3X speculative-verification library
  * (libk3xb.so, built from project-k3x_b200/csrc for sm_100a).
  *
- * Plain pointers and sizes only. Unless a name ends in _host, every array
- * argument is DEVICE memory on the context's GPU and the call is
- * asynchronous on the context's current stream (k3xb_set_stream). All
+ * Plain pointers and sizes only. Every array argument is DEVICE memory on
+ * the context's GPU and the call is asynchronous on the context's current
+ * stream (k3xb_set_stream), except where a name ends in _host and for the
+ * resident-weight uploads (k3xb_acquire_*), which read HOST arrays. All
  * entry points return a status that mirrors k3x::ErrorCode
  * (runtime/include/k3x/status.hpp:9-30); k3xb_last_error() gives the
  * message of the last failure on a context. There is no CPU fallback: a
  * missing or unsupported device returns K3XB_BACKEND_UNAVAILABLE or
  * K3XB_UNSUPPORTED_ARCHITECTURE.
  *
- * Each entry point names the reference interface it replaces; a C++20
- * adapter on the reference side maps k3x::ComputeBackend
- * (runtime/include/k3x/backend.hpp:326-462) and the free verification
- * functions onto these calls.
+ * Each entry point names the reference interface it replaces. The C++20
+ * adapter project-k3x_b200/adapter/backend_b200.cpp maps
+ * k3x::ComputeBackend (runtime/include/k3x/backend.hpp:326-462) onto these
+ * calls for the reference runtime; include/k3xb.hpp is the C++20 host
+ * layer over them.
  */
 #ifndef K3XB_H
 #define K3XB_H
