@@ -1,8 +1,11 @@
 """Expert-parallel MoE layer: the dispatch / local plan / return / combine
 algorithm of csrc/ep.cu, restated on the CPU with the oracle's expert math
-and run as 2 gloo ranks. Its output must equal the single-process oracle
-layer bit for bit (the combine keeps the one-GPU slot order), which is the
-property the CUDA path is tested for on 2 GPUs in test_gpu_ep.py.
+and run as 2 gloo ranks, for the plain MoE and for LatentMoE (latent rows
+are projected on the home rank, sent, computed and returned; the routed
+norm and up projection run at home). Its output must equal the
+single-process oracle layer bit for bit (the combine keeps the one-GPU slot
+order), which is the property the CUDA path is tested for on 2 GPUs in
+test_gpu_ep.py and with a world of one in test_gpu_latent.py.
 
 gloo has no all-to-all, so the exchange is an all_gather of the fixed-size
 per-destination buffers from which each rank takes its block: the same data
@@ -22,9 +25,10 @@ NO_ENTRY = 0xFFFFFFFF
 DIMS = dict(hidden=256, inter=128, experts=8, top_k=3, shared_inter=128, tokens_per_rank=5)
 
 
-def _layer(rs):
+def _layer(rs, latent=0):
     d = DIMS
-    return make_moe_layer(rs, 91, d["hidden"], d["inter"], d["experts"], d["top_k"], d["shared_inter"])
+    return make_moe_layer(rs, 91, d["hidden"], d["inter"], d["experts"], d["top_k"], d["shared_inter"],
+                          latent=latent)
 
 
 def _hidden(world):
@@ -32,7 +36,7 @@ def _hidden(world):
 
 
 def _expert(rs, L, e, x):
-    H, I = L["hidden"], L["inter"]
+    H, I = L.get("latent") or L["hidden"], L["inter"]   # the experts' width
     g = rs.mxfp4_matmul(x, L["gate_packed"][e], L["gate_scales"][e], I, H)
     u = rs.mxfp4_matmul(x, L["up_packed"][e], L["up_scales"][e], I, H)
     return rs.round_bf16(rs.mxfp4_matmul(rs.swiglu(g, u), L["down_packed"][e], L["down_scales"][e], H, I))
@@ -50,20 +54,23 @@ def _exchange(send, world):
     return recv.view(np.uint32) if as_int else recv
 
 
-def _ep_rank(rank, world, port, out_dir):
+def _ep_rank(rank, world, port, out_dir, latent):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     rs = Restatement()
-    L = _layer(rs)
+    L = _layer(rs, latent)
     E, K, H = L["experts"], L["top_k"], L["hidden"]
+    D = latent or H   # rows sent, computed and returned: latent rows for LatentMoE
     E_r, T = E // world, DIMS["tokens_per_rank"]
-    x = _hidden(world)[rank * T:(rank + 1) * T]
+    x_in = _hidden(world)[rank * T:(rank + 1) * T]
+    # LatentMoE: the latent projection happens on the home rank (official_moe.cpp:296)
+    x = np.stack([rs.bf16_matvec(x_in[t], L["routed_down"]) for t in range(T)]) if latent else x_in
     # route on the home rank (all E logits)
     ids = np.empty((T, K), np.uint32)
     con = np.empty((T, K), np.float32)
     for t in range(T):
-        ids[t], con[t] = rs.route(x[t], L["router"], L["correction"], K)
+        ids[t], con[t] = rs.route(x_in[t], L["router"], L["correction"], K)
     # dispatch: every row to every rank, (local expert << 8 | slot) metadata
     meta = np.full((world, T, K), NO_ENTRY, np.uint32)
     for g in range(world):
@@ -71,26 +78,29 @@ def _ep_rank(rank, world, port, out_dir):
             for j in range(K):
                 if ids[t, j] // E_r == g:
                     meta[g, t, j] = (int(ids[t, j]) - g * E_r) << 8 | j
-    send_x = np.broadcast_to(x, (world, T, H))
+    send_x = np.broadcast_to(x, (world, T, D))
     recv_meta = _exchange(meta, world)
     recv_x = _exchange(send_x, world)
     # local expert-major plan: ascending local expert, (row, slot) order
-    rows = recv_x.reshape(world * T, H)
+    rows = recv_x.reshape(world * T, D)
     m = recv_meta.reshape(world * T, K)
-    y = np.zeros((world * T, K, H), np.float32)
+    y = np.zeros((world * T, K, D), np.float32)
     for e in range(E_r):
         for r in range(world * T):
             for j in range(K):
                 if m[r, j] != NO_ENTRY and (m[r, j] >> 8) == e:
                     y[r, m[r, j] & 0xFF] = _expert(rs, L, rank * E_r + e, rows[r])
-    y_home = _exchange(y.reshape(world, T, K, H), world)
-    # combine in slot order with each slot's owner, then + shared
+    y_home = _exchange(y.reshape(world, T, K, D), world)
+    # combine in slot order with each slot's owner (then, for LatentMoE, the
+    # routed norm and up projection, :323-331), then + shared
     out = np.empty((T, H), np.float32)
     for t in range(T):
         ys = np.stack([y_home[ids[t, j] // E_r, t, j] for j in range(K)])
         mixed = rs.routed_combine(ys, con[t])
-        gs = rs.bf16_matvec(x[t], L["shared_gate"])
-        us = rs.bf16_matvec(x[t], L["shared_up"])
+        if latent:
+            mixed = rs.bf16_matvec(rs.rms_norm(mixed, L["routed_norm"], L["latent_eps"]), L["routed_up"])
+        gs = rs.bf16_matvec(x_in[t], L["shared_gate"])
+        us = rs.bf16_matvec(x_in[t], L["shared_up"])
         shared = rs.bf16_matvec(rs.swiglu(gs, us), L["shared_down"])
         out[t] = rs.round_bf16(mixed + shared)
     np.save(os.path.join(out_dir, f"out{rank}.npy"), out)
@@ -99,11 +109,11 @@ def _ep_rank(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
-def test_ep_restatement_equals_one_process(rs, tmp_path, world):
-    port = 29500 + os.getpid() % 2000
-    mp.start_processes(_ep_rank, args=(world, port, str(tmp_path)), nprocs=world, start_method="spawn")
-    L = _layer(rs)
+@pytest.mark.parametrize("world,latent", [(2, 0), (2, 128)])
+def test_ep_restatement_equals_one_process(rs, tmp_path, world, latent):
+    port = 29500 + (os.getpid() + latent) % 2000
+    mp.start_processes(_ep_rank, args=(world, port, str(tmp_path), latent), nprocs=world, start_method="spawn")
+    L = _layer(rs, latent)
     want, want_ids, _ = rs.moe_layer(L, _hidden(world))
     T = DIMS["tokens_per_rank"]
     for r in range(world):
