@@ -552,6 +552,62 @@ def run_c2_ep(args, rank, world, local, ctx, stream, cfg):
     ctx.ep_finalize()
 
 
+def run_tc_sweep(args, rank, world, local, ctx, stream):
+    """Tensor-core sweep of the expert GEMM: 8 experts x M
+    tokens each (Top-8 of 8, so every token uses every expert) for
+    M in {256, 1024, 4096}, c2 expert shapes. Reports useful TFLOP/s
+    (2 * T * k * 3 * H * I per call) and the MMA work, which is `terms`
+    times larger because each activation row enters as E2M1 terms."""
+    import ctypes as C
+
+    import torch
+
+    import k3xb
+    lines = []
+    for M in (256, 1024, 4096):
+        cfg = dict(C2, experts=8, top_k=8, tokens=M)
+        w, desc, hidden = make_c2_layer(ctx, torch, cfg, k3xb.ENGINE_MXF4, args.act_terms)
+        T, E, K, H, I = M, 8, 8, cfg["hidden"], cfg["inter"]
+        ids = torch.arange(K, dtype=torch.int32, device="cuda").repeat(T, 1).contiguous()
+        con = torch.full((T, K), 1.0 / K, dtype=torch.float32, device="cuda")
+        plan = dict(group_expert=torch.empty(E, dtype=torch.int32, device="cuda"),
+                    group_offset=torch.empty(E + 1, dtype=torch.int32, device="cuda"),
+                    assign_token=torch.empty(T * K, dtype=torch.int32, device="cuda"),
+                    assign_slot=torch.empty(T * K, dtype=torch.int32, device="cuda"),
+                    assign_contrib=torch.empty(T * K, dtype=torch.float32, device="cuda"),
+                    group_count=torch.empty(1, dtype=torch.int32, device="cuda"),
+                    status=torch.zeros(1, dtype=torch.int32, device="cuda"))
+        ctx.expert_major_plan(ids, con, E, plan)
+        slot_out = torch.empty((T * K, H), dtype=torch.float32, device="cuda")
+        pl = k3xb.Plan(*(k3xb._p(plan[k]) for k in ("group_expert", "group_offset", "assign_token",
+                                                      "assign_slot", "assign_contrib", "group_count", "status")))
+
+        def experts():
+            ctx._check(ctx.lib.k3xb_moe_experts(ctx.h, C.byref(desc), k3xb._p(hidden), T, C.byref(pl),
+                                                k3xb._p(slot_out)), "moe_experts")
+
+        for _ in range(args.warmup):
+            experts()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            experts()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        useful = 2.0 * T * K * 3 * H * I
+        lines.append({"tokens_per_expert": M, "ms": ms, "useful_tflops": useful / (ms * 1e-3) / 1e12,
+                      "mma_tflops": useful * args.act_terms / (ms * 1e-3) / 1e12})
+        del w, desc, hidden, slot_out
+        torch.cuda.empty_cache()
+    if rank == 0:
+        print(json.dumps({"metric": "expert GEMM tensor-core sweep (useful TFLOP/s)", "config":
+                          {"workload": "8 experts x M tokens, Top-8 of 8, H 7168, I 2048, MXFP4",
+                           "act_terms": args.act_terms}, "sweep": lines,
+                          "peak_note": "mxf4 dense peak 9 PFLOP/s nominal; MMA work = terms x useful"}), flush=True)
+
+
 def run_ours(args):
     import torch
 
@@ -572,6 +628,9 @@ def run_ours(args):
         return finish(ctx, world)
     if args.config == "c3":
         run_c3(args, rank, world, local, ctx, stream)
+        return finish(ctx, world)
+    if args.config == "tc":
+        run_tc_sweep(args, rank, world, local, ctx, stream)
         return finish(ctx, world)
     if world > 1:
         run_c2_ep(args, rank, world, local, ctx, stream, cfg)
@@ -805,8 +864,9 @@ def main():
     ap.add_argument("--engine", choices=["mxf4", "simt"], default=os.environ.get("K3XB_ENGINE", "mxf4"))
     ap.add_argument("--act-terms", type=int, default=6)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", choices=["c2", "c3", "c4"], default="c2",
-                    help="c2 (default, the headline line), c3 KDA tree, c4 two-layer verify step")
+    ap.add_argument("--config", choices=["c2", "c3", "c4", "tc"], default="c2",
+                    help="c2 (default, the headline line), c3 KDA tree, c4 two-layer verify step, "
+                         "tc tensor-core sweep of the expert GEMM")
     ap.add_argument("--accept", choices=["greedy", "rejection"], default="greedy", help="c4 acceptance rule")
     ap.add_argument("--sequences", type=int, default=1, help="c3: sequences sharing the draft tree")
     ap.add_argument("--experts", type=int, default=0, help="c2 with fewer experts (small profiler case)")
