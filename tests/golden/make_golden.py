@@ -112,6 +112,69 @@ def kda_block(ref):
          next_conv_q=cq, next_conv_k=ck, next_conv_v=cv, next_recurrent=r.reshape(rec.shape), **arrays, **dims)
 
 
+def kda_kat_inputs():
+    """The known-answer case of the reference's tests/cpp/test_official_kda.cpp
+    (and tests/python/test_cpp_parity.py): H 4, 2 heads of 2, conv width 3,
+    eps 1e-5, gate lower bound -5, zero state, two positions."""
+    eye = np.eye(4, dtype=np.float32)
+    conv = np.array([[0.25, -0.5, 1.0], [-0.25, 0.5, 0.75], [0.5, 0.25, -0.5], [-0.5, 0.25, 1.25]], np.float32)
+    w = dict(hidden=4, heads=2, head_dim=2, conv_width=3, eps=1e-5, gate_lower_bound=-5.0,
+             q_proj=bf16_words(eye),
+             k_proj=bf16_words(np.array([[0.5, 0, 0.25, 0], [0, 0.75, 0, -0.25], [0.25, 0, 1, 0], [0, -0.5, 0, 0.5]])),
+             v_proj=bf16_words(eye), q_conv=conv, k_conv=(conv * 0.75).astype(np.float32),
+             v_conv=(conv * -0.5).astype(np.float32),
+             f_a_proj=bf16_words(np.array([[0.5, -0.25, 0, 0.25], [0, 0.5, -0.5, 0.25]])),
+             f_b_proj=bf16_words(np.array([[1, 0], [0.5, -0.5], [0, 1], [-0.25, 0.75]])),
+             a_log=np.array([0.0, 0.5], np.float32), dt_bias=np.array([0.25, -0.5, 0.75, -0.25], np.float32),
+             b_proj=bf16_words(np.array([[0.5, -0.25, 0.25, 0], [0, 0.5, -0.5, 0.25]])),
+             g_proj=bf16_words(np.array([[0.5, 0, 0, -0.25], [0, 0.5, 0.25, 0], [-0.25, 0, 0.5, 0], [0, 0.25, 0, 0.75]])),
+             o_norm=np.array([1.0, 1.5], np.float32), o_proj=bf16_words(eye))
+    hidden = np.array([[0.5, -1.0, 0.25, 0.75], [-0.25, 0.5, 1.0, -0.5]], np.float32)
+    return w, hidden
+
+
+def kda_kat(ref):
+    """The reference's KDA known-answer case through its C++ official_kda_cpu
+    and, where the reference tree is importable, its independent torch
+    implementation (reference/k3x_ref/official_kda.py)."""
+    w, hidden = kda_kat_inputs()
+    z16 = np.zeros(2 * 4, np.uint16)
+    out, (cq, ck, cv, r) = ref.kda_block(w, hidden, z16, z16, z16, np.zeros(8, np.float32))
+    arrays = dict(out=out, conv_q=cq, conv_k=ck, conv_v=cv, recurrent=r)
+    torch_ref = _torch_kda(w, hidden)
+    if torch_ref is not None:
+        arrays.update({f"torch_{k}": v for k, v in torch_ref.items()})
+    save("kda_kat.npz", **arrays)
+
+
+def _torch_kda(w, hidden):
+    ref_root = os.environ.get("K3X_REFERENCE")
+    if not ref_root:
+        import re
+        m = re.search(r"^REF \?= (\S+)", open(os.path.join(ROOT, "oracle", "Makefile")).read(), re.M)
+        ref_root = m.group(1) if m else ""
+    pkg = os.path.join(ref_root, "reference")
+    if not os.path.isdir(os.path.join(pkg, "k3x_ref")):
+        return None
+    sys.path.insert(0, pkg)
+    import torch
+    from k3x_ref.official_kda import (OfficialKdaConfig, OfficialKdaWeights, official_kda,
+                                      zero_official_kda_state)
+    bf = lambda a: torch.from_numpy((np.asarray(a, np.uint32) << 16).view(np.float32).copy()).to(torch.bfloat16)
+    f32 = lambda a: torch.from_numpy(np.asarray(a, np.float32).copy())
+    cfg = OfficialKdaConfig(4, 2, 2, 3, 1.0e-5, -5.0)
+    weights = OfficialKdaWeights(
+        q_proj=bf(w["q_proj"]), k_proj=bf(w["k_proj"]), v_proj=bf(w["v_proj"]),
+        q_conv=f32(w["q_conv"]), k_conv=f32(w["k_conv"]), v_conv=f32(w["v_conv"]),
+        f_a_proj=bf(w["f_a_proj"]), f_b_proj=bf(w["f_b_proj"]), a_log=f32(w["a_log"]), dt_bias=f32(w["dt_bias"]),
+        b_proj=bf(w["b_proj"]), g_proj=bf(w["g_proj"]), o_norm=f32(w["o_norm"]), o_proj=bf(w["o_proj"]))
+    x = torch.from_numpy(hidden).to(torch.bfloat16).reshape(1, 2, 4)
+    res = official_kda(x, weights, zero_official_kda_state(cfg, 1, x.device), cfg)
+    words = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16).reshape(-1)
+    return dict(out=res.output.float().numpy().reshape(2, 4), conv_q=words(res.state.conv_q),
+                conv_k=words(res.state.conv_k), conv_v=words(res.state.conv_v))
+
+
 def prepare_input(ref):
     """prepare_official_moe_input (official_moe.cpp:156-209) for 4 rows."""
     g = np.random.default_rng(1007)
@@ -187,6 +250,7 @@ def main():
     moe_layer(ref, rs)
     latent_moe(ref, rs)
     kda_block(ref)
+    kda_kat(ref)
     prepare_input(ref)
     select_routing(ref)
     verify_greedy(ref)

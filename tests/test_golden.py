@@ -107,3 +107,29 @@ def test_latent_moe(rs):
     np.testing.assert_array_equal(ids, f["ids"])
     np.testing.assert_array_equal(con, f["contributions"])
     np.testing.assert_array_equal(rs.round_bf16(rs.round_bf16(f["prefix"]) + moe), f["out"])
+
+
+def test_kda_known_answer(rs):
+    """The reference's own KDA known-answer case (tests/cpp/test_official_kda.cpp,
+    tests/python/test_cpp_parity.py): the restatement equals the reference's
+    C++ official_kda_cpu bit for bit, equals its independent torch
+    implementation to 1e-6 with identical conv-state words, and running the
+    two positions one call at a time (the second from the first's state)
+    gives the same outputs and state as one call over both."""
+    from golden.make_golden import kda_kat_inputs
+    f = gu.load("kda_kat.npz")
+    w, hidden = kda_kat_inputs()
+    z16, z32 = np.zeros(8, np.uint16), np.zeros(8, np.float32)
+    out, (cq, ck, cv, r) = rs.kda_block(w, hidden, z16, z16, z16, z32)
+    np.testing.assert_array_equal(out, f["out"])
+    for got, key in ((cq, "conv_q"), (ck, "conv_k"), (cv, "conv_v"), (r, "recurrent")):
+        np.testing.assert_array_equal(got, f[key])
+    if "torch_out" in f:
+        np.testing.assert_allclose(out, f["torch_out"], atol=1e-6, rtol=0)
+        for got, key in ((cq, "conv_q"), (ck, "conv_k"), (cv, "conv_v")):
+            np.testing.assert_array_equal(got, f["torch_" + key])
+    o1, s1 = rs.kda_block(w, hidden[:1], z16, z16, z16, z32)
+    o2, s2 = rs.kda_block(w, hidden[1:], *s1)
+    np.testing.assert_array_equal(np.concatenate([o1, o2]), out)
+    for a, b in zip(s2, (cq, ck, cv, r)):
+        np.testing.assert_array_equal(a, b)
