@@ -483,6 +483,8 @@ class Reference:
         L.k3xr_select_routing.argtypes = _SELECT_ROUTING_ARGS
         L.k3xr_official_moe.argtypes = [C.c_void_p, _f32p, _f32p, _u16p, _u16p, _u16p, C.c_float, _sz, _f32p,
                                         _u32p, _f32p]
+        L.k3xr_official_layer.argtypes = [C.c_void_p, C.c_void_p, _u16p, _u16p, _u16p, _u16p, _u16p, _u16p,
+                                          C.c_float, _f32p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p, _f32p, _u32p]
 
     def decode_mxfp4(self, packed, scales, rows, cols, group=32):
         out = np.empty(rows * cols, np.float32)
@@ -619,6 +621,25 @@ class Reference:
             raise OracleError(st, "ref official_moe_cpu")
         return out, ids, con
 
+    def official_layer(self, layer: dict, hidden_in, block, conv, recurrent):
+        """official_layer_cpu (LatentMoE) over T positions of one sequence:
+        (out [T][H], ids [T][k], (conv_q, conv_k, conv_v, recurrent) after)."""
+        ks, keep_k = kda_struct(layer["kda"])
+        ms, keep_m = moe_struct(layer["moe"])
+        hidden_in, block = _c(hidden_in, np.float32), _c(block, np.float32)
+        T, H = hidden_in.shape
+        cq, ck, cv = (np.array(a, np.uint16, copy=True) for a in conv)
+        rec = np.array(recurrent, np.float32, copy=True)
+        out = np.zeros((T, H), np.float32)
+        ids = np.zeros((T, layer["moe"]["top_k"]), np.uint32)
+        st = self.lib.k3xr_official_layer(C.byref(ks), C.byref(ms), *(_c(layer[k], np.uint16) for k in (
+            "self_residual_norm", "self_residual_proj", "input_norm", "moe_residual_norm", "moe_residual_proj",
+            "post_norm")), layer["rms_eps"], hidden_in, block, T, cq, ck, cv, rec, out, ids)
+        del keep_k, keep_m
+        if st:
+            raise OracleError(st, "ref official_layer_cpu")
+        return out, ids, (cq, ck, cv, rec)
+
     def prepare_input(self, prefix, block, norm, proj, post, eps):
         out = np.empty(len(prefix), np.float32)
         st = self.lib.k3xr_prepare_moe_input(_c(prefix, np.float32), _c(block, np.float32), _c(norm, np.uint16),
@@ -723,7 +744,7 @@ def make_kda_weights(g, hidden, heads, head_dim, conv_width=4, sigma=0.02):
 
 
 def make_layer(rs: Restatement, seed, hidden, heads, head_dim, experts, top_k, inter, shared_inter,
-               conv_width=4, sigma=0.02):
+               conv_width=4, sigma=0.02, latent=0):
     """Synthetic KDA + MoE layer (BASELINE configs[0] recipe: N(0, sigma)
     weights, norms = 1, residual projections N(0, sigma), MXFP4 experts)."""
     g = np.random.default_rng(seed)
@@ -733,4 +754,5 @@ def make_layer(rs: Restatement, seed, hidden, heads, head_dim, experts, top_k, i
                 input_norm=ones, moe_residual_norm=ones,
                 moe_residual_proj=bf16_words(g.normal(0.0, sigma, size=hidden)), post_norm=ones,
                 kda=make_kda_weights(g, hidden, heads, head_dim, conv_width, sigma),
-                moe=make_moe_layer(rs, seed + 1000, hidden, inter, experts, top_k, shared_inter, sigma))
+                moe=dict(make_moe_layer(rs, seed + 1000, hidden, inter, experts, top_k, shared_inter, sigma,
+                                        latent=latent), latent_eps=1e-6))

@@ -10,6 +10,7 @@
 // arrays into the reference's C++ API and back.
 #include "k3x/expert_major.hpp"
 #include "k3x/official_kda.hpp"
+#include "k3x/official_layer.hpp"
 #include "k3x/official_moe.hpp"
 #include "k3x/routing_policy.hpp"
 #include "k3x/ops.hpp"
@@ -345,15 +346,19 @@ int k3xr_moe_layer_forward(const k3xr_moe_layer* layer, const float* hidden,
 // reference's prepare_official_moe_input (with residual_norm/proj and
 // post_norm), its route route_official_moe on that row. out [T][H] is the
 // reference's `output` (with the prefix residual); ids/contributions [T][k].
-int k3xr_official_moe(const k3xr_moe_layer* layer, const float* prefix, const float* block,
-                      const std::uint16_t* residual_norm, const std::uint16_t* residual_proj,
-                      const std::uint16_t* post_norm, float eps, std::size_t T, float* out,
-                      std::uint32_t* ids, float* contributions) {
-    const auto& L = *layer;
+}  // extern "C"
+
+namespace {
+
+std::span<const std::uint16_t> w16(const std::uint16_t* p, std::size_t n) { return {p, n}; }
+
+// The reference's OfficialMoeWeights over a LatentMoE layer's arrays;
+// `experts` receives the per-expert views it points into.
+k3x::OfficialMoeWeights official_moe_weights(const k3xr_moe_layer& L, const std::uint16_t* residual_norm,
+                                             const std::uint16_t* residual_proj, const std::uint16_t* post_norm,
+                                             std::vector<k3x::OfficialExpertView>& experts) {
     const std::size_t H = L.hidden, I = L.inter, D = L.latent, E = L.experts;
-    if (!D || L.activation != 0) return static_cast<int>(ErrorCode::invalid_state);
-    const auto w16 = [](const std::uint16_t* p, std::size_t n) { return std::span<const std::uint16_t>(p, n); };
-    std::vector<k3x::OfficialExpertView> experts(E);
+    experts.assign(E, {});
     for (std::size_t e = 0; e < E; ++e) {
         experts[e].expert_id = static_cast<std::uint32_t>(e);
         experts[e].weights.gate = {e * 3 + 1, bytes(L.gate_packed + e * I * D / 2, I * D / 2),
@@ -378,6 +383,22 @@ int k3xr_official_moe(const k3xr_moe_layer* layer, const float* prefix, const fl
         w.shared.down = {w16(L.shared_down, H * L.shared_inter), H, L.shared_inter, 10};
     }
     w.experts = experts;
+    return w;
+}
+
+}  // namespace
+
+extern "C" {
+
+int k3xr_official_moe(const k3xr_moe_layer* layer, const float* prefix, const float* block,
+                      const std::uint16_t* residual_norm, const std::uint16_t* residual_proj,
+                      const std::uint16_t* post_norm, float eps, std::size_t T, float* out,
+                      std::uint32_t* ids, float* contributions) {
+    const auto& L = *layer;
+    const std::size_t H = L.hidden;
+    if (!L.latent || L.activation != 0) return static_cast<int>(ErrorCode::invalid_state);
+    std::vector<k3x::OfficialExpertView> experts;
+    const k3x::OfficialMoeWeights w = official_moe_weights(L, residual_norm, residual_proj, post_norm, experts);
     for (std::size_t t = 0; t < T; ++t) {
         k3x::OfficialMoeInput in{std::vector<float>(prefix + t * H, prefix + (t + 1) * H),
                                  std::vector<float>(block + t * H, block + (t + 1) * H)};
@@ -442,6 +463,58 @@ int k3xr_official_kda_cpu(const k3xr_kda_weights* w, const float* hidden,
     std::copy(s.conv_v.begin(), s.conv_v.end(), conv_v);
     std::copy(s.recurrent_v_first.begin(), s.recurrent_v_first.end(), recurrent);
     std::copy(r.value().output.begin(), r.value().output.end(), out);
+    return 0;
+}
+
+// official_layer_cpu itself (official_layer.cpp:134-244: attention
+// residual + input norm, official_kda_cpu over the positions, then per
+// position the prefix, the MoE input preparation, route_official_moe and
+// official_moe_cpu with LatentMoE) for T positions of one sequence. The
+// KDA state arrays hold the initial state and receive the final one;
+// out [T][H] is each position's layer output, ids [T][k] its route.
+int k3xr_official_layer(const k3xr_kda_weights* kw, const k3xr_moe_layer* mw,
+                        const std::uint16_t* self_residual_norm, const std::uint16_t* self_residual_proj,
+                        const std::uint16_t* input_norm, const std::uint16_t* moe_residual_norm,
+                        const std::uint16_t* moe_residual_proj, const std::uint16_t* post_norm, float eps,
+                        const float* hidden_in, const float* block, std::size_t T, std::uint16_t* conv_q,
+                        std::uint16_t* conv_k, std::uint16_t* conv_v, float* recurrent, float* out,
+                        std::uint32_t* ids) {
+    const std::size_t H = kw->hidden, h = kw->heads, d = kw->head_dim, P = h * d, W = kw->conv_width;
+    if (!mw->latent || mw->activation != 0 || mw->hidden != H) return static_cast<int>(ErrorCode::invalid_state);
+    auto mat = [](const std::uint16_t* p, std::size_t rows, std::size_t cols) {
+        return k3x::Bf16WeightView{{p, rows * cols}, rows, cols, 0};
+    };
+    std::vector<k3x::OfficialExpertView> experts;
+    k3x::OfficialLayerWeights w{
+        {w16(self_residual_norm, H), 11}, {w16(self_residual_proj, H), 1, H, 12}, {w16(input_norm, H), 13},
+        k3x::OfficialKdaWeightsView{
+            mat(kw->q_proj, P, H), mat(kw->k_proj, P, H), mat(kw->v_proj, P, H),
+            {kw->q_conv, P * W}, {kw->k_conv, P * W}, {kw->v_conv, P * W},
+            mat(kw->f_a_proj, d, H), mat(kw->f_b_proj, P, d), {kw->a_log, d}, {kw->dt_bias, P},
+            mat(kw->b_proj, h, H), mat(kw->g_proj, P, H), {kw->o_norm, d}, mat(kw->o_proj, H, P)},
+        official_moe_weights(*mw, moe_residual_norm, moe_residual_proj, post_norm, experts)};
+    const k3x::OfficialKdaConfig config{H, h, d, W, eps, kw->gate_lower_bound};
+    const std::size_t hist = (W - 1) * P;
+    const k3x::OfficialKdaState state{std::vector<std::uint16_t>(conv_q, conv_q + hist),
+                                      std::vector<std::uint16_t>(conv_k, conv_k + hist),
+                                      std::vector<std::uint16_t>(conv_v, conv_v + hist),
+                                      std::vector<float>(recurrent, recurrent + h * d * d)};
+    std::vector<k3x::OfficialLayerInput> inputs(T);
+    for (std::size_t t = 0; t < T; ++t)
+        inputs[t] = {std::vector<float>(hidden_in + t * H, hidden_in + (t + 1) * H),
+                     std::vector<float>(block + t * H, block + (t + 1) * H)};
+    auto r = k3x::official_layer_cpu(inputs, w, state, config, mw->top_k, 0x1p64F, std::nullopt);
+    if (!r) return code(r);
+    for (std::size_t t = 0; t < T; ++t) {
+        const auto& step = r.value().steps[t];
+        std::copy(step.moe.output.begin(), step.moe.output.end(), out + t * H);
+        std::copy(step.route.expert_ids.begin(), step.route.expert_ids.end(), ids + t * mw->top_k);
+    }
+    const auto& s2 = r.value().kda.state;
+    std::copy(s2.conv_q.begin(), s2.conv_q.end(), conv_q);
+    std::copy(s2.conv_k.begin(), s2.conv_k.end(), conv_k);
+    std::copy(s2.conv_v.begin(), s2.conv_v.end(), conv_v);
+    std::copy(s2.recurrent_v_first.begin(), s2.recurrent_v_first.end(), recurrent);
     return 0;
 }
 

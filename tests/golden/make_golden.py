@@ -19,7 +19,7 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path[:0] = [os.path.join(ROOT, "oracle")]
 
 from oracle import (ROUTING_ADAPTIVE, ROUTING_FIXED, ROUTING_NATURAL, Reference, Restatement,  # noqa: E402
-                    bf16_normal, bf16_words, make_kda_weights, make_moe_layer)
+                    bf16_normal, bf16_words, make_kda_weights, make_layer, make_moe_layer)
 
 MOE = dict(hidden=256, inter=128, experts=8, top_k=2, shared_inter=128)
 KDA = dict(hidden=256, heads=2, head_dim=64, conv_width=4, tokens=5)
@@ -110,6 +110,27 @@ def kda_block(ref):
     dims = {f"dim_{k}": v for k, v in w.items() if not isinstance(v, np.ndarray)}
     save("kda_block.npz", x=x, conv_q=conv[0], conv_k=conv[1], conv_v=conv[2], recurrent=rec, out=out,
          next_conv_q=cq, next_conv_k=ck, next_conv_v=cv, next_recurrent=r.reshape(rec.shape), **arrays, **dims)
+
+
+def official_layer(ref, rs):
+    """official_layer_cpu (official_layer.cpp:134-244) with LatentMoE over
+    5 positions from a non-zero KDA state (one epsilon for every norm, as
+    the reference's OfficialKdaConfig has)."""
+    g = np.random.default_rng(1013)
+    H, h, d, T, W = 256, 2, 64, 5, 4
+    layer = make_layer(rs, 1014, H, h, d, 8, 2, 128, 128, latent=128)
+    layer["moe"]["latent_eps"] = layer["kda"]["eps"] = layer["rms_eps"]
+    hidden, block = bf16_normal(g, (T, H)), bf16_normal(g, (T, H))
+    conv = [bf16_words(g.normal(0, 0.5, size=(W - 1) * h * d)) for _ in range(3)]
+    rec = g.normal(0, 0.05, size=h * d * d).astype(np.float32)
+    out, ids, (cq, ck, cv, r) = ref.official_layer(layer, hidden, block, conv, rec)
+    arrays = {f"norm_{k}": layer[k] for k in ("self_residual_norm", "self_residual_proj", "input_norm",
+                                              "moe_residual_norm", "moe_residual_proj", "post_norm")}
+    arrays.update({f"kda_{k}": v for k, v in layer["kda"].items()})
+    arrays.update({f"moe_{k}": v for k, v in layer["moe"].items()})
+    save("official_layer.npz", rms_eps=layer["rms_eps"], hidden=hidden, block=block, conv_q=conv[0], conv_k=conv[1],
+         conv_v=conv[2], recurrent=rec, out=out, ids=ids, next_conv_q=cq, next_conv_k=ck, next_conv_v=cv,
+         next_recurrent=r, **arrays)
 
 
 def kda_kat_inputs():
@@ -251,6 +272,7 @@ def main():
     latent_moe(ref, rs)
     kda_block(ref)
     kda_kat(ref)
+    official_layer(ref, rs)
     prepare_input(ref)
     select_routing(ref)
     verify_greedy(ref)

@@ -46,6 +46,26 @@ def latent_moe():
     return layer, f
 
 
+def official_layer():
+    """(layer dict in make_layer's form with a LatentMoE, fixture dict)."""
+    f = load("official_layer.npz")
+    layer = {k[5:]: f[k] for k in f if k.startswith("norm_")}
+    layer["rms_eps"] = float(f["rms_eps"])
+    kda = {k[4:]: _scalar(f[k]) for k in f if k.startswith("kda_")}
+    moe = {k[4:]: _scalar(f[k]) for k in f if k.startswith("moe_")}
+    for k in ("hidden", "heads", "head_dim", "conv_width"):
+        kda[k] = int(kda[k])
+    for k in ("eps", "gate_lower_bound"):
+        kda[k] = float(kda[k])
+    for k in ("hidden", "inter", "experts", "top_k", "shared_inter", "activation", "latent"):
+        moe[k] = int(moe[k])
+    for k in ("situ_beta", "situ_linear_beta", "latent_eps"):
+        moe[k] = float(moe[k])
+    layer["kda"], layer["moe"] = kda, moe
+    layer["hidden"] = kda["hidden"]
+    return layer, f
+
+
 def kda_block():
     """(weights dict in make_kda_weights's form, fixture dict)."""
     f = load("kda_block.npz")

@@ -133,3 +133,18 @@ def test_kda_known_answer(rs):
     np.testing.assert_array_equal(np.concatenate([o1, o2]), out)
     for a, b in zip(s2, (cq, ck, cv, r)):
         np.testing.assert_array_equal(a, b)
+
+
+def test_official_layer_latent(rs):
+    """The restated layer composition with LatentMoE against the reference's
+    official_layer_cpu output, routes and final KDA state."""
+    layer, f = gu.official_layer()
+    T = f["hidden"].shape[0]
+    parent = np.arange(-1, T - 1)
+    conv = (f["conv_q"], f["conv_k"], f["conv_v"])
+    out, ids, _, xin = rs.layer_forward(layer, f["hidden"], f["block"], parent, conv, f["recurrent"], want_xin=True)
+    np.testing.assert_array_equal(ids, f["ids"])
+    np.testing.assert_array_equal(out, f["out"])
+    state = rs.kda_block_commit(layer["kda"], xin, parent, T - 1, conv, f["recurrent"])
+    for a, key in zip(state, ("next_conv_q", "next_conv_k", "next_conv_v", "next_recurrent")):
+        np.testing.assert_array_equal(a, f[key])

@@ -92,3 +92,50 @@ def test_latent_moe_ep_world_of_one_equals_layer(rs):
         ctx.ep_finalize()
     finally:
         ctx.close()
+
+
+def test_official_layer_latent_golden(rs):
+    """k3xb_layer_forward with a LatentMoE layer against the reference's
+    official_layer_cpu (golden fixture): the attention residuals, the KDA
+    block, the latent MoE and the residual, on a chain of 5 positions; the
+    committed state after the last position against the reference's final
+    KDA state. Routes may differ where the FP32 projections move a score by
+    an ulp, so outputs are compared where the routes agree (at least 4 of
+    5 positions)."""
+    import k3xb
+    torch = torch_cuda()
+    layer, f = gu.official_layer()
+    T, H = f["hidden"].shape
+    P = layer["kda"]["heads"] * layer["kda"]["head_dim"]
+    dl = dict(layer)
+    dl["kda"] = {k: (to_dev(torch, v) if isinstance(v, np.ndarray) else v) for k, v in layer["kda"].items()}
+    dl["moe"] = layer_to_dev(torch, layer["moe"])
+    for k in ("self_residual_norm", "self_residual_proj", "input_norm", "moe_residual_norm", "moe_residual_proj",
+              "post_norm"):
+        dl[k] = to_dev(torch, layer[k])
+    desc = k3xb.layer_desc(dl)
+    conv = np.stack([f["conv_q"], f["conv_k"], f["conv_v"]])[None]
+    conv_d, rec_d = to_dev(torch, conv), to_dev(torch, f["recurrent"].reshape(1, -1))
+    parent = list(range(-1, T - 1))
+    ctx = k3xb.Context(0)
+    ctx.use_stream()
+    try:
+        out = torch.empty((1, T, H), dtype=torch.float32, device="cuda")
+        ids = torch.empty((T, layer["moe"]["top_k"]), dtype=torch.int32, device="cuda")
+        trace = torch.empty(ctx.kda_trace_bytes(desc.kda, T, 1), dtype=torch.uint8, device="cuda")
+        ctx.layer_forward(desc, to_dev(torch, f["hidden"][None]), to_dev(torch, f["block"][None]), parent, conv_d,
+                          rec_d, out, ids, trace)
+        conv_o, rec_o = torch.empty_like(conv_d), torch.empty_like(rec_d)
+        ctx.kda_block_commit(desc.kda, trace, parent, 1, [T - 1], conv_d, rec_d, conv_o, rec_o)
+        ctx.sync()
+        got, gids = out.cpu().numpy()[0], from_dev(ids, np.uint32)
+    finally:
+        ctx.close()
+    same = np.all(gids == f["ids"], axis=1)
+    assert same.sum() >= T - 1, f"routes agree on {same.sum()}/{T} positions"
+    assert_mostly_close(got[same], f["out"][same], what="official layer output")
+    words = lambda a: (np.asarray(a, np.uint16).astype(np.uint32) << 16).view(np.float32)
+    co = conv_o.cpu().numpy().view(np.uint16)[0]
+    for i, key in enumerate(("next_conv_q", "next_conv_k", "next_conv_v")):
+        assert_mostly_close(words(co[i]), words(f[key]), what=key)
+    assert_mostly_close(rec_o.cpu().numpy()[0], f["next_recurrent"], what="recurrent state")

@@ -499,3 +499,28 @@ def test_latent_moe_matches_reference(rs, ref):
     np.testing.assert_array_equal(ids, want_ids)
     np.testing.assert_array_equal(con, want_con)
     np.testing.assert_array_equal(got, want)
+
+
+def test_official_layer_matches_reference(rs, ref):
+    """The whole official layer with LatentMoE: the restatement's layer
+    composition (attention residual, KDA block, prefix, MoE input, LatentMoE,
+    residual) over a chain of positions equals the reference's own
+    official_layer_cpu (official_layer.cpp:134-244) bit for bit, outputs,
+    routes and the KDA state after the last position."""
+    from oracle import bf16_normal, bf16_words, make_layer
+    g = np.random.default_rng(63)
+    H, h, d, T, W = 256, 2, 64, 4, 4
+    P = h * d
+    layer = make_layer(rs, 64, H, h, d, 16, 4, 128, 128, latent=128)
+    # official_layer_cpu has one epsilon (OfficialKdaConfig::rms_norm_epsilon) for every norm
+    layer["moe"]["latent_eps"] = layer["kda"]["eps"] = layer["rms_eps"]
+    hidden, block = bf16_normal(g, (T, H)), bf16_normal(g, (T, H))
+    conv = tuple(bf16_words(g.normal(0, 0.5, size=(W - 1) * P)) for _ in range(3))
+    rec = g.normal(0, 0.05, size=h * d * d).astype(np.float32)
+    want, want_ids, (wq, wk, wv, wr) = ref.official_layer(layer, hidden, block, conv, rec)
+    got, ids, _, xin = rs.layer_forward(layer, hidden, block, np.arange(-1, T - 1), conv, rec, want_xin=True)
+    np.testing.assert_array_equal(ids, want_ids)
+    np.testing.assert_array_equal(got, want)
+    cq, ck, cv, r = rs.kda_block_commit(layer["kda"], xin, np.arange(-1, T - 1), T - 1, conv, rec)
+    for a, b in ((cq, wq), (ck, wk), (cv, wv), (r, wr)):
+        np.testing.assert_array_equal(a, b)
