@@ -483,6 +483,8 @@ class Reference:
         L.k3xr_select_routing.argtypes = _SELECT_ROUTING_ARGS
         L.k3xr_official_moe.argtypes = [C.c_void_p, _f32p, _f32p, _u16p, _u16p, _u16p, C.c_float, _sz, _f32p,
                                         _u32p, _f32p]
+        L.k3xr_official_two_layer.argtypes = [C.c_void_p] * 2 + [C.c_void_p, C.c_float, _f32p, _f32p] + \
+            [C.c_void_p] * 4 + [_f32p]
         L.k3xr_official_layer.argtypes = [C.c_void_p, C.c_void_p, _u16p, _u16p, _u16p, _u16p, _u16p, _u16p,
                                           C.c_float, _f32p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p, _f32p, _u32p]
 
@@ -639,6 +641,27 @@ class Reference:
         if st:
             raise OracleError(st, "ref official_layer_cpu")
         return out, ids, (cq, ck, cv, rec)
+
+    def official_two_layer(self, layers, hidden_in, block, convs, recs):
+        """official_two_layer_cpu over its two positions: (out [2][H], final
+        states per layer as (conv_q, conv_k, conv_v, recurrent))."""
+        structs = [(kda_struct(L["kda"]), moe_struct(L["moe"])) for L in layers]
+        kws = (C.c_void_p * 2)(*[C.cast(C.pointer(k[0]), C.c_void_p) for k, _ in structs])
+        mws = (C.c_void_p * 2)(*[C.cast(C.pointer(m[0]), C.c_void_p) for _, m in structs])
+        names = ("self_residual_norm", "self_residual_proj", "input_norm", "moe_residual_norm",
+                 "moe_residual_proj", "post_norm")
+        norm_arrays = [[_c(L[k], np.uint16) for k in names] for L in layers]
+        norms = ((C.c_void_p * 6) * 2)(*[(C.c_void_p * 6)(*[a.ctypes.data for a in row]) for row in norm_arrays])
+        states = [[np.array(a, np.uint16, copy=True) for a in conv] + [np.array(r, np.float32, copy=True)]
+                  for conv, r in zip(convs, recs)]
+        ptrs = [(C.c_void_p * 2)(*[states[l][i].ctypes.data for l in range(2)]) for i in range(4)]
+        hidden_in, block = _c(hidden_in, np.float32), _c(block, np.float32)
+        out = np.zeros_like(hidden_in)
+        st = self.lib.k3xr_official_two_layer(kws, mws, norms, layers[0]["rms_eps"], hidden_in, block, *ptrs, out)
+        del structs, norm_arrays
+        if st:
+            raise OracleError(st, "ref official_two_layer_cpu")
+        return out, [tuple(s) for s in states]
 
     def prepare_input(self, prefix, block, norm, proj, post, eps):
         out = np.empty(len(prefix), np.float32)

@@ -2,8 +2,8 @@
 //
 // TEST INFRASTRUCTURE ONLY. oracle/Makefile compiles this file together with
 // the reference's unmodified sources (runtime/src/{ops,official_moe,
-// official_kda,official_layer,expert_major,speculative,routing_policy,
-// profile}.cpp, read in place from the reference checkout) into
+// official_kda,official_layer,official_two_layer,expert_major,speculative,
+// routing_policy,profile}.cpp, read in place from the reference checkout) into
 // oracle/_ref/libk3x_ref.so. Tests use it to pin the C restatement
 // (k3x_oracle.c); bench.py uses it as the timed CPU reference arm. Nothing
 // here is reference source: every function below only marshals plain C
@@ -11,6 +11,7 @@
 #include "k3x/expert_major.hpp"
 #include "k3x/official_kda.hpp"
 #include "k3x/official_layer.hpp"
+#include "k3x/official_two_layer.hpp"
 #include "k3x/official_moe.hpp"
 #include "k3x/routing_policy.hpp"
 #include "k3x/ops.hpp"
@@ -472,6 +473,34 @@ int k3xr_official_kda_cpu(const k3xr_kda_weights* w, const float* hidden,
 // official_moe_cpu with LatentMoE) for T positions of one sequence. The
 // KDA state arrays hold the initial state and receive the final one;
 // out [T][H] is each position's layer output, ids [T][k] its route.
+}  // extern "C"
+
+namespace {
+
+// The reference's OfficialLayerWeights over one layer's arrays; `norms`
+// are self_residual_norm, self_residual_proj, input_norm,
+// moe_residual_norm, moe_residual_proj, post_norm ([H] bf16 words each).
+k3x::OfficialLayerWeights official_layer_weights(const k3xr_kda_weights& kw, const k3xr_moe_layer& mw,
+                                                 const std::uint16_t* const norms[6],
+                                                 std::vector<k3x::OfficialExpertView>& experts) {
+    const std::size_t H = kw.hidden, h = kw.heads, d = kw.head_dim, P = h * d, W = kw.conv_width;
+    auto mat = [](const std::uint16_t* p, std::size_t rows, std::size_t cols) {
+        return k3x::Bf16WeightView{{p, rows * cols}, rows, cols, 0};
+    };
+    return k3x::OfficialLayerWeights{
+        {w16(norms[0], H), 11}, {w16(norms[1], H), 1, H, 12}, {w16(norms[2], H), 13},
+        k3x::OfficialKdaWeightsView{
+            mat(kw.q_proj, P, H), mat(kw.k_proj, P, H), mat(kw.v_proj, P, H),
+            {kw.q_conv, P * W}, {kw.k_conv, P * W}, {kw.v_conv, P * W},
+            mat(kw.f_a_proj, d, H), mat(kw.f_b_proj, P, d), {kw.a_log, d}, {kw.dt_bias, P},
+            mat(kw.b_proj, h, H), mat(kw.g_proj, P, H), {kw.o_norm, d}, mat(kw.o_proj, H, P)},
+        official_moe_weights(mw, norms[3], norms[4], norms[5], experts)};
+}
+
+}  // namespace
+
+extern "C" {
+
 int k3xr_official_layer(const k3xr_kda_weights* kw, const k3xr_moe_layer* mw,
                         const std::uint16_t* self_residual_norm, const std::uint16_t* self_residual_proj,
                         const std::uint16_t* input_norm, const std::uint16_t* moe_residual_norm,
@@ -481,18 +510,10 @@ int k3xr_official_layer(const k3xr_kda_weights* kw, const k3xr_moe_layer* mw,
                         std::uint32_t* ids) {
     const std::size_t H = kw->hidden, h = kw->heads, d = kw->head_dim, P = h * d, W = kw->conv_width;
     if (!mw->latent || mw->activation != 0 || mw->hidden != H) return static_cast<int>(ErrorCode::invalid_state);
-    auto mat = [](const std::uint16_t* p, std::size_t rows, std::size_t cols) {
-        return k3x::Bf16WeightView{{p, rows * cols}, rows, cols, 0};
-    };
     std::vector<k3x::OfficialExpertView> experts;
-    k3x::OfficialLayerWeights w{
-        {w16(self_residual_norm, H), 11}, {w16(self_residual_proj, H), 1, H, 12}, {w16(input_norm, H), 13},
-        k3x::OfficialKdaWeightsView{
-            mat(kw->q_proj, P, H), mat(kw->k_proj, P, H), mat(kw->v_proj, P, H),
-            {kw->q_conv, P * W}, {kw->k_conv, P * W}, {kw->v_conv, P * W},
-            mat(kw->f_a_proj, d, H), mat(kw->f_b_proj, P, d), {kw->a_log, d}, {kw->dt_bias, P},
-            mat(kw->b_proj, h, H), mat(kw->g_proj, P, H), {kw->o_norm, d}, mat(kw->o_proj, H, P)},
-        official_moe_weights(*mw, moe_residual_norm, moe_residual_proj, post_norm, experts)};
+    const std::uint16_t* const norms[6] = {self_residual_norm, self_residual_proj, input_norm,
+                                           moe_residual_norm,  moe_residual_proj,  post_norm};
+    const k3x::OfficialLayerWeights w = official_layer_weights(*kw, *mw, norms, experts);
     const k3x::OfficialKdaConfig config{H, h, d, W, eps, kw->gate_lower_bound};
     const std::size_t hist = (W - 1) * P;
     const k3x::OfficialKdaState state{std::vector<std::uint16_t>(conv_q, conv_q + hist),
@@ -515,6 +536,47 @@ int k3xr_official_layer(const k3xr_kda_weights* kw, const k3xr_moe_layer* mw,
     std::copy(s2.conv_k.begin(), s2.conv_k.end(), conv_k);
     std::copy(s2.conv_v.begin(), s2.conv_v.end(), conv_v);
     std::copy(s2.recurrent_v_first.begin(), s2.recurrent_v_first.end(), recurrent);
+    return 0;
+}
+
+// official_two_layer_cpu itself (official_two_layer.cpp:16-70): two
+// positions, position-major through layers 1 and 2, each layer with its own
+// KDA state, the block source unchanged between layers. Per layer l:
+// kw[l], mw[l], norms[l][6] as for k3xr_official_layer; conv_*[l] and
+// recurrent[l] hold the initial state and receive the final one. out [2][H].
+int k3xr_official_two_layer(const k3xr_kda_weights* const kw[2], const k3xr_moe_layer* const mw[2],
+                            const std::uint16_t* const norms[2][6], float eps, const float* hidden_in,
+                            const float* block, std::uint16_t* const conv_q[2], std::uint16_t* const conv_k[2],
+                            std::uint16_t* const conv_v[2], float* const recurrent[2], float* out) {
+    const std::size_t H = kw[0]->hidden, h = kw[0]->heads, d = kw[0]->head_dim, P = h * d, W = kw[0]->conv_width;
+    std::vector<k3x::OfficialExpertView> experts[2];
+    std::vector<k3x::OfficialTwoLayerWeights> layers;
+    std::vector<k3x::OfficialKdaState> states;
+    const std::size_t hist = (W - 1) * P;
+    for (int l = 0; l < 2; ++l) {
+        if (!mw[l]->latent || mw[l]->activation != 0 || kw[l]->hidden != H || mw[l]->top_k != mw[0]->top_k)
+            return static_cast<int>(ErrorCode::invalid_state);
+        layers.push_back({static_cast<std::uint32_t>(l + 1), official_layer_weights(*kw[l], *mw[l], norms[l], experts[l])});
+        states.push_back({std::vector<std::uint16_t>(conv_q[l], conv_q[l] + hist),
+                          std::vector<std::uint16_t>(conv_k[l], conv_k[l] + hist),
+                          std::vector<std::uint16_t>(conv_v[l], conv_v[l] + hist),
+                          std::vector<float>(recurrent[l], recurrent[l] + h * d * d)});
+    }
+    std::vector<k3x::OfficialLayerInput> inputs(2);
+    for (std::size_t t = 0; t < 2; ++t)
+        inputs[t] = {std::vector<float>(hidden_in + t * H, hidden_in + (t + 1) * H),
+                     std::vector<float>(block + t * H, block + (t + 1) * H)};
+    const k3x::OfficialKdaConfig config{H, h, d, W, eps, kw[0]->gate_lower_bound};
+    auto r = k3x::official_two_layer_cpu(inputs, layers, states, config, mw[0]->top_k, 0x1p64F, std::nullopt);
+    if (!r) return code(r);
+    for (std::size_t t = 0; t < 2; ++t) std::copy(r.value().outputs[t].begin(), r.value().outputs[t].end(), out + t * H);
+    for (int l = 0; l < 2; ++l) {
+        const auto& s = r.value().final_states[l];
+        std::copy(s.conv_q.begin(), s.conv_q.end(), conv_q[l]);
+        std::copy(s.conv_k.begin(), s.conv_k.end(), conv_k[l]);
+        std::copy(s.conv_v.begin(), s.conv_v.end(), conv_v[l]);
+        std::copy(s.recurrent_v_first.begin(), s.recurrent_v_first.end(), recurrent[l]);
+    }
     return 0;
 }
 

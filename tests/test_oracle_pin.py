@@ -524,3 +524,28 @@ def test_official_layer_matches_reference(rs, ref):
     cq, ck, cv, r = rs.kda_block_commit(layer["kda"], xin, np.arange(-1, T - 1), T - 1, conv, rec)
     for a, b in ((cq, wq), (ck, wk), (cv, wv), (r, wr)):
         np.testing.assert_array_equal(a, b)
+
+
+def test_two_layer_stack_matches_reference(rs, ref):
+    """Layer stacking: the restatement run layer-major (layer 1 over both
+    positions, then layer 2 over layer 1's outputs with the same block
+    source) equals the reference's official_two_layer_cpu, which runs
+    position-major, bit for bit, outputs and both layers' final KDA states."""
+    from oracle import bf16_normal, bf16_words, make_layer
+    g = np.random.default_rng(65)
+    H, h, d, W = 256, 2, 64, 4
+    layers = [make_layer(rs, 66 + l, H, h, d, 16, 4, 128, 128, latent=128) for l in range(2)]
+    for L in layers:
+        L["moe"]["latent_eps"] = L["kda"]["eps"] = L["rms_eps"]
+    hidden, block = bf16_normal(g, (2, H)), bf16_normal(g, (2, H))
+    convs = [tuple(bf16_words(g.normal(0, 0.5, size=(W - 1) * h * d)) for _ in range(3)) for _ in range(2)]
+    recs = [g.normal(0, 0.05, size=h * d * d).astype(np.float32) for _ in range(2)]
+    want, want_states = ref.official_two_layer(layers, hidden, block, convs, recs)
+    x, parent = hidden, np.arange(-1, 1)
+    for l, L in enumerate(layers):
+        out, _, _, xin = rs.layer_forward(L, x, block, parent, convs[l], recs[l], want_xin=True)
+        state = rs.kda_block_commit(L["kda"], xin, parent, 1, convs[l], recs[l])
+        for a, b in zip(state, want_states[l]):
+            np.testing.assert_array_equal(a, b)
+        x = out
+    np.testing.assert_array_equal(x, want)
