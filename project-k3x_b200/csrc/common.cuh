@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <string>
 
@@ -55,6 +56,17 @@ int ensure_io(k3xb_ctx* ctx, size_t bytes, void** out);
         if (k3xb_err_ != cudaSuccess) return k3xb::cuda_fail((ctx), k3xb_err_, "kernel launch"); \
         ++(ctx)->stats.kernel_launches;                             \
     } while (0)
+
+// Function attributes (cudaFuncSetAttribute) belong to a device: `set` runs
+// once per device id, recorded in `done` (device ids below 64).
+template <typename F>
+int configure_once(k3xb_ctx* ctx, std::atomic<uint64_t>& done, F&& set) {
+    const uint64_t bit = 1ull << (static_cast<unsigned>(ctx->device) & 63u);
+    if (done.load(std::memory_order_acquire) & bit) return K3XB_OK;
+    const int st = set();
+    if (st == K3XB_OK) done.fetch_or(bit, std::memory_order_acq_rel);
+    return st;
+}
 
 // Carves aligned sub-buffers out of one scratch allocation.
 struct Carver {

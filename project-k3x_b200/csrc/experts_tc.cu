@@ -588,14 +588,15 @@ int launch_routed(k3xb_ctx* ctx, const CUtensorMap& map_gate, const CUtensorMap&
     using RC = RoutedCfg<NM>;
     const size_t smem_gu = tcp::smem_bytes<RC::kStagesGU, 2, NM>();
     const size_t smem_d = tcp::smem_bytes<RC::kStagesGU, 2, NM>();
-    static bool configured = false;   // per template instance
-    if (!configured) {
+    static std::atomic<uint64_t> configured{0};   // per template instance
+    const int cst = configure_once(ctx, configured, [&]() -> int {
         K3XB_CUDA(ctx, cudaFuncSetAttribute(gateup_kernel<NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             static_cast<int>(smem_gu)));
         K3XB_CUDA(ctx, cudaFuncSetAttribute(down_kernel<NM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             static_cast<int>(smem_d)));
-        configured = true;
-    }
+        return K3XB_OK;
+    });
+    if (cst) return cst;
     {
         PhaseScope ph(ctx, K3XB_PHASE_EXPERT_GATEUP);
         gateup_kernel<NM><<<ctx->sm_count, kThreads, smem_gu, ctx->stream>>>(map_gate, map_up, map_bgu, gp);

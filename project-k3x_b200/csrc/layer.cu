@@ -309,12 +309,13 @@ int launch_attnres_norm(k3xb_ctx* ctx, const float* a, const float* delta, const
                         float* prefix_out, float* out) {
     const size_t smem = attnres_smem_bytes(H);
     if (smem > 200 * 1024) return fail(ctx, K3XB_INVALID_EXTENT, "attention residual: hidden too large");
-    static bool configured = false;
-    if (!configured) {
+    static std::atomic<uint64_t> configured{0};
+    const int cst = configure_once(ctx, configured, [&]() -> int {
         K3XB_CUDA(ctx, cudaFuncSetAttribute(attnres_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             200 * 1024));
-        configured = true;
-    }
+        return K3XB_OK;
+    });
+    if (cst) return cst;
     attnres_norm_kernel<<<T, 256, smem, ctx->stream>>>(a, delta, block, rnorm, rproj, post, H, eps, prefix_out, out);
     K3XB_LAUNCHED(ctx);
     return K3XB_OK;

@@ -101,13 +101,14 @@ int launch_linear_terms(k3xb_ctx* ctx, const uint16_t* xterms, uint32_t terms, c
     if ((st = make_byte_map(ctx, &map_x, xterms, static_cast<uint64_t>(K) * 2, static_cast<uint64_t>(terms) * T,
                             kTileRows)))
         return st;
-    static bool configured = false;
+    static std::atomic<uint64_t> configured{0};
     const size_t smem = tcp::smem_bytes<kStages, 1>();
-    if (!configured) {
+    const int cst = configure_once(ctx, configured, [&]() -> int {
         K3XB_CUDA(ctx, cudaFuncSetAttribute(linear_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             static_cast<int>(smem)));
-        configured = true;
-    }
+        return K3XB_OK;
+    });
+    if (cst) return cst;
     const uint32_t tpt = kTileRows / terms;
     const uint32_t items = ((T + tpt - 1) / tpt) * ((rows + kBlockM - 1) / kBlockM);
     LinParams p{T, rows, K, items, static_cast<uint32_t>(round_out ? 1 : 0), terms, out, ctx->status_word};

@@ -571,16 +571,17 @@ int launch_router_logits(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_
         CUtensorMap map;
         int st = make_byte_map(ctx, &map, W, static_cast<uint64_t>(H) * 2, E, 128);
         if (st) return st;
-        static bool tma_configured = false;
-        if (!tma_configured) {
+        static std::atomic<uint64_t> tma_configured{0};
+        st = configure_once(ctx, tma_configured, [&]() -> int {
             K3XB_CUDA(ctx, cudaFuncSetAttribute(router_tma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 static_cast<int>(kRtSmemMax)));
             K3XB_CUDA(ctx, cudaFuncSetAttribute(router_tma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 static_cast<int>(kRtSmemMax)));
             K3XB_CUDA(ctx, cudaFuncSetAttribute(router_tma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 static_cast<int>(kRtSmemMax)));
-            tma_configured = true;
-        }
+            return K3XB_OK;
+        });
+        if (st) return st;
         const dim3 grid((E + 127) / 128, (T + tw - 1) / tw);
         const size_t smem = rt_smem_bytes(H, tw);
         int* err = ctx->status_word;
@@ -590,12 +591,13 @@ int launch_router_logits(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_
         K3XB_LAUNCHED(ctx);
         return K3XB_OK;
     }
-    static bool configured = false;
-    if (!configured) {
+    static std::atomic<uint64_t> configured{0};
+    const int cst = configure_once(ctx, configured, [&]() -> int {
         K3XB_CUDA(ctx, cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             static_cast<int>(kLogitsSmem)));
-        configured = true;
-    }
+        return K3XB_OK;
+    });
+    if (cst) return cst;
     dim3 grid((E + kExp - 1) / kExp, (T + kTokCta - 1) / kTokCta);
     router_logits_kernel<<<grid, 128, kLogitsSmem, ctx->stream>>>(hidden, W, T, H, E, logits);
     K3XB_LAUNCHED(ctx);
@@ -628,12 +630,12 @@ int launch_plan(k3xb_ctx* ctx, const uint32_t* ids, const float* contrib, uint32
     const size_t smem = plan_smem_bytes(T, E);
     if (smem > 200 * 1024)
         return fail(ctx, K3XB_INVALID_EXTENT, "expert-major plan: experts * ceil(tokens/32) too large");
-    static bool configured = false;
-    if (!configured) {
-        K3XB_CUDA(ctx, cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            200 * 1024));
-        configured = true;
-    }
+    static std::atomic<uint64_t> configured{0};
+    const int cst = configure_once(ctx, configured, [&]() -> int {
+        K3XB_CUDA(ctx, cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        return K3XB_OK;
+    });
+    if (cst) return cst;
     plan_kernel<<<1, 1024, smem, ctx->stream>>>(ids, contrib, T, K, E, plan);
     K3XB_LAUNCHED(ctx);
     return K3XB_OK;
