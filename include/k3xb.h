@@ -5,7 +5,9 @@
  * Plain pointers and sizes only. Every array argument is DEVICE memory on
  * the context's GPU and the call is asynchronous on the context's current
  * stream (k3xb_set_stream), except where a name ends in _host and for the
- * resident-weight uploads (k3xb_acquire_*), which read HOST arrays. All
+ * resident-weight uploads (k3xb_acquire_*), which read HOST arrays. A call
+ * makes the context's GPU the calling thread's current device; a context is
+ * used by one thread at a time. All
  * entry points return a status that mirrors k3x::ErrorCode
  * (runtime/include/k3x/status.hpp:9-30); k3xb_last_error() gives the
  * message of the last failure on a context. There is no CPU fallback: a

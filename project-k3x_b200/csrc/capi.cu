@@ -294,13 +294,13 @@ int k3xb_last_error(const k3xb_ctx* ctx, char* buf, size_t len) {
 }
 
 int k3xb_set_stream(k3xb_ctx* ctx, void* stream) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
     return K3XB_OK;
 }
 
 int k3xb_sync(k3xb_ctx* ctx) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     K3XB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     int32_t st = 0;
     K3XB_CUDA(ctx, cudaMemcpy(&st, ctx->status_word, sizeof st, cudaMemcpyDeviceToHost));
@@ -321,7 +321,7 @@ int k3xb_get_stats(const k3xb_ctx* ctx, k3xb_stats* out) {
 int k3xb_route(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_t H, const uint16_t* router,
                const float* correction, uint32_t E, uint32_t K, uint32_t* ids, float* contrib,
                float* scores) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!T || !H || !E || !K || K > E || !hidden || !router || !correction || !ids || !contrib)
         return fail(ctx, K3XB_INVALID_EXTENT, "route arguments");
     void* base;
@@ -341,7 +341,7 @@ int k3xb_route(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_t H, const
 int k3xb_select_routing(k3xb_ctx* ctx, const float* scores, uint32_t T, uint32_t E, const float* bias, uint32_t K,
                         const k3xb_routing_policy* policy, uint32_t* ids, float* weights, uint32_t* selected,
                         uint32_t* escalated, float* stats) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!scores || !bias || !policy || !ids || !weights || !selected || !T)
         return fail(ctx, K3XB_INVALID_EXTENT, "select_routing arguments");
     // routing_policy.cpp:38-72
@@ -367,7 +367,7 @@ int k3xb_select_routing(k3xb_ctx* ctx, const float* scores, uint32_t T, uint32_t
 
 int k3xb_expert_major_plan(k3xb_ctx* ctx, const uint32_t* ids, const float* contrib, uint32_t T,
                            uint32_t K, uint32_t E, const k3xb_plan* plan) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!plan || !ids || !contrib) return fail(ctx, K3XB_INVALID_EXTENT, "plan arguments");
     if (!T || !K) return fail(ctx, K3XB_INVALID_EXTENT, "empty routes");   // expert_major.cpp:12-14
     k3xb_plan p = *plan;
@@ -378,7 +378,7 @@ int k3xb_expert_major_plan(k3xb_ctx* ctx, const uint32_t* ids, const float* cont
 
 int k3xb_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const float* hidden, uint32_t T,
                            float* out, uint32_t* ids, float* contrib) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     int st = validate_layer(ctx, layer);
     if (st) return st;
     if (!T || !hidden || !out) return fail(ctx, K3XB_INVALID_EXTENT, "moe forward arguments");
@@ -396,7 +396,7 @@ int k3xb_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const flo
 
 int k3xb_moe_layer_forward_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const float* hidden_host,
                                 uint32_t T, float* out_host, uint32_t* ids_host, float* contrib_host) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     int st = validate_layer(ctx, layer);
     if (st) return st;
     if (!T || !hidden_host || !out_host) return fail(ctx, K3XB_INVALID_EXTENT, "moe forward arguments");
@@ -429,7 +429,7 @@ int k3xb_moe_layer_forward_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer, cons
 
 int k3xb_moe_experts(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const float* hidden, uint32_t T,
                      const k3xb_plan* plan, float* slot_out) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     int st = validate_layer(ctx, layer);
     if (st) return st;
     if (!T || !hidden || !plan || !slot_out) return fail(ctx, K3XB_INVALID_EXTENT, "experts arguments");
@@ -448,7 +448,7 @@ int k3xb_moe_experts(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const float* hi
 
 int k3xb_expert_grid_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const uint32_t* expert_ids, uint32_t n,
                           const float* inputs_host, uint32_t T, float* out_host) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!layer || !expert_ids || !inputs_host || !out_host || !T || !n)
         return fail(ctx, K3XB_INVALID_EXTENT, "expert grid arguments");
     k3xb_moe_layer L = expert_view(*layer);   // inputs are rows of the experts' width
@@ -578,7 +578,7 @@ int kda_common(k3xb_ctx* ctx, const float* state, uint32_t nodes, uint32_t S, ui
 int k3xb_kda_tree(k3xb_ctx* ctx, const float* state, const int32_t* parent, uint32_t nodes,
                   uint32_t S, uint32_t heads, uint32_t head_dim, const float* q, const float* k,
                   const float* v, const float* ld, const float* beta, float* out) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!state || !parent || !nodes || !S || !heads || !q || !k || !v || !ld || !beta || !out)
         return fail(ctx, K3XB_INVALID_EXTENT, "kda_tree arguments");
     KdaSchedule sch;
@@ -591,7 +591,7 @@ int k3xb_kda_tree(k3xb_ctx* ctx, const float* state, const int32_t* parent, uint
 int k3xb_kda_commit(k3xb_ctx* ctx, const float* state, const int32_t* parent, uint32_t nodes, uint32_t S,
                     uint32_t heads, uint32_t head_dim, const float* q, const float* k, const float* v,
                     const float* ld, const float* beta, const int32_t* commit_node, float* state_out) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!state || !parent || !S || !heads || !commit_node || !state_out)
         return fail(ctx, K3XB_INVALID_EXTENT, "kda_commit arguments");
     for (uint32_t i = 0; i < nodes; ++i)
@@ -626,7 +626,7 @@ int k3xb_kda_commit(k3xb_ctx* ctx, const float* state, const int32_t* parent, ui
 int k3xb_accept_greedy(k3xb_ctx* ctx, const float* logits, const uint32_t* drafts, uint32_t S, uint32_t p,
                        uint32_t V, uint32_t* targets, uint32_t* accepted, uint32_t* committed,
                        uint32_t* count) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!logits || (!drafts && p) || !S || !V || !accepted || !committed || !count)
         return fail(ctx, K3XB_INVALID_EXTENT, "accept_greedy arguments");
     uint32_t* t = targets;
@@ -644,7 +644,7 @@ int k3xb_accept_greedy(k3xb_ctx* ctx, const float* logits, const uint32_t* draft
 int k3xb_accept_rejection(k3xb_ctx* ctx, const float* tl, const float* dl, const uint32_t* drafts, uint32_t S,
                           uint32_t p, uint32_t V, float temperature, uint64_t seed, uint64_t seq_base,
                           uint32_t* accepted, uint32_t* committed, uint32_t* count) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!tl || (p && (!dl || !drafts)) || !S || !V || !accepted || !committed || !count)
         return fail(ctx, K3XB_INVALID_EXTENT, "accept_rejection arguments");
     if (!(temperature > 0.0f)) return fail(ctx, K3XB_INVALID_EXTENT, "temperature must be positive");
@@ -664,20 +664,20 @@ int k3xb_accept_rejection(k3xb_ctx* ctx, const float* tl, const float* dl, const
 
 int k3xb_fill_normal_f32(k3xb_ctx* ctx, float* out, size_t n, uint64_t seed, uint64_t stream, float mean,
                          float sigma) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!out || !n) return fail(ctx, K3XB_INVALID_EXTENT, "fill arguments");
     return launch_fill_normal_f32(ctx, out, n, seed, stream, mean, sigma);
 }
 
 int k3xb_fill_normal_bf16(k3xb_ctx* ctx, uint16_t* out, size_t n, uint64_t seed, uint64_t stream, float sigma) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!out || !n) return fail(ctx, K3XB_INVALID_EXTENT, "fill arguments");
     return launch_fill_normal_bf16(ctx, out, n, seed, stream, sigma);
 }
 
 int k3xb_quantize_mxfp4(k3xb_ctx* ctx, const float* x, size_t rows, size_t cols, uint8_t* packed,
                         uint8_t* scales) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!x || !packed || !scales || !rows || !cols || cols % 32)
         return fail(ctx, K3XB_INVALID_MXFP4, "quantize arguments (cols % 32 == 0)");
     return launch_quantize_mxfp4(ctx, x, rows, cols, packed, scales);
@@ -685,7 +685,7 @@ int k3xb_quantize_mxfp4(k3xb_ctx* ctx, const float* x, size_t rows, size_t cols,
 
 int k3xb_linear_bf16(k3xb_ctx* ctx, const float* x, uint32_t tokens, uint32_t in_features, const uint16_t* weight,
                      uint32_t out_features, int32_t round_output, float* out) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!x || !weight || !out || !tokens || !in_features || !out_features)
         return fail(ctx, K3XB_INVALID_EXTENT, "linear arguments");
     void* base;
@@ -696,13 +696,13 @@ int k3xb_linear_bf16(k3xb_ctx* ctx, const float* x, uint32_t tokens, uint32_t in
 }
 
 int k3xb_prepare_mxfp4_scales(k3xb_ctx* ctx, const uint8_t* scales, size_t rows, size_t cols, uint8_t* out) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     return prepare_mxfp4_scales(ctx, scales, rows, cols, out);
 }
 
 int k3xb_fill_normal_mxfp4(k3xb_ctx* ctx, uint8_t* packed, uint8_t* scales, size_t rows, size_t cols,
                            uint64_t seed, uint64_t stream, float sigma) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!packed || !scales || !rows || !cols || cols % 32)
         return fail(ctx, K3XB_INVALID_MXFP4, "fill arguments (cols % 32 == 0)");
     return launch_fill_normal_mxfp4(ctx, packed, scales, rows, cols, seed, stream, sigma);
@@ -938,7 +938,7 @@ size_t k3xb_kda_trace_bytes(const k3xb_kda_layer* w, uint32_t nodes, uint32_t S)
 
 int k3xb_kda_block(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t H, const float* x, const int32_t* parent,
                    uint32_t N, uint32_t S, const uint16_t* conv, const float* rec, float* out, void* trace) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     int st = validate_kda(ctx, w, H);
     if (st) return st;
     if (!x || !parent || !N || !S || !conv || !rec || !out) return fail(ctx, K3XB_INVALID_EXTENT, "kda_block arguments");
@@ -969,7 +969,7 @@ int k3xb_kda_block(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t H, const flo
 int k3xb_kda_block_commit(k3xb_ctx* ctx, const k3xb_kda_layer* w, const void* trace, const int32_t* parent,
                           uint32_t N, uint32_t S, const int32_t* commit_node, const uint16_t* conv, const float* rec,
                           uint16_t* conv_out, float* rec_out) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!w || !trace || !parent || !N || !S || !commit_node || !conv || !rec || !conv_out || !rec_out)
         return fail(ctx, K3XB_INVALID_EXTENT, "kda_block_commit arguments");
     if (rec_out == rec) return fail(ctx, K3XB_INVALID_EXTENT, "recurrent_out must not alias recurrent");
@@ -1017,7 +1017,7 @@ int k3xb_kda_block_commit(k3xb_ctx* ctx, const k3xb_kda_layer* w, const void* tr
 
 int k3xb_kda_block_host(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t H, const float* x_host, uint32_t T,
                         uint16_t* conv_host, float* rec_host, float* out_host) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     int st = validate_kda(ctx, w, H);
     if (st) return st;
     if (!x_host || !T || !conv_host || !rec_host || !out_host)
@@ -1062,7 +1062,7 @@ int k3xb_kda_block_host(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t H, cons
 int k3xb_attention_residual_norm(k3xb_ctx* ctx, const float* a, const float* delta, const float* block,
                                  const uint16_t* rnorm, const uint16_t* rproj, const uint16_t* post, uint32_t T,
                                  uint32_t H, float eps, float* prefix_out, float* out) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!a || !block || !rnorm || !rproj || !post || !T || !H || !out || (delta && !prefix_out))
         return fail(ctx, K3XB_INVALID_EXTENT, "attention residual arguments");
     if (!(eps > 0.0f)) return fail(ctx, K3XB_INVALID_EXTENT, "eps must be positive");
@@ -1072,7 +1072,7 @@ int k3xb_attention_residual_norm(k3xb_ctx* ctx, const float* a, const float* del
 int k3xb_layer_forward(k3xb_ctx* ctx, const k3xb_layer* L, const float* hidden_in, const float* block,
                        const int32_t* parent, uint32_t N, uint32_t S, const uint16_t* conv, const float* rec,
                        float* hidden_out, uint32_t* ids_out, void* trace) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     int st = validate_full_layer(ctx, L);
     if (st) return st;
     if (!hidden_in || !block || !parent || !N || !S || !conv || !rec || !hidden_out)
@@ -1091,7 +1091,7 @@ int k3xb_layer_forward(k3xb_ctx* ctx, const k3xb_layer* L, const float* hidden_i
 }
 
 int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verify_io* io) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!m || !io || !m->layers || !m->layer || !m->vocab || !m->lm_head)
         return fail(ctx, K3XB_INVALID_EXTENT, "verify model");
     int st;
@@ -1207,7 +1207,7 @@ int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verif
 }
 
 int k3xb_draft_greedy(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_draft_io* io) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!m || !io || !m->layers || !m->layer || !m->embedding)
         return fail(ctx, K3XB_INVALID_EXTENT, "draft model (needs its embedding)");
     const uint32_t S = io->sequences, p = io->drafts, K = io->draft_top_k;
@@ -1266,7 +1266,7 @@ int k3xb_draft_greedy(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_draf
 }
 
 int k3xb_speculative_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_speculative_io* io) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!m || !io || !io->anchors || !io->conv || !io->recurrent || !io->draft_tokens || !io->accepted ||
         !io->committed || !io->committed_count || !io->sequences || !io->drafts)
         return fail(ctx, K3XB_INVALID_EXTENT, "speculative io");
@@ -1300,7 +1300,7 @@ int k3xb_speculative_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_
 
 int k3xb_ep_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* local, uint32_t E, const float* hidden,
                               uint32_t T, float* out, uint32_t* ids_out, float* contrib_out) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     int st = validate_layer(ctx, local);
     if (st) return st;
     const int G = ep_world(ctx);

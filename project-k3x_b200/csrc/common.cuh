@@ -50,6 +50,17 @@ int ensure_io(k3xb_ctx* ctx, size_t bytes, void** out);
         if (k3xb_err_ != cudaSuccess) return k3xb::cuda_fail((ctx), k3xb_err_, #call); \
     } while (0)
 
+// Entry of a C ABI call on a context: a null context is INVALID_EXTENT, and
+// the calling thread's current device becomes the context's when it is not
+// already (a process may hold contexts on several GPUs).
+#define K3XB_ENTER(ctx)                                                         \
+    do {                                                                        \
+        if (!(ctx)) return K3XB_INVALID_EXTENT;                                 \
+        int k3xb_dev_ = -1;                                                     \
+        if (cudaGetDevice(&k3xb_dev_) != cudaSuccess || k3xb_dev_ != (ctx)->device) \
+            K3XB_CUDA((ctx), cudaSetDevice((ctx)->device));                     \
+    } while (0)
+
 #define K3XB_LAUNCHED(ctx)                                          \
     do {                                                            \
         cudaError_t k3xb_err_ = cudaGetLastError();                 \

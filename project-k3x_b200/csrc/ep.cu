@@ -303,7 +303,7 @@ int k3xb_ep_unique_id(uint8_t* out) {
 }
 
 int k3xb_ep_init(k3xb_ctx* ctx, const uint8_t* unique_id, int32_t rank, int32_t world) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!unique_id || world < 1 || rank < 0 || rank >= world)
         return fail(ctx, K3XB_INVALID_EXTENT, "ep_init arguments");
     if (ctx->ep_state) return fail(ctx, K3XB_INVALID_STATE, "expert parallelism already initialised");
@@ -324,7 +324,7 @@ int k3xb_ep_init(k3xb_ctx* ctx, const uint8_t* unique_id, int32_t rank, int32_t 
 }
 
 int k3xb_ep_finalize(k3xb_ctx* ctx) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     release_ep(ctx);
     return K3XB_OK;
 }

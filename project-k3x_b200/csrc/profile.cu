@@ -101,7 +101,7 @@ void release_profiler(k3xb_ctx* ctx) {
 using namespace k3xb;
 
 int k3xb_set_profiling(k3xb_ctx* ctx, int enable) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!ctx->profiler) {
         if (!enable) return K3XB_OK;
         ctx->profiler = new (std::nothrow) Profiler();

@@ -75,7 +75,7 @@ void resident_stats(const k3xb_ctx* ctx, k3xb_stats* out) {
 using namespace k3xb;
 
 int k3xb_set_resident_capacity(k3xb_ctx* ctx, uint64_t bytes) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     Resident* r = resident_of(ctx);
     if (!r) return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "resident table: out of host memory");
     r->table.set_capacity(bytes);
@@ -85,11 +85,10 @@ int k3xb_set_resident_capacity(k3xb_ctx* ctx, uint64_t bytes) {
 int k3xb_acquire_weight(k3xb_ctx* ctx, uint64_t tensor_id, int32_t representation, uint64_t rows, uint64_t cols,
                         uint64_t group_size, const void* primary, size_t primary_bytes, const void* secondary,
                         size_t secondary_bytes, k3xb_resident* out) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!out) return fail(ctx, K3XB_INVALID_EXTENT, "acquire_weight: null result");
     Resident* r = resident_of(ctx);
     if (!r) return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "resident table: out of host memory");
-    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "cudaSetDevice");
     const char* why = "";
     const int st = r->table.acquire(ResidentKey{tensor_id, representation, rows, cols, group_size}, primary,
                                     primary_bytes, secondary, secondary_bytes, out, &why);
@@ -100,11 +99,10 @@ int k3xb_acquire_weight(k3xb_ctx* ctx, uint64_t tensor_id, int32_t representatio
 
 int k3xb_acquire_expert_stack(k3xb_ctx* ctx, uint64_t stack_id, uint32_t experts, uint32_t hidden, uint32_t inter,
                               const k3xb_mxfp4_expert_host* host, k3xb_resident_stack* out) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!out) return fail(ctx, K3XB_INVALID_EXTENT, "acquire_expert_stack: null result");
     Resident* r = resident_of(ctx);
     if (!r) return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "resident table: out of host memory");
-    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "cudaSetDevice");
     const char* why = "";
     const int st = r->table.acquire_stack(stack_id, experts, hidden, inter, host, out, &why);
     if (st) return fail(ctx, st, why);
@@ -113,7 +111,7 @@ int k3xb_acquire_expert_stack(k3xb_ctx* ctx, uint64_t stack_id, uint32_t experts
 }
 
 int k3xb_release_resident(k3xb_ctx* ctx) {
-    if (!ctx) return K3XB_INVALID_EXTENT;
+    K3XB_ENTER(ctx);
     if (!ctx->resident) return K3XB_OK;
     K3XB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     static_cast<Resident*>(ctx->resident)->table.clear();   // keeps the capacity and counters
