@@ -616,9 +616,39 @@ int k3xb_speculative_step(k3xb_ctx* ctx, const k3xb_verify_model* model,
  * transport: a store, a file, a broadcast). No reference counterpart: the
  * reference runs one process on one GPU. */
 int k3xb_ep_unique_id(uint8_t* unique_id);
-/* Joins this context (its GPU) to a world of `world` ranks. */
+/* Joins this context (its GPU) to a world of `world` ranks: a blocking
+ * communicator with the default bound (k3xb_ep_init_config with NULL). */
 int k3xb_ep_init(k3xb_ctx* ctx, const uint8_t* unique_id, int32_t rank,
                  int32_t world);
+/* Failure detection. Every wait on the communicator has a bound: the
+ * stream drains of k3xb_sync, of scratch growth, of k3xb_ep_finalize and of
+ * k3xb_destroy, and (nonblocking = 1) creation and each exchange's launch.
+ * A bound that passes, or an error NCCL reports (a peer that failed), aborts
+ * the communicator, whose kernels in flight then return; the call returns
+ * BACKEND_UNAVAILABLE with the reason in k3xb_last_error. The context's
+ * one-GPU entry points keep working; the expert-parallel ones return
+ * INVALID_STATE until k3xb_ep_finalize and a new init (with a new unique id
+ * on every rank). A caller that synchronises the stream itself (e.g. with
+ * torch) should call k3xb_sync or k3xb_ep_status instead, or it waits on
+ * NCCL's kernels without a bound. */
+#define K3XB_EP_DEFAULT_TIMEOUT_MS 300000u
+typedef struct {
+    uint32_t timeout_ms;    /* the bound; 0 = K3XB_EP_DEFAULT_TIMEOUT_MS */
+    uint32_t nonblocking;   /* 1: NCCL nonblocking communicator (creation and
+                               group launch polled under the bound) */
+} k3xb_ep_config;
+int k3xb_ep_init_config(k3xb_ctx* ctx, const uint8_t* unique_id, int32_t rank,
+                        int32_t world, const k3xb_ep_config* config);
+/* OK while the communicator is healthy (an error NCCL reported since the
+ * last call aborts it here); INVALID_STATE when there is none or it was
+ * aborted. Does not wait. */
+int k3xb_ep_status(k3xb_ctx* ctx);
+/* Ends the communicator at once, without its peers (ncclCommAbort): for a
+ * rank that found on the host that a peer is gone (k3xb.peers.PeerWatch),
+ * or that leaves while the others may not take part in a finalize. Then
+ * k3xb_ep_finalize, and k3xb_ep_init with a new unique id to go on. */
+int k3xb_ep_abort(k3xb_ctx* ctx);
+/* Drains the stream (bounded), then frees the communicator. */
 int k3xb_ep_finalize(k3xb_ctx* ctx);
 /* The MoE layer of k3xb_moe_layer_forward with the routed experts sharded:
  * this rank holds experts [rank*E/world, (rank+1)*E/world) in `local`

@@ -197,10 +197,16 @@ public:
         return check(k3xb_speculative_step(h_, &model, &io));
     }
 
-    // Expert parallelism over the GPUs of one box.
-    Outcome ep_init(std::span<const std::uint8_t, 128> unique_id, int rank, int world) {
-        return check(k3xb_ep_init(h_, unique_id.data(), rank, world));
+    // Expert parallelism over the GPUs of one box. Every wait on the
+    // communicator is bounded by `config.timeout_ms`; past it, or on an error
+    // NCCL reports, the communicator is aborted (backend_unavailable) and the
+    // expert-parallel calls answer invalid_state until ep_finalize + ep_init.
+    Outcome ep_init(std::span<const std::uint8_t, 128> unique_id, int rank, int world,
+                    const k3xb_ep_config& config = {0, 0}) {
+        return check(k3xb_ep_init_config(h_, unique_id.data(), rank, world, &config));
     }
+    Outcome ep_status() { return check(k3xb_ep_status(h_)); }
+    Outcome ep_abort() { return check(k3xb_ep_abort(h_)); }
     Outcome ep_finalize() { return check(k3xb_ep_finalize(h_)); }
 
 private:

@@ -22,9 +22,15 @@ int cuda_fail(k3xb_ctx* ctx, cudaError_t err, const char* where) {
     return fail(ctx, K3XB_BACKEND_UNAVAILABLE, msg);
 }
 
+int stream_wait(k3xb_ctx* ctx) {
+    if (ep_world(ctx)) return ep_drain(ctx);
+    K3XB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    return K3XB_OK;
+}
+
 int ensure_scratch(k3xb_ctx* ctx, size_t bytes, void** out) {
     if (bytes > ctx->scratch_bytes) {
-        K3XB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+        if (const int st = stream_wait(ctx)) return st;
         if (ctx->scratch) K3XB_CUDA(ctx, cudaFree(ctx->scratch));
         ctx->scratch = nullptr;
         ctx->scratch_bytes = 0;
@@ -40,7 +46,7 @@ int ensure_scratch(k3xb_ctx* ctx, size_t bytes, void** out) {
 
 int ensure_io(k3xb_ctx* ctx, size_t bytes, void** out) {
     if (bytes > ctx->io_bytes) {
-        K3XB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+        if (const int st = stream_wait(ctx)) return st;
         if (ctx->io) K3XB_CUDA(ctx, cudaFree(ctx->io));
         ctx->io = nullptr;
         ctx->io_bytes = 0;
@@ -270,6 +276,7 @@ int k3xb_create(int device, k3xb_ctx** out) {
 int k3xb_destroy(k3xb_ctx* ctx) {
     if (!ctx) return K3XB_OK;
     cudaSetDevice(ctx->device);
+    if (ep_world(ctx)) ep_drain(ctx);   // bounded: a failed peer's exchange is aborted, not waited for
     if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
     if (ctx->side_stream) cudaStreamSynchronize(ctx->side_stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
@@ -301,7 +308,7 @@ int k3xb_set_stream(k3xb_ctx* ctx, void* stream) {
 
 int k3xb_sync(k3xb_ctx* ctx) {
     K3XB_ENTER(ctx);
-    K3XB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    if (const int st = stream_wait(ctx)) return st;
     int32_t st = 0;
     K3XB_CUDA(ctx, cudaMemcpy(&st, ctx->status_word, sizeof st, cudaMemcpyDeviceToHost));
     if (st) {

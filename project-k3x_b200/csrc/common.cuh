@@ -43,6 +43,9 @@ int ensure_scratch(k3xb_ctx* ctx, size_t bytes, void** out);
 // points, apart from `scratch` so the device entry points they call may
 // grow the scratch.
 int ensure_io(k3xb_ctx* ctx, size_t bytes, void** out);
+// Waits for ctx->stream; with expert parallelism on, under the
+// communicator's bound (ep.cu), so a failed peer cannot hold it for ever.
+int stream_wait(k3xb_ctx* ctx);
 
 #define K3XB_CUDA(ctx, call)                                        \
     do {                                                            \

@@ -20,13 +20,24 @@
 //
 // NCCL is opened at run time (dlopen "libnccl.so.2"), which picks the copy
 // the process already loaded (torch's, when torch is imported first).
+//
+// Failure detection (ep_guard.hpp): every wait on the communicator has a
+// deadline (k3xb_ep_config.timeout_ms) — creation and group launch of a
+// nonblocking communicator, and the stream drain of k3xb_sync, of scratch
+// growth and of k3xb_destroy. On expiry, or on an asynchronous NCCL error,
+// the communicator is aborted (its kernels in flight return) and the
+// expert-parallel entry points refuse until k3xb_ep_finalize and a new init.
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
 #include <cstring>
+#include <memory>
 #include <mutex>
+#include <thread>
 
 #include "common.cuh"
+#include "ep_guard.hpp"
 #include "kernels.cuh"
 #include "profile.cuh"
 
@@ -43,8 +54,14 @@ struct NcclApi {
     decltype(&ncclGroupStart) group_start = nullptr;
     decltype(&ncclGroupEnd) group_end = nullptr;
     decltype(&ncclGetErrorString) error_string = nullptr;
+    decltype(&ncclCommInitRankConfig) comm_init_rank_config = nullptr;
+    decltype(&ncclCommGetAsyncError) comm_get_async_error = nullptr;
+    decltype(&ncclCommAbort) comm_abort = nullptr;
+    decltype(&ncclCommFinalize) comm_finalize = nullptr;
     bool ok = false;
 };
+
+static_assert(ncclSuccess == kCommSuccess && ncclInProgress == kCommInProgress, "ep_guard.hpp codes are nccl.h's");
 
 const NcclApi& nccl() {
     static NcclApi api;
@@ -60,27 +77,95 @@ const NcclApi& nccl() {
         api.group_start = reinterpret_cast<decltype(api.group_start)>(dlsym(h, "ncclGroupStart"));
         api.group_end = reinterpret_cast<decltype(api.group_end)>(dlsym(h, "ncclGroupEnd"));
         api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+        api.comm_init_rank_config =
+            reinterpret_cast<decltype(api.comm_init_rank_config)>(dlsym(h, "ncclCommInitRankConfig"));
+        api.comm_get_async_error =
+            reinterpret_cast<decltype(api.comm_get_async_error)>(dlsym(h, "ncclCommGetAsyncError"));
+        api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(dlsym(h, "ncclCommAbort"));
+        api.comm_finalize = reinterpret_cast<decltype(api.comm_finalize)>(dlsym(h, "ncclCommFinalize"));
         api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.send && api.recv &&
-                 api.group_start && api.group_end && api.error_string;
+                 api.group_start && api.group_end && api.error_string && api.comm_init_rank_config &&
+                 api.comm_get_async_error && api.comm_abort && api.comm_finalize;
     });
     return api;
 }
 
+struct EpState;
+
+// The communicator and stream operations ep_guard.hpp waits with.
+struct NcclOps {
+    EpState* ep;
+    k3xb_ctx* ctx;
+    cudaError_t last_cuda = cudaSuccess;
+    int async_error(int* state);
+    int abort();
+    int stream_query() {
+        const cudaError_t e = cudaStreamQuery(ctx->stream);
+        if (e == cudaSuccess) return 0;
+        if (e == cudaErrorNotReady) {
+            if (cudaPeekAtLastError() == cudaErrorNotReady) cudaGetLastError();
+            return 1;
+        }
+        last_cuda = e;
+        return -1;
+    }
+    uint64_t now_ms() const {
+        return static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::milliseconds>(
+                                         std::chrono::steady_clock::now().time_since_epoch())
+                                         .count());
+    }
+    void pause(uint32_t polls) const {
+        if (polls < 1024) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
+    const char* describe(int r) const { return nccl().error_string(static_cast<ncclResult_t>(r)); }
+};
+
 struct EpState {
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
+    bool nonblocking = false;
+    CommGuard<NcclOps> guard;
+    EpState(k3xb_ctx* ctx, uint32_t timeout_ms) : guard(NcclOps{this, ctx}, timeout_ms) {}
 };
 
-int nccl_fail(k3xb_ctx* ctx, ncclResult_t r, const char* where) {
-    const char* msg = nccl().error_string ? nccl().error_string(r) : "?";
-    return fail(ctx, K3XB_BACKEND_UNAVAILABLE, std::string(where) + ": " + msg);
+int NcclOps::async_error(int* state) {
+    ncclResult_t s = ncclSuccess;
+    const ncclResult_t r = nccl().comm_get_async_error(ep->comm, &s);
+    *state = static_cast<int>(s);
+    return static_cast<int>(r);
 }
 
-#define K3XB_NCCL(ctx, call)                                                \
-    do {                                                                    \
-        ncclResult_t k3xb_nr_ = (call);                                     \
-        if (k3xb_nr_ != ncclSuccess) return nccl_fail((ctx), k3xb_nr_, #call); \
-    } while (0)
+int NcclOps::abort() { return static_cast<int>(nccl().comm_abort(ep->comm)); }
+
+// Status of a guard outcome; the reason is the guard's.
+int guard_fail(k3xb_ctx* ctx, EpState* ep, CommWait w) {
+    if (w == CommWait::stuck)
+        return fail(ctx, K3XB_BACKEND_UNAVAILABLE,
+                    "expert parallelism: the stream did not drain within the bound after the communicator was "
+                    "aborted (" + ep->guard.reason() + ")");
+    if (w == CommWait::refused)
+        return fail(ctx, K3XB_INVALID_STATE,
+                    "expert parallelism: communicator aborted (" + ep->guard.reason() +
+                        "); k3xb_ep_finalize and k3xb_ep_init again");
+    return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "expert parallelism: " + ep->guard.reason());
+}
+
+// One NCCL group: `body` issues the sends and receives and returns the
+// first failing result. The group is always closed; an error or a launch
+// that does not settle in time aborts the communicator.
+template <typename F>
+int nccl_group(k3xb_ctx* ctx, EpState* ep, const char* what, F&& body) {
+    const NcclApi& api = nccl();
+    ncclResult_t r = api.group_start();
+    if (r == ncclSuccess) {
+        const ncclResult_t rb = body();
+        const ncclResult_t re = api.group_end();
+        r = rb != ncclSuccess ? rb : re;
+    }
+    const CommWait w = ep->guard.settle(static_cast<int>(r), what);
+    return w == CommWait::ok ? K3XB_OK : guard_fail(ctx, ep, w);
+}
 
 constexpr uint32_t kNoEntry = 0xffffffffu;
 
@@ -183,15 +268,17 @@ EpState* ep_of(k3xb_ctx* ctx) { return static_cast<EpState*>(ctx->ep_state); }
 int all_to_all(k3xb_ctx* ctx, const void* send, void* recv, size_t per_peer, ncclDataType_t type, size_t elem) {
     EpState* ep = ep_of(ctx);
     const NcclApi& api = nccl();
-    K3XB_NCCL(ctx, api.group_start());
-    for (int g = 0; g < ep->world; ++g) {
-        K3XB_NCCL(ctx, api.send(static_cast<const char*>(send) + g * per_peer * elem, per_peer, type, g, ep->comm,
-                                ctx->stream));
-        K3XB_NCCL(ctx, api.recv(static_cast<char*>(recv) + g * per_peer * elem, per_peer, type, g, ep->comm,
-                                ctx->stream));
-    }
-    K3XB_NCCL(ctx, api.group_end());
-    return K3XB_OK;
+    return nccl_group(ctx, ep, "return exchange", [&]() -> ncclResult_t {
+        for (int g = 0; g < ep->world; ++g) {
+            ncclResult_t r = api.send(static_cast<const char*>(send) + g * per_peer * elem, per_peer, type, g,
+                                      ep->comm, ctx->stream);
+            if (r == ncclSuccess)
+                r = api.recv(static_cast<char*>(recv) + g * per_peer * elem, per_peer, type, g, ep->comm,
+                             ctx->stream);
+            if (r != ncclSuccess) return r;
+        }
+        return ncclSuccess;
+    });
 }
 
 }  // namespace
@@ -200,10 +287,28 @@ int ep_world(const k3xb_ctx* ctx) {
     return ctx->ep_state ? static_cast<const EpState*>(ctx->ep_state)->world : 0;
 }
 
+int ep_drain(k3xb_ctx* ctx) {
+    EpState* ep = ep_of(ctx);
+    if (!ep) return K3XB_OK;
+    bool cuda_error = false;
+    const CommWait w = ep->guard.drain("stream drain", &cuda_error);
+    if (cuda_error) return cuda_fail(ctx, ep->guard.ops().last_cuda, "cudaStreamQuery");
+    return w == CommWait::ok ? K3XB_OK : guard_fail(ctx, ep, w);
+}
+
 void release_ep(k3xb_ctx* ctx) {
     EpState* ep = ep_of(ctx);
     if (!ep) return;
-    if (ep->comm && nccl().ok) nccl().comm_destroy(ep->comm);
+    // an aborted communicator is already freed (ncclCommAbort)
+    if (ep->comm && !ep->guard.aborted()) {
+        const NcclApi& api = nccl();
+        if (ep->nonblocking) {   // finalize settles like any nonblocking call, then destroy
+            const CommWait w = ep->guard.settle(static_cast<int>(api.comm_finalize(ep->comm)), "ncclCommFinalize");
+            if (w == CommWait::ok) api.comm_destroy(ep->comm);
+        } else {
+            api.comm_destroy(ep->comm);
+        }
+    }
     delete ep;
     ctx->ep_state = nullptr;
 }
@@ -229,6 +334,10 @@ size_t ep_scratch_bytes(uint32_t G, uint32_t T, uint32_t K, uint32_t H, uint32_t
 int ep_moe_forward(k3xb_ctx* ctx, const k3xb_moe_layer& L, uint32_t E, const float* hidden, uint32_t T,
                    const uint32_t* ids, const float* contrib, const float* shared, void* region, float* out) {
     EpState* ep = ep_of(ctx);
+    {   // a failure NCCL saw since the last call (a peer's) ends the communicator before new work is queued
+        const CommWait w = ep->guard.check("expert parallelism");
+        if (w != CommWait::ok) return guard_fail(ctx, ep, w);
+    }
     const uint32_t G = static_cast<uint32_t>(ep->world), K = L.top_k, H = L.hidden, E_r = L.experts;
     Carver c(region);
     float* send_x = c.take<float>(static_cast<size_t>(G) * T * H);
@@ -258,15 +367,19 @@ int ep_moe_forward(k3xb_ctx* ctx, const k3xb_moe_layer& L, uint32_t E, const flo
     {   // metadata and rows in one NCCL group
         PhaseScope ph(ctx, K3XB_PHASE_EP_EXCHANGE);
         const NcclApi& api = nccl();
-        K3XB_NCCL(ctx, api.group_start());
-        for (uint32_t g = 0; g < G; ++g) {
+        st = nccl_group(ctx, ep, "dispatch exchange", [&]() -> ncclResult_t {
             const size_t nm_g = static_cast<size_t>(T) * K, nx_g = static_cast<size_t>(T) * H;
-            K3XB_NCCL(ctx, api.send(send_meta + g * nm_g, nm_g, ncclUint32, g, ep->comm, ctx->stream));
-            K3XB_NCCL(ctx, api.recv(recv_meta + g * nm_g, nm_g, ncclUint32, g, ep->comm, ctx->stream));
-            K3XB_NCCL(ctx, api.send(send_x + g * nx_g, nx_g, ncclFloat32, g, ep->comm, ctx->stream));
-            K3XB_NCCL(ctx, api.recv(recv_x + g * nx_g, nx_g, ncclFloat32, g, ep->comm, ctx->stream));
-        }
-        K3XB_NCCL(ctx, api.group_end());
+            for (uint32_t g = 0; g < G; ++g) {
+                const int peer = static_cast<int>(g);
+                ncclResult_t r = api.send(send_meta + g * nm_g, nm_g, ncclUint32, peer, ep->comm, ctx->stream);
+                if (r == ncclSuccess) r = api.recv(recv_meta + g * nm_g, nm_g, ncclUint32, peer, ep->comm, ctx->stream);
+                if (r == ncclSuccess) r = api.send(send_x + g * nx_g, nx_g, ncclFloat32, peer, ep->comm, ctx->stream);
+                if (r == ncclSuccess) r = api.recv(recv_x + g * nx_g, nx_g, ncclFloat32, peer, ep->comm, ctx->stream);
+                if (r != ncclSuccess) return r;
+            }
+            return ncclSuccess;
+        });
+        if (st) return st;
     }
     {
         PhaseScope ph(ctx, K3XB_PHASE_PLAN);
@@ -302,31 +415,70 @@ int k3xb_ep_unique_id(uint8_t* out) {
     return K3XB_OK;
 }
 
-int k3xb_ep_init(k3xb_ctx* ctx, const uint8_t* unique_id, int32_t rank, int32_t world) {
+int k3xb_ep_init_config(k3xb_ctx* ctx, const uint8_t* unique_id, int32_t rank, int32_t world,
+                        const k3xb_ep_config* config) {
     K3XB_ENTER(ctx);
     if (!unique_id || world < 1 || rank < 0 || rank >= world)
         return fail(ctx, K3XB_INVALID_EXTENT, "ep_init arguments");
+    if (config && config->nonblocking > 1) return fail(ctx, K3XB_INVALID_EXTENT, "ep_config.nonblocking is 0 or 1");
     if (ctx->ep_state) return fail(ctx, K3XB_INVALID_STATE, "expert parallelism already initialised");
     if (!nccl().ok) return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "libnccl.so.2 could not be opened");
-    K3XB_CUDA(ctx, cudaSetDevice(ctx->device));
+    const uint32_t timeout = config && config->timeout_ms ? config->timeout_ms : K3XB_EP_DEFAULT_TIMEOUT_MS;
     ncclUniqueId id;
     std::memcpy(&id, unique_id, sizeof id);
-    auto* ep = new EpState();
+    std::unique_ptr<EpState> ep(new (std::nothrow) EpState(ctx, timeout));
+    if (!ep) return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "ep_init: out of host memory");
     ep->rank = rank;
     ep->world = world;
-    ncclResult_t r = nccl().comm_init_rank(&ep->comm, world, id, rank);
-    if (r != ncclSuccess) {
-        delete ep;
-        return nccl_fail(ctx, r, "ncclCommInitRank");
+    ep->nonblocking = config && config->nonblocking;
+    if (!ep->nonblocking) {   // creation blocks until every rank has joined
+        const ncclResult_t r = nccl().comm_init_rank(&ep->comm, world, id, rank);
+        if (r != ncclSuccess)
+            return fail(ctx, K3XB_BACKEND_UNAVAILABLE, std::string("ncclCommInitRank: ") + nccl().error_string(r));
+    } else {   // creation returns at once and settles under the deadline
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.blocking = 0;
+        const ncclResult_t r = nccl().comm_init_rank_config(&ep->comm, world, id, rank, &cfg);
+        if (!ep->comm)
+            return fail(ctx, K3XB_BACKEND_UNAVAILABLE,
+                        std::string("ncclCommInitRankConfig: ") + nccl().error_string(r));
+        const CommWait w = ep->guard.settle(static_cast<int>(r), "ncclCommInitRankConfig");
+        if (w != CommWait::ok)
+            return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "expert parallelism: " + ep->guard.reason());
     }
-    ctx->ep_state = ep;
+    ctx->ep_state = ep.release();
+    return K3XB_OK;
+}
+
+int k3xb_ep_init(k3xb_ctx* ctx, const uint8_t* unique_id, int32_t rank, int32_t world) {
+    return k3xb_ep_init_config(ctx, unique_id, rank, world, nullptr);
+}
+
+int k3xb_ep_status(k3xb_ctx* ctx) {
+    K3XB_ENTER(ctx);
+    EpState* ep = ep_of(ctx);
+    if (!ep) return fail(ctx, K3XB_INVALID_STATE, "expert parallelism not initialised");
+    const CommWait w = ep->guard.check("expert parallelism");
+    return w == CommWait::ok ? K3XB_OK : guard_fail(ctx, ep, w);
+}
+
+int k3xb_ep_abort(k3xb_ctx* ctx) {
+    K3XB_ENTER(ctx);
+    EpState* ep = ep_of(ctx);
+    if (!ep) return fail(ctx, K3XB_INVALID_STATE, "expert parallelism not initialised");
+    ep->guard.abort_now("aborted by the caller");
+    const int st = ep_drain(ctx);
+    if (st != K3XB_INVALID_STATE) return st;   // a CUDA error, or still busy after the bound
+    ctx->error.clear();                        // drained: the refusal is the state asked for
     return K3XB_OK;
 }
 
 int k3xb_ep_finalize(k3xb_ctx* ctx) {
     K3XB_ENTER(ctx);
+    int st = K3XB_OK;
+    if (ep_of(ctx) && !ep_of(ctx)->guard.aborted()) st = ep_drain(ctx);   // bounded: aborts on expiry
     release_ep(ctx);
-    return K3XB_OK;
+    return st == K3XB_INVALID_STATE ? K3XB_OK : st;
 }
 
 }  // extern "C"

@@ -111,6 +111,9 @@ size_t ep_scratch_bytes(uint32_t G, uint32_t T, uint32_t K, uint32_t H, uint32_t
 int ep_moe_forward(k3xb_ctx* ctx, const k3xb_moe_layer& local, uint32_t E, const float* hidden, uint32_t T,
                    const uint32_t* ids, const float* contrib, const float* shared, void* region, float* out);
 int ep_world(const k3xb_ctx* ctx);   // 0 when expert parallelism is not initialised
+// Waits for ctx->stream with the communicator's bound (ep_guard.hpp); OK at
+// once without expert parallelism.
+int ep_drain(k3xb_ctx* ctx);
 // shared expert on kind::f16 tensor cores; xb [2T][H], bd [2T][Is] bf16 scratch
 int launch_shared_tc(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T, uint16_t* xb,
                      uint16_t* bd, float* out);

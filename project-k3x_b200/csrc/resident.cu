@@ -113,7 +113,7 @@ int k3xb_acquire_expert_stack(k3xb_ctx* ctx, uint64_t stack_id, uint32_t experts
 int k3xb_release_resident(k3xb_ctx* ctx) {
     K3XB_ENTER(ctx);
     if (!ctx->resident) return K3XB_OK;
-    K3XB_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    if (const int st = stream_wait(ctx)) return st;
     static_cast<Resident*>(ctx->resident)->table.clear();   // keeps the capacity and counters
     return K3XB_OK;
 }

@@ -96,6 +96,13 @@ class SpeculativeIO(C.Structure):
                                   "committed_count", "logits")]
 
 
+EP_DEFAULT_TIMEOUT_MS = 300000
+
+
+class EpConfig(C.Structure):
+    _fields_ = [("timeout_ms", C.c_uint32), ("nonblocking", C.c_uint32)]
+
+
 class RoutingPolicy(C.Structure):
     _fields_ = [("mode", C.c_int32), ("fixed_k", C.c_uint32), ("mass_target", C.c_float),
                 ("minimum_gap", C.c_float), ("quality_floor_k", C.c_uint32)]
@@ -182,6 +189,9 @@ def library() -> C.CDLL:
             "k3xb_speculative_step": [vp, C.POINTER(VerifyModel), C.POINTER(SpeculativeIO)],
             "k3xb_ep_unique_id": [vp],
             "k3xb_ep_init": [vp, vp, C.c_int32, C.c_int32],
+            "k3xb_ep_init_config": [vp, vp, C.c_int32, C.c_int32, C.POINTER(EpConfig)],
+            "k3xb_ep_status": [vp],
+            "k3xb_ep_abort": [vp],
             "k3xb_ep_finalize": [vp],
             "k3xb_ep_moe_layer_forward": [vp, C.POINTER(MoeLayer), u32, vp, u32, vp, vp, vp],
             "k3xb_set_resident_capacity": [vp, u64],
@@ -351,9 +361,24 @@ class Context:
                                                 _p(trace)), "layer_forward")
 
     # ---- expert parallelism ------------------------------------------------
-    def ep_init(self, unique_id: bytes, rank: int, world: int):
+    def ep_init(self, unique_id: bytes, rank: int, world: int, timeout_ms: int = 0, nonblocking: bool = False):
+        """Joins a world of `world` ranks. Every wait on the communicator is
+        bounded by timeout_ms (0: EP_DEFAULT_TIMEOUT_MS); past it, or on an
+        error NCCL reports, the communicator is aborted and the call raises
+        (BACKEND_UNAVAILABLE), later expert-parallel calls raise
+        INVALID_STATE until ep_finalize and a new ep_init."""
         buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
-        self._check(self.lib.k3xb_ep_init(self.h, buf, rank, world), "ep_init")
+        cfg = EpConfig(timeout_ms, 1 if nonblocking else 0)
+        self._check(self.lib.k3xb_ep_init_config(self.h, buf, rank, world, C.byref(cfg)), "ep_init")
+
+    def ep_abort(self):
+        """Ends the communicator without its peers (one is known to be gone)."""
+        self._check(self.lib.k3xb_ep_abort(self.h), "ep_abort")
+
+    def ep_status(self):
+        """Raises if the communicator is gone or NCCL has reported a failure
+        (which aborts it); does not wait."""
+        self._check(self.lib.k3xb_ep_status(self.h), "ep_status")
 
     def ep_finalize(self):
         self._check(self.lib.k3xb_ep_finalize(self.h), "ep_finalize")

@@ -1,6 +1,7 @@
 """Host code under AddressSanitizer and UndefinedBehaviorSanitizer: the
-resident weight table (csrc/resident.hpp), the C++20 host layer
-(include/k3xb.hpp) and the ComputeBackend adapter, each built from the same
+resident weight table (csrc/resident.hpp), the expert-parallel bounded
+waits (csrc/ep_guard.hpp), the C++20 host layer (include/k3xb.hpp) and the
+ComputeBackend adapter, each built from the same
 sources as their plain tests with -fsanitize=address,undefined and run to a
 clean exit. Device code has no sanitizer here (compute-sanitizer is closed
 on the GPU pool); its guards are bounded waits, status words and the
@@ -37,6 +38,11 @@ def test_resident_table_sanitized(tmp_path):
     _run(tmp_path, "resident_check", [os.path.join(ROOT, "tests", "cpp", "resident_check.cpp")],
          ["-I", os.path.join(ROOT, "include"), "-I", os.path.join(ROOT, "project-k3x_b200", "csrc")],
          "resident ok", {"ASAN_OPTIONS": "detect_leaks=1"})
+
+
+def test_ep_guard_sanitized(tmp_path):
+    _run(tmp_path, "ep_guard_check", [os.path.join(ROOT, "tests", "cpp", "ep_guard_check.cpp")],
+         ["-I", os.path.join(ROOT, "project-k3x_b200", "csrc")], "ep guard ok", {"ASAN_OPTIONS": "detect_leaks=1"})
 
 
 def _needs_lib():
