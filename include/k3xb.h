@@ -383,6 +383,30 @@ int k3xb_expert_grid_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer,
                           const float* inputs_host, uint32_t tokens,
                           float* out_host);
 
+/* official_mxfp4_moe_ffn (backend.hpp:376-381; the reference's CUDA
+ * backend_cuda.cu:3717-4172) for ONE position with its route given: the
+ * LatentMoE tail of official_moe_cpu (official_moe.cpp:296-341).
+ *   latent   = bf16_matvec(hidden, routed_down)
+ *   y_k      = expert of slot k on the latent row (bf16-rounded down product)
+ *   mixed    = round_bf16(sum_k contributions[k] * y_k, in slot order)
+ *   routed   = bf16_matvec(normalized(mixed, routed_norm, latent_eps), routed_up)
+ *   combined = round_bf16(routed + shared(hidden))   (no shared expert: round_bf16(routed))
+ *   out      = round_bf16(round_bf16(prefix) + combined)
+ * `tail` gives hidden, latent, shared_inter, the routed_* and shared_*
+ * weights, latent_eps and the activation (shared and experts alike); its
+ * expert fields are not read. slots[k] (K <= 64) is one expert (experts =
+ * 1 of the latent width: latent, or hidden when latent is 0; one inter and
+ * engine for all; MXF4 needs
+ * the *_scales_tc copies), e.g. a resident stack of one
+ * (k3xb_acquire_expert_stack) or single resident MXFP4 weights for the SIMT
+ * engine. hidden is the prepared (bf16-valued) MoE input; HOST
+ * contributions [K], hidden [H], prefix [H] and out [H]; returns after out
+ * is on the host. */
+int k3xb_official_moe_ffn_host(k3xb_ctx* ctx, const k3xb_moe_layer* tail,
+                               const k3xb_moe_layer* slots, uint32_t K,
+                               const float* contributions, const float* hidden,
+                               const float* prefix, float* out);
+
 /* ---- (d) KDA recurrence -------------------------------------------------- */
 /* official_kda.cpp:319-369 applied over a draft tree for S sequences that
  * share the topology: node n continues from parent[n]'s state

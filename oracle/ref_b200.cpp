@@ -1,0 +1,143 @@
+// ref_b200.cpp — the reference's own layer driver over this library's
+// ComputeBackend.
+//
+// TEST INFRASTRUCTURE ONLY. oracle/Makefile compiles this file with the
+// reference's unmodified official_layer_cuda (runtime/src/official_layer.cpp:
+// 246-500) and the CPU pieces it calls (attention residual, RMSNorm, MoE
+// input preparation and routing: official_layer.cpp, official_moe.cpp,
+// ops.cpp), read in place from the reference checkout, together with the
+// B200Backend adapter (project-k3x_b200/adapter/backend_b200.cpp), linked
+// against libk3xb.so, into oracle/_ref/libk3x_ref_b200.so. It shows the
+// drop-in: the reference's caller, unchanged, runs a whole official layer
+// with its KDA block (official_kda, host-roundtrip state) and its LatentMoE
+// FFN (official_mxfp4_moe_ffn, host route preparation) on the B200. The
+// GPU test compares the result with official_layer_cpu's golden output.
+// Nothing here is reference source: it only marshals plain C arrays into
+// the reference's C++ API and back.
+#include "k3x/official_layer.hpp"
+
+#include <algorithm>
+#include <cstdint>
+#include <cstdio>
+#include <optional>
+#include <span>
+#include <vector>
+
+#include "backend_b200.hpp"
+#include "ref_shim.hpp"
+
+namespace {
+
+std::span<const std::uint16_t> w16(const std::uint16_t* p, std::size_t n) { return {p, n}; }
+std::span<const std::byte> bytes(const std::uint8_t* p, std::size_t n) {
+    return {reinterpret_cast<const std::byte*>(p), n};
+}
+
+void message(char* err, std::size_t len, const std::string& m) {
+    if (err && len) std::snprintf(err, len, "%s", m.c_str());
+}
+
+}  // namespace
+
+extern "C" {
+
+// official_layer_cuda(B200Backend) over T positions of one layer with a
+// LatentMoE (SwiGLU: situ_glu with beta 2^64, no linear bound), the
+// arguments of k3xr_official_layer plus the device. The KDA state arrays are
+// updated in place; out [T][H] and ids [T][top_k]. Returns the k3x::ErrorCode
+// value; err receives the message.
+int k3xr_official_layer_b200(int device, const k3xr_kda_weights* kw, const k3xr_moe_layer* mw,
+                             const std::uint16_t* self_residual_norm, const std::uint16_t* self_residual_proj,
+                             const std::uint16_t* input_norm, const std::uint16_t* moe_residual_norm,
+                             const std::uint16_t* moe_residual_proj, const std::uint16_t* post_norm, float eps,
+                             const float* hidden_in, const float* block, std::size_t T, std::uint16_t* conv_q,
+                             std::uint16_t* conv_k, std::uint16_t* conv_v, float* recurrent, float* out,
+                             std::uint32_t* ids, char* err, std::size_t err_len) {
+    using k3x::ErrorCode;
+    const std::size_t H = kw->hidden, h = kw->heads, d = kw->head_dim, P = h * d, W = kw->conv_width;
+    const std::size_t E = mw->experts, I = mw->inter, D = mw->latent, S = mw->shared_inter;
+    if (!D || mw->activation != 0 || mw->hidden != H || !S) return static_cast<int>(ErrorCode::invalid_state);
+
+    k3x::BackendOptions options{};
+    options.kind = k3x::BackendKind::cuda_custom;
+    auto made = k3x::make_b200_backend(options, device);
+    if (!made) {
+        message(err, err_len, made.message());
+        return static_cast<int>(made.error());
+    }
+    k3x::ComputeBackend& backend = *made.value();
+
+    // every tensor its own non-zero id (the device path keeps weights resident by id)
+    std::uint64_t next_id = 1;
+    const auto mat = [&](const std::uint16_t* p, std::size_t rows, std::size_t cols) {
+        return k3x::Bf16WeightView{w16(p, rows * cols), rows, cols, next_id++};
+    };
+    const auto vec = [&](const std::uint16_t* p, std::size_t n) { return k3x::Bf16VectorView{w16(p, n), next_id++}; };
+    const auto dense = [&](const float* p, std::size_t rows, std::size_t cols) {
+        return k3x::DenseWeightView{next_id++, {p, rows * cols}, rows, cols};
+    };
+    const auto dvec = [&](const float* p, std::size_t n) { return k3x::DenseVectorView{next_id++, {p, n}}; };
+
+    std::vector<k3x::OfficialExpertView> experts(E);
+    for (std::size_t e = 0; e < E; ++e) {
+        experts[e].expert_id = static_cast<std::uint32_t>(e);
+        experts[e].weights.gate = {next_id++, bytes(mw->gate_packed + e * I * D / 2, I * D / 2),
+                                   bytes(mw->gate_scales + e * I * D / 32, I * D / 32), I, D, 32};
+        experts[e].weights.up = {next_id++, bytes(mw->up_packed + e * I * D / 2, I * D / 2),
+                                 bytes(mw->up_scales + e * I * D / 32, I * D / 32), I, D, 32};
+        experts[e].weights.down = {next_id++, bytes(mw->down_packed + e * D * I / 2, D * I / 2),
+                                   bytes(mw->down_scales + e * D * I / 32, D * I / 32), D, I, 32};
+    }
+    k3x::OfficialLayerCudaWeights w{};
+    w.self_residual_norm = vec(self_residual_norm, H);
+    w.self_residual_proj = mat(self_residual_proj, 1, H);
+    w.input_norm = vec(input_norm, H);
+    w.kda = k3x::OfficialKdaCudaView{mat(kw->q_proj, P, H),   mat(kw->k_proj, P, H),   mat(kw->v_proj, P, H),
+                                     dense(kw->q_conv, P, W), dense(kw->k_conv, P, W), dense(kw->v_conv, P, W),
+                                     mat(kw->f_a_proj, d, H), mat(kw->f_b_proj, P, d), dvec(kw->a_log, d),
+                                     dvec(kw->dt_bias, P),    mat(kw->b_proj, h, H),   mat(kw->g_proj, P, H),
+                                     dvec(kw->o_norm, d),     mat(kw->o_proj, H, P)};
+    // the host-side route preparation's weights (official_moe.cpp:156-269)
+    w.moe.residual_norm = vec(moe_residual_norm, H);
+    w.moe.residual_proj = mat(moe_residual_proj, 1, H);
+    w.moe.post_norm = vec(post_norm, H);
+    w.moe.router = mat(mw->router, E, H);
+    w.moe.correction = {mw->correction, E};
+    w.moe.routed_down = mat(mw->routed_down, D, H);
+    w.moe.routed_norm = vec(mw->routed_norm, D);
+    w.moe.routed_up = mat(mw->routed_up, H, D);
+    w.moe.shared = {mat(mw->shared_gate, S, H), mat(mw->shared_up, S, H), mat(mw->shared_down, H, S)};
+    w.moe.experts = experts;
+    // the FFN the backend runs shares the tensors (and their ids)
+    w.moe_ffn = {w.moe.routed_down, w.moe.routed_norm, w.moe.routed_up, w.moe.shared};
+
+    const std::size_t hist = (W - 1) * P;
+    const k3x::OfficialKdaState state{std::vector<std::uint16_t>(conv_q, conv_q + hist),
+                                      std::vector<std::uint16_t>(conv_k, conv_k + hist),
+                                      std::vector<std::uint16_t>(conv_v, conv_v + hist),
+                                      std::vector<float>(recurrent, recurrent + h * d * d)};
+    const k3x::OfficialKdaConfig config{H, h, d, W, eps, kw->gate_lower_bound};
+    std::vector<k3x::OfficialLayerInput> inputs(T);
+    for (std::size_t t = 0; t < T; ++t)
+        inputs[t] = {std::vector<float>(hidden_in + t * H, hidden_in + (t + 1) * H),
+                     std::vector<float>(block + t * H, block + (t + 1) * H)};
+    auto r = k3x::official_layer_cuda(backend, inputs, w, state, config, mw->top_k, 0x1p64F, std::nullopt, 0,
+                                      k3x::ProfilePhase::decode, {}, k3x::OfficialMoeRoutePreparationMode::host);
+    if (!r) {
+        message(err, err_len, r.message());
+        return static_cast<int>(r.error());
+    }
+    for (std::size_t t = 0; t < T; ++t) {
+        const auto& step = r.value().steps[t];
+        std::copy(step.output.begin(), step.output.end(), out + t * H);
+        std::copy(step.route.expert_ids.begin(), step.route.expert_ids.end(), ids + t * mw->top_k);
+    }
+    const auto& s = r.value().kda_state;
+    std::copy(s.conv_q.begin(), s.conv_q.end(), conv_q);
+    std::copy(s.conv_k.begin(), s.conv_k.end(), conv_k);
+    std::copy(s.conv_v.begin(), s.conv_v.end(), conv_v);
+    std::copy(s.recurrent_v_first.begin(), s.recurrent_v_first.end(), recurrent);
+    return 0;
+}
+
+}  // extern "C"

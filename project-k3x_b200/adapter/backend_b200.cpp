@@ -131,9 +131,9 @@ public:
         if (!rest_) return unavailable<std::vector<float>>("dense_situ_mlp is not on the B200 path");
         return rest_->dense_situ_mlp(input, weights, situ_beta, situ_linear, layer, phase);
     }
-    // The latent-space MoE of the reference's official/resident layers
-    // (routed_down / routed_norm / routed_up) is not the plain hidden-space
-    // MoE this library runs.
+    // The resident layer of backend_cpu.cpp:308-341 takes f32 dense
+    // projections and mixes unrounded expert outputs in float: not the bf16
+    // arithmetic of official_moe_cpu that this library's kernels compute.
     Result<ResidentMoeLayerResult> resident_mxfp4_moe_layer(std::span<const float> input, ResidentMoeLayerView w,
                                                             std::span<const Mxfp4MlpView> experts,
                                                             std::span<const float> contributions, float epsilon,
@@ -143,15 +143,93 @@ public:
         return rest_->resident_mxfp4_moe_layer(input, w, experts, contributions, epsilon, beta, linear, layer,
                                                phase);
     }
+
+    // ---- the official LatentMoE FFN of one position (k3xb_official_moe_ffn_host)
+    // Checks of backend_cuda.cu:3770-3875 (same failures, invalid_mxfp4);
+    // then each bf16 projection resident by tensor id, each routed expert a
+    // resident stack of one, and the tail on the device.
     Result<OfficialMoeFfnResult> official_mxfp4_moe_ffn(std::span<const float> hidden, std::span<const float> prefix,
                                                         OfficialMoeFfnView w, std::span<const Mxfp4MlpView> experts,
                                                         std::span<const std::uint32_t> ids,
                                                         std::span<const float> contributions, float epsilon,
                                                         float beta, std::optional<float> linear,
                                                         std::uint32_t layer, ProfilePhase phase) override {
-        if (!rest_) return unavailable<OfficialMoeFfnResult>("latent MoE FFN is not on the B200 path");
-        return rest_->official_mxfp4_moe_ffn(hidden, prefix, w, experts, ids, contributions, epsilon, beta, linear,
-                                             layer, phase);
+        using R = Result<OfficialMoeFfnResult>;
+        const auto finite = [](std::span<const float> v) {
+            for (const float x : v)
+                if (!std::isfinite(x)) return false;
+            return true;
+        };
+        const auto valid_bf16 = [](const Bf16WeightView& v) {
+            return v.tensor_id && v.rows && v.cols && v.rows <= SIZE_MAX / v.cols && v.values.size() == v.rows * v.cols;
+        };
+        if (hidden.empty() || hidden.size() != prefix.size() || experts.empty() || experts.size() > 65535 ||
+            experts.size() != ids.size() || experts.size() != contributions.size() || !finite(hidden) ||
+            !finite(prefix) || !finite(contributions) || !std::isfinite(epsilon) || epsilon <= 0.0F ||
+            !valid_activation(beta, linear) || !valid_bf16(w.routed_down) || !valid_bf16(w.routed_up) ||
+            !valid_bf16(w.shared.gate) || !valid_bf16(w.shared.up) || !valid_bf16(w.shared.down) ||
+            !w.routed_norm.tensor_id || w.routed_norm.values.empty())
+            return R::failure(ErrorCode::invalid_mxfp4);
+        const std::size_t H = hidden.size(), D = w.routed_down.rows, Dout = experts.front().down.rows,
+                          I = experts.front().gate.rows, Is = w.shared.gate.rows;
+        if (w.routed_down.cols != H || w.routed_norm.values.size() != Dout || w.routed_up.rows != H ||
+            w.routed_up.cols != Dout || w.shared.gate.cols != H || w.shared.up.rows != Is || w.shared.up.cols != H ||
+            w.shared.down.rows != H || w.shared.down.cols != Is)
+            return R::failure(ErrorCode::invalid_mxfp4);
+        std::unordered_set<std::uint64_t> tensors;
+        const auto fresh = [&tensors](std::uint64_t id) { return id && tensors.insert(id).second; };
+        if (!fresh(w.routed_down.tensor_id) || !fresh(w.routed_norm.tensor_id) || !fresh(w.routed_up.tensor_id) ||
+            !fresh(w.shared.gate.tensor_id) || !fresh(w.shared.up.tensor_id) || !fresh(w.shared.down.tensor_id))
+            return R::failure(ErrorCode::invalid_mxfp4);
+        std::unordered_set<std::uint32_t> selected;
+        double sum = 0.0;
+        for (std::size_t k = 0; k < experts.size(); ++k) {
+            const auto& e = experts[k];
+            if (!selected.insert(ids[k]).second || contributions[k] <= 0.0F || !valid_matrix(e.gate, I, D) ||
+                !valid_matrix(e.up, I, D) || !valid_matrix(e.down, Dout, I) || !fresh(e.gate.tensor_id) ||
+                !fresh(e.up.tensor_id) || !fresh(e.down.tensor_id))
+                return R::failure(ErrorCode::invalid_mxfp4);
+            sum += contributions[k];
+        }
+        if (std::abs(sum - 1.0) > 1.0e-5) return R::failure(ErrorCode::invalid_mxfp4);
+        // this library's shapes: expert output width = latent width, bf16
+        // linears over multiples of 8, MXFP4 groups of 32, at most 64 slots
+        if (Dout != D || H % 8 || D % 32 || I % 32 || experts.size() > 64) {
+            if (!rest_) return unavailable<OfficialMoeFfnResult>("official MoE FFN shape is not on the B200 path");
+            return rest_->official_mxfp4_moe_ffn(hidden, prefix, w, experts, ids, contributions, epsilon, beta,
+                                                 linear, layer, phase);
+        }
+        ErrorCode st = ErrorCode::ok;
+        const auto bf16 = [&](std::uint64_t id, std::span<const std::uint16_t> v, std::size_t rows,
+                              std::size_t cols) {
+            return static_cast<const std::uint16_t*>(
+                resident(id, K3XB_WEIGHT_BF16, rows, cols, v.data(), v.size() * 2, &st));
+        };
+        k3xb_moe_layer tail{};
+        tail.hidden = static_cast<std::uint32_t>(H);
+        tail.latent = static_cast<std::uint32_t>(D);
+        tail.shared_inter = static_cast<std::uint32_t>(Is);
+        tail.routed_down = bf16(w.routed_down.tensor_id, w.routed_down.values, D, H);
+        tail.routed_norm = bf16(w.routed_norm.tensor_id, w.routed_norm.values, 1, D);
+        tail.routed_up = bf16(w.routed_up.tensor_id, w.routed_up.values, H, D);
+        tail.shared_gate = bf16(w.shared.gate.tensor_id, w.shared.gate.values, Is, H);
+        tail.shared_up = bf16(w.shared.up.tensor_id, w.shared.up.values, Is, H);
+        tail.shared_down = bf16(w.shared.down.tensor_id, w.shared.down.values, H, Is);
+        if (st != ErrorCode::ok) return R::failure(st, last_error());
+        tail.activation = K3XB_ACT_SITU;
+        tail.situ_beta = beta;
+        tail.situ_linear_beta = linear ? *linear : 0.0F;
+        tail.latent_eps = epsilon;
+        std::vector<k3xb_moe_layer> slots(experts.size());
+        for (std::size_t k = 0; k < experts.size(); ++k)
+            if ((st = expert_of(experts[k], D, I, &slots[k])) != ErrorCode::ok) return R::failure(st, last_error());
+        tail.engine = slots.front().engine;
+        std::vector<float> out(H);
+        const int rc = k3xb_official_moe_ffn_host(ctx_, &tail, slots.data(), static_cast<std::uint32_t>(slots.size()),
+                                                  contributions.data(), hidden.data(), prefix.data(), out.data());
+        if (rc != K3XB_OK) return R::failure(static_cast<ErrorCode>(rc), last_error());
+        ++moe_calls_;
+        return R::success({true, std::move(out), {ids.begin(), ids.end()}});
     }
 
     // ---- expert FFNs on tcgen05 (k3xb_expert_grid_host) --------------------
@@ -341,6 +419,7 @@ public:
                         conv.begin() + static_cast<std::ptrdiff_t>(2 * hist));
         r.conv_v.assign(conv.begin() + static_cast<std::ptrdiff_t>(2 * hist), conv.end());
         r.executed = true;
+        r.state_published = true;   // host round trip: the new state is the caller's (backend_cuda.cu:2578-2580)
         ++kda_calls_;
         return Result<OfficialKdaCudaResult>::success(std::move(r));
     }
@@ -411,11 +490,43 @@ private:
         return ErrorCode::ok;
     }
 
-    // y [tokens][H] of one expert (gate/up, SiTU, down on tcgen05).
+    // One expert as a one-expert layer: a resident stack on the tcgen05
+    // engine where its dims are multiples of 128, else its three matrices
+    // resident one by one on the CUDA-core engine (any multiple of 32).
+    ErrorCode expert_of(const Mxfp4MlpView& e, std::size_t H, std::size_t I, k3xb_moe_layer* L) {
+        if (H % 128 == 0 && I % 128 == 0) return stack_of(e, H, I, L);
+        if (H % 32 || I % 32) return ErrorCode::backend_unavailable;
+        k3xb_resident g{}, u{}, d{};
+        const auto take = [this](const Mxfp4WeightView& w, k3xb_resident* r) {
+            const int rc = k3xb_acquire_weight(ctx_, w.tensor_id, K3XB_WEIGHT_MXFP4, w.rows, w.cols, 32,
+                                               w.packed.data(), w.packed.size(), w.scales.data(), w.scales.size(), r);
+            if (rc != K3XB_OK) return static_cast<ErrorCode>(rc);
+            return r->disposition == K3XB_RESIDENT_BYPASS ? ErrorCode::backend_unavailable : ErrorCode::ok;
+        };
+        ErrorCode st = take(e.gate, &g);
+        if (st == ErrorCode::ok) st = take(e.up, &u);
+        if (st == ErrorCode::ok) st = take(e.down, &d);
+        if (st != ErrorCode::ok) return st;
+        *L = k3xb_moe_layer{};
+        L->hidden = static_cast<std::uint32_t>(H);
+        L->inter = static_cast<std::uint32_t>(I);
+        L->experts = 1;
+        L->top_k = 1;
+        L->gate_packed = static_cast<const std::uint8_t*>(g.primary);
+        L->gate_scales = static_cast<const std::uint8_t*>(g.secondary);
+        L->up_packed = static_cast<const std::uint8_t*>(u.primary);
+        L->up_scales = static_cast<const std::uint8_t*>(u.secondary);
+        L->down_packed = static_cast<const std::uint8_t*>(d.primary);
+        L->down_scales = static_cast<const std::uint8_t*>(d.secondary);
+        L->engine = K3XB_ENGINE_SIMT;
+        return ErrorCode::ok;
+    }
+
+    // y [tokens][H] of one expert (gate/up, SiTU, down).
     Result<std::vector<float>> run_expert(const Mxfp4MlpView& e, std::size_t H, std::size_t I, const float* x,
                                           std::size_t tokens, float beta, std::optional<float> linear) {
         k3xb_moe_layer L{};
-        if (auto st = stack_of(e, H, I, &L); st != ErrorCode::ok)
+        if (auto st = expert_of(e, H, I, &L); st != ErrorCode::ok)
             return Result<std::vector<float>>::failure(st, last_error());
         L.activation = K3XB_ACT_SITU;
         L.situ_beta = beta;

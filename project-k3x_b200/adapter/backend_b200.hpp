@@ -13,6 +13,11 @@
 // On the B200:
 //   mxfp4_situ_mlp_group / _batch / _grid, mxfp4_situ_moe and their
 //   prefetch / _prepared forms  -> k3xb_acquire_expert_stack + k3xb_expert_grid_host
+//                                  (dims not multiples of 128: single resident
+//                                  MXFP4 weights on the CUDA-core engine)
+//   official_mxfp4_moe_ffn (the LatentMoE FFN of one position, its route
+//   given; the call official_layer_cuda makes with host route preparation)
+//                                -> k3xb_acquire_weight / _expert_stack + k3xb_official_moe_ffn_host
 //   official_kda (host-roundtrip state)  -> k3xb_acquire_weight + k3xb_kda_block_host
 // Weights are uploaded once, keyed by tensor id (BackendOptions::
 // cuda_resident_bytes bounds them when cuda_weights is resident).

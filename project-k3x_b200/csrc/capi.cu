@@ -516,6 +516,156 @@ int k3xb_expert_grid_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer, const uint
     return k3xb_sync(ctx);
 }
 
+int k3xb_official_moe_ffn_host(k3xb_ctx* ctx, const k3xb_moe_layer* tail, const k3xb_moe_layer* slots, uint32_t K,
+                               const float* contributions_host, const float* hidden_host, const float* prefix_host,
+                               float* out_host) {
+    K3XB_ENTER(ctx);
+    if (!tail || !slots || !K || K > 64 || !contributions_host || !hidden_host || !prefix_host || !out_host)
+        return fail(ctx, K3XB_INVALID_EXTENT, "official moe ffn arguments (1 <= slots <= 64)");
+    const k3xb_moe_layer& W = *tail;
+    const uint32_t H = W.hidden, D = W.latent, Is = W.shared_gate ? W.shared_inter : 0;
+    if (!H || !D || H % 8 || D % 32 || !W.routed_down || !W.routed_norm || !W.routed_up || !(W.latent_eps > 0.0f))
+        return fail(ctx, K3XB_INVALID_EXTENT, "official moe ffn: latent projections (hidden % 8, latent % 32)");
+    if (W.shared_gate && (!W.shared_up || !W.shared_down || !Is))
+        return fail(ctx, K3XB_INVALID_EXTENT, "official moe ffn: incomplete shared expert");
+    if (W.activation != K3XB_ACT_SWIGLU && W.activation != K3XB_ACT_SITU)
+        return fail(ctx, K3XB_INVALID_STATE, "unknown activation");
+    if (W.activation == K3XB_ACT_SITU && !(W.situ_beta > 0.0f))
+        return fail(ctx, K3XB_INVALID_STATE, "SiTU beta must be positive");
+    // every slot: one expert of the latent width, the tail's activation
+    const uint32_t I = slots[0].inter;
+    const int engine = slots[0].engine;
+    for (uint32_t k = 0; k < K; ++k) {
+        const k3xb_moe_layer& e = slots[k];
+        const uint32_t width = e.latent ? e.latent : e.hidden;   // the expert's input width
+        if (e.experts != 1 || width != D || e.inter != I || !I || I % 32 || e.engine != engine ||
+            !e.gate_packed || !e.gate_scales || !e.up_packed || !e.up_scales || !e.down_packed || !e.down_scales)
+            return fail(ctx, K3XB_INVALID_MXFP4,
+                        "official moe ffn: each slot one expert of the latent width, one inter, one engine");
+        if (engine == K3XB_ENGINE_MXF4 && (!e.gate_scales_tc || !e.up_scales_tc || !e.down_scales_tc))
+            return fail(ctx, K3XB_INVALID_MXFP4, "official moe ffn: the tcgen05 engine needs the *_scales_tc copies");
+    }
+    if (engine != K3XB_ENGINE_SIMT && engine != K3XB_ENGINE_MXF4)
+        return fail(ctx, K3XB_INVALID_STATE, "unknown expert engine");
+    k3xb_moe_layer E1 = slots[0];   // the per-slot view the engines run
+    E1.hidden = D;
+    E1.top_k = 1;
+    E1.latent = 0;
+    E1.shared_gate = E1.shared_up = E1.shared_down = nullptr;
+    E1.shared_inter = 0;
+    E1.activation = W.activation;
+    E1.situ_beta = W.situ_beta;
+    E1.situ_linear_beta = W.situ_linear_beta;
+
+    const size_t HD = H > D ? H : D;
+    Sizer sz;
+    sz.take<float>(2 * size_t(H) + K);            // hidden, prefix, contributions (one upload)
+    sz.take<uint32_t>(2);                         // the one-token plan's route: expert 0, contribution 1
+    sz.take<float>(D);                            // latent
+    sz.take<uint16_t>(2 * HD);                    // linear input terms
+    sz.take<float>(size_t(K) * D);                // slot outputs
+    for (int i = 0; i < 2; ++i) sz.take<float>(D);            // mixed, normed
+    for (int i = 0; i < 3; ++i) sz.take<float>(H);            // routed, shared, combined
+    for (int i = 0; i < 3; ++i) sz.take<float>(Is ? Is : 1);  // shared gate, up, activation
+    sz.take<float>(H);                            // out
+    for (int i = 0; i < 2; ++i) sz.take<uint32_t>(2);         // plan groups
+    for (int i = 0; i < 4; ++i) sz.take<uint32_t>(1);         // plan assignments, group count
+    sz.take<float>(I);                            // SIMT activations
+    sz.used += mxf4_scratch_bytes(E1, 1) + 1024;
+    void* base;
+    int st;
+    if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
+    Carver c(base);
+    float* in = c.take<float>(2 * size_t(H) + K);
+    float *hidden = in, *prefix = in + H, *contrib = in + 2 * size_t(H);
+    uint32_t* route1 = c.take<uint32_t>(2);
+    float* lat = c.take<float>(D);
+    uint16_t* xt = c.take<uint16_t>(2 * HD);
+    float* slot_out = c.take<float>(size_t(K) * D);
+    float* mixed = c.take<float>(D);
+    float* normed = c.take<float>(D);
+    float* routed = c.take<float>(H);
+    float* shared = c.take<float>(H);
+    float* combined = c.take<float>(H);
+    float* sg = c.take<float>(Is ? Is : 1);
+    float* su = c.take<float>(Is ? Is : 1);
+    float* sa = c.take<float>(Is ? Is : 1);
+    float* out = c.take<float>(H);
+    k3xb_plan plan{};
+    plan.group_expert = c.take<uint32_t>(2);
+    plan.group_offset = c.take<uint32_t>(2);
+    plan.assign_token = c.take<uint32_t>(1);
+    plan.assign_slot = c.take<uint32_t>(1);
+    plan.assign_contrib = c.take<float>(1);
+    plan.group_count = c.take<uint32_t>(1);
+    plan.status = ctx->status_word;
+    float* act = c.take<float>(I);
+    set_mxf4_scratch(ctx, reinterpret_cast<char*>(base) + c.used);
+
+    // official_moe_ffn inputs: hidden and prefix of one position, the route's contributions
+    const size_t hbytes = sizeof(float) * H;
+    K3XB_CUDA(ctx, cudaMemcpyAsync(hidden, hidden_host, hbytes, cudaMemcpyHostToDevice, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(prefix, prefix_host, hbytes, cudaMemcpyHostToDevice, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(contrib, contributions_host, sizeof(float) * K, cudaMemcpyHostToDevice,
+                                   ctx->stream));
+    const uint32_t one_route[2] = {0u, 0x3f800000u};   // expert 0, contribution 1.0f
+    K3XB_CUDA(ctx, cudaMemcpyAsync(route1, one_route, sizeof one_route, cudaMemcpyHostToDevice, ctx->stream));
+    ctx->stats.h2d_bytes += 2 * hbytes + sizeof(float) * K + sizeof one_route;
+
+    // backend_cuda.cu:4036-4106 in this library's arithmetic (official_moe.cpp:296-341)
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_LATENT);   // :296 latent = bf16_matvec(hidden, routed_down)
+        if ((st = launch_linear_bf16(ctx, hidden, W.routed_down, 1, D, H, 1, xt, lat))) return st;
+    }
+    if ((st = launch_plan(ctx, route1, reinterpret_cast<const float*>(route1 + 1), 1, 1, 1, plan))) return st;
+    for (uint32_t k = 0; k < K; ++k) {   // slot k's expert, its output unweighted in slot k
+        k3xb_moe_layer Ek = E1;
+        Ek.gate_packed = slots[k].gate_packed;
+        Ek.gate_scales = slots[k].gate_scales;
+        Ek.up_packed = slots[k].up_packed;
+        Ek.up_scales = slots[k].up_scales;
+        Ek.down_packed = slots[k].down_packed;
+        Ek.down_scales = slots[k].down_scales;
+        Ek.gate_scales_tc = slots[k].gate_scales_tc;
+        Ek.up_scales_tc = slots[k].up_scales_tc;
+        Ek.down_scales_tc = slots[k].down_scales_tc;
+        float* yk = slot_out + size_t(k) * D;
+        if (engine == K3XB_ENGINE_SIMT) {
+            PhaseScope ph(ctx, K3XB_PHASE_EXPERT_GATEUP);
+            st = launch_simt_experts(ctx, Ek, lat, 1, plan, act, yk);
+        } else {
+            st = launch_mxf4_experts(ctx, Ek, lat, 1, plan, yk);
+        }
+        if (st) return st;
+    }
+    {   // :313-322 mixed = round_bf16(slot-ordered combine)
+        PhaseScope ph(ctx, K3XB_PHASE_COMBINE);
+        if ((st = launch_combine(ctx, slot_out, contrib, nullptr, 1, K, D, mixed))) return st;
+    }
+    {   // :323-331 routed = bf16_matvec(normalized(mixed, routed_norm), routed_up)
+        PhaseScope ph(ctx, K3XB_PHASE_LATENT);
+        if ((st = launch_rms_norm(ctx, mixed, W.routed_norm, 1, D, W.latent_eps, normed))) return st;
+        if ((st = launch_linear_bf16(ctx, normed, W.routed_up, 1, H, D, 1, xt, routed))) return st;
+    }
+    if (Is) {   // :332-335 the shared expert on the hidden row
+        PhaseScope ph(ctx, K3XB_PHASE_SHARED);
+        if ((st = launch_bf16_rows(ctx, hidden, W.shared_gate, 1, Is, H, sg))) return st;
+        if ((st = launch_bf16_rows(ctx, hidden, W.shared_up, 1, Is, H, su))) return st;
+        if ((st = launch_act(ctx, sg, su, Is, W.activation, W.situ_beta, W.situ_linear_beta, sa))) return st;
+        if ((st = launch_bf16_rows(ctx, sa, W.shared_down, 1, H, Is, shared))) return st;
+        st = launch_residual(ctx, routed, shared, H, combined);   // :336 round_bf16(routed + shared)
+    } else {
+        st = launch_residual_round(ctx, routed, H, combined);
+    }
+    if (st) return st;
+    // :337-341 out = round_bf16(round_bf16(prefix) + combined)
+    if ((st = launch_residual(ctx, prefix, combined, H, out))) return st;
+    K3XB_CUDA(ctx, cudaMemcpyAsync(out_host, out, hbytes, cudaMemcpyDeviceToHost, ctx->stream));
+    ctx->stats.d2h_bytes += hbytes;
+    ++ctx->stats.moe_layer_calls;
+    return k3xb_sync(ctx);
+}
+
 // ---- KDA -------------------------------------------------------------------
 
 namespace {

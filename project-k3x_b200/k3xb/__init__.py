@@ -200,6 +200,7 @@ def library() -> C.CDLL:
                                           C.POINTER(ResidentStack)],
             "k3xb_release_resident": [vp],
             "k3xb_expert_grid_host": [vp, C.POINTER(MoeLayer), vp, u32, vp, u32, vp],
+            "k3xb_official_moe_ffn_host": [vp, C.POINTER(MoeLayer), C.POINTER(MoeLayer), u32, vp, vp, vp, vp],
             "k3xb_set_profiling": [vp, C.c_int],
             "k3xb_get_profile": [vp, C.POINTER(PhaseTime), C.POINTER(u64)],
             "k3xb_kda_block_host": [vp, C.POINTER(KdaLayer), u32, vp, u32, vp, vp, vp],
@@ -520,6 +521,22 @@ class Context:
 
     def release_resident(self):
         self._check(self.lib.k3xb_release_resident(self.h), "release_resident")
+
+    def official_moe_ffn_host(self, tail: MoeLayer, slots, contributions, hidden, prefix):
+        """official_mxfp4_moe_ffn for one position (k3xb_official_moe_ffn_host):
+        `slots` is a list of one-expert MoeLayer descriptors in route order;
+        HOST contributions [K], hidden [H], prefix [H] -> HOST out [H]."""
+        import numpy as np
+        K = len(slots)
+        arr = (MoeLayer * K)(*slots)
+        con = np.ascontiguousarray(contributions, dtype=np.float32)
+        x = np.ascontiguousarray(hidden, dtype=np.float32)
+        p = np.ascontiguousarray(prefix, dtype=np.float32)
+        out = np.empty_like(x)
+        self._check(self.lib.k3xb_official_moe_ffn_host(self.h, C.byref(tail), arr, K, con.ctypes.data,
+                                                        x.ctypes.data, p.ctypes.data, out.ctypes.data),
+                    "official_moe_ffn_host")
+        return out
 
     def prepare_layer_scales(self, w: dict):
         """Adds tcgen05-layout copies of the three expert scale arrays to a

@@ -102,6 +102,14 @@ public:
         ++calls;
         return Result<std::vector<float>>::success({});
     }
+    Result<OfficialMoeFfnResult> official_mxfp4_moe_ffn(std::span<const float>, std::span<const float>,
+                                                        OfficialMoeFfnView, std::span<const Mxfp4MlpView>,
+                                                        std::span<const std::uint32_t> ids, std::span<const float>,
+                                                        float, float, std::optional<float>, std::uint32_t,
+                                                        ProfilePhase) override {
+        ++calls;
+        return Result<OfficialMoeFfnResult>::success({true, {8.0F}, {ids.begin(), ids.end()}});
+    }
     Result<OfficialKdaCudaResult> official_kda(std::span<const float>, OfficialKdaCudaView,
                                                OfficialKdaCudaStateView, OfficialKdaCudaConfig, std::uint32_t,
                                                ProfilePhase, OfficialKdaStateControl) override {
@@ -207,11 +215,11 @@ int argument_checks() {
     g.view.down.group_size = 16;
     CHECK(b->mxfp4_situ_mlp_group(x, std::vector<Mxfp4MlpView>{g.view}, 1.0F, std::nullopt, 0, P).error() ==
           ErrorCode::invalid_mxfp4);
-    // shapes the tcgen05 tiles cannot take: backend_unavailable, before any device call
+    // shapes the tcgen05 tiles cannot take run on the CUDA-core engine: the call reaches the C ABI
     ExpertBuffers h(96, 128, 40);
     const std::vector<float> x96(96, 1.0F);
     CHECK(b->mxfp4_situ_mlp_group(x96, std::vector<Mxfp4MlpView>{h.view}, 1.0F, std::nullopt, 0, P).error() ==
-          ErrorCode::backend_unavailable);
+          ErrorCode::invalid_extent);
     // prefetch tokens
     CHECK(b->mxfp4_situ_mlp_group_prepared(x, Mxfp4PrefetchToken{99, 0}, 1.0F, std::nullopt, 0, P).error() ==
           ErrorCode::invalid_state);
@@ -233,10 +241,87 @@ int argument_checks() {
     return 0;
 }
 
+// The official LatentMoE FFN's views: H hidden, D latent (= the experts'
+// width and output width unless `dout` differs), I expert inter, S shared.
+struct OfficialFfn {
+    std::vector<std::uint16_t> down, norm, up, sg, su, sd;
+    ExpertBuffers e1, e2;
+    OfficialMoeFfnView view{};
+    std::vector<Mxfp4MlpView> experts;
+    OfficialFfn(std::size_t H, std::size_t D, std::size_t I, std::size_t S)
+        : down(D * H), norm(D), up(H * D), sg(S * H), su(S * H), sd(H * S), e1(D, I, 200), e2(D, I, 210) {
+        view.routed_down = {down, D, H, 100};
+        view.routed_norm = {norm, 101};
+        view.routed_up = {up, H, D, 102};
+        view.shared = {{sg, S, H, 103}, {su, S, H, 104}, {sd, H, S, 105}};
+        experts = {e1.view, e2.view};
+    }
+};
+
+int official_ffn() {
+    const auto P = ProfilePhase::decode;
+    const std::vector<float> x(128, 0.5F), prefix(128, 0.25F), c{0.75F, 0.25F};
+    const std::vector<std::uint32_t> ids{3, 9};
+    BackendOptions o{};
+    {   // on the path: reaches the C ABI (NULL context -> invalid_extent), never the other backend
+        auto rest = std::make_unique<FakeRest>();
+        FakeRest* fake = rest.get();
+        auto b = wrap_b200_context(o, nullptr, std::move(rest));
+        OfficialFfn f(128, 128, 128, 128);
+        auto r = b->official_mxfp4_moe_ffn(x, prefix, f.view, f.experts, ids, c, 1e-6F, 1.0F, std::nullopt, 0, P);
+        CHECK(!r && r.error() == ErrorCode::invalid_extent && fake->calls == 0);
+        // latent 96 (a multiple of 32, not of 128): the CUDA-core engine, still the C ABI
+        OfficialFfn g(128, 96, 64, 128);
+        r = b->official_mxfp4_moe_ffn(x, prefix, g.view, g.experts, ids, c, 1e-6F, 1.0F, std::nullopt, 0, P);
+        CHECK(!r && r.error() == ErrorCode::invalid_extent && fake->calls == 0);
+        // hidden not a multiple of 8: not this library's shape, so the other backend
+        const std::vector<float> x12(12, 0.5F), p12(12, 0.25F);
+        OfficialFfn h(12, 32, 32, 32);
+        r = b->official_mxfp4_moe_ffn(x12, p12, h.view, h.experts, ids, c, 1e-6F, 1.0F, std::nullopt, 0, P);
+        CHECK(r && r.value().output.size() == 1 && r.value().selected_expert_ids == ids && fake->calls == 1);
+    }
+    auto b = wrap_b200_context(o, nullptr);
+    OfficialFfn f(128, 128, 128, 128);
+    const auto call = [&](std::span<const float> hx, std::span<const float> px, const OfficialMoeFfnView& v,
+                          std::span<const Mxfp4MlpView> ex, std::span<const std::uint32_t> ix,
+                          std::span<const float> cx, float eps = 1e-6F) {
+        return b->official_mxfp4_moe_ffn(hx, px, v, ex, ix, cx, eps, 1.0F, std::nullopt, 0, P).error();
+    };
+    // the reference's checks (backend_cuda.cu:3770-3875): all invalid_mxfp4
+    CHECK(call(x, std::span<const float>(prefix).first(64), f.view, f.experts, ids, c) == ErrorCode::invalid_mxfp4);
+    CHECK(call(x, prefix, f.view, f.experts, std::span<const std::uint32_t>(ids).first(1), c) ==
+          ErrorCode::invalid_mxfp4);
+    CHECK(call(x, prefix, f.view, f.experts, ids, c, 0.0F) == ErrorCode::invalid_mxfp4);
+    const std::vector<std::uint32_t> same{3, 3};
+    CHECK(call(x, prefix, f.view, f.experts, same, c) == ErrorCode::invalid_mxfp4);       // repeated expert
+    const std::vector<float> neg{1.25F, -0.25F}, off{0.5F, 0.25F};
+    CHECK(call(x, prefix, f.view, f.experts, ids, neg) == ErrorCode::invalid_mxfp4);      // contribution <= 0
+    CHECK(call(x, prefix, f.view, f.experts, ids, off) == ErrorCode::invalid_mxfp4);      // sum != 1
+    OfficialMoeFfnView shared_id = f.view;
+    shared_id.shared.up.tensor_id = 100;                                                // a tensor id twice
+    CHECK(call(x, prefix, shared_id, f.experts, ids, c) == ErrorCode::invalid_mxfp4);
+    OfficialMoeFfnView narrow = f.view;
+    narrow.routed_norm.values = std::span<const std::uint16_t>(f.norm).first(64);       // routed width
+    CHECK(call(x, prefix, narrow, f.experts, ids, c) == ErrorCode::invalid_mxfp4);
+    // a routed width other than the latent width is not this library's shape
+    OfficialFfn w(128, 128, 128, 128);
+    const std::vector<std::uint16_t> norm64(64), up64(128 * 64);
+    ExpertBuffers n1(128, 128, 320), n2(128, 128, 330);
+    std::vector<std::byte> dp1(64 * 128 / 2), ds1(64 * 128 / 32), dp2(64 * 128 / 2), ds2(64 * 128 / 32);
+    n1.view.down = {322, dp1, ds1, 64, 128, 32};
+    n2.view.down = {332, dp2, ds2, 64, 128, 32};
+    OfficialMoeFfnView v64 = w.view;
+    v64.routed_norm = {norm64, 101};
+    v64.routed_up = {up64, 128, 64, 102};
+    const std::vector<Mxfp4MlpView> e64{n1.view, n2.view};
+    CHECK(call(x, prefix, v64, e64, ids, c) == ErrorCode::backend_unavailable);
+    return 0;
+}
+
 }  // namespace
 
 int main() {
-    if (factory() || split_and_forwarding() || no_rest() || argument_checks()) return 1;
+    if (factory() || split_and_forwarding() || no_rest() || argument_checks() || official_ffn()) return 1;
     std::printf("backend adapter ok\n");
     return 0;
 }

@@ -47,3 +47,27 @@ def test_backend_adapter_against_reference_interface(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert out.returncode == 0, out.stderr
     assert out.stdout.startswith("backend adapter ok"), out.stdout
+
+
+def test_reference_layer_driver_harness_loads_and_reports_no_gpu():
+    """oracle/_ref/libk3x_ref_b200.so (the reference's official_layer_cuda
+    over B200Backend) resolves every symbol, marshals a real layer, and
+    without a B200 ends in make_b200_backend's status, BACKEND_UNAVAILABLE
+    (the GPU test runs it to completion)."""
+    import numpy as np
+    import torch
+
+    import golden_util as gu
+    from oracle import OracleError, ReferenceOnB200, have_reference_on_b200
+    if not have_reference_on_b200():
+        if reference_include():
+            pytest.fail("oracle/_ref/libk3x_ref_b200.so is not built (make -C oracle after libk3xb.so)")
+        pytest.skip("reference tree absent and no prebuilt harness")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present: tests/test_gpu_latent.py runs the harness")
+    layer, f = gu.official_layer()
+    with pytest.raises(OracleError) as e:
+        ReferenceOnB200().official_layer(layer, f["hidden"], f["block"], (f["conv_q"], f["conv_k"], f["conv_v"]),
+                                         f["recurrent"])
+    assert e.value.status == 17, str(e.value)
+    assert np.isfinite(f["hidden"]).all()

@@ -139,3 +139,71 @@ def test_official_layer_latent_golden(rs):
     for i, key in enumerate(("next_conv_q", "next_conv_k", "next_conv_v")):
         assert_mostly_close(words(co[i]), words(f[key]), what=key)
     assert_mostly_close(rec_o.cpu().numpy()[0], f["next_recurrent"], what="recurrent state")
+
+
+def _one_expert(layer, e):
+    """Expert e of a stacked layer dict as a one-expert layer dict (HOST arrays)."""
+    d = dict(layer)
+    for name in ("gate_packed", "gate_scales", "up_packed", "up_scales", "down_packed", "down_scales"):
+        d[name] = np.ascontiguousarray(layer[name][e:e + 1])
+    d["experts"], d["top_k"] = 1, 1
+    return d
+
+
+@pytest.mark.parametrize("engine", ["mxf4", "simt"])
+def test_official_moe_ffn_one_position_equals_the_layer(rs, engine):
+    """k3xb_official_moe_ffn_host (official_mxfp4_moe_ffn: one position, the
+    route given, each slot its own one-expert stack) equals the layer path
+    with the prefix residual bit for bit (same kernels, same order), and so
+    the reference's official_moe_cpu output within the bars above."""
+    import k3xb
+    torch = torch_cuda()
+    layer, f = gu.latent_moe()
+    layer["latent_eps"] = float(f["eps"])
+    hidden = _prepared(rs, f)
+    eng = k3xb.ENGINE_MXF4 if engine == "mxf4" else k3xb.ENGINE_SIMT
+    ctx = k3xb.Context(0)
+    ctx.use_stream()
+    try:
+        out, ids, con = _forward(torch, ctx, layer, hidden, eng)
+        want = rs.round_bf16(rs.round_bf16(f["prefix"]) + out)
+        dl = layer_to_dev(torch, layer)   # kept alive: descriptors hold raw pointers
+        tail = k3xb.moe_layer_desc(dl, engine=eng)
+        keep = []
+        for t in range(hidden.shape[0]):
+            slots = []
+            for e in f["ids"][t]:
+                d = layer_to_dev(torch, _one_expert(layer, int(e)))
+                if eng == k3xb.ENGINE_MXF4:
+                    ctx.prepare_layer_scales(d)
+                keep.append(d)
+                slots.append(k3xb.moe_layer_desc(d, engine=eng))
+            got = ctx.official_moe_ffn_host(tail, slots, f["contributions"][t], hidden[t], f["prefix"][t])
+            np.testing.assert_array_equal(got, want[t])
+            assert_mostly_close(got, f["out"][t], what=f"official moe ffn ({engine}), position {t}")
+    finally:
+        ctx.close()
+
+
+def test_reference_layer_driver_on_the_b200_backend():
+    """The drop-in, whole-layer: the reference's own official_layer_cuda
+    (official_layer.cpp:246-500, host route preparation), unchanged, drives
+    this library's ComputeBackend (B200Backend: official_kda on
+    k3xb_kda_block_host, official_mxfp4_moe_ffn on
+    k3xb_official_moe_ffn_host) through oracle/_ref/libk3x_ref_b200.so,
+    against the golden official_layer_cpu output with the bars of the test
+    above; the final KDA state as well."""
+    from oracle import ReferenceOnB200, have_reference_on_b200
+    if not have_reference_on_b200():
+        pytest.fail("oracle/_ref/libk3x_ref_b200.so is not built (oracle/Makefile, with the reference tree)")
+    layer, f = gu.official_layer()
+    T = f["hidden"].shape[0]
+    out, ids, state = ReferenceOnB200().official_layer(layer, f["hidden"], f["block"],
+                                                       (f["conv_q"], f["conv_k"], f["conv_v"]), f["recurrent"])
+    same = np.all(ids == f["ids"], axis=1)
+    assert same.sum() >= T - 1, f"routes agree on {same.sum()}/{T} positions"
+    assert_mostly_close(out[same], f["out"][same], what="official_layer_cuda on B200Backend")
+    words = lambda a: (np.asarray(a, np.uint16).astype(np.uint32) << 16).view(np.float32)
+    for got, key in zip(state[:3], ("next_conv_q", "next_conv_k", "next_conv_v")):
+        assert_mostly_close(words(got), words(f[key]), what=key)
+    assert_mostly_close(state[3].reshape(f["next_recurrent"].shape), f["next_recurrent"], what="recurrent state")
