@@ -43,7 +43,12 @@ def _free_port():
 def _watch_rank(rank, world, port, out_dir, mode, steps, timeout_s):
     from k3xb.peers import PeerLost, PeerWatch, make_store
 
-    store = make_store(rank, world, port=port, timeout_s=30)
+    from datetime import timedelta
+    store = make_store(rank, world, port=port, timeout_s=120)
+    # every rank up before the bounded steps: a process that is still
+    # importing torch is slow to start, not gone
+    store.set(f"ready/{rank}", b"1")
+    store.wait([f"ready/{g}" for g in range(world)], timedelta(seconds=120))
     watch = PeerWatch(store, rank, world, timeout_s=timeout_s)
     result = "ok"
     t0 = time.monotonic()
@@ -61,7 +66,12 @@ def _watch_rank(rank, world, port, out_dir, mode, steps, timeout_s):
         result = f"lost step={e.step} missing={e.missing} departed={e.departed}"
     elapsed = time.monotonic() - t0
     open(os.path.join(out_dir, f"r{rank}.txt"), "w").write(f"{result}\n{elapsed:.3f}")
-    if rank == 0:   # the store's server outlives the other ranks' last use of it
+    # the store's server (rank 0) outlives the other ranks' last use of it
+    if mode == "healthy":
+        store.set(f"done/{rank}", b"1")
+        if rank == 0:
+            store.wait([f"done/{g}" for g in range(world)], timedelta(seconds=120))
+    elif rank == 0:
         time.sleep(0.2)
 
 
