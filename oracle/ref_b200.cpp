@@ -10,8 +10,10 @@
 // against libk3xb.so, into oracle/_ref/libk3x_ref_b200.so. It shows the
 // drop-in: the reference's caller, unchanged, runs a whole official layer
 // with its KDA block (official_kda, host-roundtrip state) and its LatentMoE
-// FFN (official_mxfp4_moe_ffn, host route preparation) on the B200. The
-// GPU test compares the result with official_layer_cpu's golden output.
+// FFN on the B200: official_mxfp4_moe_ffn after host route preparation, or
+// prepare_official_moe_route + official_mxfp4_moe_ffn_prepared after device
+// route preparation. The GPU test compares the result with
+// official_layer_cpu's golden output.
 // Nothing here is reference source: it only marshals plain C arrays into
 // the reference's C++ API and back.
 #include "k3x/official_layer.hpp"
@@ -43,10 +45,11 @@ extern "C" {
 
 // official_layer_cuda(B200Backend) over T positions of one layer with a
 // LatentMoE (SwiGLU: situ_glu with beta 2^64, no linear bound), the
-// arguments of k3xr_official_layer plus the device. The KDA state arrays are
+// arguments of k3xr_official_layer plus the device and the route
+// preparation (0 host, 1 device). The KDA state arrays are
 // updated in place; out [T][H] and ids [T][top_k]. Returns the k3x::ErrorCode
 // value; err receives the message.
-int k3xr_official_layer_b200(int device, const k3xr_kda_weights* kw, const k3xr_moe_layer* mw,
+int k3xr_official_layer_b200(int device, int device_route, const k3xr_kda_weights* kw, const k3xr_moe_layer* mw,
                              const std::uint16_t* self_residual_norm, const std::uint16_t* self_residual_proj,
                              const std::uint16_t* input_norm, const std::uint16_t* moe_residual_norm,
                              const std::uint16_t* moe_residual_proj, const std::uint16_t* post_norm, float eps,
@@ -122,7 +125,9 @@ int k3xr_official_layer_b200(int device, const k3xr_kda_weights* kw, const k3xr_
         inputs[t] = {std::vector<float>(hidden_in + t * H, hidden_in + (t + 1) * H),
                      std::vector<float>(block + t * H, block + (t + 1) * H)};
     auto r = k3x::official_layer_cuda(backend, inputs, w, state, config, mw->top_k, 0x1p64F, std::nullopt, 0,
-                                      k3x::ProfilePhase::decode, {}, k3x::OfficialMoeRoutePreparationMode::host);
+                                      k3x::ProfilePhase::decode, {},
+                                      device_route ? k3x::OfficialMoeRoutePreparationMode::device
+                                                   : k3x::OfficialMoeRoutePreparationMode::host);
     if (!r) {
         message(err, err_len, r.message());
         return static_cast<int>(r.error());

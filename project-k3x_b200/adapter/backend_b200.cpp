@@ -2,6 +2,7 @@
 // libk3xb (see backend_b200.hpp for the method split).
 #include "backend_b200.hpp"
 
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -145,27 +146,133 @@ public:
     }
 
     // ---- the official LatentMoE FFN of one position (k3xb_official_moe_ffn_host)
-    // Checks of backend_cuda.cu:3770-3875 (same failures, invalid_mxfp4);
-    // then each bf16 projection resident by tensor id, each routed expert a
-    // resident stack of one, and the tail on the device.
+    // A direct call ends a prepared route still held (backend_cuda.cu:3724-3732).
     Result<OfficialMoeFfnResult> official_mxfp4_moe_ffn(std::span<const float> hidden, std::span<const float> prefix,
                                                         OfficialMoeFfnView w, std::span<const Mxfp4MlpView> experts,
                                                         std::span<const std::uint32_t> ids,
                                                         std::span<const float> contributions, float epsilon,
                                                         float beta, std::optional<float> linear,
                                                         std::uint32_t layer, ProfilePhase phase) override {
-        using R = Result<OfficialMoeFfnResult>;
-        const auto finite = [](std::span<const float> v) {
-            for (const float x : v)
-                if (!std::isfinite(x)) return false;
-            return true;
+        prepared_.active = false;
+        if (hidden.empty() || hidden.size() != prefix.size() || !finite(hidden) || !finite(prefix))
+            return Result<OfficialMoeFfnResult>::failure(ErrorCode::invalid_mxfp4);
+        return official_ffn(hidden, prefix, false, w, experts, ids, contributions, epsilon, beta, linear, layer,
+                            phase);
+    }
+
+    // ---- device route preparation (k3xb_prepare_moe_route_host) -----------
+    // prepare_official_moe_route with the checks of backend_cuda.cu:3478-3570
+    // (invalid_extent): the MoE input and its router logits computed on the
+    // device. The prepared input and the prefix are kept (on the host, a few
+    // KB) for the one official_mxfp4_moe_ffn_prepared that may consume them;
+    // a new preparation or a direct FFN call ends the old one.
+    Result<OfficialMoeRoutePrepareResult> prepare_official_moe_route(std::span<const float> prefix,
+                                                                     std::span<const float> block,
+                                                                     OfficialMoeRoutePrepareView w, float epsilon,
+                                                                     std::uint32_t layer, ProfilePhase) override {
+        using R = Result<OfficialMoeRoutePrepareResult>;
+        const std::size_t H = prefix.size();
+        const auto valid_bf16 = [](const Bf16WeightView& v, std::size_t rows, std::size_t cols) {
+            return v.tensor_id && v.rows == rows && v.cols == cols && rows && cols && rows <= SIZE_MAX / cols &&
+                   v.values.size() == rows * cols;
         };
+        if (!H || block.size() != H || !finite(prefix) || !finite(block) || !std::isfinite(epsilon) ||
+            epsilon <= 0.0F || !w.residual_norm.tensor_id || w.residual_norm.values.size() != H ||
+            !valid_bf16(w.residual_proj, 1, H) || !w.post_norm.tensor_id || w.post_norm.values.size() != H ||
+            !valid_bf16(w.router, w.router.rows, H))
+            return R::failure(ErrorCode::invalid_extent);
+        std::unordered_set<std::uint64_t> tensors;
+        for (const std::uint64_t id : {w.residual_norm.tensor_id, w.residual_proj.tensor_id, w.post_norm.tensor_id,
+                                       w.router.tensor_id})
+            if (!tensors.insert(id).second) return R::failure(ErrorCode::invalid_extent);
+        // bf16 words with an all-ones exponent are refused, each tensor scanned at its first use
+        const std::pair<std::uint64_t, std::span<const std::uint16_t>> scans[] = {
+            {w.residual_norm.tensor_id, w.residual_norm.values},
+            {w.residual_proj.tensor_id, w.residual_proj.values},
+            {w.post_norm.tensor_id, w.post_norm.values},
+            {w.router.tensor_id, w.router.values}};
+        for (const auto& [id, values] : scans) {
+            if (scanned_.count(id)) continue;
+            for (const std::uint16_t word : values)
+                if ((word & 0x7f80U) == 0x7f80U) return R::failure(ErrorCode::invalid_extent);
+            scanned_.insert(id);
+        }
+        ErrorCode st = ErrorCode::ok;
+        const auto bf16 = [&](std::uint64_t id, std::span<const std::uint16_t> v, std::size_t rows, std::size_t cols) {
+            return static_cast<const std::uint16_t*>(
+                resident(id, K3XB_WEIGHT_BF16, rows, cols, v.data(), v.size() * 2, &st));
+        };
+        const std::size_t E = w.router.rows;
+        const std::uint16_t* rnorm = bf16(w.residual_norm.tensor_id, w.residual_norm.values, 1, H);
+        const std::uint16_t* rproj = bf16(w.residual_proj.tensor_id, w.residual_proj.values, 1, H);
+        const std::uint16_t* post = bf16(w.post_norm.tensor_id, w.post_norm.values, 1, H);
+        const std::uint16_t* router = bf16(w.router.tensor_id, w.router.values, E, H);
+        if (st != ErrorCode::ok) return R::failure(st, last_error());
+        prepared_.active = false;
+        std::vector<float> hidden(H);
+        OfficialMoeRoutePrepareResult out;
+        out.router_logits.resize(E);
+        const int rc = k3xb_prepare_moe_route_host(ctx_, prefix.data(), block.data(), static_cast<std::uint32_t>(H),
+                                                   rnorm, rproj, post, epsilon, router, static_cast<std::uint32_t>(E),
+                                                   hidden.data(), out.router_logits.data());
+        if (rc != K3XB_OK) return R::failure(static_cast<ErrorCode>(rc), last_error());
+        if (!finite(out.router_logits)) return R::failure(ErrorCode::backend_unavailable, "non-finite router logits");
+        if (!++prepared_.generation) ++prepared_.generation;
+        prepared_.layer = layer;
+        prepared_.prefix.assign(prefix.begin(), prefix.end());
+        prepared_.hidden = std::move(hidden);
+        prepared_.active = true;
+        out.executed = true;
+        out.prepared = {owner_, prepared_.generation};
+        return R::success(std::move(out));
+    }
+
+    // Consumes the prepared route of the same layer (backend_cuda.cu:3738-3748, :3779-3784).
+    Result<OfficialMoeFfnResult> official_mxfp4_moe_ffn_prepared(OfficialMoePreparedToken token, OfficialMoeFfnView w,
+                                                                 std::span<const Mxfp4MlpView> experts,
+                                                                 std::span<const std::uint32_t> ids,
+                                                                 std::span<const float> contributions, float epsilon,
+                                                                 float beta, std::optional<float> linear,
+                                                                 std::uint32_t layer, ProfilePhase phase) override {
+        if (!prepared_.active || token.owner != owner_ || token.generation != prepared_.generation ||
+            prepared_.layer != layer)
+            return Result<OfficialMoeFfnResult>::failure(ErrorCode::invalid_mxfp4);
+        const std::vector<float> hidden = prepared_.hidden, prefix = prepared_.prefix;
+        return official_ffn(hidden, prefix, true, w, experts, ids, contributions, epsilon, beta, linear, layer,
+                            phase);
+    }
+
+    Result<bool> discard_official_moe_prepared(OfficialMoePreparedToken token) override {
+        if (!prepared_.active || token.owner != owner_ || token.generation != prepared_.generation)
+            return Result<bool>::failure(ErrorCode::invalid_state);
+        prepared_.active = false;
+        return Result<bool>::success(true);
+    }
+
+private:
+    static bool finite(std::span<const float> v) {
+        for (const float x : v)
+            if (!std::isfinite(x)) return false;
+        return true;
+    }
+
+    // Checks of backend_cuda.cu:3770-3875 (same failures, invalid_mxfp4);
+    // then each bf16 projection resident by tensor id, each routed expert a
+    // resident stack of one, and the tail on the device. `prepared`: the
+    // inputs are a prepared route's, consumed once the checks pass.
+    Result<OfficialMoeFfnResult> official_ffn(std::span<const float> hidden, std::span<const float> prefix,
+                                              bool prepared, OfficialMoeFfnView w,
+                                              std::span<const Mxfp4MlpView> experts,
+                                              std::span<const std::uint32_t> ids,
+                                              std::span<const float> contributions, float epsilon, float beta,
+                                              std::optional<float> linear, std::uint32_t layer, ProfilePhase phase) {
+        using R = Result<OfficialMoeFfnResult>;
         const auto valid_bf16 = [](const Bf16WeightView& v) {
             return v.tensor_id && v.rows && v.cols && v.rows <= SIZE_MAX / v.cols && v.values.size() == v.rows * v.cols;
         };
-        if (hidden.empty() || hidden.size() != prefix.size() || experts.empty() || experts.size() > 65535 ||
-            experts.size() != ids.size() || experts.size() != contributions.size() || !finite(hidden) ||
-            !finite(prefix) || !finite(contributions) || !std::isfinite(epsilon) || epsilon <= 0.0F ||
+        if (experts.empty() || experts.size() > 65535 ||
+            experts.size() != ids.size() || experts.size() != contributions.size() ||
+            !finite(contributions) || !std::isfinite(epsilon) || epsilon <= 0.0F ||
             !valid_activation(beta, linear) || !valid_bf16(w.routed_down) || !valid_bf16(w.routed_up) ||
             !valid_bf16(w.shared.gate) || !valid_bf16(w.shared.up) || !valid_bf16(w.shared.down) ||
             !w.routed_norm.tensor_id || w.routed_norm.values.empty())
@@ -192,10 +299,12 @@ public:
             sum += contributions[k];
         }
         if (std::abs(sum - 1.0) > 1.0e-5) return R::failure(ErrorCode::invalid_mxfp4);
+        if (prepared) prepared_.active = false;   // consumed
         // this library's shapes: expert output width = latent width, bf16
         // linears over multiples of 8, MXFP4 groups of 32, at most 64 slots
         if (Dout != D || H % 8 || D % 32 || I % 32 || experts.size() > 64) {
-            if (!rest_) return unavailable<OfficialMoeFfnResult>("official MoE FFN shape is not on the B200 path");
+            if (!rest_ || prepared)   // a prepared route lives here: the other backend cannot consume it
+                return unavailable<OfficialMoeFfnResult>("official MoE FFN shape is not on the B200 path");
             return rest_->official_mxfp4_moe_ffn(hidden, prefix, w, experts, ids, contributions, epsilon, beta,
                                                  linear, layer, phase);
         }
@@ -231,6 +340,8 @@ public:
         ++moe_calls_;
         return R::success({true, std::move(out), {ids.begin(), ids.end()}});
     }
+
+public:
 
     // ---- expert FFNs on tcgen05 (k3xb_expert_grid_host) --------------------
     Result<std::vector<std::vector<float>>> mxfp4_situ_mlp_group(std::span<const float> input,
@@ -544,6 +655,20 @@ private:
     k3xb_ctx* ctx_;
     std::unique_ptr<ComputeBackend> rest_;
     std::map<std::uint64_t, std::vector<Mxfp4MlpView>> prefetched_;
+    // the one prepared route (prepare_official_moe_route), its owner this backend
+    struct PreparedRoute {
+        bool active = false;
+        std::uint64_t generation = 0;
+        std::uint32_t layer = 0;
+        std::vector<float> prefix, hidden;
+    } prepared_;
+    const std::uint64_t owner_ = next_owner();
+    std::unordered_set<std::uint64_t> scanned_;   // bf16 route weights checked for non-finite words
+
+    static std::uint64_t next_owner() {
+        static std::atomic<std::uint64_t> n{0};
+        return ++n;
+    }
     std::uint64_t next_token_ = 0;
     std::uint64_t grid_calls_ = 0, grid_tokens_ = 0, moe_calls_ = 0, kda_calls_ = 0;
 };

@@ -18,6 +18,9 @@
 //   official_mxfp4_moe_ffn (the LatentMoE FFN of one position, its route
 //   given; the call official_layer_cuda makes with host route preparation)
 //                                -> k3xb_acquire_weight / _expert_stack + k3xb_official_moe_ffn_host
+//   prepare_official_moe_route, official_mxfp4_moe_ffn_prepared, discard_
+//   official_moe_prepared (device route preparation)
+//                                -> k3xb_prepare_moe_route_host, then as above
 //   official_kda (host-roundtrip state)  -> k3xb_acquire_weight + k3xb_kda_block_host
 // Weights are uploaded once, keyed by tensor id (BackendOptions::
 // cuda_resident_bytes bounds them when cuda_weights is resident).

@@ -1226,6 +1226,45 @@ int k3xb_attention_residual_norm(k3xb_ctx* ctx, const float* a, const float* del
     return launch_attnres_norm(ctx, a, delta, block, rnorm, rproj, post, T, H, eps, prefix_out, out);
 }
 
+int k3xb_prepare_moe_route_host(k3xb_ctx* ctx, const float* prefix_host, const float* block_host, uint32_t H,
+                                const uint16_t* rnorm, const uint16_t* rproj, const uint16_t* post, float eps,
+                                const uint16_t* router, uint32_t E, float* hidden_host, float* logits_host) {
+    K3XB_ENTER(ctx);
+    if (!prefix_host || !block_host || !H || !rnorm || !rproj || !post || !router || !E || !hidden_host ||
+        !logits_host)
+        return fail(ctx, K3XB_INVALID_EXTENT, "prepare moe route arguments");
+    if (!(eps > 0.0f)) return fail(ctx, K3XB_INVALID_EXTENT, "eps must be positive");
+    Sizer sz;
+    sz.take<float>(2 * size_t(H));   // prefix, block (one upload each)
+    sz.take<float>(H);               // the prepared MoE input
+    sz.take<float>(E);               // router logits
+    void* base;
+    int st;
+    if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
+    Carver c(base);
+    float* in = c.take<float>(2 * size_t(H));
+    float* hidden = c.take<float>(H);
+    float* logits = c.take<float>(E);
+    const size_t hbytes = sizeof(float) * H;
+    K3XB_CUDA(ctx, cudaMemcpyAsync(in, prefix_host, hbytes, cudaMemcpyHostToDevice, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(in + H, block_host, hbytes, cudaMemcpyHostToDevice, ctx->stream));
+    ctx->stats.h2d_bytes += 2 * hbytes;
+    {   // prepare_official_moe_input (official_moe.cpp:156-209)
+        PhaseScope ph(ctx, K3XB_PHASE_ATTN_RESIDUAL);
+        if ((st = launch_attnres_norm(ctx, in, nullptr, in + H, rnorm, rproj, post, 1, H, eps, nullptr, hidden)))
+            return st;
+    }
+    {   // route_official_moe_logits' input (official_moe.cpp:211-245): FP64 sums in h order
+        PhaseScope ph(ctx, K3XB_PHASE_ROUTE);
+        if ((st = launch_router_logits(ctx, hidden, 1, H, router, E, logits))) return st;
+    }
+    K3XB_CUDA(ctx, cudaMemcpyAsync(hidden_host, hidden, hbytes, cudaMemcpyDeviceToHost, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(logits_host, logits, sizeof(float) * E, cudaMemcpyDeviceToHost, ctx->stream));
+    ctx->stats.d2h_bytes += hbytes + sizeof(float) * E;
+    ++ctx->stats.route_calls;
+    return k3xb_sync(ctx);
+}
+
 int k3xb_layer_forward(k3xb_ctx* ctx, const k3xb_layer* L, const float* hidden_in, const float* block,
                        const int32_t* parent, uint32_t N, uint32_t S, const uint16_t* conv, const float* rec,
                        float* hidden_out, uint32_t* ids_out, void* trace) {

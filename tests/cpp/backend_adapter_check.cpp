@@ -315,6 +315,27 @@ int official_ffn() {
     v64.routed_up = {up64, 128, 64, 102};
     const std::vector<Mxfp4MlpView> e64{n1.view, n2.view};
     CHECK(call(x, prefix, v64, e64, ids, c) == ErrorCode::backend_unavailable);
+
+    // prepared routes (backend_cuda.cu:3478-3716): nothing prepared yet
+    auto none = b->official_mxfp4_moe_ffn_prepared(OfficialMoePreparedToken{1, 1}, f.view, f.experts, ids, c, 1e-6F,
+                                                   1.0F, std::nullopt, 0, P);
+    CHECK(!none && none.error() == ErrorCode::invalid_mxfp4);
+    CHECK(b->discard_official_moe_prepared(OfficialMoePreparedToken{1, 1}).error() == ErrorCode::invalid_state);
+    // the preparation's checks: invalid_extent
+    std::vector<std::uint16_t> rn(128), rp(128), pn(128), rt(8 * 128);
+    OfficialMoeRoutePrepareView pv{{rn, 401}, {rp, 1, 128, 402}, {pn, 403}, {rt, 8, 128, 404}};
+    const auto prep = [&](std::span<const float> px, std::span<const float> bx, const OfficialMoeRoutePrepareView& v,
+                          float eps = 1e-6F) { return b->prepare_official_moe_route(px, bx, v, eps, 0, P).error(); };
+    CHECK(prep(prefix, std::span<const float>(x).first(64), pv) == ErrorCode::invalid_extent);
+    CHECK(prep(prefix, x, pv, -1.0F) == ErrorCode::invalid_extent);
+    OfficialMoeRoutePrepareView twice = pv;
+    twice.router.tensor_id = 401;
+    CHECK(prep(prefix, x, twice) == ErrorCode::invalid_extent);
+    OfficialMoeRoutePrepareView narrow_proj = pv;
+    narrow_proj.residual_proj.cols = 64;
+    CHECK(prep(prefix, x, narrow_proj) == ErrorCode::invalid_extent);
+    rt[5] = 0x7f80;   // an infinite router word
+    CHECK(prep(prefix, x, pv) == ErrorCode::invalid_extent);
     return 0;
 }
 
