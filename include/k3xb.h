@@ -495,6 +495,26 @@ int k3xb_kda_block_host(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t hidden,
                         const float* x_host, uint32_t tokens, uint16_t* conv_host,
                         float* recurrent_host, float* out_host);
 
+/* official_kda with the state held on the device between calls
+ * (OfficialKdaStateMode device_seed / device_continue / device_publish,
+ * backend.hpp:242-259; the reference's CUDA backend_cuda.cu:2564-3140): the
+ * positions of k3xb_kda_block_host as a chain from the state held in
+ * `slot` of the context. SEED takes the state from conv_host/rec_host
+ * (layouts as k3xb_kda_block_host) and holds the new one; CONTINUE runs
+ * from the held state and holds the new one (conv_host/rec_host unused,
+ * may be NULL); PUBLISH runs from the held state and also copies the new
+ * one to conv_host/rec_host. A slot holds one state of one shape; CONTINUE
+ * and PUBLISH on a slot without a state of this block's shape are
+ * INVALID_STATE. The tokens and lifetime rules of the reference's modes are
+ * the caller's (the ComputeBackend adapter keeps them). HOST x [tokens][H]
+ * and out; returns after the results are on the host. */
+#define K3XB_KDA_HELD_SLOTS 8
+enum { K3XB_KDA_SEED = 0, K3XB_KDA_CONTINUE = 1, K3XB_KDA_PUBLISH = 2 };
+int k3xb_kda_block_held(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t hidden,
+                        const float* x_host, uint32_t tokens, uint32_t slot,
+                        int32_t mode, uint16_t* conv_host, float* recurrent_host,
+                        float* out_host);
+
 /* prepare_official_moe_input (official_moe.cpp:156-209) and the layer's
  * input path (official_layer.cpp:159-172): attention_residual of the two
  * sources (official_layer.cpp:42-102), then rms_norm (:104-125) with

@@ -700,12 +700,14 @@ class ReferenceOnB200:
     def __init__(self, path: str = REFERENCE_B200_SO):
         L = C.CDLL(path)
         self.lib = L
-        L.k3xr_official_layer_b200.argtypes = [C.c_int, C.c_int, C.c_void_p, C.c_void_p] + [_u16p] * 6 + [
+        L.k3xr_official_layer_b200.argtypes = [C.c_int, C.c_int, _sz, C.c_void_p, C.c_void_p] + [_u16p] * 6 + [
             C.c_float, _f32p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p, _f32p, _u32p, C.c_char_p, _sz]
 
-    def official_layer(self, layer: dict, hidden_in, block, conv, recurrent, device=0, device_route=False):
+    def official_layer(self, layer: dict, hidden_in, block, conv, recurrent, device=0, device_route=False,
+                       kda_split=0):
         """official_layer_cuda(B200Backend) with host (or, device_route,
-        device) route preparation: the arguments and results of
+        device) route preparation; kda_split > 0 runs two calls, the KDA
+        state kept on the device between them: the arguments and results of
         Reference.official_layer."""
         ks, keep_k = kda_struct(layer["kda"])
         ms, keep_m = moe_struct(layer["moe"])
@@ -716,7 +718,7 @@ class ReferenceOnB200:
         out = np.zeros((T, H), np.float32)
         ids = np.zeros((T, layer["moe"]["top_k"]), np.uint32)
         err = C.create_string_buffer(512)
-        st = self.lib.k3xr_official_layer_b200(device, 1 if device_route else 0, C.byref(ks), C.byref(ms), *(_c(layer[k], np.uint16) for k in (
+        st = self.lib.k3xr_official_layer_b200(device, 1 if device_route else 0, kda_split, C.byref(ks), C.byref(ms), *(_c(layer[k], np.uint16) for k in (
             "self_residual_norm", "self_residual_proj", "input_norm", "moe_residual_norm", "moe_residual_proj",
             "post_norm")), layer["rms_eps"], hidden_in, block, T, cq, ck, cv, rec, out, ids, err, len(err))
         del keep_k, keep_m

@@ -9,7 +9,8 @@
 // B200Backend adapter (project-k3x_b200/adapter/backend_b200.cpp), linked
 // against libk3xb.so, into oracle/_ref/libk3x_ref_b200.so. It shows the
 // drop-in: the reference's caller, unchanged, runs a whole official layer
-// with its KDA block (official_kda, host-roundtrip state) and its LatentMoE
+// with its KDA block (official_kda: host-roundtrip state, or device_seed then
+// device_publish across two calls) and its LatentMoE
 // FFN on the B200: official_mxfp4_moe_ffn after host route preparation, or
 // prepare_official_moe_route + official_mxfp4_moe_ffn_prepared after device
 // route preparation. The GPU test compares the result with
@@ -45,11 +46,15 @@ extern "C" {
 
 // official_layer_cuda(B200Backend) over T positions of one layer with a
 // LatentMoE (SwiGLU: situ_glu with beta 2^64, no linear bound), the
-// arguments of k3xr_official_layer plus the device and the route
-// preparation (0 host, 1 device). The KDA state arrays are
+// arguments of k3xr_official_layer plus the device, the route preparation
+// (0 host, 1 device) and kda_split: 0 for one call that brings the KDA state
+// and takes it back, else two calls, positions [0, kda_split) with
+// device_seed and the rest with device_publish from the state the device
+// kept. The KDA state arrays are
 // updated in place; out [T][H] and ids [T][top_k]. Returns the k3x::ErrorCode
 // value; err receives the message.
-int k3xr_official_layer_b200(int device, int device_route, const k3xr_kda_weights* kw, const k3xr_moe_layer* mw,
+int k3xr_official_layer_b200(int device, int device_route, std::size_t kda_split, const k3xr_kda_weights* kw,
+                             const k3xr_moe_layer* mw,
                              const std::uint16_t* self_residual_norm, const std::uint16_t* self_residual_proj,
                              const std::uint16_t* input_norm, const std::uint16_t* moe_residual_norm,
                              const std::uint16_t* moe_residual_proj, const std::uint16_t* post_norm, float eps,
@@ -124,20 +129,47 @@ int k3xr_official_layer_b200(int device, int device_route, const k3xr_kda_weight
     for (std::size_t t = 0; t < T; ++t)
         inputs[t] = {std::vector<float>(hidden_in + t * H, hidden_in + (t + 1) * H),
                      std::vector<float>(block + t * H, block + (t + 1) * H)};
-    auto r = k3x::official_layer_cuda(backend, inputs, w, state, config, mw->top_k, 0x1p64F, std::nullopt, 0,
-                                      k3x::ProfilePhase::decode, {},
-                                      device_route ? k3x::OfficialMoeRoutePreparationMode::device
-                                                   : k3x::OfficialMoeRoutePreparationMode::host);
-    if (!r) {
-        message(err, err_len, r.message());
-        return static_cast<int>(r.error());
+    const auto route = device_route ? k3x::OfficialMoeRoutePreparationMode::device
+                                    : k3x::OfficialMoeRoutePreparationMode::host;
+    const auto run = [&](std::size_t t0, std::size_t t1, const k3x::OfficialKdaState& from,
+                         k3x::OfficialKdaStateControl control) {
+        const std::vector<k3x::OfficialLayerInput> part(inputs.begin() + static_cast<std::ptrdiff_t>(t0),
+                                                        inputs.begin() + static_cast<std::ptrdiff_t>(t1));
+        return k3x::official_layer_cuda(backend, part, w, from, config, mw->top_k, 0x1p64F, std::nullopt, 1,
+                                        k3x::ProfilePhase::decode, control, route);
+    };
+    std::vector<k3x::OfficialLayerCudaStepResult> steps;
+    k3x::OfficialKdaState final_state;
+    if (!kda_split || kda_split >= T) {   // one call, the state brought and taken back
+        auto r = run(0, T, state, {});
+        if (!r) {
+            message(err, err_len, r.message());
+            return static_cast<int>(r.error());
+        }
+        steps = std::move(r.value().steps);
+        final_state = std::move(r.value().kda_state);
+    } else {   // two calls: the first seeds the device-held state, the second continues it and publishes
+        auto a = run(0, kda_split, state, {k3x::OfficialKdaStateMode::device_seed, {}});
+        if (!a) {
+            message(err, err_len, "device_seed: " + a.message());
+            return static_cast<int>(a.error());
+        }
+        auto b = run(kda_split, T, k3x::OfficialKdaState{},
+                     {k3x::OfficialKdaStateMode::device_publish, a.value().kda_device_state});
+        if (!b) {
+            message(err, err_len, "device_publish: " + b.message());
+            return static_cast<int>(b.error());
+        }
+        steps = std::move(a.value().steps);
+        for (auto& s : b.value().steps) steps.push_back(std::move(s));
+        final_state = std::move(b.value().kda_state);
     }
     for (std::size_t t = 0; t < T; ++t) {
-        const auto& step = r.value().steps[t];
+        const auto& step = steps[t];
         std::copy(step.output.begin(), step.output.end(), out + t * H);
         std::copy(step.route.expert_ids.begin(), step.route.expert_ids.end(), ids + t * mw->top_k);
     }
-    const auto& s = r.value().kda_state;
+    const auto& s = final_state;
     std::copy(s.conv_q.begin(), s.conv_q.end(), conv_q);
     std::copy(s.conv_k.begin(), s.conv_k.end(), conv_k);
     std::copy(s.conv_v.begin(), s.conv_v.end(), conv_v);

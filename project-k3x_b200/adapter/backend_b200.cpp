@@ -460,18 +460,38 @@ public:
                                                OfficialKdaCudaStateView state, OfficialKdaCudaConfig config,
                                                std::uint32_t layer, ProfilePhase phase,
                                                OfficialKdaStateControl control) override {
-        if (control.mode != OfficialKdaStateMode::host_roundtrip) {
-            // device-held state between calls is the verify step's job here
-            if (!rest_) return unavailable<OfficialKdaCudaResult>("device KDA state modes are not on the B200 path");
-            return rest_->official_kda(input, w, state, config, layer, phase, control);
-        }
+        // the state modes (backend_cuda.cu:2564-2625, :2691-2702): the host
+        // round trip brings the state and takes it back; device_seed brings it
+        // and the device keeps the new one; device_continue runs from the kept
+        // state and keeps the new one; device_publish runs from it and hands
+        // the new one back. Layers 1 and 2 have a slot each.
+        (void)phase;
+        using Mode = OfficialKdaStateMode;
+        const Mode mode = control.mode;
+        if (mode != Mode::host_roundtrip && mode != Mode::device_seed && mode != Mode::device_continue &&
+            mode != Mode::device_publish)
+            return Result<OfficialKdaCudaResult>::failure(ErrorCode::invalid_extent);
+        const bool host_in = mode == Mode::host_roundtrip || mode == Mode::device_seed;
+        const bool from_device = mode == Mode::device_continue || mode == Mode::device_publish;
+        const bool publish = mode == Mode::host_roundtrip || mode == Mode::device_publish;
+        const bool retain = mode == Mode::device_seed || mode == Mode::device_continue;
         const std::size_t H = config.hidden_size, h = config.heads, d = config.head_dim, cw = config.conv_width;
         const std::size_t P = h * d;
         if (!H || !h || !d || cw < 2 || !std::isfinite(config.rms_norm_epsilon) || config.rms_norm_epsilon <= 0.0F ||
             !std::isfinite(config.gate_lower_bound) || config.gate_lower_bound >= 0.0F || input.empty() ||
-            input.size() % H || state.conv_q.size() != (cw - 1) * P || state.conv_k.size() != (cw - 1) * P ||
-            state.conv_v.size() != (cw - 1) * P || state.recurrent_v_first.size() != h * d * d)
+            input.size() % H ||
+            (host_in && (state.conv_q.size() != (cw - 1) * P || state.conv_k.size() != (cw - 1) * P ||
+                         state.conv_v.size() != (cw - 1) * P || state.recurrent_v_first.size() != h * d * d)) ||
+            (!host_in && (!state.conv_q.empty() || !state.conv_k.empty() || !state.conv_v.empty() ||
+                          !state.recurrent_v_first.empty())) ||
+            (host_in && (control.token.owner || control.token.generation)))
             return Result<OfficialKdaCudaResult>::failure(ErrorCode::invalid_extent);
+        KdaSlot* slot = layer == 1 ? &kda_slots_[0] : layer == 2 ? &kda_slots_[1] : nullptr;
+        if (mode != Mode::host_roundtrip && !slot) return Result<OfficialKdaCudaResult>::failure(ErrorCode::invalid_state);
+        if ((mode == Mode::device_seed && slot->active) ||
+            (from_device && (!slot->active || control.token.owner != owner_ ||
+                             control.token.generation != slot->generation || !same_config(slot->config, config))))
+            return Result<OfficialKdaCudaResult>::failure(ErrorCode::invalid_state);
         k3xb_kda_layer K{};
         K.heads = static_cast<std::uint32_t>(h);
         K.head_dim = static_cast<std::uint32_t>(d);
@@ -513,26 +533,69 @@ public:
         K.o_proj = bf16(w.o_proj, H, P);
         if (st != ErrorCode::ok) return Result<OfficialKdaCudaResult>::failure(st, last_error());
 
+        // a host round trip ends the layer's kept state; a continuation ends
+        // the token it came with (a new one follows when the state is kept)
+        if (slot && (mode == Mode::host_roundtrip || from_device)) slot->active = false;
+
         const std::size_t hist = (cw - 1) * P;
-        std::vector<std::uint16_t> conv(3 * hist);
-        std::memcpy(conv.data(), state.conv_q.data(), hist * 2);
-        std::memcpy(conv.data() + hist, state.conv_k.data(), hist * 2);
-        std::memcpy(conv.data() + 2 * hist, state.conv_v.data(), hist * 2);
+        std::vector<std::uint16_t> conv(host_in || publish ? 3 * hist : 0);
+        if (host_in) {
+            std::memcpy(conv.data(), state.conv_q.data(), hist * 2);
+            std::memcpy(conv.data() + hist, state.conv_k.data(), hist * 2);
+            std::memcpy(conv.data() + 2 * hist, state.conv_v.data(), hist * 2);
+        }
         OfficialKdaCudaResult r;
-        r.recurrent_v_first.assign(state.recurrent_v_first.begin(), state.recurrent_v_first.end());
+        if (host_in) r.recurrent_v_first.assign(state.recurrent_v_first.begin(), state.recurrent_v_first.end());
+        else if (publish) r.recurrent_v_first.resize(h * d * d);
         r.output.resize(input.size());
-        const int rc = k3xb_kda_block_host(ctx_, &K, static_cast<std::uint32_t>(H), input.data(),
-                                           static_cast<std::uint32_t>(input.size() / H), conv.data(),
-                                           r.recurrent_v_first.data(), r.output.data());
-        if (rc != K3XB_OK) return Result<OfficialKdaCudaResult>::failure(static_cast<ErrorCode>(rc), last_error());
-        r.conv_q.assign(conv.begin(), conv.begin() + static_cast<std::ptrdiff_t>(hist));
-        r.conv_k.assign(conv.begin() + static_cast<std::ptrdiff_t>(hist),
-                        conv.begin() + static_cast<std::ptrdiff_t>(2 * hist));
-        r.conv_v.assign(conv.begin() + static_cast<std::ptrdiff_t>(2 * hist), conv.end());
+        const auto T = static_cast<std::uint32_t>(input.size() / H);
+        int rc;
+        if (mode == Mode::host_roundtrip) {
+            rc = k3xb_kda_block_host(ctx_, &K, static_cast<std::uint32_t>(H), input.data(), T, conv.data(),
+                                     r.recurrent_v_first.data(), r.output.data());
+        } else {
+            const std::int32_t held = mode == Mode::device_seed       ? K3XB_KDA_SEED
+                                      : mode == Mode::device_continue ? K3XB_KDA_CONTINUE
+                                                                      : K3XB_KDA_PUBLISH;
+            rc = k3xb_kda_block_held(ctx_, &K, static_cast<std::uint32_t>(H), input.data(), T,
+                                     static_cast<std::uint32_t>(slot - kda_slots_), held,
+                                     conv.empty() ? nullptr : conv.data(),
+                                     r.recurrent_v_first.empty() ? nullptr : r.recurrent_v_first.data(),
+                                     r.output.data());
+        }
+        if (rc != K3XB_OK) {
+            if (slot && mode != Mode::host_roundtrip) slot->active = false;
+            return Result<OfficialKdaCudaResult>::failure(static_cast<ErrorCode>(rc), last_error());
+        }
+        if (publish) {
+            r.conv_q.assign(conv.begin(), conv.begin() + static_cast<std::ptrdiff_t>(hist));
+            r.conv_k.assign(conv.begin() + static_cast<std::ptrdiff_t>(hist),
+                            conv.begin() + static_cast<std::ptrdiff_t>(2 * hist));
+            r.conv_v.assign(conv.begin() + static_cast<std::ptrdiff_t>(2 * hist), conv.end());
+        } else {
+            r.recurrent_v_first.clear();
+        }
         r.executed = true;
-        r.state_published = true;   // host round trip: the new state is the caller's (backend_cuda.cu:2578-2580)
+        r.state_published = publish;   // backend_cuda.cu:2578-2580
+        if (retain) {
+            if (!++kda_generation_) ++kda_generation_;
+            slot->generation = kda_generation_;
+            slot->config = config;
+            slot->active = true;
+            r.device_state = {owner_, kda_generation_};
+        }
         ++kda_calls_;
         return Result<OfficialKdaCudaResult>::success(std::move(r));
+    }
+
+    Result<bool> discard_official_kda_device_state(OfficialKdaDeviceStateToken token) override {
+        if (token.owner != owner_) return Result<bool>::failure(ErrorCode::invalid_state);
+        for (KdaSlot& s : kda_slots_)
+            if (s.active && s.generation == token.generation) {
+                s.active = false;
+                return Result<bool>::success(true);
+            }
+        return Result<bool>::failure(ErrorCode::invalid_state);
     }
 
 private:
@@ -664,6 +727,19 @@ private:
     } prepared_;
     const std::uint64_t owner_ = next_owner();
     std::unordered_set<std::uint64_t> scanned_;   // bf16 route weights checked for non-finite words
+    // the KDA states kept on the device for layers 1 and 2 (k3xb_kda_block_held slots 0 and 1)
+    struct KdaSlot {
+        bool active = false;
+        std::uint64_t generation = 0;
+        OfficialKdaCudaConfig config{};
+    } kda_slots_[2];
+    std::uint64_t kda_generation_ = 0;
+
+    static bool same_config(const OfficialKdaCudaConfig& a, const OfficialKdaCudaConfig& b) {
+        return a.hidden_size == b.hidden_size && a.heads == b.heads && a.head_dim == b.head_dim &&
+               a.conv_width == b.conv_width && a.rms_norm_epsilon == b.rms_norm_epsilon &&
+               a.gate_lower_bound == b.gate_lower_bound;
+    }
 
     static std::uint64_t next_owner() {
         static std::atomic<std::uint64_t> n{0};

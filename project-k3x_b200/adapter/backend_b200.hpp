@@ -21,7 +21,10 @@
 //   prepare_official_moe_route, official_mxfp4_moe_ffn_prepared, discard_
 //   official_moe_prepared (device route preparation)
 //                                -> k3xb_prepare_moe_route_host, then as above
-//   official_kda (host-roundtrip state)  -> k3xb_acquire_weight + k3xb_kda_block_host
+//   official_kda, host-roundtrip state  -> k3xb_acquire_weight + k3xb_kda_block_host
+//   official_kda, device_seed / _continue / _publish (layers 1 and 2, the
+//   reference's token rules) and discard_official_kda_device_state
+//                                -> k3xb_kda_block_held (the state stays on the GPU)
 // Weights are uploaded once, keyed by tensor id (BackendOptions::
 // cuda_resident_bytes bounds them when cuda_weights is resident).
 //

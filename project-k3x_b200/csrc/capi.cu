@@ -44,6 +44,25 @@ int ensure_scratch(k3xb_ctx* ctx, size_t bytes, void** out) {
     return K3XB_OK;
 }
 
+// One device-held KDA state slot (k3xb_kda_block_held): two states in one
+// allocation, `cur` the one that holds the slot's state; a call reads it and
+// its commit writes the other, so nothing aliases.
+struct KdaHeld {
+    void* buf = nullptr;
+    size_t state_bytes = 0, conv_n = 0, rec_n = 0;
+    int cur = 0;
+    bool valid = false;
+};
+
+void release_kda_held(k3xb_ctx* ctx) {
+    if (!ctx->kda_held) return;
+    KdaHeld* slots = static_cast<KdaHeld*>(ctx->kda_held);
+    for (int i = 0; i < K3XB_KDA_HELD_SLOTS; ++i)
+        if (slots[i].buf) cudaFree(slots[i].buf);
+    delete[] slots;
+    ctx->kda_held = nullptr;
+}
+
 int ensure_io(k3xb_ctx* ctx, size_t bytes, void** out) {
     if (bytes > ctx->io_bytes) {
         if (const int st = stream_wait(ctx)) return st;
@@ -285,6 +304,7 @@ int k3xb_destroy(k3xb_ctx* ctx) {
     release_mxf4_resources(ctx);
     release_resident(ctx);
     release_profiler(ctx);
+    release_kda_held(ctx);
     release_ep(ctx);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     if (ctx->side_stream) cudaStreamDestroy(ctx->side_stream);
@@ -1214,6 +1234,90 @@ int k3xb_kda_block_host(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t H, cons
     K3XB_CUDA(ctx, cudaMemcpyAsync(rec_host, rec + rec_n, rec_n * 4, cudaMemcpyDeviceToHost, ctx->stream));
     ctx->stats.d2h_bytes += xbytes + conv_n * 2 + rec_n * 4;
     return k3xb_sync(ctx);
+}
+
+int k3xb_kda_block_held(k3xb_ctx* ctx, const k3xb_kda_layer* w, uint32_t H, const float* x_host, uint32_t T,
+                        uint32_t slot, int32_t mode, uint16_t* conv_host, float* rec_host, float* out_host) {
+    K3XB_ENTER(ctx);
+    int st = validate_kda(ctx, w, H);
+    if (st) return st;
+    if (!x_host || !T || !out_host || slot >= K3XB_KDA_HELD_SLOTS)
+        return fail(ctx, K3XB_INVALID_EXTENT, "kda_block_held arguments (slot < K3XB_KDA_HELD_SLOTS)");
+    if (mode != K3XB_KDA_SEED && mode != K3XB_KDA_CONTINUE && mode != K3XB_KDA_PUBLISH)
+        return fail(ctx, K3XB_INVALID_STATE, "kda_block_held: unknown mode");
+    if ((mode != K3XB_KDA_CONTINUE) && (!conv_host || !rec_host))
+        return fail(ctx, K3XB_INVALID_EXTENT, "kda_block_held: seed and publish take the host state arrays");
+    const size_t P = static_cast<size_t>(w->heads) * w->head_dim;
+    const size_t conv_n = 3 * static_cast<size_t>(w->conv_width - 1) * P;
+    const size_t rec_n = static_cast<size_t>(w->heads) * w->head_dim * w->head_dim;
+    if (!ctx->kda_held) {
+        ctx->kda_held = new (std::nothrow) KdaHeld[K3XB_KDA_HELD_SLOTS];
+        if (!ctx->kda_held) return fail(ctx, K3XB_BACKEND_UNAVAILABLE, "kda_block_held: out of host memory");
+    }
+    KdaHeld& h = static_cast<KdaHeld*>(ctx->kda_held)[slot];
+    Sizer one;   // one state: conv words, then the recurrent state
+    one.take<uint16_t>(conv_n);
+    one.take<float>(rec_n);
+    const size_t state_bytes = (one.used + 255) / 256 * 256;
+    if (mode == K3XB_KDA_SEED) {
+        if (h.state_bytes != state_bytes) {   // (re)shape the slot: two states, read one, write the other
+            if ((st = stream_wait(ctx))) return st;
+            if (h.buf) K3XB_CUDA(ctx, cudaFree(h.buf));
+            h = KdaHeld{};
+            K3XB_CUDA(ctx, cudaMalloc(&h.buf, 2 * state_bytes));
+            h.state_bytes = state_bytes;
+            h.conv_n = conv_n;
+            h.rec_n = rec_n;
+        }
+        h.valid = false;
+    } else if (!h.valid || h.conv_n != conv_n || h.rec_n != rec_n) {
+        return fail(ctx, K3XB_INVALID_STATE, "kda_block_held: no state of this shape held in the slot");
+    }
+    const auto state_at = [&](int i, uint16_t** conv, float** rec) {
+        Carver c(static_cast<char*>(h.buf) + static_cast<size_t>(i) * state_bytes);
+        *conv = c.take<uint16_t>(conv_n);
+        *rec = c.take<float>(rec_n);
+    };
+    uint16_t *conv_in, *conv_out;
+    float *rec_in, *rec_out;
+    state_at(h.cur, &conv_in, &rec_in);
+    state_at(h.cur ^ 1, &conv_out, &rec_out);
+    const size_t xbytes = sizeof(float) * T * H;
+    Sizer sz;
+    sz.take<float>(static_cast<size_t>(T) * H);
+    sz.take<float>(static_cast<size_t>(T) * H);
+    sz.take<uint8_t>(k3xb_kda_trace_bytes(w, T, 1));
+    void* base;
+    if ((st = ensure_io(ctx, sz.used, &base))) return st;
+    Carver c(base);
+    float* x = c.take<float>(static_cast<size_t>(T) * H);
+    float* out = c.take<float>(static_cast<size_t>(T) * H);
+    void* trace = c.take<uint8_t>(k3xb_kda_trace_bytes(w, T, 1));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(x, x_host, xbytes, cudaMemcpyHostToDevice, ctx->stream));
+    ctx->stats.h2d_bytes += xbytes;
+    if (mode == K3XB_KDA_SEED) {
+        K3XB_CUDA(ctx, cudaMemcpyAsync(conv_in, conv_host, conv_n * 2, cudaMemcpyHostToDevice, ctx->stream));
+        K3XB_CUDA(ctx, cudaMemcpyAsync(rec_in, rec_host, rec_n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        ctx->stats.h2d_bytes += conv_n * 2 + rec_n * 4;
+    }
+    // the positions are a chain from the held state; its last node is the new state
+    std::vector<int32_t> parent(T);
+    for (uint32_t n = 0; n < T; ++n) parent[n] = static_cast<int32_t>(n) - 1;
+    const int32_t last = static_cast<int32_t>(T) - 1;
+    if ((st = k3xb_kda_block(ctx, w, H, x, parent.data(), T, 1, conv_in, rec_in, out, trace))) return st;
+    if ((st = k3xb_kda_block_commit(ctx, w, trace, parent.data(), T, 1, &last, conv_in, rec_in, conv_out, rec_out)))
+        return st;
+    K3XB_CUDA(ctx, cudaMemcpyAsync(out_host, out, xbytes, cudaMemcpyDeviceToHost, ctx->stream));
+    ctx->stats.d2h_bytes += xbytes;
+    if (mode == K3XB_KDA_PUBLISH) {
+        K3XB_CUDA(ctx, cudaMemcpyAsync(conv_host, conv_out, conv_n * 2, cudaMemcpyDeviceToHost, ctx->stream));
+        K3XB_CUDA(ctx, cudaMemcpyAsync(rec_host, rec_out, rec_n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        ctx->stats.d2h_bytes += conv_n * 2 + rec_n * 4;
+    }
+    if ((st = k3xb_sync(ctx))) return st;
+    h.cur ^= 1;   // the new state is the one just written
+    h.valid = true;
+    return K3XB_OK;
 }
 
 int k3xb_attention_residual_norm(k3xb_ctx* ctx, const float* a, const float* delta, const float* block,

@@ -28,6 +28,7 @@ struct k3xb_ctx {
     void* ep_state = nullptr;         // expert parallelism: NCCL communicator
     void* resident = nullptr;         // resident weight table (resident.cu)
     void* profiler = nullptr;         // phase timing (profile.cu), NULL when off
+    void* kda_held = nullptr;         // device-held KDA states (k3xb_kda_block_held)
 };
 
 namespace k3xb {

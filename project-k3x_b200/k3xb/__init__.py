@@ -96,6 +96,9 @@ class SpeculativeIO(C.Structure):
                                   "committed_count", "logits")]
 
 
+KDA_SEED, KDA_CONTINUE, KDA_PUBLISH = 0, 1, 2   # k3xb_kda_block_held modes
+KDA_HELD_SLOTS = 8
+
 EP_DEFAULT_TIMEOUT_MS = 300000
 
 
@@ -204,6 +207,7 @@ def library() -> C.CDLL:
             "k3xb_set_profiling": [vp, C.c_int],
             "k3xb_get_profile": [vp, C.POINTER(PhaseTime), C.POINTER(u64)],
             "k3xb_kda_block_host": [vp, C.POINTER(KdaLayer), u32, vp, u32, vp, vp, vp],
+            "k3xb_kda_block_held": [vp, C.POINTER(KdaLayer), u32, vp, u32, u32, C.c_int32, vp, vp, vp],
         }
         for name, args in sigs.items():
             fn = getattr(lib, name)
@@ -517,6 +521,22 @@ class Context:
         self._check(self.lib.k3xb_kda_block_host(self.h, C.byref(w), hidden, x.ctypes.data, x.shape[0],
                                                  conv.ctypes.data, recurrent.ctypes.data, out.ctypes.data),
                     "kda_block_host")
+        return out
+
+    def kda_block_held(self, w: KdaLayer, hidden, x, slot, mode, conv=None, recurrent=None):
+        """k3xb_kda_block_held: x [T][H] float32 (HOST) -> out [T][H] from the
+        state held in `slot`. mode KDA_SEED takes conv/recurrent as the
+        starting state; KDA_PUBLISH writes the new state into them."""
+        import numpy as np
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        for a, dt in ((conv, np.uint16), (recurrent, np.float32)):
+            if a is not None and (a.dtype != dt or not a.flags.c_contiguous):
+                raise K3xbError(INVALID_EXTENT, "conv must be contiguous uint16 and recurrent float32")
+        out = np.empty((x.shape[0], hidden), np.float32)
+        self._check(self.lib.k3xb_kda_block_held(self.h, C.byref(w), hidden, x.ctypes.data, x.shape[0], slot, mode,
+                                                 None if conv is None else conv.ctypes.data,
+                                                 None if recurrent is None else recurrent.ctypes.data,
+                                                 out.ctypes.data), "kda_block_held")
         return out
 
     def release_resident(self):

@@ -164,12 +164,12 @@ int split_and_forwarding() {
     const std::vector<float> c{1.0F};
     auto m = b->mxfp4_situ_moe(x, experts, c, 1.0e6F, std::nullopt, 0, ProfilePhase::decode);
     CHECK(!m && m.error() == ErrorCode::invalid_extent && fake->calls == 1);
-    // device KDA state modes go to the other backend
+    // device KDA state modes run here too, never on the other backend
     OfficialKdaStateControl ctl{};
     ctl.mode = OfficialKdaStateMode::device_seed;
-    auto k = b->official_kda(x, OfficialKdaCudaView{}, OfficialKdaCudaStateView{}, OfficialKdaCudaConfig{}, 0,
+    auto k = b->official_kda(x, OfficialKdaCudaView{}, OfficialKdaCudaStateView{}, OfficialKdaCudaConfig{}, 1,
                              ProfilePhase::decode, ctl);
-    CHECK(k && k.value().output.size() == 1 && fake->calls == 2);
+    CHECK(!k && k.error() == ErrorCode::invalid_extent && fake->calls == 1);
     return 0;
 }
 
@@ -182,11 +182,6 @@ int no_rest() {
     auto r = b->resident_mxfp4_moe_layer(x, ResidentMoeLayerView{}, {}, {}, 1e-6F, 1.0F, std::nullopt, 0,
                                          ProfilePhase::decode);
     CHECK(!r && r.error() == ErrorCode::backend_unavailable);
-    OfficialKdaStateControl ctl{};
-    ctl.mode = OfficialKdaStateMode::device_continue;
-    auto k = b->official_kda(x, OfficialKdaCudaView{}, OfficialKdaCudaStateView{}, OfficialKdaCudaConfig{}, 0,
-                             ProfilePhase::decode, ctl);
-    CHECK(!k && k.error() == ErrorCode::backend_unavailable);
     return 0;
 }
 
@@ -238,6 +233,23 @@ int argument_checks() {
     CHECK(b->official_kda(x3, OfficialKdaCudaView{}, short_state, cfg, 0, P).error() == ErrorCode::invalid_extent);
     // weight views of the wrong shape
     CHECK(b->official_kda(x3, OfficialKdaCudaView{}, st, cfg, 0, P).error() == ErrorCode::invalid_extent);
+    // the state modes' rules (backend_cuda.cu:2564-2625, :2691-2702)
+    const auto kda = [&](OfficialKdaStateMode mode, const OfficialKdaCudaStateView& s, std::uint32_t layer,
+                         OfficialKdaDeviceStateToken token = {}) {
+        return b->official_kda(x3, OfficialKdaCudaView{}, s, cfg, layer, P, OfficialKdaStateControl{mode, token}).error();
+    };
+    using M = OfficialKdaStateMode;
+    const OfficialKdaCudaStateView empty{};
+    CHECK(kda(M::device_continue, st, 1) == ErrorCode::invalid_extent);            // a continuation brings no state
+    CHECK(kda(M::device_seed, empty, 1) == ErrorCode::invalid_extent);             // a seed brings one
+    CHECK(kda(M::host_roundtrip, empty, 1) == ErrorCode::invalid_extent);
+    CHECK(kda(M::device_seed, st, 1, {5, 6}) == ErrorCode::invalid_extent);        // a seed takes no token
+    CHECK(kda(M::device_seed, st, 3) == ErrorCode::invalid_state);                 // slots for layers 1 and 2 only
+    CHECK(kda(M::device_continue, empty, 1, {5, 6}) == ErrorCode::invalid_state);  // nothing kept
+    CHECK(kda(M::device_publish, empty, 2, {5, 6}) == ErrorCode::invalid_state);
+    CHECK(b->discard_official_kda_device_state({5, 6}).error() == ErrorCode::invalid_state);
+    // a seed that passes the rules reaches the weight checks (empty views: invalid_extent)
+    CHECK(kda(M::device_seed, st, 1) == ErrorCode::invalid_extent);
     return 0;
 }
 

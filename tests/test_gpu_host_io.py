@@ -113,3 +113,45 @@ def test_kda_block_host_equals_device_chain_and_resident_weights(torch, ctx, rs)
     np.testing.assert_array_equal(c2, want_conv)
     np.testing.assert_array_equal(r2, want_rec)
     ctx.release_resident()
+
+
+def test_kda_block_held_split_equals_one_call(torch, ctx, rs):
+    """k3xb_kda_block_held (official_kda's device_seed / device_continue /
+    device_publish): the five positions of the test above as seed (2),
+    continue (1) and publish (2) from the state the device keeps give the
+    one-call outputs and final state bit for bit (a chain split at any
+    position is the same recurrence); the restatement's incremental run
+    equals its full run the same way (tests/test_golden.py). A continuation
+    on an empty slot, or on a slot holding a state of another shape, is
+    INVALID_STATE."""
+    import k3xb
+    g = np.random.default_rng(84)
+    H, h, dh, W, T = 256, 2, 64, 4, 5
+    P = h * dh
+    w = make_kda_weights(g, H, h, dh, W)
+    conv = np.stack([bf16_words(g.normal(0, 0.5, size=(W - 1) * P)) for _ in range(3)])
+    rec = g.normal(0, 0.05, size=(h, dh, dh)).astype(np.float32)
+    x = bf16_normal(g, (T, H))
+    wd = {k: (to_dev(torch, v) if isinstance(v, np.ndarray) else v) for k, v in w.items()}
+    desc = k3xb.kda_layer_desc(wd)
+    c1, r1 = conv.copy(), rec.copy()
+    want = ctx.kda_block_host(desc, H, x, c1, r1)
+
+    with pytest.raises(k3xb.K3xbError) as e:
+        ctx.kda_block_held(desc, H, x[:1], 5, k3xb.KDA_CONTINUE)
+    assert e.value.status == k3xb.INVALID_STATE
+    c2, r2 = conv.copy(), rec.copy()
+    parts = [ctx.kda_block_held(desc, H, x[:2], 3, k3xb.KDA_SEED, c2, r2),
+             ctx.kda_block_held(desc, H, x[2:3], 3, k3xb.KDA_CONTINUE)]
+    c3, r3 = np.zeros_like(conv), np.zeros_like(rec)
+    parts.append(ctx.kda_block_held(desc, H, x[3:], 3, k3xb.KDA_PUBLISH, c3, r3))
+    np.testing.assert_array_equal(np.concatenate(parts), want)
+    np.testing.assert_array_equal(c3, c1)
+    np.testing.assert_array_equal(r3, r1)
+    np.testing.assert_array_equal(c2, conv)   # a seed reads its arrays and leaves them
+    # another block shape on the same slot
+    w2 = make_kda_weights(g, H, 1, dh, W)
+    wd2 = {k: (to_dev(torch, v) if isinstance(v, np.ndarray) else v) for k, v in w2.items()}
+    with pytest.raises(k3xb.K3xbError) as e:
+        ctx.kda_block_held(k3xb.kda_layer_desc(wd2), H, x[:1], 3, k3xb.KDA_CONTINUE)
+    assert e.value.status == k3xb.INVALID_STATE

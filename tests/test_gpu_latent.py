@@ -185,8 +185,8 @@ def test_official_moe_ffn_one_position_equals_the_layer(rs, engine):
         ctx.close()
 
 
-@pytest.mark.parametrize("route", ["host", "device"])
-def test_reference_layer_driver_on_the_b200_backend(route):
+@pytest.mark.parametrize("route,kda_split", [("host", 0), ("device", 0), ("host", 2), ("device", 3)])
+def test_reference_layer_driver_on_the_b200_backend(route, kda_split):
     """The drop-in, whole-layer: the reference's own official_layer_cuda
     (official_layer.cpp:246-500), unchanged, drives this library's
     ComputeBackend (B200Backend: official_kda on k3xb_kda_block_host; host
@@ -195,7 +195,9 @@ def test_reference_layer_driver_on_the_b200_backend(route):
     k3xb_prepare_moe_route_host, then official_mxfp4_moe_ffn_prepared)
     through oracle/_ref/libk3x_ref_b200.so, against the golden
     official_layer_cpu output with the bars of the test above; the final
-    KDA state as well."""
+    KDA state as well. kda_split > 0 runs the positions as two calls, the
+    first with device_seed and the second with device_publish from the
+    state the device kept (k3xb_kda_block_held), which must equal one call."""
     from oracle import ReferenceOnB200, have_reference_on_b200
     if not have_reference_on_b200():
         pytest.fail("oracle/_ref/libk3x_ref_b200.so is not built (oracle/Makefile, with the reference tree)")
@@ -203,7 +205,7 @@ def test_reference_layer_driver_on_the_b200_backend(route):
     T = f["hidden"].shape[0]
     out, ids, state = ReferenceOnB200().official_layer(layer, f["hidden"], f["block"],
                                                        (f["conv_q"], f["conv_k"], f["conv_v"]), f["recurrent"],
-                                                       device_route=route == "device")
+                                                       device_route=route == "device", kda_split=kda_split)
     same = np.all(ids == f["ids"], axis=1)
     assert same.sum() >= T - 1, f"routes agree on {same.sum()}/{T} positions"
     assert_mostly_close(out[same], f["out"][same], what="official_layer_cuda on B200Backend")
