@@ -407,6 +407,27 @@ int k3xb_official_moe_ffn_host(k3xb_ctx* ctx, const k3xb_moe_layer* tail,
                                const float* contributions, const float* hidden,
                                const float* prefix, float* out);
 
+/* dense_matvec (backend.hpp:332-334; CPU semantics backend_cpu.cpp:23-47)
+ * for `tokens` inputs: y[t][r] = float(sum over c in column order of
+ * double(W[r][c]) * x[t][c]), bit-identical to the reference CPU backend.
+ * Device W [rows][cols] float, x [tokens][cols], y [tokens][rows]. */
+int k3xb_dense_matvec(k3xb_ctx* ctx, const float* W, uint32_t rows,
+                      uint32_t cols, const float* x, uint32_t tokens,
+                      float* y);
+/* The same for one HOST input x [cols] and HOST y [rows] (W on the device,
+ * e.g. resident); returns after y is on the host. */
+int k3xb_dense_matvec_host(k3xb_ctx* ctx, const float* W, uint32_t rows,
+                           uint32_t cols, const float* x_host, float* y_host);
+/* dense_situ_mlp (backend.hpp:344-347; CPU semantics backend_cpu.cpp:
+ * 107-122): down(situ_glu(gate x, up x)) with the products above; device
+ * gate/up [inter][cols], down [out_rows][inter]; linear_beta 0 = no linear
+ * bound. situ_glu uses the device's tanhf/expf, so the activation can differ
+ * from the host's libm in the last bit. HOST x [cols], y [out_rows]. */
+int k3xb_dense_situ_mlp_host(k3xb_ctx* ctx, const float* gate, const float* up,
+                             const float* down, uint32_t inter, uint32_t cols,
+                             uint32_t out_rows, const float* x_host, float beta,
+                             float linear_beta, float* y_host);
+
 /* ---- (d) KDA recurrence -------------------------------------------------- */
 /* official_kda.cpp:319-369 applied over a draft tree for S sequences that
  * share the topology: node n continues from parent[n]'s state

@@ -251,6 +251,20 @@ int k3xo_bf16_matvec(const float* x, const uint16_t* w, size_t rows,
     return K3XO_OK;
 }
 
+/* backend_cpu.cpp:23-47: the CPU backend's f32 dense product, one double
+ * chain per row in column order (its validity check, :368-377, is shapes
+ * only: non-finite values pass through). */
+int k3xo_dense_matvec(const float* x, const float* w, size_t rows, size_t cols,
+                      float* out)
+{
+    for (size_t r = 0; r < rows; ++r) {
+        double sum = 0.0;
+        for (size_t c = 0; c < cols; ++c) sum += (double)w[r * cols + c] * x[c];
+        out[r] = (float)sum;
+    }
+    return K3XO_OK;
+}
+
 /* official_layer.cpp:104-125 (== official_moe.cpp:61-80 for finite input) */
 int k3xo_rms_norm_bf16(const float* x, const uint16_t* weight, size_t n,
                        float eps, float* out)

@@ -69,6 +69,8 @@ void k3xo_situ_glu(float* out, const float* gate, const float* up, size_t n,
  * (g * sigmoid(g)) * u, all float. */
 void k3xo_swiglu(float* out, const float* gate, const float* up, size_t n);
 /* official_moe.cpp:39-59: FP64 accumulation, output rounded to bf16. */
+int k3xo_dense_matvec(const float* x, const float* w, size_t rows, size_t cols,
+                      float* out);   /* backend_cpu.cpp:23-47 */
 int k3xo_bf16_matvec(const float* x, const uint16_t* w, size_t rows,
                      size_t cols, float* out);
 /* official_moe.cpp:61-80 / official_layer.cpp:104-125 (bf16 weight). */

@@ -149,6 +149,7 @@ class Restatement:
         L.k3xo_swiglu.argtypes = [_f32p, _f32p, _f32p, _sz]
         L.k3xo_swiglu.restype = None
         L.k3xo_bf16_matvec.argtypes = [_f32p, _u16p, _sz, _sz, _f32p]
+        L.k3xo_dense_matvec.argtypes = [_f32p, _f32p, _sz, _sz, _f32p]
         L.k3xo_router_logits.argtypes = [_f32p, _u16p, _sz, _sz, _f32p]
         L.k3xo_route_logits.argtypes = [_f32p, _f32p, _sz, _sz, _u32p, _f32p, C.c_void_p]
         L.k3xo_expert_major_plan.argtypes = [_u32p, _f32p, _sz, _sz, _u32p, _u32p, _u32p,
@@ -231,6 +232,18 @@ class Restatement:
         self._check(self.lib.k3xo_bf16_matvec(_c(x, np.float32), w, w.shape[0], w.shape[1], out),
                     "bf16_matvec")
         return out
+
+    def dense_matvec(self, x, w):
+        """The CPU backend's f32 dense product (backend_cpu.cpp:23-47)."""
+        w = _c(w, np.float32)
+        out = np.empty(w.shape[0], np.float32)
+        self._check(self.lib.k3xo_dense_matvec(_c(x, np.float32), w, w.shape[0], w.shape[1], out), "dense_matvec")
+        return out
+
+    def dense_situ_mlp(self, x, gate, up, down, beta, linear_beta=0.0):
+        """dense_situ_mlp (backend_cpu.cpp:107-122)."""
+        a = self.situ_glu(self.dense_matvec(x, gate), self.dense_matvec(x, up), beta, linear_beta)
+        return self.dense_matvec(a, down)
 
     def router_logits(self, hidden, router):
         router = _c(router, np.uint16)
@@ -485,6 +498,8 @@ class Reference:
                                         _u32p, _f32p]
         L.k3xr_official_two_layer.argtypes = [C.c_void_p] * 2 + [C.c_void_p, C.c_float, _f32p, _f32p] + \
             [C.c_void_p] * 4 + [_f32p]
+        L.k3xr_dense_matvec.argtypes = [_f32p, _sz, _sz, _f32p, _f32p]
+        L.k3xr_dense_situ_mlp.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _f32p, C.c_float, C.c_float, _f32p]
         L.k3xr_official_layer.argtypes = [C.c_void_p, C.c_void_p, _u16p, _u16p, _u16p, _u16p, _u16p, _u16p,
                                           C.c_float, _f32p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p, _f32p, _u32p]
 
@@ -508,6 +523,24 @@ class Reference:
         g, u = _c(gate, np.float32), _c(up, np.float32)
         out = np.empty_like(g)
         self.lib.k3xr_situ_glu(out, g, u, g.size, beta, linear_beta)
+        return out
+
+    def dense_matvec(self, x, w):
+        """The reference CPU backend's dense_matvec (make_cpu_backend)."""
+        w = _c(w, np.float32)
+        out = np.empty(w.shape[0], np.float32)
+        st = self.lib.k3xr_dense_matvec(w, w.shape[0], w.shape[1], _c(x, np.float32), out)
+        if st:
+            raise OracleError(st, "ref dense_matvec")
+        return out
+
+    def dense_situ_mlp(self, x, gate, up, down, beta, linear_beta=0.0):
+        gate, up, down = _c(gate, np.float32), _c(up, np.float32), _c(down, np.float32)
+        out = np.empty(down.shape[0], np.float32)
+        st = self.lib.k3xr_dense_situ_mlp(gate, up, down, gate.shape[0], gate.shape[1], down.shape[0],
+                                          _c(x, np.float32), beta, linear_beta, out)
+        if st:
+            raise OracleError(st, "ref dense_situ_mlp")
         return out
 
     def route(self, hidden, router, correction, top_k, want_scores=False):

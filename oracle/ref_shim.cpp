@@ -8,6 +8,7 @@
 // (k3x_oracle.c); bench.py uses it as the timed CPU reference arm. Nothing
 // here is reference source: every function below only marshals plain C
 // arrays into the reference's C++ API and back.
+#include "k3x/backend.hpp"
 #include "k3x/expert_major.hpp"
 #include "k3x/official_kda.hpp"
 #include "k3x/official_layer.hpp"
@@ -544,6 +545,27 @@ int k3xr_official_two_layer(const k3xr_kda_weights* const kw[2], const k3xr_moe_
         std::copy(s.recurrent_v_first.begin(), s.recurrent_v_first.end(), recurrent[l]);
     }
     return 0;
+}
+
+// The reference CPU backend's dense_matvec (backend_cpu.cpp:23-47) and
+// dense_situ_mlp (:107-122) through make_cpu_backend. y [rows] / [out_rows].
+int k3xr_dense_matvec(const float* W, std::size_t rows, std::size_t cols, const float* x, float* y) {
+    auto backend = k3x::make_cpu_backend();
+    auto r = backend->dense_matvec({x, cols}, k3x::DenseWeightView{1, {W, rows * cols}, rows, cols}, 0,
+                                   k3x::ProfilePhase::decode);
+    if (r) std::copy(r.value().begin(), r.value().end(), y);
+    return code(r);
+}
+
+int k3xr_dense_situ_mlp(const float* gate, const float* up, const float* down, std::size_t inter, std::size_t cols,
+                        std::size_t out_rows, const float* x, float beta, float linear_beta, float* y) {
+    auto backend = k3x::make_cpu_backend();
+    const k3x::DenseMlpView w{{1, {gate, inter * cols}, inter, cols},
+                              {2, {up, inter * cols}, inter, cols},
+                              {3, {down, out_rows * inter}, out_rows, inter}};
+    auto r = backend->dense_situ_mlp({x, cols}, w, beta, linear(linear_beta), 0, k3x::ProfilePhase::decode);
+    if (r) std::copy(r.value().begin(), r.value().end(), y);
+    return code(r);
 }
 
 }  // extern "C"

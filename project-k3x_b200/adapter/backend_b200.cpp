@@ -103,11 +103,26 @@ public:
         return m;
     }
 
-    // ---- not on the B200 path: the maintainer's other backend -------------
+    // ---- f32 dense products (k3xb_dense_matvec_host, k3xb_dense_situ_mlp_host)
+    // The CPU backend's checks (backend_cpu.cpp:368-377, :404-410,
+    // invalid_extent) and its arithmetic bit for bit (one FP64 chain per row
+    // in column order). A weight is kept resident by its tensor id; one
+    // without an id (0) cannot be, and goes to the other backend.
     Result<std::vector<float>> dense_matvec(std::span<const float> input, DenseWeightView weight,
                                             std::uint32_t layer, ProfilePhase phase) override {
-        if (!rest_) return unavailable<std::vector<float>>("dense_matvec is not on the B200 path");
-        return rest_->dense_matvec(input, weight, layer, phase);
+        if (!valid_dense(input, weight)) return Result<std::vector<float>>::failure(ErrorCode::invalid_extent);
+        if (!weight.tensor_id || !weight.rows) {
+            if (!rest_) return unavailable<std::vector<float>>("dense_matvec: a weight without a tensor id");
+            return rest_->dense_matvec(input, weight, layer, phase);
+        }
+        ErrorCode st = ErrorCode::ok;
+        const float* W = dense_resident(weight, &st);
+        if (!W) return Result<std::vector<float>>::failure(st, last_error());
+        std::vector<float> y(weight.rows);
+        const int rc = k3xb_dense_matvec_host(ctx_, W, static_cast<std::uint32_t>(weight.rows),
+                                              static_cast<std::uint32_t>(weight.cols), input.data(), y.data());
+        if (rc != K3XB_OK) return Result<std::vector<float>>::failure(static_cast<ErrorCode>(rc), last_error());
+        return Result<std::vector<float>>::success(std::move(y));
     }
     Result<std::vector<float>> mxfp4_matvec(std::span<const float> input, Mxfp4WeightView weight,
                                             std::uint32_t layer, ProfilePhase phase) override {
@@ -117,8 +132,17 @@ public:
     Result<std::vector<std::vector<float>>> dense_matvec_group(std::span<const float> input,
                                                                std::span<const DenseWeightView> weights,
                                                                std::uint32_t layer, ProfilePhase phase) override {
-        if (!rest_) return unavailable<std::vector<std::vector<float>>>("dense_matvec_group is not on the B200 path");
-        return rest_->dense_matvec_group(input, weights, layer, phase);
+        using R = Result<std::vector<std::vector<float>>>;
+        for (const auto& w : weights)   // backend_cpu.cpp:61-80: every weight checked first
+            if (!valid_dense(input, w)) return R::failure(ErrorCode::invalid_extent);
+        std::vector<std::vector<float>> out;
+        out.reserve(weights.size());
+        for (const auto& w : weights) {
+            auto y = dense_matvec(input, w, layer, phase);
+            if (!y) return R::failure(y.error(), y.message());
+            out.push_back(std::move(y.value()));
+        }
+        return R::success(std::move(out));
     }
     Result<std::vector<std::vector<float>>> mxfp4_matvec_group(std::span<const float> input,
                                                                std::span<const Mxfp4WeightView> weights,
@@ -129,9 +153,30 @@ public:
     Result<std::vector<float>> dense_situ_mlp(std::span<const float> input, DenseMlpView weights, float situ_beta,
                                               std::optional<float> situ_linear, std::uint32_t layer,
                                               ProfilePhase phase) override {
-        if (!rest_) return unavailable<std::vector<float>>("dense_situ_mlp is not on the B200 path");
-        return rest_->dense_situ_mlp(input, weights, situ_beta, situ_linear, layer, phase);
+        const auto& g = weights.gate;
+        if (!valid_dense(input, g) || !valid_dense(input, weights.up) || !g.rows || g.rows != weights.up.rows ||
+            weights.down.cols != g.rows || weights.down.values.size() != weights.down.rows * weights.down.cols)
+            return Result<std::vector<float>>::failure(ErrorCode::invalid_extent);
+        if (!g.tensor_id || !weights.up.tensor_id || !weights.down.tensor_id || !weights.down.rows ||
+            !valid_activation(situ_beta, situ_linear)) {
+            if (!rest_) return unavailable<std::vector<float>>("dense_situ_mlp: untracked weights or SiTU parameters");
+            return rest_->dense_situ_mlp(input, weights, situ_beta, situ_linear, layer, phase);
+        }
+        ErrorCode st = ErrorCode::ok;
+        const float* G = dense_resident(g, &st);
+        const float* U = G ? dense_resident(weights.up, &st) : nullptr;
+        const float* D = U ? dense_resident(weights.down, &st) : nullptr;
+        if (!D) return Result<std::vector<float>>::failure(st, last_error());
+        std::vector<float> y(weights.down.rows);
+        const int rc = k3xb_dense_situ_mlp_host(ctx_, G, U, D, static_cast<std::uint32_t>(g.rows),
+                                                static_cast<std::uint32_t>(g.cols),
+                                                static_cast<std::uint32_t>(weights.down.rows), input.data(),
+                                                situ_beta, situ_linear ? *situ_linear : 0.0F, y.data());
+        if (rc != K3XB_OK) return Result<std::vector<float>>::failure(static_cast<ErrorCode>(rc), last_error());
+        return Result<std::vector<float>>::success(std::move(y));
     }
+
+    // ---- not on the B200 path: the maintainer's other backend -------------
     // The resident layer of backend_cpu.cpp:308-341 takes f32 dense
     // projections and mixes unrounded expert outputs in float: not the bf16
     // arithmetic of official_moe_cpu that this library's kernels compute.
@@ -250,6 +295,18 @@ public:
     }
 
 private:
+    // backend_cpu.cpp:368-377
+    static bool valid_dense(std::span<const float> input, const DenseWeightView& w) {
+        if (input.size() != w.cols || w.rows > w.values.size() || (w.cols != 0 && w.rows > w.values.size() / w.cols))
+            return false;
+        return w.values.size() == w.rows * w.cols;
+    }
+
+    const float* dense_resident(const DenseWeightView& w, ErrorCode* st) {
+        return static_cast<const float*>(
+            resident(w.tensor_id, K3XB_WEIGHT_F32, w.rows, w.cols, w.values.data(), w.values.size() * 4, st));
+    }
+
     static bool finite(std::span<const float> v) {
         for (const float x : v)
             if (!std::isfinite(x)) return false;

@@ -11,6 +11,9 @@
 // returned as it is; it is never retried on `rest`.
 //
 // On the B200:
+//   dense_matvec / _group, dense_situ_mlp (weights with a tensor id)
+//                                -> k3xb_acquire_weight (f32) + k3xb_dense_matvec_host /
+//                                   k3xb_dense_situ_mlp_host (bit-identical to the CPU backend)
 //   mxfp4_situ_mlp_group / _batch / _grid, mxfp4_situ_moe and their
 //   prefetch / _prepared forms  -> k3xb_acquire_expert_stack + k3xb_expert_grid_host
 //                                  (dims not multiples of 128: single resident

@@ -80,6 +80,9 @@ int launch_linear_bf16(k3xb_ctx* ctx, const float* x, const uint16_t* W, uint32_
 int launch_split_terms(k3xb_ctx* ctx, const float* x, uint32_t T, uint32_t K, uint32_t terms, uint16_t* xterms);
 int launch_linear_terms(k3xb_ctx* ctx, const uint16_t* xterms, uint32_t terms, const uint16_t* W, uint32_t T,
                         uint32_t rows, uint32_t K, int round_out, float* out);
+// dense.cu — f32 dense products in the reference CPU backend's FP64 column order
+int launch_dense_matvec(k3xb_ctx* ctx, const float* W, uint32_t rows, uint32_t cols, const float* x, uint32_t T,
+                        float* y);
 // resident.cu — the resident weight table
 void release_resident(k3xb_ctx* ctx);
 void resident_stats(const k3xb_ctx* ctx, k3xb_stats* out);

@@ -207,6 +207,9 @@ def library() -> C.CDLL:
             "k3xb_set_profiling": [vp, C.c_int],
             "k3xb_get_profile": [vp, C.POINTER(PhaseTime), C.POINTER(u64)],
             "k3xb_kda_block_host": [vp, C.POINTER(KdaLayer), u32, vp, u32, vp, vp, vp],
+            "k3xb_dense_matvec": [vp, vp, u32, u32, vp, u32, vp],
+            "k3xb_dense_matvec_host": [vp, vp, u32, u32, vp, vp],
+            "k3xb_dense_situ_mlp_host": [vp, vp, vp, vp, u32, u32, u32, vp, C.c_float, C.c_float, vp],
             "k3xb_kda_block_held": [vp, C.POINTER(KdaLayer), u32, vp, u32, u32, C.c_int32, vp, vp, vp],
         }
         for name, args in sigs.items():
@@ -522,6 +525,31 @@ class Context:
                                                  conv.ctypes.data, recurrent.ctypes.data, out.ctypes.data),
                     "kda_block_host")
         return out
+
+    def dense_matvec(self, W, x, y):
+        """y [T][rows] = W [rows][cols] x [T][cols] (device float32 tensors),
+        the reference CPU backend's FP64 column-order sums."""
+        rows, cols = W.shape
+        self._check(self.lib.k3xb_dense_matvec(self.h, _p(W), rows, cols, _p(x), x.shape[0], _p(y)), "dense_matvec")
+
+    def dense_matvec_host(self, W, x):
+        """W device [rows][cols]; HOST x [cols] -> HOST y [rows]."""
+        import numpy as np
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty(W.shape[0], np.float32)
+        self._check(self.lib.k3xb_dense_matvec_host(self.h, _p(W), W.shape[0], W.shape[1], x.ctypes.data,
+                                                    y.ctypes.data), "dense_matvec_host")
+        return y
+
+    def dense_situ_mlp_host(self, gate, up, down, x, beta, linear_beta=0.0):
+        """Device gate/up [inter][cols], down [out][inter]; HOST x -> HOST y."""
+        import numpy as np
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty(down.shape[0], np.float32)
+        self._check(self.lib.k3xb_dense_situ_mlp_host(self.h, _p(gate), _p(up), _p(down), gate.shape[0],
+                                                      gate.shape[1], down.shape[0], x.ctypes.data, beta,
+                                                      linear_beta, y.ctypes.data), "dense_situ_mlp_host")
+        return y
 
     def kda_block_held(self, w: KdaLayer, hidden, x, slot, mode, conv=None, recurrent=None):
         """k3xb_kda_block_held: x [T][H] float32 (HOST) -> out [T][H] from the

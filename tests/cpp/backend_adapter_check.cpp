@@ -153,9 +153,19 @@ int split_and_forwarding() {
     CHECK(b->kind() == BackendKind::cuda_custom && !b->device_name().empty());
     CHECK(b->runtime_stats().weight_cache_hits == 5 && b->memory_stats().current_device_bytes == 3);
     const std::vector<float> x(128, 1.0F);
-    // not on the path: forwarded
-    auto d = b->dense_matvec(x, DenseWeightView{1, x, 1, 128}, 0, ProfilePhase::decode);
-    CHECK(d && d.value().size() == 1 && d.value()[0] == 42.0F && fake->calls == 1);
+    // not on the path: forwarded (a single MXFP4 product; a dense weight without a tensor id)
+    auto mv = b->mxfp4_matvec(x, Mxfp4WeightView{}, 0, ProfilePhase::decode);
+    CHECK(mv && mv.value().size() == 1 && mv.value()[0] == 43.0F && fake->calls == 1);
+    auto d = b->dense_matvec(x, DenseWeightView{0, x, 1, 128}, 0, ProfilePhase::decode);
+    CHECK(d && d.value().size() == 1 && d.value()[0] == 42.0F && fake->calls == 2);
+    fake->calls = 1;
+    // a tracked dense weight is on the path: the C ABI (NULL context -> invalid_extent)
+    auto dt = b->dense_matvec(x, DenseWeightView{1, x, 1, 128}, 0, ProfilePhase::decode);
+    CHECK(!dt && dt.error() == ErrorCode::invalid_extent && fake->calls == 1);
+    // the CPU backend's shape check (backend_cpu.cpp:368-377) comes first
+    auto ds = b->dense_matvec(std::span<const float>(x).first(100), DenseWeightView{1, x, 1, 128}, 0,
+                              ProfilePhase::decode);
+    CHECK(!ds && ds.error() == ErrorCode::invalid_extent && fake->calls == 1);
     // on the path: reaches the C ABI (NULL context -> invalid_extent), never the other backend
     ExpertBuffers e(128, 128, 10);
     const std::vector<Mxfp4MlpView> experts{e.view};
@@ -177,7 +187,7 @@ int no_rest() {
     BackendOptions o{};
     auto b = wrap_b200_context(o, nullptr);
     const std::vector<float> x(128, 1.0F);
-    auto d = b->dense_matvec(x, DenseWeightView{1, x, 1, 128}, 0, ProfilePhase::decode);
+    auto d = b->dense_matvec(x, DenseWeightView{0, x, 1, 128}, 0, ProfilePhase::decode);
     CHECK(!d && d.error() == ErrorCode::backend_unavailable);
     auto r = b->resident_mxfp4_moe_layer(x, ResidentMoeLayerView{}, {}, {}, 1e-6F, 1.0F, std::nullopt, 0,
                                          ProfilePhase::decode);

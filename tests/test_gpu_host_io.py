@@ -155,3 +155,32 @@ def test_kda_block_held_split_equals_one_call(torch, ctx, rs):
     with pytest.raises(k3xb.K3xbError) as e:
         ctx.kda_block_held(k3xb.kda_layer_desc(wd2), H, x[:1], 3, k3xb.KDA_CONTINUE)
     assert e.value.status == k3xb.INVALID_STATE
+
+
+def test_dense_matvec_bit_identical_to_the_cpu_backend(torch, ctx, rs):
+    """k3xb_dense_matvec / _host (dense_matvec, backend_cpu.cpp:23-47): one
+    FP64 chain per row in column order, so bit-identical to the reference
+    CPU backend's (the restatement is pinned to it in test_oracle_pin.py),
+    over odd shapes, unaligned rows, several tokens and a released-size
+    matrix; dense_situ_mlp within 1e-5 (the activation's tanhf/expf are the
+    device's)."""
+    g = np.random.default_rng(172)
+    for rows, cols, T in ((1, 1, 1), (7, 33, 2), (130, 257, 3), (7168, 2048, 1)):
+        w = (g.normal(0, 1, size=(rows, cols)) * np.exp(g.normal(0, 2, size=(rows, cols)))).astype(np.float32)
+        x = g.normal(0, 1, size=(T, cols)).astype(np.float32)
+        wd = to_dev(torch, w)
+        y = torch.empty((T, rows), dtype=torch.float32, device="cuda")
+        ctx.dense_matvec(wd, to_dev(torch, x), y)
+        ctx.sync()
+        got = y.cpu().numpy()
+        for t in range(T):
+            want = rs.dense_matvec(x[t], w)
+            np.testing.assert_array_equal(got[t], want, err_msg=f"{rows}x{cols} token {t}")
+        np.testing.assert_array_equal(ctx.dense_matvec_host(wd, x[0]), rs.dense_matvec(x[0], w))
+    inter, cols, out_rows = 256, 512, 384
+    gate, up = (g.normal(0, 0.05, size=(inter, cols)).astype(np.float32) for _ in range(2))
+    down = g.normal(0, 0.05, size=(out_rows, inter)).astype(np.float32)
+    x = g.normal(0, 1, size=cols).astype(np.float32)
+    for beta, lin in ((4.0, 0.0), (2.0, 25.0)):
+        got = ctx.dense_situ_mlp_host(to_dev(torch, gate), to_dev(torch, up), to_dev(torch, down), x, beta, lin)
+        np.testing.assert_allclose(got, rs.dense_situ_mlp(x, gate, up, down, beta, lin), rtol=1e-5, atol=1e-7)
