@@ -735,6 +735,9 @@ class ReferenceOnB200:
         self.lib = L
         L.k3xr_official_layer_b200.argtypes = [C.c_int, C.c_int, _sz, C.c_void_p, C.c_void_p] + [_u16p] * 6 + [
             C.c_float, _f32p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p, _f32p, _u32p, C.c_char_p, _sz]
+        L.k3xr_official_two_layer_b200.argtypes = [C.c_int] + [C.c_void_p] * 2 + [C.c_void_p, C.c_float, _f32p,
+                                                                                 _f32p] + [C.c_void_p] * 4 + [
+            _f32p, C.c_char_p, _sz]
 
     def official_layer(self, layer: dict, hidden_in, block, conv, recurrent, device=0, device_route=False,
                        kda_split=0):
@@ -758,6 +761,30 @@ class ReferenceOnB200:
         if st:
             raise OracleError(st, "official_layer_cuda on B200Backend: " + err.value.decode(errors="replace"))
         return out, ids, (cq, ck, cv, rec)
+
+
+    def official_two_layer(self, layers, hidden_in, block, convs, recs, device=0):
+        """official_two_layer_cuda(B200Backend, host_round_trip): the
+        arguments and results of Reference.official_two_layer."""
+        structs = [(kda_struct(L["kda"]), moe_struct(L["moe"])) for L in layers]
+        kws = (C.c_void_p * 2)(*[C.cast(C.pointer(k[0]), C.c_void_p) for k, _ in structs])
+        mws = (C.c_void_p * 2)(*[C.cast(C.pointer(m[0]), C.c_void_p) for _, m in structs])
+        names = ("self_residual_norm", "self_residual_proj", "input_norm", "moe_residual_norm",
+                 "moe_residual_proj", "post_norm")
+        norm_arrays = [[_c(L[k], np.uint16) for k in names] for L in layers]
+        norms = ((C.c_void_p * 6) * 2)(*[(C.c_void_p * 6)(*[a.ctypes.data for a in row]) for row in norm_arrays])
+        states = [[np.array(a, np.uint16, copy=True) for a in conv] + [np.array(r, np.float32, copy=True)]
+                  for conv, r in zip(convs, recs)]
+        ptrs = [(C.c_void_p * 2)(*[states[l][i].ctypes.data for l in range(2)]) for i in range(4)]
+        hidden_in, block = _c(hidden_in, np.float32), _c(block, np.float32)
+        out = np.zeros_like(hidden_in)
+        err = C.create_string_buffer(512)
+        st = self.lib.k3xr_official_two_layer_b200(device, kws, mws, norms, layers[0]["rms_eps"], hidden_in, block,
+                                                   *ptrs, out, err, len(err))
+        del structs, norm_arrays
+        if st:
+            raise OracleError(st, "official_two_layer_cuda on B200Backend: " + err.value.decode(errors="replace"))
+        return out, [tuple(s) for s in states]
 
 
 def have_reference_on_b200() -> bool:

@@ -71,3 +71,7 @@ def test_reference_layer_driver_harness_loads_and_reports_no_gpu():
                                          f["recurrent"])
     assert e.value.status == 17, str(e.value)
     assert np.isfinite(f["hidden"]).all()
+    with pytest.raises(OracleError) as e:
+        ReferenceOnB200().official_two_layer([layer, layer], f["hidden"][:2], f["block"][:2],
+                                             [(f["conv_q"], f["conv_k"], f["conv_v"])] * 2, [f["recurrent"]] * 2)
+    assert e.value.status == 17, str(e.value)
