@@ -552,19 +552,25 @@ int k3xb_attention_residual_norm(k3xb_ctx* ctx, const float* a,
 
 /* prepare_official_moe_route (backend.hpp:384-389; the reference's CUDA
  * backend_cuda.cu:3478-3699) for one position: the MoE input
- * prepare_official_moe_input makes of (prefix, block) (as
- * k3xb_attention_residual_norm with delta NULL) and its router logits
- * (float of the FP64 sum in h order, bit-identical to
- * route_official_moe_logits' input). HOST prefix [H], block [H], hidden_out
- * [H] (the prepared input) and logits_out [E]; norms, proj and router
- * [E][H] are device bf16 words. Returns after the results are on the host. */
-int k3xb_prepare_moe_route_host(k3xb_ctx* ctx, const float* prefix,
-                                const float* block, uint32_t hidden,
-                                const uint16_t* residual_norm,
+ * prepare_official_moe_input makes of (a, block), as
+ * k3xb_attention_residual_norm, and its router logits (float of the FP64
+ * sum in h order, bit-identical to route_official_moe_logits' input). With
+ * delta (may be NULL) the first source is the prefix
+ * round_bf16(round_bf16(a) + delta), also written to prefix_out; this is the
+ * layer front's "prefix from the KDA output" (backend_cuda.cu:3342-3359).
+ * router NULL: no logits (experts and logits_out unused), which with the
+ * input norm in place of post_norm is the layer's KDA input preparation.
+ * HOST a, delta, block, prefix_out, hidden_out [H] and logits_out [E];
+ * norms, proj and router [E][H] are device bf16 words. Returns after the
+ * results are on the host. */
+int k3xb_prepare_moe_route_host(k3xb_ctx* ctx, const float* a,
+                                const float* delta, const float* block,
+                                uint32_t hidden, const uint16_t* residual_norm,
                                 const uint16_t* residual_proj,
                                 const uint16_t* post_norm, float eps,
                                 const uint16_t* router, uint32_t experts,
-                                float* hidden_out, float* logits_out);
+                                float* prefix_out, float* hidden_out,
+                                float* logits_out);
 
 /* One KDA + MoE layer: official_layer_cpu (official_layer.cpp:134-244) with
  * the plain hidden-space MoE (official_moe.cpp:271-344 without the latent

@@ -735,7 +735,7 @@ class ReferenceOnB200:
         self.lib = L
         L.k3xr_official_layer_b200.argtypes = [C.c_int, C.c_int, _sz, C.c_void_p, C.c_void_p] + [_u16p] * 6 + [
             C.c_float, _f32p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p, _f32p, _u32p, C.c_char_p, _sz]
-        L.k3xr_official_two_layer_b200.argtypes = [C.c_int] + [C.c_void_p] * 2 + [C.c_void_p, C.c_float, _f32p,
+        L.k3xr_official_two_layer_b200.argtypes = [C.c_int, C.c_int] + [C.c_void_p] * 2 + [C.c_void_p, C.c_float, _f32p,
                                                                                  _f32p] + [C.c_void_p] * 4 + [
             _f32p, C.c_char_p, _sz]
 
@@ -763,9 +763,10 @@ class ReferenceOnB200:
         return out, ids, (cq, ck, cv, rec)
 
 
-    def official_two_layer(self, layers, hidden_in, block, convs, recs, device=0):
-        """official_two_layer_cuda(B200Backend, host_round_trip): the
-        arguments and results of Reference.official_two_layer."""
+    def official_two_layer(self, layers, hidden_in, block, convs, recs, device=0, device_closure=False):
+        """official_two_layer_cuda(B200Backend) in its host_round_trip (or,
+        device_closure, its front/tail) mode: the arguments and results of
+        Reference.official_two_layer."""
         structs = [(kda_struct(L["kda"]), moe_struct(L["moe"])) for L in layers]
         kws = (C.c_void_p * 2)(*[C.cast(C.pointer(k[0]), C.c_void_p) for k, _ in structs])
         mws = (C.c_void_p * 2)(*[C.cast(C.pointer(m[0]), C.c_void_p) for _, m in structs])
@@ -779,7 +780,7 @@ class ReferenceOnB200:
         hidden_in, block = _c(hidden_in, np.float32), _c(block, np.float32)
         out = np.zeros_like(hidden_in)
         err = C.create_string_buffer(512)
-        st = self.lib.k3xr_official_two_layer_b200(device, kws, mws, norms, layers[0]["rms_eps"], hidden_in, block,
+        st = self.lib.k3xr_official_two_layer_b200(device, 1 if device_closure else 0, kws, mws, norms, layers[0]["rms_eps"], hidden_in, block,
                                                    *ptrs, out, err, len(err))
         del structs, norm_arrays
         if st:

@@ -208,13 +208,16 @@ int k3xr_official_layer_b200(int device, int device_route, std::size_t kda_split
     return 0;
 }
 
-// official_two_layer_cuda (official_two_layer.cpp:102-414) in its
-// host_round_trip mode over B200Backend: two positions, position-major
-// through layers 1 and 2, each layer's KDA state seeded on the device at
-// position 0 and published at position 1 (device_seed / device_publish),
-// device route preparation. The arguments of k3xr_official_two_layer plus
-// the device; the state arrays receive the final states, out [2][H].
-int k3xr_official_two_layer_b200(int device, const k3xr_kda_weights* const kw[2], const k3xr_moe_layer* const mw[2],
+// official_two_layer_cuda (official_two_layer.cpp:102-414) over
+// B200Backend: two positions, position-major through layers 1 and 2, each
+// layer's KDA state seeded on the device at position 0 and published at
+// position 1 (device_seed / device_publish). host_round_trip mode: each
+// layer an official_layer_cuda with device route preparation;
+// device_closure: official_layer_front / _tail, layer 1's output held for
+// layer 2's front. The arguments of k3xr_official_two_layer plus the device
+// and the mode; the state arrays receive the final states, out [2][H].
+int k3xr_official_two_layer_b200(int device, int device_closure, const k3xr_kda_weights* const kw[2],
+                                 const k3xr_moe_layer* const mw[2],
                                  const std::uint16_t* const norms[2][6], float eps, const float* hidden_in,
                                  const float* block, std::uint16_t* const conv_q[2], std::uint16_t* const conv_k[2],
                                  std::uint16_t* const conv_v[2], float* const recurrent[2], float* out, char* err,
@@ -251,7 +254,9 @@ int k3xr_official_two_layer_b200(int device, const k3xr_kda_weights* const kw[2]
     const k3x::OfficialKdaConfig config{H, h, d, W, eps, kw[0]->gate_lower_bound};
     auto r = k3x::official_two_layer_cuda(*made.value(), inputs, layers, states, config, mw[0]->top_k, 0x1p64F,
                                           std::nullopt, k3x::ProfilePhase::decode,
-                                          k3x::OfficialTwoLayerCudaMode::host_round_trip, nullptr, nullptr);
+                                          device_closure ? k3x::OfficialTwoLayerCudaMode::device_closure
+                                                         : k3x::OfficialTwoLayerCudaMode::host_round_trip,
+                                          nullptr, nullptr);
     if (!r) {
         message(err, err_len, r.message());
         return static_cast<int>(r.error());

@@ -198,7 +198,7 @@ public:
                                                         std::span<const float> contributions, float epsilon,
                                                         float beta, std::optional<float> linear,
                                                         std::uint32_t layer, ProfilePhase phase) override {
-        prepared_.active = false;
+        end_prepared();
         if (hidden.empty() || hidden.size() != prefix.size() || !finite(hidden) || !finite(prefix))
             return Result<OfficialMoeFfnResult>::failure(ErrorCode::invalid_mxfp4);
         return official_ffn(hidden, prefix, false, w, experts, ids, contributions, epsilon, beta, linear, layer,
@@ -215,63 +215,13 @@ public:
                                                                      std::span<const float> block,
                                                                      OfficialMoeRoutePrepareView w, float epsilon,
                                                                      std::uint32_t layer, ProfilePhase) override {
-        using R = Result<OfficialMoeRoutePrepareResult>;
         const std::size_t H = prefix.size();
-        const auto valid_bf16 = [](const Bf16WeightView& v, std::size_t rows, std::size_t cols) {
-            return v.tensor_id && v.rows == rows && v.cols == cols && rows && cols && rows <= SIZE_MAX / cols &&
-                   v.values.size() == rows * cols;
-        };
-        if (!H || block.size() != H || !finite(prefix) || !finite(block) || !std::isfinite(epsilon) ||
-            epsilon <= 0.0F || !w.residual_norm.tensor_id || w.residual_norm.values.size() != H ||
-            !valid_bf16(w.residual_proj, 1, H) || !w.post_norm.tensor_id || w.post_norm.values.size() != H ||
-            !valid_bf16(w.router, w.router.rows, H))
-            return R::failure(ErrorCode::invalid_extent);
-        std::unordered_set<std::uint64_t> tensors;
-        for (const std::uint64_t id : {w.residual_norm.tensor_id, w.residual_proj.tensor_id, w.post_norm.tensor_id,
-                                       w.router.tensor_id})
-            if (!tensors.insert(id).second) return R::failure(ErrorCode::invalid_extent);
-        // bf16 words with an all-ones exponent are refused, each tensor scanned at its first use
-        const std::pair<std::uint64_t, std::span<const std::uint16_t>> scans[] = {
-            {w.residual_norm.tensor_id, w.residual_norm.values},
-            {w.residual_proj.tensor_id, w.residual_proj.values},
-            {w.post_norm.tensor_id, w.post_norm.values},
-            {w.router.tensor_id, w.router.values}};
-        for (const auto& [id, values] : scans) {
-            if (scanned_.count(id)) continue;
-            for (const std::uint16_t word : values)
-                if ((word & 0x7f80U) == 0x7f80U) return R::failure(ErrorCode::invalid_extent);
-            scanned_.insert(id);
-        }
-        ErrorCode st = ErrorCode::ok;
-        const auto bf16 = [&](std::uint64_t id, std::span<const std::uint16_t> v, std::size_t rows, std::size_t cols) {
-            return static_cast<const std::uint16_t*>(
-                resident(id, K3XB_WEIGHT_BF16, rows, cols, v.data(), v.size() * 2, &st));
-        };
-        const std::size_t E = w.router.rows;
-        const std::uint16_t* rnorm = bf16(w.residual_norm.tensor_id, w.residual_norm.values, 1, H);
-        const std::uint16_t* rproj = bf16(w.residual_proj.tensor_id, w.residual_proj.values, 1, H);
-        const std::uint16_t* post = bf16(w.post_norm.tensor_id, w.post_norm.values, 1, H);
-        const std::uint16_t* router = bf16(w.router.tensor_id, w.router.values, E, H);
-        if (st != ErrorCode::ok) return R::failure(st, last_error());
-        prepared_.active = false;
-        std::vector<float> hidden(H);
-        OfficialMoeRoutePrepareResult out;
-        out.router_logits.resize(E);
-        const int rc = k3xb_prepare_moe_route_host(ctx_, prefix.data(), block.data(), static_cast<std::uint32_t>(H),
-                                                   rnorm, rproj, post, epsilon, router, static_cast<std::uint32_t>(E),
-                                                   hidden.data(), out.router_logits.data());
-        if (rc != K3XB_OK) return R::failure(static_cast<ErrorCode>(rc), last_error());
-        if (!finite(out.router_logits)) return R::failure(ErrorCode::backend_unavailable, "non-finite router logits");
-        if (!++prepared_.generation) ++prepared_.generation;
-        prepared_.layer = layer;
-        prepared_.prefix.assign(prefix.begin(), prefix.end());
-        prepared_.hidden = std::move(hidden);
-        prepared_.active = true;
-        out.executed = true;
-        out.prepared = {owner_, prepared_.generation};
-        return R::success(std::move(out));
+        if (!H || block.size() != H || !finite(prefix) || !finite(block))
+            return Result<OfficialMoeRoutePrepareResult>::failure(ErrorCode::invalid_extent);
+        return prepare_route(prefix, {}, block, w, epsilon, layer, 2);
     }
 
+    // Consumes the prepared route of the same layer (backend_cuda.cu:3738-3748, :3779-3784).
     // Consumes the prepared route of the same layer (backend_cuda.cu:3738-3748, :3779-3784).
     Result<OfficialMoeFfnResult> official_mxfp4_moe_ffn_prepared(OfficialMoePreparedToken token, OfficialMoeFfnView w,
                                                                  std::span<const Mxfp4MlpView> experts,
@@ -290,11 +240,241 @@ public:
     Result<bool> discard_official_moe_prepared(OfficialMoePreparedToken token) override {
         if (!prepared_.active || token.owner != owner_ || token.generation != prepared_.generation)
             return Result<bool>::failure(ErrorCode::invalid_state);
-        prepared_.active = false;
+        end_prepared();
+        return Result<bool>::success(true);
+    }
+
+    // ---- a layer's front and tail with its hidden rows held between them
+    // (official_layer_front / _tail / discard_official_layer_hidden,
+    // backend_cuda.cu:3161-3476: the device_closure mode of
+    // official_two_layer_cuda). Two hidden slots (free, live, prepared) with
+    // the reference's token rules; the rows a slot holds (hidden input and
+    // block source, a few KB) stay in the adapter between calls, the compute
+    // runs on the device.
+    Result<OfficialLayerFrontResult> official_layer_front(std::span<const float> host_hidden,
+                                                          std::span<const float> host_block,
+                                                          OfficialLayerHiddenToken in, OfficialLayerFrontWeights w,
+                                                          OfficialKdaCudaStateView state, OfficialKdaCudaConfig config,
+                                                          std::uint32_t layer, ProfilePhase phase,
+                                                          OfficialKdaStateControl control) override {
+        using R = Result<OfficialLayerFrontResult>;
+        using Mode = OfficialKdaStateMode;
+        const std::size_t H = config.hidden_size;
+        const bool host_input = !host_hidden.empty() || !host_block.empty();
+        const bool token_input = in.owner || in.generation || in.producing_layer || in.width || in.slot;
+        if (layer < 1 || layer > 2 || !H || H > SIZE_MAX / 16 || host_input == token_input ||
+            (control.mode != Mode::device_seed && control.mode != Mode::device_continue &&
+             control.mode != Mode::device_publish) ||
+            (host_input && (layer != 1 || host_hidden.size() != H || host_block.size() != H || !finite(host_hidden) ||
+                            !finite(host_block))) ||
+            !w.self_residual_norm.tensor_id || w.self_residual_norm.values.size() != H ||
+            !w.input_norm.tensor_id || w.input_norm.values.size() != H)
+            return R::failure(ErrorCode::invalid_extent);
+        if (prepared_.active) return R::failure(ErrorCode::invalid_state);
+        std::uint32_t slot = 2;
+        if (host_input) {
+            for (const HiddenSlot& s : hidden_slots_)
+                if (s.state != HiddenSlot::kFree) return R::failure(ErrorCode::invalid_state);
+            slot = 0;
+        } else {
+            if (in.owner != owner_ || !in.generation || in.slot >= 2 || in.producing_layer + 1 != layer ||
+                in.width != H)
+                return R::failure(ErrorCode::invalid_state);
+            slot = in.slot;
+            const HiddenSlot& s = hidden_slots_[slot];
+            if (s.state != HiddenSlot::kLive || s.generation != in.generation ||
+                s.producing_layer != in.producing_layer || s.width != in.width ||
+                hidden_slots_[1 - slot].state != HiddenSlot::kFree)
+                return R::failure(ErrorCode::invalid_state);
+        }
+        // the self-attention residual's weights: distinct ids, well-formed bf16 (backend_cuda.cu:3271-3318)
+        const Bf16WeightView self_views[] = {{w.self_residual_norm.values, 1, H, w.self_residual_norm.tensor_id},
+                                             w.self_residual_proj,
+                                             {w.input_norm.values, 1, H, w.input_norm.tensor_id}};
+        std::unordered_set<std::uint64_t> tensors;
+        for (const auto& v : self_views)
+            if (!tensors.insert(v.tensor_id).second || !v.tensor_id || v.rows != 1 || v.cols != H ||
+                v.values.size() != H || !scan_bf16(v.tensor_id, v.values))
+                return R::failure(ErrorCode::invalid_extent);
+        ErrorCode st = ErrorCode::ok;
+        const std::uint16_t* dev[3];
+        for (int i = 0; i < 3; ++i)
+            if (!(dev[i] = static_cast<const std::uint16_t*>(resident(self_views[i].tensor_id, K3XB_WEIGHT_BF16, 1, H,
+                                                                      self_views[i].values.data(), H * 2, &st))))
+                return R::failure(st, last_error());
+        HiddenSlot& hs = hidden_slots_[slot];
+        if (host_input) {
+            hs.hidden.assign(host_hidden.begin(), host_hidden.end());
+            hs.block.assign(host_block.begin(), host_block.end());
+        }
+        hs.state = HiddenSlot::kPrepared;
+        // the KDA input: attention residual over (hidden, block), input norm (official_layer.cpp:159-172)
+        std::vector<float> normalized(H);
+        const int rc = k3xb_prepare_moe_route_host(ctx_, hs.hidden.data(), nullptr, hs.block.data(),
+                                                   static_cast<std::uint32_t>(H), dev[0], dev[1], dev[2],
+                                                   config.rms_norm_epsilon, nullptr, 0, nullptr, normalized.data(),
+                                                   nullptr);
+        if (rc != K3XB_OK) {
+            hs.state = HiddenSlot::kFree;
+            return R::failure(static_cast<ErrorCode>(rc), last_error());
+        }
+        auto kda = official_kda(normalized, w.kda, state, config, layer, phase, control);
+        if (!kda) {
+            hs.state = HiddenSlot::kFree;
+            return R::failure(kda.error(), kda.message());
+        }
+        // the prefix round_bf16(round_bf16(hidden) + kda) and its MoE route (official_layer.cpp:190-205)
+        auto route = prepare_route(hs.hidden, kda.value().output, hs.block, w.moe, config.rms_norm_epsilon, layer,
+                                   slot);
+        if (!route) {
+            if (kda.value().device_state.owner) (void)discard_official_kda_device_state(kda.value().device_state);
+            hs.state = HiddenSlot::kFree;
+            return R::failure(route.error(), route.message());
+        }
+        OfficialLayerFrontResult out;
+        out.executed = true;
+        out.kda = std::move(kda.value());
+        out.kda.output.clear();   // the KDA output stays with the layer (the reference keeps it on the device)
+        out.route = std::move(route.value());
+        return R::success(std::move(out));
+    }
+
+    Result<OfficialLayerTailResult> official_layer_tail(OfficialMoePreparedToken prepared, OfficialMoeFfnView w,
+                                                        std::span<const Mxfp4MlpView> experts,
+                                                        std::span<const std::uint32_t> ids,
+                                                        std::span<const float> contributions, float epsilon,
+                                                        float beta, std::optional<float> linear, std::uint32_t layer,
+                                                        ProfilePhase phase, bool retain_hidden) override {
+        using R = Result<OfficialLayerTailResult>;
+        if (!prepared_.active || prepared_.hidden_slot >= 2 || prepared.owner != owner_ ||
+            prepared.generation != prepared_.generation || prepared_.layer != layer)
+            return R::failure(ErrorCode::invalid_state);
+        const std::uint32_t source = prepared_.hidden_slot, target = 1 - source;
+        if (hidden_slots_[source].state != HiddenSlot::kPrepared ||
+            (retain_hidden && hidden_slots_[target].state != HiddenSlot::kFree))
+            return R::failure(ErrorCode::invalid_state);
+        auto moe = official_mxfp4_moe_ffn_prepared(prepared, w, experts, ids, contributions, epsilon, beta, linear,
+                                                   layer, phase);
+        if (!moe) {
+            if (prepared_.active && prepared.generation == prepared_.generation) {
+                end_prepared();
+            } else {
+                hidden_slots_[source].state = HiddenSlot::kFree;
+                prepared_.hidden_slot = 2;
+            }
+            return R::failure(moe.error(), moe.message());
+        }
+        hidden_slots_[source].state = HiddenSlot::kFree;
+        OfficialLayerTailResult out;
+        out.executed = true;
+        out.selected_expert_ids = std::move(moe.value().selected_expert_ids);
+        if (retain_hidden) {   // the output is the next layer's hidden input; the block source carries over
+            if (!++hidden_generation_) ++hidden_generation_;
+            HiddenSlot& t = hidden_slots_[target];
+            t.hidden = std::move(moe.value().output);
+            t.block = hidden_slots_[source].block;
+            t.generation = hidden_generation_;
+            t.producing_layer = layer;
+            t.width = t.hidden.size();
+            t.state = HiddenSlot::kLive;
+            out.hidden = {owner_, hidden_generation_, layer, t.width, target};
+        } else {
+            out.output = std::move(moe.value().output);
+        }
+        prepared_.hidden_slot = 2;
+        return R::success(std::move(out));
+    }
+
+    Result<bool> discard_official_layer_hidden(OfficialLayerHiddenToken token) override {
+        if (token.owner != owner_ || token.slot >= 2) return Result<bool>::failure(ErrorCode::invalid_state);
+        HiddenSlot& s = hidden_slots_[token.slot];
+        if (s.state != HiddenSlot::kLive || s.generation != token.generation ||
+            s.producing_layer != token.producing_layer || s.width != token.width)
+            return Result<bool>::failure(ErrorCode::invalid_state);
+        s.state = HiddenSlot::kFree;
         return Result<bool>::success(true);
     }
 
 private:
+    // A prepared route ends (a discard, a new preparation, a direct FFN
+    // call); the hidden slot it held is freed (backend_cuda.cu:3594-3603).
+    void end_prepared() {
+        if (prepared_.active && prepared_.hidden_slot < 2) hidden_slots_[prepared_.hidden_slot].state = HiddenSlot::kFree;
+        prepared_.hidden_slot = 2;
+        prepared_.active = false;
+    }
+
+    // bf16 words with an all-ones exponent are refused; each tensor id is scanned at its first use
+    bool scan_bf16(std::uint64_t id, std::span<const std::uint16_t> values) {
+        if (scanned_.count(id)) return true;
+        for (const std::uint16_t word : values)
+            if ((word & 0x7f80U) == 0x7f80U) return false;
+        scanned_.insert(id);
+        return true;
+    }
+
+    // prepare_official_moe_route's checks (backend_cuda.cu:3478-3570,
+    // invalid_extent) and work: from the prefix `a`, or with `delta` from the
+    // prefix round_bf16(round_bf16(a) + delta); `hidden_slot` is the layer
+    // hidden slot the route holds (2: none).
+    Result<OfficialMoeRoutePrepareResult> prepare_route(std::span<const float> a, std::span<const float> delta,
+                                                        std::span<const float> block,
+                                                        const OfficialMoeRoutePrepareView& w, float epsilon,
+                                                        std::uint32_t layer, std::uint32_t hidden_slot) {
+        using R = Result<OfficialMoeRoutePrepareResult>;
+        const std::size_t H = a.size();
+        const auto valid_bf16 = [](const Bf16WeightView& v, std::size_t rows, std::size_t cols) {
+            return v.tensor_id && v.rows == rows && v.cols == cols && rows && cols && rows <= SIZE_MAX / cols &&
+                   v.values.size() == rows * cols;
+        };
+        if ((!delta.empty() && delta.size() != H) || !std::isfinite(epsilon) ||
+            epsilon <= 0.0F || !w.residual_norm.tensor_id || w.residual_norm.values.size() != H ||
+
+            !valid_bf16(w.residual_proj, 1, H) || !w.post_norm.tensor_id || w.post_norm.values.size() != H ||
+            !valid_bf16(w.router, w.router.rows, H))
+            return R::failure(ErrorCode::invalid_extent);
+        std::unordered_set<std::uint64_t> tensors;
+        for (const std::uint64_t id : {w.residual_norm.tensor_id, w.residual_proj.tensor_id, w.post_norm.tensor_id,
+                                       w.router.tensor_id})
+            if (!tensors.insert(id).second) return R::failure(ErrorCode::invalid_extent);
+        if (!scan_bf16(w.residual_norm.tensor_id, w.residual_norm.values) ||
+            !scan_bf16(w.residual_proj.tensor_id, w.residual_proj.values) ||
+            !scan_bf16(w.post_norm.tensor_id, w.post_norm.values) || !scan_bf16(w.router.tensor_id, w.router.values))
+            return R::failure(ErrorCode::invalid_extent);
+        ErrorCode st = ErrorCode::ok;
+        const auto bf16 = [&](std::uint64_t id, std::span<const std::uint16_t> v, std::size_t rows, std::size_t cols) {
+            return static_cast<const std::uint16_t*>(
+                resident(id, K3XB_WEIGHT_BF16, rows, cols, v.data(), v.size() * 2, &st));
+        };
+        const std::size_t E = w.router.rows;
+        const std::uint16_t* rnorm = bf16(w.residual_norm.tensor_id, w.residual_norm.values, 1, H);
+        const std::uint16_t* rproj = bf16(w.residual_proj.tensor_id, w.residual_proj.values, 1, H);
+        const std::uint16_t* post = bf16(w.post_norm.tensor_id, w.post_norm.values, 1, H);
+        const std::uint16_t* router = bf16(w.router.tensor_id, w.router.values, E, H);
+        if (st != ErrorCode::ok) return R::failure(st, last_error());
+        end_prepared();
+        std::vector<float> hidden(H), prefix(delta.empty() ? 0 : H);
+        OfficialMoeRoutePrepareResult out;
+        out.router_logits.resize(E);
+        const int rc = k3xb_prepare_moe_route_host(ctx_, a.data(), delta.empty() ? nullptr : delta.data(), block.data(),
+                                                   static_cast<std::uint32_t>(H), rnorm, rproj, post, epsilon, router,
+                                                   static_cast<std::uint32_t>(E), prefix.empty() ? nullptr : prefix.data(),
+                                                   hidden.data(), out.router_logits.data());
+        if (rc != K3XB_OK) return R::failure(static_cast<ErrorCode>(rc), last_error());
+        if (!finite(out.router_logits)) return R::failure(ErrorCode::backend_unavailable, "non-finite router logits");
+        if (!++prepared_.generation) ++prepared_.generation;
+        prepared_.layer = layer;
+        if (delta.empty()) prepared_.prefix.assign(a.begin(), a.end());
+        else prepared_.prefix = std::move(prefix);
+        prepared_.hidden = std::move(hidden);
+        prepared_.hidden_slot = hidden_slot;
+        prepared_.active = true;
+        out.executed = true;
+        out.prepared = {owner_, prepared_.generation};
+        return R::success(std::move(out));
+    }
+
+
     // backend_cpu.cpp:368-377
     static bool valid_dense(std::span<const float> input, const DenseWeightView& w) {
         if (input.size() != w.cols || w.rows > w.values.size() || (w.cols != 0 && w.rows > w.values.size() / w.cols))
@@ -780,8 +960,18 @@ private:
         bool active = false;
         std::uint64_t generation = 0;
         std::uint32_t layer = 0;
+        std::uint32_t hidden_slot = 2;   // the layer hidden slot it holds (2: none)
         std::vector<float> prefix, hidden;
     } prepared_;
+    // a layer's hidden rows between its tail and the next layer's front
+    struct HiddenSlot {
+        enum State { kFree, kLive, kPrepared } state = kFree;
+        std::uint64_t generation = 0;
+        std::uint32_t producing_layer = 0;
+        std::size_t width = 0;
+        std::vector<float> hidden, block;
+    } hidden_slots_[2];
+    std::uint64_t hidden_generation_ = 0;
     const std::uint64_t owner_ = next_owner();
     std::unordered_set<std::uint64_t> scanned_;   // bf16 route weights checked for non-finite words
     // the KDA states kept on the device for layers 1 and 2 (k3xb_kda_block_held slots 0 and 1)

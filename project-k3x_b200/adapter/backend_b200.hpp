@@ -24,6 +24,9 @@
 //   prepare_official_moe_route, official_mxfp4_moe_ffn_prepared, discard_
 //   official_moe_prepared (device route preparation)
 //                                -> k3xb_prepare_moe_route_host, then as above
+//   official_layer_front / _tail, discard_official_layer_hidden (the
+//   two-layer driver's device_closure mode; the hidden rows a slot holds stay
+//   in the adapter)       -> k3xb_prepare_moe_route_host + the KDA and FFN rows
 //   official_kda, host-roundtrip state  -> k3xb_acquire_weight + k3xb_kda_block_host
 //   official_kda, device_seed / _continue / _publish (layers 1 and 2, the
 //   reference's token rules) and discard_official_kda_device_state

@@ -1330,42 +1330,51 @@ int k3xb_attention_residual_norm(k3xb_ctx* ctx, const float* a, const float* del
     return launch_attnres_norm(ctx, a, delta, block, rnorm, rproj, post, T, H, eps, prefix_out, out);
 }
 
-int k3xb_prepare_moe_route_host(k3xb_ctx* ctx, const float* prefix_host, const float* block_host, uint32_t H,
-                                const uint16_t* rnorm, const uint16_t* rproj, const uint16_t* post, float eps,
-                                const uint16_t* router, uint32_t E, float* hidden_host, float* logits_host) {
+int k3xb_prepare_moe_route_host(k3xb_ctx* ctx, const float* a_host, const float* delta_host, const float* block_host,
+                                uint32_t H, const uint16_t* rnorm, const uint16_t* rproj, const uint16_t* post, float eps,
+                                const uint16_t* router, uint32_t E, float* prefix_host, float* hidden_host,
+                                float* logits_host) {
     K3XB_ENTER(ctx);
-    if (!prefix_host || !block_host || !H || !rnorm || !rproj || !post || !router || !E || !hidden_host ||
-        !logits_host)
+    if (!a_host || !block_host || !H || !rnorm || !rproj || !post || !hidden_host || (delta_host && !prefix_host) ||
+        (router && (!E || !logits_host)))
         return fail(ctx, K3XB_INVALID_EXTENT, "prepare moe route arguments");
     if (!(eps > 0.0f)) return fail(ctx, K3XB_INVALID_EXTENT, "eps must be positive");
+    const uint32_t n_logits = router ? E : 0;
     Sizer sz;
-    sz.take<float>(2 * size_t(H));   // prefix, block (one upload each)
-    sz.take<float>(H);               // the prepared MoE input
-    sz.take<float>(E);               // router logits
+    sz.take<float>(3 * size_t(H));   // a, delta, block (one upload each)
+    sz.take<float>(H);               // the prefix (with delta)
+    sz.take<float>(H);               // the prepared input
+    sz.take<float>(n_logits ? n_logits : 1);
     void* base;
     int st;
     if ((st = ensure_scratch(ctx, sz.used, &base))) return st;
     Carver c(base);
-    float* in = c.take<float>(2 * size_t(H));
+    float* in = c.take<float>(3 * size_t(H));
+    float* prefix = c.take<float>(H);
     float* hidden = c.take<float>(H);
-    float* logits = c.take<float>(E);
+    float* logits = c.take<float>(n_logits ? n_logits : 1);
     const size_t hbytes = sizeof(float) * H;
-    K3XB_CUDA(ctx, cudaMemcpyAsync(in, prefix_host, hbytes, cudaMemcpyHostToDevice, ctx->stream));
-    K3XB_CUDA(ctx, cudaMemcpyAsync(in + H, block_host, hbytes, cudaMemcpyHostToDevice, ctx->stream));
-    ctx->stats.h2d_bytes += 2 * hbytes;
-    {   // prepare_official_moe_input (official_moe.cpp:156-209)
+    K3XB_CUDA(ctx, cudaMemcpyAsync(in, a_host, hbytes, cudaMemcpyHostToDevice, ctx->stream));
+    if (delta_host) K3XB_CUDA(ctx, cudaMemcpyAsync(in + H, delta_host, hbytes, cudaMemcpyHostToDevice, ctx->stream));
+    K3XB_CUDA(ctx, cudaMemcpyAsync(in + 2 * size_t(H), block_host, hbytes, cudaMemcpyHostToDevice, ctx->stream));
+    ctx->stats.h2d_bytes += (delta_host ? 3 : 2) * hbytes;
+    {   // prepare_official_moe_input (official_moe.cpp:156-209); with delta the
+        // first source is the prefix round_bf16(round_bf16(a) + delta) (official_layer.cpp:190-193)
         PhaseScope ph(ctx, K3XB_PHASE_ATTN_RESIDUAL);
-        if ((st = launch_attnres_norm(ctx, in, nullptr, in + H, rnorm, rproj, post, 1, H, eps, nullptr, hidden)))
+        if ((st = launch_attnres_norm(ctx, in, delta_host ? in + H : nullptr, in + 2 * size_t(H), rnorm, rproj, post, 1,
+                                      H, eps, delta_host ? prefix : nullptr, hidden)))
             return st;
     }
-    {   // route_official_moe_logits' input (official_moe.cpp:211-245): FP64 sums in h order
+    if (router) {   // route_official_moe_logits' input (official_moe.cpp:211-245): FP64 sums in h order
         PhaseScope ph(ctx, K3XB_PHASE_ROUTE);
         if ((st = launch_router_logits(ctx, hidden, 1, H, router, E, logits))) return st;
     }
     K3XB_CUDA(ctx, cudaMemcpyAsync(hidden_host, hidden, hbytes, cudaMemcpyDeviceToHost, ctx->stream));
-    K3XB_CUDA(ctx, cudaMemcpyAsync(logits_host, logits, sizeof(float) * E, cudaMemcpyDeviceToHost, ctx->stream));
-    ctx->stats.d2h_bytes += hbytes + sizeof(float) * E;
-    ++ctx->stats.route_calls;
+    if (delta_host) K3XB_CUDA(ctx, cudaMemcpyAsync(prefix_host, prefix, hbytes, cudaMemcpyDeviceToHost, ctx->stream));
+    if (router)
+        K3XB_CUDA(ctx, cudaMemcpyAsync(logits_host, logits, sizeof(float) * E, cudaMemcpyDeviceToHost, ctx->stream));
+    ctx->stats.d2h_bytes += (delta_host ? 2 : 1) * hbytes + sizeof(float) * n_logits;
+    if (router) ++ctx->stats.route_calls;
     return k3xb_sync(ctx);
 }
 

@@ -358,6 +358,29 @@ int official_ffn() {
     CHECK(prep(prefix, x, narrow_proj) == ErrorCode::invalid_extent);
     rt[5] = 0x7f80;   // an infinite router word
     CHECK(prep(prefix, x, pv) == ErrorCode::invalid_extent);
+
+    // a layer's front and tail (backend_cuda.cu:3161-3476)
+    std::vector<std::uint16_t> sn(128), sp(128), in(128);
+    OfficialLayerFrontWeights fw{{sn, 501}, {sp, 1, 128, 502}, {in, 503}, OfficialKdaCudaView{}, pv};
+    const OfficialKdaCudaConfig kc{128, 2, 64, 4, 1e-5F, -5.0F};
+    const auto front = [&](std::span<const float> hx, std::span<const float> bx, OfficialLayerHiddenToken tok,
+                           std::uint32_t layer, OfficialKdaStateMode mode) {
+        return b->official_layer_front(hx, bx, tok, fw, OfficialKdaCudaStateView{}, kc, layer, P,
+                                       OfficialKdaStateControl{mode, {}})
+            .error();
+    };
+    using M = OfficialKdaStateMode;
+    const OfficialLayerHiddenToken tok{7, 1, 1, 128, 0};
+    CHECK(front(x, prefix, tok, 1, M::device_seed) == ErrorCode::invalid_extent);      // host rows and a token
+    CHECK(front({}, {}, {}, 1, M::device_seed) == ErrorCode::invalid_extent);          // neither
+    CHECK(front(x, prefix, {}, 2, M::device_seed) == ErrorCode::invalid_extent);       // host rows: layer 1 only
+    CHECK(front(x, prefix, {}, 1, M::host_roundtrip) == ErrorCode::invalid_extent);    // device state modes only
+    CHECK(front(x, prefix, {}, 3, M::device_seed) == ErrorCode::invalid_extent);
+    CHECK(front({}, {}, tok, 2, M::device_continue) == ErrorCode::invalid_state);      // not this backend's token
+    CHECK(b->official_layer_tail(OfficialMoePreparedToken{1, 1}, f.view, f.experts, ids, c, 1e-6F, 1.0F,
+                                 std::nullopt, 1, P, true)
+              .error() == ErrorCode::invalid_state);                                   // nothing prepared
+    CHECK(b->discard_official_layer_hidden(tok).error() == ErrorCode::invalid_state);
     return 0;
 }
 

@@ -215,11 +215,14 @@ def test_reference_layer_driver_on_the_b200_backend(route, kda_split):
     assert_mostly_close(state[3].reshape(f["next_recurrent"].shape), f["next_recurrent"], what="recurrent state")
 
 
-def test_reference_two_layer_driver_on_the_b200_backend(rs, ref):
+@pytest.mark.parametrize("mode", ["host_round_trip", "device_closure"])
+def test_reference_two_layer_driver_on_the_b200_backend(rs, ref, mode):
     """The reference's own official_two_layer_cuda (official_two_layer.cpp:
-    102-414, host_round_trip mode: each layer's KDA state seeded on the
-    device at position 0 and published at position 1, device route
-    preparation), unchanged, over B200Backend, against the reference's
+    102-414: each layer's KDA state seeded on the device at position 0 and
+    published at position 1; host_round_trip: official_layer_cuda with
+    device route preparation per layer; device_closure: official_layer_front
+    / _tail with layer 1's output held for layer 2), unchanged, over
+    B200Backend, against the reference's
     official_two_layer_cpu run here on the same inputs (the case of
     test_oracle_pin.py::test_two_layer_stack_matches_reference): outputs
     and both layers' final states within the bars above."""
@@ -235,7 +238,8 @@ def test_reference_two_layer_driver_on_the_b200_backend(rs, ref):
     convs = [tuple(bf16_words(g.normal(0, 0.5, size=(W - 1) * h * d)) for _ in range(3)) for _ in range(2)]
     recs = [g.normal(0, 0.05, size=h * d * d).astype(np.float32) for _ in range(2)]
     want, want_states = ref.official_two_layer(layers, hidden, block, convs, recs)
-    got, got_states = ReferenceOnB200().official_two_layer(layers, hidden, block, convs, recs)
+    got, got_states = ReferenceOnB200().official_two_layer(layers, hidden, block, convs, recs,
+                                                           device_closure=mode == "device_closure")
     assert_mostly_close(got, want, what="official_two_layer_cuda on B200Backend")
     words = lambda a: (np.asarray(a, np.uint16).astype(np.uint32) << 16).view(np.float32)
     for l in range(2):
