@@ -428,6 +428,49 @@ int k3xb_dense_situ_mlp_host(k3xb_ctx* ctx, const float* gate, const float* up,
                              uint32_t out_rows, const float* x_host, float beta,
                              float linear_beta, float* y_host);
 
+/* mxfp4_matvec (backend.hpp:335-337; CPU semantics mxfp4_matmul,
+ * ops.cpp:44-76) for `tokens` inputs: y[t][r] = float(sum over c in column
+ * order of double(x[t][c]) * w[r][c]), w the decoded MXFP4 value
+ * (ldexp(e2m1, scale - 127)), bit-identical to the reference. Device packed
+ * [rows][cols/2], scales [rows][cols/32] (group 32, 0xFF refused at
+ * admission, e.g. k3xb_acquire_weight), x [tokens][cols], y [tokens][rows]. */
+int k3xb_mxfp4_matvec(k3xb_ctx* ctx, const uint8_t* packed, const uint8_t* scales,
+                      uint32_t rows, uint32_t cols, const float* x, uint32_t tokens,
+                      float* y);
+/* The same for one HOST x [cols] and HOST y [rows]. */
+int k3xb_mxfp4_matvec_host(k3xb_ctx* ctx, const uint8_t* packed, const uint8_t* scales,
+                           uint32_t rows, uint32_t cols, const float* x_host,
+                           float* y_host);
+
+/* One expert's DEVICE MXFP4 arrays (layouts of k3xb_mxfp4_expert_host). */
+typedef struct {
+    const uint8_t* gate_packed;
+    const uint8_t* gate_scales;
+    const uint8_t* up_packed;
+    const uint8_t* up_scales;
+    const uint8_t* down_packed;
+    const uint8_t* down_scales;
+} k3xb_mxfp4_expert;
+/* resident_mxfp4_moe_layer (backend.hpp:369-375; CPU semantics
+ * backend_cpu.cpp:305-339) for one position, f32 dense projections:
+ * latent = dense(x, routed_down [D][H]); per slot k the expert's
+ * gate/up [I][D] and down [D][I] MXFP4 products (k3xb_mxfp4_matvec) around
+ * situ_glu, unrounded; mixed = sum over slots in order of contributions[k] *
+ * y_k in float; rms_norm(mixed, routed_norm [D], eps) in float (FP64
+ * squares); routed = dense(., routed_up [H][D]); plus the dense SiTU shared
+ * MLP (shared_gate/up [Hs][H], shared_down [H][Hs]) in float. The products
+ * and norm are bit-identical to the CPU backend; situ_glu uses the device's
+ * tanhf/expf. Weights are device arrays; HOST contributions [K], x [H],
+ * y [H]; returns after y is on the host. */
+int k3xb_resident_moe_layer_host(k3xb_ctx* ctx, uint32_t hidden, uint32_t latent,
+                                 uint32_t inter, uint32_t shared_inter,
+                                 const float* routed_down, const float* routed_norm,
+                                 const float* routed_up, const float* shared_gate,
+                                 const float* shared_up, const float* shared_down,
+                                 const k3xb_mxfp4_expert* experts, uint32_t K,
+                                 const float* contributions, float eps, float beta,
+                                 float linear_beta, const float* x_host, float* y_host);
+
 /* ---- (d) KDA recurrence -------------------------------------------------- */
 /* official_kda.cpp:319-369 applied over a draft tree for S sequences that
  * share the topology: node n continues from parent[n]'s state

@@ -245,6 +245,32 @@ class Restatement:
         a = self.situ_glu(self.dense_matvec(x, gate), self.dense_matvec(x, up), beta, linear_beta)
         return self.dense_matvec(a, down)
 
+    def resident_moe_layer(self, w: dict, experts: dict, contributions, x, eps, beta, linear_beta=0.0):
+        """resident_mxfp4_moe_layer (backend_cpu.cpp:305-339) composed of the
+        restated pieces: f32 products, unrounded expert outputs, a float mix
+        in slot order, rms_norm (ops.cpp:10-18) in float with FP64 squares."""
+        D, H = w["routed_down"].shape
+        K, I = experts["gate_packed"].shape[:2]
+        latent = self.dense_matvec(x, w["routed_down"])
+        ys = []
+        for k in range(K):
+            g = self.mxfp4_matmul(latent, experts["gate_packed"][k], experts["gate_scales"][k], I, D)
+            u = self.mxfp4_matmul(latent, experts["up_packed"][k], experts["up_scales"][k], I, D)
+            a = self.situ_glu(g, u, beta, linear_beta)
+            ys.append(self.mxfp4_matmul(a, experts["down_packed"][k], experts["down_scales"][k], D, I))
+        c = np.asarray(contributions, np.float32)
+        mixed = np.zeros(D, np.float32)
+        for k in range(K):
+            mixed = (mixed + c[k] * ys[k]).astype(np.float32)   # float32 ops, slot order
+        squares = 0.0
+        for v in mixed.tolist():   # FP64, index order; a float square is exact in FP64
+            squares += v * v
+        inverse = np.float32(1.0) / np.sqrt(np.float32(np.float32(squares / D) + np.float32(eps)))
+        normed = (mixed * inverse).astype(np.float32) * np.asarray(w["routed_norm"], np.float32)
+        routed = self.dense_matvec(normed.astype(np.float32), w["routed_up"])
+        shared = self.dense_situ_mlp(x, w["shared_gate"], w["shared_up"], w["shared_down"], beta, linear_beta)
+        return (routed + shared).astype(np.float32)
+
     def router_logits(self, hidden, router):
         router = _c(router, np.uint16)
         out = np.empty(router.shape[0], np.float32)
@@ -499,6 +525,8 @@ class Reference:
         L.k3xr_official_two_layer.argtypes = [C.c_void_p] * 2 + [C.c_void_p, C.c_float, _f32p, _f32p] + \
             [C.c_void_p] * 4 + [_f32p]
         L.k3xr_dense_matvec.argtypes = [_f32p, _sz, _sz, _f32p, _f32p]
+        L.k3xr_resident_moe_layer.argtypes = [_sz] * 4 + [_f32p] * 6 + [_u8p] * 6 + [_sz, _f32p, C.c_float, C.c_float,
+                                                                                  C.c_float, _f32p, _f32p]
         L.k3xr_dense_situ_mlp.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _f32p, C.c_float, C.c_float, _f32p]
         L.k3xr_official_layer.argtypes = [C.c_void_p, C.c_void_p, _u16p, _u16p, _u16p, _u16p, _u16p, _u16p,
                                           C.c_float, _f32p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p, _f32p, _u32p]
@@ -532,6 +560,24 @@ class Reference:
         st = self.lib.k3xr_dense_matvec(w, w.shape[0], w.shape[1], _c(x, np.float32), out)
         if st:
             raise OracleError(st, "ref dense_matvec")
+        return out
+
+    def resident_moe_layer(self, w: dict, experts: dict, contributions, x, eps, beta, linear_beta=0.0):
+        """The CPU backend's resident_mxfp4_moe_layer (backend_cpu.cpp:305-339):
+        w holds the f32 projections, experts the stacked MXFP4 arrays of the
+        slots in route order (gate_packed [K][I][D/2], ...)."""
+        D, H = w["routed_down"].shape
+        S = w["shared_gate"].shape[0]
+        K, I = experts["gate_packed"].shape[:2]
+        out = np.empty(H, np.float32)
+        st = self.lib.k3xr_resident_moe_layer(
+            H, D, I, S, *(_c(w[k], np.float32) for k in ("routed_down", "routed_norm", "routed_up", "shared_gate",
+                                                         "shared_up", "shared_down")),
+            *(_c(experts[k], np.uint8) for k in ("gate_packed", "gate_scales", "up_packed", "up_scales",
+                                                 "down_packed", "down_scales")),
+            K, _c(contributions, np.float32), eps, beta, linear_beta, _c(x, np.float32), out)
+        if st:
+            raise OracleError(st, "ref resident_mxfp4_moe_layer")
         return out
 
     def dense_situ_mlp(self, x, gate, up, down, beta, linear_beta=0.0):
@@ -845,6 +891,23 @@ def make_moe_layer(rs: Restatement, seed, hidden, inter, experts, top_k, shared_
         layer["routed_norm"] = bf16_words(1.0 + g.normal(0.0, 0.1, size=latent))
         layer["routed_up"] = bf16_words(g.normal(0.0, sigma, size=(hidden, latent)))
     return layer
+
+
+def make_resident_moe_case(rs: Restatement, seed, H=128, D=64, I=96, S=64, K=3):
+    """Synthetic inputs of resident_mxfp4_moe_layer (backend_cpu.cpp:305-339):
+    (f32 projections, stacked MXFP4 experts of K slots, contributions summing
+    to 1, x [H])."""
+    g = np.random.default_rng(seed)
+    f32 = lambda *shape, s=0.05: g.normal(0, s, size=shape).astype(np.float32)
+    w = dict(routed_down=f32(D, H), routed_norm=(1 + f32(D, s=0.1)).astype(np.float32), routed_up=f32(H, D),
+             shared_gate=f32(S, H), shared_up=f32(S, H), shared_down=f32(H, S))
+    ex = {}
+    for name, rows, cols in (("gate", I, D), ("up", I, D), ("down", D, I)):
+        pk, sc = zip(*[rs.quantize_mxfp4(f32(rows, cols, s=0.1)) for _ in range(K)])
+        ex[f"{name}_packed"], ex[f"{name}_scales"] = np.stack(pk), np.stack(sc)
+    con = g.random(K).astype(np.float32)
+    con /= con.sum()
+    return w, ex, con, g.normal(0, 1, size=H).astype(np.float32)
 
 
 def bf16_normal(g, shape, sigma=1.0):

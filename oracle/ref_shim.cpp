@@ -568,4 +568,38 @@ int k3xr_dense_situ_mlp(const float* gate, const float* up, const float* down, s
     return code(r);
 }
 
+// The reference CPU backend's resident_mxfp4_moe_layer (backend_cpu.cpp:
+// 305-339) for one position: f32 projections routed_down [D][H], routed_norm
+// [D], routed_up [H][D], shared gate/up [S][H] and down [H][S]; K experts
+// gate/up [I][D], down [D][I] (MXFP4, group 32, stacked per expert). y [H].
+int k3xr_resident_moe_layer(std::size_t H, std::size_t D, std::size_t I, std::size_t S, const float* routed_down,
+                            const float* routed_norm, const float* routed_up, const float* shared_gate,
+                            const float* shared_up, const float* shared_down, const std::uint8_t* gate_packed,
+                            const std::uint8_t* gate_scales, const std::uint8_t* up_packed,
+                            const std::uint8_t* up_scales, const std::uint8_t* down_packed,
+                            const std::uint8_t* down_scales, std::size_t K, const float* contributions, float eps,
+                            float beta, float linear_beta, const float* x, float* y) {
+    auto backend = k3x::make_cpu_backend();
+    std::uint64_t id = 1;
+    const k3x::ResidentMoeLayerView w{{id++, {routed_down, D * H}, D, H},
+                                      {id++, {routed_norm, D}},
+                                      {id++, {routed_up, H * D}, H, D},
+                                      {{id++, {shared_gate, S * H}, S, H},
+                                       {id++, {shared_up, S * H}, S, H},
+                                       {id++, {shared_down, H * S}, H, S}}};
+    std::vector<k3x::Mxfp4MlpView> experts(K);
+    for (std::size_t k = 0; k < K; ++k) {
+        experts[k].gate = {id++, bytes(gate_packed + k * I * D / 2, I * D / 2), bytes(gate_scales + k * I * D / 32, I * D / 32),
+                           I, D, 32};
+        experts[k].up = {id++, bytes(up_packed + k * I * D / 2, I * D / 2), bytes(up_scales + k * I * D / 32, I * D / 32),
+                         I, D, 32};
+        experts[k].down = {id++, bytes(down_packed + k * D * I / 2, D * I / 2),
+                           bytes(down_scales + k * D * I / 32, D * I / 32), D, I, 32};
+    }
+    auto r = backend->resident_mxfp4_moe_layer({x, H}, w, experts, {contributions, K}, eps, beta, linear(linear_beta), 0,
+                                               k3x::ProfilePhase::decode);
+    if (r) std::copy(r.value().output.begin(), r.value().output.end(), y);
+    return code(r);
+}
+
 }  // extern "C"

@@ -124,10 +124,28 @@ public:
         if (rc != K3XB_OK) return Result<std::vector<float>>::failure(static_cast<ErrorCode>(rc), last_error());
         return Result<std::vector<float>>::success(std::move(y));
     }
+    // single MXFP4 products (k3xb_mxfp4_matvec_host): mxfp4_matmul's checks
+    // (ops.cpp:32-60, invalid_mxfp4) and arithmetic bit for bit
     Result<std::vector<float>> mxfp4_matvec(std::span<const float> input, Mxfp4WeightView weight,
                                             std::uint32_t layer, ProfilePhase phase) override {
-        if (!rest_) return unavailable<std::vector<float>>("mxfp4_matvec is not on the B200 path");
-        return rest_->mxfp4_matvec(input, weight, layer, phase);
+        if (input.size() != weight.cols || !weight.rows || !weight.cols || !weight.group_size ||
+            weight.cols % weight.group_size || weight.cols % 2 || weight.packed.size() != weight.rows * weight.cols / 2 ||
+            weight.scales.size() != weight.rows * weight.cols / weight.group_size)
+            return Result<std::vector<float>>::failure(ErrorCode::invalid_mxfp4);
+        if (!weight.tensor_id || weight.group_size != 32) {   // nothing to keep it resident by, or not group 32
+            if (!rest_) return unavailable<std::vector<float>>("mxfp4_matvec: no tensor id, or a group other than 32");
+            return rest_->mxfp4_matvec(input, weight, layer, phase);
+        }
+        k3xb_resident r{};
+        const ErrorCode st = mxfp4_resident(weight, &r);
+        if (st != ErrorCode::ok) return Result<std::vector<float>>::failure(st, last_error());
+        std::vector<float> y(weight.rows);
+        const int rc = k3xb_mxfp4_matvec_host(ctx_, static_cast<const std::uint8_t*>(r.primary),
+                                              static_cast<const std::uint8_t*>(r.secondary),
+                                              static_cast<std::uint32_t>(weight.rows),
+                                              static_cast<std::uint32_t>(weight.cols), input.data(), y.data());
+        if (rc != K3XB_OK) return Result<std::vector<float>>::failure(static_cast<ErrorCode>(rc), last_error());
+        return Result<std::vector<float>>::success(std::move(y));
     }
     Result<std::vector<std::vector<float>>> dense_matvec_group(std::span<const float> input,
                                                                std::span<const DenseWeightView> weights,
@@ -147,8 +165,15 @@ public:
     Result<std::vector<std::vector<float>>> mxfp4_matvec_group(std::span<const float> input,
                                                                std::span<const Mxfp4WeightView> weights,
                                                                std::uint32_t layer, ProfilePhase phase) override {
-        if (!rest_) return unavailable<std::vector<std::vector<float>>>("mxfp4_matvec_group is not on the B200 path");
-        return rest_->mxfp4_matvec_group(input, weights, layer, phase);
+        using R = Result<std::vector<std::vector<float>>>;
+        std::vector<std::vector<float>> out;
+        out.reserve(weights.size());
+        for (const auto& w : weights) {
+            auto y = mxfp4_matvec(input, w, layer, phase);
+            if (!y) return R::failure(y.error(), y.message());
+            out.push_back(std::move(y.value()));
+        }
+        return R::success(std::move(out));
     }
     Result<std::vector<float>> dense_situ_mlp(std::span<const float> input, DenseMlpView weights, float situ_beta,
                                               std::optional<float> situ_linear, std::uint32_t layer,
@@ -176,18 +201,80 @@ public:
         return Result<std::vector<float>>::success(std::move(y));
     }
 
-    // ---- not on the B200 path: the maintainer's other backend -------------
-    // The resident layer of backend_cpu.cpp:308-341 takes f32 dense
-    // projections and mixes unrounded expert outputs in float: not the bf16
-    // arithmetic of official_moe_cpu that this library's kernels compute.
+    // The resident layer (backend_cpu.cpp:305-339): f32 projections, the
+    // experts' unrounded outputs mixed in float, with the CPU backend's checks
+    // (:442-500, invalid_mxfp4); k3xb_resident_moe_layer_host runs it with
+    // the CPU backend's products and norm bit for bit.
     Result<ResidentMoeLayerResult> resident_mxfp4_moe_layer(std::span<const float> input, ResidentMoeLayerView w,
                                                             std::span<const Mxfp4MlpView> experts,
                                                             std::span<const float> contributions, float epsilon,
                                                             float beta, std::optional<float> linear,
                                                             std::uint32_t layer, ProfilePhase phase) override {
-        if (!rest_) return unavailable<ResidentMoeLayerResult>("latent MoE layer is not on the B200 path");
-        return rest_->resident_mxfp4_moe_layer(input, w, experts, contributions, epsilon, beta, linear, layer,
-                                               phase);
+        using R = Result<ResidentMoeLayerResult>;
+        const auto& sh = w.shared;
+        const bool mlp_ok = valid_dense(input, sh.gate) && valid_dense(input, sh.up) && sh.gate.rows &&
+                            sh.gate.rows == sh.up.rows && sh.down.cols == sh.gate.rows && sh.down.rows &&
+                            sh.down.values.size() == sh.down.rows * sh.down.cols;
+        if (input.empty() || experts.empty() || experts.size() != contributions.size() || !std::isfinite(epsilon) ||
+            epsilon <= 0.0F || !valid_activation(beta, linear) || !finite(input) || !finite(contributions) ||
+            !finite(w.routed_down.values) || !finite(w.routed_norm.values) || !finite(w.routed_up.values) ||
+            !finite(sh.gate.values) || !finite(sh.up.values) || !finite(sh.down.values) ||
+            !valid_dense(input, w.routed_down) || !mlp_ok)
+            return R::failure(ErrorCode::invalid_mxfp4);
+        const std::size_t H = input.size(), D = w.routed_down.rows, Dout = experts.front().down.rows,
+                          I = experts.front().gate.rows, S = sh.gate.rows;
+        if (!D || !Dout || w.routed_norm.values.size() != Dout || w.routed_up.cols != Dout || !w.routed_up.rows ||
+            w.routed_up.values.size() != w.routed_up.rows * w.routed_up.cols || w.routed_up.rows != H ||
+            sh.down.rows != H)
+            return R::failure(ErrorCode::invalid_mxfp4);
+        std::unordered_set<std::uint64_t> tensors;
+        const auto fresh = [&tensors](std::uint64_t id) { return id && tensors.insert(id).second; };
+        if (!fresh(w.routed_down.tensor_id) || !fresh(w.routed_norm.tensor_id) || !fresh(w.routed_up.tensor_id) ||
+            !fresh(sh.gate.tensor_id) || !fresh(sh.up.tensor_id) || !fresh(sh.down.tensor_id))
+            return R::failure(ErrorCode::invalid_mxfp4);
+        for (const auto& e : experts)
+            if (!valid_matrix(e.gate, I, D) || !valid_matrix(e.up, I, D) || !valid_matrix(e.down, Dout, I) ||
+                !fresh(e.gate.tensor_id) || !fresh(e.up.tensor_id) || !fresh(e.down.tensor_id))
+                return R::failure(ErrorCode::invalid_mxfp4);
+        if (Dout != D) {   // a routed width other than the latent width: not this library's shape
+            if (!rest_) return unavailable<ResidentMoeLayerResult>("resident MoE layer shape is not on the B200 path");
+            return rest_->resident_mxfp4_moe_layer(input, w, experts, contributions, epsilon, beta, linear, layer,
+                                                   phase);
+        }
+        ErrorCode st = ErrorCode::ok;
+        const auto f32 = [&](std::uint64_t id, std::span<const float> v, std::size_t rows, std::size_t cols) {
+            return st == ErrorCode::ok ? static_cast<const float*>(
+                                             resident(id, K3XB_WEIGHT_F32, rows, cols, v.data(), v.size() * 4, &st))
+                                       : nullptr;
+        };
+        const float* rd = f32(w.routed_down.tensor_id, w.routed_down.values, D, H);
+        const float* rn = f32(w.routed_norm.tensor_id, w.routed_norm.values, 1, D);
+        const float* ru = f32(w.routed_up.tensor_id, w.routed_up.values, H, D);
+        const float* sg = f32(sh.gate.tensor_id, sh.gate.values, S, H);
+        const float* su = f32(sh.up.tensor_id, sh.up.values, S, H);
+        const float* sd = f32(sh.down.tensor_id, sh.down.values, H, S);
+        if (st != ErrorCode::ok) return R::failure(st, last_error());
+        std::vector<k3xb_mxfp4_expert> dev(experts.size());
+        for (std::size_t k = 0; k < experts.size(); ++k) {
+            k3xb_resident g{}, u{}, d{};
+            if ((st = mxfp4_resident(experts[k].gate, &g)) != ErrorCode::ok ||
+                (st = mxfp4_resident(experts[k].up, &u)) != ErrorCode::ok ||
+                (st = mxfp4_resident(experts[k].down, &d)) != ErrorCode::ok)
+                return R::failure(st, last_error());
+            dev[k] = {static_cast<const std::uint8_t*>(g.primary), static_cast<const std::uint8_t*>(g.secondary),
+                      static_cast<const std::uint8_t*>(u.primary), static_cast<const std::uint8_t*>(u.secondary),
+                      static_cast<const std::uint8_t*>(d.primary), static_cast<const std::uint8_t*>(d.secondary)};
+        }
+        ResidentMoeLayerResult out;
+        out.output.resize(H);
+        const int rc = k3xb_resident_moe_layer_host(
+            ctx_, static_cast<std::uint32_t>(H), static_cast<std::uint32_t>(D), static_cast<std::uint32_t>(I),
+            static_cast<std::uint32_t>(S), rd, rn, ru, sg, su, sd, dev.data(), static_cast<std::uint32_t>(dev.size()),
+            contributions.data(), epsilon, beta, linear ? *linear : 0.0F, input.data(), out.output.data());
+        if (rc != K3XB_OK) return R::failure(static_cast<ErrorCode>(rc), last_error());
+        out.executed = true;
+        ++moe_calls_;
+        return R::success(std::move(out));
     }
 
     // ---- the official LatentMoE FFN of one position (k3xb_official_moe_ffn_host)
@@ -480,6 +567,14 @@ private:
         if (input.size() != w.cols || w.rows > w.values.size() || (w.cols != 0 && w.rows > w.values.size() / w.cols))
             return false;
         return w.values.size() == w.rows * w.cols;
+    }
+
+    // One MXFP4 matrix resident by its tensor id (its scales checked for 0xFF at admission).
+    ErrorCode mxfp4_resident(const Mxfp4WeightView& w, k3xb_resident* r) {
+        const int rc = k3xb_acquire_weight(ctx_, w.tensor_id, K3XB_WEIGHT_MXFP4, w.rows, w.cols, w.group_size,
+                                           w.packed.data(), w.packed.size(), w.scales.data(), w.scales.size(), r);
+        if (rc != K3XB_OK) return static_cast<ErrorCode>(rc);
+        return r->disposition == K3XB_RESIDENT_BYPASS ? ErrorCode::backend_unavailable : ErrorCode::ok;
     }
 
     const float* dense_resident(const DenseWeightView& w, ErrorCode* st) {

@@ -11,6 +11,9 @@
 // returned as it is; it is never retried on `rest`.
 //
 // On the B200:
+//   mxfp4_matvec / _group, resident_mxfp4_moe_layer (weights with a tensor id)
+//                                -> k3xb_acquire_weight + k3xb_mxfp4_matvec_host /
+//                                   k3xb_resident_moe_layer_host (the CPU backend's products)
 //   dense_matvec / _group, dense_situ_mlp (weights with a tensor id)
 //                                -> k3xb_acquire_weight (f32) + k3xb_dense_matvec_host /
 //                                   k3xb_dense_situ_mlp_host (bit-identical to the CPU backend)

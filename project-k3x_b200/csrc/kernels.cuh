@@ -83,6 +83,8 @@ int launch_linear_terms(k3xb_ctx* ctx, const uint16_t* xterms, uint32_t terms, c
 // dense.cu — f32 dense products in the reference CPU backend's FP64 column order
 int launch_dense_matvec(k3xb_ctx* ctx, const float* W, uint32_t rows, uint32_t cols, const float* x, uint32_t T,
                         float* y);
+int launch_mxfp4_matvec(k3xb_ctx* ctx, const uint8_t* packed, const uint8_t* scales, uint32_t rows, uint32_t cols,
+                        const float* x, uint32_t T, float* y);
 // resident.cu — the resident weight table
 void release_resident(k3xb_ctx* ctx);
 void resident_stats(const k3xb_ctx* ctx, k3xb_stats* out);

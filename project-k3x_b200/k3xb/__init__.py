@@ -208,6 +208,10 @@ def library() -> C.CDLL:
             "k3xb_get_profile": [vp, C.POINTER(PhaseTime), C.POINTER(u64)],
             "k3xb_kda_block_host": [vp, C.POINTER(KdaLayer), u32, vp, u32, vp, vp, vp],
             "k3xb_dense_matvec": [vp, vp, u32, u32, vp, u32, vp],
+            "k3xb_mxfp4_matvec": [vp, vp, vp, u32, u32, vp, u32, vp],
+            "k3xb_mxfp4_matvec_host": [vp, vp, vp, u32, u32, vp, vp],
+            "k3xb_resident_moe_layer_host": [vp, u32, u32, u32, u32] + [vp] * 6 + [vp, u32, vp, C.c_float, C.c_float,
+                                                                                    C.c_float, vp, vp],
             "k3xb_dense_matvec_host": [vp, vp, u32, u32, vp, vp],
             "k3xb_dense_situ_mlp_host": [vp, vp, vp, vp, u32, u32, u32, vp, C.c_float, C.c_float, vp],
             "k3xb_kda_block_held": [vp, C.POINTER(KdaLayer), u32, vp, u32, u32, C.c_int32, vp, vp, vp],
@@ -531,6 +535,32 @@ class Context:
         the reference CPU backend's FP64 column-order sums."""
         rows, cols = W.shape
         self._check(self.lib.k3xb_dense_matvec(self.h, _p(W), rows, cols, _p(x), x.shape[0], _p(y)), "dense_matvec")
+
+    def mxfp4_matvec(self, packed, scales, rows, cols, x, y):
+        """y [T][rows] = MXFP4 [rows][cols] x [T][cols] (device tensors), the
+        reference's mxfp4_matmul FP64 column-order sums."""
+        self._check(self.lib.k3xb_mxfp4_matvec(self.h, _p(packed), _p(scales), rows, cols, _p(x), x.shape[0], _p(y)),
+                    "mxfp4_matvec")
+
+    def resident_moe_layer_host(self, w: dict, experts, contributions, x, eps, beta, linear_beta=0.0):
+        """resident_mxfp4_moe_layer: w holds device f32 projections, experts a
+        list of dicts of device MXFP4 arrays (gate_packed, ...), one per slot;
+        HOST contributions, x -> HOST y."""
+        import numpy as np
+        D, H = w["routed_down"].shape
+        S = w["shared_gate"].shape[0]
+        I = experts[0]["gate_scales"].shape[0]
+        names = ("gate_packed", "gate_scales", "up_packed", "up_scales", "down_packed", "down_scales")
+        arr = (C.c_void_p * (6 * len(experts)))(*[e[n].data_ptr() for e in experts for n in names])
+        con = np.ascontiguousarray(contributions, dtype=np.float32)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty(H, np.float32)
+        self._check(self.lib.k3xb_resident_moe_layer_host(
+            self.h, H, D, I, S, *(_p(w[k]) for k in ("routed_down", "routed_norm", "routed_up", "shared_gate",
+                                                      "shared_up", "shared_down")),
+            arr, len(experts), con.ctypes.data, eps, beta, linear_beta, x.ctypes.data, y.ctypes.data),
+            "resident_moe_layer_host")
+        return y
 
     def dense_matvec_host(self, W, x):
         """W device [rows][cols]; HOST x [cols] -> HOST y [rows]."""

@@ -153,9 +153,14 @@ int split_and_forwarding() {
     CHECK(b->kind() == BackendKind::cuda_custom && !b->device_name().empty());
     CHECK(b->runtime_stats().weight_cache_hits == 5 && b->memory_stats().current_device_bytes == 3);
     const std::vector<float> x(128, 1.0F);
-    // not on the path: forwarded (a single MXFP4 product; a dense weight without a tensor id)
-    auto mv = b->mxfp4_matvec(x, Mxfp4WeightView{}, 0, ProfilePhase::decode);
+    // weights without a tensor id cannot stay resident: forwarded
+    std::vector<std::byte> pk1(64), sc1(4);
+    auto mv = b->mxfp4_matvec(x, Mxfp4WeightView{0, pk1, sc1, 1, 128, 32}, 0, ProfilePhase::decode);
     CHECK(mv && mv.value().size() == 1 && mv.value()[0] == 43.0F && fake->calls == 1);
+    auto mt = b->mxfp4_matvec(x, Mxfp4WeightView{9, pk1, sc1, 1, 128, 32}, 0, ProfilePhase::decode);
+    CHECK(!mt && mt.error() == ErrorCode::invalid_extent && fake->calls == 1);   // tracked: the C ABI
+    auto mb = b->mxfp4_matvec(x, Mxfp4WeightView{9, pk1, sc1, 2, 128, 32}, 0, ProfilePhase::decode);
+    CHECK(!mb && mb.error() == ErrorCode::invalid_mxfp4 && fake->calls == 1);    // mxfp4_matmul's size check
     auto d = b->dense_matvec(x, DenseWeightView{0, x, 1, 128}, 0, ProfilePhase::decode);
     CHECK(d && d.value().size() == 1 && d.value()[0] == 42.0F && fake->calls == 2);
     fake->calls = 1;
@@ -191,7 +196,20 @@ int no_rest() {
     CHECK(!d && d.error() == ErrorCode::backend_unavailable);
     auto r = b->resident_mxfp4_moe_layer(x, ResidentMoeLayerView{}, {}, {}, 1e-6F, 1.0F, std::nullopt, 0,
                                          ProfilePhase::decode);
-    CHECK(!r && r.error() == ErrorCode::backend_unavailable);
+    CHECK(!r && r.error() == ErrorCode::invalid_mxfp4);   // the CPU backend's checks (backend_cpu.cpp:442-500)
+    // a well-formed resident layer reaches the C ABI (NULL context -> invalid_extent)
+    const std::size_t H = 128, D = 64, I = 64, S = 64;
+    std::vector<float> rd(D * H), rn(D, 1.0F), ru(H * D), sg(S * H), su(S * H), sd(H * S);
+    ResidentMoeLayerView rv{{1, rd, D, H}, {2, rn}, {3, ru, H, D}, {{4, sg, S, H}, {5, su, S, H}, {6, sd, H, S}}};
+    ExpertBuffers e1(D, I, 10);
+    const std::vector<Mxfp4MlpView> one{e1.view};
+    const std::vector<float> c1{1.0F};
+    auto rr = b->resident_mxfp4_moe_layer(x, rv, one, c1, 1e-6F, 4.0F, std::nullopt, 0, ProfilePhase::decode);
+    CHECK(!rr && rr.error() == ErrorCode::invalid_extent);
+    ResidentMoeLayerView dup = rv;
+    dup.routed_up.tensor_id = 1;   // a tensor id twice
+    auto rdup = b->resident_mxfp4_moe_layer(x, dup, one, c1, 1e-6F, 4.0F, std::nullopt, 0, ProfilePhase::decode);
+    CHECK(!rdup && rdup.error() == ErrorCode::invalid_mxfp4);
     return 0;
 }
 

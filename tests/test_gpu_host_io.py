@@ -186,3 +186,31 @@ def test_dense_matvec_bit_identical_to_the_cpu_backend(torch, ctx, rs):
     for beta, lin in ((4.0, 0.0), (2.0, 25.0)):
         got = ctx.dense_situ_mlp_host(to_dev(torch, gate), to_dev(torch, up), to_dev(torch, down), x, beta, lin)
         np.testing.assert_allclose(got, rs.dense_situ_mlp(x, gate, up, down, beta, lin), rtol=1e-5, atol=1e-7)
+
+
+def test_mxfp4_matvec_and_resident_layer_vs_cpu_backend(torch, ctx, rs):
+    """k3xb_mxfp4_matvec (mxfp4_matmul, ops.cpp:44-76) bit-identical to the
+    restatement (pinned to the reference), including rows and chunks that are
+    not multiples of the tile; k3xb_resident_moe_layer_host
+    (resident_mxfp4_moe_layer, backend_cpu.cpp:305-339) within 1e-5 of the
+    restated composition (pinned in test_oracle_pin.py): its products and
+    norm are the reference's bit for bit, its situ_glu uses the device's
+    tanhf/expf."""
+    from oracle import make_resident_moe_case
+    g = np.random.default_rng(191)
+    for rows, cols, T in ((1, 32, 1), (130, 96, 2), (257, 1024, 1), (2048, 7168, 1)):
+        packed, scales = rs.quantize_mxfp4(g.normal(0, 0.1, size=(rows, cols)).astype(np.float32))
+        x = g.normal(0, 1, size=(T, cols)).astype(np.float32)
+        y = torch.empty((T, rows), dtype=torch.float32, device="cuda")
+        ctx.mxfp4_matvec(to_dev(torch, packed), to_dev(torch, scales), rows, cols, to_dev(torch, x), y)
+        ctx.sync()
+        got = y.cpu().numpy()
+        for t in range(T):
+            np.testing.assert_array_equal(got[t], rs.mxfp4_matmul(x[t], packed, scales, rows, cols),
+                                          err_msg=f"{rows}x{cols} token {t}")
+    for seed, lin in ((181, 0.0), (182, 25.0)):
+        w, ex, con, x = make_resident_moe_case(rs, seed)
+        wd = {k: to_dev(torch, v) for k, v in w.items()}
+        experts = [{k: to_dev(torch, v[e]) for k, v in ex.items()} for e in range(len(con))]
+        got = ctx.resident_moe_layer_host(wd, experts, con, x, 1e-6, 4.0, lin)
+        np.testing.assert_allclose(got, rs.resident_moe_layer(w, ex, con, x, 1e-6, 4.0, lin), rtol=1e-5, atol=1e-6)

@@ -567,3 +567,13 @@ def test_dense_matvec_and_situ_mlp_match_reference_cpu_backend(rs, ref):
     for beta, lin in ((4.0, 0.0), (2.0, 25.0)):
         np.testing.assert_array_equal(rs.dense_situ_mlp(x, gate, up, down, beta, lin),
                                       ref.dense_situ_mlp(x, gate, up, down, beta, lin))
+
+
+def test_resident_moe_layer_matches_reference_cpu_backend(rs, ref):
+    """resident_mxfp4_moe_layer of the reference CPU backend (backend_cpu.cpp:
+    305-339): the restated composition is bit-identical."""
+    from oracle import make_resident_moe_case
+    for seed, lin in ((181, 0.0), (182, 25.0)):
+        w, ex, con, x = make_resident_moe_case(rs, seed)
+        np.testing.assert_array_equal(rs.resident_moe_layer(w, ex, con, x, 1e-6, 4.0, lin),
+                                      ref.resident_moe_layer(w, ex, con, x, 1e-6, 4.0, lin))
