@@ -36,12 +36,13 @@ def ref():
 # GPU files in dependency order: the kernels first, then what is composed of
 # them or added on top (golden end-to-end cases, the routing policy, expert
 # parallelism, LatentMoE, the device drafter, the host-I/O entry points,
-# resident weights, phase timing), so that a run which stops at the first failure
+# resident weights, phase timing, expert-parallel failure detection, the
+# reference's own layer drivers over the adapter), so that a run which stops at the first failure
 # stops at the lowest broken layer. Files not listed keep their place after
 # these; test_zz_no_alloc.py stays last.
 _GPU_ORDER = ["test_gpu_parity", "test_gpu_mxf4", "test_gpu_linear", "test_gpu_layer", "test_gpu_golden",
               "test_gpu_routing_policy", "test_gpu_ep", "test_gpu_latent", "test_gpu_draft", "test_gpu_host_io",
-              "test_gpu_resident", "test_gpu_profile"]
+              "test_gpu_resident", "test_gpu_profile", "test_gpu_ep_failure", "test_gpu_reference_drivers"]
 
 
 def pytest_collection_modifyitems(session, config, items):
