@@ -371,6 +371,9 @@ def run_c4(args, rank, world, local, ctx, stream):
                      "alg_bytes_per_launch": step_bytes, "unique_experts_layer0": unique, "traffic": None},
         "gpu_launches": launches, "clocks": clk.summary(),
         "accepted_mean": float(acc.float().mean().item()),
+        # the same inputs every step, so the last step's decisions are every step's
+        "accepted_tokens_per_s": sum_over_ranks(int(acc.sum().item()), world) / (ms * 1e-3),
+        "committed_tokens_per_s": sum_over_ranks(int(cnt.sum().item()), world) / (ms * 1e-3),
     }
     if args.profile:
         result["phases"] = phase_profile(ctx, torch, step, max(3, args.steps))
