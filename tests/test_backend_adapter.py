@@ -75,3 +75,38 @@ def test_reference_layer_driver_harness_loads_and_reports_no_gpu():
         ReferenceOnB200().official_two_layer([layer, layer], f["hidden"][:2], f["block"][:2],
                                              [(f["conv_q"], f["conv_k"], f["conv_v"])] * 2, [f["recurrent"]] * 2)
     assert e.value.status == 17, str(e.value)
+
+
+def protocol_sources():
+    """The adapter protocol check's sources: the check, the scripted C ABI, the
+    adapter, and the reference's drivers and the CPU steps they call."""
+    inc = reference_include()
+    if not inc:
+        return None, None
+    src = os.path.join(os.path.dirname(inc), "src")
+    ref = [os.path.join(src, f) for f in ("official_layer.cpp", "official_two_layer.cpp", "official_moe.cpp",
+                                          "official_kda.cpp", "ops.cpp", "profile.cpp")]
+    ours = [os.path.join(ROOT, "tests", "cpp", "adapter_protocol_check.cpp"),
+            os.path.join(ROOT, "tests", "cpp", "fake_k3xb.cpp"), os.path.join(ADAPTER, "backend_b200.cpp")]
+    return inc, ours + ref
+
+
+def test_adapter_keeps_the_reference_drivers_protocol(tmp_path):
+    """The reference's official_layer_cuda (host and device route
+    preparation, KDA state seeded then published across calls) and
+    official_two_layer_cuda (host_round_trip, device_closure), unchanged,
+    over B200Backend with a scripted C ABI (tests/cpp/fake_k3xb.cpp): every
+    token, publication flag and output size the drivers check is right, and
+    nothing leaks from one run into the next."""
+    cxx = shutil.which("g++")
+    if not cxx:
+        pytest.skip("no C++ compiler")
+    inc, sources = protocol_sources()
+    if not inc:
+        pytest.skip("reference sources absent")
+    exe = tmp_path / "adapter_protocol_check"
+    subprocess.run([cxx, "-std=c++20", "-O1", "-Wall", "-Wextra", "-Werror", "-isystem", inc,
+                    "-I", os.path.join(ROOT, "include"), "-I", ADAPTER, *sources, "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.startswith("adapter protocol ok"), out.stdout

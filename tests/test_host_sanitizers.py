@@ -40,6 +40,19 @@ def test_resident_table_sanitized(tmp_path):
          "resident ok", {"ASAN_OPTIONS": "detect_leaks=1"})
 
 
+def test_adapter_protocol_sanitized(tmp_path):
+    """The adapter's token and slot bookkeeping under the reference's drivers
+    (tests/cpp/adapter_protocol_check.cpp) with leak checking: everything is
+    host code there (the C ABI is the scripted stand-in)."""
+    from test_backend_adapter import protocol_sources
+    inc, sources = protocol_sources()
+    if not inc:
+        pytest.skip("reference sources absent")
+    _run(tmp_path, "adapter_protocol_check", sources, ["-isystem", inc, "-I", os.path.join(ROOT, "include"),
+                                                      "-I", ADAPTER], "adapter protocol ok",
+         {"ASAN_OPTIONS": "detect_leaks=1"})
+
+
 def test_ep_guard_sanitized(tmp_path):
     _run(tmp_path, "ep_guard_check", [os.path.join(ROOT, "tests", "cpp", "ep_guard_check.cpp")],
          ["-I", os.path.join(ROOT, "project-k3x_b200", "csrc")], "ep guard ok", {"ASAN_OPTIONS": "detect_leaks=1"})
