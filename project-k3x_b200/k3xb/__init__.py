@@ -209,6 +209,7 @@ def library() -> C.CDLL:
             "k3xb_kda_block_host": [vp, C.POINTER(KdaLayer), u32, vp, u32, vp, vp, vp],
             "k3xb_dense_matvec": [vp, vp, u32, u32, vp, u32, vp],
             "k3xb_mxfp4_matvec": [vp, vp, vp, u32, u32, vp, u32, vp],
+            "k3xb_prepare_moe_route_host": [vp, vp, vp, vp, u32, vp, vp, vp, C.c_float, vp, u32, vp, vp, vp],
             "k3xb_mxfp4_matvec_host": [vp, vp, vp, u32, u32, vp, vp],
             "k3xb_resident_moe_layer_host": [vp, u32, u32, u32, u32] + [vp] * 6 + [vp, u32, vp, C.c_float, C.c_float,
                                                                                     C.c_float, vp, vp],
@@ -535,6 +536,25 @@ class Context:
         the reference CPU backend's FP64 column-order sums."""
         rows, cols = W.shape
         self._check(self.lib.k3xb_dense_matvec(self.h, _p(W), rows, cols, _p(x), x.shape[0], _p(y)), "dense_matvec")
+
+    def prepare_moe_route_host(self, a, block, norm, proj, post, eps, router=None, delta=None):
+        """k3xb_prepare_moe_route_host: HOST a, block (and delta) [H]; device
+        bf16 norm/proj/post [H] and router [E][H] (or None) -> HOST (prefix or
+        None, prepared input [H], logits [E] or None)."""
+        import numpy as np
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        block = np.ascontiguousarray(block, dtype=np.float32)
+        H = a.shape[0]
+        E = router.shape[0] if router is not None else 0
+        d = None if delta is None else np.ascontiguousarray(delta, dtype=np.float32)
+        prefix = np.empty(H, np.float32) if d is not None else None
+        hidden = np.empty(H, np.float32)
+        logits = np.empty(E, np.float32) if E else None
+        self._check(self.lib.k3xb_prepare_moe_route_host(
+            self.h, a.ctypes.data, None if d is None else d.ctypes.data, block.ctypes.data, H, _p(norm), _p(proj),
+            _p(post), eps, _p(router), E, None if prefix is None else prefix.ctypes.data, hidden.ctypes.data,
+            None if logits is None else logits.ctypes.data), "prepare_moe_route_host")
+        return prefix, hidden, logits
 
     def mxfp4_matvec(self, packed, scales, rows, cols, x, y):
         """y [T][rows] = MXFP4 [rows][cols] x [T][cols] (device tensors), the

@@ -214,3 +214,30 @@ def test_mxfp4_matvec_and_resident_layer_vs_cpu_backend(torch, ctx, rs):
         experts = [{k: to_dev(torch, v[e]) for k, v in ex.items()} for e in range(len(con))]
         got = ctx.resident_moe_layer_host(wd, experts, con, x, 1e-6, 4.0, lin)
         np.testing.assert_allclose(got, rs.resident_moe_layer(w, ex, con, x, 1e-6, 4.0, lin), rtol=1e-5, atol=1e-6)
+
+
+def test_prepare_moe_route_host_vs_restatement(torch, ctx, rs):
+    """k3xb_prepare_moe_route_host (prepare_official_moe_route): the prepared
+    input within the attention-residual bars of test_gpu_golden.py, its
+    router logits bit-identical to the restatement's over that input (the
+    router's FP64 chains), and with delta the prefix round_bf16(round_bf16(a)
+    + delta) bit for bit; without a router, no logits."""
+    import golden_util as gu
+    from test_gpu_latent import assert_mostly_close
+    f = gu.load("prepare_input.npz")
+    g = np.random.default_rng(193)
+    H = f["prefix"].shape[1]
+    E = 64
+    router = bf16_words(g.normal(0, 0.02, size=(E, H)))
+    dv = lambda x: to_dev(torch, x)
+    norm, proj, post, rd = dv(f["norm"]), dv(f["proj"]), dv(f["post"]), dv(router)
+    eps = float(f["eps"])
+    for t in range(f["prefix"].shape[0]):
+        _, hidden, logits = ctx.prepare_moe_route_host(f["prefix"][t], f["block"][t], norm, proj, post, eps, rd)
+        assert_mostly_close(hidden, f["out"][t], what="prepared input")
+        np.testing.assert_array_equal(logits, rs.router_logits(hidden, router))
+    delta = g.normal(0, 0.5, size=H).astype(np.float32)
+    prefix, hidden, logits = ctx.prepare_moe_route_host(f["prefix"][0], f["block"][0], norm, proj, post, eps,
+                                                        None, delta)
+    np.testing.assert_array_equal(prefix, rs.round_bf16(rs.round_bf16(f["prefix"][0]) + delta))
+    assert logits is None and np.isfinite(hidden).all()
