@@ -399,7 +399,10 @@ int k3xb_expert_grid_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer,
  * engine for all; MXF4 needs
  * the *_scales_tc copies), e.g. a resident stack of one
  * (k3xb_acquire_expert_stack) or single resident MXFP4 weights for the SIMT
- * engine. hidden is the prepared (bf16-valued) MoE input; HOST
+ * engine. The shared expert runs on the tensor cores with the MXF4 engine
+ * when hidden and shared_inter are multiples of 128 (as in
+ * k3xb_moe_layer_forward), else on the CUDA cores, so the result equals the
+ * layer path's bit for bit. hidden is the prepared (bf16-valued) MoE input; HOST
  * contributions [K], hidden [H], prefix [H] and out [H]; returns after out
  * is on the host. */
 int k3xb_official_moe_ffn_host(k3xb_ctx* ctx, const k3xb_moe_layer* tail,

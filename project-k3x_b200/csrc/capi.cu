@@ -587,6 +587,8 @@ int k3xb_official_moe_ffn_host(k3xb_ctx* ctx, const k3xb_moe_layer* tail, const 
     for (int i = 0; i < 2; ++i) sz.take<float>(D);            // mixed, normed
     for (int i = 0; i < 3; ++i) sz.take<float>(H);            // routed, shared, combined
     for (int i = 0; i < 3; ++i) sz.take<float>(Is ? Is : 1);  // shared gate, up, activation
+    sz.take<uint16_t>(2 * size_t(H));             // tensor-core shared expert: input terms
+    sz.take<uint16_t>(2 * size_t(Is ? Is : 1));   // and its down operand
     sz.take<float>(H);                            // out
     for (int i = 0; i < 2; ++i) sz.take<uint32_t>(2);         // plan groups
     for (int i = 0; i < 4; ++i) sz.take<uint32_t>(1);         // plan assignments, group count
@@ -610,6 +612,8 @@ int k3xb_official_moe_ffn_host(k3xb_ctx* ctx, const k3xb_moe_layer* tail, const 
     float* sg = c.take<float>(Is ? Is : 1);
     float* su = c.take<float>(Is ? Is : 1);
     float* sa = c.take<float>(Is ? Is : 1);
+    uint16_t* sxb = c.take<uint16_t>(2 * size_t(H));
+    uint16_t* sbd = c.take<uint16_t>(2 * size_t(Is ? Is : 1));
     float* out = c.take<float>(H);
     k3xb_plan plan{};
     plan.group_expert = c.take<uint32_t>(2);
@@ -667,12 +671,16 @@ int k3xb_official_moe_ffn_host(k3xb_ctx* ctx, const k3xb_moe_layer* tail, const 
         if ((st = launch_rms_norm(ctx, mixed, W.routed_norm, 1, D, W.latent_eps, normed))) return st;
         if ((st = launch_linear_bf16(ctx, normed, W.routed_up, 1, H, D, 1, xt, routed))) return st;
     }
-    if (Is) {   // :332-335 the shared expert on the hidden row
+    if (Is) {   // :332-335 the shared expert on the hidden row, with the layer path's kernels
         PhaseScope ph(ctx, K3XB_PHASE_SHARED);
-        if ((st = launch_bf16_rows(ctx, hidden, W.shared_gate, 1, Is, H, sg))) return st;
-        if ((st = launch_bf16_rows(ctx, hidden, W.shared_up, 1, Is, H, su))) return st;
-        if ((st = launch_act(ctx, sg, su, Is, W.activation, W.situ_beta, W.situ_linear_beta, sa))) return st;
-        if ((st = launch_bf16_rows(ctx, sa, W.shared_down, 1, H, Is, shared))) return st;
+        if (engine == K3XB_ENGINE_MXF4 && H % 128 == 0 && Is % 128 == 0) {
+            if ((st = launch_shared_tc(ctx, W, hidden, 1, sxb, sbd, shared))) return st;
+        } else {
+            if ((st = launch_bf16_rows(ctx, hidden, W.shared_gate, 1, Is, H, sg))) return st;
+            if ((st = launch_bf16_rows(ctx, hidden, W.shared_up, 1, Is, H, su))) return st;
+            if ((st = launch_act(ctx, sg, su, Is, W.activation, W.situ_beta, W.situ_linear_beta, sa))) return st;
+            if ((st = launch_bf16_rows(ctx, sa, W.shared_down, 1, H, Is, shared))) return st;
+        }
         st = launch_residual(ctx, routed, shared, H, combined);   // :336 round_bf16(routed + shared)
     } else {
         st = launch_residual_round(ctx, routed, H, combined);
