@@ -783,7 +783,7 @@ class ReferenceOnB200:
             C.c_float, _f32p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p, _f32p, _u32p, C.c_char_p, _sz]
         L.k3xr_official_two_layer_b200.argtypes = [C.c_int, C.c_int] + [C.c_void_p] * 2 + [C.c_void_p, C.c_float, _f32p,
                                                                                  _f32p] + [C.c_void_p] * 4 + [
-            _f32p, C.c_char_p, _sz]
+            _f32p, _u32p, C.c_char_p, _sz]
 
     def official_layer(self, layer: dict, hidden_in, block, conv, recurrent, device=0, device_route=False,
                        kda_split=0):
@@ -825,13 +825,15 @@ class ReferenceOnB200:
         ptrs = [(C.c_void_p * 2)(*[states[l][i].ctypes.data for l in range(2)]) for i in range(4)]
         hidden_in, block = _c(hidden_in, np.float32), _c(block, np.float32)
         out = np.zeros_like(hidden_in)
+        ids = np.zeros((2, 2, layers[0]["moe"]["top_k"]), np.uint32)
         err = C.create_string_buffer(512)
-        st = self.lib.k3xr_official_two_layer_b200(device, 1 if device_closure else 0, kws, mws, norms, layers[0]["rms_eps"], hidden_in, block,
-                                                   *ptrs, out, err, len(err))
+        st = self.lib.k3xr_official_two_layer_b200(device, 1 if device_closure else 0, kws, mws, norms,
+                                                   layers[0]["rms_eps"], hidden_in, block, *ptrs, out, ids, err,
+                                                   len(err))
         del structs, norm_arrays
         if st:
             raise OracleError(st, "official_two_layer_cuda on B200Backend: " + err.value.decode(errors="replace"))
-        return out, [tuple(s) for s in states]
+        return out, [tuple(s) for s in states], ids
 
 
 def have_reference_on_b200() -> bool:

@@ -215,13 +215,14 @@ int k3xr_official_layer_b200(int device, int device_route, std::size_t kda_split
 // layer an official_layer_cuda with device route preparation;
 // device_closure: official_layer_front / _tail, layer 1's output held for
 // layer 2's front. The arguments of k3xr_official_two_layer plus the device
-// and the mode; the state arrays receive the final states, out [2][H].
+// and the mode; the state arrays receive the final states, out [2][H], ids
+// [2 positions][2 layers][top_k].
 int k3xr_official_two_layer_b200(int device, int device_closure, const k3xr_kda_weights* const kw[2],
                                  const k3xr_moe_layer* const mw[2],
                                  const std::uint16_t* const norms[2][6], float eps, const float* hidden_in,
                                  const float* block, std::uint16_t* const conv_q[2], std::uint16_t* const conv_k[2],
-                                 std::uint16_t* const conv_v[2], float* const recurrent[2], float* out, char* err,
-                                 std::size_t err_len) {
+                                 std::uint16_t* const conv_v[2], float* const recurrent[2], float* out,
+                                 std::uint32_t* ids, char* err, std::size_t err_len) {
     using k3x::ErrorCode;
     const std::size_t H = kw[0]->hidden, h = kw[0]->heads, d = kw[0]->head_dim, P = h * d, W = kw[0]->conv_width;
     for (int l = 0; l < 2; ++l)
@@ -262,6 +263,10 @@ int k3xr_official_two_layer_b200(int device, int device_closure, const k3xr_kda_
         return static_cast<int>(r.error());
     }
     for (std::size_t t = 0; t < 2; ++t) std::copy(r.value().outputs[t].begin(), r.value().outputs[t].end(), out + t * H);
+    // routes [position][layer][top_k], from the steps (position-major)
+    for (const auto& step : r.value().steps)
+        std::copy(step.route.expert_ids.begin(), step.route.expert_ids.end(),
+                  ids + (step.position * 2 + (step.layer_id - 1)) * mw[0]->top_k);
     for (int l = 0; l < 2; ++l) {
         const auto& s = r.value().final_states[l];
         std::copy(s.conv_q.begin(), s.conv_q.end(), conv_q[l]);
