@@ -172,13 +172,13 @@ def test_official_moe_ffn_one_position_equals_the_layer(rs, engine):
         keep = []
         for t in range(hidden.shape[0]):
             slots = []
-            for e in f["ids"][t]:
+            for e in ids[t]:   # the layer path's own route (equal to the fixture's, test above)
                 d = layer_to_dev(torch, _one_expert(layer, int(e)))
                 if eng == k3xb.ENGINE_MXF4:
                     ctx.prepare_layer_scales(d)
                 keep.append(d)
                 slots.append(k3xb.moe_layer_desc(d, engine=eng))
-            got = ctx.official_moe_ffn_host(tail, slots, f["contributions"][t], hidden[t], f["prefix"][t])
+            got = ctx.official_moe_ffn_host(tail, slots, con[t], hidden[t], f["prefix"][t])
             np.testing.assert_array_equal(got, want[t])
             assert_mostly_close(got, f["out"][t], what=f"official moe ffn ({engine}), position {t}")
     finally:
