@@ -1,6 +1,6 @@
 """Expert-parallel MoE layer: the dispatch / local plan / return / combine
 algorithm of csrc/ep.cu, restated on the CPU with the oracle's expert math
-and run as 2 gloo ranks, for the plain MoE and for LatentMoE (latent rows
+and run as 2 and 4 gloo ranks (experts split 4 and 2 per rank), for the plain MoE and for LatentMoE (latent rows
 are projected on the home rank, sent, computed and returned; the routed
 norm and up projection run at home). Its output must equal the
 single-process oracle layer bit for bit (the combine keeps the one-GPU slot
@@ -109,9 +109,9 @@ def _ep_rank(rank, world, port, out_dir, latent):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,latent", [(2, 0), (2, 128)])
+@pytest.mark.parametrize("world,latent", [(2, 0), (2, 128), (4, 0)])
 def test_ep_restatement_equals_one_process(rs, tmp_path, world, latent):
-    port = 29500 + (os.getpid() + latent) % 2000
+    port = 29500 + (os.getpid() + latent + 7 * world) % 2000
     mp.start_processes(_ep_rank, args=(world, port, str(tmp_path), latent), nprocs=world, start_method="spawn")
     L = _layer(rs, latent)
     want, want_ids, _ = rs.moe_layer(L, _hidden(world))
