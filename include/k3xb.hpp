@@ -209,6 +209,42 @@ public:
     Outcome ep_abort() { return check(k3xb_ep_abort(h_)); }
     Outcome ep_finalize() { return check(k3xb_ep_finalize(h_)); }
 
+    // The reference's per-call ComputeBackend shapes (host vectors in and
+    // out, device weights): each returns after its results are on the host.
+    // f32 dense product (dense_matvec), bit-identical to the CPU backend.
+    Outcome dense_matvec(const float* W, std::uint32_t rows, std::span<const float> x, std::span<float> y) {
+        if (y.size() != rows || x.empty()) return Outcome(Status::invalid_extent, "dense_matvec: sizes");
+        return check(k3xb_dense_matvec_host(h_, W, rows, static_cast<std::uint32_t>(x.size()), x.data(), y.data()));
+    }
+    // MXFP4 product (mxfp4_matvec), bit-identical to mxfp4_matmul.
+    Outcome mxfp4_matvec(const std::uint8_t* packed, const std::uint8_t* scales, std::uint32_t rows,
+                         std::span<const float> x, std::span<float> y) {
+        if (y.size() != rows || x.empty()) return Outcome(Status::invalid_extent, "mxfp4_matvec: sizes");
+        return check(k3xb_mxfp4_matvec_host(h_, packed, scales, rows, static_cast<std::uint32_t>(x.size()), x.data(),
+                                            y.data()));
+    }
+    // The official LatentMoE FFN of one position, its route given
+    // (official_mxfp4_moe_ffn): one one-expert layer per slot.
+    Outcome official_moe_ffn(const k3xb_moe_layer& tail, std::span<const k3xb_moe_layer> slots,
+                             std::span<const float> contributions, std::span<const float> hidden,
+                             std::span<const float> prefix, std::span<float> out) {
+        if (slots.size() != contributions.size() || hidden.size() != tail.hidden || prefix.size() != tail.hidden ||
+            out.size() != tail.hidden)
+            return Outcome(Status::invalid_extent, "official_moe_ffn: sizes");
+        return check(k3xb_official_moe_ffn_host(h_, &tail, slots.data(), static_cast<std::uint32_t>(slots.size()),
+                                                contributions.data(), hidden.data(), prefix.data(), out.data()));
+    }
+    // The KDA block with its state held on the device between calls
+    // (official_kda's device state modes); conv/recurrent as k3xb_kda_block_held.
+    Outcome kda_block_held(const k3xb_kda_layer& w, std::uint32_t hidden, std::span<const float> x,
+                           std::uint32_t slot, std::int32_t mode, std::uint16_t* conv, float* recurrent,
+                           std::span<float> out) {
+        if (!hidden || x.size() % hidden || out.size() != x.size())
+            return Outcome(Status::invalid_extent, "kda_block_held: sizes");
+        return check(k3xb_kda_block_held(h_, &w, hidden, x.data(), static_cast<std::uint32_t>(x.size() / hidden),
+                                         slot, mode, conv, recurrent, out.data()));
+    }
+
 private:
     explicit Context(k3xb_ctx* h) : h_(h) {}
     void reset() noexcept {

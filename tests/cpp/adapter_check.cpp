@@ -79,6 +79,18 @@ int main() {
     CHECK(drafter.seen[0].accepted == 1 && drafter.seen[0].committed == (std::vector<std::uint32_t>{2, 0}));
     CHECK(drafter.seen[1].accepted == 1);
 
+    // the host-vector calls check their sizes before the C ABI; an empty
+    // context is answered by the C ABI (INVALID_EXTENT), never by a fallback
+    k3xb::Context none;
+    const std::vector<float> x(8, 1.0F);
+    std::vector<float> y(3), y4(4);
+    CHECK(none.dense_matvec(nullptr, 4, x, y).status() == k3xb::Status::invalid_extent);
+    CHECK(none.dense_matvec(nullptr, 4, x, y4).status() == k3xb::Status::invalid_extent);
+    CHECK(none.mxfp4_matvec(nullptr, nullptr, 4, x, y).status() == k3xb::Status::invalid_extent);
+    k3xb_kda_layer w{};
+    CHECK(none.kda_block_held(w, 3, x, 0, K3XB_KDA_SEED, nullptr, nullptr, y).status() ==
+          k3xb::Status::invalid_extent);
+
     // no B200 here: creation must fail with a status, never fall back
     auto ctx = k3xb::Context::create(0);
     if (ctx) {
