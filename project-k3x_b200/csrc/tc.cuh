@@ -4,8 +4,8 @@
 // Descriptor formats follow the PTX ISA for tcgen05 (shared-memory matrix
 // descriptor, instruction descriptor for .kind::mxf4 block scaling); the
 // field positions were checked against the CUTLASS sm100 headers
-// (cute/arch/mma_sm100_desc.hpp). No TMA load here uses
-// .multicast::cluster.
+// (cute/arch/mma_sm100_desc.hpp). No TMA load here multicasts to the
+// CTAs of a cluster.
 #pragma once
 
 #include <cuda.h>
