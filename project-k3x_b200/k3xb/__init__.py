@@ -653,9 +653,13 @@ class Context:
 
 
 def moe_layer_desc(w: dict, engine=ENGINE_SIMT, act_terms=6) -> MoeLayer:
-    """Builds the C descriptor from a dict of torch CUDA tensors + dims
-    (keeps no references: the caller keeps the tensors alive)."""
+    """Builds the C descriptor from a dict of torch CUDA tensors + dims. The
+    descriptor holds a reference to the dict, so the tensors it points at
+    stay allocated as long as the descriptor object lives (a struct copied
+    by value into another descriptor does not carry it: layer_desc and
+    verify_model_desc keep their parts themselves)."""
     L = MoeLayer()
+    L._keep = w
     L.hidden, L.inter, L.experts, L.top_k = w["hidden"], w["inter"], w["experts"], w["top_k"]
     L.shared_inter = w.get("shared_inter", 0)
     for name in ("router", "correction", "gate_packed", "gate_scales", "up_packed", "up_scales",
@@ -697,6 +701,7 @@ def stack_layer_desc(stack: ResidentStack, w: dict, engine=ENGINE_MXF4, act_term
 def kda_layer_desc(w: dict) -> KdaLayer:
     """C descriptor of a KDA block from a dict of torch CUDA tensors + dims."""
     K = KdaLayer()
+    K._keep = w   # the tensors stay allocated while the descriptor lives
     K.heads, K.head_dim, K.conv_width = w["heads"], w["head_dim"], w["conv_width"]
     K.eps, K.gate_lower_bound = w["eps"], w["gate_lower_bound"]
     for name in ("q_proj", "k_proj", "v_proj", "q_conv", "k_conv", "v_conv", "f_a_proj", "f_b_proj", "a_log",
@@ -709,6 +714,7 @@ def layer_desc(w: dict, engine=ENGINE_MXF4, act_terms=6) -> Layer:
     """C descriptor of a KDA + MoE layer: w["kda"], w["moe"] sub-dicts and
     the six [H] bf16 norm/projection vectors."""
     L = Layer()
+    L._keep = w   # the norm vectors and both sub-dicts' tensors
     L.hidden = w["hidden"]
     L.rms_eps = w["rms_eps"]
     for name in ("self_residual_norm", "self_residual_proj", "input_norm", "moe_residual_norm",
@@ -734,7 +740,7 @@ def verify_model_desc(layers, vocab, lm_head, embedding=None, final_norm=None, f
     m.final_norm = None if final_norm is None else final_norm.data_ptr()
     m.final_eps = final_eps
     m.lm_head = lm_head.data_ptr()
-    m._keep = arr
+    m._keep = (arr, list(layers), lm_head, embedding, final_norm)
     return m
 
 
@@ -750,6 +756,8 @@ def verify_io_desc(sequences, drafts, conv, recurrent, accepted, committed, comm
     io.seed, io.sequence_base = seed, sequence_base
     io.logits, io.accepted, io.committed = ptr(logits), ptr(accepted), ptr(committed)
     io.committed_count = ptr(committed_count)
+    io._keep = (tokens, hidden_in, block_source, draft_tokens, conv, recurrent, draft_logits, logits, accepted,
+                committed, committed_count)
     return io
 
 

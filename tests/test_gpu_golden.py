@@ -76,7 +76,8 @@ def test_moe_layer_golden(torch, ctx, engine):
     import k3xb
     layer, hidden, want_out, want_ids, want_con = gu.moe_layer()
     eng = k3xb.ENGINE_MXF4 if engine == "mxf4" else k3xb.ENGINE_SIMT
-    desc = k3xb.moe_layer_desc(layer_to_dev(torch, layer), engine=eng)
+    d = layer_to_dev(torch, layer)   # the device weights live as long as this test
+    desc = k3xb.moe_layer_desc(d, engine=eng)
     T, K, H = hidden.shape[0], layer["top_k"], layer["hidden"]
     out = torch.empty((T, H), dtype=torch.float32, device="cuda")
     ids = torch.empty((T, K), dtype=torch.int32, device="cuda")

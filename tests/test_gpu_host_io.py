@@ -42,7 +42,8 @@ def test_expert_grid_host_vs_oracle_and_single_expert_stacks(torch, ctx, rs):
     d = DIMS
     L = make_moe_layer(rs, 81, d["hidden"], d["inter"], d["experts"], d["top_k"])
     x = bf16_normal(np.random.default_rng(82), (5, d["hidden"]))
-    desc = k3xb.moe_layer_desc(layer_to_dev(torch, L), engine=k3xb.ENGINE_MXF4)
+    d_dev = layer_to_dev(torch, L)
+    desc = k3xb.moe_layer_desc(d_dev, engine=k3xb.ENGINE_MXF4)
     ids = [3, 0, 7]
     got = ctx.expert_grid_host(desc, ids, x)
     assert got.shape == (3, 5, d["hidden"])
@@ -185,7 +186,11 @@ def test_dense_matvec_bit_identical_to_the_cpu_backend(torch, ctx, rs):
     x = g.normal(0, 1, size=cols).astype(np.float32)
     for beta, lin in ((4.0, 0.0), (2.0, 25.0)):
         got = ctx.dense_situ_mlp_host(to_dev(torch, gate), to_dev(torch, up), to_dev(torch, down), x, beta, lin)
-        np.testing.assert_allclose(got, rs.dense_situ_mlp(x, gate, up, down, beta, lin), rtol=1e-5, atol=1e-7)
+        want = rs.dense_situ_mlp(x, gate, up, down, beta, lin)
+        # the products are exact; only situ_glu's tanhf/expf (device vs glibc)
+        # may differ by an ulp, and the down projection carries that into an
+        # output as a few ulps of the output scale (|y| up to ~1)
+        np.testing.assert_allclose(got, want, rtol=1e-5, atol=8 * np.finfo(np.float32).eps * np.abs(want).max())
 
 
 def test_mxfp4_matvec_and_resident_layer_vs_cpu_backend(torch, ctx, rs):

@@ -19,7 +19,8 @@ def test_phase_profile_moe_layer(rs):
     ctx = k3xb.Context(0)
     ctx.use_stream()
     try:
-        desc = k3xb.moe_layer_desc(layer_to_dev(torch, layer), engine=k3xb.ENGINE_MXF4)
+        d = layer_to_dev(torch, layer)
+        desc = k3xb.moe_layer_desc(d, engine=k3xb.ENGINE_MXF4)
         plain = torch.empty((7, 256), dtype=torch.float32, device="cuda")
         ctx.moe_layer_forward(desc, x, plain)
         ctx.sync()
