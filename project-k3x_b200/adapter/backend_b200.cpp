@@ -56,8 +56,7 @@ bool valid_activation(float beta, std::optional<float> linear) {
 
 class B200Backend final : public ComputeBackend {
 public:
-    B200Backend(const BackendOptions& options, k3xb_ctx* ctx, std::unique_ptr<ComputeBackend> rest)
-        : options_(options), ctx_(ctx), rest_(std::move(rest)) {
+    B200Backend(const BackendOptions& options, k3xb_ctx* ctx) : options_(options), ctx_(ctx) {
         if (ctx_ && options_.cuda_weights == CudaWeightMode::resident && options_.cuda_resident_bytes)
             k3xb_set_resident_capacity(ctx_, options_.cuda_resident_bytes);
     }
@@ -72,7 +71,7 @@ public:
     std::string_view device_name() const noexcept override { return "NVIDIA B200 (libk3xb, sm_100a)"; }
 
     BackendRuntimeStats runtime_stats() const noexcept override {
-        BackendRuntimeStats r = rest_ ? rest_->runtime_stats() : BackendRuntimeStats{};
+        BackendRuntimeStats r{};
         k3xb_stats s{};
         if (ctx_ && k3xb_get_stats(ctx_, &s) == K3XB_OK) {
             r.weight_cache_hits += s.weight_cache_hits;
@@ -94,7 +93,7 @@ public:
     }
 
     BackendMemoryStats memory_stats() const noexcept override {
-        BackendMemoryStats m = rest_ ? rest_->memory_stats() : BackendMemoryStats{};
+        BackendMemoryStats m{};
         k3xb_stats s{};
         if (ctx_ && k3xb_get_stats(ctx_, &s) == K3XB_OK) {
             m.current_device_bytes += s.resident_weight_bytes + s.scratch_bytes;
@@ -107,14 +106,12 @@ public:
     // The CPU backend's checks (backend_cpu.cpp:368-377, :404-410,
     // invalid_extent) and its arithmetic bit for bit (one FP64 chain per row
     // in column order). A weight is kept resident by its tensor id; one
-    // without an id (0) cannot be, and goes to the other backend.
+    // without an id (0) cannot be: backend_unavailable (backend.hpp:357-362).
     Result<std::vector<float>> dense_matvec(std::span<const float> input, DenseWeightView weight,
-                                            std::uint32_t layer, ProfilePhase phase) override {
+                                            std::uint32_t /*layer*/, ProfilePhase /*phase*/) override {
         if (!valid_dense(input, weight)) return Result<std::vector<float>>::failure(ErrorCode::invalid_extent);
-        if (!weight.tensor_id || !weight.rows) {
-            if (!rest_) return unavailable<std::vector<float>>("dense_matvec: a weight without a tensor id");
-            return rest_->dense_matvec(input, weight, layer, phase);
-        }
+        if (!weight.tensor_id || !weight.rows)
+            return unavailable<std::vector<float>>("dense_matvec: a weight without a tensor id");
         ErrorCode st = ErrorCode::ok;
         const float* W = dense_resident(weight, &st);
         if (!W) return Result<std::vector<float>>::failure(st, last_error());
@@ -127,15 +124,13 @@ public:
     // single MXFP4 products (k3xb_mxfp4_matvec_host): mxfp4_matmul's checks
     // (ops.cpp:32-60, invalid_mxfp4) and arithmetic bit for bit
     Result<std::vector<float>> mxfp4_matvec(std::span<const float> input, Mxfp4WeightView weight,
-                                            std::uint32_t layer, ProfilePhase phase) override {
+                                            std::uint32_t /*layer*/, ProfilePhase /*phase*/) override {
         if (input.size() != weight.cols || !weight.rows || !weight.cols || !weight.group_size ||
             weight.cols % weight.group_size || weight.cols % 2 || weight.packed.size() != weight.rows * weight.cols / 2 ||
             weight.scales.size() != weight.rows * weight.cols / weight.group_size)
             return Result<std::vector<float>>::failure(ErrorCode::invalid_mxfp4);
-        if (!weight.tensor_id || weight.group_size != 32) {   // nothing to keep it resident by, or not group 32
-            if (!rest_) return unavailable<std::vector<float>>("mxfp4_matvec: no tensor id, or a group other than 32");
-            return rest_->mxfp4_matvec(input, weight, layer, phase);
-        }
+        if (!weight.tensor_id || weight.group_size != 32)   // nothing to keep it resident by, or not group 32
+            return unavailable<std::vector<float>>("mxfp4_matvec: no tensor id, or a group other than 32");
         k3xb_resident r{};
         const ErrorCode st = mxfp4_resident(weight, &r);
         if (st != ErrorCode::ok) return Result<std::vector<float>>::failure(st, last_error());
@@ -176,17 +171,15 @@ public:
         return R::success(std::move(out));
     }
     Result<std::vector<float>> dense_situ_mlp(std::span<const float> input, DenseMlpView weights, float situ_beta,
-                                              std::optional<float> situ_linear, std::uint32_t layer,
-                                              ProfilePhase phase) override {
+                                              std::optional<float> situ_linear, std::uint32_t /*layer*/,
+                                              ProfilePhase /*phase*/) override {
         const auto& g = weights.gate;
         if (!valid_dense(input, g) || !valid_dense(input, weights.up) || !g.rows || g.rows != weights.up.rows ||
             weights.down.cols != g.rows || weights.down.values.size() != weights.down.rows * weights.down.cols)
             return Result<std::vector<float>>::failure(ErrorCode::invalid_extent);
         if (!g.tensor_id || !weights.up.tensor_id || !weights.down.tensor_id || !weights.down.rows ||
-            !valid_activation(situ_beta, situ_linear)) {
-            if (!rest_) return unavailable<std::vector<float>>("dense_situ_mlp: untracked weights or SiTU parameters");
-            return rest_->dense_situ_mlp(input, weights, situ_beta, situ_linear, layer, phase);
-        }
+            !valid_activation(situ_beta, situ_linear))
+            return unavailable<std::vector<float>>("dense_situ_mlp: untracked weights or SiTU parameters");
         ErrorCode st = ErrorCode::ok;
         const float* G = dense_resident(g, &st);
         const float* U = G ? dense_resident(weights.up, &st) : nullptr;
@@ -209,7 +202,7 @@ public:
                                                             std::span<const Mxfp4MlpView> experts,
                                                             std::span<const float> contributions, float epsilon,
                                                             float beta, std::optional<float> linear,
-                                                            std::uint32_t layer, ProfilePhase phase) override {
+                                                            std::uint32_t /*layer*/, ProfilePhase /*phase*/) override {
         using R = Result<ResidentMoeLayerResult>;
         const auto& sh = w.shared;
         const bool mlp_ok = valid_dense(input, sh.gate) && valid_dense(input, sh.up) && sh.gate.rows &&
@@ -236,11 +229,8 @@ public:
             if (!valid_matrix(e.gate, I, D) || !valid_matrix(e.up, I, D) || !valid_matrix(e.down, Dout, I) ||
                 !fresh(e.gate.tensor_id) || !fresh(e.up.tensor_id) || !fresh(e.down.tensor_id))
                 return R::failure(ErrorCode::invalid_mxfp4);
-        if (Dout != D) {   // a routed width other than the latent width: not this library's shape
-            if (!rest_) return unavailable<ResidentMoeLayerResult>("resident MoE layer shape is not on the B200 path");
-            return rest_->resident_mxfp4_moe_layer(input, w, experts, contributions, epsilon, beta, linear, layer,
-                                                   phase);
-        }
+        if (Dout != D)   // a routed width other than the latent width: not this library's shape
+            return unavailable<ResidentMoeLayerResult>("resident MoE layer shape is not on the B200 path");
         ErrorCode st = ErrorCode::ok;
         const auto f32 = [&](std::uint64_t id, std::span<const float> v, std::size_t rows, std::size_t cols) {
             return st == ErrorCode::ok ? static_cast<const float*>(
@@ -597,7 +587,7 @@ private:
                                               std::span<const Mxfp4MlpView> experts,
                                               std::span<const std::uint32_t> ids,
                                               std::span<const float> contributions, float epsilon, float beta,
-                                              std::optional<float> linear, std::uint32_t layer, ProfilePhase phase) {
+                                              std::optional<float> linear, std::uint32_t /*layer*/, ProfilePhase /*phase*/) {
         using R = Result<OfficialMoeFfnResult>;
         const auto valid_bf16 = [](const Bf16WeightView& v) {
             return v.tensor_id && v.rows && v.cols && v.rows <= SIZE_MAX / v.cols && v.values.size() == v.rows * v.cols;
@@ -634,12 +624,8 @@ private:
         if (prepared) prepared_.active = false;   // consumed
         // this library's shapes: expert output width = latent width, bf16
         // linears over multiples of 8, MXFP4 groups of 32, at most 64 slots
-        if (Dout != D || H % 8 || D % 32 || I % 32 || experts.size() > 64) {
-            if (!rest_ || prepared)   // a prepared route lives here: the other backend cannot consume it
-                return unavailable<OfficialMoeFfnResult>("official MoE FFN shape is not on the B200 path");
-            return rest_->official_mxfp4_moe_ffn(hidden, prefix, w, experts, ids, contributions, epsilon, beta,
-                                                 linear, layer, phase);
-        }
+        if (Dout != D || H % 8 || D % 32 || I % 32 || experts.size() > 64)
+            return unavailable<OfficialMoeFfnResult>("official MoE FFN shape is not on the B200 path");
         ErrorCode st = ErrorCode::ok;
         const auto bf16 = [&](std::uint64_t id, std::span<const std::uint16_t> v, std::size_t rows,
                               std::size_t cols) {
@@ -1048,7 +1034,6 @@ private:
 
     BackendOptions options_;
     k3xb_ctx* ctx_;
-    std::unique_ptr<ComputeBackend> rest_;
     std::map<std::uint64_t, std::vector<Mxfp4MlpView>> prefetched_;
     // the one prepared route (prepare_official_moe_route), its owner this backend
     struct PreparedRoute {
@@ -1093,19 +1078,17 @@ private:
 
 }  // namespace
 
-std::unique_ptr<ComputeBackend> wrap_b200_context(const BackendOptions& options, k3xb_ctx* ctx,
-                                                  std::unique_ptr<ComputeBackend> rest) {
-    return std::make_unique<B200Backend>(options, ctx, std::move(rest));
+std::unique_ptr<ComputeBackend> wrap_b200_context(const BackendOptions& options, k3xb_ctx* ctx) {
+    return std::make_unique<B200Backend>(options, ctx);
 }
 
-Result<std::unique_ptr<ComputeBackend>> make_b200_backend(const BackendOptions& options, int device,
-                                                          std::unique_ptr<ComputeBackend> rest) {
+Result<std::unique_ptr<ComputeBackend>> make_b200_backend(const BackendOptions& options, int device) {
     k3xb_ctx* ctx = nullptr;
     const int rc = k3xb_create(device, &ctx);
     if (rc != K3XB_OK)
         return Result<std::unique_ptr<ComputeBackend>>::failure(static_cast<ErrorCode>(rc),
                                                                 "B200 backend: k3xb_create failed");
-    return Result<std::unique_ptr<ComputeBackend>>::success(wrap_b200_context(options, ctx, std::move(rest)));
+    return Result<std::unique_ptr<ComputeBackend>>::success(wrap_b200_context(options, ctx));
 }
 
 }  // namespace k3x

@@ -5,10 +5,11 @@
 // is what a maintainer adds next to it (runtime/src/backend_b200.cpp, linked
 // with libk3xb.so): the hot-path methods of ComputeBackend
 // (runtime/include/k3x/backend.hpp:326-462) run on the B200 through the C
-// ABI of k3xb.h, everything else goes to a backend the maintainer passes
-// in (`rest`, e.g. the reference's CPU or dense CUDA backend) or returns
-// backend_unavailable when there is none. A failing hot-path call is
-// returned as it is; it is never retried on `rest`.
+// ABI of k3xb.h. A call this library cannot take (a weight without a tensor
+// id, which cannot stay resident, or a shape outside these kernels) returns
+// backend_unavailable, as the reference's contract asks for unsupported
+// shapes (backend.hpp:357-362): nothing falls back to the CPU. A failing
+// call is returned as it is.
 //
 // On the B200:
 //   mxfp4_matvec / _group, resident_mxfp4_moe_layer (weights with a tensor id)
@@ -52,11 +53,9 @@ namespace k3x {
 // Creates a context on `device` (k3xb_create: compute capability 10.x only)
 // and wraps it. Fails with the C ABI's status (backend_unavailable without a
 // GPU, unsupported_architecture on other GPUs).
-Result<std::unique_ptr<ComputeBackend>> make_b200_backend(const BackendOptions& options, int device = 0,
-                                                          std::unique_ptr<ComputeBackend> rest = nullptr);
+Result<std::unique_ptr<ComputeBackend>> make_b200_backend(const BackendOptions& options, int device = 0);
 
 // Wraps an existing context and takes ownership of it.
-std::unique_ptr<ComputeBackend> wrap_b200_context(const BackendOptions& options, k3xb_ctx* ctx,
-                                                  std::unique_ptr<ComputeBackend> rest = nullptr);
+std::unique_ptr<ComputeBackend> wrap_b200_context(const BackendOptions& options, k3xb_ctx* ctx);
 
 }  // namespace k3x
