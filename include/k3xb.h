@@ -149,11 +149,15 @@ int k3xb_route(k3xb_ctx* ctx, const float* hidden, uint32_t tokens,
  * 1 MiB array compiled into the library (one per GPU, held until exit), so
  * tokens * experts must be <= 262144, else K3XB_INVALID_EXTENT. Runs on
  * `stream` (a cudaStream_t, NULL = legacy default stream) of the current
- * device and returns before the work finishes. `status` (device int32, may
- * be NULL) receives K3XB_INVALID_EXTENT for non-finite inputs. All calls on
- * a device share the array, so calls that overlap on the GPU race. The
- * first call on each device looks the array up once; make it before any
- * stream capture starts. */
+ * device and returns before the work finishes. `status` (device int32)
+ * receives K3XB_INVALID_EXTENT for non-finite inputs and
+ * K3XB_BACKEND_UNAVAILABLE when a bounded wait in the logits kernel ran out;
+ * with status NULL those device-side failures are dropped (the call still
+ * returns K3XB_OK and ids/contributions are then undefined), so callers
+ * that cannot rule them out should pass a status word. All calls on a
+ * device share the array, so calls that overlap on the GPU race. The first
+ * call on each device looks the array up once; make it before any stream
+ * capture starts. */
 int k3xb_route_static(const float* hidden, uint32_t tokens, uint32_t hidden_size,
                       const uint16_t* router, const float* correction,
                       uint32_t experts, uint32_t top_k, uint32_t* ids,
@@ -744,7 +748,7 @@ typedef struct {
 int k3xb_speculative_step(k3xb_ctx* ctx, const k3xb_verify_model* model,
                           const k3xb_speculative_io* io);
 
-/* ---- expert parallelism (NCCL over NVLink) ---------------------------------- */
+/* ---- expert parallelism (peer memory over NVLink; NCCL for set-up) ---------- */
 /* 128-byte NCCL unique id, made on one rank and handed to all (any
  * transport: a store, a file, a broadcast). No reference counterpart: the
  * reference runs one process on one GPU. */
@@ -753,11 +757,13 @@ int k3xb_ep_unique_id(uint8_t* unique_id);
  * communicator with the default bound (k3xb_ep_init_config with NULL). */
 int k3xb_ep_init(k3xb_ctx* ctx, const uint8_t* unique_id, int32_t rank,
                  int32_t world);
-/* Failure detection. Every wait on the communicator has a bound: the
- * stream drains of k3xb_sync, of scratch growth, of k3xb_ep_finalize and of
- * k3xb_destroy, and (nonblocking = 1) creation and each exchange's launch.
- * A bound that passes, or an error NCCL reports (a peer that failed), aborts
- * the communicator, whose kernels in flight then return; the call returns
+/* Failure detection. Every wait has a bound: on the host the stream drains
+ * of k3xb_sync, of scratch and window growth, of k3xb_ep_finalize and of
+ * k3xb_destroy, and (nonblocking = 1) communicator creation and each NCCL
+ * launch; on the device each kernel's wait for the other ranks' exchange
+ * flags (5 s). A bound that passes, or an error NCCL reports (a peer that
+ * failed), aborts the exchange (its kernels in flight return); the call, or
+ * the next k3xb_sync after a device wait gave up, returns
  * BACKEND_UNAVAILABLE with the reason in k3xb_last_error. The context's
  * one-GPU entry points keep working; the expert-parallel ones return
  * INVALID_STATE until k3xb_ep_finalize and a new init (with a new unique id
@@ -787,15 +793,33 @@ int k3xb_ep_finalize(k3xb_ctx* ctx);
  * this rank holds experts [rank*E/world, (rank+1)*E/world) in `local`
  * (local->experts == E / world; router [E][H], correction [E] and the shared
  * expert are the full, replicated ones) and `tokens` tokens of its own
- * sequences, the same count on every rank. Tokens reach the experts' ranks
- * and the outputs come back by NCCL all-to-all; the combine runs on the
- * token's rank with the one-GPU arithmetic, so out/ids/contributions equal
- * the single-GPU layer's bit for bit. Every rank calls it with the same
- * shapes (a collective). MXF4 engine only. */
+ * sequences, the same count on every rank. Each rank owns an exchange
+ * window that the others map (CUDA IPC handles all-gathered over the
+ * communicator at the first call, and again if a call needs a larger one):
+ * a token's row goes only to the ranks that own one of its experts, and
+ * the down projection stores each (token, slot) output row straight into
+ * the token's rank's window; epoch flags with bounded waits order the
+ * steps. The combine runs on the token's rank with the one-GPU arithmetic,
+ * so out/ids/contributions equal the single-GPU layer's bit for bit. Every
+ * rank calls it with the same shapes (a collective). MXF4 engine only; at
+ * most 8 ranks. */
 int k3xb_ep_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* local,
                               uint32_t experts_total, const float* hidden,
                               uint32_t tokens, float* out, uint32_t* ids,
                               float* contributions);
+
+/* The verify step (k3xb_verify_step) over this rank's own sequences, with
+ * every layer's MoE expert parallel: each layer descriptor's experts are
+ * this rank's slice of experts_total (ranks hold equal slices in rank
+ * order); router, correction, shared expert, KDA, norms, embedding and LM
+ * head are whole on every rank. KDA, routing, the shared expert, the LM head
+ * and acceptance run on the token's rank (data parallel over sequences); the
+ * routed experts run on the rank that owns them, reached through the
+ * exchange windows as in k3xb_ep_moe_layer_forward. Replaces the reference's
+ * one-process Engine::forward_expert_major_block (model.cpp:133-420) for
+ * one box of GPUs; every rank calls it with the same shapes (a collective). */
+int k3xb_ep_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* model,
+                        const k3xb_verify_io* io, uint32_t experts_total);
 
 /* ---- (e) acceptance ------------------------------------------------------- */
 /* verify_greedy_target_block (runtime/src/speculative.cpp:74-112) for S

@@ -111,9 +111,11 @@ k3xb_moe_layer expert_view(const k3xb_moe_layer& L) {
     return v;
 }
 
+// ep_E: the experts a route picks from in an expert-parallel layer (L then
+// holds this rank's slice); 0 otherwise.
 template <typename A>
-void layout_moe(A& a, const k3xb_moe_layer& L, uint32_t T, bool host, MoeScratch* s) {
-    const size_t E = L.experts, K = L.top_k, H = L.hidden, I = L.inter, Is = L.shared_inter;
+void layout_moe(A& a, const k3xb_moe_layer& L, uint32_t T, bool host, MoeScratch* s, uint32_t ep_E = 0) {
+    const size_t E = ep_E ? ep_E : L.experts, K = L.top_k, H = L.hidden, I = L.inter, Is = L.shared_inter;
     const size_t D = L.latent ? L.latent : H;   // the experts' width
     MoeScratch tmp{};
     MoeScratch& r = s ? *s : tmp;
@@ -174,9 +176,14 @@ int validate_layer(k3xb_ctx* ctx, const k3xb_moe_layer* L) {
     return K3XB_OK;
 }
 
+// With ep_E != 0 the layer is expert parallel: L is this rank's slice of
+// ep_E experts, the route picks from all ep_E, and the experts run through
+// the exchange (ep.cu) with the plan and engine scratch in ep_region; the
+// rows it sends are bf16-valued (the MoE input and the latent rows are).
 int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T,
-                       float* out, uint32_t* ids_out, float* contrib_out, MoeScratch& s) {
-    const uint32_t E = L.experts, K = L.top_k, H = L.hidden;
+                       float* out, uint32_t* ids_out, float* contrib_out, MoeScratch& s, uint32_t ep_E = 0,
+                       void* ep_region = nullptr) {
+    const uint32_t E = ep_E ? ep_E : L.experts, K = L.top_k, H = L.hidden;
     uint32_t* ids = ids_out ? ids_out : s.ids;
     float* contrib = contrib_out ? contrib_out : s.contrib;
     s.plan.status = ctx->status_word;
@@ -199,6 +206,30 @@ int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidd
         if ((st = launch_router_logits(ctx, hidden, T, H, L.router, E, s.logits))) return st;
         if ((st = launch_topk(ctx, s.logits, L.correction, T, E, K, ids, contrib, nullptr, s.plan.status)))
             return st;
+    }
+    if (ep_E) {
+        const k3xb_moe_layer LE = expert_view(L);
+        const float* shared = L.shared_gate ? s.shared_out : nullptr;
+        if (!L.latent) {
+            if (shared) K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
+            if ((st = ep_moe_forward(ctx, L, E, hidden, T, ids, contrib, shared, ep_region, out, true))) return st;
+        } else {   // official_moe.cpp:296, the experts on latent rows, then :322-336
+            {
+                PhaseScope ph(ctx, K3XB_PHASE_LATENT);
+                if ((st = launch_linear_bf16(ctx, hidden, L.routed_down, T, LE.hidden, H, 1, s.xt, s.lat))) return st;
+            }
+            if ((st = ep_moe_forward(ctx, LE, E, s.lat, T, ids, contrib, nullptr, ep_region, s.mixed, true)))
+                return st;
+            PhaseScope ph(ctx, K3XB_PHASE_LATENT);
+            if ((st = launch_rms_norm(ctx, s.mixed, L.routed_norm, T, LE.hidden, L.latent_eps, s.normed))) return st;
+            if ((st = launch_linear_bf16(ctx, s.normed, L.routed_up, T, H, LE.hidden, 1, s.xt, s.routed))) return st;
+            if (shared) K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
+            const size_t n = static_cast<size_t>(T) * H;
+            st = shared ? launch_residual(ctx, s.routed, shared, n, out) : launch_residual_round(ctx, s.routed, n, out);
+            if (st) return st;
+        }
+        ++ctx->stats.moe_layer_calls;
+        return K3XB_OK;
     }
     {
         PhaseScope ph(ctx, K3XB_PHASE_PLAN);
@@ -329,6 +360,7 @@ int k3xb_set_stream(k3xb_ctx* ctx, void* stream) {
 int k3xb_sync(k3xb_ctx* ctx) {
     K3XB_ENTER(ctx);
     if (const int st = stream_wait(ctx)) return st;
+    if (const int st = ep_check_waits(ctx)) return st;
     int32_t st = 0;
     K3XB_CUDA(ctx, cudaMemcpy(&st, ctx->status_word, sizeof st, cudaMemcpyDeviceToHost));
     if (st) {
@@ -1041,7 +1073,7 @@ int validate_full_layer(k3xb_ctx* ctx, const k3xb_layer* L) {
 // Scratch of one layer forward (its region starts at the scratch base).
 template <typename A>
 void layout_layer(A& a, const k3xb_layer& L, uint32_t N, uint32_t S, bool own_trace, KdaTrace* tr, KdaWork* wk,
-                  float** bufs, MoeScratch* ms) {
+                  float** bufs, MoeScratch* ms, uint32_t ep_E = 0, void** ep_region = nullptr) {
     const size_t T = static_cast<size_t>(N) * S, H = L.hidden;
     const size_t P = static_cast<size_t>(L.kda.heads) * L.kda.head_dim;
     if (own_trace) layout_trace(a, T, P, L.kda.heads, tr);
@@ -1050,31 +1082,41 @@ void layout_layer(A& a, const k3xb_layer& L, uint32_t N, uint32_t S, bool own_tr
         float* b = a.template take<float>(T * H);
         if (bufs) bufs[i] = b;
     }
-    layout_moe(a, L.moe, static_cast<uint32_t>(T), false, ms);
+    layout_moe(a, L.moe, static_cast<uint32_t>(T), false, ms, ep_E);
+    if (ep_E) {   // the local plan over the received rows (ep.cu)
+        const uint32_t G = static_cast<uint32_t>(ep_E / L.moe.experts);
+        void* r = a.template take<uint8_t>(ep_scratch_bytes(G, static_cast<uint32_t>(T), L.moe.top_k,
+                                                            expert_view(L.moe).hidden, L.moe.experts), 1024);
+        if (ep_region) *ep_region = r;
+    }
 }
 
-size_t layer_work_bytes(const k3xb_layer& L, uint32_t N, uint32_t S, bool own_trace) {
+// The engine's region comes last; expert parallel, it holds the rows that
+// every rank sends (world x T).
+size_t layer_work_bytes(const k3xb_layer& L, uint32_t N, uint32_t S, bool own_trace, uint32_t ep_E = 0) {
     Sizer sz;
-    layout_layer(sz, L, N, S, own_trace, nullptr, nullptr, nullptr, nullptr);
-    return sz.used + mxf4_scratch_bytes(expert_view(L.moe), N * S) + 1024;
+    layout_layer(sz, L, N, S, own_trace, nullptr, nullptr, nullptr, nullptr, ep_E);
+    const uint32_t rows = ep_E ? N * S * (ep_E / L.moe.experts) : N * S;
+    return sz.used + mxf4_scratch_bytes(expert_view(L.moe), rows) + 1024;
 }
 
 // official_layer_cpu with the plain MoE; d_tables = device anc table +
 // recurrence schedule for `sch`.
 int layer_forward_impl(k3xb_ctx* ctx, const k3xb_layer& L, const float* hidden_in, const float* block, uint32_t N,
                        uint32_t S, const uint16_t* conv, const float* rec, float* hidden_out, uint32_t* ids_out,
-                       void* trace, const KdaSchedule& sch, const int32_t* d_tables) {
+                       void* trace, const KdaSchedule& sch, const int32_t* d_tables, uint32_t ep_E = 0) {
     const uint32_t T = N * S, H = L.hidden;
     const size_t P = static_cast<size_t>(L.kda.heads) * L.kda.head_dim;
     void* base;
-    int st = ensure_scratch(ctx, layer_work_bytes(L, N, S, trace == nullptr), &base);
+    int st = ensure_scratch(ctx, layer_work_bytes(L, N, S, trace == nullptr, ep_E), &base);
     if (st) return st;
     Carver c(base);
     KdaTrace tr{};
     KdaWork wk{};
     float* bufs[4];
     MoeScratch ms{};
-    layout_layer(c, L, N, S, trace == nullptr, &tr, &wk, bufs, &ms);
+    void* ep_region = nullptr;
+    layout_layer(c, L, N, S, trace == nullptr, &tr, &wk, bufs, &ms, ep_E, &ep_region);
     if (trace) {
         Carver t(trace);
         layout_trace(t, T, P, L.kda.heads, &tr);
@@ -1096,7 +1138,8 @@ int layer_forward_impl(k3xb_ctx* ctx, const k3xb_layer& L, const float* hidden_i
             return st;
     }
     // plain MoE: combined = round_bf16(routed + shared), then the residual (official_moe.cpp:336-341)
-    if ((st = moe_forward_device(ctx, L.moe, moe_in, T, hidden_out, ids_out, nullptr, ms))) return st;
+    if ((st = moe_forward_device(ctx, L.moe, moe_in, T, hidden_out, ids_out, nullptr, ms, ep_E, ep_region)))
+        return st;
     return launch_residual(ctx, prefix, hidden_out, static_cast<size_t>(T) * H, hidden_out);
 }
 
@@ -1407,8 +1450,10 @@ int k3xb_layer_forward(k3xb_ctx* ctx, const k3xb_layer* L, const float* hidden_i
     return layer_forward_impl(ctx, *L, hidden_in, block, N, S, conv, rec, hidden_out, ids_out, trace, sch, d_tables);
 }
 
-int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verify_io* io) {
-    K3XB_ENTER(ctx);
+// The verify step; with ep_E != 0 every layer's MoE is expert parallel
+// (its descriptor holds this rank's slice of ep_E experts) and the step
+// covers this rank's own sequences.
+static int verify_step_impl(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verify_io* io, uint32_t ep_E) {
     if (!m || !io || !m->layers || !m->layer || !m->vocab || !m->lm_head)
         return fail(ctx, K3XB_INVALID_EXTENT, "verify model");
     int st;
@@ -1436,8 +1481,17 @@ int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verif
     if ((st = schedule_tree(ctx, parent.data(), N, sch))) return st;
     const uint32_t cw = L0.kda.conv_width, h = L0.kda.heads, d = L0.kda.head_dim, P = h * d;
     const std::vector<int32_t> tables = kda_tables(parent.data(), N, cw, sch);
+    if (ep_E) {   // the exchange window for the widest layer, before anything is queued
+        uint32_t Kmax = 0, Dmax = 0;
+        for (uint32_t l = 0; l < m->layers; ++l) {
+            Kmax = std::max(Kmax, m->layer[l].moe.top_k);
+            Dmax = std::max(Dmax, expert_view(m->layer[l].moe).hidden);
+        }
+        if ((st = ep_reserve(ctx, T, Kmax, Dmax))) return st;
+    }
     size_t own = 0;
-    for (uint32_t l = 0; l < m->layers; ++l) own = std::max(own, layer_work_bytes(m->layer[l], N, S, false));
+    for (uint32_t l = 0; l < m->layers; ++l)
+        own = std::max(own, layer_work_bytes(m->layer[l], N, S, false, ep_E));
     const size_t TH = static_cast<size_t>(T) * H, trace_bytes = k3xb_kda_trace_bytes(&L0.kda, N, S);
     Sizer sz;
     sz.take<uint8_t>(own);
@@ -1476,7 +1530,7 @@ int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verif
     for (uint32_t l = 0; l < m->layers; ++l) {
         float* out = buf[l & 1u];
         if ((st = layer_forward_impl(ctx, m->layer[l], x, block, N, S, io->conv + l * conv_stride,
-                                     io->recurrent + l * rec_stride, out, nullptr, traces[l], sch, d_tables)))
+                                     io->recurrent + l * rec_stride, out, nullptr, traces[l], sch, d_tables, ep_E)))
             return st;
         x = out;
     }
@@ -1521,6 +1575,30 @@ int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verif
             return st;
     }
     return K3XB_OK;
+}
+
+int k3xb_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verify_io* io) {
+    K3XB_ENTER(ctx);
+    return verify_step_impl(ctx, m, io, 0);
+}
+
+int k3xb_ep_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_verify_io* io,
+                        uint32_t experts_total) {
+    K3XB_ENTER(ctx);
+    const int G = ep_world(ctx);
+    if (G < 1) return fail(ctx, K3XB_INVALID_STATE, "expert parallelism not initialised (k3xb_ep_init)");
+    if (!m || !m->layer || !m->layers) return fail(ctx, K3XB_INVALID_EXTENT, "verify model");
+    if (!experts_total || experts_total % static_cast<uint32_t>(G) || experts_total > 1024)
+        return fail(ctx, K3XB_INVALID_EXTENT, "experts_total must split evenly over the world (<= 1024)");
+    for (uint32_t l = 0; l < m->layers; ++l) {
+        const k3xb_moe_layer& M = m->layer[l].moe;
+        if (M.engine != K3XB_ENGINE_MXF4) return fail(ctx, K3XB_INVALID_STATE, "expert parallelism runs the MXF4 engine");
+        if (M.experts != experts_total / static_cast<uint32_t>(G))
+            return fail(ctx, K3XB_INVALID_EXTENT, "every layer's experts must be experts_total / world (this rank's slice)");
+        if (M.top_k > 32 || M.top_k > experts_total)
+            return fail(ctx, K3XB_INVALID_EXTENT, "expert parallel route: top_k <= 32");
+    }
+    return verify_step_impl(ctx, m, io, experts_total);
 }
 
 int k3xb_draft_greedy(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_draft_io* io) {
@@ -1628,6 +1706,7 @@ int k3xb_ep_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* local, uint32
     if (local->top_k > E || local->top_k > 32 || E > 1024 || local->top_k > 255)
         return fail(ctx, K3XB_INVALID_EXTENT, "route: need top_k <= 32 and experts <= 1024");
     if (!T || !hidden || !out) return fail(ctx, K3XB_INVALID_EXTENT, "ep forward arguments");
+    if ((st = ep_reserve(ctx, T, local->top_k, expert_view(*local).hidden))) return st;
     const uint32_t K = local->top_k, H = local->hidden, Is = local->shared_inter;
     const bool shared = local->shared_gate != nullptr;
     // a LatentMoE layer sends, computes and returns latent rows (width D)
@@ -1692,14 +1771,14 @@ int k3xb_ep_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* local, uint32
     if (!local->latent) {
         if (shared) K3XB_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
         if ((st = ep_moe_forward(ctx, *local, E, hidden, T, ids, contrib, shared ? shared_out : nullptr, region,
-                                 out)))
+                                 out, false)))
             return st;
     } else {   // official_moe.cpp:296, then the experts on latent rows, then :322-336
         {
             PhaseScope ph(ctx, K3XB_PHASE_LATENT);
             if ((st = launch_linear_bf16(ctx, hidden, local->routed_down, T, D, H, 1, xt, lat))) return st;
         }
-        if ((st = ep_moe_forward(ctx, LE, E, lat, T, ids, contrib, nullptr, region, mixed))) return st;
+        if ((st = ep_moe_forward(ctx, LE, E, lat, T, ids, contrib, nullptr, region, mixed, true))) return st;
         PhaseScope ph(ctx, K3XB_PHASE_LATENT);
         if ((st = launch_rms_norm(ctx, mixed, local->routed_norm, T, D, local->latent_eps, normed))) return st;
         if ((st = launch_linear_bf16(ctx, normed, local->routed_up, T, H, D, 1, xt, routed))) return st;

@@ -31,6 +31,7 @@
 //                  scatters each row to its (token, slot) for the ordered
 //                  combine (c)
 #include "common.cuh"
+#include "ep_sync.cuh"
 #include "kernels.cuh"
 #include "profile.cuh"
 #include "tc_pipeline.cuh"
@@ -135,7 +136,10 @@ __global__ void __launch_bounds__(1024) worklist_kernel(const uint32_t* group_co
 // One warp per (row, 32-element block), lane = element: the block maximum
 // is a warp max (exact), each lane codes and subtracts its own element, and
 // groups of 8 lanes OR their nibbles into one 32-bit word.
-__global__ void __launch_bounds__(256) split_tokens_kernel(const float* __restrict__ hidden, uint32_t T,
+// Rows are floats, or bf16 words when hidden16 is given (the expert-parallel
+// receive window).
+__global__ void __launch_bounds__(256) split_tokens_kernel(const float* __restrict__ hidden,
+                                                           const uint16_t* __restrict__ hidden16, uint32_t T,
                                                            uint32_t H, uint32_t terms,
                                                            uint8_t* __restrict__ tsplit,
                                                            uint8_t* __restrict__ tsf) {
@@ -143,7 +147,8 @@ __global__ void __launch_bounds__(256) split_tokens_kernel(const float* __restri
     const size_t w = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
     if (w >= static_cast<size_t>(T) * kbc) return;
     const uint32_t t = static_cast<uint32_t>(w / kbc), kb = static_cast<uint32_t>(w % kbc);
-    float r = hidden[static_cast<size_t>(t) * H + kb * 32 + lane];
+    const size_t at = static_cast<size_t>(t) * H + kb * 32 + lane;
+    float r = hidden16 ? decode_bf16(hidden16[at]) : hidden[at];
     for (uint32_t term = 0; term < terms; ++term) {
         const float amax = warp_max(fabsf(r));
         const int s = amax > 0.0f ? e2m1_block_exponent(amax) : 0;
@@ -228,6 +233,7 @@ struct DParams {
     int* error;
     uint32_t rowblocks;       // 128-row blocks of the stacked down weights (E * H / 128)
     uint16_t* slot_out16;     // when set: bf16 words instead of slot_out floats
+    EpTarget ep;              // when ep.world: rows go straight to their home ranks' windows
 };
 
 // TMEM columns. Routed gate/up: gate accumulator at 0, up at RoutedCfg::kColUp,
@@ -322,10 +328,16 @@ __global__ void __launch_bounds__(kThreads, 1) down_kernel(const __grid_constant
         const uint32_t used = ntok * terms;
         const uint32_t lane_base = (32u * q) << 16;
         const uint32_t h0 = r0 + 32u * q + lane, h1 = h0 + kBlockM;
-        // destination rows of up to 32 tokens per round trip (lane j holds token j's)
+        // destination rows of up to 32 tokens per round trip (lane j holds token j's).
+        // Expert parallel: received row r is token r % home_rows of home rank
+        // r / home_rows, packed as rank << 24 | (token * top_k + slot)
         auto fetch_dst = [&](uint32_t j0) {
             const uint32_t a = tok0 + j0 + lane;
-            return j0 + lane < ntok ? __ldg(p.assign_token + a) * p.top_k + __ldg(p.assign_slot + a) : 0u;
+            if (j0 + lane >= ntok) return 0u;
+            const uint32_t row = __ldg(p.assign_token + a), slot = __ldg(p.assign_slot + a);
+            if (!p.ep.world) return row * p.top_k + slot;
+            const uint32_t g = row / p.ep.home_rows;
+            return g << 24 | ((row - g * p.ep.home_rows) * p.top_k + slot);
         };
         uint32_t dsts = fetch_dst(0);
         float y0 = 0.0f, y1 = 0.0f;
@@ -342,7 +354,18 @@ __global__ void __launch_bounds__(kThreads, 1) down_kernel(const __grid_constant
                 if (second) y1 = __fadd_rn(y1, v1[i]);
                 if (++tcount < terms) continue;
                 if (j % 32 == 0 && j) dsts = fetch_dst(j);
-                const size_t dst = __shfl_sync(0xffffffffu, dsts, j % 32);
+                const uint32_t packed = __shfl_sync(0xffffffffu, dsts, j % 32);
+                if (p.ep.world) {   // a store into the home rank's window (NVLink for a peer)
+                    uint16_t* y = reinterpret_cast<uint16_t*>(p.ep.win[packed >> 24] + p.ep.y_off) +
+                                  static_cast<size_t>(packed & 0xffffffu) * p.H;
+                    y[h0] = encode_bf16(y0);
+                    if (second) y[h1] = encode_bf16(y1);
+                    y0 = y1 = 0.0f;
+                    tcount = 0;
+                    ++j;
+                    continue;
+                }
+                const size_t dst = packed;
                 if (p.slot_out16) {
                     p.slot_out16[dst * p.H + h0] = encode_bf16(y0);
                     if (second) p.slot_out16[dst * p.H + h1] = encode_bf16(y1);
@@ -361,6 +384,9 @@ __global__ void __launch_bounds__(kThreads, 1) down_kernel(const __grid_constant
                           kColSfbGU, kBlockM, NM, p.rowblocks};
     tcp::run_pipeline<RC::kStagesGU, 2, false, RC::kAccbGU>(sm, &map_down, &map_down, &map_b, cfg, sfa, p.sfb,
                                                             p.error, get_desc, epilogue);
+    // Expert parallel: the last CTA to finish tells every home rank that this
+    // rank's outputs for the call have landed (every thread's stores first)
+    if (p.ep.world) ep_signal_grid_done(p.ep.done, p.ep.win, p.ep.flag_off, p.ep.rank, p.ep.world, p.ep.epoch);
 }
 
 // ---------------------------------------------------------------------------
@@ -630,7 +656,8 @@ size_t mxf4_scratch_bytes(const k3xb_moe_layer& L, uint32_t T) {
 void set_mxf4_scratch(k3xb_ctx* ctx, void* region) { ctx->mxf4_scratch = region; }
 
 int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T,
-                        const k3xb_plan& plan, float* slot_out, uint16_t* slot_out16) {
+                        const k3xb_plan& plan, float* slot_out, uint16_t* slot_out16, const EpTarget* ep,
+                        const uint16_t* hidden16) {
     const uint32_t H = L.hidden, I = L.inter;
     if (H % 128 || I % 128)
         return fail(ctx, K3XB_INVALID_EXTENT, "MXF4 engine needs hidden and inter multiples of 128");
@@ -665,8 +692,8 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
     K3XB_LAUNCHED(ctx);
     {
         const size_t n = static_cast<size_t>(T) * (H / 32);
-        split_tokens_kernel<<<static_cast<unsigned>((n * 32 + 255) / 256), 256, 0, ctx->stream>>>(hidden, T, H, l.terms,
-                                                                                          bf.tsplit, bf.tsf);
+        split_tokens_kernel<<<static_cast<unsigned>((n * 32 + 255) / 256), 256, 0, ctx->stream>>>(hidden, hidden16, T, H,
+                                                                                          l.terms, bf.tsplit, bf.tsf);
         K3XB_LAUNCHED(ctx);
     }
     gather_gu_kernel<<<l.max_tiles, 256, 0, ctx->stream>>>(bf.tsplit, bf.tsf, H, plan.assign_token, bf.tb, l.terms,
@@ -678,7 +705,7 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
                 L.activation, L.situ_beta, L.situ_linear_beta, ctx->status_word};
     DParams dp{bf.tb.desc_d, bf.tb.counts + 2, plan.assign_token, plan.assign_slot, sfa_down, bf.sfb_d, slot_out,
                H, I, l.terms, L.top_k, ctx->status_word, static_cast<uint32_t>(static_cast<size_t>(L.experts) * H / kBlockM),
-               slot_out16};
+               slot_out16, ep ? *ep : EpTarget{}};
     return l.nmax == 64 ? launch_routed<64>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, dp)
                         : launch_routed<128>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, dp);
 }

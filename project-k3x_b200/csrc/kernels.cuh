@@ -61,12 +61,28 @@ int launch_fill_normal_mxfp4(k3xb_ctx* ctx, uint8_t* packed, uint8_t* scales, si
 }  // namespace k3xb
 
 namespace k3xb {
+// Where an expert-parallel call's down projection puts its outputs: received
+// row r is token r % home_rows of home rank g = r / home_rows, and its
+// (token, slot) output row goes to win[g] + y_off, row token * top_k + slot,
+// as bf16 words. When every CTA is done, the last one stores `epoch` into
+// flag word `rank` at win[g] + flag_off of every rank g (ep.cu).
+struct EpTarget {
+    uint8_t* win[8];        // each rank's exchange window as mapped in this process
+    uint64_t y_off;         // byte offset of this call's output rows in every window
+    uint64_t flag_off;      // byte offset of the return flags in every window
+    uint32_t* done;         // this rank's grid-completion counter (device, zero between calls)
+    uint32_t home_rows;     // rows each home rank sent (its token count)
+    uint32_t rank, world, epoch;   // world 0: not expert parallel
+};
 // experts_tc.cu — tcgen05 block-scaled expert engine
 size_t mxf4_scratch_bytes(const k3xb_moe_layer& L, uint32_t T);
 void set_mxf4_scratch(k3xb_ctx* ctx, void* region);
-// slot_out [T*k][H] float, or bf16 words in slot_out16 when that is given
+// slot_out [T*k][H] float, or bf16 words in slot_out16 when that is given, or
+// (expert parallel) the home ranks' windows; rows are floats, or bf16 words
+// in hidden16 when that is given
 int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T,
-                        const k3xb_plan& plan, float* slot_out, uint16_t* slot_out16 = nullptr);
+                        const k3xb_plan& plan, float* slot_out, uint16_t* slot_out16 = nullptr,
+                        const EpTarget* ep = nullptr, const uint16_t* hidden16 = nullptr);
 void release_mxf4_resources(k3xb_ctx* ctx);
 int prepare_mxfp4_scales(k3xb_ctx* ctx, const uint8_t* scales, size_t rows, size_t cols, uint8_t* out);
 // 2-D byte tensor map (128B swizzle, box {128 B, box_rows}); map is a CUtensorMap*
@@ -110,11 +126,18 @@ int launch_conv_commit_linear(k3xb_ctx* ctx, const float* const proj[3], const u
 int launch_rms_norm(k3xb_ctx* ctx, const float* x, const uint16_t* w, uint32_t T, uint32_t H, float eps, float* out);
 int launch_embed(k3xb_ctx* ctx, const uint32_t* tokens, const uint16_t* table, uint32_t V, uint32_t T, uint32_t H,
                  float* out);
-// ep.cu — expert parallelism (NCCL all-to-all dispatch / combine)
+// ep.cu — expert parallelism (rows and expert outputs through peer-memory windows)
 void release_ep(k3xb_ctx* ctx);
 size_t ep_scratch_bytes(uint32_t G, uint32_t T, uint32_t K, uint32_t H, uint32_t E_r);
+// rows_bf16: the rows are bf16-valued, so they travel as bf16 words
 int ep_moe_forward(k3xb_ctx* ctx, const k3xb_moe_layer& local, uint32_t E, const float* hidden, uint32_t T,
-                   const uint32_t* ids, const float* contrib, const float* shared, void* region, float* out);
+                   const uint32_t* ids, const float* contrib, const float* shared, void* region, float* out,
+                   bool rows_bf16);
+// Sizes the exchange window for T tokens x K slots of width D before a
+// sequence of calls is queued (collective; growing drains the stream).
+int ep_reserve(k3xb_ctx* ctx, uint32_t T, uint32_t K, uint32_t D);
+// After a drain: a bounded device wait that gave up aborts the exchange.
+int ep_check_waits(k3xb_ctx* ctx);
 int ep_world(const k3xb_ctx* ctx);   // 0 when expert parallelism is not initialised
 // Waits for ctx->stream with the communicator's bound (ep_guard.hpp); OK at
 // once without expert parallelism.

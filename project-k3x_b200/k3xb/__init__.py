@@ -188,6 +188,7 @@ def library() -> C.CDLL:
             "k3xb_attention_residual_norm": [vp, vp, vp, vp, vp, vp, vp, u32, u32, f32, vp, vp],
             "k3xb_layer_forward": [vp, C.POINTER(Layer), vp, vp, vp, u32, u32, vp, vp, vp, vp, vp],
             "k3xb_verify_step": [vp, C.POINTER(VerifyModel), C.POINTER(VerifyIO)],
+            "k3xb_ep_verify_step": [vp, C.POINTER(VerifyModel), C.POINTER(VerifyIO), u32],
             "k3xb_draft_greedy": [vp, C.POINTER(VerifyModel), C.POINTER(DraftIO)],
             "k3xb_speculative_step": [vp, C.POINTER(VerifyModel), C.POINTER(SpeculativeIO)],
             "k3xb_ep_unique_id": [vp],
@@ -403,6 +404,13 @@ class Context:
 
     def verify_step(self, model: "VerifyModel", io: "VerifyIO"):
         self._check(self.lib.k3xb_verify_step(self.h, C.byref(model), C.byref(io)), "verify_step")
+
+    def ep_verify_step(self, model: "VerifyModel", io: "VerifyIO", experts_total: int):
+        """The verify step over this rank's sequences with every MoE layer
+        expert parallel (each layer descriptor holds this rank's expert slice,
+        ep_local_layer); needs ep_init first."""
+        self._check(self.lib.k3xb_ep_verify_step(self.h, C.byref(model), C.byref(io), experts_total),
+                    "ep_verify_step")
 
     def draft_greedy(self, model: "VerifyModel", anchors, conv, recurrent, draft_tokens, draft_top_k):
         """AURORA reduced-Top-K self-draft: draft_tokens [S][p] (device int32)

@@ -1,15 +1,22 @@
 """Expert-parallel MoE layer: the dispatch / local plan / return / combine
 algorithm of csrc/ep.cu, restated on the CPU with the oracle's expert math
-and run as 2 and 4 gloo ranks (experts split 4 and 2 per rank), for the plain MoE and for LatentMoE (latent rows
-are projected on the home rank, sent, computed and returned; the routed
-norm and up projection run at home). Its output must equal the
-single-process oracle layer bit for bit (the combine keeps the one-GPU slot
-order), which is the property the CUDA path is tested for on 2 GPUs in
-test_gpu_ep.py and with a world of one in test_gpu_latent.py.
+and run as 2 and 4 gloo ranks (experts split 4 and 2 per rank), for the
+plain MoE and for LatentMoE (latent rows are projected on the home rank,
+sent, computed and returned; the routed norm and up projection run at
+home). Its output must equal the single-process oracle layer bit for bit
+(the combine keeps the one-GPU slot order), which is the property the CUDA
+path is tested for on 2 GPUs in test_gpu_ep.py / test_gpu_ep_verify.py and
+with a world of one in test_gpu_latent.py.
 
-gloo has no all-to-all, so the exchange is an all_gather of the fixed-size
-per-destination buffers from which each rank takes its block: the same data
-movement as the ncclSend/ncclRecv group, just more of it.
+The CUDA path stores into the other ranks' windows over peer memory. Here
+each rank's stores are all-gathered (gloo has no one-sided puts) and every
+rank keeps those addressed to it:
+- dispatch: a token's metadata to every rank, its row (as bf16, exact for
+  the bf16-valued rows) only to the ranks that own one of its experts; the
+  rows a rank does not receive are NaN here, so a plan that read one would
+  poison the output;
+- return: each (token, slot) output row is stored by exactly one rank, the
+  owner of the slot's expert, into the home rank's output region.
 """
 import os
 
@@ -71,31 +78,41 @@ def _ep_rank(rank, world, port, out_dir, latent):
     con = np.empty((T, K), np.float32)
     for t in range(T):
         ids[t], con[t] = rs.route(x_in[t], L["router"], L["correction"], K)
-    # dispatch: every row to every rank, (local expert << 8 | slot) metadata
+    # dispatch: metadata (local expert << 8 | slot, or none) to every rank;
+    # the row only where one of its slots' experts lives, as bf16 words
     meta = np.full((world, T, K), NO_ENTRY, np.uint32)
     for g in range(world):
         for t in range(T):
             for j in range(K):
                 if ids[t, j] // E_r == g:
                     meta[g, t, j] = (int(ids[t, j]) - g * E_r) << 8 | j
-    send_x = np.broadcast_to(x, (world, T, D))
+    assert np.array_equal(rs.round_bf16(x), x)   # bf16-valued rows travel as bf16 exactly
+    send_x = np.full((world, T, D), np.nan, np.float32)
+    for g in range(world):
+        for t in range(T):
+            if (meta[g, t] != NO_ENTRY).any():
+                send_x[g, t] = x[t]
     recv_meta = _exchange(meta, world)
     recv_x = _exchange(send_x, world)
     # local expert-major plan: ascending local expert, (row, slot) order
     rows = recv_x.reshape(world * T, D)
     m = recv_meta.reshape(world * T, K)
-    y = np.zeros((world * T, K, D), np.float32)
+    put = np.full((world, T, K, D), np.nan, np.float32)   # stores addressed to each home rank
     for e in range(E_r):
         for r in range(world * T):
             for j in range(K):
                 if m[r, j] != NO_ENTRY and (m[r, j] >> 8) == e:
-                    y[r, m[r, j] & 0xFF] = _expert(rs, L, rank * E_r + e, rows[r])
-    y_home = _exchange(y.reshape(world, T, K, D), world)
+                    home, t = divmod(r, T)
+                    put[home, t, m[r, j] & 0xFF] = _expert(rs, L, rank * E_r + e, rows[r])
+    landed = _exchange(put, world)   # landed[g]: what rank g stored into this rank's region
+    written = ~np.isnan(landed).all(axis=3)
+    assert (written.sum(axis=0) == 1).all(), "every (token, slot) row is stored by exactly one rank"
+    y_home = np.nansum(np.where(written[..., None], landed, 0.0), axis=0).astype(np.float32)
     # combine in slot order with each slot's owner (then, for LatentMoE, the
     # routed norm and up projection, :323-331), then + shared
     out = np.empty((T, H), np.float32)
     for t in range(T):
-        ys = np.stack([y_home[ids[t, j] // E_r, t, j] for j in range(K)])
+        ys = np.stack([y_home[t, j] for j in range(K)])
         mixed = rs.routed_combine(ys, con[t])
         if latent:
             mixed = rs.bf16_matvec(rs.rms_norm(mixed, L["routed_norm"], L["latent_eps"]), L["routed_up"])
