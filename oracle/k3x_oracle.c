@@ -1067,3 +1067,115 @@ int k3xo_verify_rejection(const float* target_logits,
     free(sq);
     return K3XO_OK;
 }
+
+/* ------------------------------------------------------------------------ */
+/* seeded synthetic workloads: the library's generator (csrc/synth.cu)       */
+/* ------------------------------------------------------------------------ */
+
+static uint64_t mix64(uint64_t z)
+{
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+/* ln(k * 2^-24), k in [1, 2^24]: k = m * 2^e, m in [sqrt(1/2), sqrt(2)),
+ * ln m = 2 atanh((m - 1) / (m + 1)) by its series to s^11. */
+static float synth_log(uint32_t k)
+{
+    int e = 31;
+    while (!(k >> e)) --e;
+    const uint32_t mant = e <= 23 ? k << (23 - e) : k >> (e - 23);
+    float m = u2f((mant & 0x7fffffu) | 0x3f800000u);
+    if (m > 0x1.6a09e6p+0f) {
+        m = m * 0.5f;
+        ++e;
+    }
+    const float s = (m + -1.0f) / (m + 1.0f);
+    const float s2 = s * s;
+    float p = 0x1.745d18p-4f;
+    p = p * s2 + 0x1.c71c72p-4f;
+    p = p * s2 + 0x1.24924ap-3f;
+    p = p * s2 + 0x1.99999ap-3f;
+    p = p * s2 + 0x1.555556p-2f;
+    p = p * s2 + 1.0f;
+    const float lnm = (2.0f * s) * p;
+    return (float)(e - 24) * 0x1.62e430p-1f + lnm;
+}
+
+/* cos and sin of 2*pi*k*2^-24, k in [0, 2^24): quadrant from the top two
+ * bits, Taylor series to x^14 / x^15 on [0, pi/2). */
+static void synth_cos_sin(uint32_t k, float* c_out, float* s_out)
+{
+    const uint32_t q = k >> 22;
+    const float f = (float)(k & 0x3fffffu) * 0x1.0p-24f;
+    const float x = f * 0x1.921fb6p+2f, x2 = x * x;
+    float c = -0x1.93974cp-37f, sn = -0x1.ae7f3ep-41f;
+    c = c * x2 + 0x1.1eed8ep-29f;
+    c = c * x2 + -0x1.27e4fcp-22f;
+    c = c * x2 + 0x1.a01a02p-16f;
+    c = c * x2 + -0x1.6c16c2p-10f;
+    c = c * x2 + 0x1.555556p-5f;
+    c = c * x2 + -0.5f;
+    c = c * x2 + 1.0f;
+    sn = sn * x2 + 0x1.612462p-33f;
+    sn = sn * x2 + -0x1.ae6456p-26f;
+    sn = sn * x2 + 0x1.71de3ap-19f;
+    sn = sn * x2 + -0x1.a01a02p-13f;
+    sn = sn * x2 + 0x1.111112p-7f;
+    sn = sn * x2 + -0x1.555556p-3f;
+    sn = (sn * x2) * x + x;
+    switch (q) {
+    case 0: *c_out = c; *s_out = sn; break;
+    case 1: *c_out = -sn; *s_out = c; break;
+    case 2: *c_out = -c; *s_out = -sn; break;
+    default: *c_out = sn; *s_out = -c; break;
+    }
+}
+
+void k3xo_normal_pair(uint64_t seed, uint64_t stream, uint64_t pair, float* z0, float* z1)
+{
+    const uint64_t r = mix64(mix64(mix64(seed) ^ stream) ^ pair);
+    const uint32_t k1 = (uint32_t)(r >> 40) + 1u;
+    const uint32_t k2 = (uint32_t)((r >> 16) & 0xffffffu);
+    const float rad = sqrtf(-2.0f * synth_log(k1));
+    float c, s;
+    synth_cos_sin(k2, &c, &s);
+    *z0 = rad * c;
+    *z1 = rad * s;
+}
+
+static float synth_normal(uint64_t seed, uint64_t stream, uint64_t element)
+{
+    float z0, z1;
+    k3xo_normal_pair(seed, stream, element >> 1, &z0, &z1);
+    return (element & 1u) ? z1 : z0;
+}
+
+void k3xo_fill_normal_f32(float* out, size_t n, uint64_t first, uint64_t seed, uint64_t stream,
+                          float mean, float sigma)
+{
+    for (size_t j = 0; j < n; ++j) out[j] = mean + sigma * synth_normal(seed, stream, first + j);
+}
+
+void k3xo_fill_normal_bf16(uint16_t* out, size_t n, uint64_t first, uint64_t seed, uint64_t stream,
+                           float sigma)
+{
+    for (size_t j = 0; j < n; ++j) out[j] = k3xo_encode_bf16(sigma * synth_normal(seed, stream, first + j));
+}
+
+void k3xo_fill_normal_mxfp4(uint8_t* packed, uint8_t* scales, size_t blocks, uint64_t first,
+                            uint64_t seed, uint64_t stream, float sigma)
+{
+    float v[32];
+    for (size_t b = 0; b < blocks; ++b) {
+        for (int i = 0; i < 16; ++i) {
+            float z0, z1;
+            k3xo_normal_pair(seed, stream, (first + b) * 16 + (uint64_t)i, &z0, &z1);
+            v[2 * i] = sigma * z0;
+            v[2 * i + 1] = sigma * z1;
+        }
+        k3xo_quantize_mxfp4(v, 1, 32, packed + b * 16, scales + b);
+    }
+}

@@ -231,6 +231,27 @@ int k3xo_verify_rejection(const float* target_logits,
                           uint64_t seed, uint64_t sequence, size_t* accepted,
                           uint32_t* committed, size_t* committed_count);
 
+/* ---- seeded synthetic workloads (restates the library's generator) ------ */
+/* The library's counter-based generator (project-k3x_b200/csrc/synth.cu):
+ * pair i of (seed, stream) = SplitMix64 -> two 24-bit uniforms -> Box-Muller
+ * with its own float series for log and sine/cosine, every operation
+ * rounded to nearest, so the same bits come out here. Not a reference
+ * function: it lets a CPU rebuild any slice of a workload that the GPU
+ * generates in place (bench.py's reference arm). */
+void k3xo_normal_pair(uint64_t seed, uint64_t stream, uint64_t pair, float* z0, float* z1);
+/* out[j] = mean + sigma * z for global element first + j (element e uses
+ * component e & 1 of pair e >> 1), as k3xb_fill_normal_f32. */
+void k3xo_fill_normal_f32(float* out, size_t n, uint64_t first, uint64_t seed, uint64_t stream,
+                          float mean, float sigma);
+/* bf16 words of sigma * z, as k3xb_fill_normal_bf16. */
+void k3xo_fill_normal_bf16(uint16_t* out, size_t n, uint64_t first, uint64_t seed, uint64_t stream,
+                           float sigma);
+/* MXFP4 32-blocks first .. first + blocks - 1 of sigma * z (block b holds
+ * pairs 16b .. 16b + 15), quantised as k3xo_quantize_mxfp4, as
+ * k3xb_fill_normal_mxfp4: packed [blocks][16] bytes, scales [blocks]. */
+void k3xo_fill_normal_mxfp4(uint8_t* packed, uint8_t* scales, size_t blocks, uint64_t first,
+                            uint64_t seed, uint64_t stream, float sigma);
+
 #ifdef __cplusplus
 }
 #endif

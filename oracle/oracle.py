@@ -172,6 +172,32 @@ class Restatement:
         L.k3xo_uniform.argtypes = [C.c_uint64] * 4
         L.k3xo_verify_rejection.argtypes = [_f32p, _f32p, _u32p, _sz, _sz, C.c_float,
                                             C.c_uint64, C.c_uint64, _szp, _u32p, _szp]
+        u64 = C.c_uint64
+        L.k3xo_fill_normal_f32.argtypes = [_f32p, _sz, u64, u64, u64, C.c_float, C.c_float]
+        L.k3xo_fill_normal_f32.restype = None
+        L.k3xo_fill_normal_bf16.argtypes = [_u16p, _sz, u64, u64, u64, C.c_float]
+        L.k3xo_fill_normal_bf16.restype = None
+        L.k3xo_fill_normal_mxfp4.argtypes = [_u8p, _u8p, _sz, u64, u64, u64, C.c_float]
+        L.k3xo_fill_normal_mxfp4.restype = None
+
+    # -- the library's seeded generator (csrc/synth.cu), any slice ---------------
+    def fill_normal_f32(self, n, seed, stream, first=0, mean=0.0, sigma=1.0):
+        out = np.empty(n, np.float32)
+        self.lib.k3xo_fill_normal_f32(out, n, first, seed, stream, mean, sigma)
+        return out
+
+    def fill_normal_bf16(self, n, seed, stream, first=0, sigma=1.0):
+        """bf16 words."""
+        out = np.empty(n, np.uint16)
+        self.lib.k3xo_fill_normal_bf16(out, n, first, seed, stream, sigma)
+        return out
+
+    def fill_normal_mxfp4(self, blocks, seed, stream, first=0, sigma=0.02):
+        """(packed [blocks*16] bytes, scales [blocks]) of 32-blocks first..first+blocks-1."""
+        packed = np.empty(blocks * 16, np.uint8)
+        scales = np.empty(blocks, np.uint8)
+        self.lib.k3xo_fill_normal_mxfp4(packed, scales, blocks, first, seed, stream, sigma)
+        return packed, scales
 
     # -- helpers ---------------------------------------------------------------
     @staticmethod
@@ -528,6 +554,8 @@ class Reference:
         L.k3xr_resident_moe_layer.argtypes = [_sz] * 4 + [_f32p] * 6 + [_u8p] * 6 + [_sz, _f32p, C.c_float, C.c_float,
                                                                                   C.c_float, _f32p, _f32p]
         L.k3xr_dense_situ_mlp.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _f32p, C.c_float, C.c_float, _f32p]
+        L.k3xr_plain_layer.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, _sz, _sz, _f32p, _f32p,
+                                       _u16p, _f32p, _f32p, _u32p, C.c_int, C.c_int]
         L.k3xr_official_layer.argtypes = [C.c_void_p, C.c_void_p, _u16p, _u16p, _u16p, _u16p, _u16p, _u16p,
                                           C.c_float, _f32p, _f32p, _sz, _u16p, _u16p, _u16p, _f32p, _f32p, _u32p]
 
@@ -720,6 +748,31 @@ class Reference:
         if st:
             raise OracleError(st, "ref official_layer_cpu")
         return out, ids, (cq, ck, cv, rec)
+
+    def plain_layer(self, layer: dict, hidden_in, block, conv, recurrent, route_only=False, threads=1):
+        """One KDA + plain-MoE layer through the reference's own functions
+        (ref_shim.cpp:k3xr_plain_layer) for S sequences of T positions:
+        hidden_in, block [S][T][H]; conv [S][3][(w-1)*P] bf16 words,
+        recurrent [S][h][d][d] (copied, not changed). Returns (out [S][T][H],
+        ids [S][T][k], conv after, recurrent after)."""
+        ks, keep_k = kda_struct(layer["kda"])
+        ms, keep_m = moe_struct(layer["moe"])
+        hidden_in, block = _c(hidden_in, np.float32), _c(block, np.float32)
+        S, T, H = hidden_in.shape
+        conv = np.array(conv, np.uint16, copy=True)
+        rec = np.array(recurrent, np.float32, copy=True)
+        out = np.zeros((S, T, H), np.float32)
+        ids = np.zeros((S, T, layer["moe"]["top_k"]), np.uint32)
+        names = ("self_residual_norm", "self_residual_proj", "input_norm", "moe_residual_norm", "moe_residual_proj",
+                 "post_norm")
+        arrays = [_c(layer[k], np.uint16) for k in names]
+        norms = (C.c_void_p * 6)(*[a.ctypes.data for a in arrays])
+        st = self.lib.k3xr_plain_layer(C.byref(ks), C.byref(ms), norms, layer["rms_eps"], S, T, hidden_in, block,
+                                       conv, rec, out, ids, 1 if route_only else 0, threads)
+        del keep_k, keep_m, arrays
+        if st:
+            raise OracleError(st, "ref plain layer")
+        return out, ids, conv, rec
 
     def official_two_layer(self, layers, hidden_in, block, convs, recs):
         """official_two_layer_cpu over its two positions: (out [2][H], final

@@ -272,6 +272,44 @@ static int bf16_matvec(const float* x, const std::uint16_t* w, std::size_t rows,
     return 0;
 }
 
+// Scratch of one plain-MoE position.
+struct MoeBufs {
+    std::vector<float> y, mixed, shared, g, u, a;
+    explicit MoeBufs(const k3xr_moe_layer& L)
+        : y(L.top_k * L.hidden), mixed(L.hidden), shared(L.hidden), g(L.shared_inter), u(L.shared_inter),
+          a(L.shared_inter) {}
+};
+
+// One position of the plain (hidden-space) MoE: the reference's routing,
+// expert primitives and slot-ordered combine rule (official_moe.cpp:271-344
+// without the latent projections); out = round_bf16(round_bf16(mix) + shared).
+// With route_only the experts are not run.
+static int plain_moe_position(const k3xr_moe_layer& L, const float* x, std::uint32_t* ids, float* con,
+                              bool route_only, float* out, MoeBufs& b) {
+    const std::size_t H = L.hidden, K = L.top_k;
+    int st = k3xr_route_official_moe(x, L.router, L.experts, H, L.correction, K, ids, con, nullptr);
+    if (st || route_only) return st;
+    for (std::size_t s = 0; s < K && !st; ++s) st = expert_ffn(L, ids[s], x, b.y.data() + s * H);
+    if (st) return st;
+    std::fill(b.mixed.begin(), b.mixed.end(), 0.0F);
+    for (std::size_t s = 0; s < K; ++s)
+        for (std::size_t i = 0; i < H; ++i) b.mixed[i] += con[s] * b.y[s * H + i];
+    for (auto& v : b.mixed) v = round_bf16(v);
+    if (L.shared_gate) {
+        bf16_matvec(x, L.shared_gate, L.shared_inter, H, b.g.data());
+        bf16_matvec(x, L.shared_up, L.shared_inter, H, b.u.data());
+        if (L.activation == 1)
+            k3x::situ_glu(b.a, b.g, b.u, L.situ_beta, linear(L.situ_linear_beta));
+        else
+            k3x::situ_glu(b.a, b.g, b.u, 0x1p64F, std::nullopt);
+        bf16_matvec(b.a.data(), L.shared_down, H, L.shared_inter, b.shared.data());
+    } else {
+        std::fill(b.shared.begin(), b.shared.end(), 0.0F);
+    }
+    for (std::size_t i = 0; i < H; ++i) out[i] = round_bf16(b.mixed[i] + b.shared[i]);
+    return 0;
+}
+
 // Plain (hidden-space) MoE layer composed of the reference's routing,
 // expert primitives and its slot-ordered combine rule
 // (official_moe.cpp:271-344 without the latent projections). Tokens
@@ -285,34 +323,13 @@ int k3xr_moe_layer_forward(const k3xr_moe_layer* layer, const float* hidden,
     std::atomic<std::size_t> next{token_begin};
     std::atomic<int> status{0};
     auto worker = [&]() {
-        std::vector<float> y(K * H), mixed(H), shared(L.hidden);
-        std::vector<float> g(L.shared_inter), u(L.shared_inter), a(L.shared_inter);
+        MoeBufs b(L);
         for (;;) {
             std::size_t t = next.fetch_add(1);
             if (t >= token_end || status.load()) break;
-            const float* x = hidden + t * H;
-            int st = k3xr_route_official_moe(x, L.router, L.experts, H, L.correction, K,
-                                             ids + t * K, contributions + t * K, nullptr);
-            for (std::size_t s = 0; s < K && !st; ++s)
-                st = expert_ffn(L, ids[t * K + s], x, y.data() + s * H);
+            const int st = plain_moe_position(L, hidden + t * H, ids + t * K, contributions + t * K, false,
+                                              out + t * H, b);
             if (st) { status.store(st); break; }
-            std::fill(mixed.begin(), mixed.end(), 0.0F);
-            for (std::size_t s = 0; s < K; ++s)
-                for (std::size_t i = 0; i < H; ++i)
-                    mixed[i] += contributions[t * K + s] * y[s * H + i];
-            for (auto& v : mixed) v = round_bf16(v);
-            if (L.shared_gate) {
-                bf16_matvec(x, L.shared_gate, L.shared_inter, H, g.data());
-                bf16_matvec(x, L.shared_up, L.shared_inter, H, u.data());
-                if (L.activation == 1)
-                    k3x::situ_glu(a, g, u, L.situ_beta, linear(L.situ_linear_beta));
-                else
-                    k3x::situ_glu(a, g, u, 0x1p64F, std::nullopt);
-                bf16_matvec(a.data(), L.shared_down, H, L.shared_inter, shared.data());
-            } else {
-                std::fill(shared.begin(), shared.end(), 0.0F);
-            }
-            for (std::size_t i = 0; i < H; ++i) out[t * H + i] = round_bf16(mixed[i] + shared[i]);
         }
     };
     if (threads < 1) threads = 1;
@@ -432,6 +449,71 @@ int k3xr_official_kda_cpu(const k3xr_kda_weights* w, const float* hidden,
     std::copy(s.recurrent_v_first.begin(), s.recurrent_v_first.end(), recurrent);
     std::copy(r.value().output.begin(), r.value().output.end(), out);
     return 0;
+}
+
+// One KDA + plain-MoE layer for S independent sequences of T positions,
+// through the reference's own functions in official_layer_cpu's order
+// (official_layer.cpp:134-244, with the plain hidden-space MoE of the
+// BASELINE configs in place of official_moe_cpu's LatentMoE): per position
+// prepare_official_moe_input (attention residual + input norm), then
+// official_kda_cpu over the sequence's positions, then per position the
+// prefix round_bf16(round_bf16(hidden) + kda), the MoE input (the same
+// preparation with the MoE norms), route_official_moe, the experts through
+// mxfp4_matmul / situ_glu, the slot-ordered combine and the shared expert,
+// and out = round_bf16(round_bf16(prefix) + combined). norms: self_residual_
+// norm, self_residual_proj, input_norm, moe_residual_norm, moe_residual_proj,
+// post_norm ([H] bf16 words each). Arrays are per sequence: hidden_in, block,
+// out [S][T][H]; conv [S][3][(W-1)*P] and recurrent [S][h][d][d] hold the
+// initial states and receive the final ones; ids [S][T][k]. Sequences are
+// shared out over `threads` workers. With route_only the routed experts and
+// the rest of the MoE are skipped (ids are still the route): the caller can
+// then build only the experts a sample needs before it runs the layer.
+int k3xr_plain_layer(const k3xr_kda_weights* kw, const k3xr_moe_layer* mw, const std::uint16_t* const norms[6],
+                     float rms_eps, std::size_t S, std::size_t T, const float* hidden_in, const float* block,
+                     std::uint16_t* conv, float* recurrent, float* out, std::uint32_t* ids, int route_only,
+                     int threads) {
+    const std::size_t H = kw->hidden, h = kw->heads, d = kw->head_dim, P = h * d, W = kw->conv_width;
+    const std::size_t K = mw->top_k, hist = (W - 1) * P;
+    if (mw->latent || mw->hidden != H) return static_cast<int>(ErrorCode::invalid_state);
+    std::atomic<std::size_t> next{0};
+    std::atomic<int> status{0};
+    auto worker = [&]() {
+        MoeBufs b(*mw);
+        std::vector<float> xin(T * H), kda(T * H), prefix(H), moe_in(H), con(K), combined(H);
+        for (;;) {
+            const std::size_t sq = next.fetch_add(1);
+            if (sq >= S || status.load()) break;
+            const float* hin = hidden_in + sq * T * H;
+            const float* blk = block + sq * T * H;
+            int st = 0;
+            for (std::size_t t = 0; t < T && !st; ++t)
+                st = k3xr_prepare_moe_input(hin + t * H, blk + t * H, norms[0], norms[1], norms[2], H, rms_eps,
+                                            xin.data() + t * H);
+            std::uint16_t* cv = conv + sq * 3 * hist;
+            if (!st)
+                st = k3xr_official_kda_cpu(kw, xin.data(), T, cv, cv + hist, cv + 2 * hist,
+                                           recurrent + sq * h * d * d, kda.data());
+            for (std::size_t t = 0; t < T && !st; ++t) {
+                for (std::size_t i = 0; i < H; ++i)
+                    prefix[i] = round_bf16(round_bf16(hin[t * H + i]) + kda[t * H + i]);
+                st = k3xr_prepare_moe_input(prefix.data(), blk + t * H, norms[3], norms[4], norms[5], H, rms_eps,
+                                            moe_in.data());
+                if (!st)
+                    st = plain_moe_position(*mw, moe_in.data(), ids + (sq * T + t) * K, con.data(), route_only != 0,
+                                            combined.data(), b);
+                if (!st && !route_only)
+                    for (std::size_t i = 0; i < H; ++i)
+                        out[(sq * T + t) * H + i] = round_bf16(round_bf16(prefix[i]) + combined[i]);
+            }
+            if (st) { status.store(st); break; }
+        }
+    };
+    if (threads < 1) threads = 1;
+    std::vector<std::thread> pool;
+    for (int i = 1; i < threads; ++i) pool.emplace_back(worker);
+    worker();
+    for (auto& th : pool) th.join();
+    return status.load();
 }
 
 // official_layer_cpu itself (official_layer.cpp:134-244: attention

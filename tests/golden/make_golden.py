@@ -169,11 +169,8 @@ def kda_kat(ref):
 
 
 def _torch_kda(w, hidden):
-    ref_root = os.environ.get("K3X_REFERENCE")
-    if not ref_root:
-        import re
-        m = re.search(r"^REF \?= (\S+)", open(os.path.join(ROOT, "oracle", "Makefile")).read(), re.M)
-        ref_root = m.group(1) if m else ""
+    # the reference tree: K3X_REFERENCE, else a checkout beside this repository (oracle/Makefile's rule)
+    ref_root = os.environ.get("K3X_REFERENCE") or os.path.abspath(os.path.join(ROOT, "..", "reference"))
     pkg = os.path.join(ref_root, "reference")
     if not os.path.isdir(os.path.join(pkg, "k3x_ref")):
         return None

@@ -6,10 +6,10 @@ behaviour (method split, argument checks, statuses, no retry on the other
 backend) runs here; its device calls are the C ABI entry points the GPU
 tests cover (test_gpu_host_io.py, test_gpu_resident.py).
 
-The reference tree is found through K3X_REFERENCE or the REF default of
-oracle/Makefile; without it the test skips."""
+The reference tree is K3X_REFERENCE when set, else a checkout named
+`reference` beside this repository (as in oracle/Makefile); without it the
+test skips."""
 import os
-import re
 import shutil
 import subprocess
 
@@ -20,12 +20,12 @@ LIBDIR = os.path.join(ROOT, "project-k3x_b200", "k3xb")
 ADAPTER = os.path.join(ROOT, "project-k3x_b200", "adapter")
 
 
+def reference_root():
+    return os.environ.get("K3X_REFERENCE") or os.path.abspath(os.path.join(ROOT, "..", "reference"))
+
+
 def reference_include():
-    ref = os.environ.get("K3X_REFERENCE")
-    if not ref:
-        m = re.search(r"^REF \?= (\S+)", open(os.path.join(ROOT, "oracle", "Makefile")).read(), re.M)
-        ref = m.group(1) if m else ""
-    inc = os.path.join(ref, "runtime", "include")
+    inc = os.path.join(reference_root(), "runtime", "include")
     return inc if os.path.exists(os.path.join(inc, "k3x", "backend.hpp")) else None
 
 

@@ -577,3 +577,35 @@ def test_resident_moe_layer_matches_reference_cpu_backend(rs, ref):
         w, ex, con, x = make_resident_moe_case(rs, seed)
         np.testing.assert_array_equal(rs.resident_moe_layer(w, ex, con, x, 1e-6, 4.0, lin),
                                       ref.resident_moe_layer(w, ex, con, x, 1e-6, 4.0, lin))
+
+
+def test_plain_layer_matches_reference(rs, ref):
+    """The KDA + plain-MoE layer that bench.py's reference arm times
+    (ref_shim.cpp:k3xr_plain_layer: the reference's prepare_official_moe_input,
+    official_kda_cpu, route_official_moe and expert primitives in
+    official_layer_cpu's order) equals the restatement's layer composition
+    bit for bit for several sequences on several threads, outputs, routes and
+    final KDA states; route_only gives the same routes."""
+    from oracle import bf16_normal, bf16_words, make_layer
+    g = np.random.default_rng(67)
+    H, h, d, T, W, S = 256, 2, 64, 3, 4, 3
+    P = h * d
+    layer = make_layer(rs, 68, H, h, d, 16, 4, 128, 128)
+    layer["kda"]["eps"] = layer["rms_eps"]
+    hidden, block = bf16_normal(g, (S, T, H)), bf16_normal(g, (S, T, H))
+    conv = np.stack([np.stack([bf16_words(g.normal(0, 0.5, size=(W - 1) * P)) for _ in range(3)])
+                     for _ in range(S)])
+    rec = g.normal(0, 0.05, size=(S, h, d, d)).astype(np.float32)
+    out, ids, conv_after, rec_after = ref.plain_layer(layer, hidden, block, conv, rec, threads=2)
+    _, route_ids, _, _ = ref.plain_layer(layer, hidden, block, conv, rec, route_only=True, threads=3)
+    np.testing.assert_array_equal(route_ids, ids)
+    parent = np.arange(-1, T - 1)
+    for s in range(S):
+        c = tuple(conv[s])
+        want, want_ids, _, xin = rs.layer_forward(layer, hidden[s], block[s], parent, c, rec[s].reshape(-1),
+                                                  want_xin=True)
+        np.testing.assert_array_equal(out[s], want)
+        np.testing.assert_array_equal(ids[s], want_ids)
+        cq, ck, cv, r = rs.kda_block_commit(layer["kda"], xin, parent, T - 1, c, rec[s].reshape(-1))
+        np.testing.assert_array_equal(conv_after[s], np.stack([cq, ck, cv]))
+        np.testing.assert_array_equal(rec_after[s].reshape(-1), r)
