@@ -21,8 +21,13 @@
 //    streams, or different host threads) race on it and must be
 //    serialised by the caller.
 //  * The first call on each device looks the array's device address up
-//    once (cudaGetSymbolAddress, with that device current). Make that first
-//    call before any stream capture begins.
+//    once (cudaGetSymbolAddress, with that device current) and keeps it with
+//    a small host-side launch record. Make that first call before any stream
+//    capture begins.
+//  * Device-side failures (a non-finite input, a bounded wait in the logits
+//    kernel that ran out) are written to the caller's `status` word. With
+//    status NULL they go to a word inside the array that nothing reads: the
+//    call still returns K3XB_OK and ids/contributions are then undefined.
 #include <mutex>
 
 #include "common.cuh"
@@ -38,21 +43,38 @@ constexpr size_t kStaticBytes = kStatusOffset + 256;
 // Logits [tokens][experts] followed by a device status word.
 static __device__ __align__(256) unsigned char g_route_scratch[kStaticBytes];
 
-std::mutex g_setup_lock;
+// Per device: the array's device address and a launch context that carries
+// the stream and status word for the shared launchers. Both are made by the
+// first call on the device and kept until exit, so later calls do no
+// host-side set-up (the launch context also keeps the tensor-map encoder it
+// resolved). The context owns no device memory.
+struct Site {
+    void* base = nullptr;
+    k3xb_ctx launch;
+};
+std::mutex g_lock;   // held for the host side of each call (set-up and launches)
 constexpr int kMaxDevices = 128;
-void* g_scratch_addr[kMaxDevices] = {};
+Site* g_site[kMaxDevices] = {};
 
-// The array's name is only a host-side handle; the kernels need its device
-// address, resolved once per device with that device current.
-int scratch_address(int device, void** out) {
+// With g_lock held: the site of `device`, made with that device current.
+int site_of(int device, Site** out) {
     if (device < 0 || device >= kMaxDevices) return K3XB_INVALID_EXTENT;
-    std::lock_guard<std::mutex> guard(g_setup_lock);
-    if (!g_scratch_addr[device]) {
+    if (!g_site[device]) {
+        // the array's name is only a host-side handle; kernels need its
+        // device address, resolved once per device with that device current
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_route_scratch) != cudaSuccess || !p) return K3XB_BACKEND_UNAVAILABLE;
-        g_scratch_addr[device] = p;
+        Site* s = new (std::nothrow) Site();
+        if (!s) return K3XB_BACKEND_UNAVAILABLE;
+        s->base = p;
+        s->launch.device = device;
+        if (cudaDeviceGetAttribute(&s->launch.sm_count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+            delete s;
+            return K3XB_BACKEND_UNAVAILABLE;
+        }
+        g_site[device] = s;
     }
-    *out = g_scratch_addr[device];
+    *out = g_site[device];
     return K3XB_OK;
 }
 
@@ -70,22 +92,18 @@ extern "C" int k3xb_route_static(const float* hidden, uint32_t tokens, uint32_t 
     if (static_cast<size_t>(tokens) * experts > kStaticLogits) return K3XB_INVALID_EXTENT;
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess) return K3XB_BACKEND_UNAVAILABLE;
-    void* base = nullptr;
-    int st = scratch_address(device, &base);
+    std::lock_guard<std::mutex> guard(g_lock);
+    Site* site = nullptr;
+    int st = site_of(device, &site);
     if (st) return st;
-    float* logits = static_cast<float*>(base);
-    int32_t* word = status ? status : reinterpret_cast<int32_t*>(static_cast<unsigned char*>(base) + kStatusOffset);
+    float* logits = static_cast<float*>(site->base);
+    int32_t* word = status ? status : reinterpret_cast<int32_t*>(static_cast<unsigned char*>(site->base) + kStatusOffset);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // the status word must start at zero; the logits are fully overwritten
     if (cudaMemsetAsync(word, 0, sizeof(int32_t), s) != cudaSuccess) return K3XB_BACKEND_UNAVAILABLE;
-    k3xb_ctx launch;   // carries the stream for the shared launchers; owns no device memory
-    launch.device = device;
-    launch.stream = s;
-    if (cudaDeviceGetAttribute(&launch.sm_count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
-        return K3XB_BACKEND_UNAVAILABLE;
-    launch.status_word = word;
-    st = launch_router_logits(&launch, hidden, tokens, hidden_size, router, experts, logits);
-    release_mxf4_resources(&launch);   // host-side tensor-map state of the local context
+    site->launch.stream = s;
+    site->launch.status_word = word;
+    st = launch_router_logits(&site->launch, hidden, tokens, hidden_size, router, experts, logits);
     if (st) return st;
-    return launch_topk(&launch, logits, correction, tokens, experts, top_k, ids, contributions, nullptr, word);
+    return launch_topk(&site->launch, logits, correction, tokens, experts, top_k, ids, contributions, nullptr, word);
 }

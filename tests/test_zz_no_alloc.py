@@ -61,6 +61,42 @@ def test_route_static_matches_route_on_two_calls():
     ctx.close()
 
 
+def test_route_static_allocates_nothing_and_runs_without_status():
+    """A warm call changes no device memory reservation (cudaMemGetInfo's
+    free bytes are the same before and after it), and a call with status
+    NULL gives the same routes as k3xb_route."""
+    torch = torch_cuda()
+    import k3xb
+    ctx = k3xb.Context(0)
+    ctx.use_stream()
+    fn = _static_fn()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    g = np.random.default_rng(2027)
+    T, H, E, K = 32, 7168, 384, 16
+    router = to_dev(torch, bf16_words(g.normal(0, 0.02, size=(E, H))))
+    corr = to_dev(torch, g.normal(0, 0.02, size=E).astype(np.float32))
+    hidden = to_dev(torch, bf16_normal(g, (T, H)))
+    ids_ref = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    con_ref = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    ctx.route(hidden, router, corr, K, ids_ref, con_ref)
+    ctx.sync()
+    ids = torch.full((T, K), -1, dtype=torch.int32, device="cuda")
+    con = torch.zeros((T, K), dtype=torch.float32, device="cuda")
+    args = (_dev_ptr(hidden), T, H, _dev_ptr(router), _dev_ptr(corr), E, K, _dev_ptr(ids), _dev_ptr(con), None,
+            stream)
+    assert fn(*args) == k3xb.OK   # the first call on the device does its one-time set-up
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        assert fn(*args) == k3xb.OK
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, f"device free memory moved by {free0 - free1} bytes"
+    np.testing.assert_array_equal(ids.cpu().numpy(), ids_ref.cpu().numpy())
+    np.testing.assert_allclose(con.cpu().numpy(), con_ref.cpu().numpy(), rtol=1e-6, atol=0)
+    ctx.close()
+
+
 def test_route_static_rejects_oversize():
     torch = torch_cuda()
     import k3xb
