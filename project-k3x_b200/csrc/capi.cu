@@ -731,13 +731,18 @@ int k3xb_official_moe_ffn_host(k3xb_ctx* ctx, const k3xb_moe_layer* tail, const 
 namespace {
 
 struct KdaSchedule {
+    // per visited entry: node, depth (1 = root) and flags (kKdaReset: reload
+    // the prefix state first; kKdaReplay: recompute only, no output)
     std::vector<int32_t> order, depth, from_stack;
     uint32_t levels = 0;
 };
 
+constexpr int32_t kKdaReset = 1, kKdaReplay = 2;
+
 // DFS preorder of the draft forest (roots = parent -1, children in index
-// order); from_stack marks nodes whose parent is not the node visited just
-// before them.
+// order). A node whose parent is not the node visited just before it starts
+// from the prefix state: the entries before it replay its ancestors root..
+// parent (no output), so no state is kept per depth.
 int schedule_tree(k3xb_ctx* ctx, const int32_t* parent, uint32_t n, KdaSchedule& out) {
     std::vector<std::vector<int32_t>> children(n);
     std::vector<int32_t> roots;
@@ -747,20 +752,29 @@ int schedule_tree(k3xb_ctx* ctx, const int32_t* parent, uint32_t n, KdaSchedule&
         if (parent[i] < 0) roots.push_back(static_cast<int32_t>(i));
         else children[parent[i]].push_back(static_cast<int32_t>(i));
     }
-    std::vector<int32_t> dep(n, 0);
     std::vector<std::pair<int32_t, int32_t>> stack;   // (node, depth)
     for (auto it = roots.rbegin(); it != roots.rend(); ++it) stack.push_back({*it, 1});
     int32_t prev = -1;
+    std::vector<int32_t> path;
     while (!stack.empty()) {
         auto [node, d] = stack.back();
         stack.pop_back();
+        const int32_t p = parent[node];
+        int32_t flags = 0;
+        if (p != prev && !out.order.empty()) {   // off the current chain: from the prefix
+            path.clear();
+            for (int32_t x = p; x >= 0; x = parent[x]) path.push_back(x);
+            flags = kKdaReset;
+            for (size_t i = path.size(); i-- > 0;) {
+                out.order.push_back(path[i]);
+                out.depth.push_back(static_cast<int32_t>(path.size() - i));
+                out.from_stack.push_back(flags | kKdaReplay);
+                flags = 0;
+            }
+        }
         out.order.push_back(node);
         out.depth.push_back(d);
-        // the registers hold the prefix state before the first node and the
-        // previous node's state afterwards
-        const bool reload = parent[node] != prev;
-        out.from_stack.push_back(reload ? 1 : 0);
-        if (reload) out.levels = std::max<uint32_t>(out.levels, static_cast<uint32_t>(d));
+        out.from_stack.push_back(flags);
         for (auto c = children[node].rbegin(); c != children[node].rend(); ++c) stack.push_back({*c, d + 1});
         prev = node;
     }

@@ -24,8 +24,10 @@
 //   split_tokens   E2M1-term split of every hidden row, once per token
 //   gather_gu      tile-major gate/up B operand + scale atoms
 //   gateup         gate and up share the B tile; the epilogue applies
-//                  SwiGLU / SiTU (official_moe.cpp:95-96) and splits the result
-//                  into the down projection's E2M1 operand and scales
+//                  SwiGLU / SiTU (official_moe.cpp:95-96) and stores the
+//                  activation rows (coalesced floats)
+//   split_act      the activation rows split into the down projection's
+//                  E2M1 operand and scale atoms, all tiles in parallel
 //   down           two weight tiles per item; the epilogue sums term
 //                  columns, rounds to bf16 (official_moe.cpp:101) and
 //                  scatters each row to its (token, slot) for the ordered
@@ -131,39 +133,72 @@ __global__ void __launch_bounds__(1024) worklist_kernel(const uint32_t* group_co
 }
 
 // ---------------------------------------------------------------------------
-// E2M1-term split (bit-identical to oracle/k3x_oracle.c:k3xo_e2m1_terms).
+// E2M1-term split (bit-identical to oracle/k3x_oracle.c:k3xo_e2m1_terms) of
+// one 32-element MX block held by one thread: per term, the block maximum,
+// its E8M0 exponent, each element's code (round to nearest even on the
+// E2M1 grid), and the exact residual. Term t's 16 packed bytes go to
+// rows[t * row_stride] (low nibble = even element), its scale byte to
+// scales[t * scale_stride].
+__device__ __forceinline__ void split_block32(float (&v)[32], uint32_t terms, uint8_t* rows, size_t row_stride,
+                                              uint8_t* scales, size_t scale_stride) {
+    for (uint32_t t = 0; t < terms; ++t) {
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        const int s = amax > 0.0f ? e2m1_block_exponent(amax) : 0;
+        const float inv = exp2i(-s), scale = exp2i(s);
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const uint32_t code = e2m1_code(fabsf(v[i]) * inv);
+            const bool neg = signbit(v[i]) && code;
+            const float qv = e2m1_magnitude(code) * scale;
+            v[i] = neg ? __fadd_rn(v[i], qv) : __fsub_rn(v[i], qv);
+            w[i / 8] |= (code | (neg ? 8u : 0u)) << (4 * (i % 8));
+        }
+        *reinterpret_cast<uint4*>(rows + t * row_stride) = make_uint4(w[0], w[1], w[2], w[3]);
+        scales[t * scale_stride] = static_cast<uint8_t>(s + 127);
+    }
+}
+
+__device__ __forceinline__ void load_block32(const float* src, float (&v)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+        const float4 q = *reinterpret_cast<const float4*>(src + i);
+        v[i] = q.x; v[i + 1] = q.y; v[i + 2] = q.z; v[i + 3] = q.w;
+    }
+}
+
 // Every token's hidden row once: tsplit[t][term][H/2], tsf[t][term][H/32].
-// One warp per (row, 32-element block), lane = element: the block maximum
-// is a warp max (exact), each lane codes and subtracts its own element, and
-// groups of 8 lanes OR their nibbles into one 32-bit word.
-// Rows are floats, or bf16 words when hidden16 is given (the expert-parallel
-// receive window).
+// One thread per (row, 32-element block); rows are floats, or bf16 words
+// when hidden16 is given (the expert-parallel receive window).
 __global__ void __launch_bounds__(256) split_tokens_kernel(const float* __restrict__ hidden,
                                                            const uint16_t* __restrict__ hidden16, uint32_t T,
                                                            uint32_t H, uint32_t terms,
                                                            uint8_t* __restrict__ tsplit,
                                                            uint8_t* __restrict__ tsf) {
-    const uint32_t kbc = H / 32, lane = threadIdx.x % 32;
-    const size_t w = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
-    if (w >= static_cast<size_t>(T) * kbc) return;
-    const uint32_t t = static_cast<uint32_t>(w / kbc), kb = static_cast<uint32_t>(w % kbc);
-    const size_t at = static_cast<size_t>(t) * H + kb * 32 + lane;
-    float r = hidden16 ? decode_bf16(hidden16[at]) : hidden[at];
-    for (uint32_t term = 0; term < terms; ++term) {
-        const float amax = warp_max(fabsf(r));
-        const int s = amax > 0.0f ? e2m1_block_exponent(amax) : 0;
-        const uint32_t code = e2m1_code(fabsf(r) * exp2i(-s));
-        const bool neg = signbit(r) && code;
-        const float qv = e2m1_magnitude(code) * exp2i(s);
-        r = neg ? __fadd_rn(r, qv) : __fsub_rn(r, qv);
-        uint32_t word = (code | (neg ? 8u : 0u)) << (4 * (lane % 8));
-        word |= __shfl_xor_sync(0xffffffffu, word, 1);
-        word |= __shfl_xor_sync(0xffffffffu, word, 2);
-        word |= __shfl_xor_sync(0xffffffffu, word, 4);
-        const size_t row = static_cast<size_t>(t) * terms + term;
-        if (lane % 8 == 0) *reinterpret_cast<uint32_t*>(tsplit + row * (H / 2) + kb * 16 + (lane / 8) * 4) = word;
-        if (lane == 0) tsf[row * kbc + kb] = static_cast<uint8_t>(s + 127);
+    const uint32_t kbc = H / 32;
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<size_t>(T) * kbc) return;
+    const uint32_t t = static_cast<uint32_t>(i / kbc), kb = static_cast<uint32_t>(i % kbc);
+    const size_t at = static_cast<size_t>(t) * H + kb * 32;
+    float v[32];
+    if (hidden16) {
+#pragma unroll
+        for (int k = 0; k < 32; k += 8) {
+            const uint4 q = *reinterpret_cast<const uint4*>(hidden16 + at + k);
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                v[k + 2 * m] = __uint_as_float(w[m] << 16);
+                v[k + 2 * m + 1] = __uint_as_float(w[m] & 0xffff0000u);
+            }
+        }
+    } else {
+        load_block32(hidden + at, v);
     }
+    const size_t row = static_cast<size_t>(t) * terms;
+    split_block32(v, terms, tsplit + row * (H / 2) + kb * 16, H / 2, tsf + row * kbc + kb, kbc);
 }
 
 // Tile-major gate/up B operand (+ scale atoms) gathered from the per-token
@@ -195,6 +230,56 @@ __global__ void __launch_bounds__(256) gather_gu_kernel(const uint8_t* __restric
     }
 }
 
+// The down projection's B operand from the activation rows (gate/up
+// epilogue output): per tile, token j's row becomes `terms` E2M1 rows
+// j*terms + t with their scale atoms, and rows [ntok*terms, n) are zero,
+// n the tile's MMA N. One thread per (token, 32-element block of I).
+__global__ void __launch_bounds__(256) split_act_kernel(const float* __restrict__ act, Tables tb, uint32_t I,
+                                                        uint32_t terms, uint32_t tpt, uint32_t nmax,
+                                                        uint8_t* __restrict__ b, uint8_t* __restrict__ sfb) {
+    const uint32_t tile = blockIdx.y;
+    if (tile >= tb.counts[0]) return;
+    const uint32_t ntok = tb.tile_ntok[tile], used = ntok * terms, n = round16(used);
+    const uint32_t kbc = I / 32;
+    const size_t row_stride = I / 2;
+    uint8_t* base = b + static_cast<size_t>(tile) * nmax * row_stride;
+    uint8_t* atoms = sfb + static_cast<size_t>(tile) * (I / 128) * kAtomBytes;
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < ntok * kbc; i += stride) {
+        const uint32_t j = i / kbc, kb = i % kbc;
+        float v[32];
+        load_block32(act + (static_cast<size_t>(tile) * tpt + j) * I + kb * 32, v);
+        // term t of token j is MMA row j*terms + t: bytes at row * row_stride + kb * 16, its scale in
+        // atom kb / 4 at byte (row % 32) * 16 + (row / 32) * 4 + kb % 4
+        for (uint32_t t = 0; t < terms; ++t) {
+            float amax = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
+            const int s = amax > 0.0f ? e2m1_block_exponent(amax) : 0;
+            const float inv = exp2i(-s), scale = exp2i(s);
+            uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const uint32_t code = e2m1_code(fabsf(v[e]) * inv);
+                const bool neg = signbit(v[e]) && code;
+                const float qv = e2m1_magnitude(code) * scale;
+                v[e] = neg ? __fadd_rn(v[e], qv) : __fsub_rn(v[e], qv);
+                w[e / 8] |= (code | (neg ? 8u : 0u)) << (4 * (e % 8));
+            }
+            const uint32_t row = j * terms + t;
+            *reinterpret_cast<uint4*>(base + static_cast<size_t>(row) * row_stride + kb * 16) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+            atoms[(kb / 4) * kAtomBytes + (row % 32) * 16 + (row / 32) * 4 + kb % 4] = static_cast<uint8_t>(s + 127);
+        }
+    }
+    // padding rows of the MMA N: zero codes, unit scales
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < (n - used) * kbc; i += stride) {
+        const uint32_t row = used + i / kbc, kb = i % kbc;
+        *reinterpret_cast<uint4*>(base + static_cast<size_t>(row) * row_stride + kb * 16) = make_uint4(0, 0, 0, 0);
+        atoms[(kb / 4) * kAtomBytes + (row % 32) * 16 + (row / 32) * 4 + kb % 4] = 127;
+    }
+}
+
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float activate(float g, float u, int act, float beta, float lbeta) {
     // SwiGLU: (g * sigmoid(g)) * u; SiTU: runtime/src/ops.cpp:20-30.
@@ -213,10 +298,10 @@ struct GuParams {
     const uint8_t* sfa_gate;
     const uint8_t* sfa_up;
     const uint8_t* sfb;       // gather_gu scales
-    uint8_t* b_down;          // epilogue outputs: the down projection's B operand
-    uint8_t* sfb_down;
+    float* act;               // epilogue output: act[tile * tpt + j][I], token j of the tile
+    uint32_t tpt;             // tokens per tile (the act rows a tile owns)
     uint32_t H, I, terms;
-    int act;
+    int act_kind;
     float beta, lbeta;
     int* error;
 };
@@ -251,14 +336,15 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_consta
     const uint32_t terms = p.terms;
     const uint32_t mtc = p.I / kBlockM;
     auto get_desc = [&](uint32_t item) { return __ldg(p.desc + item); };
+    // The epilogue adds each token's term columns, applies SwiGLU / SiTU and
+    // stores the activation row (a warp's 32 rows of I are 32 consecutive
+    // floats); split_act_kernel then builds the down projection's operand.
     auto epilogue = [&](const uint4& d, uint32_t tmem, uint32_t q, uint32_t lane) {
         const uint32_t tile = d.y / NM, mt = (d.x / kBlockM) % mtc;
         const uint32_t ntok = tcp::desc_ntok(d);
-        const uint32_t used = ntok * terms, n = tcp::desc_n(d);
+        const uint32_t used = ntok * terms;
         const uint32_t lane_base = (32u * q) << 16;
-        const size_t row_stride = p.I / 2;
-        uint8_t* brow = p.b_down + static_cast<size_t>(tile) * NM * row_stride + mt * 64 + q * 16;
-        uint8_t* sfbase = p.sfb_down + (static_cast<size_t>(tile) * (p.I / 128) + mt) * kAtomBytes + q;
+        float* arow = p.act + static_cast<size_t>(tile) * p.tpt * p.I + mt * kBlockM + 32u * q + lane;
         float gs = 0.0f, us = 0.0f;
         uint32_t tcount = 0, j = 0;
         for (uint32_t c0 = 0; c0 < used; c0 += 16) {
@@ -272,33 +358,11 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_consta
                 gs = __fadd_rn(gs, vg[i]);
                 us = __fadd_rn(us, vu[i]);
                 if (++tcount < terms) continue;
-                // token j done: a = act(g, u), split over this warp's 32 rows
-                // (one MX block of the down projection's K)
-                float r = activate(gs, us, p.act, p.beta, p.lbeta);
-                for (uint32_t t = 0; t < terms; ++t) {
-                    const float amax = warp_max(fabsf(r));
-                    const int s = amax > 0.0f ? e2m1_block_exponent(amax) : 0;
-                    const uint32_t cd = e2m1_code(fabsf(r) * exp2i(-s));
-                    const bool neg = signbit(r) && cd;
-                    const float qv = e2m1_magnitude(cd) * exp2i(s);
-                    r = neg ? __fadd_rn(r, qv) : __fsub_rn(r, qv);
-                    uint32_t word = (cd | (neg ? 8u : 0u)) << (4 * (lane % 8));
-                    word |= __shfl_xor_sync(0xffffffffu, word, 1);
-                    word |= __shfl_xor_sync(0xffffffffu, word, 2);
-                    word |= __shfl_xor_sync(0xffffffffu, word, 4);
-                    const uint32_t row = j * terms + t;
-                    if (lane % 8 == 0)
-                        *reinterpret_cast<uint32_t*>(brow + static_cast<size_t>(row) * row_stride + (lane / 8) * 4) = word;
-                    if (lane == 0) sfbase[(row % 32) * 16 + (row / 32) * 4] = static_cast<uint8_t>(s + 127);
-                }
+                arow[static_cast<size_t>(j) * p.I] = activate(gs, us, p.act_kind, p.beta, p.lbeta);
                 gs = us = 0.0f;
                 tcount = 0;
                 ++j;
             }
-        }
-        for (uint32_t row = used; row < n; ++row) {   // zero padding rows
-            if (lane % 8 == 0) *reinterpret_cast<uint32_t*>(brow + static_cast<size_t>(row) * row_stride + (lane / 8) * 4) = 0u;
-            if (lane == 0) sfbase[(row % 32) * 16 + (row / 32) * 4] = 127;
         }
     };
     const uint8_t* sfa[2] = {p.sfa_gate, p.sfa_up};
@@ -556,6 +620,7 @@ struct Layout {
     size_t b_gu, sfb_gu, b_d, sfb_d;
     size_t sf_gate, sf_up, sf_down;   // per-call re-laid scales (0 when prepared)
     size_t tsplit, tsf;               // per-token E2M1 split of the hidden rows
+    size_t act;                       // activation rows [max_tiles * tpt][I] (floats)
 };
 
 Layout layout_of(const k3xb_moe_layer& L, uint32_t T) {
@@ -580,12 +645,14 @@ Layout layout_of(const k3xb_moe_layer& L, uint32_t T) {
     l.sf_down = L.down_scales_tc ? 0 : sf_gu;
     l.tsplit = static_cast<size_t>(T) * l.terms * (L.hidden / 2);
     l.tsf = static_cast<size_t>(T) * l.terms * (L.hidden / 32);
+    l.act = static_cast<size_t>(l.max_tiles) * l.tpt * L.inter;
     return l;
 }
 
 struct Buffers {
     Tables tb;
     uint8_t *b_gu, *sfb_gu, *b_d, *sfb_d, *sf[3], *tsplit, *tsf;
+    float* act;
 };
 
 template <typename A>
@@ -606,11 +673,21 @@ void carve(A& a, const Layout& l, Buffers* out) {
     r.sf[2] = a.template take<uint8_t>(l.sf_down, 1024);
     r.tsplit = a.template take<uint8_t>(l.tsplit, 1024);
     r.tsf = a.template take<uint8_t>(l.tsf, 1024);
+    r.act = a.template take<float>(l.act, 1024);
 }
+
+struct SplitArgs {
+    const float* act;
+    Tables tb;
+    uint32_t I, terms, tpt, nmax;
+    uint8_t *b, *sfb;
+    uint32_t max_tiles;
+};
 
 template <uint32_t NM>
 int launch_routed(k3xb_ctx* ctx, const CUtensorMap& map_gate, const CUtensorMap& map_up, const CUtensorMap& map_bgu,
-                  const CUtensorMap& map_down, const CUtensorMap& map_bd, const GuParams& gp, const DParams& dp) {
+                  const CUtensorMap& map_down, const CUtensorMap& map_bd, const GuParams& gp, const SplitArgs& sa,
+                  const DParams& dp) {
     using RC = RoutedCfg<NM>;
     const size_t smem_gu = tcp::smem_bytes<RC::kStagesGU, 2, NM>();
     const size_t smem_d = tcp::smem_bytes<RC::kStagesGU, 2, NM>();
@@ -626,6 +703,14 @@ int launch_routed(k3xb_ctx* ctx, const CUtensorMap& map_gate, const CUtensorMap&
     {
         PhaseScope ph(ctx, K3XB_PHASE_EXPERT_GATEUP);
         gateup_kernel<NM><<<ctx->sm_count, kThreads, smem_gu, ctx->stream>>>(map_gate, map_up, map_bgu, gp);
+        K3XB_LAUNCHED(ctx);
+    }
+    {
+        PhaseScope ph(ctx, K3XB_PHASE_EXPERT_PREP);
+        // one thread per (token, 32-block) of a tile
+        const uint32_t per_tile = (sa.tpt * (sa.I / 32) + 255u) / 256u;
+        split_act_kernel<<<dim3(per_tile, sa.max_tiles), 256, 0, ctx->stream>>>(sa.act, sa.tb, sa.I, sa.terms, sa.tpt,
+                                                                               sa.nmax, sa.b, sa.sfb);
         K3XB_LAUNCHED(ctx);
     }
     PhaseScope ph(ctx, K3XB_PHASE_EXPERT_DOWN);
@@ -692,7 +777,7 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
     K3XB_LAUNCHED(ctx);
     {
         const size_t n = static_cast<size_t>(T) * (H / 32);
-        split_tokens_kernel<<<static_cast<unsigned>((n * 32 + 255) / 256), 256, 0, ctx->stream>>>(hidden, hidden16, T, H,
+        split_tokens_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(hidden, hidden16, T, H,
                                                                                           l.terms, bf.tsplit, bf.tsf);
         K3XB_LAUNCHED(ctx);
     }
@@ -701,13 +786,14 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
     K3XB_LAUNCHED(ctx);
     prep.end();
 
-    GuParams gp{bf.tb.desc_gu, bf.tb.counts + 1, sfa_gate, sfa_up, bf.sfb_gu, bf.b_d, bf.sfb_d, H, I, l.terms,
+    GuParams gp{bf.tb.desc_gu, bf.tb.counts + 1, sfa_gate, sfa_up, bf.sfb_gu, bf.act, l.tpt, H, I, l.terms,
                 L.activation, L.situ_beta, L.situ_linear_beta, ctx->status_word};
+    SplitArgs sa{bf.act, bf.tb, I, l.terms, l.tpt, l.nmax, bf.b_d, bf.sfb_d, l.max_tiles};
     DParams dp{bf.tb.desc_d, bf.tb.counts + 2, plan.assign_token, plan.assign_slot, sfa_down, bf.sfb_d, slot_out,
                H, I, l.terms, L.top_k, ctx->status_word, static_cast<uint32_t>(static_cast<size_t>(L.experts) * H / kBlockM),
                slot_out16, ep ? *ep : EpTarget{}};
-    return l.nmax == 64 ? launch_routed<64>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, dp)
-                        : launch_routed<128>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, dp);
+    return l.nmax == 64 ? launch_routed<64>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, sa, dp)
+                        : launch_routed<128>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, sa, dp);
 }
 
 int launch_shared_tc(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T, uint16_t* xb,

@@ -2,21 +2,30 @@
 // trees (official_kda.cpp:319-369 per node).
 //
 // In the reference's V-first layout S[h][v][k] every value row v evolves on
-// its own: decayed = alpha (.) S[v]; pred = <k, decayed>; delta = (v_v -
-// pred) * beta; S[v] = decayed + k * delta; o_v = <q, S[v]>. One warp owns
-// ROWS consecutive value rows of one head; lane l holds keys
-// [l*KPL, l*KPL+KPL) of each row in registers, so the state is streamed from
-// HBM once (coalesced 128*KPL-byte rows), both dot products are warp
-// shuffles, and q/k/alpha of a node are read once per warp for ROWS rows.
+// its own: decayed = alpha (.) S[v]; pred = sum_k k_k * decayed_k; delta =
+// (v_v - pred) * beta; S[v] = decayed + k * delta; o_v = sum_k q_k * S[v][k].
+// One thread owns one value row and holds its d keys in registers; a block
+// owns R rows of one head of one sequence. Per node the block stages the
+// head's k, q and alpha = exp(log_decay) (computed once per key) in shared
+// memory, and every thread then runs both dot products as sequential loops
+// in key order: the reference's own float operation order (every product
+// and sum rounded, no contraction), so on the same inputs the recurrence
+// reproduces official_kda_cpu's arithmetic up to the exp of the decay. The
+// state crosses HBM once each way per call (read coalesced through shared
+// memory, written as 16-byte rows).
 //
 // Trees: nodes are visited in DFS preorder (computed on the host). When a
 // node's parent is the node just visited, the state stays in registers;
-// otherwise the parent's state is reloaded from a per-warp shared-memory
-// stack indexed by depth (the prefix state is depth 0). Linear drafts never
-// touch the stack. Commit mode replays a root..node path and writes that
-// node's state, bit-identical to what the tree pass computed for it; with a
-// device commit array the pass writes the state after commit[s] instead
-// (linear drafts committed from device-side acceptance).
+// otherwise the schedule restarts from the prefix state (reloaded from the
+// input, in L2) and replays the ancestors without output, so a block keeps
+// no per-depth copies of the state and runs with full occupancy. Linear
+// drafts never restart. Commit mode replays a root..node path and writes
+// that node's state, bit-identical to what the tree pass computed for it;
+// with a device commit array the pass writes the state after commit[s]
+// instead, and stops there (linear drafts committed from device-side
+// acceptance).
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -24,93 +33,121 @@ namespace k3xb {
 
 namespace {
 
-constexpr int kRows = 2;   // value rows per warp
+struct KdaArgs {
+    const float* state;
+    const int32_t* order;
+    const int32_t* flags;   // per entry: 1 = restart from the prefix state, 2 = replay (no output)
+    uint32_t visit, nodes, heads;
+    const float *q, *k, *v, *log_decay, *beta;
+    float* out;
+    float* state_out;
+    const int32_t* commit;
+};
 
-template <int KPL>
-__global__ void __launch_bounds__(128) kda_tree_kernel(
-    const float* __restrict__ state, const int32_t* __restrict__ order,
-    const int32_t* __restrict__ depth, const int32_t* __restrict__ from_stack, uint32_t visit,
-    uint32_t nodes, uint32_t heads, const float* __restrict__ q, const float* __restrict__ k,
-    const float* __restrict__ v, const float* __restrict__ log_decay,
-    const float* __restrict__ beta, float* __restrict__ out, float* __restrict__ state_out,
-    uint32_t levels, const int32_t* __restrict__ commit) {
-    constexpr int D = 32 * KPL;
-    extern __shared__ float stack[];   // [warps][levels][kRows][D]; level 0 = prefix
-    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+// shared memory: k, q, alpha [D], v [R], beta, then [R][D + 1] for staging
+// the prefix rows
+template <int D, int R>
+constexpr size_t kda_smem_floats() {
+    return 3 * D + R + 4 + static_cast<size_t>(R) * (D + 1);
+}
+
+template <int D, int R>
+__global__ void __launch_bounds__(R) kda_rows_kernel(const KdaArgs a) {
+    extern __shared__ float smem[];
+    float* kk = smem;
+    float* qq = kk + D;
+    float* al = qq + D;
+    float* vv = al + D;
+    float* bsh = vv + R;
+    float* stage = bsh + 4;
+    constexpr int kChunks = D / R;
+    const uint32_t t = threadIdx.x;
+    const uint32_t h = blockIdx.x / kChunks, r0 = (blockIdx.x % kChunks) * R;
     const uint32_t s = blockIdx.y;
-    const uint32_t row_global = (blockIdx.x * (blockDim.x / 32) + warp) * kRows;   // h*D + v
-    if (row_global >= heads * D) return;
-    const uint32_t h = row_global / D, v0 = row_global % D;
-    const size_t hd = static_cast<size_t>(heads) * D;
-    float* my_stack = stack + static_cast<size_t>(warp) * levels * kRows * D;
-
-    float st[kRows][KPL];
-    const float* src = state + static_cast<size_t>(s) * heads * D * D + static_cast<size_t>(h) * D * D;
-    float* dst = state_out ? state_out + static_cast<size_t>(s) * heads * D * D + static_cast<size_t>(h) * D * D
-                           : nullptr;
-    // commit (device array, per sequence): state_out receives the state after
-    // node commit[s] (the prefix state for -1) instead of after the last node
-    const int32_t keep = commit ? commit[s] : INT32_MIN;
+    if (h >= a.heads) return;
+    const size_t hd = static_cast<size_t>(a.heads) * D;
+    const size_t head_state = (static_cast<size_t>(s) * a.heads + h) * D * D + static_cast<size_t>(r0) * D;
+    // the prefix rows, coalesced through shared memory, then each thread's row to registers
+    const float* src = a.state + head_state;
+    for (uint32_t i = t; i < static_cast<uint32_t>(R * D); i += R) stage[(i / D) * (D + 1) + i % D] = src[i];
+    __syncthreads();
+    float S[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) S[i] = stage[t * (D + 1) + i];
+    float* dst = a.state_out ? a.state_out + head_state + static_cast<size_t>(t) * D : nullptr;
     auto save = [&]() {
 #pragma unroll
-        for (int r = 0; r < kRows; ++r)
-#pragma unroll
-            for (int i = 0; i < KPL; ++i) dst[static_cast<size_t>(v0 + r) * D + lane * KPL + i] = st[r][i];
+        for (int i = 0; i < D; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
     };
-#pragma unroll
-    for (int r = 0; r < kRows; ++r)
-#pragma unroll
-        for (int i = 0; i < KPL; ++i) {
-            st[r][i] = src[static_cast<size_t>(v0 + r) * D + lane * KPL + i];
-            if (levels) my_stack[r * D + lane * KPL + i] = st[r][i];
-        }
-    if (dst && keep == -1) save();
-
-    for (uint32_t it = 0; it < visit; ++it) {
-        const int32_t n = order[it];
-        const int32_t dn = depth[it];
-        if (from_stack[it]) {
-#pragma unroll
-            for (int r = 0; r < kRows; ++r)
-#pragma unroll
-                for (int i = 0; i < KPL; ++i)
-                    st[r][i] = my_stack[(static_cast<size_t>(dn - 1) * kRows + r) * D + lane * KPL + i];
-        }
-        const size_t base = (static_cast<size_t>(s) * nodes + n) * hd + static_cast<size_t>(h) * D;
-        float kk[KPL], qq[KPL], al[KPL];
-#pragma unroll
-        for (int i = 0; i < KPL; ++i) {
-            kk[i] = k[base + lane * KPL + i];
-            qq[i] = q[base + lane * KPL + i];
-            al[i] = expf(log_decay[base + lane * KPL + i]);
-        }
-        const float b = beta[(static_cast<size_t>(s) * nodes + n) * heads + h];
-#pragma unroll
-        for (int r = 0; r < kRows; ++r) {
-            float part = 0.0f;
-#pragma unroll
-            for (int i = 0; i < KPL; ++i) {
-                st[r][i] = __fmul_rn(al[i], st[r][i]);
-                part = __fadd_rn(part, __fmul_rn(kk[i], st[r][i]));
-            }
-            const float pred = warp_sum(part);
-            const float delta = __fmul_rn(__fsub_rn(v[base + v0 + r], pred), b);
-            float o = 0.0f;
-#pragma unroll
-            for (int i = 0; i < KPL; ++i) {
-                st[r][i] = __fadd_rn(st[r][i], __fmul_rn(kk[i], delta));
-                o = __fadd_rn(o, __fmul_rn(qq[i], st[r][i]));
-            }
-            o = warp_sum(o);
-            if (out && lane == 0) out[base + v0 + r] = o;
-            if (static_cast<uint32_t>(dn) < levels)
-#pragma unroll
-                for (int i = 0; i < KPL; ++i)
-                    my_stack[(static_cast<size_t>(dn) * kRows + r) * D + lane * KPL + i] = st[r][i];
-        }
-        if (dst && n == keep) save();
+    // commit (device array, per sequence): state_out receives the state after
+    // node commit[s] (the prefix state for -1) instead of after the last node
+    const int32_t keep = a.commit ? a.commit[s] : INT32_MIN;
+    if (dst && keep == -1) {
+        save();
+        return;
     }
-    if (dst && !commit) save();
+    for (uint32_t it = 0; it < a.visit; ++it) {
+        const int32_t n = a.order[it];
+        const int32_t fl = a.flags[it];
+        if (fl & 1) {   // restart from the prefix state (this thread's row, 16-byte loads)
+#pragma unroll
+            for (int i = 0; i < D; i += 4) {
+                const float4 q4 = *reinterpret_cast<const float4*>(src + static_cast<size_t>(t) * D + i);
+                S[i] = q4.x; S[i + 1] = q4.y; S[i + 2] = q4.z; S[i + 3] = q4.w;
+            }
+        }
+        const bool emit = !(fl & 2);
+        const size_t base = (static_cast<size_t>(s) * a.nodes + n) * hd + static_cast<size_t>(h) * D;
+        __syncthreads();   // the previous node's vectors are no longer read
+        for (uint32_t i = t; i < static_cast<uint32_t>(D); i += R) {
+            kk[i] = a.k[base + i];
+            qq[i] = a.q[base + i];
+            al[i] = expf(a.log_decay[base + i]);
+        }
+        vv[t] = a.v[base + r0 + t];
+        if (t == 0) bsh[0] = a.beta[(static_cast<size_t>(s) * a.nodes + n) * a.heads + h];
+        __syncthreads();
+        // the node vectors are read in program order (volatile), so the
+        // compiler does not hoist all of them into registers next to S
+        const volatile float* vk = kk;
+        const volatile float* va = al;
+        const volatile float* vq = qq;
+        float pred = 0.0f;
+#pragma unroll
+        for (int i = 0; i < D; ++i) {
+            S[i] = __fmul_rn(va[i], S[i]);
+            pred = __fadd_rn(pred, __fmul_rn(vk[i], S[i]));
+        }
+        const float delta = __fmul_rn(__fsub_rn(vv[t], pred), bsh[0]);
+        float o = 0.0f;
+#pragma unroll
+        for (int i = 0; i < D; ++i) {
+            S[i] = __fadd_rn(S[i], __fmul_rn(vk[i], delta));
+            o = __fadd_rn(o, __fmul_rn(vq[i], S[i]));
+        }
+        if (a.out && emit) a.out[base + r0 + t] = o;
+        if (dst && emit && n == keep) {   // the committed node: nothing after it is needed
+            save();
+            return;
+        }
+    }
+    if (dst && !a.commit) save();
+}
+
+template <int D, int R>
+int launch_rows(k3xb_ctx* ctx, const KdaArgs& a, uint32_t sequences) {
+    const size_t smem = kda_smem_floats<D, R>() * sizeof(float);
+    static std::atomic<uint64_t> configured{0};   // per template instance
+    const int cst = configure_once(ctx, configured, [&]() -> int {
+        K3XB_CUDA(ctx, cudaFuncSetAttribute(kda_rows_kernel<D, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem)));
+        return K3XB_OK;
+    });
+    if (cst) return cst;
+    dim3 grid(a.heads * (D / R), sequences);
+    kda_rows_kernel<D, R><<<grid, R, smem, ctx->stream>>>(a);
+    K3XB_LAUNCHED(ctx);
+    return K3XB_OK;
 }
 
 }  // namespace
@@ -120,29 +157,15 @@ int launch_kda(k3xb_ctx* ctx, const float* state, const int32_t* order, const in
                uint32_t heads, uint32_t head_dim, const float* q, const float* k, const float* v,
                const float* log_decay, const float* beta, float* out, float* state_out,
                uint32_t levels, const int32_t* commit) {
-    const uint32_t warps = 4;
-    const size_t smem = static_cast<size_t>(warps) * levels * kRows * head_dim * sizeof(float);
-    if (smem > 200 * 1024) return fail(ctx, K3XB_INVALID_EXTENT, "KDA draft tree too deep for the state stack");
-    const uint32_t rows = heads * head_dim;
-    dim3 grid((rows / kRows + warps - 1) / warps, sequences);
+    (void)depth;
+    (void)levels;
+    const KdaArgs a{state, order, from_stack, visit, nodes, heads, q, k, v, log_decay, beta, out, state_out, commit};
     switch (head_dim) {
-#define K3XB_KDA_CASE(KPL)                                                                      \
-    case 32 * KPL:                                                                              \
-        K3XB_CUDA(ctx, cudaFuncSetAttribute(kda_tree_kernel<KPL>,                               \
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); \
-        kda_tree_kernel<KPL><<<grid, 32 * warps, smem, ctx->stream>>>(                          \
-            state, order, depth, from_stack, visit, nodes, heads, q, k, v, log_decay, beta, out, \
-            state_out, levels, commit);                                                    \
-        break;
-        K3XB_KDA_CASE(1)
-        K3XB_KDA_CASE(2)
-        K3XB_KDA_CASE(4)
-#undef K3XB_KDA_CASE
-        default:
-            return fail(ctx, K3XB_INVALID_EXTENT, "KDA head_dim must be 32, 64 or 128");
+        case 32: return launch_rows<32, 32>(ctx, a, sequences);
+        case 64: return launch_rows<64, 64>(ctx, a, sequences);
+        case 128: return launch_rows<128, 128>(ctx, a, sequences);
+        default: return fail(ctx, K3XB_INVALID_EXTENT, "KDA head_dim must be 32, 64 or 128");
     }
-    K3XB_LAUNCHED(ctx);
-    return K3XB_OK;
 }
 
 }  // namespace k3xb

@@ -233,6 +233,36 @@ def test_kda_tree_parity(torch, ctx, rs, shape):
     np.testing.assert_array_equal(from_dev(st_out, np.float32), state)
 
 
+@pytest.mark.parametrize("shape", ["tree_c3", "linear"])
+def test_kda_recurrence_in_reference_order(torch, ctx, rs, shape):
+    """Every product and sum of the recurrence in the reference's order
+    (official_kda.cpp:319-369: the dot products as sequential sums over the
+    keys, no contraction): with the decay's exp exact on both sides
+    (log_decay 0, alpha 1) outputs and committed states equal the oracle's
+    bit for bit; otherwise they differ only through exp's last bit."""
+    g = np.random.default_rng(5)
+    if shape == "tree_c3":
+        S, h, d, parent = 1, 32, 128, _tree(2)
+    else:
+        S, h, d, parent = 2, 8, 128, np.arange(-1, 8, dtype=np.int32)
+    N = parent.size
+    state = (g.normal(0, 0.05, size=(S, h, d, d))).astype(np.float32)
+    q, k, v, _, be = _kda_inputs(g, S, N, h, d)
+    ld = np.zeros_like(q)
+    dev = [to_dev(torch, a) for a in (state, q, k, v, ld, be)]
+    out = torch.empty((S, N, h * d), dtype=torch.float32, device="cuda")
+    ctx.kda_tree(dev[0], parent, *dev[1:], out)
+    commit = [N - 1 - s for s in range(S)]
+    st_out = torch.empty_like(dev[0])
+    ctx.kda_commit(dev[0], parent, *dev[1:], commit, st_out)
+    ctx.sync()
+    got, got_state = from_dev(out, np.float32), from_dev(st_out, np.float32)
+    for s in range(S):
+        want, states = rs.kda_tree(state[s], parent, q[s], k[s], v[s], ld[s], be[s], h, d, want_states=True)
+        np.testing.assert_array_equal(got[s], want)
+        np.testing.assert_array_equal(got_state[s], states[commit[s]])
+
+
 def test_kda_commit_bit_identical_to_tree_pass(torch, ctx):
     """The committed state replays exactly the ops of the verify pass: a
     second tree pass continuing from the committed state equals the
