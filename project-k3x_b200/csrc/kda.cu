@@ -51,6 +51,18 @@ constexpr size_t kda_smem_floats() {
     return 3 * D + R + 4 + static_cast<size_t>(R) * (D + 1);
 }
 
+// Four consecutive floats of shared memory (16-byte aligned), as a
+// volatile load: ptxas keeps these loads in program order, so each group is
+// fetched one group ahead of its use instead of all at once (the state
+// already holds D registers per thread).
+__device__ __forceinline__ float4 lds4(const float* p) {
+    float4 v;
+    asm volatile("ld.volatile.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+    return v;
+}
+
 template <int D, int R>
 __global__ void __launch_bounds__(R) kda_rows_kernel(const KdaArgs a) {
     extern __shared__ float smem[];
@@ -107,23 +119,44 @@ __global__ void __launch_bounds__(R) kda_rows_kernel(const KdaArgs a) {
         vv[t] = a.v[base + r0 + t];
         if (t == 0) bsh[0] = a.beta[(static_cast<size_t>(s) * a.nodes + n) * a.heads + h];
         __syncthreads();
-        // the node vectors are read in program order (volatile), so the
-        // compiler does not hoist all of them into registers next to S
-        const volatile float* vk = kk;
-        const volatile float* va = al;
-        const volatile float* vq = qq;
+        // the node vectors in groups of four keys, each group loaded one
+        // group ahead of its sums
         float pred = 0.0f;
+        {
+            float4 na = lds4(al), nk = lds4(kk);
 #pragma unroll
-        for (int i = 0; i < D; ++i) {
-            S[i] = __fmul_rn(va[i], S[i]);
-            pred = __fadd_rn(pred, __fmul_rn(vk[i], S[i]));
+            for (int c = 0; c < D; c += 4) {
+                const float4 ca = na, ck = nk;
+                if (c + 4 < D) {
+                    na = lds4(al + c + 4);
+                    nk = lds4(kk + c + 4);
+                }
+                const float xa[4] = {ca.x, ca.y, ca.z, ca.w}, xk[4] = {ck.x, ck.y, ck.z, ck.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    S[c + i] = __fmul_rn(xa[i], S[c + i]);
+                    pred = __fadd_rn(pred, __fmul_rn(xk[i], S[c + i]));
+                }
+            }
         }
         const float delta = __fmul_rn(__fsub_rn(vv[t], pred), bsh[0]);
         float o = 0.0f;
+        {
+            float4 nk = lds4(kk), nq = lds4(qq);
 #pragma unroll
-        for (int i = 0; i < D; ++i) {
-            S[i] = __fadd_rn(S[i], __fmul_rn(vk[i], delta));
-            o = __fadd_rn(o, __fmul_rn(vq[i], S[i]));
+            for (int c = 0; c < D; c += 4) {
+                const float4 ck = nk, cq = nq;
+                if (c + 4 < D) {
+                    nk = lds4(kk + c + 4);
+                    nq = lds4(qq + c + 4);
+                }
+                const float xk[4] = {ck.x, ck.y, ck.z, ck.w}, xq[4] = {cq.x, cq.y, cq.z, cq.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    S[c + i] = __fadd_rn(S[c + i], __fmul_rn(xk[i], delta));
+                    o = __fadd_rn(o, __fmul_rn(xq[i], S[c + i]));
+                }
+            }
         }
         if (a.out && emit) a.out[base + r0 + t] = o;
         if (dst && emit && n == keep) {   // the committed node: nothing after it is needed
