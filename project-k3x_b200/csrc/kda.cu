@@ -98,6 +98,24 @@ __global__ void __launch_bounds__(R) kda_rows_kernel(const KdaArgs a) {
         save();
         return;
     }
+    // the next entry's node vectors are loaded into registers while this
+    // entry computes (one element of k, q, log_decay per key this thread
+    // stages, v of its row, beta)
+    constexpr int PER = D / R;
+    float pk[PER], pq[PER], pl[PER], pv = 0.0f, pb = 0.0f;
+    auto prefetch = [&](uint32_t it) {
+        const int32_t n = a.order[it];
+        const size_t base = (static_cast<size_t>(s) * a.nodes + n) * hd + static_cast<size_t>(h) * D;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            pk[j] = a.k[base + t + j * R];
+            pq[j] = a.q[base + t + j * R];
+            pl[j] = a.log_decay[base + t + j * R];
+        }
+        pv = a.v[base + r0 + t];
+        pb = t == 0 ? a.beta[(static_cast<size_t>(s) * a.nodes + n) * a.heads + h] : 0.0f;
+    };
+    if (a.visit) prefetch(0);
     for (uint32_t it = 0; it < a.visit; ++it) {
         const int32_t n = a.order[it];
         const int32_t fl = a.flags[it];
@@ -111,14 +129,16 @@ __global__ void __launch_bounds__(R) kda_rows_kernel(const KdaArgs a) {
         const bool emit = !(fl & 2);
         const size_t base = (static_cast<size_t>(s) * a.nodes + n) * hd + static_cast<size_t>(h) * D;
         __syncthreads();   // the previous node's vectors are no longer read
-        for (uint32_t i = t; i < static_cast<uint32_t>(D); i += R) {
-            kk[i] = a.k[base + i];
-            qq[i] = a.q[base + i];
-            al[i] = expf(a.log_decay[base + i]);
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            kk[t + j * R] = pk[j];
+            qq[t + j * R] = pq[j];
+            al[t + j * R] = expf(pl[j]);
         }
-        vv[t] = a.v[base + r0 + t];
-        if (t == 0) bsh[0] = a.beta[(static_cast<size_t>(s) * a.nodes + n) * a.heads + h];
+        vv[t] = pv;
+        if (t == 0) bsh[0] = pb;
         __syncthreads();
+        if (it + 1 < a.visit) prefetch(it + 1);
         // the node vectors in groups of four keys, each group loaded one
         // group ahead of its sums
         float pred = 0.0f;
