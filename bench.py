@@ -277,7 +277,7 @@ def gpu_moe(ctx, torch, cfg, seed, rank=0, world=1):
     return w
 
 
-def gpu_stack(ctx, torch, cfg, rank=0, world=1):
+def gpu_stack(ctx, torch, cfg, rank=0, world=1, act_terms=0):
     import k3xb
     layers, keep = [], []
     for l in range(cfg["layers"]):
@@ -288,7 +288,7 @@ def gpu_stack(ctx, torch, cfg, rank=0, world=1):
                    gate_lower_bound=-5.0)
         w.update(hidden=cfg["hidden"], rms_eps=1e-6, kda=kda, moe=gpu_moe(ctx, torch, cfg, seed, rank, world))
         keep.append(w)
-        layers.append(k3xb.layer_desc(w))
+        layers.append(k3xb.layer_desc(w, act_terms=act_terms))
     H, V = cfg["hidden"], cfg["vocab"]
     emb = gpu_tensor(ctx, torch, ("bf16", (V, H), cfg["seed"], 70, 1.0))
     lm = gpu_tensor(ctx, torch, ("bf16", (V, H), cfg["seed"], 71, 0.02))
@@ -553,7 +553,7 @@ def run_stack(args, rank, world, local, ctx, stream, cfg):
         uid = [k3xb.ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         ctx.ep_init(uid[0], rank, world)
-    model, keep = gpu_stack(ctx, torch, cfg, rank, world)
+    model, keep = gpu_stack(ctx, torch, cfg, rank, world, args.act_terms)
     Sr = S // world
     mine = slice(rank * Sr, (rank + 1) * Sr)
     tokens = stack_tokens(cfg)[mine]
@@ -659,7 +659,7 @@ def run_stack(args, rank, world, local, ctx, stream, cfg):
                                        "scaled by the experts streamed (profiles/expert_ffn_traffic_128x24.md)",
                      "whole_step": {"alg_bytes": step_bytes, "achieved": step_achieved,
                                     "frac": step_achieved / hbm}},
-        "gpu_launches": launches, "clocks": clk.summary(),
+        "gpu_launches": launches, "clocks": clk.summary(), "mxf4_act_terms": cfg["terms"],
         "accepted_tokens_per_s": sum_over_ranks(accepted, world) / (ms * 1e-3),
         "committed_tokens_per_s": sum_over_ranks(committed, world) / (ms * 1e-3),
         "phases": prof,
@@ -673,6 +673,16 @@ def run_stack(args, rank, world, local, ctx, stream, cfg):
 
 
 # ---- c2: one MoE layer ---------------------------------------------------------------------
+
+def c2_config(cfg, parallelism):
+    return {"workload": "c2: single released-shape MoE layer, expert-major verify"
+            + ("" if (cfg["experts"], cfg["tokens"]) == (C2["experts"], C2["tokens"])
+               else f" (reduced: {cfg['experts']} experts, {cfg['tokens']} tokens)"),
+            "hidden": cfg["hidden"], "experts": cfg["experts"], "top_k": cfg["top_k"], "inter": cfg["inter"],
+            "shared_inter": cfg["shared_inter"], "verify_tokens": cfg["tokens"], "sequences_x_drafts": "8x8",
+            "layers": 1, "seed": cfg["seed"], "parallelism": parallelism,
+            "l2": "no flush: each step streams ~8 GB of expert weights (>> 126 MB L2)"}
+
 
 def make_c2_layer(ctx, torch, cfg, engine, act_terms, rank=0, world=1):
     import k3xb
@@ -811,13 +821,8 @@ def run_c2(args, rank, world, local, ctx, stream, cfg):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "mxfp4",
         "data": "synthetic (seeded; generated in HBM by the library's generator)",
-        "config": {"workload": "c2: single released-shape MoE layer, expert-major verify",
-                   "hidden": H, "experts": E, "top_k": K, "inter": cfg["inter"], "shared_inter": cfg["shared_inter"],
-                   "verify_tokens": T, "sequences_x_drafts": "8x8", "layers": 1, "engine": args.engine,
-                   "act_terms": args.act_terms,
-                   "parallelism": f"expert parallel x{world}" if world > 1 else "single GPU",
-                   "cuda_graph": used_graph,
-                   "l2": "no flush: each step streams ~8 GB of expert weights (>> 126 MB L2)"},
+        "config": c2_config(cfg, f"expert parallel x{world}" if world > 1 else "single GPU"),
+        "cuda_graph": used_graph,
         "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
                 "d2h_bytes_per_step": T * H * 4 + 2 * T * K * 4},
         "roofline": {"bound": "hbm", "kernel": "expert FFN" + (" (timed alone)" if exp_ms else " (whole layer, per GPU)"),
@@ -827,7 +832,8 @@ def run_c2(args, rank, world, local, ctx, stream, cfg):
                      "traffic": unique * EXPERT_BYTES * EXPERT_TRAFFIC_RATIO,
                      "traffic_source": "ncu dram__bytes_read+write of gate/up + down on a reduced c2 case, "
                                        "scaled by unique experts (profiles/expert_ffn_traffic_128x24.md)"},
-        "gpu_launches": per_step * args.steps, "clocks": clk.summary(),
+        "gpu_launches": per_step * args.steps, "clocks": clk.summary(), "engine": args.engine,
+        "mxf4_act_terms": args.act_terms or k3xb.default_act_terms(T * K, E),
     }
     if args.profile:
         result["phases"] = phase_profile(ctx, torch, step, max(3, args.steps))
@@ -960,14 +966,15 @@ def run_tc_sweep(args, rank, world, local, ctx, stream):
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / args.steps
         useful = 2.0 * T * K * 3 * H * I
-        lines.append({"tokens_per_expert": M, "ms": ms, "useful_tflops": useful / (ms * 1e-3) / 1e12,
-                      "mma_tflops": useful * args.act_terms / (ms * 1e-3) / 1e12})
+        terms = args.act_terms or k3xb.default_act_terms(T * K, E)
+        lines.append({"tokens_per_expert": M, "ms": ms, "act_terms": terms,
+                      "useful_tflops": useful / (ms * 1e-3) / 1e12, "mma_tflops": useful * terms / (ms * 1e-3) / 1e12})
         del w, desc, hidden, slot_out
         torch.cuda.empty_cache()
     if rank == 0:
         print(json.dumps({"metric": "expert GEMM tensor-core sweep (useful TFLOP/s)", "config":
                           {"workload": "8 experts x M tokens, Top-8 of 8, H 7168, I 2048, MXFP4",
-                           "act_terms": args.act_terms}, "sweep": lines,
+                           "act_terms": args.act_terms or "library default"}, "sweep": lines,
                           "peak_note": "mxf4 dense peak 9 PFLOP/s nominal; MMA work = terms x useful"}), flush=True)
 
 
@@ -984,6 +991,8 @@ def run_ours(args):
     try:
         if args.config in ("c4", "c5"):
             cfg = dict(C5 if args.config == "c5" else C4, name=args.config)
+            cfg["terms"] = args.act_terms or k3xb.default_act_terms(cfg["sequences"] * (cfg["drafts"] + 1) * cfg["top_k"],
+                                                                  cfg["experts"])
             run_stack(args, rank, world, local, ctx, stream, cfg)
         elif args.config == "c3":
             run_c3(args, rank, world, local, ctx, stream)
@@ -1025,10 +1034,7 @@ def run_reference(args):
     dt = statistics.mean(times)
     value = sample.units() / dt
     if args.config == "c2":
-        config = {"workload": "c2: single released-shape MoE layer, expert-major verify", "hidden": C2["hidden"],
-                  "experts": C2["experts"], "top_k": C2["top_k"], "inter": C2["inter"],
-                  "shared_inter": C2["shared_inter"], "verify_tokens": C2["tokens"], "sequences_x_drafts": "8x8",
-                  "layers": 1, "parallelism": f"{sample.n} host threads"}
+        config = c2_config(dict(C2), f"{sample.n} host threads")
     else:
         cfg = dict(C5 if args.config == "c5" else C4, name=args.config)
         config = stack_config(cfg, 1)
@@ -1051,7 +1057,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--engine", choices=["mxf4", "simt"], default=os.environ.get("K3XB_ENGINE", "mxf4"))
-    ap.add_argument("--act-terms", type=int, default=6)
+    ap.add_argument("--act-terms", type=int, default=0,
+                    help="E2M1 activation terms of the MXF4 engine (0: the library default, k3xb_default_act_terms)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", choices=["c5", "c4", "c2", "c3", "tc"], default="c5",
                     help="c5 (default: 8-layer KDA+MoE verify step, expert parallel at N > 1), c4 (2 layers), "

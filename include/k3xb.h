@@ -232,7 +232,11 @@ typedef struct {
     int32_t activation;            /* K3XB_ACT_* */
     float situ_beta, situ_linear_beta;  /* linear_beta <= 0: none */
     int32_t engine;                /* K3XB_ENGINE_* */
-    int32_t act_terms;             /* E2M1 activation terms (MXF4 engine), 0 = 6 */
+    int32_t act_terms;             /* E2M1 activation terms (MXF4 engine); 0 = the
+                                      library default: 6 (exact for bf16 rows)
+                                      while the batch gives experts fewer than 12
+                                      tokens on average (tokens x top_k / experts),
+                                      4 from there on (k3xb_default_act_terms) */
     /* Optional copies of the three scale arrays in the tcgen05 layout made by
      * k3xb_prepare_mxfp4_scales (same byte count). When NULL the MXF4 engine
      * re-lays the scales into its scratch on every call. */
@@ -282,6 +286,12 @@ int k3xb_moe_layer_forward_host(k3xb_ctx* ctx, const k3xb_moe_layer* layer,
                                 const float* hidden_host, uint32_t tokens,
                                 float* out_host, uint32_t* ids_host,
                                 float* contributions_host);
+
+/* The E2M1 activation term count the MXF4 engine uses for a layer whose
+ * act_terms is 0, for a batch of `assignments` (tokens x top_k) over
+ * `experts` routed experts (the whole batch for an expert-parallel layer).
+ * No reference counterpart (the reference multiplies float activations). */
+uint32_t k3xb_default_act_terms(uint64_t assignments, uint32_t experts);
 
 /* Expert FFN only, for an existing plan (mxfp4_situ_mlp_grid,
  * backend.hpp:357-363): y[t][slot][D] = round_bf16(expert(hidden[t])), D the

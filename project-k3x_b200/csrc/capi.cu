@@ -295,6 +295,10 @@ using namespace k3xb;
 
 extern "C" {
 
+uint32_t k3xb_default_act_terms(uint64_t assignments, uint32_t experts) {
+    return mxf4_default_terms(assignments, experts);
+}
+
 int k3xb_create(int device, k3xb_ctx** out) {
     if (!out) return K3XB_INVALID_EXTENT;
     *out = nullptr;

@@ -556,7 +556,12 @@ int ep_moe_forward(k3xb_ctx* ctx, const k3xb_moe_layer& L, uint32_t E, const flo
     tgt.world = G;
     tgt.epoch = epoch;
     const uint8_t* rows = w.own + w.off_rows[b];
-    if ((st = launch_mxf4_experts(ctx, L, rows_bf16 ? nullptr : reinterpret_cast<const float*>(rows), G * T, plan,
+    // the default term count from the whole batch (every rank's tokens over
+    // all experts), as the one-GPU layer chooses it
+    k3xb_moe_layer LT = L;
+    if (!LT.act_terms)
+        LT.act_terms = static_cast<int32_t>(mxf4_default_terms(static_cast<uint64_t>(G) * T * K, E));
+    if ((st = launch_mxf4_experts(ctx, LT, rows_bf16 ? nullptr : reinterpret_cast<const float*>(rows), G * T, plan,
                                   nullptr, nullptr, &tgt,
                                   rows_bf16 ? reinterpret_cast<const uint16_t*>(rows) : nullptr)))
         return st;
@@ -565,7 +570,6 @@ int ep_moe_forward(k3xb_ctx* ctx, const k3xb_moe_layer& L, uint32_t E, const flo
     ep_combine_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(
         w.own, w.off_y[b], ids, contrib, shared, T, K, D, G, epoch, out, status);
     K3XB_LAUNCHED(ctx);
-    (void)E;
     return K3XB_OK;
 }
 

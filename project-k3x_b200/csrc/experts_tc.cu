@@ -623,9 +623,9 @@ struct Layout {
     size_t act;                       // activation rows [max_tiles * tpt][I] (floats)
 };
 
-Layout layout_of(const k3xb_moe_layer& L, uint32_t T) {
+Layout layout_of(const k3xb_moe_layer& L, uint32_t T, uint32_t terms) {
     Layout l{};
-    l.terms = L.act_terms > 0 ? static_cast<uint32_t>(L.act_terms) : 6u;
+    l.terms = terms;
     const uint32_t assigns = T * L.top_k;
     // 64-row B tiles when an average expert gets at most 64 rows of terms
     // (c2: ~3 tokens x 6 terms), otherwise 128
@@ -731,11 +731,31 @@ int prepare_mxfp4_scales(k3xb_ctx* ctx, const uint8_t* scales, size_t rows, size
     return relayout(ctx, scales, rows, static_cast<uint32_t>(cols), out);
 }
 
+uint32_t mxf4_default_terms(uint64_t assignments, uint32_t experts) {
+    // Few tokens per expert: the expert GEMM streams weights from HBM and the
+    // MMA has slack, so the exact 6-term split costs nothing. From 12 tokens
+    // per expert on, the operand and MMA work grow with the terms, and 4
+    // terms keep the outputs within the north-star tolerance.
+    const uint64_t avg = experts ? (assignments + experts - 1) / experts : 0;
+    return avg >= 12 ? 4u : 6u;
+}
+
+uint32_t resolve_terms(const k3xb_moe_layer& L, uint32_t T) {
+    return L.act_terms > 0 ? static_cast<uint32_t>(L.act_terms)
+                           : mxf4_default_terms(static_cast<uint64_t>(T) * L.top_k, L.experts);
+}
+
+// With the default term count either split may be chosen at launch (an
+// expert-parallel rank resolves it from the whole batch): room for both.
 size_t mxf4_scratch_bytes(const k3xb_moe_layer& L, uint32_t T) {
     if (L.engine != K3XB_ENGINE_MXF4) return 0;
-    Sizer s;
-    carve(s, layout_of(L, T), nullptr);
-    return s.used + 1024;
+    auto bytes = [&](uint32_t terms) {
+        Sizer s;
+        carve(s, layout_of(L, T, terms), nullptr);
+        return s.used;
+    };
+    const size_t need = L.act_terms > 0 ? bytes(static_cast<uint32_t>(L.act_terms)) : std::max(bytes(4), bytes(6));
+    return need + 1024;
 }
 
 void set_mxf4_scratch(k3xb_ctx* ctx, void* region) { ctx->mxf4_scratch = region; }
@@ -747,9 +767,9 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
     if (H % 128 || I % 128)
         return fail(ctx, K3XB_INVALID_EXTENT, "MXF4 engine needs hidden and inter multiples of 128");
     if (L.act_terms < 0 || L.act_terms > 16)
-        return fail(ctx, K3XB_INVALID_EXTENT, "act_terms must be in [1, 16] (0 = default 6)");
+        return fail(ctx, K3XB_INVALID_EXTENT, "act_terms must be in [1, 16] (0 = the library default)");
     if (L.experts > 1024) return fail(ctx, K3XB_INVALID_EXTENT, "MXF4 engine supports <= 1024 experts");
-    const Layout l = layout_of(L, T);
+    const Layout l = layout_of(L, T, resolve_terms(L, T));
     if (static_cast<uint64_t>(l.max_tiles) * l.nmax >= (1ull << 31))
         return fail(ctx, K3XB_INVALID_EXTENT, "MXF4 work list too large");
     int st;

@@ -194,6 +194,10 @@ int launch_rows(k3xb_ctx* ctx, const KdaArgs& a, uint32_t sequences) {
     const int cst = configure_once(ctx, configured, [&]() -> int {
         K3XB_CUDA(ctx, cudaFuncSetAttribute(kda_rows_kernel<D, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             static_cast<int>(smem)));
+        // the whole unified L1 as shared memory, so two blocks (each ~68 KB
+        // and 128 threads of ~230 registers) share an SM
+        K3XB_CUDA(ctx, cudaFuncSetAttribute(kda_rows_kernel<D, R>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                            cudaSharedmemCarveoutMaxShared));
         return K3XB_OK;
     });
     if (cst) return cst;

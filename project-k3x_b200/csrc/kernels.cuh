@@ -76,6 +76,9 @@ struct EpTarget {
 };
 // experts_tc.cu — tcgen05 block-scaled expert engine
 size_t mxf4_scratch_bytes(const k3xb_moe_layer& L, uint32_t T);
+// E2M1 activation terms when a layer leaves act_terms 0, from the whole
+// batch's assignments (tokens x top_k) and its experts
+uint32_t mxf4_default_terms(uint64_t assignments, uint32_t experts);
 void set_mxf4_scratch(k3xb_ctx* ctx, void* region);
 // slot_out [T*k][H] float, or bf16 words in slot_out16 when that is given, or
 // (expert parallel) the home ranks' windows; rows are floats, or bf16 words

@@ -224,6 +224,8 @@ def library() -> C.CDLL:
             fn.restype = C.c_int
         lib.k3xb_kda_trace_bytes.argtypes = [C.POINTER(KdaLayer), u32, u32]
         lib.k3xb_kda_trace_bytes.restype = sz
+        lib.k3xb_default_act_terms.argtypes = [u64, u32]
+        lib.k3xb_default_act_terms.restype = u32
         lib.k3xb_phase_name.argtypes = [C.c_int]
         lib.k3xb_phase_name.restype = C.c_char_p
         _lib = lib
@@ -660,7 +662,7 @@ class Context:
                                                     sigma), "fill_normal_mxfp4")
 
 
-def moe_layer_desc(w: dict, engine=ENGINE_SIMT, act_terms=6) -> MoeLayer:
+def moe_layer_desc(w: dict, engine=ENGINE_SIMT, act_terms=0) -> MoeLayer:
     """Builds the C descriptor from a dict of torch CUDA tensors + dims. The
     descriptor holds a reference to the dict, so the tensors it points at
     stay allocated as long as the descriptor object lives (a struct copied
@@ -688,12 +690,17 @@ def moe_layer_desc(w: dict, engine=ENGINE_SIMT, act_terms=6) -> MoeLayer:
     return L
 
 
+def default_act_terms(assignments: int, experts: int) -> int:
+    """The MXF4 engine's E2M1 term count for act_terms 0 (k3xb_default_act_terms)."""
+    return int(library().k3xb_default_act_terms(assignments, experts))
+
+
 def phase_name(i: int) -> str:
     n = library().k3xb_phase_name(i)
     return n.decode() if n else None
 
 
-def stack_layer_desc(stack: ResidentStack, w: dict, engine=ENGINE_MXF4, act_terms=6) -> MoeLayer:
+def stack_layer_desc(stack: ResidentStack, w: dict, engine=ENGINE_MXF4, act_terms=0) -> MoeLayer:
     """moe_layer_desc with the expert arrays taken from a resident stack
     (k3xb_acquire_expert_stack); router, correction and the shared expert
     still come from the dict."""
@@ -718,7 +725,7 @@ def kda_layer_desc(w: dict) -> KdaLayer:
     return K
 
 
-def layer_desc(w: dict, engine=ENGINE_MXF4, act_terms=6) -> Layer:
+def layer_desc(w: dict, engine=ENGINE_MXF4, act_terms=0) -> Layer:
     """C descriptor of a KDA + MoE layer: w["kda"], w["moe"] sub-dicts and
     the six [H] bf16 norm/projection vectors."""
     L = Layer()

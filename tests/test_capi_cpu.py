@@ -95,3 +95,14 @@ def test_draft_entry_point_rejects_null_context():
     lib = k3xb.library()
     io = k3xb.DraftIO(1, 1, 1, None, None, None, None)
     assert lib.k3xb_draft_greedy(None, C.byref(k3xb.VerifyModel()), C.byref(io)) == k3xb.INVALID_EXTENT
+
+
+def test_default_act_terms_rule():
+    """The MXF4 engine's default E2M1 term count (k3xb_default_act_terms, a
+    host function): exact 6 terms while experts see fewer than 12 tokens on
+    average, 4 from there on."""
+    import k3xb
+    assert k3xb.default_act_terms(64 * 16, 384) == 6       # c2: ~2.7 tokens per expert
+    assert k3xb.default_act_terms(144 * 16, 384) == 6      # c4: 6
+    assert k3xb.default_act_terms(576 * 16, 384) == 4      # c5: 24
+    assert k3xb.default_act_terms(11 * 384, 384) == 6 and k3xb.default_act_terms(12 * 384, 384) == 4

@@ -155,3 +155,35 @@ def test_mxf4_c2_shape_vs_oracle(torch, ctx, rs):
         assert_hidden_close(b[t], want, scale)
     del d
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("terms", [4, 5])
+@pytest.mark.parametrize("dims", [(256, 384, 8, 2, 100), (512, 256, 16, 8, 96)])
+def test_mxf4_fewer_terms_within_tolerance(torch, ctx, rs, terms, dims):
+    """Fewer E2M1 terms per activation row (cheaper large-M tiles) against
+    the FP64 oracle at ~25-48 rows per expert: within the north-star
+    tolerance (rel 2e-2 / abs 1e-3), with the bf16 rounding-point allowance
+    of assert_hidden_close."""
+    import k3xb
+    H, I, E, K, T = dims
+    layer = make_moe_layer(rs, H + I + terms, hidden=H, inter=I, experts=E, top_k=K, shared_inter=128)
+    hidden = bf16_normal(np.random.default_rng(H + T), (T, H))
+    d = layer_to_dev(torch, layer)
+    got, ids = _run(torch, ctx, d, to_dev(torch, hidden), T, k3xb.ENGINE_MXF4, terms)
+    want, want_ids, _ = rs.moe_layer(layer, hidden)
+    np.testing.assert_array_equal(ids, want_ids)
+    assert_hidden_close(got, want, np.abs(want))
+
+
+def test_mxf4_library_default_terms_at_large_m(torch, ctx, rs):
+    """act_terms 0 (the library default) at ~25 rows per expert resolves to
+    4 terms and stays within the north-star tolerance of the FP64 oracle."""
+    import k3xb
+    H, I, E, K, T = 256, 384, 8, 2, 100
+    assert k3xb.default_act_terms(T * K, E) == 4
+    layer = make_moe_layer(rs, 77, hidden=H, inter=I, experts=E, top_k=K, shared_inter=128)
+    hidden = bf16_normal(np.random.default_rng(78), (T, H))
+    got, ids = _run(torch, ctx, layer_to_dev(torch, layer), to_dev(torch, hidden), T, k3xb.ENGINE_MXF4, 0)
+    want, want_ids, _ = rs.moe_layer(layer, hidden)
+    np.testing.assert_array_equal(ids, want_ids)
+    assert_hidden_close(got, want, np.abs(want))
