@@ -705,15 +705,15 @@ int launch_routed(k3xb_ctx* ctx, const CUtensorMap& map_gate, const CUtensorMap&
         gateup_kernel<NM><<<ctx->sm_count, kThreads, smem_gu, ctx->stream>>>(map_gate, map_up, map_bgu, gp);
         K3XB_LAUNCHED(ctx);
     }
+    // the down projection's phase: its operand from the activation rows, then the GEMM
+    PhaseScope ph(ctx, K3XB_PHASE_EXPERT_DOWN);
     {
-        PhaseScope ph(ctx, K3XB_PHASE_EXPERT_PREP);
         // one thread per (token, 32-block) of a tile
         const uint32_t per_tile = (sa.tpt * (sa.I / 32) + 255u) / 256u;
         split_act_kernel<<<dim3(per_tile, sa.max_tiles), 256, 0, ctx->stream>>>(sa.act, sa.tb, sa.I, sa.terms, sa.tpt,
                                                                                sa.nmax, sa.b, sa.sfb);
         K3XB_LAUNCHED(ctx);
     }
-    PhaseScope ph(ctx, K3XB_PHASE_EXPERT_DOWN);
     down_kernel<NM><<<ctx->sm_count, kThreads, smem_d, ctx->stream>>>(map_down, map_bd, dp);
     K3XB_LAUNCHED(ctx);
     return K3XB_OK;
