@@ -46,18 +46,26 @@ using tcp::kAtomBytes;
 using tcp::kBlockM;
 using tcp::kThreads;
 
-// B-tile height NM (activation rows = tokens x terms per tile) is 64 or 128.
+// B-tile height NM (activation rows = tokens x terms per tile) is 64 or 112.
 // With few tokens per expert (c2: ~3) a 64-row B slot leaves room for more
 // weight stages in shared memory — bytes in flight are what bound an
-// HBM-streaming GEMM — and for a double-buffered gate/up accumulator.
+// HBM-streaming GEMM. Both keep the two accumulators (gate and up, or the
+// down projection's two weight tiles) double-buffered in TMEM, so the MMAs
+// of one item overlap the epilogue of the previous one and the weight
+// stream never waits for an epilogue: 112 is the widest N for which two
+// buffers of two accumulators and the 24 block-scale columns fit in 512.
+// TMEM columns (buffer b adds b * kStrideGU): accumulator 0 at 0,
+// accumulator 1 at kColUp; block scales of A0, A1 and B at kColSf*.
 template <uint32_t NM> struct RoutedCfg;
 template <> struct RoutedCfg<64> {
     static constexpr uint32_t kStagesGU = 5, kAccbGU = 2;
     static constexpr uint32_t kColUp = 64, kStrideGU = 128;
+    static constexpr uint32_t kColSfa0 = 256, kColSfa1 = 264, kColSfb = 272;
 };
-template <> struct RoutedCfg<128> {
-    static constexpr uint32_t kStagesGU = 4, kAccbGU = 1;
-    static constexpr uint32_t kColUp = 128, kStrideGU = 0;
+template <> struct RoutedCfg<112> {
+    static constexpr uint32_t kStagesGU = 4, kAccbGU = 2;
+    static constexpr uint32_t kColUp = 128, kStrideGU = 256;
+    static constexpr uint32_t kColSfa0 = 112, kColSfa1 = 240, kColSfb = 368;   // gaps after N <= 112
 };
 constexpr uint32_t kStagesGU = 4;   // shared expert (kind::f16) pipelines
 constexpr uint32_t kStagesD = 6;
@@ -321,9 +329,9 @@ struct DParams {
     EpTarget ep;              // when ep.world: rows go straight to their home ranks' windows
 };
 
-// TMEM columns. Routed gate/up: gate accumulator at 0, up at RoutedCfg::kColUp,
-// second buffer (NM = 64) kStrideGU further; block scales from 256.
-constexpr uint32_t kColAccGate = 0, kColAccUp = 128, kColSfaGate = 256, kColSfaUp = 264, kColSfbGU = 272;
+// TMEM columns of the accumulators (routed: RoutedCfg; shared expert: gate
+// at 0, up at 128).
+constexpr uint32_t kColAccGate = 0, kColAccUp = 128;
 
 template <uint32_t NM>
 __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_constant__ CUtensorMap map_gate,
@@ -366,8 +374,8 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_consta
         }
     };
     const uint8_t* sfa[2] = {p.sfa_gate, p.sfa_up};
-    const tcp::Config cfg{p.H, *p.n_items, 512, kColAccGate, RC::kColUp, RC::kStrideGU, kColSfaGate, kColSfaUp,
-                          kColSfbGU, 0, NM};
+    const tcp::Config cfg{p.H, *p.n_items, 512, kColAccGate, RC::kColUp, RC::kStrideGU, RC::kColSfa0, RC::kColSfa1,
+                          RC::kColSfb, 0, NM};
     tcp::run_pipeline<RC::kStagesGU, 2, false, RC::kAccbGU>(sm, &map_gate, &map_up, &map_b, cfg, sfa, p.sfb,
                                                             p.error, get_desc, epilogue);
 }
@@ -444,8 +452,8 @@ __global__ void __launch_bounds__(kThreads, 1) down_kernel(const __grid_constant
         }
     };
     const uint8_t* sfa[2] = {p.sfa, p.sfa};
-    const tcp::Config cfg{p.I, *p.n_items, 512, kColAccGate, RC::kColUp, RC::kStrideGU, kColSfaGate, kColSfaUp,
-                          kColSfbGU, kBlockM, NM, p.rowblocks};
+    const tcp::Config cfg{p.I, *p.n_items, 512, kColAccGate, RC::kColUp, RC::kStrideGU, RC::kColSfa0, RC::kColSfa1,
+                          RC::kColSfb, kBlockM, NM, p.rowblocks};
     tcp::run_pipeline<RC::kStagesGU, 2, false, RC::kAccbGU>(sm, &map_down, &map_down, &map_b, cfg, sfa, p.sfb,
                                                             p.error, get_desc, epilogue);
     // Expert parallel: the last CTA to finish tells every home rank that this
@@ -628,9 +636,9 @@ Layout layout_of(const k3xb_moe_layer& L, uint32_t T, uint32_t terms) {
     l.terms = terms;
     const uint32_t assigns = T * L.top_k;
     // 64-row B tiles when an average expert gets at most 64 rows of terms
-    // (c2: ~3 tokens x 6 terms), otherwise 128
+    // (c2: ~3 tokens x 6 terms), otherwise 112
     const uint32_t avg_rows = (assigns + L.experts - 1) / L.experts * l.terms;
-    l.nmax = (avg_rows <= 64 && l.terms <= 64) ? 64u : 128u;
+    l.nmax = (avg_rows <= 64 && l.terms <= 64) ? 64u : 112u;
     l.tpt = l.nmax / l.terms;
     l.max_tiles = std::min(L.experts, assigns) + (assigns + l.tpt - 1) / l.tpt;
     l.mt_gu = L.inter / kBlockM;
@@ -813,7 +821,7 @@ int launch_mxf4_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
                H, I, l.terms, L.top_k, ctx->status_word, static_cast<uint32_t>(static_cast<size_t>(L.experts) * H / kBlockM),
                slot_out16, ep ? *ep : EpTarget{}};
     return l.nmax == 64 ? launch_routed<64>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, sa, dp)
-                        : launch_routed<128>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, sa, dp);
+                        : launch_routed<112>(ctx, map_gate, map_up, map_bgu, map_down, map_bd, gp, sa, dp);
 }
 
 int launch_shared_tc(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidden, uint32_t T, uint16_t* xb,
