@@ -141,6 +141,14 @@ int k3xb_route(k3xb_ctx* ctx, const float* hidden, uint32_t tokens,
                const float* correction, uint32_t experts, uint32_t top_k,
                uint32_t* ids, float* contributions, float* scores);
 
+/* The logits of route_official_moe alone (official_moe.cpp:255-267): the
+ * [T][E] floats k3xb_route feeds to its Top-k, for a caller that routes them
+ * itself (route_official_moe_logits, official_moe.cpp:211-245, takes
+ * them). Bit-identical to the reference's sequential double sums. */
+int k3xb_router_logits(k3xb_ctx* ctx, const float* hidden, uint32_t tokens,
+                       uint32_t hidden_size, const uint16_t* router,
+                       uint32_t experts, float* logits);
+
 /* Same routing as k3xb_route for callers that may not allocate device
  * memory while they run (a serving loop that reserved all of HBM up front,
  * an application whose own allocator owns the device, a latency-critical

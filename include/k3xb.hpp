@@ -40,6 +40,9 @@ enum class Status : int {
     unsupported_architecture = K3XB_UNSUPPORTED_ARCHITECTURE,
 };
 
+// The C ABI counts in uint32_t; a larger host count is an extent error, not a wrap.
+constexpr bool fits_u32(std::size_t n) noexcept { return n <= 0xffffffffull; }
+
 inline const char* status_name(Status s) noexcept {
     switch (s) {
         case Status::ok: return "OK";
@@ -162,7 +165,8 @@ public:
                   std::span<const float> correction, std::uint32_t top_k, std::span<std::uint32_t> ids,
                   std::span<float> contributions) {
         const auto E = static_cast<std::uint32_t>(correction.size());
-        if (!hidden_size || hidden.size() % hidden_size || router.size() != std::size_t(E) * hidden_size)
+        if (!hidden_size || hidden.size() % hidden_size || router.size() != std::size_t(E) * hidden_size ||
+            !fits_u32(correction.size()) || !fits_u32(hidden.size() / hidden_size))
             return Outcome(Status::invalid_extent, "route: sizes");
         const auto T = static_cast<std::uint32_t>(hidden.size() / hidden_size);
         if (ids.size() != std::size_t(T) * top_k || contributions.size() != ids.size())
@@ -213,13 +217,15 @@ public:
     // out, device weights): each returns after its results are on the host.
     // f32 dense product (dense_matvec), bit-identical to the CPU backend.
     Outcome dense_matvec(const float* W, std::uint32_t rows, std::span<const float> x, std::span<float> y) {
-        if (y.size() != rows || x.empty()) return Outcome(Status::invalid_extent, "dense_matvec: sizes");
+        if (y.size() != rows || x.empty() || !fits_u32(x.size()))
+            return Outcome(Status::invalid_extent, "dense_matvec: sizes");
         return check(k3xb_dense_matvec_host(h_, W, rows, static_cast<std::uint32_t>(x.size()), x.data(), y.data()));
     }
     // MXFP4 product (mxfp4_matvec), bit-identical to mxfp4_matmul.
     Outcome mxfp4_matvec(const std::uint8_t* packed, const std::uint8_t* scales, std::uint32_t rows,
                          std::span<const float> x, std::span<float> y) {
-        if (y.size() != rows || x.empty()) return Outcome(Status::invalid_extent, "mxfp4_matvec: sizes");
+        if (y.size() != rows || x.empty() || !fits_u32(x.size()))
+            return Outcome(Status::invalid_extent, "mxfp4_matvec: sizes");
         return check(k3xb_mxfp4_matvec_host(h_, packed, scales, rows, static_cast<std::uint32_t>(x.size()), x.data(),
                                             y.data()));
     }
@@ -228,21 +234,30 @@ public:
     Outcome official_moe_ffn(const k3xb_moe_layer& tail, std::span<const k3xb_moe_layer> slots,
                              std::span<const float> contributions, std::span<const float> hidden,
                              std::span<const float> prefix, std::span<float> out) {
-        if (slots.size() != contributions.size() || hidden.size() != tail.hidden || prefix.size() != tail.hidden ||
-            out.size() != tail.hidden)
+        if (slots.size() != contributions.size() || !fits_u32(slots.size()) || hidden.size() != tail.hidden ||
+            prefix.size() != tail.hidden || out.size() != tail.hidden)
             return Outcome(Status::invalid_extent, "official_moe_ffn: sizes");
         return check(k3xb_official_moe_ffn_host(h_, &tail, slots.data(), static_cast<std::uint32_t>(slots.size()),
                                                 contributions.data(), hidden.data(), prefix.data(), out.data()));
     }
     // The KDA block with its state held on the device between calls
     // (official_kda's device state modes); conv/recurrent as k3xb_kda_block_held.
+    // conv is [3][conv_width - 1][heads * head_dim] bf16 words and recurrent
+    // [heads][head_dim][head_dim]: SEED reads them and PUBLISH writes them,
+    // so there both must have exactly those sizes; CONTINUE ignores them.
     Outcome kda_block_held(const k3xb_kda_layer& w, std::uint32_t hidden, std::span<const float> x,
-                           std::uint32_t slot, std::int32_t mode, std::uint16_t* conv, float* recurrent,
-                           std::span<float> out) {
-        if (!hidden || x.size() % hidden || out.size() != x.size())
+                           std::uint32_t slot, std::int32_t mode, std::span<std::uint16_t> conv,
+                           std::span<float> recurrent, std::span<float> out) {
+        if (!hidden || x.size() % hidden || out.size() != x.size() || !fits_u32(x.size() / hidden))
             return Outcome(Status::invalid_extent, "kda_block_held: sizes");
+        const std::size_t width = std::size_t(w.heads) * w.head_dim;
+        const std::size_t conv_n = w.conv_width ? 3 * std::size_t(w.conv_width - 1) * width : 0;
+        const std::size_t rec_n = width * w.head_dim;
+        if (mode != K3XB_KDA_CONTINUE && (conv.size() != conv_n || recurrent.size() != rec_n))
+            return Outcome(Status::invalid_extent, "kda_block_held: state sizes");
         return check(k3xb_kda_block_held(h_, &w, hidden, x.data(), static_cast<std::uint32_t>(x.size() / hidden),
-                                         slot, mode, conv, recurrent, out.data()));
+                                         slot, mode, conv.empty() ? nullptr : conv.data(),
+                                         recurrent.empty() ? nullptr : recurrent.data(), out.data()));
     }
 
 private:

@@ -401,6 +401,17 @@ int k3xb_route(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_t H, const
     return K3XB_OK;
 }
 
+int k3xb_router_logits(k3xb_ctx* ctx, const float* hidden, uint32_t T, uint32_t H, const uint16_t* router,
+                       uint32_t E, float* logits) {
+    K3XB_ENTER(ctx);
+    if (!T || !H || !E || !hidden || !router || !logits) return fail(ctx, K3XB_INVALID_EXTENT, "router_logits arguments");
+    PhaseScope ph(ctx, K3XB_PHASE_ROUTE);
+    const int st = launch_router_logits(ctx, hidden, T, H, router, E, logits);
+    if (st) return st;
+    ++ctx->stats.route_calls;
+    return K3XB_OK;
+}
+
 int k3xb_select_routing(k3xb_ctx* ctx, const float* scores, uint32_t T, uint32_t E, const float* bias, uint32_t K,
                         const k3xb_routing_policy* policy, uint32_t* ids, float* weights, uint32_t* selected,
                         uint32_t* escalated, float* stats) {
@@ -1041,12 +1052,10 @@ int kda_block_device(k3xb_ctx* ctx, const k3xb_kda_layer& w, uint32_t H, const f
             xin = wk.xr;
         }
         if ((st = launch_split_terms(ctx, xin, T, H, 1, wk.xt_h))) return st;
-        if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.q_proj, T, P, H, 1, tr.pq))) return st;
-        if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.k_proj, T, P, H, 1, tr.pk))) return st;
-        if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.v_proj, T, P, H, 1, tr.pv))) return st;
-        if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.g_proj, T, P, H, 1, wk.og))) return st;
-        if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.f_a_proj, T, d, H, 1, wk.fl))) return st;
-        if ((st = launch_linear_terms(ctx, wk.xt_h, 1, w.b_proj, T, h, H, 1, wk.bp))) return st;
+        // the six input projections of official_kda.cpp:228-245 in one launch
+        const LinearJob jobs[6] = {{w.q_proj, P, tr.pq}, {w.k_proj, P, tr.pk},  {w.v_proj, P, tr.pv},
+                                   {w.g_proj, P, wk.og}, {w.f_a_proj, d, wk.fl}, {w.b_proj, h, wk.bp}};
+        if ((st = launch_linear_group(ctx, wk.xt_h, 1, T, H, jobs, 6, 1))) return st;
         if ((st = launch_split_terms(ctx, wk.fl, T, d, 1, wk.xt_d))) return st;
         if ((st = launch_linear_terms(ctx, wk.xt_d, 1, w.f_b_proj, T, P, d, 1, wk.fg))) return st;
     }

@@ -99,6 +99,14 @@ int launch_linear_bf16(k3xb_ctx* ctx, const float* x, const uint16_t* W, uint32_
 int launch_split_terms(k3xb_ctx* ctx, const float* x, uint32_t T, uint32_t K, uint32_t terms, uint16_t* xterms);
 int launch_linear_terms(k3xb_ctx* ctx, const uint16_t* xterms, uint32_t terms, const uint16_t* W, uint32_t T,
                         uint32_t rows, uint32_t K, int round_out, float* out);
+// up to 8 products of the same split x in one launch: out_j[T][rows_j] = W_j . x
+struct LinearJob {
+    const uint16_t* W;   // [rows][K] bf16 words
+    uint32_t rows;
+    float* out;
+};
+int launch_linear_group(k3xb_ctx* ctx, const uint16_t* xterms, uint32_t terms, uint32_t T, uint32_t K,
+                        const LinearJob* jobs, uint32_t njobs, int round_out);
 // dense.cu — f32 dense products in the reference CPU backend's FP64 column order
 int launch_dense_matvec(k3xb_ctx* ctx, const float* W, uint32_t rows, uint32_t cols, const float* x, uint32_t T,
                         float* y);

@@ -9,7 +9,8 @@
 // (kind::f16); each MMA consumes 32 bytes of every row.
 //
 // Work items are 16-byte descriptors {a_row, b_row, n | ntok << 16, aux}
-// produced by `get_desc(item)`; every role prefetches the next item's
+// produced by `get_desc(item)` (with Config::a_maps > 1 the top 4 bits of
+// a_row pick one of several A0 tensor maps); every role prefetches the next item's
 // descriptor while it works on the current one. With ACCB = 2 the TMEM
 // accumulator is double-buffered so the MMA of item i+1 overlaps the
 // epilogue of item i.
@@ -62,7 +63,16 @@ struct Config {
     uint32_t a1_row_off = 0;          // A1 tile rows = A0 rows + a1_row_off (same tensor map allowed)
     uint32_t b_box = 16;              // B rows per TMA box (the B tensor map's box height)
     uint32_t a_rowblocks = 0xffffffffu;   // 128-row scale blocks of A (clamps the A1 scale row)
+    uint32_t a_maps = 1;              // A0 tensor maps at map_a0[0 .. a_maps): item map = a_row >> 28
 };
+
+// A descriptor's A0 row, and which of the cfg.a_maps A0 tensor maps it is in.
+__device__ __forceinline__ uint32_t desc_a_row(const uint4& d, const Config& c) {
+    return c.a_maps > 1 ? (d.x & 0x0fffffffu) : d.x;
+}
+__device__ __forceinline__ uint32_t desc_a_map(const uint4& d, const Config& c) {
+    return c.a_maps > 1 ? (d.x >> 28) : 0u;
+}
 
 __device__ __forceinline__ uint32_t desc_n(const uint4& d) { return d.z & 0xffffu; }
 __device__ __forceinline__ uint32_t desc_ntok(const uint4& d) { return d.z >> 16; }
@@ -103,14 +113,15 @@ __device__ __forceinline__ void run_pipeline(Smem<S, NA, BROWS>& sm, const CUten
 
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer ----------------
-        tc::prefetch_tensormap(map_a0);
+        for (uint32_t m = 0; m < cfg.a_maps; ++m) tc::prefetch_tensormap(map_a0 + m);
         if (NA == 2) tc::prefetch_tensormap(map_a1);
         tc::prefetch_tensormap(map_b);
         uint32_t it = 0;
         uint4 d = blockIdx.x < n_items ? get_desc(blockIdx.x) : make_uint4(0, 0, 0, 0);
         for (uint32_t item = blockIdx.x; item < n_items && !*abort; item += stride) {
             const uint4 nd = item + stride < n_items ? get_desc(item + stride) : d;
-            const uint32_t a_row = d.x, b_row = d.y, n = desc_n(d);
+            const uint32_t a_row = desc_a_row(d, cfg), b_row = d.y, n = desc_n(d);
+            const CUtensorMap* ma0 = map_a0 + desc_a_map(d, cfg);
             for (uint32_t s = 0; s < ksteps; ++s, ++it) {
                 const uint32_t st = it % S, ph = (it / S) & 1u;
                 if (!tc::mbar_wait(&sm.empty[st], ph ^ 1u, abort)) break;
@@ -119,7 +130,7 @@ __device__ __forceinline__ void run_pipeline(Smem<S, NA, BROWS>& sm, const CUten
                 const uint32_t bytes = NA * kTileBytes + b_loads * cfg.b_box * 128u + (NA + 1) * atoms * kAtomBytes;
                 tc::mbar_arrive_expect_tx(&sm.full[st], bytes);
                 const int x = static_cast<int>(s * 128u);
-                tc::tma_load_2d(sm.a[0][st], map_a0, &sm.full[st], x, static_cast<int>(a_row));
+                tc::tma_load_2d(sm.a[0][st], ma0, &sm.full[st], x, static_cast<int>(a_row));
                 if (NA == 2)
                     tc::tma_load_2d(sm.a[NA - 1][st], map_a1, &sm.full[st], x, static_cast<int>(a_row + cfg.a1_row_off));
                 for (uint32_t r = 0; r < b_loads; ++r)

@@ -168,6 +168,7 @@ def library() -> C.CDLL:
             "k3xb_sync": [vp],
             "k3xb_get_stats": [vp, C.POINTER(Stats)],
             "k3xb_route": [vp, vp, u32, u32, vp, vp, u32, u32, vp, vp, vp],
+            "k3xb_router_logits": [vp, vp, u32, u32, vp, u32, vp],
             "k3xb_expert_major_plan": [vp, vp, vp, u32, u32, u32, C.POINTER(Plan)],
             "k3xb_select_routing": [vp, vp, u32, u32, vp, u32, C.POINTER(RoutingPolicy), vp, vp, vp, vp, vp],
             "k3xb_moe_layer_forward": [vp, C.POINTER(MoeLayer), vp, u32, vp, vp, vp],
@@ -297,6 +298,11 @@ class Context:
         E = router.shape[0]
         self._check(self.lib.k3xb_route(self.h, _p(hidden), T, H, _p(router), _p(correction), E, top_k,
                                         _p(ids), _p(contrib), _p(scores)), "route")
+
+    def router_logits(self, hidden, router, logits):
+        T, H = hidden.shape
+        self._check(self.lib.k3xb_router_logits(self.h, _p(hidden), T, H, _p(router), router.shape[0],
+                                                _p(logits)), "router_logits")
 
     def expert_major_plan(self, ids, contrib, experts, plan: dict):
         T, K = ids.shape

@@ -88,7 +88,17 @@ int main() {
     CHECK(none.dense_matvec(nullptr, 4, x, y4).status() == k3xb::Status::invalid_extent);
     CHECK(none.mxfp4_matvec(nullptr, nullptr, 4, x, y).status() == k3xb::Status::invalid_extent);
     k3xb_kda_layer w{};
-    CHECK(none.kda_block_held(w, 3, x, 0, K3XB_KDA_SEED, nullptr, nullptr, y).status() ==
+    CHECK(none.kda_block_held(w, 3, x, 0, K3XB_KDA_SEED, {}, {}, y).status() == k3xb::Status::invalid_extent);
+    // a seed or publish must bring state arrays of the layer's sizes
+    w.heads = 2;
+    w.head_dim = 4;
+    w.conv_width = 4;
+    std::vector<std::uint16_t> conv(3 * 3 * 8), conv_short(3 * 3 * 8 - 1);
+    std::vector<float> rec(2 * 4 * 4), y9(9);
+    const std::vector<float> x9(9, 1.0F);
+    CHECK(none.kda_block_held(w, 3, x9, 0, K3XB_KDA_SEED, conv_short, rec, y9).status() ==
+          k3xb::Status::invalid_extent);
+    CHECK(none.kda_block_held(w, 3, x9, 0, K3XB_KDA_PUBLISH, conv, {}, y9).status() ==
           k3xb::Status::invalid_extent);
 
     // no B200 here: creation must fail with a status, never fall back

@@ -59,6 +59,51 @@ def test_route_parity(torch, ctx, rs, T, E, H, K):
         assert abs(gc[0, 0] - 0.6497964859) <= 1e-6
 
 
+# (T, E, H): token counts that pick each logits kernel on a 148-SM B200 (the
+# TMA kernel with 1, 2 and 4 tokens per thread; the register-blocked kernel
+# with 2 x 2 and 4 x 2 chains per thread), ragged tiles (E % 32, T % 16 and
+# H % 64 nonzero) and rows that are not 16-byte multiples or H % 64 != 0
+# (the element-wise kernel).
+@pytest.mark.parametrize("T,E,H", [(1, 384, 7168), (64, 384, 7168), (144, 384, 7168), (300, 384, 7168),
+                                   (576, 384, 7168), (2400, 100, 1032), (1500, 100, 1032), (577, 100, 1032),
+                                   (1, 7, 1032), (9, 7, 1032), (9, 7, 1030)])
+def test_router_logits_bit_exact(torch, ctx, rs, T, E, H):
+    g = np.random.default_rng(7 * T + E)
+    router = bf16_words(g.normal(0, 0.02, size=(E, H)))
+    hidden = g.normal(0, 1.0, size=(T, H)).astype(np.float32)   # any float: double(w) * x is exact
+    out = torch.empty((T, E), dtype=torch.float32, device="cuda")
+    ctx.router_logits(to_dev(torch, hidden), to_dev(torch, router), out)
+    ctx.sync()
+    got = from_dev(out, np.float32)
+    for t in range(T):
+        want = rs.router_logits(hidden[t], router)
+        assert np.array_equal(got[t].view(np.uint32), want.view(np.uint32)), f"token {t}: logits differ"
+
+
+@pytest.mark.parametrize("T,E", [(3, 96), (64, 96), (576, 384), (2400, 100)])
+def test_router_logits_zeros_and_subnormals(torch, ctx, rs, T, E):
+    """The kernels build each double from the float's fields; zeros (both
+    signs) and subnormal weights and hidden values must stay exact."""
+    H = 1024
+    g = np.random.default_rng(5 + T)
+    router = bf16_words(g.normal(0, 0.02, size=(E, H)))
+    hidden = g.normal(0, 1.0, size=(T, H)).astype(np.float32)
+    specials_w = np.array([0x0000, 0x8000, 0x0001, 0x8001, 0x007F, 0x807F, 0x0040, 0x0080, 0x8080], np.uint16)
+    specials_x = np.array([0.0, -0.0, 1e-45, -1e-45, 1.1754942e-38, 3e-39, -5e-40, 1.1754944e-38],
+                          np.float32)
+    wi = g.integers(0, E * H, size=4000)
+    router.reshape(-1)[wi] = specials_w[g.integers(0, specials_w.size, size=wi.size)]
+    xi = g.integers(0, T * H, size=max(T * 40, 50))
+    hidden.reshape(-1)[xi] = specials_x[g.integers(0, specials_x.size, size=xi.size)]
+    out = torch.empty((T, E), dtype=torch.float32, device="cuda")
+    ctx.router_logits(to_dev(torch, hidden), to_dev(torch, router), out)
+    ctx.sync()
+    got = from_dev(out, np.float32)
+    for t in range(T):
+        want = rs.router_logits(hidden[t], router)
+        assert np.array_equal(got[t].view(np.uint32), want.view(np.uint32)), f"token {t}: logits differ"
+
+
 def test_route_ties_lower_index(torch, ctx):
     router = np.zeros((8, 64), np.uint16)
     hidden = np.zeros((2, 64), np.float32)
