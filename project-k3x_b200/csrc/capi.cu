@@ -243,12 +243,19 @@ int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidd
         if ((st = launch_linear_bf16(ctx, hidden, L.routed_down, T, D, H, 1, s.xt, s.lat))) return st;
         xe = s.lat;
     }
+    // the MXF4 engine stores its bf16-rounded expert rows as bf16 words (in
+    // the slot_out region): half the bytes written and read by the combine
+    uint16_t* y16 = L.engine == K3XB_ENGINE_MXF4 ? reinterpret_cast<uint16_t*>(s.slot_out) : nullptr;
     if (L.engine == K3XB_ENGINE_SIMT) {
         PhaseScope ph(ctx, K3XB_PHASE_EXPERT_GATEUP);
         if ((st = launch_simt_experts(ctx, LE, xe, T, s.plan, s.act, s.slot_out))) return st;
     } else {
-        if ((st = launch_mxf4_experts(ctx, LE, xe, T, s.plan, s.slot_out))) return st;
+        if ((st = launch_mxf4_experts(ctx, LE, xe, T, s.plan, nullptr, y16))) return st;
     }
+    auto combine = [&](const float* sh, uint32_t width, float* dst) {
+        return y16 ? launch_combine16(ctx, y16, contrib, sh, T, K, width, dst)
+                   : launch_combine(ctx, s.slot_out, contrib, sh, T, K, width, dst);
+    };
     const float* shared = nullptr;
     if (L.shared_gate && L.engine == K3XB_ENGINE_MXF4) {
         // the shared expert depends on the hidden rows only: it runs on the
@@ -269,7 +276,7 @@ int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidd
     if (L.latent) {
         {   // :313-322: mixed = round_bf16(slot-ordered combine), in the latent width
             PhaseScope ph(ctx, K3XB_PHASE_COMBINE);
-            if ((st = launch_combine(ctx, s.slot_out, contrib, nullptr, T, K, D, s.mixed))) return st;
+            if ((st = combine(nullptr, D, s.mixed))) return st;
         }
         // :323-331: routed = bf16_matvec(normalized(mixed, routed_norm), routed_up); then
         // :336 combined = round_bf16(routed + shared)
@@ -281,7 +288,7 @@ int moe_forward_device(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hidd
         if (st) return st;
     } else {
         PhaseScope ph(ctx, K3XB_PHASE_COMBINE);
-        if ((st = launch_combine(ctx, s.slot_out, contrib, shared, T, K, H, out))) return st;
+        if ((st = combine(shared, H, out))) return st;
     }
     ++ctx->stats.moe_layer_calls;
     return K3XB_OK;

@@ -183,6 +183,25 @@ __global__ void combine_kernel(const float* __restrict__ slot_out, const float* 
     out[i] = round_bf16(__fadd_rn(mixed, sh));
 }
 
+// The same combine over bf16 expert rows: the MXF4 engine's down epilogue
+// already rounds each row to bf16 (official_moe.cpp:101), so the words hold
+// the rows exactly at half the bytes.
+__global__ void combine16_kernel(const uint16_t* __restrict__ y, const float* __restrict__ contrib,
+                                 const float* __restrict__ shared, uint32_t T, uint32_t K, uint32_t H,
+                                 float* __restrict__ out) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<size_t>(T) * H) return;
+    const size_t t = i / H, h = i % H;
+    float mixed = 0.0f;
+    for (uint32_t s = 0; s < K; ++s) {
+        const float v = __uint_as_float(static_cast<uint32_t>(y[(t * K + s) * H + h]) << 16);
+        mixed = __fadd_rn(mixed, __fmul_rn(contrib[t * K + s], v));
+    }
+    mixed = round_bf16(mixed);
+    const float sh = shared ? shared[i] : 0.0f;
+    out[i] = round_bf16(__fadd_rn(mixed, sh));
+}
+
 // bf16 matvec for T tokens (official_moe.cpp:39-59 semantics with FP32
 // accumulation): out[t][r] = round_bf16(sum_k W[r][k] * x[t][k]). One warp
 // per (row, 4 tokens); x may be any float.
@@ -245,6 +264,15 @@ int launch_combine(k3xb_ctx* ctx, const float* slot_out, const float* contrib, c
     const size_t n = static_cast<size_t>(T) * H;
     combine_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(
         slot_out, contrib, shared, T, K, H, out);
+    K3XB_LAUNCHED(ctx);
+    return K3XB_OK;
+}
+
+int launch_combine16(k3xb_ctx* ctx, const uint16_t* slot_out16, const float* contrib, const float* shared,
+                     uint32_t T, uint32_t K, uint32_t H, float* out) {
+    const size_t n = static_cast<size_t>(T) * H;
+    combine16_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, ctx->stream>>>(slot_out16, contrib, shared,
+                                                                                      T, K, H, out);
     K3XB_LAUNCHED(ctx);
     return K3XB_OK;
 }

@@ -23,6 +23,9 @@ int launch_simt_experts(k3xb_ctx* ctx, const k3xb_moe_layer& L, const float* hid
                         const k3xb_plan& plan, float* act_buf, float* slot_out);
 int launch_combine(k3xb_ctx* ctx, const float* slot_out, const float* contrib, const float* shared,
                    uint32_t T, uint32_t K, uint32_t H, float* out);
+// the same over bf16 expert rows [T*k][H]
+int launch_combine16(k3xb_ctx* ctx, const uint16_t* slot_out16, const float* contrib, const float* shared,
+                     uint32_t T, uint32_t K, uint32_t H, float* out);
 int launch_bf16_rows(k3xb_ctx* ctx, const float* x, const uint16_t* W, uint32_t T, uint32_t rows,
                      uint32_t cols, float* out);
 int launch_act(k3xb_ctx* ctx, const float* g, const float* u, size_t n, int act, float beta,

@@ -40,7 +40,7 @@ def ref():
 # reference's own layer drivers over the adapter), so that a run which stops at the first failure
 # stops at the lowest broken layer. Files not listed keep their place after
 # these; test_zz_no_alloc.py stays last.
-_GPU_ORDER = ["test_gpu_synth", "test_gpu_parity", "test_gpu_mxf4", "test_gpu_linear", "test_gpu_layer", "test_gpu_golden",
+_GPU_ORDER = ["test_gpu_synth", "test_gpu_parity", "test_gpu_mxf4", "test_gpu_linear", "test_gpu_layer", "test_gpu_golden", "test_gpu_c4_oracle",
               "test_gpu_routing_policy", "test_gpu_ep", "test_gpu_ep_verify", "test_gpu_latent", "test_gpu_draft", "test_gpu_host_io",
               "test_gpu_resident", "test_gpu_profile", "test_gpu_ep_failure", "test_gpu_reference_drivers"]
 
