@@ -218,6 +218,17 @@ def zipf_correction(cfg):
     return (ZIPF_SCALE * (perm + 1.0) ** -cfg["zipf"]).astype(np.float32)
 
 
+def ep_owner(cfg, world):
+    """The expert placement of an expert-parallel run: with a routing bias
+    (c5's Zipf), the experts dealt over the ranks by bias (k3xb_ep_balance),
+    so the hot experts of every layer (the bias is the same in each) land on
+    different ranks; otherwise contiguous ranges (None). Placement changes
+    no result."""
+    import k3xb
+    zc = zipf_correction(cfg)
+    return None if zc is None else k3xb.ep_balance(zc, world)
+
+
 def stack_tokens(cfg):
     import numpy as np
     return np.random.default_rng(cfg["seed"]).integers(0, cfg["vocab"], size=(cfg["sequences"], cfg["drafts"] + 1),
@@ -267,7 +278,7 @@ def gpu_moe(ctx, torch, cfg, seed, rank=0, world=1):
     if zc is not None:
         w["correction"] = torch.from_numpy(zc).cuda()
     if world > 1:
-        local = k3xb.ep_local_layer(w, rank, world)
+        local = k3xb.ep_local_layer(w, rank, world, owner=ep_owner(cfg, world))
         for k in ("gate_packed", "gate_scales", "up_packed", "up_scales", "down_packed", "down_scales"):
             local[k] = local[k].clone()
         w = local
@@ -534,8 +545,9 @@ def stack_config(cfg, world):
             "shared_inter": cfg["shared_inter"], "heads": cfg["heads"], "head_dim": cfg["head_dim"],
             "sequences_x_drafts": f"{S}x{cfg['drafts']}", "verify_positions": S * (cfg["drafts"] + 1),
             "layers": L, "vocab": cfg["vocab"], "seed": cfg["seed"],
-            "parallelism": (f"expert parallel x{world} (experts {cfg['experts'] // world} per GPU, "
-                            f"{S // world} sequences per GPU, peer-memory exchange)") if world > 1 else "single GPU",
+            "parallelism": (f"expert parallel x{world} (experts {cfg['experts'] // world} per GPU"
+                            + (", dealt by routing bias (k3xb_ep_balance)" if cfg.get("zipf") else "")
+                            + f", {S // world} sequences per GPU, peer-memory exchange)") if world > 1 else "single GPU",
             "l2": "no flush: each step streams tens of GB of weights (>> 126 MB L2)"}
 
 

@@ -263,6 +263,15 @@ typedef struct {
     const uint16_t* routed_norm;   /* [L] bf16 */
     const uint16_t* routed_up;     /* [H][L] bf16 */
     float latent_eps;
+    /* Expert placement for the expert-parallel entry points (device array
+     * [experts_total], or NULL): entry e = rank << 16 | local, the rank that
+     * holds expert e and its index in that rank's stacks. Every (rank,
+     * local) with rank < world and local < E / world appears exactly once.
+     * NULL: rank r holds experts [r*E/world, (r+1)*E/world) in order.
+     * Placement moves no result: the outputs are bit-identical for any
+     * table (k3xb_ep_balance makes one from expected loads). Ignored by the
+     * one-GPU entry points. */
+    const uint32_t* ep_owner;
 } k3xb_moe_layer;
 
 /* bf16_matvec (runtime/src/official_moe.cpp:39-59) for many tokens on
@@ -808,7 +817,8 @@ int k3xb_ep_abort(k3xb_ctx* ctx);
 /* Drains the stream (bounded), then frees the communicator. */
 int k3xb_ep_finalize(k3xb_ctx* ctx);
 /* The MoE layer of k3xb_moe_layer_forward with the routed experts sharded:
- * this rank holds experts [rank*E/world, (rank+1)*E/world) in `local`
+ * this rank holds experts [rank*E/world, (rank+1)*E/world) in `local` (or,
+ * with local->ep_owner, the experts that table gives this rank)
  * (local->experts == E / world; router [E][H], correction [E] and the shared
  * expert are the full, replicated ones) and `tokens` tokens of its own
  * sequences, the same count on every rank. Each rank owns an exchange
@@ -838,6 +848,16 @@ int k3xb_ep_moe_layer_forward(k3xb_ctx* ctx, const k3xb_moe_layer* local,
  * one box of GPUs; every rank calls it with the same shapes (a collective). */
 int k3xb_ep_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* model,
                         const k3xb_verify_io* io, uint32_t experts_total);
+
+/* An expert placement for k3xb_moe_layer.ep_owner (HOST arrays, no
+ * context): experts dealt in descending order of `load` (any expected
+ * per-expert work, e.g. routing counts or the routing bias) over `world`
+ * ranks in a snake (ranks 0..world-1, then world-1..0, ...), so the
+ * heaviest experts land on different ranks and every rank gets
+ * experts / world of them. Ties keep the lower expert id first. owner[e] =
+ * rank << 16 | index in that rank's stacks (ascending order of dealing).
+ * No counterpart in the reference (one process, one GPU). */
+int k3xb_ep_balance(const float* load, uint32_t experts, uint32_t world, uint32_t* owner);
 
 /* ---- (e) acceptance ------------------------------------------------------- */
 /* verify_greedy_target_block (runtime/src/speculative.cpp:74-112) for S

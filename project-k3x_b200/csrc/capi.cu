@@ -1,4 +1,5 @@
 // capi.cu — the extern "C" boundary of libk3xb (include/k3xb.h).
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -1633,6 +1634,22 @@ int k3xb_ep_verify_step(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_ve
             return fail(ctx, K3XB_INVALID_EXTENT, "expert parallel route: top_k <= 32");
     }
     return verify_step_impl(ctx, m, io, experts_total);
+}
+
+int k3xb_ep_balance(const float* load, uint32_t E, uint32_t world, uint32_t* owner) {
+    if (!load || !owner || !E || !world || E % world || E / world > 0xffffu) return K3XB_INVALID_EXTENT;
+    std::vector<uint32_t> order(E);
+    for (uint32_t e = 0; e < E; ++e) {
+        if (!std::isfinite(load[e])) return K3XB_INVALID_EXTENT;
+        order[e] = e;
+    }
+    std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return load[a] > load[b]; });
+    for (uint32_t i = 0; i < E; ++i) {
+        const uint32_t round = i / world, pos = i % world;
+        const uint32_t rank = round % 2 == 0 ? pos : world - 1 - pos;
+        owner[order[i]] = rank << 16 | round;
+    }
+    return K3XB_OK;
 }
 
 int k3xb_draft_greedy(k3xb_ctx* ctx, const k3xb_verify_model* m, const k3xb_draft_io* io) {

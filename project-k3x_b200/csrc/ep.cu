@@ -2,7 +2,8 @@
 // the GPUs of one box, rows and expert outputs moved through peer memory
 // over NVLink.
 //
-// Rank r owns experts [r*E_r, (r+1)*E_r) (E_r = E / world) and T tokens of
+// Rank r owns experts [r*E_r, (r+1)*E_r) (E_r = E / world), or those a
+// placement table gives it (k3xb_moe_layer.ep_owner), and T tokens of
 // its own sequences (data parallel); the router, the shared expert and the
 // combine stay on the token's home rank. Every rank owns an exchange window
 // that the other ranks map (CUDA IPC; the handles are all-gathered over an
@@ -227,6 +228,8 @@ struct DispatchArgs {
     uint32_t rank, world, epoch, T, K, D, E_r;
     int rows_bf16;
     uint32_t* done;
+    const uint32_t* owner;   // k3xb_moe_layer.ep_owner, or NULL: contiguous ranges
+    int32_t* status;
 };
 
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(const float* __restrict__ x,
@@ -238,8 +241,18 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const float* __restric
     uint32_t* meta = reinterpret_cast<uint32_t*>(a.win[g] + a.off_meta) + (static_cast<size_t>(a.rank) * a.T + t) * a.K;
     for (uint32_t j = threadIdx.x; j < a.K; j += blockDim.x) {
         const uint32_t e = ids[static_cast<size_t>(t) * a.K + j];
-        const bool here = e / a.E_r == g;
-        meta[j] = here ? ((e - g * a.E_r) << 8 | j) : kNoEntry;
+        uint32_t owner_rank = e / a.E_r, local = e - owner_rank * a.E_r;
+        if (a.owner) {
+            const uint32_t o = __ldg(a.owner + e);
+            owner_rank = o >> 16;
+            local = o & 0xffffu;
+            if (owner_rank >= a.world || local >= a.E_r) {   // not a placement of this world: drop, report
+                if (g == 0) atomicExch(a.status, K3XB_INVALID_STATE);
+                owner_rank = a.world;
+            }
+        }
+        const bool here = owner_rank == g;
+        meta[j] = here ? (local << 8 | j) : kNoEntry;
         if (here) present = 1;
     }
     __syncthreads();
@@ -537,6 +550,8 @@ int ep_moe_forward(k3xb_ctx* ctx, const k3xb_moe_layer& L, uint32_t E, const flo
         a.E_r = E_r;
         a.rows_bf16 = rows_bf16 ? 1 : 0;
         a.done = counters;
+        a.owner = L.ep_owner;
+        a.status = status;
         ep_dispatch_kernel<<<dim3(T, G), 256, 0, ctx->stream>>>(hidden, ids, a);
         K3XB_LAUNCHED(ctx);
     }

@@ -49,7 +49,13 @@ __device__ double block_sum_d(double v, double* red) {
 // attention_residual (official_layer.cpp:42-102) followed by rms_norm
 // (:104-125); one CTA per row. With `delta`, the first source is
 // prefix = round_bf16(round_bf16(a) + delta) (official_layer.cpp:190-193),
-// also written to prefix_out.
+// also written to prefix_out. With VEC (H % 4 == 0 and every row pointer
+// 16-byte aligned, weights 8-byte aligned) each thread moves 4 columns per
+// access and the loops are unrolled, so several loads are in flight; the
+// sums of squares and scores are FP64 partials per thread combined by a
+// deterministic block tree, rounded to float as the reference's sequential
+// double sums are.
+template <bool VEC>
 __global__ void __launch_bounds__(256) attnres_norm_kernel(const float* __restrict__ a, const float* __restrict__ delta,
                                                            const float* __restrict__ block,
                                                            const uint16_t* __restrict__ rnorm,
@@ -63,28 +69,101 @@ __global__ void __launch_bounds__(256) attnres_norm_kernel(const float* __restri
     const size_t row = blockIdx.x;
     const float* pa = a + row * H;
     const float* pb = block + row * H;
-    double sq_p = 0.0, sq_b = 0.0;
-    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) {
-        float p = pa[i];
-        if (delta) {
-            p = round_bf16(__fadd_rn(round_bf16(p), delta[row * H + i]));
-            prefix_out[row * H + i] = p;
+    const float* pd = delta ? delta + row * H : nullptr;
+    float* po = prefix_out ? prefix_out + row * H : nullptr;
+    constexpr uint32_t W = VEC ? 4u : 1u;
+    const uint32_t n = H / W;
+    auto ld = [](const float* p, uint32_t i, float (&v)[W]) {
+        if constexpr (VEC) {
+            const float4 q = __ldg(reinterpret_cast<const float4*>(p) + i);
+            v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+        } else {
+            v[0] = p[i];
         }
-        const float vp = round_bf16(p), vb = round_bf16(pb[i]);
-        rp[i] = vp;
-        rb[i] = vb;
-        sq_p = fma(static_cast<double>(vp), static_cast<double>(vp), sq_p);
-        sq_b = fma(static_cast<double>(vb), static_cast<double>(vb), sq_b);
+    };
+    // shared-memory rows (rp, rb): plain loads (__ldg is for global memory only)
+    auto lds = [](const float* p, uint32_t i, float (&v)[W]) {
+        if constexpr (VEC) {
+            const float4 q = reinterpret_cast<const float4*>(p)[i];
+            v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+        } else {
+            v[0] = p[i];
+        }
+    };
+    auto st = [](float* p, uint32_t i, const float (&v)[W]) {
+        if constexpr (VEC) reinterpret_cast<float4*>(p)[i] = make_float4(v[0], v[1], v[2], v[3]);
+        else p[i] = v[0];
+    };
+    auto ldw = [](const uint16_t* p, uint32_t i, float (&v)[W]) {
+        if constexpr (VEC) {
+            const uint2 q = __ldg(reinterpret_cast<const uint2*>(p) + i);
+            v[0] = __uint_as_float(q.x << 16); v[1] = __uint_as_float(q.x & 0xffff0000u);
+            v[2] = __uint_as_float(q.y << 16); v[3] = __uint_as_float(q.y & 0xffff0000u);
+        } else {
+            v[0] = decode_bf16(p[i]);
+        }
+    };
+    double sq_p = 0.0, sq_b = 0.0;
+    // batches of kB iterations: every global load of a batch is issued
+    // before any of its values is used
+    constexpr uint32_t kB = 4;
+    for (uint32_t i0 = threadIdx.x; i0 < n; i0 += kB * blockDim.x) {
+        float va[kB][W], vb[kB][W], vd[kB][W];
+#pragma unroll
+        for (uint32_t j = 0; j < kB; ++j) {
+            const uint32_t i = i0 + j * blockDim.x;
+            if (i < n) {
+                ld(pa, i, va[j]);
+                ld(pb, i, vb[j]);
+                if (pd) ld(pd, i, vd[j]);
+            }
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < kB; ++j) {
+            const uint32_t i = i0 + j * blockDim.x;
+            if (i >= n) break;
+#pragma unroll
+            for (uint32_t k = 0; k < W; ++k) {
+                if (pd) va[j][k] = round_bf16(__fadd_rn(round_bf16(va[j][k]), vd[j][k]));
+                va[j][k] = round_bf16(va[j][k]);
+                vb[j][k] = round_bf16(vb[j][k]);
+                sq_p = fma(static_cast<double>(va[j][k]), static_cast<double>(va[j][k]), sq_p);
+                sq_b = fma(static_cast<double>(vb[j][k]), static_cast<double>(vb[j][k]), sq_b);
+            }
+            if (po) st(po, i, va[j]);   // the prefix: round_bf16 leaves it unchanged
+            st(rp, i, va[j]);
+            st(rb, i, vb[j]);
+        }
     }
     sq_p = block_sum_d(sq_p, red);
     sq_b = block_sum_d(sq_b, red);
     const float inv_p = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(sq_p / H), eps)));
     const float inv_b = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(sq_b / H), eps)));
     double sc_p = 0.0, sc_b = 0.0;
-    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) {
-        const double nw = static_cast<double>(decode_bf16(rnorm[i])) * static_cast<double>(decode_bf16(rproj[i]));
-        sc_p += static_cast<double>(__fmul_rn(rp[i], inv_p)) * nw;   // exact product, as (v*inv)*norm*proj
-        sc_b += static_cast<double>(__fmul_rn(rb[i], inv_b)) * nw;
+    for (uint32_t i0 = threadIdx.x; i0 < n; i0 += kB * blockDim.x) {
+        float nv[kB][W], pv[kB][W];
+#pragma unroll
+        for (uint32_t j = 0; j < kB; ++j) {
+            const uint32_t i = i0 + j * blockDim.x;
+            if (i < n) {
+                ldw(rnorm, i, nv[j]);
+                ldw(rproj, i, pv[j]);
+            }
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < kB; ++j) {
+            const uint32_t i = i0 + j * blockDim.x;
+            if (i >= n) break;
+            float xp[W], xb[W];
+            lds(rp, i, xp);
+            lds(rb, i, xb);
+#pragma unroll
+            for (uint32_t k = 0; k < W; ++k) {
+                const double nw = static_cast<double>(nv[j][k]) * static_cast<double>(pv[j][k]);
+                sc_p += static_cast<double>(__fmul_rn(xp[k], inv_p)) * nw;   // exact product, as (v*inv)*norm*proj
+                sc_b += static_cast<double>(__fmul_rn(xb[k], inv_b)) * nw;
+            }
+        }
     }
     const float score_p = static_cast<float>(block_sum_d(sc_p, red));
     const float score_b = static_cast<float>(block_sum_d(sc_b, red));
@@ -93,15 +172,29 @@ __global__ void __launch_bounds__(256) attnres_norm_kernel(const float* __restri
     const float den = __fadd_rn(eb, ep);
     const float wb = __fdiv_rn(eb, den), wp = __fdiv_rn(ep, den);
     double sq = 0.0;
-    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) {
-        const float r = round_bf16(__fadd_rn(__fmul_rn(wb, rb[i]), __fmul_rn(wp, rp[i])));
-        rb[i] = r;
-        sq = fma(static_cast<double>(r), static_cast<double>(r), sq);
+#pragma unroll 4
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        float xp[W], xb[W];
+        lds(rp, i, xp);
+        lds(rb, i, xb);
+#pragma unroll
+        for (uint32_t k = 0; k < W; ++k) {
+            xb[k] = round_bf16(__fadd_rn(__fmul_rn(wb, xb[k]), __fmul_rn(wp, xp[k])));
+            sq = fma(static_cast<double>(xb[k]), static_cast<double>(xb[k]), sq);
+        }
+        st(rb, i, xb);
     }
     sq = block_sum_d(sq, red);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(sq / H), eps)));
-    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x)
-        out[row * H + i] = round_bf16(__fmul_rn(__fmul_rn(rb[i], inv), decode_bf16(post[i])));
+#pragma unroll 4
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        float xb[W], pw[W];
+        lds(rb, i, xb);
+        ldw(post, i, pw);
+#pragma unroll
+        for (uint32_t k = 0; k < W; ++k) xb[k] = round_bf16(__fmul_rn(__fmul_rn(xb[k], inv), pw[k]));
+        st(out + row * H, i, xb);
+    }
 }
 
 // Short causal conv + SiLU (official_kda.cpp:95-143) along each node's
@@ -311,12 +404,22 @@ int launch_attnres_norm(k3xb_ctx* ctx, const float* a, const float* delta, const
     if (smem > 200 * 1024) return fail(ctx, K3XB_INVALID_EXTENT, "attention residual: hidden too large");
     static std::atomic<uint64_t> configured{0};
     const int cst = configure_once(ctx, configured, [&]() -> int {
-        K3XB_CUDA(ctx, cudaFuncSetAttribute(attnres_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        K3XB_CUDA(ctx, cudaFuncSetAttribute(attnres_norm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            200 * 1024));
+        K3XB_CUDA(ctx, cudaFuncSetAttribute(attnres_norm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             200 * 1024));
         return K3XB_OK;
     });
     if (cst) return cst;
-    attnres_norm_kernel<<<T, 256, smem, ctx->stream>>>(a, delta, block, rnorm, rproj, post, H, eps, prefix_out, out);
+    auto al = [](const void* p, uintptr_t m) { return (reinterpret_cast<uintptr_t>(p) & m) == 0; };
+    const bool vec = H % 4 == 0 && al(a, 15) && al(delta, 15) && al(block, 15) && al(prefix_out, 15) && al(out, 15) &&
+                     al(rnorm, 7) && al(rproj, 7) && al(post, 7);
+    if (vec)
+        attnres_norm_kernel<true><<<T, 256, smem, ctx->stream>>>(a, delta, block, rnorm, rproj, post, H, eps,
+                                                                 prefix_out, out);
+    else
+        attnres_norm_kernel<false><<<T, 256, smem, ctx->stream>>>(a, delta, block, rnorm, rproj, post, H, eps,
+                                                                  prefix_out, out);
     K3XB_LAUNCHED(ctx);
     return K3XB_OK;
 }

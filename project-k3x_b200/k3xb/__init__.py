@@ -54,7 +54,7 @@ class MoeLayer(C.Structure):
                 ("gate_scales_tc", C.c_void_p), ("up_scales_tc", C.c_void_p),
                 ("down_scales_tc", C.c_void_p),
                 ("latent", C.c_uint32), ("routed_down", C.c_void_p), ("routed_norm", C.c_void_p),
-                ("routed_up", C.c_void_p), ("latent_eps", C.c_float)]
+                ("routed_up", C.c_void_p), ("latent_eps", C.c_float), ("ep_owner", C.c_void_p)]
 
 
 class KdaLayer(C.Structure):
@@ -169,6 +169,7 @@ def library() -> C.CDLL:
             "k3xb_get_stats": [vp, C.POINTER(Stats)],
             "k3xb_route": [vp, vp, u32, u32, vp, vp, u32, u32, vp, vp, vp],
             "k3xb_router_logits": [vp, vp, u32, u32, vp, u32, vp],
+            "k3xb_ep_balance": [vp, u32, u32, vp],
             "k3xb_expert_major_plan": [vp, vp, vp, u32, u32, u32, C.POINTER(Plan)],
             "k3xb_select_routing": [vp, vp, u32, u32, vp, u32, C.POINTER(RoutingPolicy), vp, vp, vp, vp, vp],
             "k3xb_moe_layer_forward": [vp, C.POINTER(MoeLayer), vp, u32, vp, vp, vp],
@@ -693,6 +694,8 @@ def moe_layer_desc(w: dict, engine=ENGINE_SIMT, act_terms=0) -> MoeLayer:
         t = w.get(name)
         setattr(L, name, None if t is None else t.data_ptr())
     L.latent_eps = w.get("latent_eps", 1e-6)
+    t = w.get("ep_owner")   # expert placement (device uint32 [experts_total]) for expert parallelism
+    L.ep_owner = None if t is None else t.data_ptr()
     return L
 
 
@@ -791,14 +794,47 @@ def ep_unique_id() -> bytes:
     return bytes(buf)
 
 
-def ep_local_layer(w: dict, rank: int, world: int) -> dict:
-    """The expert shard of rank `rank`: experts [rank*E/world, ...) of the
-    stacked MXFP4 arrays (views, no copies), router/correction/shared kept
-    whole."""
+def ep_balance(load, world: int):
+    """k3xb_ep_balance: an expert placement (numpy uint32 [E], entry
+    rank << 16 | local index) dealing experts in descending `load` over the
+    ranks in a snake."""
+    import numpy as np
+    load = np.ascontiguousarray(load, np.float32)
+    owner = np.empty(load.size, np.uint32)
+    st = library().k3xb_ep_balance(load.ctypes.data, load.size, world, owner.ctypes.data)
+    if st:
+        raise K3xbError(st, "ep_balance")
+    return owner
+
+
+def ep_local_layer(w: dict, rank: int, world: int, owner=None) -> dict:
+    """The expert shard of rank `rank`, router/correction/shared kept whole.
+    Without `owner`: experts [rank*E/world, ...) of the stacked MXFP4 arrays
+    (views, no copies). With `owner` (numpy uint32 [E], as ep_balance makes):
+    the experts it gives this rank, in their local order (copies), and the
+    table itself on the device as the layer's ep_owner."""
     E = w["experts"]
     if E % world:
         raise K3xbError(INVALID_EXTENT, "experts must divide evenly over the world")
     n = E // world
+    if owner is not None:
+        import numpy as np
+        import torch
+        owner = np.ascontiguousarray(owner, np.uint32)
+        mine = [(int(o) & 0xffff, e) for e, o in enumerate(owner) if int(o) >> 16 == rank]
+        mine.sort()
+        if len(owner) != E or [loc for loc, _ in mine] != list(range(n)):
+            raise K3xbError(INVALID_EXTENT, "ep_local_layer: owner must give every rank E/world experts")
+        idx = torch.tensor([e for _, e in mine], dtype=torch.long, device=w["gate_packed"].device)
+        out = dict(w, experts=n)
+        for k in ("gate_packed", "gate_scales", "up_packed", "up_scales", "down_packed", "down_scales"):
+            out[k] = w[k].index_select(0, idx)
+        I, H = w["inter"], w["hidden"]
+        for k in ("gate_scales_tc", "up_scales_tc", "down_scales_tc"):
+            if w.get(k) is not None:   # whole experts are contiguous in the atom layout
+                out[k] = w[k].view(E, -1).index_select(0, idx).view(-1)
+        out["ep_owner"] = torch.from_numpy(owner.view(np.int32)).to(w["gate_packed"].device)
+        return out
     lo, hi = rank * n, (rank + 1) * n
     out = dict(w, experts=n)
     for k in ("gate_packed", "gate_scales", "up_packed", "up_scales", "down_packed", "down_scales"):

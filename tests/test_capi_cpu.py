@@ -4,6 +4,7 @@ import ctypes as C
 import os
 import re
 
+import numpy as np
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -95,6 +96,32 @@ def test_draft_entry_point_rejects_null_context():
     lib = k3xb.library()
     io = k3xb.DraftIO(1, 1, 1, None, None, None, None)
     assert lib.k3xb_draft_greedy(None, C.byref(k3xb.VerifyModel()), C.byref(io)) == k3xb.INVALID_EXTENT
+
+
+def test_ep_balance_deals_by_load():
+    """k3xb_ep_balance (host function): experts dealt in descending load over
+    the ranks in a snake; every rank gets E/world, local indices 0.. in
+    dealing order; ties keep the lower id first; bad arguments are
+    INVALID_EXTENT."""
+    import k3xb
+    E, world = 48, 4
+    load = np.random.default_rng(3).random(E).astype(np.float32)
+    owner = k3xb.ep_balance(load, world)
+    rank, local = owner >> 16, owner & 0xFFFF
+    order = np.argsort(-load, kind="stable")
+    for i, e in enumerate(order):
+        r, p = divmod(i, world)
+        assert rank[e] == (p if r % 2 == 0 else world - 1 - p) and local[e] == r
+    for g in range(world):
+        assert sorted(local[rank == g].tolist()) == list(range(E // world))
+    hot = order[:world]
+    assert len(set(rank[hot].tolist())) == world          # the heaviest experts on different ranks
+    tie = k3xb.ep_balance(np.zeros(8, np.float32), 2)   # all equal: ids in order, snake
+    assert (tie >> 16).tolist() == [0, 1, 1, 0, 0, 1, 1, 0] and (tie & 0xFFFF).tolist() == [0, 0, 1, 1, 2, 2, 3, 3]
+    with pytest.raises(k3xb.K3xbError):
+        k3xb.ep_balance(np.ones(10, np.float32), 4)      # does not split evenly
+    with pytest.raises(k3xb.K3xbError):
+        k3xb.ep_balance(np.array([1.0, np.nan], np.float32), 2)
 
 
 def test_default_act_terms_rule():

@@ -61,7 +61,13 @@ def _exchange(send, world):
     return recv.view(np.uint32) if as_int else recv
 
 
-def _ep_rank(rank, world, port, out_dir, latent):
+def _owner(E, world):
+    """A placement (k3xb_ep_balance of a seeded load), or the ranges."""
+    import k3xb
+    return k3xb.ep_balance(np.random.default_rng(11).random(E).astype(np.float32), world)
+
+
+def _ep_rank(rank, world, port, out_dir, latent, placed=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -70,6 +76,12 @@ def _ep_rank(rank, world, port, out_dir, latent):
     E, K, H = L["experts"], L["top_k"], L["hidden"]
     D = latent or H   # rows sent, computed and returned: latent rows for LatentMoE
     E_r, T = E // world, DIMS["tokens_per_rank"]
+    owner = _owner(E, world) if placed else None
+
+    def own(e):   # (rank, local index) holding expert e
+        e = int(e)
+        return (int(owner[e]) >> 16, int(owner[e]) & 0xFFFF) if owner is not None else divmod(e, E_r)
+    expert_at = {own(e): e for e in range(E)}
     x_in = _hidden(world)[rank * T:(rank + 1) * T]
     # LatentMoE: the latent projection happens on the home rank (official_moe.cpp:296)
     x = np.stack([rs.bf16_matvec(x_in[t], L["routed_down"]) for t in range(T)]) if latent else x_in
@@ -84,8 +96,9 @@ def _ep_rank(rank, world, port, out_dir, latent):
     for g in range(world):
         for t in range(T):
             for j in range(K):
-                if ids[t, j] // E_r == g:
-                    meta[g, t, j] = (int(ids[t, j]) - g * E_r) << 8 | j
+                g_e, local = own(ids[t, j])
+                if g_e == g:
+                    meta[g, t, j] = local << 8 | j
     assert np.array_equal(rs.round_bf16(x), x)   # bf16-valued rows travel as bf16 exactly
     send_x = np.full((world, T, D), np.nan, np.float32)
     for g in range(world):
@@ -103,7 +116,7 @@ def _ep_rank(rank, world, port, out_dir, latent):
             for j in range(K):
                 if m[r, j] != NO_ENTRY and (m[r, j] >> 8) == e:
                     home, t = divmod(r, T)
-                    put[home, t, m[r, j] & 0xFF] = _expert(rs, L, rank * E_r + e, rows[r])
+                    put[home, t, m[r, j] & 0xFF] = _expert(rs, L, expert_at[(rank, e)], rows[r])
     landed = _exchange(put, world)   # landed[g]: what rank g stored into this rank's region
     written = ~np.isnan(landed).all(axis=3)
     assert (written.sum(axis=0) == 1).all(), "every (token, slot) row is stored by exactly one rank"
@@ -126,10 +139,12 @@ def _ep_rank(rank, world, port, out_dir, latent):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,latent", [(2, 0), (2, 128), (4, 0)])
-def test_ep_restatement_equals_one_process(rs, tmp_path, world, latent):
-    port = 29500 + (os.getpid() + latent + 7 * world) % 2000
-    mp.start_processes(_ep_rank, args=(world, port, str(tmp_path), latent), nprocs=world, start_method="spawn")
+@pytest.mark.parametrize("world,latent,placed", [(2, 0, False), (2, 128, False), (4, 0, False), (4, 0, True),
+                                                 (2, 128, True)])
+def test_ep_restatement_equals_one_process(rs, tmp_path, world, latent, placed):
+    port = 29500 + (os.getpid() + latent + 7 * world + 3 * placed) % 2000
+    mp.start_processes(_ep_rank, args=(world, port, str(tmp_path), latent, placed), nprocs=world,
+                       start_method="spawn")
     L = _layer(rs, latent)
     want, want_ids, _ = rs.moe_layer(L, _hidden(world))
     T = DIMS["tokens_per_rank"]

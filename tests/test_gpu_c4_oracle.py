@@ -7,10 +7,11 @@ on the host), each layer held against oracle/_ref's k3xr_plain_layer
 (official_kda_cpu, prepare_official_moe_input, route_official_moe,
 mxfp4_matmul, situ_glu, composed as official_layer.cpp:134-244) on the
 same inputs:
-- the selected expert sets agree on at least 90% of the tokens, and the
-  layer outputs are within rel 2e-2 / abs 1e-3 where they agree
-  (test_gpu_layer.py says why a projection output can land one bf16 step
-  away; at 384 experts that mostly reorders neighbours inside the Top-16);
+- the selected expert sets agree on at least 90% of the tokens, and where
+  they agree each layer-output row is within rel 2e-2 of its own scale
+  (assert_row_close; test_gpu_layer.py says why a projection output can
+  land one bf16 step away; at 384 experts that mostly reorders neighbours
+  inside the Top-16);
 - the verify step's logits equal the final norm and LM head of the
   reference's bf16_matvec over the GPU layers' output, within the same
   tolerance, and greedy acceptance on them is bit-exact
@@ -36,6 +37,19 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 S = 2
+
+
+def assert_row_close(got, want, rtol=2e-2, what=""):
+    """A residual-stream row (out = round_bf16(prefix + combined)) held to the
+    north-star relative bar against its own scale: the relative L2 error of
+    the row, and every element's error against the row's largest magnitude.
+    Element-wise relative error is ill-conditioned here: where prefix and
+    combined (magnitudes up to ~8 at these dims) cancel, one bf16 step of an
+    operand (0.03-0.06) is a large fraction of a near-zero sum."""
+    err = np.abs(got - want)
+    rel = float(np.linalg.norm(err) / max(np.linalg.norm(want), 1e-30))
+    worst = float(err.max() / max(np.abs(want).max(), 1e-30))
+    assert rel <= rtol and worst <= rtol, f"{what}: relative L2 error {rel:.2e}, max error {worst:.2e} of max |row|"
 
 
 def _bf16_f32(words):
@@ -96,7 +110,8 @@ def test_c4_layers_and_verify_step_vs_reference(rs, ref):
             assert same.sum() >= 0.9 * S * N, (f"layer {l}: expert sets agree on {same.sum()}/{S * N} tokens "
                                                f"(ordered ids on {ordered.sum()})")
             for s in range(S):
-                assert_mostly_close(gout[s][same[s]], want[s][same[s]], what=f"layer {l} output, sequence {s}")
+                for i in np.nonzero(same[s])[0]:
+                    assert_row_close(gout[s, i], want[s, i], what=f"layer {l} output, sequence {s}, position {i}")
             xl_d = out_d
         final = xl_d.cpu().numpy()
 

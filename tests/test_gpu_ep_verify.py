@@ -4,7 +4,8 @@ counts, committed tokens and the committed KDA states, over several
 consecutive steps (each step starts from the states the previous one
 committed, and the exchange alternates its window halves).
 
-Expert parallelism moves bf16-valued rows and bf16-rounded expert outputs,
+With and without an expert placement (k3xb_moe_layer.ep_owner from
+k3xb_ep_balance). Expert parallelism moves bf16-valued rows and bf16-rounded expert outputs,
 and every per-token quantity is computed by the same kernels in the same
 order whichever rank runs it, so equality is exact. A world of one runs on
 any GPU box; the two-rank case needs two GPUs (one process per GPU) and
@@ -40,14 +41,21 @@ def _setup(rs, S):
     return layers, emb, lm, fnorm, conv, rec, tokens
 
 
-def _model(torch, layers, emb, lm, fnorm, rank=None, world=None):
+def _owner(world):
+    """An expert placement that is not the contiguous ranges (k3xb_ep_balance
+    of a seeded load)."""
+    import k3xb
+    return k3xb.ep_balance(np.random.default_rng(17).random(DIMS["experts"]).astype(np.float32), world)
+
+
+def _model(torch, layers, emb, lm, fnorm, rank=None, world=None, owner=None):
     import k3xb
     from test_gpu_draft import _layer_dev
     descs, keep = [], []
     for layer in layers:
         d = _layer_dev(torch, layer)
         if world is not None:
-            d = dict(d, moe=k3xb.ep_local_layer(d["moe"], rank, world))
+            d = dict(d, moe=k3xb.ep_local_layer(d["moe"], rank, world, owner=owner))
         keep.append(d)
         descs.append(k3xb.layer_desc(d))
     e, l, f = to_dev(torch, emb), to_dev(torch, lm), to_dev(torch, fnorm)
@@ -84,7 +92,8 @@ def _assert_same(got, want, what):
             np.testing.assert_array_equal(a, b, err_msg=f"{what}: step {i} {name}")
 
 
-def test_ep_verify_world_of_one_equals_verify_step(rs):
+@pytest.mark.parametrize("placed", [False, True])
+def test_ep_verify_world_of_one_equals_verify_step(rs, placed):
     import k3xb
     torch = torch_cuda()
     layers, emb, lm, fnorm, conv, rec, tokens = _setup(rs, S_PER_RANK)
@@ -94,7 +103,8 @@ def test_ep_verify_world_of_one_equals_verify_step(rs):
         model, keep = _model(torch, layers, emb, lm, fnorm)
         want, want_conv, want_rec = _steps(torch, ctx, model, conv, rec, tokens)
         ctx.ep_init(k3xb.ep_unique_id(), 0, 1)
-        ep_model, ep_keep = _model(torch, layers, emb, lm, fnorm, 0, 1)
+        ep_model, ep_keep = _model(torch, layers, emb, lm, fnorm, 0, 1,
+                                   owner=_owner(1) if placed else None)   # placed: a permuted stack
         got, got_conv, got_rec = _steps(torch, ctx, ep_model, conv, rec, tokens, DIMS["experts"])
         _assert_same(got, want, "world of one")
         np.testing.assert_array_equal(got_conv, want_conv)
@@ -105,7 +115,7 @@ def test_ep_verify_world_of_one_equals_verify_step(rs):
         ctx.close()
 
 
-def _rank_main(rank, world, uid, out_dir):
+def _rank_main(rank, world, uid, out_dir, placed=False):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [os.path.join(root, "project-k3x_b200"), os.path.join(root, "oracle"), os.path.join(root, "tests")]
@@ -119,7 +129,7 @@ def _rank_main(rank, world, uid, out_dir):
     ctx = k3xb.Context(rank)
     ctx.use_stream()
     ctx.ep_init(uid, rank, world)
-    model, keep = _model(torch, layers, emb, lm, fnorm, rank, world)
+    model, keep = _model(torch, layers, emb, lm, fnorm, rank, world, owner=_owner(world) if placed else None)
     got, got_conv, got_rec = _steps(torch, ctx, model, np.ascontiguousarray(conv[:, mine]),
                                     np.ascontiguousarray(rec[:, mine]), np.ascontiguousarray(tokens[:, mine]),
                                     DIMS["experts"])
@@ -132,7 +142,8 @@ def _rank_main(rank, world, uid, out_dir):
     ctx.close()
 
 
-def test_ep_verify_two_ranks_equal_one_gpu(rs, tmp_path):
+@pytest.mark.parametrize("placed", [False, True])
+def test_ep_verify_two_ranks_equal_one_gpu(rs, tmp_path, placed):
     torch = torch_cuda()
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -141,7 +152,7 @@ def test_ep_verify_two_ranks_equal_one_gpu(rs, tmp_path):
     import k3xb
     world = 2
     uid = k3xb.ep_unique_id()
-    mp.start_processes(_rank_main, args=(world, uid, str(tmp_path)), nprocs=world, start_method="spawn")
+    mp.start_processes(_rank_main, args=(world, uid, str(tmp_path), placed), nprocs=world, start_method="spawn")
     layers, emb, lm, fnorm, conv, rec, tokens = _setup(rs, S_PER_RANK * world)
     ctx = k3xb.Context(0)
     ctx.use_stream()
