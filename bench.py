@@ -50,12 +50,14 @@ C5 = dict(C4, layers=8, sequences=64, seed=4, zipf=1.1)
 C3 = dict(heads=32, head_dim=128, nodes=32, depth=4, prefix=1024, seed=2)
 ZIPF_SCALE = 0.5   # c5: the rank-r expert's bias is ZIPF_SCALE * r^-1.1 (ranks a seeded permutation)
 EXPERT_BYTES = 3 * 7168 * 2048 * (0.5 + 1 / 32)   # S_e = 23,396,352 B per expert
-# DRAM bytes (read + write) of the routed gate/up + down kernels per
-# algorithmic byte, from one ncu capture of a reduced c2 case (128 experts,
-# 24 tokens): 2963.3 MB against 2872 MB algorithmic (expected 122.8 unique
-# experts). Traffic grows with the unique experts, so a full-size launch is
-# this ratio times its algorithmic bytes (profiles/expert_ffn_traffic_128x24.md).
-EXPERT_TRAFFIC_RATIO = (1969.4 + 7.3 + 976.3 + 10.3) / (122.8 * 3 * 7168 * 2048 * 0.53125 / 1e6)
+# DRAM bytes (read + write) of the routed expert kernels per algorithmic
+# byte, from single-launch ncu captures: gate/up 1047.2 MB against 998.2 MB
+# (64 experts x 96 tokens, profiles/expert_ffn_c5_density_64x96.md), down
+# 985.2 MB against 957.9 MB (128 experts x 24 tokens,
+# profiles/expert_ffn_traffic_128x24.md), weighted 2:1 as their bytes are.
+# Traffic grows with the experts streamed, so a full-size launch is this
+# ratio times its algorithmic bytes.
+EXPERT_TRAFFIC_RATIO = (2 * (1032.679 + 14.555) / 998.244 + (976.479 + 8.689) / 957.9) / 3
 
 
 def peaks():
@@ -667,7 +669,7 @@ def run_stack(args, rank, world, local, ctx, stream, cfg):
                      "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
                      "alg_bytes_per_step": ffn_bytes, "experts_per_layer_expected": used,
                      "ffn_ms_per_step": ffn_ms, "traffic": ffn_bytes * EXPERT_TRAFFIC_RATIO,
-                     "traffic_source": "ncu dram__bytes_read+write of gate/up + down on a reduced c2 case, "
+                     "traffic_source": "ncu dram__bytes_read+write per algorithmic byte of gate/up (64x96) and down (128x24), "
                                        "scaled by the experts streamed (profiles/expert_ffn_traffic_128x24.md)",
                      "whole_step": {"alg_bytes": step_bytes, "achieved": step_achieved,
                                     "frac": step_achieved / hbm}},
@@ -842,7 +844,7 @@ def run_c2(args, rank, world, local, ctx, stream, cfg):
                      "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
                      "alg_bytes_per_launch": alg_bytes, "unique_experts": unique, "launch_ms": timed,
                      "traffic": unique * EXPERT_BYTES * EXPERT_TRAFFIC_RATIO,
-                     "traffic_source": "ncu dram__bytes_read+write of gate/up + down on a reduced c2 case, "
+                     "traffic_source": "ncu dram__bytes_read+write per algorithmic byte of gate/up (64x96) and down (128x24), "
                                        "scaled by unique experts (profiles/expert_ffn_traffic_128x24.md)"},
         "gpu_launches": per_step * args.steps, "clocks": clk.summary(), "engine": args.engine,
         "mxf4_act_terms": args.act_terms or k3xb.default_act_terms(T * K, E),
