@@ -10,7 +10,8 @@ the experts are sharded over the GPUs and the sequences split between
 them (k3xb_ep_verify_step): the same 512 drafts, so the scaling is strong.
 One step = the whole verify step (layers, LM head, acceptance, state
 commit). Other lines with --config: c4 (2 layers, 16 sequences), c2 (one
-MoE layer, 64 tokens), c3 (KDA draft tree), tc (tensor-core sweep).
+MoE layer, 64 tokens), c3 (KDA draft tree), tc (tensor-core sweep),
+attnres (block attention residual over many sources).
 
 Inputs are seeded synthetic data of the configs' shapes. Both arms build
 them from one spec (seed, stream, sigma per tensor): the GPU arm with the
@@ -935,6 +936,61 @@ def run_c3(args, rank, world, local, ctx, stream):
         print(json.dumps(result), flush=True)
 
 
+def run_attnres(args, rank, world, local, ctx, stream):
+    """The block attention residual with many sources (model.cpp:645-666)
+    over c5's 576 verify positions at H 7168, with `--sources` block
+    sources (default 8). HBM-bound: every value row is read once and the
+    output written once."""
+    import torch
+    T, H, S = C5["sequences"] * (C5["drafts"] + 1), C5["hidden"], args.sources
+    values = gpu_tensor(ctx, torch, ("f32", (S + 1, T, H), 11, 1, 1.0, 0.0))
+    norm = gpu_tensor(ctx, torch, ("f32", (H,), 11, 2, 0.1, 1.0))
+    proj = gpu_tensor(ctx, torch, ("f32", (H,), 11, 3, 3.0 / H ** 0.5, 0.0))
+    sources, prefix = (values[:S] if S else None), values[S]
+    out = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    eps = 1e-6
+
+    def step():
+        ctx.block_attention_residual(prefix, sources, norm, proj, eps, out)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")   # > L2: each step starts cold
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    with Clocks(local) as clk:
+        for i in range(args.steps):
+            flush.add_(1)
+            ev[2 * i].record(stream)
+            step()
+            ev[2 * i + 1].record(stream)
+        torch.cuda.synchronize()
+    ctx.sync()
+    ms = max_over_ranks(statistics.mean(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)), world)
+    alg = (S + 2) * T * H * 4 + 2 * H * 4
+    # DRAM bytes per algorithmic byte from one ncu capture of this command at
+    # the default 8 sources (profiles/block_attnres_576x9.md): (249.28 + 8.14)
+    # MB over 165.21 MB; other source counts were not captured
+    traffic = alg * (249.280 + 8.138) / 165.208 if S == 8 else None
+    hbm, peak_kind = peaks()
+    result = {
+        "metric": "attention-residual positions/s", "value": sum_over_ranks(T, world) / (ms * 1e-3),
+        "unit": "positions/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (FP64 score sums)",
+        "data": "synthetic (seeded, generated on the GPU)",
+        "config": {"workload": "block attention residual over many sources", "positions": T, "hidden": H,
+                   "sources": S, "l2": "flushed (256 MB write) before every timed step"},
+        "roofline": {"bound": "hbm", "kernel": "block_attnres_kernel", "achieved": alg / (ms * 1e-3) / 1e9,
+                     "peak": hbm, "unit": "GB/s", "frac": alg / (ms * 1e-3) / 1e9 / hbm,
+                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})", "alg_bytes_per_launch": alg,
+                     "traffic": traffic},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
 def run_tc_sweep(args, rank, world, local, ctx, stream):
     """Tensor-core sweep of the expert GEMM: 8 experts x M tokens each (Top-8
     of 8, so every token uses every expert) for M in {256, 1024, 4096}, c2
@@ -1012,6 +1068,8 @@ def run_ours(args):
             run_c3(args, rank, world, local, ctx, stream)
         elif args.config == "tc":
             run_tc_sweep(args, rank, world, local, ctx, stream)
+        elif args.config == "attnres":
+            run_attnres(args, rank, world, local, ctx, stream)
         else:
             cfg = dict(C2)
             if args.experts:   # reduced c2 case for profiler captures (a few GB on the device)
@@ -1032,9 +1090,11 @@ def run_reference(args):
     workload (the same spec, built on the host). Rank 0 alone runs."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    if args.config in ("c3", "tc"):
+    if args.config in ("c3", "tc", "attnres"):
         print(json.dumps({"impl": "reference", "unavailable": f"--config {args.config} has no reference CPU path "
-                                                              "(the reference has no draft tree and no tensor cores)"}))
+                                                              "(the reference has no draft tree, no tensor cores, "
+                                                              "and its block attention residual is private to its "
+                                                              "model engine)"}))
         return
     sample = reference_sample(args.config)
     if sample is None:
@@ -1074,10 +1134,11 @@ def main():
     ap.add_argument("--act-terms", type=int, default=0,
                     help="E2M1 activation terms of the MXF4 engine (0: the library default, k3xb_default_act_terms)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", choices=["c5", "c4", "c2", "c3", "tc"], default="c5",
+    ap.add_argument("--config", choices=["c5", "c4", "c2", "c3", "tc", "attnres"], default="c5",
                     help="c5 (default: 8-layer KDA+MoE verify step, expert parallel at N > 1), c4 (2 layers), "
                          "c2 (one MoE layer), c3 (KDA draft tree), tc (tensor-core sweep of the expert GEMM)")
     ap.add_argument("--sequences", type=int, default=1, help="c3: sequences sharing the draft tree")
+    ap.add_argument("--sources", type=int, default=8, help="attnres: block sources besides the prefix")
     ap.add_argument("--experts", type=int, default=0, help="c2 with fewer experts (small profiler case)")
     ap.add_argument("--tokens", type=int, default=0, help="c2 with another verify-token count")
     ap.add_argument("--no-graph", action="store_true", help="c2: time eager launches instead of a CUDA graph")

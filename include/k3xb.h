@@ -627,6 +627,25 @@ int k3xb_attention_residual_norm(k3xb_ctx* ctx, const float* a,
                                  uint32_t hidden, float eps,
                                  float* prefix_out, float* out);
 
+/* The block attention residual of the K3 token graph with many sources
+ * (Engine::attention_residual, runtime/src/model.cpp:645-666; its torch form
+ * reference/k3x_ref/attn_res.py:9-23). For each row t the values are the
+ * S block sources in push order, then the prefix:
+ *   key_d = rms_norm(value_d, norm, eps) (ops.cpp:10-18),
+ *   score_d = key_d . projection, p = softmax over the S + 1 scores,
+ *   out[t] = sum_d p_d * value_d[t], summed in depth order.
+ * Device pointers: prefix, out [T][H]; sources [S][T][H] (depth-major, may
+ * be NULL when S = 0, which gives out = prefix); norm, projection [H]
+ * floats. S <= 63, hidden <= 49152; eps finite and >= 0. Scores are FP64
+ * sums rounded once to float (the reference rounds each product and chains
+ * float adds), so results agree with it to float tolerance, not bit for
+ * bit. */
+int k3xb_block_attention_residual(k3xb_ctx* ctx, const float* prefix,
+                                  const float* sources, uint32_t sources_count,
+                                  uint32_t tokens, uint32_t hidden,
+                                  const float* norm, const float* projection,
+                                  float eps, float* out);
+
 /* prepare_official_moe_route (backend.hpp:384-389; the reference's CUDA
  * backend_cuda.cu:3478-3699) for one position: the MoE input
  * prepare_official_moe_input makes of (a, block), as

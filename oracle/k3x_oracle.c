@@ -321,6 +321,62 @@ int k3xo_attention_residual(const float* prefix, const float* block,
     return K3XO_OK;
 }
 
+/* ops.cpp:10-18 */
+void k3xo_rms_norm_f32(const float* x, const float* weight, size_t n,
+                       float eps, float* out)
+{
+    double squares = 0.0;
+    for (size_t i = 0; i < n; ++i) squares += (double)x[i] * x[i];
+    float inverse = 1.0f / sqrtf((float)(squares / n) + eps);
+    for (size_t i = 0; i < n; ++i) out[i] = x[i] * inverse * weight[i];
+}
+
+/* model.cpp:645-666: values = the S sources in push order, then the prefix;
+ * key = rms_norm(value, norm); score = float inner product of key and
+ * projection (std::inner_product from 0.0F); softmax in float with the sum
+ * taken in depth order; out = sum_d p_d * value_d from 0, in depth order. */
+int k3xo_block_attention_residual(const float* prefix, const float* sources,
+                                  size_t S, size_t T, size_t H,
+                                  const float* norm, const float* proj,
+                                  float eps, float* out)
+{
+    if (!H || !T || (S && !sources)) return K3XO_INVALID_EXTENT;
+    float* key = (float*)malloc(H * sizeof(float));
+    float* scores = (float*)malloc((S + 1) * sizeof(float));
+    if (!key || !scores) {
+        free(key);
+        free(scores);
+        return K3XO_INVALID_EXTENT;
+    }
+    for (size_t t = 0; t < T; ++t) {
+        for (size_t d = 0; d <= S; ++d) {
+            const float* v = d < S ? sources + (d * T + t) * H : prefix + t * H;
+            k3xo_rms_norm_f32(v, norm, H, eps, key);
+            float score = 0.0f;
+            for (size_t i = 0; i < H; ++i) score = score + key[i] * proj[i];
+            scores[d] = score;
+        }
+        float maximum = scores[0];
+        for (size_t d = 1; d <= S; ++d)
+            if (scores[d] > maximum) maximum = scores[d];
+        float denominator = 0.0f;
+        for (size_t d = 0; d <= S; ++d) {
+            scores[d] = expf(scores[d] - maximum);
+            denominator += scores[d];
+        }
+        float* o = out + t * H;
+        for (size_t i = 0; i < H; ++i) o[i] = 0.0f;
+        for (size_t d = 0; d <= S; ++d) {
+            const float p = scores[d] / denominator;
+            const float* v = d < S ? sources + (d * T + t) * H : prefix + t * H;
+            for (size_t i = 0; i < H; ++i) o[i] += p * v[i];
+        }
+    }
+    free(key);
+    free(scores);
+    return K3XO_OK;
+}
+
 /* ------------------------------------------------------------------------ */
 /* router (a)                                                                */
 /* ------------------------------------------------------------------------ */

@@ -80,6 +80,16 @@ int k3xo_rms_norm_bf16(const float* x, const uint16_t* weight, size_t n,
 int k3xo_attention_residual(const float* prefix, const float* block,
                             const uint16_t* norm, const uint16_t* proj,
                             size_t n, float eps, float* out);
+/* ops.cpp:10-18: rms_norm with float weights (FP64 squares, float
+ * inverse, (x * inverse) * weight). */
+void k3xo_rms_norm_f32(const float* x, const float* weight, size_t n,
+                       float eps, float* out);
+/* model.cpp:645-666: block attention residual over S sources [S][T][H]
+ * (depth-major) and the prefix [T][H]; float norm and projection [H]. */
+int k3xo_block_attention_residual(const float* prefix, const float* sources,
+                                  size_t S, size_t T, size_t H,
+                                  const float* norm, const float* proj,
+                                  float eps, float* out);
 
 /* ---- router (a) --------------------------------------------------------- */
 /* official_moe.cpp:255-267: logits[e] = float(sum_h double(bf16 W[e][h]) * x[h]). */

@@ -164,6 +164,9 @@ class Restatement:
         L.k3xo_rms_norm_bf16.argtypes = [_f32p, _u16p, _sz, C.c_float, _f32p]
         L.k3xo_select_routing.argtypes = _SELECT_ROUTING_ARGS
         L.k3xo_attention_residual.argtypes = [_f32p, _f32p, _u16p, _u16p, _sz, C.c_float, _f32p]
+        L.k3xo_rms_norm_f32.argtypes = [_f32p, _f32p, _sz, C.c_float, _f32p]
+        L.k3xo_rms_norm_f32.restype = None
+        L.k3xo_block_attention_residual.argtypes = [_f32p, _f32p, _sz, _sz, _sz, _f32p, _f32p, C.c_float, _f32p]
         L.k3xo_argmax.restype = C.c_uint32
         L.k3xo_argmax.argtypes = [_f32p, _sz]
         L.k3xo_verify_greedy_block.argtypes = [C.c_uint32, _u32p, _sz, _sz, _sz, _u32p,
@@ -404,6 +407,24 @@ class Restatement:
                     "attention_residual")
         return out
 
+    def rms_norm_f32(self, x, weight, eps):
+        """rms_norm (ops.cpp:10-18) with float weights, one row."""
+        x = _c(x, np.float32)
+        out = np.empty_like(x)
+        self.lib.k3xo_rms_norm_f32(x, _c(weight, np.float32), x.size, eps, out)
+        return out
+
+    def block_attention_residual(self, prefix, sources, norm, proj, eps):
+        """model.cpp:645-666 over T rows: prefix [T][H], sources [S][T][H]."""
+        prefix = _c(np.atleast_2d(prefix), np.float32)
+        T, H = prefix.shape
+        sources = _c(np.asarray(sources, np.float32).reshape(-1, T, H), np.float32)
+        out = np.empty_like(prefix)
+        self._check(self.lib.k3xo_block_attention_residual(prefix, sources, sources.shape[0], T, H,
+                                                           _c(norm, np.float32), _c(proj, np.float32), eps, out),
+                    "block_attention_residual")
+        return out
+
     def prepare_input(self, prefix, block, norm, proj, post, eps):
         """prepare_official_moe_input (official_moe.cpp:156-209) for one row:
         attention residual then RMSNorm."""
@@ -529,6 +550,8 @@ class Reference:
         L.k3xr_decode_mxfp4.argtypes = [_u8p, _u8p, _sz, _sz, _sz, _f32p]
         L.k3xr_mxfp4_matmul.argtypes = [_f32p, _u8p, _u8p, _sz, _sz, _sz, _f32p]
         L.k3xr_situ_glu.argtypes = [_f32p, _f32p, _f32p, _sz, C.c_float, C.c_float]
+        L.k3xr_rms_norm.argtypes = [_f32p, _f32p, _f32p, _sz, C.c_float]
+        L.k3xr_rms_norm.restype = None
         L.k3xr_situ_glu.restype = None
         L.k3xr_route_official_moe.argtypes = [_f32p, _u16p, _sz, _sz, _f32p, _sz, _u32p, _f32p,
                                               C.c_void_p]
@@ -579,6 +602,13 @@ class Reference:
         g, u = _c(gate, np.float32), _c(up, np.float32)
         out = np.empty_like(g)
         self.lib.k3xr_situ_glu(out, g, u, g.size, beta, linear_beta)
+        return out
+
+    def rms_norm_f32(self, x, weight, eps):
+        """The reference's rms_norm (ops.cpp:10-18), float weights, one row."""
+        x = _c(x, np.float32)
+        out = np.empty_like(x)
+        self.lib.k3xr_rms_norm(out, x, _c(weight, np.float32), x.size, eps)
         return out
 
     def dense_matvec(self, x, w):

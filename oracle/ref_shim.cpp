@@ -86,6 +86,12 @@ void k3xr_situ_glu(float* out, const float* gate, const float* up, std::size_t n
     k3x::situ_glu({out, n}, {gate, n}, {up, n}, beta, linear(linear_beta));
 }
 
+// rms_norm (ops.cpp:10-18) with float weights: the key of the model's block
+// attention residual (model.cpp:63-67, :652-655).
+void k3xr_rms_norm(float* out, const float* x, const float* weight, std::size_t n, float eps) {
+    k3x::rms_norm({out, n}, {x, n}, {weight, n}, eps);
+}
+
 // prepare_official_moe_input (official_moe.cpp:156-209): attention residual
 // of {block, prefix} then RMSNorm with post_norm; only the three weights it
 // reads are set.

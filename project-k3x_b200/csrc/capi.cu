@@ -1416,6 +1416,19 @@ int k3xb_attention_residual_norm(k3xb_ctx* ctx, const float* a, const float* del
     return launch_attnres_norm(ctx, a, delta, block, rnorm, rproj, post, T, H, eps, prefix_out, out);
 }
 
+int k3xb_block_attention_residual(k3xb_ctx* ctx, const float* prefix, const float* sources, uint32_t S, uint32_t T,
+                                  uint32_t H, const float* norm, const float* projection, float eps, float* out) {
+    K3XB_ENTER(ctx);
+    if (!prefix || (S && !sources) || !norm || !projection || !out || !T || !H)
+        return fail(ctx, K3XB_INVALID_EXTENT, "block attention residual arguments");
+    if (S >= kBlockAttnResMaxDepth)
+        return fail(ctx, K3XB_INVALID_EXTENT, "block attention residual: at most 63 sources");
+    if (T > 0x7fffffffu) return fail(ctx, K3XB_INVALID_EXTENT, "block attention residual: too many rows");
+    if (!std::isfinite(eps) || eps < 0.0f) return fail(ctx, K3XB_INVALID_EXTENT, "eps must be finite and >= 0");
+    PhaseScope ph(ctx, K3XB_PHASE_ATTN_RESIDUAL);
+    return launch_block_attnres(ctx, prefix, sources, S, T, H, norm, projection, eps, out);
+}
+
 int k3xb_prepare_moe_route_host(k3xb_ctx* ctx, const float* a_host, const float* delta_host, const float* block_host,
                                 uint32_t H, const uint16_t* rnorm, const uint16_t* rproj, const uint16_t* post, float eps,
                                 const uint16_t* router, uint32_t E, float* prefix_host, float* hidden_host,

@@ -118,6 +118,10 @@ int launch_mxfp4_matvec(k3xb_ctx* ctx, const uint8_t* packed, const uint8_t* sca
 // resident.cu — the resident weight table
 void release_resident(k3xb_ctx* ctx);
 void resident_stats(const k3xb_ctx* ctx, k3xb_stats* out);
+// attnres.cu — block attention residual over many sources
+constexpr uint32_t kBlockAttnResMaxDepth = 64;   // sources + the prefix
+int launch_block_attnres(k3xb_ctx* ctx, const float* prefix, const float* sources, uint32_t S, uint32_t T, uint32_t H,
+                         const float* norm, const float* proj, float eps, float* out);
 // layer.cu — KDA block and layer steps around the GEMMs
 size_t attnres_smem_bytes(uint32_t H);
 int launch_attnres_norm(k3xb_ctx* ctx, const float* a, const float* delta, const float* block, const uint16_t* rnorm,

@@ -188,6 +188,7 @@ def library() -> C.CDLL:
             "k3xb_kda_block": [vp, C.POINTER(KdaLayer), u32, vp, vp, u32, u32, vp, vp, vp, vp],
             "k3xb_kda_block_commit": [vp, C.POINTER(KdaLayer), vp, vp, u32, u32, vp, vp, vp, vp, vp],
             "k3xb_attention_residual_norm": [vp, vp, vp, vp, vp, vp, vp, u32, u32, f32, vp, vp],
+            "k3xb_block_attention_residual": [vp, vp, vp, u32, u32, u32, vp, vp, f32, vp],
             "k3xb_layer_forward": [vp, C.POINTER(Layer), vp, vp, vp, u32, u32, vp, vp, vp, vp, vp],
             "k3xb_verify_step": [vp, C.POINTER(VerifyModel), C.POINTER(VerifyIO)],
             "k3xb_ep_verify_step": [vp, C.POINTER(VerifyModel), C.POINTER(VerifyIO), u32],
@@ -374,6 +375,14 @@ class Context:
         self._check(self.lib.k3xb_attention_residual_norm(self.h, _p(a), _p(delta), _p(block), _p(norm), _p(proj),
                                                           _p(post), T, H, eps, _p(prefix_out), _p(out)),
                     "attention_residual_norm")
+
+    def block_attention_residual(self, prefix, sources, norm, proj, eps, out):
+        """Depth attention over the block sources [S][T][H] (S may be 0:
+        sources None) and the prefix [T][H] (model.cpp:645-666)."""
+        T, H = prefix.shape
+        S = 0 if sources is None else sources.shape[0]
+        self._check(self.lib.k3xb_block_attention_residual(self.h, _p(prefix), _p(sources), S, T, H, _p(norm),
+                                                           _p(proj), eps, _p(out)), "block_attention_residual")
 
     def layer_forward(self, layer: "Layer", hidden_in, block, parent, conv, recurrent, hidden_out,
                       expert_ids=None, trace=None):

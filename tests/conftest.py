@@ -37,12 +37,14 @@ def ref():
 # them or added on top (golden end-to-end cases, the routing policy, expert
 # parallelism, LatentMoE, the device drafter, the host-I/O entry points,
 # resident weights, phase timing, expert-parallel failure detection, the
-# reference's own layer drivers over the adapter), so that a run which stops at the first failure
+# reference's own layer drivers over the adapter, the block attention
+# residual of the token graph), so that a run which stops at the first failure
 # stops at the lowest broken layer. Files not listed keep their place after
 # these; test_zz_no_alloc.py stays last.
 _GPU_ORDER = ["test_gpu_synth", "test_gpu_parity", "test_gpu_mxf4", "test_gpu_linear", "test_gpu_layer", "test_gpu_golden", "test_gpu_c4_oracle",
               "test_gpu_routing_policy", "test_gpu_ep", "test_gpu_ep_verify", "test_gpu_latent", "test_gpu_draft", "test_gpu_host_io",
-              "test_gpu_resident", "test_gpu_profile", "test_gpu_ep_failure", "test_gpu_reference_drivers"]
+              "test_gpu_resident", "test_gpu_profile", "test_gpu_ep_failure", "test_gpu_reference_drivers",
+              "test_gpu_attnres"]
 
 
 def pytest_collection_modifyitems(session, config, items):

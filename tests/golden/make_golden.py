@@ -7,7 +7,7 @@ fixture stores inputs and the reference's outputs, so the oracle pin
 (tests/test_golden.py) and the GPU parity tests (tests/test_gpu_golden.py)
 run where neither the reference tree nor its build exists.
 
-Run from the repository root: python tests/golden/make_golden.py
+Run from the repository root: python tests/golden/make_golden.py [fixture function ...]
 """
 import os
 import sys
@@ -260,8 +260,43 @@ def verify_greedy(ref):
          count=count)
 
 
+def block_attn_res(ref, rs):
+    """The block attention residual with many sources (model.cpp:645-666):
+    the reference's torch form (reference/k3x_ref/attn_res.py:9-23) on 5 rows
+    x 3 sources, and the reference's own known-answer case
+    (tests/python/test_attn_res.py). The torch form sums in its own order,
+    so it is a float-tolerance pin for the restatement. Skipped when the
+    reference tree is not importable."""
+    ref_root = os.environ.get("K3X_REFERENCE") or os.path.abspath(os.path.join(ROOT, "..", "reference"))
+    pkg = os.path.join(ref_root, "reference")
+    if not os.path.isdir(os.path.join(pkg, "k3x_ref")):
+        print("block_attn_res: reference tree not found, skipped")
+        return
+    sys.path.insert(0, pkg)
+    import torch
+    from k3x_ref.attn_res import apply_attn_res
+    g = np.random.default_rng(1013)
+    T, S, H, eps = 5, 3, 256, 1e-6
+    scale = np.array([0.5, 1.0, 2.0, 4.0], np.float32)[:, None, None]
+    values = (g.normal(size=(S + 1, T, H)) * scale).astype(np.float32)
+    sources, prefix = values[:S], values[S]
+    norm = (1.0 + 0.1 * g.normal(size=H)).astype(np.float32)
+    proj = (g.normal(size=H) / np.sqrt(H)).astype(np.float32)
+    got = apply_attn_res(torch.from_numpy(prefix), torch.from_numpy(np.ascontiguousarray(sources.transpose(1, 0, 2))),
+                         torch.from_numpy(norm), torch.from_numpy(proj), eps).numpy()
+    kat = apply_attn_res(torch.tensor([[1.0, 1.0]]), torch.tensor([[[3.0, 0.0], [0.0, 4.0]]]), torch.ones(2),
+                         torch.tensor([1.0, 0.0]), 0.0).numpy()
+    save("block_attn_res.npz", prefix=prefix, sources=sources, norm=norm, proj=proj, eps=np.float32(eps),
+         torch_out=got, kat_out=kat)
+
+
 def main():
     ref, rs = Reference(), Restatement()
+    if len(sys.argv) > 1:   # named fixtures only
+        for name in sys.argv[1:]:
+            fn = globals()[name]
+            fn(*[a for a, p in ((ref, "ref"), (rs, "rs")) if p in fn.__code__.co_varnames[:fn.__code__.co_argcount]])
+        return
     route(ref)
     expert_major(ref)
     mxfp4(ref, rs)
@@ -273,6 +308,7 @@ def main():
     prepare_input(ref)
     select_routing(ref)
     verify_greedy(ref)
+    block_attn_res(ref, rs)
 
 
 if __name__ == "__main__":
