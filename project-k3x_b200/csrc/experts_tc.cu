@@ -141,29 +141,66 @@ __global__ void __launch_bounds__(1024) worklist_kernel(const uint32_t* group_co
 }
 
 // ---------------------------------------------------------------------------
+// Eight floats to eight E2M1 codes, nibble i = x[i]: the hardware
+// conversion rounds to nearest even on the E2M1 grid and saturates at 6,
+// which is e2m1_code's rounding. A negative value that rounds to zero comes
+// out as code 8 (-0); the split writes 0 there, so the sign bit is kept only
+// on nonzero magnitudes.
+__device__ __forceinline__ uint32_t e2m1_pack8(const float* x) {
+    uint32_t w;
+    asm("{\n.reg .b8 b0, b1, b2, b3;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n"
+        "mov.b32 %0, {b0, b1, b2, b3};\n}"
+        : "=r"(w)
+        : "f"(x[0]), "f"(x[1]), "f"(x[2]), "f"(x[3]), "f"(x[4]), "f"(x[5]), "f"(x[6]), "f"(x[7]));
+    const uint32_t mag = w & 0x77777777u;
+    const uint32_t nonzero = (mag + 0x77777777u) & 0x88888888u;   // bit 3 of each nibble with a magnitude
+    return mag | (w & nonzero);
+}
+
+// One E2M1 term of a 32-element MX block held by one thread (bit-identical
+// to a term of oracle/k3x_oracle.c:k3xo_e2m1_terms): the block maximum, its
+// E8M0 exponent s, each element's code of v * 2^-s, and v replaced by the
+// exact residual. Returns s; w gets the 16 packed bytes (low nibble = even
+// element).
+__device__ __forceinline__ int e2m1_term32(float (&v)[32], uint32_t (&w)[4]) {
+    float m16[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m16[i] = fmaxf(fabsf(v[i]), fabsf(v[i + 16]));
+#pragma unroll
+    for (int h = 8; h > 0; h >>= 1)
+#pragma unroll
+        for (int i = 0; i < h; ++i) m16[i] = fmaxf(m16[i], m16[i + h]);
+    const float amax = m16[0];
+    const int s = amax > 0.0f ? e2m1_block_exponent(amax) : 0;
+    const float inv = exp2i(-s), scale = exp2i(s);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = v[8 * k + i] * inv;
+        w[k] = e2m1_pack8(x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t c = (w[k] >> (4 * i)) & 15u;
+            const float qv = e2m1_magnitude(c & 7u) * scale;
+            v[8 * k + i] = (c & 8u) ? __fadd_rn(v[8 * k + i], qv) : __fsub_rn(v[8 * k + i], qv);
+        }
+    }
+    return s;
+}
+
 // E2M1-term split (bit-identical to oracle/k3x_oracle.c:k3xo_e2m1_terms) of
-// one 32-element MX block held by one thread: per term, the block maximum,
-// its E8M0 exponent, each element's code (round to nearest even on the
-// E2M1 grid), and the exact residual. Term t's 16 packed bytes go to
-// rows[t * row_stride] (low nibble = even element), its scale byte to
-// scales[t * scale_stride].
+// one 32-element MX block held by one thread. Term t's 16 packed bytes go to
+// rows[t * row_stride], its scale byte to scales[t * scale_stride].
 __device__ __forceinline__ void split_block32(float (&v)[32], uint32_t terms, uint8_t* rows, size_t row_stride,
                                               uint8_t* scales, size_t scale_stride) {
     for (uint32_t t = 0; t < terms; ++t) {
-        float amax = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-        const int s = amax > 0.0f ? e2m1_block_exponent(amax) : 0;
-        const float inv = exp2i(-s), scale = exp2i(s);
-        uint32_t w[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const uint32_t code = e2m1_code(fabsf(v[i]) * inv);
-            const bool neg = signbit(v[i]) && code;
-            const float qv = e2m1_magnitude(code) * scale;
-            v[i] = neg ? __fadd_rn(v[i], qv) : __fsub_rn(v[i], qv);
-            w[i / 8] |= (code | (neg ? 8u : 0u)) << (4 * (i % 8));
-        }
+        uint32_t w[4];
+        const int s = e2m1_term32(v, w);
         *reinterpret_cast<uint4*>(rows + t * row_stride) = make_uint4(w[0], w[1], w[2], w[3]);
         scales[t * scale_stride] = static_cast<uint8_t>(s + 127);
     }
@@ -260,20 +297,8 @@ __global__ void __launch_bounds__(256) split_act_kernel(const float* __restrict_
         // term t of token j is MMA row j*terms + t: bytes at row * row_stride + kb * 16, its scale in
         // atom kb / 4 at byte (row % 32) * 16 + (row / 32) * 4 + kb % 4
         for (uint32_t t = 0; t < terms; ++t) {
-            float amax = 0.0f;
-#pragma unroll
-            for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
-            const int s = amax > 0.0f ? e2m1_block_exponent(amax) : 0;
-            const float inv = exp2i(-s), scale = exp2i(s);
-            uint32_t w[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const uint32_t code = e2m1_code(fabsf(v[e]) * inv);
-                const bool neg = signbit(v[e]) && code;
-                const float qv = e2m1_magnitude(code) * scale;
-                v[e] = neg ? __fadd_rn(v[e], qv) : __fsub_rn(v[e], qv);
-                w[e / 8] |= (code | (neg ? 8u : 0u)) << (4 * (e % 8));
-            }
+            uint32_t w[4];
+            const int s = e2m1_term32(v, w);
             const uint32_t row = j * terms + t;
             *reinterpret_cast<uint4*>(base + static_cast<size_t>(row) * row_stride + kb * 16) =
                 make_uint4(w[0], w[1], w[2], w[3]);
