@@ -517,6 +517,58 @@ class ReferenceSampleC2:
                 f"route_official_moe, mxfp4_matmul and situ_glu on {self.n} threads, {dt:.2f} s per sample")
 
 
+class AttnResSample:
+    """The CPU arm of the attnres line: the block attention residual over
+    all 576 positions (the whole workload; it takes well under a second of
+    CPU), through the pinned restatement of model.cpp:645-666
+    (oracle/k3x_oracle.c:k3xo_block_attention_residual). The reference's own
+    function is private to its model engine, so this is the port. Inputs
+    are the GPU arm's, built on the host with the generator's restatement;
+    the positions are split into one contiguous chunk per host thread."""
+
+    def __init__(self, sources):
+        import numpy as np
+
+        from oracle import Restatement
+        self.rs = Restatement()
+        self.threads = host_threads()
+        T, H, S = C5["sequences"] * (C5["drafts"] + 1), C5["hidden"], sources
+        self.T, self.S, self.n = T, S, T
+        t0 = time.perf_counter()
+        spec = ("f32", ((S + 1) * T, H), 11, 1, 1.0, 0.0)   # the GPU arm's [S + 1][T][H] values, flattened
+        values = np.stack([host_tensor(self.rs, spec, self.threads, rows=(d * T, (d + 1) * T)) for d in range(S + 1)])
+        self.norm = host_tensor(self.rs, ("f32", (H,), 11, 2, 0.1, 1.0))
+        self.proj = host_tensor(self.rs, ("f32", (H,), 11, 3, 3.0 / H ** 0.5, 0.0))
+        step = (T + self.threads - 1) // self.threads
+        self.chunks = [(np.ascontiguousarray(values[S, a:a + step]), np.ascontiguousarray(values[:S, a:a + step]))
+                       for a in range(0, T, step)]
+        self.build_s = time.perf_counter() - t0
+
+    def step(self):
+        t0 = time.perf_counter()
+        parallel(lambda c: self.rs.block_attention_residual(c[0], c[1], self.norm, self.proj, 1e-6), self.chunks,
+                 len(self.chunks))
+        return time.perf_counter() - t0
+
+    def units(self):
+        return float(self.T)
+
+    def describe(self, dt):
+        return (f"all {self.T} positions x {self.S + 1} depths at H {C5['hidden']} through the restatement of "
+                f"model.cpp:645-666 (the reference's function is private to its engine), {len(self.chunks)} "
+                f"threads, {dt * 1e3:.1f} ms per step")
+
+
+def attnres_cpu_baseline(sources):
+    """The attnres line's CPU port on this host: one untimed step, then the
+    mean of three timed."""
+    s = AttnResSample(sources)
+    s.step()
+    dt = statistics.mean(s.step() for _ in range(3))
+    return {"value": s.units() / dt, "unit": "positions/s", "cores": len(s.chunks), "kind": "port",
+            "sample": s.describe(dt) + f"; built on the host in {s.build_s:.1f} s"}
+
+
 def reference_sample(cfg_name):
     from oracle import have_reference
     if not have_reference():
@@ -987,6 +1039,8 @@ def run_attnres(args, rank, world, local, ctx, stream):
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = attnres_cpu_baseline(S)
     if rank == 0:
         print(json.dumps(result), flush=True)
 
@@ -1084,17 +1138,43 @@ def run_ours(args):
             dist.destroy_process_group()
 
 
+def run_reference_attnres(args):
+    """--impl reference --config attnres: the port (the reference's function
+    is private to its engine) on all host threads, same metric and config."""
+    sample = AttnResSample(args.sources)
+    times = []
+    for i in range(args.warmup + args.steps):
+        dt = sample.step()
+        if i >= args.warmup:
+            times.append(dt)
+    dt = statistics.mean(times)
+    value = sample.units() / dt
+    print(json.dumps({
+        "impl": "reference", "metric": "attention-residual positions/s", "value": value, "unit": "positions/s",
+        "n_gpus": 0, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (FP64 squares; the reference's float chains)",
+        "data": "synthetic (the same spec, built on the host by the generator's restatement)",
+        "config": {"workload": "block attention residual over many sources", "positions": sample.T,
+                   "hidden": C5["hidden"], "sources": sample.S,
+                   "l2": "flushed (256 MB write) before every timed step"},
+        "cpu_baseline": {"value": value, "unit": "positions/s", "cores": len(sample.chunks), "kind": "port",
+                         "sample": sample.describe(dt)},
+        "e2e": {"value": value, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def run_reference(args):
     """--impl reference: the reference's own CPU implementation of the path
     (oracle/_ref), on this host's cores, on a bounded sample of the same
     workload (the same spec, built on the host). Rank 0 alone runs."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    if args.config in ("c3", "tc", "attnres"):
+    if args.config in ("c3", "tc"):
         print(json.dumps({"impl": "reference", "unavailable": f"--config {args.config} has no reference CPU path "
-                                                              "(the reference has no draft tree, no tensor cores, "
-                                                              "and its block attention residual is private to its "
-                                                              "model engine)"}))
+                                                              "(the reference has no draft tree and no tensor cores)"}))
+        return
+    if args.config == "attnres":
+        run_reference_attnres(args)
         return
     sample = reference_sample(args.config)
     if sample is None:
