@@ -79,6 +79,62 @@ def test_e2m1_terms_exact_decomposition(rs):
             assert resid <= np.abs(x).max() * 2.0 ** (-2 * nterms + 1)
 
 
+_E2M1_GRID = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
+
+
+def _rne_e2m1(v):
+    """Round to nearest on the E2M1 grid, ties to the even code (mantissa bit
+    0), saturating at 6; the sign bit only on a nonzero code."""
+    a = abs(float(v))
+    d = np.abs(_E2M1_GRID - min(a, 6.0))
+    best = np.flatnonzero(d == d.min())
+    code = int(best[0]) if len(best) == 1 else int(best[best % 2 == 0][0])
+    return code | (8 if (np.signbit(v) and code) else 0)
+
+
+def test_e2m1_split_rounding_is_round_half_even(rs):
+    """The split's per-element rule is round-half-even onto the E2M1 grid with
+    saturation at 6, and a negative value that rounds to zero gets code 0.
+    That is what lets the device split use the hardware conversion
+    (cvt.rn.satfinite.e2m1x2.f32, plus a fix-up of -0 codes) and stay
+    bit-identical. A block whose maximum is 6 has scale exponent 0, so its
+    first term's codes are the rounding of the values themselves."""
+    g = np.random.default_rng(17)
+    ties = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0])
+    near = np.concatenate([np.nextafter(ties.astype(np.float32), np.float32(0)),
+                           np.nextafter(ties.astype(np.float32), np.float32(7))])
+    vals = np.concatenate([np.arange(-384, 385) / 64.0, ties, -ties, near, -near, g.uniform(-6, 6, 500),
+                           [0.0, -0.0, -1e-30, 1e-30, -0.2, 5.999, -5.5]]).astype(np.float32)
+    for i in range(0, len(vals), 31):
+        chunk = vals[i:i + 31]
+        block = np.zeros(32, np.float32)
+        block[0] = 6.0
+        block[1:1 + len(chunk)] = chunk
+        packed, scales, _ = rs.e2m1_terms(block, 1)
+        assert scales[0] == 127
+        for j in range(32):
+            nib = (int(packed[0][j // 2]) >> (4 * (j % 2))) & 15
+            assert nib == _rne_e2m1(block[j]), (block[j], nib)
+
+
+def test_e2m1_negative_zero_fixup_arithmetic():
+    """The device split's fix-up after the hardware conversion
+    (experts_tc.cu:e2m1_pack8): mag = w & 0x77777777, and
+    (mag + 0x77777777) & 0x88888888 marks the nibbles with a nonzero
+    magnitude, so mag | (w & that) keeps a sign bit only there."""
+    g = np.random.default_rng(19)
+    words = np.concatenate([g.integers(0, 2 ** 32, size=20000, dtype=np.uint64),
+                            [0x88888888, 0x80000008, 0xF0F0F0F0, 0x08080808, 0]]).astype(np.uint64)
+    for w in words.tolist():
+        mag = w & 0x77777777
+        fixed = mag | (w & ((mag + 0x77777777) & 0x88888888))
+        want = 0
+        for k in range(8):
+            n = (w >> (4 * k)) & 15
+            want |= (n if n & 7 else 0) << (4 * k)
+        assert fixed == want, hex(w)
+
+
 # ---------------------------------------------------------- activations ----
 
 def test_situ_glu_matches_reference(rs, ref):
