@@ -1235,3 +1235,91 @@ void k3xo_fill_normal_mxfp4(uint8_t* packed, uint8_t* scales, size_t blocks, uin
         k3xo_quantize_mxfp4(v, 1, 32, packed + b * 16, scales + b);
     }
 }
+
+/* ------------------------------------------------------------------------ */
+/* gated MLA (model.cpp:755-811) and KV crop (model.cpp:1235-1251)           */
+/* ------------------------------------------------------------------------ */
+
+static float mla_sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }   /* model.cpp:60 */
+
+int k3xo_mla_step(const k3xo_mla_weights* w, const float* x, float* keys, float* values,
+                  float* shared, size_t capacity, size_t* length, float* out)
+{
+    if (!w || !x || !keys || !values || !shared || !length || !out || *length >= capacity)
+        return K3XO_INVALID_EXTENT;
+    const size_t H = w->hidden, nh = w->heads, qm = w->q_main, qe = w->q_extra, vd = w->value_dim;
+    const size_t qw = qm + qe;
+    float* q_latent = (float*)malloc(w->q_rank * sizeof(float));
+    float* q_normed = (float*)malloc(w->q_rank * sizeof(float));
+    float* query = (float*)malloc(nh * qw * sizeof(float));
+    float* compressed = (float*)malloc((w->kv_rank + qe) * sizeof(float));
+    float* latent = (float*)malloc(w->kv_rank * sizeof(float));
+    float* expanded = (float*)malloc(nh * (qm + vd) * sizeof(float));
+    float* merged = (float*)calloc(nh * vd, sizeof(float));
+    float* gate = (float*)malloc(nh * vd * sizeof(float));
+    float* scores = (float*)malloc((*length + 1) * sizeof(float));
+    int st = K3XO_INVALID_EXTENT;
+    if (!q_latent || !q_normed || !query || !compressed || !latent || !expanded || !merged || !gate || !scores)
+        goto done;
+    /* model.cpp:758-772: query from the q latent, key/value from the kv latent */
+    k3xo_dense_matvec(x, w->q_a_proj, w->q_rank, H, q_latent);
+    k3xo_rms_norm_f32(q_latent, w->q_a_norm, w->q_rank, w->eps, q_normed);
+    k3xo_dense_matvec(q_normed, w->q_b_proj, nh * qw, w->q_rank, query);
+    k3xo_dense_matvec(x, w->kv_a_proj, w->kv_rank + qe, H, compressed);
+    k3xo_rms_norm_f32(compressed, w->kv_a_norm, w->kv_rank, w->eps, latent);
+    k3xo_dense_matvec(latent, w->kv_b_proj, nh * (qm + vd), w->kv_rank, expanded);
+    /* model.cpp:773-784: append this position */
+    const size_t p0 = (*length)++;
+    memcpy(shared + p0 * qe, compressed + w->kv_rank, qe * sizeof(float));
+    for (size_t h = 0; h < nh; ++h) {
+        memcpy(keys + (p0 * nh + h) * qm, expanded + h * (qm + vd), qm * sizeof(float));
+        memcpy(values + (p0 * nh + h) * vd, expanded + h * (qm + vd) + qm, vd * sizeof(float));
+    }
+    /* model.cpp:785-804: per head, FP64 sums of float products, float softmax */
+    const float scale = 1.0f / sqrtf((float)qw);
+    const size_t n = *length;
+    for (size_t h = 0; h < nh; ++h) {
+        for (size_t p = 0; p < n; ++p) {
+            double score = 0.0;
+            for (size_t i = 0; i < qm; ++i)
+                score += query[h * qw + i] * keys[(p * nh + h) * qm + i];
+            for (size_t i = 0; i < qe; ++i)
+                score += query[h * qw + qm + i] * shared[p * qe + i];
+            scores[p] = (float)score * scale;
+        }
+        float maximum = scores[0];
+        for (size_t p = 1; p < n; ++p)
+            if (scores[p] > maximum) maximum = scores[p];
+        float denominator = 0.0f;
+        for (size_t p = 0; p < n; ++p) {
+            scores[p] = expf(scores[p] - maximum);
+            denominator += scores[p];
+        }
+        for (size_t p = 0; p < n; ++p)
+            for (size_t i = 0; i < vd; ++i)
+                merged[h * vd + i] += scores[p] / denominator * values[(p * nh + h) * vd + i];
+    }
+    /* model.cpp:805-810: output gate, then o_proj */
+    k3xo_dense_matvec(x, w->g_proj, nh * vd, H, gate);
+    for (size_t i = 0; i < nh * vd; ++i) merged[i] *= mla_sigmoid(gate[i]);
+    k3xo_dense_matvec(merged, w->o_proj, H, nh * vd, out);
+    st = K3XO_OK;
+done:
+    free(q_latent);
+    free(q_normed);
+    free(query);
+    free(compressed);
+    free(latent);
+    free(expanded);
+    free(merged);
+    free(gate);
+    free(scores);
+    return st;
+}
+
+int k3xo_mla_crop(size_t* length, size_t keep)
+{
+    if (!length || keep > *length) return K3XO_INVALID_EXTENT;
+    *length = keep;
+    return K3XO_OK;
+}

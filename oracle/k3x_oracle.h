@@ -262,6 +262,31 @@ void k3xo_fill_normal_bf16(uint16_t* out, size_t n, uint64_t first, uint64_t see
 void k3xo_fill_normal_mxfp4(uint8_t* packed, uint8_t* scales, size_t blocks, uint64_t first,
                             uint64_t seed, uint64_t stream, float sigma);
 
+/* ---- gated MLA (model.cpp:755-811) and its KV crop (model.cpp:1235-1251) -- */
+/* Weights are f32 [rows][cols]; the products are the CPU backend's FP64
+ * dense_matvec (backend_cpu.cpp:23-47), the norms ops.cpp:10-18. */
+typedef struct {
+    size_t hidden, heads, q_rank, kv_rank, q_main, q_extra, value_dim;
+    float eps;
+    const float* q_a_proj;    /* [q_rank][hidden] */
+    const float* q_a_norm;    /* [q_rank] */
+    const float* q_b_proj;    /* [heads * (q_main + q_extra)][q_rank] */
+    const float* kv_a_proj;   /* [kv_rank + q_extra][hidden] */
+    const float* kv_a_norm;   /* [kv_rank] */
+    const float* kv_b_proj;   /* [heads * (q_main + value_dim)][kv_rank] */
+    const float* g_proj;      /* [heads * value_dim][hidden] */
+    const float* o_proj;      /* [hidden][heads * value_dim] */
+} k3xo_mla_weights;
+/* One position: appends its key, value and shared key at *length (the
+ * state is position-major: keys [cap][heads][q_main], values
+ * [cap][heads][value_dim], shared [cap][q_extra]), attends over positions
+ * 0 .. *length, writes out [hidden] and increments *length. */
+int k3xo_mla_step(const k3xo_mla_weights* w, const float* x, float* keys, float* values,
+                  float* shared, size_t capacity, size_t* length, float* out);
+/* Crop to `keep` positions (a rejected draft's rollback); keep > *length
+ * is invalid, as the reference's restore refuses it. */
+int k3xo_mla_crop(size_t* length, size_t keep);
+
 #ifdef __cplusplus
 }
 #endif

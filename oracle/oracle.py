@@ -96,6 +96,19 @@ class _KdaWeights(C.Structure):
     ]
 
 
+class _MlaWeights(C.Structure):
+    _fields_ = [
+        ("hidden", _sz), ("heads", _sz), ("q_rank", _sz), ("kv_rank", _sz), ("q_main", _sz), ("q_extra", _sz),
+        ("value_dim", _sz), ("eps", C.c_float),
+        ("q_a_proj", C.c_void_p), ("q_a_norm", C.c_void_p), ("q_b_proj", C.c_void_p),
+        ("kv_a_proj", C.c_void_p), ("kv_a_norm", C.c_void_p), ("kv_b_proj", C.c_void_p),
+        ("g_proj", C.c_void_p), ("o_proj", C.c_void_p),
+    ]
+
+
+MLA_TENSORS = ("q_a_proj", "q_a_norm", "q_b_proj", "kv_a_proj", "kv_a_norm", "kv_b_proj", "g_proj", "o_proj")
+
+
 def moe_struct(layer: dict):
     """Builds the C layer descriptor from a dict of numpy arrays; returns
     (struct, keepalive)."""
@@ -167,6 +180,8 @@ class Restatement:
         L.k3xo_rms_norm_f32.argtypes = [_f32p, _f32p, _sz, C.c_float, _f32p]
         L.k3xo_rms_norm_f32.restype = None
         L.k3xo_block_attention_residual.argtypes = [_f32p, _f32p, _sz, _sz, _sz, _f32p, _f32p, C.c_float, _f32p]
+        L.k3xo_mla_step.argtypes = [C.c_void_p, _f32p, _f32p, _f32p, _f32p, _sz, _szp, _f32p]
+        L.k3xo_mla_crop.argtypes = [_szp, _sz]
         L.k3xo_argmax.restype = C.c_uint32
         L.k3xo_argmax.argtypes = [_f32p, _sz]
         L.k3xo_verify_greedy_block.argtypes = [C.c_uint32, _u32p, _sz, _sz, _sz, _u32p,
@@ -424,6 +439,41 @@ class Restatement:
                                                            _c(norm, np.float32), _c(proj, np.float32), eps, out),
                     "block_attention_residual")
         return out
+
+    def mla_state(self, w: dict, capacity):
+        """An empty MLA state (model.cpp:70): position-major keys, values and
+        shared keys with room for `capacity` positions."""
+        return {"keys": np.zeros((capacity, w["heads"], w["q_main"]), np.float32),
+                "values": np.zeros((capacity, w["heads"], w["value_dim"]), np.float32),
+                "shared": np.zeros((capacity, w["q_extra"]), np.float32), "length": 0}
+
+    def mla_prefill(self, w: dict, x, state=None, capacity=64):
+        """Gated MLA (model.cpp:755-811) over the rows of x, one position at a
+        time, appending to `state` (made empty when None). w holds the dims
+        (hidden, heads, q_rank, kv_rank, q_main, q_extra, value_dim, eps) and
+        the f32 weights of MLA_TENSORS."""
+        x = _c(np.atleast_2d(x), np.float32)
+        st = state if state is not None else self.mla_state(w, capacity)
+        keep = [_c(w[k], np.float32) for k in MLA_TENSORS]
+        ws = _MlaWeights(w["hidden"], w["heads"], w["q_rank"], w["kv_rank"], w["q_main"], w["q_extra"],
+                         w["value_dim"], w["eps"], *(a.ctypes.data for a in keep))
+        out = np.empty((x.shape[0], w["hidden"]), np.float32)
+        length = C.c_size_t(st["length"])
+        for i in range(x.shape[0]):
+            row = np.empty(w["hidden"], np.float32)
+            self._check(self.lib.k3xo_mla_step(C.byref(ws), x[i], st["keys"], st["values"], st["shared"],
+                                               st["keys"].shape[0], C.byref(length), row), "mla_step")
+            out[i] = row
+        st["length"] = length.value
+        del keep
+        return out, st
+
+    def mla_crop(self, state, keep):
+        """The rollback of rejected drafts (model.cpp:1235-1251)."""
+        length = C.c_size_t(state["length"])
+        self._check(self.lib.k3xo_mla_crop(C.byref(length), keep), "mla_crop")
+        state["length"] = length.value
+        return state
 
     def prepare_input(self, prefix, block, norm, proj, post, eps):
         """prepare_official_moe_input (official_moe.cpp:156-209) for one row:

@@ -290,6 +290,39 @@ def block_attn_res(ref, rs):
          torch_out=got, kat_out=kat)
 
 
+def mla(ref, rs):
+    """The gated MLA (model.cpp:755-811) through the reference's torch form
+    (reference/k3x_ref/mla.py: mla_prefill, NoPE with a shared extra key) at
+    the reference's default synthetic config, 5 positions from an empty
+    state: outputs and the final keys, values and shared keys (position-major
+    here). The torch form sums in its own order, so it is a float-tolerance
+    pin. Skipped when the reference tree is not importable."""
+    ref_root = os.environ.get("K3X_REFERENCE") or os.path.abspath(os.path.join(ROOT, "..", "reference"))
+    pkg = os.path.join(ref_root, "reference")
+    if not os.path.isdir(os.path.join(pkg, "k3x_ref")):
+        print("mla: reference tree not found, skipped")
+        return
+    sys.path.insert(0, pkg)
+    import torch
+    from k3x_ref.config import SyntheticK3Config
+    from k3x_ref.mla import MLAWeights, mla_prefill
+    cfg = SyntheticK3Config.default()
+    H, nh, qr, kr = cfg.hidden_size, cfg.mla_heads, cfg.q_lora_rank, cfg.kv_lora_rank
+    qm, qe, vd = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim
+    g = np.random.default_rng(1019)
+    f = lambda *shape, sd=0.15: (g.normal(0, sd, size=shape)).astype(np.float32)
+    w = dict(q_a_proj=f(qr, H), q_a_norm=(1 + f(qr, sd=0.1)), q_b_proj=f(nh * (qm + qe), qr),
+             kv_a_proj=f(kr + qe, H), kv_a_norm=(1 + f(kr, sd=0.1)), kv_b_proj=f(nh * (qm + vd), kr),
+             g_proj=f(nh * vd, H), o_proj=f(H, nh * vd))
+    x = g.normal(size=(5, H)).astype(np.float32)
+    t = {k: torch.from_numpy(v) for k, v in w.items()}
+    out, st = mla_prefill(torch.from_numpy(x).reshape(1, 5, H), MLAWeights(**t), None, cfg)
+    save("mla.npz", x=x, eps=np.float32(cfg.rms_norm_eps),
+         dims=np.array([H, nh, qr, kr, qm, qe, vd], np.int64), torch_out=out.reshape(5, H).numpy(),
+         torch_keys=st.keys[0].transpose(0, 1).numpy(), torch_values=st.values[0].transpose(0, 1).numpy(),
+         torch_shared=st.shared_keys[0, 0].numpy(), **w)
+
+
 def main():
     ref, rs = Reference(), Restatement()
     if len(sys.argv) > 1:   # named fixtures only
@@ -309,6 +342,7 @@ def main():
     select_routing(ref)
     verify_greedy(ref)
     block_attn_res(ref, rs)
+    mla(ref, rs)
 
 
 if __name__ == "__main__":
