@@ -1242,78 +1242,162 @@ void k3xo_fill_normal_mxfp4(uint8_t* packed, uint8_t* scales, size_t blocks, uin
 
 static float mla_sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }   /* model.cpp:60 */
 
+/* model.cpp:758-772: one position's query [heads][q_main + q_extra], its
+ * key [heads][q_main], value [heads][value_dim] and shared key [q_extra]. */
+static int mla_project(const k3xo_mla_weights* w, const float* x, float* query, float* key,
+                       float* value, float* shared_key)
+{
+    const size_t H = w->hidden, nh = w->heads, qm = w->q_main, qe = w->q_extra, vd = w->value_dim;
+    float* q_latent = (float*)malloc(w->q_rank * sizeof(float));
+    float* q_normed = (float*)malloc(w->q_rank * sizeof(float));
+    float* compressed = (float*)malloc((w->kv_rank + qe) * sizeof(float));
+    float* latent = (float*)malloc(w->kv_rank * sizeof(float));
+    float* expanded = (float*)malloc(nh * (qm + vd) * sizeof(float));
+    int st = K3XO_INVALID_EXTENT;
+    if (q_latent && q_normed && compressed && latent && expanded) {
+        k3xo_dense_matvec(x, w->q_a_proj, w->q_rank, H, q_latent);
+        k3xo_rms_norm_f32(q_latent, w->q_a_norm, w->q_rank, w->eps, q_normed);
+        k3xo_dense_matvec(q_normed, w->q_b_proj, nh * (qm + qe), w->q_rank, query);
+        k3xo_dense_matvec(x, w->kv_a_proj, w->kv_rank + qe, H, compressed);
+        k3xo_rms_norm_f32(compressed, w->kv_a_norm, w->kv_rank, w->eps, latent);
+        k3xo_dense_matvec(latent, w->kv_b_proj, nh * (qm + vd), w->kv_rank, expanded);
+        memcpy(shared_key, compressed + w->kv_rank, qe * sizeof(float));
+        for (size_t h = 0; h < nh; ++h) {
+            memcpy(key + h * qm, expanded + h * (qm + vd), qm * sizeof(float));
+            memcpy(value + h * vd, expanded + h * (qm + vd) + qm, vd * sizeof(float));
+        }
+        st = K3XO_OK;
+    }
+    free(q_latent);
+    free(q_normed);
+    free(compressed);
+    free(latent);
+    free(expanded);
+    return st;
+}
+
+/* model.cpp:785-810: attention of one query over n positions in the given
+ * order (position p's key rows kp[p] [heads][q_main], values vp[p]
+ * [heads][value_dim], shared key sp[p] [q_extra]), FP64 sums of float
+ * products, float softmax, the output gate and o_proj. */
+static int mla_attend(const k3xo_mla_weights* w, const float* x, const float* query,
+                      const float* const* kp, const float* const* vp, const float* const* sp,
+                      size_t n, float* out)
+{
+    const size_t H = w->hidden, nh = w->heads, qm = w->q_main, qe = w->q_extra, vd = w->value_dim;
+    const size_t qw = qm + qe;
+    float* merged = (float*)calloc(nh * vd, sizeof(float));
+    float* gate = (float*)malloc(nh * vd * sizeof(float));
+    float* scores = (float*)malloc(n * sizeof(float));
+    int st = K3XO_INVALID_EXTENT;
+    if (merged && gate && scores && n) {
+        const float scale = 1.0f / sqrtf((float)qw);
+        for (size_t h = 0; h < nh; ++h) {
+            for (size_t p = 0; p < n; ++p) {
+                double score = 0.0;
+                for (size_t i = 0; i < qm; ++i) score += query[h * qw + i] * kp[p][h * qm + i];
+                for (size_t i = 0; i < qe; ++i) score += query[h * qw + qm + i] * sp[p][i];
+                scores[p] = (float)score * scale;
+            }
+            float maximum = scores[0];
+            for (size_t p = 1; p < n; ++p)
+                if (scores[p] > maximum) maximum = scores[p];
+            float denominator = 0.0f;
+            for (size_t p = 0; p < n; ++p) {
+                scores[p] = expf(scores[p] - maximum);
+                denominator += scores[p];
+            }
+            for (size_t p = 0; p < n; ++p)
+                for (size_t i = 0; i < vd; ++i)
+                    merged[h * vd + i] += scores[p] / denominator * vp[p][h * vd + i];
+        }
+        k3xo_dense_matvec(x, w->g_proj, nh * vd, H, gate);
+        for (size_t i = 0; i < nh * vd; ++i) merged[i] *= mla_sigmoid(gate[i]);
+        k3xo_dense_matvec(merged, w->o_proj, H, nh * vd, out);
+        st = K3XO_OK;
+    }
+    free(merged);
+    free(gate);
+    free(scores);
+    return st;
+}
+
 int k3xo_mla_step(const k3xo_mla_weights* w, const float* x, float* keys, float* values,
                   float* shared, size_t capacity, size_t* length, float* out)
 {
     if (!w || !x || !keys || !values || !shared || !length || !out || *length >= capacity)
         return K3XO_INVALID_EXTENT;
-    const size_t H = w->hidden, nh = w->heads, qm = w->q_main, qe = w->q_extra, vd = w->value_dim;
-    const size_t qw = qm + qe;
-    float* q_latent = (float*)malloc(w->q_rank * sizeof(float));
-    float* q_normed = (float*)malloc(w->q_rank * sizeof(float));
-    float* query = (float*)malloc(nh * qw * sizeof(float));
-    float* compressed = (float*)malloc((w->kv_rank + qe) * sizeof(float));
-    float* latent = (float*)malloc(w->kv_rank * sizeof(float));
-    float* expanded = (float*)malloc(nh * (qm + vd) * sizeof(float));
-    float* merged = (float*)calloc(nh * vd, sizeof(float));
-    float* gate = (float*)malloc(nh * vd * sizeof(float));
-    float* scores = (float*)malloc((*length + 1) * sizeof(float));
+    const size_t nh = w->heads, qm = w->q_main, qe = w->q_extra, vd = w->value_dim;
+    const size_t p0 = *length, n = p0 + 1;
+    float* query = (float*)malloc(nh * (qm + qe) * sizeof(float));
+    const float** kp = (const float**)malloc(n * sizeof(float*));
+    const float** vp = (const float**)malloc(n * sizeof(float*));
+    const float** sp = (const float**)malloc(n * sizeof(float*));
     int st = K3XO_INVALID_EXTENT;
-    if (!q_latent || !q_normed || !query || !compressed || !latent || !expanded || !merged || !gate || !scores)
-        goto done;
-    /* model.cpp:758-772: query from the q latent, key/value from the kv latent */
-    k3xo_dense_matvec(x, w->q_a_proj, w->q_rank, H, q_latent);
-    k3xo_rms_norm_f32(q_latent, w->q_a_norm, w->q_rank, w->eps, q_normed);
-    k3xo_dense_matvec(q_normed, w->q_b_proj, nh * qw, w->q_rank, query);
-    k3xo_dense_matvec(x, w->kv_a_proj, w->kv_rank + qe, H, compressed);
-    k3xo_rms_norm_f32(compressed, w->kv_a_norm, w->kv_rank, w->eps, latent);
-    k3xo_dense_matvec(latent, w->kv_b_proj, nh * (qm + vd), w->kv_rank, expanded);
-    /* model.cpp:773-784: append this position */
-    const size_t p0 = (*length)++;
-    memcpy(shared + p0 * qe, compressed + w->kv_rank, qe * sizeof(float));
-    for (size_t h = 0; h < nh; ++h) {
-        memcpy(keys + (p0 * nh + h) * qm, expanded + h * (qm + vd), qm * sizeof(float));
-        memcpy(values + (p0 * nh + h) * vd, expanded + h * (qm + vd) + qm, vd * sizeof(float));
-    }
-    /* model.cpp:785-804: per head, FP64 sums of float products, float softmax */
-    const float scale = 1.0f / sqrtf((float)qw);
-    const size_t n = *length;
-    for (size_t h = 0; h < nh; ++h) {
-        for (size_t p = 0; p < n; ++p) {
-            double score = 0.0;
-            for (size_t i = 0; i < qm; ++i)
-                score += query[h * qw + i] * keys[(p * nh + h) * qm + i];
-            for (size_t i = 0; i < qe; ++i)
-                score += query[h * qw + qm + i] * shared[p * qe + i];
-            scores[p] = (float)score * scale;
+    if (query && kp && vp && sp) {
+        /* model.cpp:773-784: append this position, then attend over all */
+        st = mla_project(w, x, query, keys + p0 * nh * qm, values + p0 * nh * vd, shared + p0 * qe);
+        if (st == K3XO_OK) {
+            *length = n;
+            for (size_t p = 0; p < n; ++p) {
+                kp[p] = keys + p * nh * qm;
+                vp[p] = values + p * nh * vd;
+                sp[p] = shared + p * qe;
+            }
+            st = mla_attend(w, x, query, kp, vp, sp, n, out);
         }
-        float maximum = scores[0];
-        for (size_t p = 1; p < n; ++p)
-            if (scores[p] > maximum) maximum = scores[p];
-        float denominator = 0.0f;
-        for (size_t p = 0; p < n; ++p) {
-            scores[p] = expf(scores[p] - maximum);
-            denominator += scores[p];
-        }
-        for (size_t p = 0; p < n; ++p)
-            for (size_t i = 0; i < vd; ++i)
-                merged[h * vd + i] += scores[p] / denominator * values[(p * nh + h) * vd + i];
     }
-    /* model.cpp:805-810: output gate, then o_proj */
-    k3xo_dense_matvec(x, w->g_proj, nh * vd, H, gate);
-    for (size_t i = 0; i < nh * vd; ++i) merged[i] *= mla_sigmoid(gate[i]);
-    k3xo_dense_matvec(merged, w->o_proj, H, nh * vd, out);
-    st = K3XO_OK;
-done:
-    free(q_latent);
-    free(q_normed);
     free(query);
-    free(compressed);
-    free(latent);
-    free(expanded);
-    free(merged);
-    free(gate);
-    free(scores);
+    free(kp);
+    free(vp);
+    free(sp);
+    return st;
+}
+
+int k3xo_mla_tree(const k3xo_mla_weights* w, const float* keys, const float* values,
+                  const float* shared, size_t length, const int32_t* parent, size_t nodes,
+                  const float* x, float* node_keys, float* node_values, float* node_shared,
+                  float* out)
+{
+    if (!w || (length && (!keys || !values || !shared)) || !parent || !nodes || !x || !node_keys ||
+        !node_values || !node_shared || !out)
+        return K3XO_INVALID_EXTENT;
+    for (size_t i = 0; i < nodes; ++i)
+        if (parent[i] < -1 || parent[i] >= (int32_t)i) return K3XO_INVALID_EXTENT;
+    const size_t H = w->hidden, nh = w->heads, qm = w->q_main, qe = w->q_extra, vd = w->value_dim;
+    const size_t cap = length + nodes;
+    float* query = (float*)malloc(nh * (qm + qe) * sizeof(float));
+    size_t* path = (size_t*)malloc(nodes * sizeof(size_t));
+    const float** kp = (const float**)malloc(cap * sizeof(float*));
+    const float** vp = (const float**)malloc(cap * sizeof(float*));
+    const float** sp = (const float**)malloc(cap * sizeof(float*));
+    int st = (query && path && kp && vp && sp) ? K3XO_OK : K3XO_INVALID_EXTENT;
+    for (size_t p = 0; st == K3XO_OK && p < length; ++p) {
+        kp[p] = keys + p * nh * qm;
+        vp[p] = values + p * nh * vd;
+        sp[p] = shared + p * qe;
+    }
+    for (size_t i = 0; st == K3XO_OK && i < nodes; ++i) {
+        st = mla_project(w, x + i * H, query, node_keys + i * nh * qm, node_values + i * nh * vd,
+                         node_shared + i * qe);
+        if (st != K3XO_OK) break;
+        /* the committed positions, then the node's ancestors root first and
+         * the node itself: on a chain, the order a sequential prefill sees */
+        size_t depth = 0;
+        for (int32_t a = (int32_t)i; a >= 0; a = parent[a]) path[depth++] = (size_t)a;
+        for (size_t k = 0; k < depth; ++k) {
+            const size_t a = path[depth - 1 - k];
+            kp[length + k] = node_keys + a * nh * qm;
+            vp[length + k] = node_values + a * nh * vd;
+            sp[length + k] = node_shared + a * qe;
+        }
+        st = mla_attend(w, x + i * H, query, kp, vp, sp, length + depth, out + i * H);
+    }
+    free(query);
+    free(path);
+    free(kp);
+    free(vp);
+    free(sp);
     return st;
 }
 

@@ -283,6 +283,17 @@ typedef struct {
  * 0 .. *length, writes out [hidden] and increments *length. */
 int k3xo_mla_step(const k3xo_mla_weights* w, const float* x, float* keys, float* values,
                   float* shared, size_t capacity, size_t* length, float* out);
+/* A draft tree verified against a committed state of `length` positions:
+ * node i (parent[i] < i, -1 = a root on the committed state) is projected
+ * like a position of k3xo_mla_step and attends to the committed positions,
+ * then its ancestors root first, then itself; on a chain this is the
+ * sequential prefill bit for bit. Writes each node's key, value and shared
+ * key (node_* [nodes][...], for the commit) and its output out [nodes][H].
+ * New: the reference verifies chains only. */
+int k3xo_mla_tree(const k3xo_mla_weights* w, const float* keys, const float* values,
+                  const float* shared, size_t length, const int32_t* parent, size_t nodes,
+                  const float* x, float* node_keys, float* node_values, float* node_shared,
+                  float* out);
 /* Crop to `keep` positions (a rejected draft's rollback); keep > *length
  * is invalid, as the reference's restore refuses it. */
 int k3xo_mla_crop(size_t* length, size_t keep);

@@ -182,6 +182,8 @@ class Restatement:
         L.k3xo_block_attention_residual.argtypes = [_f32p, _f32p, _sz, _sz, _sz, _f32p, _f32p, C.c_float, _f32p]
         L.k3xo_mla_step.argtypes = [C.c_void_p, _f32p, _f32p, _f32p, _f32p, _sz, _szp, _f32p]
         L.k3xo_mla_crop.argtypes = [_szp, _sz]
+        L.k3xo_mla_tree.argtypes = [C.c_void_p, _f32p, _f32p, _f32p, _sz, _i32p, _sz, _f32p, _f32p, _f32p,
+                                    _f32p, _f32p]
         L.k3xo_argmax.restype = C.c_uint32
         L.k3xo_argmax.argtypes = [_f32p, _sz]
         L.k3xo_verify_greedy_block.argtypes = [C.c_uint32, _u32p, _sz, _sz, _sz, _u32p,
@@ -467,6 +469,26 @@ class Restatement:
         st["length"] = length.value
         del keep
         return out, st
+
+    def mla_tree(self, w: dict, state, parent, x):
+        """A draft tree over the committed `state` (new: the reference
+        verifies chains only): node i attends to the committed positions, its
+        ancestors root first, and itself. Returns the outputs [nodes][H] and
+        each node's key, value and shared key; the state is not changed."""
+        x = _c(np.atleast_2d(x), np.float32)
+        n = x.shape[0]
+        par = np.ascontiguousarray(parent, np.int32)
+        keep = [_c(w[k], np.float32) for k in MLA_TENSORS]
+        ws = _MlaWeights(w["hidden"], w["heads"], w["q_rank"], w["kv_rank"], w["q_main"], w["q_extra"],
+                         w["value_dim"], w["eps"], *(a.ctypes.data for a in keep))
+        nk = np.empty((n, w["heads"], w["q_main"]), np.float32)
+        nv = np.empty((n, w["heads"], w["value_dim"]), np.float32)
+        ns = np.empty((n, w["q_extra"]), np.float32)
+        out = np.empty((n, w["hidden"]), np.float32)
+        self._check(self.lib.k3xo_mla_tree(C.byref(ws), state["keys"], state["values"], state["shared"],
+                                           state["length"], par, n, x, nk, nv, ns, out), "mla_tree")
+        del keep
+        return out, nk, nv, ns
 
     def mla_crop(self, state, keep):
         """The rollback of rejected drafts (model.cpp:1235-1251)."""

@@ -6,7 +6,10 @@ CPU, before any device path is built on it:
     synthetic config: outputs and the final keys, values and shared keys to
     2e-6 of their largest value (torch sums in its own order);
   * the crop: rolling back to k positions and replaying gives the same bits
-    as never having gone past k.
+    as never having gone past k;
+  * the draft-tree form the device path will implement (new; the reference
+    verifies chains): a node's output is, bit for bit, the sequential
+    prefill over the committed rows and its root-to-node path.
 CPU only."""
 import os
 
@@ -82,3 +85,49 @@ def test_single_position_attends_to_itself(rs):
     sig = (np.float32(1) / (np.float32(1) + np.exp(-gate))).astype(np.float32)
     want = (np.asarray(w["o_proj"], np.float64) @ (merged * sig).astype(np.float64)).astype(np.float32)
     _close(out[0], want, "single position")
+
+
+def _copy_state(st):
+    return {k: (v.copy() if isinstance(v, np.ndarray) else v) for k, v in st.items()}
+
+
+def test_tree_on_a_chain_is_the_prefill(rs):
+    z = np.load(GOLDEN)
+    w = _weights(z)
+    x = z["x"]
+    full, full_st = rs.mla_prefill(w, x)
+    _, st = rs.mla_prefill(w, x[:2])
+    out, nk, nv, ns = rs.mla_tree(w, st, [-1, 0, 1], x[2:])
+    assert np.array_equal(out, full[2:])
+    assert np.array_equal(nk, full_st["keys"][2:5]) and np.array_equal(nv, full_st["values"][2:5])
+    assert np.array_equal(ns, full_st["shared"][2:5])
+    assert st["length"] == 2   # the tree leaves the committed state alone
+
+
+def test_tree_node_is_the_prefill_of_its_path(rs):
+    """Every node of a branching tree gives the bits of a sequential prefill
+    over the committed rows and its root-to-node path."""
+    z = np.load(GOLDEN)
+    w = _weights(z)
+    g = np.random.default_rng(29)
+    parent = [-1, 0, 0, 1, 1, 2, -1, 6]
+    nodes = g.normal(size=(len(parent), w["hidden"])).astype(np.float32)
+    _, st = rs.mla_prefill(w, z["x"][:3])
+    out, _, _, _ = rs.mla_tree(w, st, parent, nodes)
+    for i in range(len(parent)):
+        path = []
+        a = i
+        while a >= 0:
+            path.append(a)
+            a = parent[a]
+        rows = nodes[path[::-1]]
+        ref_out, _ = rs.mla_prefill(w, rows, _copy_state(st))
+        assert np.array_equal(out[i], ref_out[-1]), i
+
+
+def test_tree_rejects_forward_parents(rs):
+    z = np.load(GOLDEN)
+    w = _weights(z)
+    _, st = rs.mla_prefill(w, z["x"][:1])
+    with pytest.raises(OracleError):
+        rs.mla_tree(w, st, [-1, 2, 0], z["x"][1:4])
